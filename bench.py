@@ -1,0 +1,412 @@
+#!/usr/bin/env python
+"""Benchmark of the INT4 group-quantised decode GEMV on B200.
+
+Workload (one step = one GEMV, i.e. one decode token through one linear):
+  x fp32 [1, 4096] ~ N(0,1); W [4096 x 14336] ~ N(0, 0.02) quantised to the
+  reference INT4 layout with group 32 along K (asymmetric: fp16 scale + int8
+  zero point per group and column, two nibbles per byte); y fp32 [1, 14336].
+Weights are packed once on the device by the library's own packer.  Eight
+distinct copies of the packed weights (8 x 34.9 MB = 279 MB > 126 MB L2) are
+cycled so every step streams its weights from HBM.
+
+Arms:
+  (default)          our kernel through the C ABI; value = aggregate HBM GB/s
+                     of algorithmic bytes over all ranks (weak scaling: every
+                     rank runs the full workload on its own GPU, no collective
+                     on the data path).
+  --impl reference   the reference's own CPU kernel (matmul_int4_grouped_neon,
+                     compiled from its header into oracle/_ref) on all host
+                     threads; rank 0 only.
+
+Launch for N > 1: python -m torch.distributed.run --nproc-per-node N bench.py --gpus N
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import ctypes
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "INT4 decode tokens/s & GEMV HBM GB/s; flash-attn TFLOP/s at 1/2/4/8 B200"
+K_DIM, N_DIM, GS = 4096, 14336, 32
+WORKLOAD = (f"int4_gemv: x fp32 [1,{K_DIM}] x W[{K_DIM}x{N_DIM}] int4 asym group {GS} "
+            f"(fp16 scale + int8 zero), y fp32 [1,{N_DIM}]")
+
+
+def algorithmic_bytes(K=K_DIM, N=N_DIM, gs=GS) -> int:
+    G = (K + gs - 1) // gs
+    return ((K + 1) // 2) * N + G * N * 2 + G * N * 1 + K * 4 + N * 4
+
+
+def rank_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def read_peak_hbm():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            return float(json.load(fh)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def read_profile_traffic():
+    """DRAM bytes per launch of the GEMV kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "w4_gemv_k4096_n14336_g32.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip().split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled during the timed region."""
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax = max(smax, float(parts[1]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[4:8]):
+                if v.lower() in ("active", "1", "yes"):
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def cpu_baseline_sample(seconds=12.0):
+    """The reference's own INT4 kernel (oracle/_ref), 1 thread, full config shape."""
+    import oracle
+    if oracle.ref_available():
+        R = oracle.ref()
+        fn, kind = R.sgref_neon_matmul_int4_grouped, "reference"
+    else:
+        fn, kind = None, "port"
+    K, N, gs = K_DIM, N_DIM, GS
+    rng = np.random.default_rng(7)
+    B = rng.integers(0, 256, (K // 2, N), dtype=np.uint8)
+    S = (rng.random((K // gs, N)) * 0.01).astype(np.float16)
+    Z = rng.integers(-8, 8, (K // gs, N), dtype=np.int8)
+    C = np.zeros(N, np.float16)
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+    if kind == "reference":
+        A = rng.integers(-128, 128, K, dtype=np.int8)
+        call = lambda: fn(P(A), P(B), P(S), P(Z), P(C), K, N, gs)  # noqa: E731
+    else:
+        x = rng.standard_normal((1, K)).astype(np.float32)
+        call = lambda: oracle.matmul_int4_grouped(x, B, S, Z, K, N, gs)  # noqa: E731
+    call()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        call()
+        n += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    gbs = n * algorithmic_bytes() / dt / 1e9
+    return {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind,
+            "sample": f"{n} full GEMV calls (K={K}, N={N}, gs={gs}, int8 activations: the reference "
+                      f"INT4 kernel's only activation type) in {dt:.1f} s on 1 host thread"}
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from silicongraph_b200 import _lib, kernels
+
+    rank, local_rank, world = rank_env()
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    lib = _lib.load()
+    dev = torch.device("cuda", local_rank)
+    K, N, gs = K_DIM, N_DIM, GS
+    G = K // gs
+    nbytes = algorithmic_bytes()
+
+    # inputs generated on the host, copied; weights packed on the device by our packer
+    rng = np.random.default_rng(1234 + rank)
+    W = torch.from_numpy((rng.standard_normal((K, N)) * 0.02).astype(np.float32)).to(dev)
+    x_host = torch.from_numpy(rng.standard_normal((1, K)).astype(np.float32)).pin_memory()
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    copies = max(2, math.ceil(2.0 * l2 / (nbytes - K * 4 - N * 4)))
+    Bs, Ss, Zs = [], [], []
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for _ in range(copies):
+            B = torch.empty((K // 2, N), dtype=torch.uint8, device=dev)
+            S = torch.empty((G, N), dtype=torch.float16, device=dev)
+            Z = torch.empty((G, N), dtype=torch.int8, device=dev)
+            _lib.check(lib.sg_quantize_int4_grouped(W.data_ptr(), K, N, gs, 0, B.data_ptr(), S.data_ptr(),
+                                                    Z.data_ptr(), stream.cuda_stream))
+            Bs.append(B)
+            Ss.append(S)
+            Zs.append(Z)
+    stream.synchronize()
+    del W
+    x = x_host.to(dev)
+    y = torch.empty((1, N), dtype=torch.float32, device=dev)
+    params = [kernels.matmul_params(x, Bs[i], y, M=1, K=K, N=N, scales=Ss[i], zeros=Zs[i], group_size=gs)
+              for i in range(copies)]
+    pptr = [ctypes.byref(p) for p in params]
+    st = stream.cuda_stream
+    fn = lib.sg_matmul_int4_grouped
+
+    def launch(i):
+        r = fn(pptr[i % copies], st)
+        if r != 0:
+            raise _lib.SgError(r, _lib.last_error())
+
+    # warm-up (also allocates the library scratch for this stream, outside capture)
+    for i in range(args.warmup):
+        launch(i)
+    stream.synchronize()
+
+    graph_len = max(copies, (args.graph_len // copies) * copies)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(graph_len):
+            launch(i)
+    g.replay()
+    stream.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- timed region: exactly K steps
+    clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps // graph_len):
+            g.replay()
+        for i in range(args.steps % graph_len):
+            launch(i)
+        e1.record(stream)
+    stream.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop() if clocks else None
+    ms_local = e0.elapsed_time(e1)
+    ms = max_over_ranks(ms_local)
+    value = world * args.steps * nbytes / (ms / 1e3) / 1e9
+    per_gpu = args.steps * nbytes / (ms / 1e3) / 1e9
+
+    # ---- end to end: host x -> device, GEMV through the C ABI, y -> host, every step
+    e2e_steps = min(args.steps, args.e2e_steps)
+    y_host = torch.empty((1, N), dtype=torch.float32).pin_memory()
+    barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(e2e_steps):
+            x.copy_(x_host, non_blocking=True)
+            launch(i)
+            y_host.copy_(y, non_blocking=True)
+            stream.synchronize()
+        e1.record(stream)
+    stream.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = world * e2e_steps * nbytes / (e2e_ms / 1e3) / 1e9
+
+    del g
+    peak, peak_kind = read_peak_hbm()
+    traffic = read_profile_traffic()
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, host-generated)",
+        "config": {"workload": WORKLOAD, "K": K, "N": N, "group_size": gs,
+                   "bytes_per_step": nbytes, "weight_copies": copies,
+                   "l2": f"{copies} rotating weight copies ({copies * nbytes / 1e6:.0f} MB > L2 {l2 / 1e6:.0f} MB)",
+                   "parallelism": f"replicas x{world} (no data-path collective)",
+                   "timing": f"CUDA graph of {graph_len} launches, CUDA events, max over ranks"},
+        "roofline": {"bound": "hbm", "achieved": round(per_gpu, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(per_gpu / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                     "traffic": traffic, "achieved_basis": "algorithmic bytes per launch x launches / "
+                     "event time of back-to-back launches (includes inter-launch gaps)"},
+        "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "steps": e2e_steps,
+                "h2d_bytes_per_step": int(x_host.numel() * 4), "d2h_bytes_per_step": int(y_host.numel() * 4)},
+        "gpu_launches": args.steps,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            line["cpu_baseline"] = cpu_baseline_sample(args.cpu_seconds)
+        except Exception as e:  # the baseline is reported, never required
+            line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    rank, _, world = rank_env()
+    if rank != 0:
+        return
+    import oracle
+    K, N, gs = K_DIM, N_DIM, GS
+    if oracle.ref_available():
+        fn, kind = oracle.ref().sgref_neon_matmul_int4_grouped, "reference"
+    else:
+        fn, kind = None, "port"
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(7)
+    B = rng.integers(0, 256, (K // 2, N), dtype=np.uint8)
+    S = (rng.random((K // gs, N)) * 0.01).astype(np.float16)
+    Z = rng.integers(-8, 8, (K // gs, N), dtype=np.int8)
+    A = rng.integers(-128, 128, K, dtype=np.int8)
+    xf = rng.standard_normal((1, K)).astype(np.float32)
+    Cs = [np.zeros(N, np.float16) for _ in range(threads)]
+    base = [a.ctypes.data for a in (A, B, S, Z)]
+
+    def slice_call(t, k0, rows):
+        if kind == "reference":
+            fn(ctypes.c_void_p(base[0] + k0), ctypes.c_void_p(base[1] + (k0 // 2) * N),
+               ctypes.c_void_p(base[2] + (k0 // gs) * N * 2), ctypes.c_void_p(base[3] + (k0 // gs) * N),
+               Cs[t].ctypes.data_as(ctypes.c_void_p), rows, N, gs)
+        else:
+            sl = slice(k0 // gs, (k0 + rows) // gs)
+            oracle.matmul_int4_grouped(xf[:, k0:k0 + rows], B[k0 // 2:(k0 + rows) // 2], S[sl], Z[sl], rows, N, gs)
+
+    pool = cf.ThreadPoolExecutor(threads)
+    units = K // gs  # slices are whole groups
+
+    def step(rows_per_thread, s):
+        futs = []
+        for t in range(threads):
+            k0 = ((s * threads + t) * rows_per_thread) % K
+            k0 = min(k0, K - rows_per_thread)
+            futs.append(pool.submit(slice_call, t, k0, rows_per_thread))
+        for f in futs:
+            f.result()
+
+    # calibrate: per-thread slice size so the whole run stays within the time budget
+    rows = gs
+    t0 = time.perf_counter()
+    step(rows, 0)
+    t_unit = max(time.perf_counter() - t0, 1e-5)
+    budget = args.ref_budget_s / max(1, args.steps + args.warmup)
+    rows = int(max(1, min(units, budget / t_unit))) * gs
+    for s in range(args.warmup):
+        step(rows, s)
+    t0 = time.perf_counter()
+    for s in range(args.steps):
+        step(rows, s)
+    dt = time.perf_counter() - t0
+    bytes_per_step = threads * ((rows // 2) * N + (rows // gs) * N * 3 + rows + N * 2)
+    value = args.steps * bytes_per_step / dt / 1e9
+    sample = (f"each step: {threads} threads each run the reference INT4 kernel on a {rows}-row K slice "
+              f"at full N={N} (int8 activations, its only activation type); {args.steps} steps in {dt:.1f} s")
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "K": K, "N": N, "group_size": gs},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100000)
+    ap.add_argument("--warmup", type=int, default=1000)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--graph-len", type=int, default=256)
+    ap.add_argument("--e2e-steps", type=int, default=5000)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--ref-budget-s", type=float, default=120.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    _, _, world = rank_env()
+    if world != args.gpus and args.impl == "ours":
+        if args.gpus > 1 and world == 1:
+            ap.error("for --gpus N > 1 launch with torch.distributed.run --nproc-per-node N")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,181 @@
+/*
+ * SiliconGraph-B200 kernel C ABI.
+ *
+ * The reference dispatches its CPU kernels "via function pointer through the
+ * runtime's kernel table" (compiler/kernels/cpu/matmul_neon.h:9) with the
+ * signature `void k(const MatMulParams&)` (matmul_neon.h:32-43) and
+ * `void flash_attention_fp16(const FlashAttentionParams&)`
+ * (flash_attention.h:25-42, :95).  This header is the table a CUDA graph
+ * profile binds instead: the parameter structs keep the reference's field
+ * names and meanings, with device pointers, an explicit CUDA stream and a
+ * status return added.
+ *
+ * Conventions
+ *  - Every pointer in a params struct is a DEVICE pointer (cudaMalloc'd or
+ *    otherwise device-accessible), caller-owned.
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *    Calls are asynchronous on that stream and never abort the process.
+ *  - Return value: SG_OK (0) or a negative code whose values equal the
+ *    reference SDK's ArmStatus (compiler/include/armcc_sdk.h:80-87).  On error
+ *    sg_last_error() returns a thread-local message.
+ *  - Zero-initialised extension fields select the reference's behaviour.
+ *  - There is no CPU fallback: without a usable CUDA device every compute
+ *    entry point returns SG_ERR_RUNTIME.
+ */
+#ifndef SG_KERNELS_H_
+#define SG_KERNELS_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t SgStatus;
+#define SG_OK 0
+#define SG_ERR_NOT_FOUND (-1)   /* ARMCC_ERR_NOT_FOUND */
+#define SG_ERR_INVALID (-2)     /* ARMCC_ERR_INVALID_PACKAGE: bad argument / layout */
+#define SG_ERR_OOM (-3)         /* ARMCC_ERR_OOM */
+#define SG_ERR_UNSUPPORTED (-4) /* ARMCC_ERR_UNSUPPORTED */
+#define SG_ERR_RUNTIME (-5)     /* ARMCC_ERR_RUNTIME: CUDA error */
+
+/* Element types.  SG_DT_DEFAULT means "the reference kernel's own type". */
+typedef enum {
+  SG_DT_DEFAULT = 0,
+  SG_DT_F32 = 1,
+  SG_DT_F16 = 2,
+  SG_DT_BF16 = 3,
+  SG_DT_I8 = 4
+} SgDType;
+
+/*
+ * Mirrors armcc::kernels::cpu::MatMulParams (matmul_neon.h:32-43).
+ * Fields up to group_size keep the reference's names and meanings; the
+ * reference declares scales_B as `const float*` but its INT4 kernel reads it
+ * as fp16 (matmul_neon.h:40,118,132) -- here it is `const void*` and its
+ * element type is fixed per entry point (documented on each).
+ */
+typedef struct SgMatMulParams {
+  const void* A;          /* [M, K] activations (row m at m*lda)               */
+  const void* B;          /* weights; layout per entry point                   */
+  const void* bias;       /* [N] fp16, or NULL                                 */
+  void* C;                /* [M, N] output (row m at m*ldc)                    */
+  int32_t M, K, N;
+  int32_t lda, ldb, ldc;  /* leading dims in elements; <= 0 means dense       */
+  float scale_A;          /* int8 activation dequant scale                     */
+  const void* scales_B;   /* per-group (INT4) or per-channel (INT8) scales     */
+  const int8_t* zeros_B;  /* per-group INT4 zero points in [-8, 7], or NULL    */
+  int32_t group_size;     /* INT4 group along K; <= 0 means 128 (:120)         */
+  /* ---- extensions (zero = reference behaviour) ---- */
+  int32_t a_dtype;        /* SgDType of A                                      */
+  int32_t c_dtype;        /* SgDType of C                                      */
+  void* workspace;        /* optional caller scratch, see *_workspace_size()   */
+  size_t workspace_bytes;
+} SgMatMulParams;
+
+/*
+ * Mirrors armcc::kernels::cpu::FlashAttentionParams (flash_attention.h:25-42),
+ * layouts [B, heads, S, head_dim] (flash_attention.h:116,124,137).
+ */
+typedef struct SgFlashAttentionParams {
+  const void* Q;          /* [B, num_heads,    S_q,  head_dim]                 */
+  const void* K;          /* [B, num_kv_heads, S_kv, head_dim]                 */
+  const void* V;          /* [B, num_kv_heads, S_kv, head_dim]                 */
+  void* O;                /* [B, num_heads,    S_q,  head_dim]                 */
+  const void* mask;       /* must be NULL (the reference never reads it)       */
+  int32_t B;
+  int32_t S;              /* query length (== key length unless S_kv > 0)      */
+  int32_t num_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  float scale;            /* <= 0 means 1/sqrt(head_dim) (flash_attention.h:101) */
+  int32_t causal;         /* bool in the reference                             */
+  int32_t streaming;      /* accepted and ignored, as in the reference         */
+  int32_t chunk_size;     /* accepted and ignored, as in the reference         */
+  /* ---- extensions (zero = reference behaviour) ---- */
+  int32_t io_dtype;       /* SgDType of Q/K/V/O; DEFAULT = fp16 (:96-99)       */
+  int32_t S_kv;           /* key/value length; <= 0 means S                    */
+  int32_t q_pos0;         /* position of query 0 for the causal test; < 0 means S_kv - S */
+  int64_t kv_batch_stride;/* elements between batches of K/V; <= 0 = dense     */
+  int64_t kv_head_stride; /* elements between kv heads of K/V; <= 0 = dense    */
+  void* workspace;        /* optional caller scratch (decode split-K)          */
+  size_t workspace_bytes;
+} SgFlashAttentionParams;
+
+/* ---------------------------------------------------------------- status */
+const char* sg_last_error(void);
+int32_t sg_version(void);       /* (major << 16) | (minor << 8) | patch */
+/* Number of CUDA devices usable by the library (0 when none). */
+int32_t sg_device_count(void);
+/* Override a launch heuristic (benchmark sweeps).  Keys:
+ *   "w4_gemv.groups_per_warp"  INT4 GEMV split-K granularity (0 = heuristic)
+ * Returns SG_ERR_NOT_FOUND for an unknown key.  No reference counterpart. */
+int32_t sg_set_tuning(const char* key, int32_t value);
+
+/* ---------------------------------------------------------- linear layers */
+
+/*
+ * INT4 grouped dequant GEMV/GEMM.  Replaces matmul_int4_grouped_neon
+ * (compiler/kernels/cpu/matmul_neon.h:113-148).
+ *   B        u8  [ceil(K/2), N]: byte (k/2)*N + n, low nibble = even k   (:127)
+ *   scales_B f16 [ceil(K/gs), N]                                           (:132)
+ *   zeros_B  i8  [ceil(K/gs), N] in [-8, 7], or NULL                       (:133)
+ *   C[m, n] = sum_k A[m, k] * scale * ((nibble - 8) - zero)
+ * a_dtype: DEFAULT/I8 (reference), F32, F16, BF16.  c_dtype: DEFAULT/F16
+ * (reference), F32, BF16.  For int8 A the sum is multiplied by scale_A
+ * (the reference ignores scale_A; pass 1.0 for its exact behaviour).  bias,
+ * when non-NULL, is added before the output rounding (the reference ignores
+ * bias).  ldb must be <= 0 or N.  group_size must be even or K <= group_size.
+ */
+SgStatus sg_matmul_int4_grouped(const SgMatMulParams* p, void* stream);
+/* Scratch bytes the call needs when p->workspace is NULL the library supplies
+ * it from a per-device cache; a caller-supplied workspace must be at least
+ * this large and zero-filled once before its first use (calls leave it
+ * zero-filled).  Returns 0 when no scratch is needed. */
+size_t sg_matmul_int4_grouped_workspace_size(const SgMatMulParams* p);
+
+/*
+ * INT8 per-channel GEMV/GEMM.  Replaces the GLSL gemm_int8 shader
+ * (compiler/kernels/gpu/vulkan_shaders.h:53-82) and OpenCL gemm_int8_m1
+ * (compiler/kernels/gpu/opencl_kernels.h:36-52).
+ *   B        i8  [K, N] row-major (B[k*N + n])
+ *   scales_B f32 [N]
+ * a_dtype DEFAULT/I8: C[m,n] = float(sum_k A*B as int32) * scale_A * scales_B[n]
+ *                     (the shader's exact arithmetic; c_dtype DEFAULT = F32)
+ * a_dtype F32/F16/BF16: weight-only variant C[m,n] = scales_B[n] * sum_k A*B
+ *                     in fp32 (scale_A unused).
+ */
+SgStatus sg_matmul_int8_channel(const SgMatMulParams* p, void* stream);
+size_t sg_matmul_int8_channel_workspace_size(const SgMatMulParams* p);
+
+/*
+ * fp16-weight GEMV/GEMM.  Replaces matmul_fp16_neon_m1 (matmul_neon.h:48-107).
+ *   B f16 [K, N] row-major; bias f16 [N] or NULL, added in fp32 before the
+ *   output rounding (as the reference's NEON tail loop, :90-94).
+ * a_dtype DEFAULT = F16; c_dtype DEFAULT = F16.
+ */
+SgStatus sg_matmul_fp16(const SgMatMulParams* p, void* stream);
+size_t sg_matmul_fp16_workspace_size(const SgMatMulParams* p);
+
+/*
+ * Device-side INT4 packer: quantises W f32 [K, N] (row-major, W[k*N+n]) per
+ * (group of group_size along K, column) into the layout above.
+ * symmetric == 0: scale = (max-min)/15, zp = clamp(round(-8 - min/scale), -8, 7)
+ *   (python/armcc/calibration.py:37-50, per group and column); zeros required.
+ * symmetric != 0: scale = absmax/7, zeros may be NULL (nothing written).
+ * Bit-identical to the CPU packer of the same convention.
+ */
+SgStatus sg_quantize_int4_grouped(const float* W, int32_t K, int32_t N, int32_t group_size,
+                                  int32_t symmetric, uint8_t* B, uint16_t* scales,
+                                  int8_t* zeros, void* stream);
+/* Unpack to f32 W[k*N+n] = float(scale) * ((nibble - 8) - zero), the
+ * reference's w0f/w1f (matmul_neon.h:127-136), bit for bit. */
+SgStatus sg_dequantize_int4_grouped(const uint8_t* B, const uint16_t* scales,
+                                    const int8_t* zeros, int32_t K, int32_t N,
+                                    int32_t group_size, float* W, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SG_KERNELS_H_ */

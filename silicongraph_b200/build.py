@@ -1,0 +1,111 @@
+"""Build recipe for the native library ``silicongraph_b200/lib/libsg_b200.so``.
+
+Every CUDA source under ``csrc/`` is compiled for sm_100a only
+(``-gencode arch=compute_100a,code=sm_100a``) and linked, together with the
+C++ host runtime, into one shared library with a plain C ABI
+(``include/sg_kernels.h``, ``include/armcc_sdk.h``).  The library is built
+in-tree so it travels with the repository snapshot; nothing is installed.
+
+Usage: ``python -m silicongraph_b200.build [-j N] [--force]``
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import glob
+import hashlib
+import os
+import shutil
+import subprocess
+import sys
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+CSRC = os.path.join(PKG, "csrc")
+INCLUDE = os.path.join(ROOT, "include")
+BUILD = os.path.join(PKG, "_build")
+LIBDIR = os.path.join(PKG, "lib")
+LIB = os.path.join(LIBDIR, "libsg_b200.so")
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
+              "-Xptxas", "-v", "-DNDEBUG"]
+
+
+def nvcc() -> str:
+    cand = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not os.path.exists(cand):
+        raise RuntimeError("nvcc not found")
+    return cand
+
+
+def _sources():
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + sorted(glob.glob(os.path.join(CSRC, "*.cpp")))
+
+
+def _headers():
+    return sorted(glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h")) +
+                  glob.glob(os.path.join(INCLUDE, "*.h")))
+
+
+def _digest(src: str, hdrs) -> str:
+    h = hashlib.sha256()
+    for f in [src, *hdrs]:
+        with open(f, "rb") as fh:
+            h.update(fh.read())
+    h.update(" ".join(ARCH + NVCC_FLAGS).encode())
+    return h.hexdigest()[:16]
+
+
+def _compile(src: str, hdrs, force: bool) -> tuple[str, str]:
+    base = os.path.splitext(os.path.basename(src))[0]
+    obj = os.path.join(BUILD, base + ".o")
+    stamp = obj + ".sha"
+    dig = _digest(src, hdrs)
+    if not force and os.path.exists(obj) and os.path.exists(stamp) and open(stamp).read() == dig:
+        return obj, ""
+    cmd = [nvcc(), *ARCH, *NVCC_FLAGS, "-I", INCLUDE, "-I", CSRC, "-c", src, "-o", obj]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed for {src}:\n{r.stdout}\n{r.stderr}")
+    with open(stamp, "w") as fh:
+        fh.write(dig)
+    return obj, r.stderr
+
+
+def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -> str:
+    os.makedirs(BUILD, exist_ok=True)
+    os.makedirs(LIBDIR, exist_ok=True)
+    hdrs = _headers()
+    srcs = _sources()
+    jobs = jobs or min(8, os.cpu_count() or 4)
+    with cf.ThreadPoolExecutor(jobs) as ex:
+        results = list(ex.map(lambda s: _compile(s, hdrs, force), srcs))
+    objs = [o for o, _ in results]
+    if verbose:
+        for _, log in results:
+            if log:
+                sys.stderr.write(log)
+    newest = max(os.path.getmtime(o) for o in objs)
+    if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < newest:
+        tmp = LIB + ".tmp"
+        cmd = [nvcc(), *ARCH, "-shared", "-o", tmp, *objs, "-cudart", "static", "-lcuda",
+               "-L/usr/local/cuda/lib64/stubs"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+        os.replace(tmp, LIB)
+    return LIB
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("-j", type=int, default=None)
+    ap.add_argument("-v", action="store_true")
+    a = ap.parse_args()
+    print(build(force=a.force, jobs=a.j, verbose=a.v))
+
+
+if __name__ == "__main__":
+    main()

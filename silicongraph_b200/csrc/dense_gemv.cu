@@ -1,0 +1,450 @@
+// INT8 per-channel and fp16-weight GEMV (decode) for sm_100a.
+//
+// sg_matmul_int8_channel replaces the GLSL gemm_int8 shader
+// (compiler/kernels/gpu/vulkan_shaders.h:53-82) / OpenCL gemm_int8_m1
+// (opencl_kernels.h:36-52):  B int8 [K, N] row-major, scales f32 [N],
+//   int8 A:  C[n] = float(sum_k A[k]*B[k,n] as int32) * scale_A * scales[n]
+//   float A: C[n] = scales[n] * sum_k A[k]*float(B[k,n])           (fp32)
+// sg_matmul_fp16 replaces matmul_fp16_neon_m1 (matmul_neon.h:48-107):
+//   B fp16 [K, N] row-major, C[n] = sum_k A[k]*B[k,n] (+ bias[n]).
+//
+// Same streaming structure as the INT4 kernel: a lane owns 16 consecutive
+// columns and reads one row of them per 128-bit load (two for fp16), 8 warps
+// split the block's rows, blocks split K, and partials are reduced by the
+// last block of each column tile in fixed order.
+//   * int8 A: four rows of a lane are transposed 4x4 bytes with PRMT so each
+//     32-bit word holds one column's four k values, then dp4a accumulates in
+//     int32 -- exact, hence bit-identical to the shader for any split.
+//   * float A: int8 bytes become exact fp32 via (b ^ 0x80) placed in the low
+//     byte of 2^23 (PRMT) minus (2^23 + 128), then packed fp32x2 FMAs.
+//   * fp16 B: half2 -> float2 conversion and packed fp32x2 FMAs.
+#include <algorithm>
+
+#include "sg_common.cuh"
+
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kColsPerLane = 16;
+constexpr int kColsPerBlock = 32 * kColsPerLane;  // 512
+constexpr int kRowsPerChunk = 8;                   // rows per warp step (multiple of 4)
+
+enum WKind { W_INT8_IA = 0, W_INT8_FA = 1, W_F16 = 2 };
+
+struct DArgs {
+  const void* A;
+  const uint8_t* B;      // byte pointer to weights
+  const float* scales;   // int8: [N]
+  const __half* bias;    // fp16: [N] or NULL
+  void* C;
+  int M, K, N, lda, ldc;
+  int a_dt, c_dt;
+  float scale_A;
+  int rows_per_split, ksplit;
+  float* partial;      // [ksplit][M][N] (float)  or int32 for W_INT8_IA
+  unsigned* tickets;
+};
+
+__device__ __forceinline__ float load_act(const void* A, int dt, int64_t i) {
+  switch (dt) {
+    case SG_DT_F32: return sgd::load_as_float<SG_DT_F32>(A, i);
+    case SG_DT_F16: return sgd::load_as_float<SG_DT_F16>(A, i);
+    case SG_DT_BF16: return sgd::load_as_float<SG_DT_BF16>(A, i);
+    default: return sgd::load_as_float<SG_DT_I8>(A, i);
+  }
+}
+
+__device__ __forceinline__ void store_out(void* C, int dt, int64_t i, float v) {
+  switch (dt) {
+    case SG_DT_F32: sgd::store_from_float<SG_DT_F32>(C, i, v); break;
+    case SG_DT_BF16: sgd::store_from_float<SG_DT_BF16>(C, i, v); break;
+    default: sgd::store_from_float<SG_DT_F16>(C, i, v); break;
+  }
+}
+
+template <int KIND>
+__device__ __forceinline__ float finalize_f(const DArgs& a, int col, float v) {
+  if (KIND == W_INT8_FA) v = v * a.scales[col];
+  if (KIND == W_F16 && a.bias) v = v + __half2float(a.bias[col]);
+  return v;
+}
+
+__device__ __forceinline__ float finalize_i(const DArgs& a, int col, int acc) {
+  // vulkan_shaders.h:80: float(acc) * scale_A * Scales[n], left to right
+  return __fmul_rn(__fmul_rn((float)acc, a.scale_A), a.scales[col]);
+}
+
+// 4x4 byte transpose: in w[r] = row r (bytes = columns 0..3); out c[b] = column b (bytes = rows 0..3).
+__device__ __forceinline__ void transpose4x4(const uint32_t w0, const uint32_t w1, const uint32_t w2,
+                                             const uint32_t w3, uint32_t c[4]) {
+  const uint32_t t0 = __byte_perm(w0, w1, 0x5140);  // w0.b0 w1.b0 w0.b1 w1.b1
+  const uint32_t t1 = __byte_perm(w2, w3, 0x5140);  // w2.b0 w3.b0 w2.b1 w3.b1
+  const uint32_t t2 = __byte_perm(w0, w1, 0x7362);  // w0.b2 w1.b2 w0.b3 w1.b3
+  const uint32_t t3 = __byte_perm(w2, w3, 0x7362);
+  c[0] = __byte_perm(t0, t1, 0x5410);
+  c[1] = __byte_perm(t0, t1, 0x7632);
+  c[2] = __byte_perm(t2, t3, 0x5410);
+  c[3] = __byte_perm(t2, t3, 0x7632);
+}
+
+// Exact fp32 values of the 4 signed bytes of w as two pairs (b0,b1), (b2,b3).
+__device__ __forceinline__ void i8word_to_f32(uint32_t w, float2& p01, float2& p23) {
+  const uint32_t u = w ^ 0x80808080u;  // biased: byte + 128 in [0, 255]
+  const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440));
+  const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441));
+  const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442));
+  const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443));
+  constexpr float OFF = -8388736.0f;  // -(2^23 + 128)
+  const float2 one = make_float2(1.f, 1.f), off = make_float2(OFF, OFF);
+  p01 = sgd::ffma2(make_float2(f0, f1), one, off);
+  p23 = sgd::ffma2(make_float2(f2, f3), one, off);
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(kThreads, 2) dense_gemv_kernel(DArgs a) {
+  extern __shared__ float xs_f[];  // staged activations for this block's rows
+  const int tile = blockIdx.x, split = blockIdx.y;
+  const int r_begin = split * a.rows_per_split;
+  const int r_end = min(a.K, r_begin + a.rows_per_split);
+  const int nrows = r_end - r_begin;
+  const int nrows_pad = (nrows + kRowsPerChunk - 1) / kRowsPerChunk * kRowsPerChunk;
+
+  // stage x (zero padded to a whole number of chunks)
+  if (KIND == W_INT8_IA) {
+    int32_t* xq = reinterpret_cast<int32_t*>(xs_f);  // packed int8 quads
+    for (int i = threadIdx.x; i < nrows_pad / 4; i += kThreads) {
+      uint32_t v = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int k = r_begin + 4 * i + j;
+        const int8_t x = (k < r_end) ? static_cast<const int8_t*>(a.A)[k] : (int8_t)0;
+        v |= (uint32_t)(uint8_t)x << (8 * j);
+      }
+      xq[i] = (int32_t)v;
+    }
+  } else {
+    for (int i = threadIdx.x; i < nrows_pad; i += kThreads) {
+      const int k = r_begin + i;
+      xs_f[i] = (k < r_end) ? load_act(a.A, a.a_dt, k) : 0.f;
+    }
+  }
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int col0 = tile * kColsPerBlock + lane * kColsPerLane;
+  const bool col_ok = col0 < a.N;
+  constexpr int ESZ = (KIND == W_F16) ? 2 : 1;
+
+  float accf[16];
+  int acci[16];
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    accf[c] = 0.f;
+    acci[c] = 0;
+  }
+
+  if (col_ok) {
+    const uint8_t* Bcol = a.B + (int64_t)col0 * ESZ;
+    for (int ch = warp * kRowsPerChunk; ch < nrows_pad; ch += kWarps * kRowsPerChunk) {
+      if (KIND == W_F16) {
+        uint4 wv[kRowsPerChunk][2];
+#pragma unroll
+        for (int r = 0; r < kRowsPerChunk; ++r) {
+          const int k = r_begin + ch + r;
+          if (k < r_end) {
+            const uint8_t* p = Bcol + (int64_t)k * a.N * 2;
+            wv[r][0] = sgd::ldg_stream(p);
+            wv[r][1] = sgd::ldg_stream(p + 16);
+          } else {
+            wv[r][0] = wv[r][1] = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < kRowsPerChunk; ++r) {
+          const float x = xs_f[ch + r];
+          const float2 xx = make_float2(x, x);
+          const uint32_t words[8] = {wv[r][0].x, wv[r][0].y, wv[r][0].z, wv[r][0].w,
+                                     wv[r][1].x, wv[r][1].y, wv[r][1].z, wv[r][1].w};
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float2 w2 = __half22float2(*reinterpret_cast<const __half2*>(&words[q]));
+            const float2 acc2 = sgd::ffma2(w2, xx, make_float2(accf[2 * q], accf[2 * q + 1]));
+            accf[2 * q] = acc2.x;
+            accf[2 * q + 1] = acc2.y;
+          }
+        }
+      } else {
+        uint4 wv[kRowsPerChunk];
+#pragma unroll
+        for (int r = 0; r < kRowsPerChunk; ++r) {
+          const int k = r_begin + ch + r;
+          wv[r] = (k < r_end) ? sgd::ldg_stream(Bcol + (int64_t)k * a.N) : make_uint4(0u, 0u, 0u, 0u);
+        }
+        if (KIND == W_INT8_IA) {
+          const int32_t* xq = reinterpret_cast<const int32_t*>(xs_f);
+#pragma unroll
+          for (int r4 = 0; r4 < kRowsPerChunk; r4 += 4) {
+            const int32_t a4 = xq[(ch + r4) / 4];
+            const uint32_t rows[4][4] = {{wv[r4].x, wv[r4].y, wv[r4].z, wv[r4].w},
+                                         {wv[r4 + 1].x, wv[r4 + 1].y, wv[r4 + 1].z, wv[r4 + 1].w},
+                                         {wv[r4 + 2].x, wv[r4 + 2].y, wv[r4 + 2].z, wv[r4 + 2].w},
+                                         {wv[r4 + 3].x, wv[r4 + 3].y, wv[r4 + 3].z, wv[r4 + 3].w}};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint32_t cw[4];
+              transpose4x4(rows[0][q], rows[1][q], rows[2][q], rows[3][q], cw);
+#pragma unroll
+              for (int b = 0; b < 4; ++b) acci[4 * q + b] = __dp4a((int)cw[b], a4, acci[4 * q + b]);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int r = 0; r < kRowsPerChunk; ++r) {
+            const float x = xs_f[ch + r];
+            const float2 xx = make_float2(x, x);
+            const uint32_t words[4] = {wv[r].x, wv[r].y, wv[r].z, wv[r].w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float2 p01, p23;
+              i8word_to_f32(words[q], p01, p23);
+              float2 a01 = sgd::ffma2(p01, xx, make_float2(accf[4 * q], accf[4 * q + 1]));
+              float2 a23 = sgd::ffma2(p23, xx, make_float2(accf[4 * q + 2], accf[4 * q + 3]));
+              accf[4 * q] = a01.x;
+              accf[4 * q + 1] = a01.y;
+              accf[4 * q + 2] = a23.x;
+              accf[4 * q + 3] = a23.y;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  // ---- reduce the 8 warps (fixed order), then split-K
+  __syncthreads();
+  __shared__ bool s_last;
+  float* red = xs_f;  // [kWarps][512] (int32 bits for W_INT8_IA)
+  if (col_ok) {
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+      red[warp * kColsPerBlock + lane * kColsPerLane + c] =
+          (KIND == W_INT8_IA) ? __int_as_float(acci[c]) : accf[c];
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < kColsPerBlock; c += kThreads) {
+    const int col = tile * kColsPerBlock + c;
+    if (col >= a.N) continue;
+    if (KIND == W_INT8_IA) {
+      int v = 0;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) v += __float_as_int(red[w * kColsPerBlock + c]);
+      if (a.ksplit == 1) store_out(a.C, a.c_dt, col, finalize_i(a, col, v));
+      else reinterpret_cast<int*>(a.partial)[(int64_t)split * a.N + col] = v;
+    } else {
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) v += red[w * kColsPerBlock + c];
+      if (a.ksplit == 1) store_out(a.C, a.c_dt, col, finalize_f<KIND>(a, col, v));
+      else a.partial[(int64_t)split * a.N + col] = v;
+    }
+  }
+  if (a.ksplit == 1) return;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(&a.tickets[tile], 1u);
+    s_last = (prev == (unsigned)(a.ksplit - 1));
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int c = threadIdx.x; c < kColsPerBlock; c += kThreads) {
+    const int col = tile * kColsPerBlock + c;
+    if (col >= a.N) continue;
+    if (KIND == W_INT8_IA) {
+      int v = 0;
+      for (int sp = 0; sp < a.ksplit; ++sp)
+        v += __ldcg(&reinterpret_cast<const int*>(a.partial)[(int64_t)sp * a.N + col]);
+      store_out(a.C, a.c_dt, col, finalize_i(a, col, v));
+    } else {
+      float v = 0.f;
+      for (int sp = 0; sp < a.ksplit; ++sp) v += __ldcg(&a.partial[(int64_t)sp * a.N + col]);
+      store_out(a.C, a.c_dt, col, finalize_f<KIND>(a, col, v));
+    }
+  }
+  if (threadIdx.x == 0) a.tickets[tile] = 0u;
+}
+
+// Reference-order loops, one thread per output (any shape / alignment).
+template <int KIND>
+__global__ void dense_gemv_generic_kernel(DArgs a) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  const int m = blockIdx.y;
+  if (n >= a.N || m >= a.M) return;
+  if (KIND == W_INT8_IA) {
+    int acc = 0;
+    for (int k = 0; k < a.K; ++k)
+      acc += (int)static_cast<const int8_t*>(a.A)[(int64_t)m * a.lda + k] *
+             (int)reinterpret_cast<const int8_t*>(a.B)[(int64_t)k * a.N + n];
+    store_out(a.C, a.c_dt, (int64_t)m * a.ldc + n, finalize_i(a, n, acc));
+  } else {
+    float acc = 0.f;
+    for (int k = 0; k < a.K; ++k) {
+      const float w = (KIND == W_F16) ? __half2float(reinterpret_cast<const __half*>(a.B)[(int64_t)k * a.N + n])
+                                      : (float)reinterpret_cast<const int8_t*>(a.B)[(int64_t)k * a.N + n];
+      acc = __fadd_rn(acc, __fmul_rn(load_act(a.A, a.a_dt, (int64_t)m * a.lda + k), w));
+    }
+    if (KIND == W_INT8_FA) acc = __fmul_rn(acc, a.scales[n]);
+    if (KIND == W_F16 && a.bias) acc = __fadd_rn(acc, __half2float(a.bias[n]));
+    store_out(a.C, a.c_dt, (int64_t)m * a.ldc + n, acc);
+  }
+}
+
+struct Plan {
+  bool fast = false;
+  int rows_per_split = 0, ksplit = 1, n_tiles = 0;
+  size_t smem = 0, ws_bytes = 0, tickets_bytes = 0;
+};
+
+Plan make_plan(int kind, const SgMatMulParams* p, int sms) {
+  Plan pl;
+  const int esz = kind == W_F16 ? 2 : 1;
+  pl.fast = p->M >= 1 && p->K > 0 && (p->N % 16 == 0) && sg::aligned16(p->B);
+  if (!pl.fast) return pl;
+  (void)esz;
+  pl.n_tiles = (p->N + kColsPerBlock - 1) / kColsPerBlock;
+  // chunks of 8 rows are the unit of work of one warp step
+  const long chunks = (p->K + kRowsPerChunk - 1) / kRowsPerChunk;
+  const long units = (long)pl.n_tiles * chunks;
+  const long target = (long)sms * 4 * kWarps * 2;  // ~2 chunks per warp, ~4 blocks per SM
+  long chunks_per_split = std::max<long>(kWarps, (units + target - 1) / target * kWarps);
+  chunks_per_split = std::min<long>(chunks_per_split, 4096 / kRowsPerChunk);  // x stage <= 16 KB
+  pl.rows_per_split = (int)(chunks_per_split * kRowsPerChunk);
+  pl.ksplit = (p->K + pl.rows_per_split - 1) / pl.rows_per_split;
+  const size_t xs_bytes = (size_t)pl.rows_per_split * 4;
+  const size_t red_bytes = (size_t)kWarps * kColsPerBlock * 4;
+  pl.smem = std::max(xs_bytes, red_bytes);
+  if (pl.ksplit > 1) {
+    pl.tickets_bytes = sg::align_up((size_t)pl.n_tiles * 4, 256);
+    pl.ws_bytes = pl.tickets_bytes + (size_t)pl.ksplit * p->N * 4;
+  }
+  return pl;
+}
+
+int kind_of(bool int8_weights, int a_dt) {
+  if (!int8_weights) return W_F16;
+  return a_dt == SG_DT_I8 ? W_INT8_IA : W_INT8_FA;
+}
+
+SgStatus validate(const char* name, const SgMatMulParams* p, bool int8_weights) {
+  SG_CHECK_ARG(p != nullptr, "%s: params is NULL", name);
+  SG_CHECK_ARG(p->M >= 0 && p->K >= 0 && p->N >= 0, "%s: negative size", name);
+  if (p->M == 0 || p->N == 0) return SG_OK;
+  SG_CHECK_ARG(p->C != nullptr, "%s: C is NULL", name);
+  SG_CHECK_ARG(p->K == 0 || (p->A && p->B), "%s: A and B must be non-NULL", name);
+  SG_CHECK_ARG(!int8_weights || p->scales_B, "%s: scales_B must be non-NULL", name);
+  SG_CHECK_ARG(p->ldb <= 0 || p->ldb == p->N, "%s: ldb must be N", name);
+  SG_CHECK_ARG(p->lda <= 0 || p->lda >= p->K, "%s: lda < K", name);
+  SG_CHECK_ARG(p->ldc <= 0 || p->ldc >= p->N, "%s: ldc < N", name);
+  const int adt = p->a_dtype == SG_DT_DEFAULT ? (int8_weights ? SG_DT_I8 : SG_DT_F16) : p->a_dtype;
+  SG_CHECK_ARG(adt >= SG_DT_F32 && adt <= SG_DT_I8, "%s: bad a_dtype %d", name, p->a_dtype);
+  const int cdt = p->c_dtype == SG_DT_DEFAULT ? (int8_weights ? SG_DT_F32 : SG_DT_F16) : p->c_dtype;
+  SG_CHECK_ARG(cdt == SG_DT_F32 || cdt == SG_DT_F16 || cdt == SG_DT_BF16, "%s: bad c_dtype %d", name,
+               p->c_dtype);
+  return SG_OK;
+}
+
+SgStatus dense_run(const char* name, const SgMatMulParams* p, void* stream, bool int8_weights) {
+  SgStatus st = validate(name, p, int8_weights);
+  if (st != SG_OK) return st;
+  if (p->M == 0 || p->N == 0) return SG_OK;
+  int dev = 0;
+  st = sg::current_device(&dev);
+  if (st != SG_OK) return st;
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+
+  DArgs a{};
+  a.A = p->A;
+  a.B = static_cast<const uint8_t*>(p->B);
+  a.scales = static_cast<const float*>(p->scales_B);
+  a.bias = static_cast<const __half*>(p->bias);
+  a.C = p->C;
+  a.M = p->M;
+  a.K = p->K;
+  a.N = p->N;
+  a.lda = p->lda > 0 ? p->lda : p->K;
+  a.ldc = p->ldc > 0 ? p->ldc : p->N;
+  a.a_dt = p->a_dtype == SG_DT_DEFAULT ? (int8_weights ? SG_DT_I8 : SG_DT_F16) : p->a_dtype;
+  a.c_dt = p->c_dtype == SG_DT_DEFAULT ? (int8_weights ? SG_DT_F32 : SG_DT_F16) : p->c_dtype;
+  a.scale_A = p->scale_A;
+  const int kind = kind_of(int8_weights, a.a_dt);
+
+  const Plan pl = make_plan(kind, p, sg::sm_count(dev));
+  if (!pl.fast) {
+    dim3 grid((p->N + 127) / 128, p->M);
+    switch (kind) {
+      case W_INT8_IA: dense_gemv_generic_kernel<W_INT8_IA><<<grid, 128, 0, cs>>>(a); break;
+      case W_INT8_FA: dense_gemv_generic_kernel<W_INT8_FA><<<grid, 128, 0, cs>>>(a); break;
+      default: dense_gemv_generic_kernel<W_F16><<<grid, 128, 0, cs>>>(a); break;
+    }
+    return sg::check_launch(name);
+  }
+  a.rows_per_split = pl.rows_per_split;
+  a.ksplit = pl.ksplit;
+  if (pl.ksplit > 1) {
+    void* ws = p->workspace;
+    if (ws == nullptr) {
+      st = sg::library_workspace(stream, pl.ws_bytes, &ws);
+      if (st != SG_OK) return st;
+    } else {
+      SG_CHECK_ARG(p->workspace_bytes >= pl.ws_bytes && sg::aligned16(ws),
+                   "%s: workspace too small or unaligned (%zu < %zu bytes)", name, p->workspace_bytes,
+                   pl.ws_bytes);
+    }
+    a.tickets = static_cast<unsigned*>(ws);
+    a.partial = reinterpret_cast<float*>(static_cast<char*>(ws) + pl.tickets_bytes);
+  }
+  dim3 grid(pl.n_tiles, pl.ksplit);
+  for (int m = 0; m < p->M; ++m) {
+    DArgs ar = a;
+    ar.M = 1;
+    ar.A = static_cast<const char*>(p->A) + (size_t)m * a.lda * sg::elem_size(a.a_dt);
+    ar.C = static_cast<char*>(p->C) + (size_t)m * a.ldc * sg::elem_size(a.c_dt);
+    switch (kind) {
+      case W_INT8_IA: dense_gemv_kernel<W_INT8_IA><<<grid, kThreads, pl.smem, cs>>>(ar); break;
+      case W_INT8_FA: dense_gemv_kernel<W_INT8_FA><<<grid, kThreads, pl.smem, cs>>>(ar); break;
+      default: dense_gemv_kernel<W_F16><<<grid, kThreads, pl.smem, cs>>>(ar); break;
+    }
+    st = sg::check_launch(name);
+    if (st != SG_OK) return st;
+  }
+  return SG_OK;
+}
+
+size_t dense_ws(const SgMatMulParams* p, bool int8_weights) {
+  if (validate("workspace_size", p, int8_weights) != SG_OK || p->M == 0 || p->N == 0) return 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    dev = 0;
+  }
+  const int adt = p->a_dtype == SG_DT_DEFAULT ? (int8_weights ? SG_DT_I8 : SG_DT_F16) : p->a_dtype;
+  return make_plan(kind_of(int8_weights, adt), p, sg::sm_count(dev)).ws_bytes;
+}
+
+}  // namespace
+
+extern "C" {
+
+SgStatus sg_matmul_int8_channel(const SgMatMulParams* p, void* stream) {
+  return dense_run("sg_matmul_int8_channel", p, stream, true);
+}
+size_t sg_matmul_int8_channel_workspace_size(const SgMatMulParams* p) { return dense_ws(p, true); }
+
+SgStatus sg_matmul_fp16(const SgMatMulParams* p, void* stream) {
+  return dense_run("sg_matmul_fp16", p, stream, false);
+}
+size_t sg_matmul_fp16_workspace_size(const SgMatMulParams* p) { return dense_ws(p, false); }
+
+}  // extern "C"

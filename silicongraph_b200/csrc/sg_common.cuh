@@ -1,0 +1,134 @@
+// Shared host/device helpers for the SiliconGraph-B200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+
+#include "sg_kernels.h"
+
+namespace sg {
+
+// ------------------------------------------------------------------ errors
+// Thread-local last-error message (sg_last_error()).
+void set_error(const char* fmt, ...);
+const char* last_error();
+
+#define SG_CHECK_ARG(cond, ...)          \
+  do {                                   \
+    if (!(cond)) {                       \
+      ::sg::set_error(__VA_ARGS__);      \
+      return SG_ERR_INVALID;             \
+    }                                    \
+  } while (0)
+
+#define SG_CUDA_TRY(expr)                                                               \
+  do {                                                                                  \
+    cudaError_t e_ = (expr);                                                            \
+    if (e_ != cudaSuccess) {                                                            \
+      ::sg::set_error("%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, \
+                      __LINE__);                                                        \
+      return SG_ERR_RUNTIME;                                                            \
+    }                                                                                   \
+  } while (0)
+
+// After a launch: report configuration errors (bad grid, smem, ...).
+SgStatus check_launch(const char* what);
+
+// Current device ordinal, or error if no usable device.
+SgStatus current_device(int* dev);
+
+// Number of SMs of the current device (cached per device).
+int sm_count(int dev);
+
+// ---------------------------------------------------------------- workspace
+// Library-owned scratch, one buffer per (device, stream), grown on demand and
+// zero-filled when (re)allocated.  Growth synchronises the device, so the
+// first call with a larger shape must not run under stream capture.
+SgStatus library_workspace(void* stream, size_t bytes, void** out);
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// ------------------------------------------------------------------ dtypes
+inline int elem_size(int dt) {
+  switch (dt) {
+    case SG_DT_F32: return 4;
+    case SG_DT_F16:
+    case SG_DT_BF16: return 2;
+    case SG_DT_I8: return 1;
+    default: return 0;
+  }
+}
+
+inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+}  // namespace sg
+
+// ------------------------------------------------------------ device helpers
+namespace sgd {
+
+template <int DT>
+__device__ __forceinline__ float load_as_float(const void* p, int64_t i);
+template <>
+__device__ __forceinline__ float load_as_float<SG_DT_F32>(const void* p, int64_t i) {
+  return static_cast<const float*>(p)[i];
+}
+template <>
+__device__ __forceinline__ float load_as_float<SG_DT_F16>(const void* p, int64_t i) {
+  return __half2float(static_cast<const __half*>(p)[i]);
+}
+template <>
+__device__ __forceinline__ float load_as_float<SG_DT_BF16>(const void* p, int64_t i) {
+  return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+}
+template <>
+__device__ __forceinline__ float load_as_float<SG_DT_I8>(const void* p, int64_t i) {
+  return (float)static_cast<const int8_t*>(p)[i];
+}
+
+template <int DT>
+__device__ __forceinline__ void store_from_float(void* p, int64_t i, float v);
+template <>
+__device__ __forceinline__ void store_from_float<SG_DT_F32>(void* p, int64_t i, float v) {
+  static_cast<float*>(p)[i] = v;
+}
+template <>
+__device__ __forceinline__ void store_from_float<SG_DT_F16>(void* p, int64_t i, float v) {
+  static_cast<__half*>(p)[i] = __float2half_rn(v);
+}
+template <>
+__device__ __forceinline__ void store_from_float<SG_DT_BF16>(void* p, int64_t i, float v) {
+  static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+}
+
+// 128-bit streaming load that does not allocate in L1 (weights are read once).
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t orv) {
+  uint32_t d;
+  // (a & mask) | orv  -> immLut = (0xF0 & 0xCC) | 0xAA = 0xEA
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(mask), "r"(orv));
+  return d;
+}
+
+// Packed fp32x2 FMA (sm_100): d = a * b + c, lane-wise, round-to-nearest.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  uint64_t ra, rb, rc, rd;
+  ra = ((uint64_t)__float_as_uint(a.y) << 32) | __float_as_uint(a.x);
+  rb = ((uint64_t)__float_as_uint(b.y) << 32) | __float_as_uint(b.x);
+  rc = ((uint64_t)__float_as_uint(c.y) << 32) | __float_as_uint(c.x);
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(rd) : "l"(ra), "l"(rb), "l"(rc));
+  return make_float2(__uint_as_float((uint32_t)rd), __uint_as_float((uint32_t)(rd >> 32)));
+}
+
+}  // namespace sgd

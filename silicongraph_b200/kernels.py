@@ -1,0 +1,93 @@
+"""Host-side mirror of the reference kernel table, over the C ABI.
+
+The reference calls ``matmul_int4_grouped_neon(const MatMulParams&)`` and
+``flash_attention_fp16(const FlashAttentionParams&)`` directly
+(compiler/kernels/cpu/matmul_neon.h:9,113; flash_attention.h:95).  These
+functions take the same parameters -- as torch CUDA tensors, which supply
+device memory and the current stream -- fill the C structs of
+``include/sg_kernels.h`` and call the native library.  Nothing here computes
+on the CPU; a missing library or device raises.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import (SG_DT_BF16, SG_DT_DEFAULT, SG_DT_F16, SG_DT_F32, SG_DT_I8, SgFlashAttentionParams,
+                   SgMatMulParams, check)
+
+_TORCH_DT = {
+    torch.float32: SG_DT_F32,
+    torch.float16: SG_DT_F16,
+    torch.bfloat16: SG_DT_BF16,
+    torch.int8: SG_DT_I8,
+}
+
+
+def dtype_code(t: torch.dtype) -> int:
+    return _TORCH_DT[t]
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError("tensor must live on a CUDA device")
+    return t.data_ptr()
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, torch.cuda.Stream):
+        return stream.cuda_stream
+    return int(stream)
+
+
+def matmul_params(A, B, C, *, M: int, K: int, N: int, scales=None, zeros=None, bias=None,
+                  group_size: int = 0, scale_A: float = 1.0, lda: int = 0, ldc: int = 0,
+                  workspace: torch.Tensor | None = None) -> SgMatMulParams:
+    p = SgMatMulParams()
+    p.A = _ptr(A)
+    p.B = _ptr(B)
+    p.bias = _ptr(bias)
+    p.C = _ptr(C)
+    p.M, p.K, p.N = M, K, N
+    p.lda, p.ldb, p.ldc = lda, 0, ldc
+    p.scale_A = scale_A
+    p.scales_B = _ptr(scales)
+    p.zeros_B = _ptr(zeros)
+    p.group_size = group_size
+    p.a_dtype = dtype_code(A.dtype) if A is not None else SG_DT_DEFAULT
+    p.c_dtype = dtype_code(C.dtype)
+    if workspace is not None:
+        p.workspace = _ptr(workspace)
+        p.workspace_bytes = workspace.numel() * workspace.element_size()
+    return p
+
+
+def matmul_int4_grouped(A: torch.Tensor, B: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor | None,
+                        K: int, N: int, group_size: int, *, out_dtype=torch.float16, bias=None,
+                        scale_A: float = 1.0, C: torch.Tensor | None = None, stream=None,
+                        workspace=None) -> torch.Tensor:
+    """C[M, N] = A[M, K] @ dequant(B) -- the reference INT4 layout (matmul_neon.h:113-143)."""
+    M = A.shape[0] if A.dim() == 2 else 1
+    if C is None:
+        C = torch.empty((M, N), dtype=out_dtype, device=A.device)
+    p = matmul_params(A, B, C, M=M, K=K, N=N, scales=scales, zeros=zeros, bias=bias,
+                      group_size=group_size, scale_A=scale_A, workspace=workspace)
+    check(_lib.load().sg_matmul_int4_grouped(ctypes.byref(p), _stream(stream)))
+    return C
+
+
+def matmul_int4_grouped_workspace_size(A, B, scales, zeros, K, N, group_size, out_dtype=torch.float16) -> int:
+    M = A.shape[0] if A.dim() == 2 else 1
+    C = torch.empty((M, N), dtype=out_dtype, device=A.device)
+    p = matmul_params(A, B, C, M=M, K=K, N=N, scales=scales, zeros=zeros, group_size=group_size)
+    return int(_lib.load().sg_matmul_int4_grouped_workspace_size(ctypes.byref(p)))
+
+
+def set_tuning(key: str, value: int) -> None:
+    check(_lib.load().sg_set_tuning(key.encode(), int(value)))

@@ -1,0 +1,258 @@
+"""Parity of the CUDA linear kernels with the oracle and the reference goldens,
+called through the C ABI (silicongraph_b200.kernels -> libsg_b200.so).
+
+Tolerance for floating outputs: |got - want| <= 2e-3 + 1e-2 |want|.
+Integer work (packing, unpacking, int8 x int8) is compared bit for bit."""
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, golden
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-2, 2e-3
+DEV = "cuda"
+
+
+def close(got, want, rtol=RTOL, atol=ATOL):
+    got = np.asarray(got, np.float32)
+    want = np.asarray(want, np.float32)
+    err = np.abs(got - want)
+    bad = err > atol + rtol * np.abs(want)
+    assert not bad.any(), f"{bad.sum()} / {bad.size} outside tolerance; max err {err.max():.3e}"
+
+
+def t(a, dtype=None):
+    x = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None:
+        x = x.to(dtype)
+    return x.to(DEV)
+
+
+def bf16_tensor(a32):
+    return torch.from_numpy(np.ascontiguousarray(a32, np.float32)).to(torch.bfloat16).to(DEV)
+
+
+def w4_problem(oracle, K, N, gs, seed=0, sym=False):
+    rng = np.random.default_rng(seed)
+    W = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+    B, S, Z = oracle.quantize_int4_grouped(W, gs, sym)
+    return B, S, Z
+
+
+INT4_CASES = sorted(os.path.basename(p) for p in glob.glob(os.path.join(GOLDEN, "int4_gemv_*.npz")))
+
+
+@pytest.mark.parametrize("name", INT4_CASES)
+def test_int4_gemv_matches_reference_golden(sg, name):
+    g = golden(name)
+    K, N, gs = int(g["K"]), int(g["N"]), int(g["gs"])
+    Z = t(g["Z"]) if "Z" in g else None
+    C = sg.matmul_int4_grouped(t(g["A"]).view(1, K), t(g["B"]), t(g["S"]), Z, K, N, gs)
+    close(C.cpu().numpy().ravel(), g["C"])
+
+
+@pytest.mark.parametrize("K,N,gs", [(127, 33, 16), (96, 20, 7), (130, 40, 32), (64, 24, 0)])
+def test_int4_generic_path_bitexact(sg, oracle_mod, K, N, gs):
+    """Shapes outside the fast path run the reference's loop order exactly."""
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=K)
+    rng = np.random.default_rng(1)
+    A = rng.standard_normal((2, K)).astype(np.float32)
+    want = oracle_mod.matmul_int4_grouped(A, B, S, Z, K, N, gs, M=2, c_dt=oracle_mod.DT_F32)
+    C = sg.matmul_int4_grouped(t(A), t(B), t(S), t(Z), K, N, gs, out_dtype=torch.float32)
+    assert np.array_equal(C.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("K,N,gs,sym", [
+    (4096, 14336, 32, False),   # the INT4 GEMV benchmark shape (x fp32 [1, 4096])
+    (2048, 8192, 64, True),
+    (4096, 512, 128, False),
+    (272, 48, 16, False),       # single split
+    (4000, 1024, 32, False),    # partial last group
+    (18944, 3584, 128, False),  # Qwen-7B down projection
+])
+def test_int4_fast_path_fp32_activation(sg, oracle_mod, K, N, gs, sym):
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=N, sym=sym)
+    x = np.random.default_rng(K).standard_normal((1, K)).astype(np.float32)
+    want = oracle_mod.matmul_int4_grouped(x, B, S, Z, K, N, gs, c_dt=oracle_mod.DT_F32)
+    C = sg.matmul_int4_grouped(t(x), t(B), t(S), t(Z) if Z is not None else None, K, N, gs,
+                               out_dtype=torch.float32)
+    close(C.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8])
+@pytest.mark.parametrize("adt", ["f32", "f16", "bf16", "i8"])
+def test_int4_rows_and_dtypes(sg, oracle_mod, M, adt):
+    K, N, gs = 1024, 1536, 32
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=11)
+    rng = np.random.default_rng(M)
+    x32 = rng.standard_normal((M, K)).astype(np.float32)
+    bias = (0.1 * rng.standard_normal(N)).astype(np.float16)
+    if adt == "f32":
+        xo, xt, kw = x32, t(x32), {}
+    elif adt == "f16":
+        xo = x32.astype(np.float16)
+        xt, kw = t(xo), {}
+    elif adt == "bf16":
+        xo = oracle_mod.f32_to_bf16_bits(x32)
+        xt, kw = bf16_tensor(x32), {"a_bf16": True}
+    else:
+        xo = rng.integers(-128, 128, (M, K), dtype=np.int8)
+        xt, kw = t(xo), {}
+    scale_A = 0.05 if adt == "i8" else 1.0
+    for cdt, tdt in ((oracle_mod.DT_F32, torch.float32), (oracle_mod.DT_F16, torch.float16)):
+        want = oracle_mod.matmul_int4_grouped(xo, B, S, Z, K, N, gs, M=M, bias=bias, c_dt=cdt,
+                                              scale_A=scale_A, **kw)
+        C = sg.matmul_int4_grouped(xt, t(B), t(S), t(Z), K, N, gs, out_dtype=tdt, bias=t(bias),
+                                   scale_A=scale_A)
+        close(C.float().cpu().numpy(), want.astype(np.float32))
+
+
+def test_int4_bf16_output(sg, oracle_mod):
+    K, N, gs = 512, 1024, 64
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=5)
+    x = np.random.default_rng(9).standard_normal((1, K)).astype(np.float32)
+    want = oracle_mod.matmul_int4_grouped(x, B, S, Z, K, N, gs, c_dt=oracle_mod.DT_F32)
+    C = sg.matmul_int4_grouped(t(x), t(B), t(S), t(Z), K, N, gs, out_dtype=torch.bfloat16)
+    close(C.float().cpu().numpy(), want, rtol=1e-2, atol=1e-2)
+
+
+def test_int4_deterministic_and_k0(sg, oracle_mod):
+    K, N, gs = 4096, 2048, 32
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=2)
+    x = t(np.random.default_rng(0).standard_normal((1, K)).astype(np.float32))
+    a = sg.matmul_int4_grouped(x, t(B), t(S), t(Z), K, N, gs, out_dtype=torch.float32)
+    b = sg.matmul_int4_grouped(x, t(B), t(S), t(Z), K, N, gs, out_dtype=torch.float32)
+    assert torch.equal(a, b)
+    # K == 0: the reference writes zeros (acc never updated)
+    C = torch.full((1, 16), 7.0, dtype=torch.float16, device=DEV)
+    sg.matmul_int4_grouped(x[:, :0], t(B), t(S), t(Z), 0, 16, gs, C=C)
+    assert (C == 0).all()
+
+
+def test_int4_caller_workspace(sg, oracle_mod):
+    from silicongraph_b200._lib import SgError
+    K, N, gs = 4096, 4096, 32
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=3)
+    x = t(np.random.default_rng(4).standard_normal((1, K)).astype(np.float32))
+    args = (x, t(B), t(S), t(Z), K, N, gs)
+    need = sg.matmul_int4_grouped_workspace_size(*args, out_dtype=torch.float32)
+    assert need > 0
+    ws = torch.zeros(need, dtype=torch.uint8, device=DEV)
+    a = sg.matmul_int4_grouped(*args, out_dtype=torch.float32, workspace=ws)
+    b = sg.matmul_int4_grouped(*args, out_dtype=torch.float32)
+    assert torch.equal(a, b)
+    a2 = sg.matmul_int4_grouped(*args, out_dtype=torch.float32, workspace=ws)  # tickets were reset
+    assert torch.equal(a, a2)
+    with pytest.raises(SgError):
+        sg.matmul_int4_grouped(*args, out_dtype=torch.float32, workspace=ws[: need // 2])
+
+
+@pytest.mark.parametrize("gpw", [1, 2, 4, 8])
+def test_int4_split_granularity_invariant(sg, oracle_mod, gpw):
+    K, N, gs = 4096, 14336, 32
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=7)
+    x = np.random.default_rng(8).standard_normal((1, K)).astype(np.float32)
+    want = oracle_mod.matmul_int4_grouped(x, B, S, Z, K, N, gs, c_dt=oracle_mod.DT_F32)
+    try:
+        sg.set_tuning("w4_gemv.groups_per_warp", gpw)
+        C = sg.matmul_int4_grouped(t(x), t(B), t(S), t(Z), K, N, gs, out_dtype=torch.float32)
+    finally:
+        sg.set_tuning("w4_gemv.groups_per_warp", 0)
+    close(C.cpu().numpy(), want)
+
+
+# ------------------------------------------------------------------ packer
+@pytest.mark.parametrize("K,N,gs,sym", [(256, 64, 32, False), (127, 33, 16, True), (96, 20, 7, False),
+                                        (4096, 1024, 32, False), (130, 48, 0, False)])
+def test_device_packer_bitexact(sg, oracle_mod, K, N, gs, sym):
+    import ctypes
+    from silicongraph_b200 import _lib
+    rng = np.random.default_rng(K + N)
+    W = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+    W[: min(K, 5), 0] = 0.0  # a degenerate-ish column start
+    B0, S0, Z0 = oracle_mod.quantize_int4_grouped(W, gs, sym)
+    Wd = t(W)
+    B = torch.zeros(B0.shape, dtype=torch.uint8, device=DEV)
+    S = torch.zeros(S0.shape, dtype=torch.float16, device=DEV)
+    Z = torch.zeros(S0.shape, dtype=torch.int8, device=DEV)
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.check(_lib.load().sg_quantize_int4_grouped(Wd.data_ptr(), K, N, gs, int(sym), B.data_ptr(),
+                                                     S.data_ptr(), None if sym else Z.data_ptr(), st))
+    assert np.array_equal(B.cpu().numpy(), B0)
+    assert np.array_equal(S.cpu().numpy().view(np.uint16), S0.view(np.uint16))
+    if not sym:
+        assert np.array_equal(Z.cpu().numpy(), Z0)
+    # unpack
+    Wq = torch.zeros((K, N), dtype=torch.float32, device=DEV)
+    _lib.check(_lib.load().sg_dequantize_int4_grouped(B.data_ptr(), S.data_ptr(),
+                                                       None if sym else Z.data_ptr(), K, N, gs,
+                                                       Wq.data_ptr(), st))
+    want = oracle_mod.dequant_int4_grouped(B0, S0, Z0, K, N, gs)
+    assert np.array_equal(Wq.cpu().numpy(), want)
+    del ctypes
+
+
+# ------------------------------------------------------------------ int8 / fp16
+def _mm(sg, fn, A, B, C, M, K, N, scales=None, bias=None, scale_A=1.0):
+    import ctypes
+    from silicongraph_b200 import _lib
+    p = sg.matmul_params(A, B, C, M=M, K=K, N=N, scales=scales, bias=bias, scale_A=scale_A)
+    _lib.check(getattr(_lib.load(), fn)(ctypes.byref(p), torch.cuda.current_stream().cuda_stream))
+    return C
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 2048, 8192), (1, 37, 20), (3, 1000, 512), (1, 4096, 14336)])
+def test_int8_channel_int8_activations_bitexact(sg, oracle_mod, M, K, N):
+    rng = np.random.default_rng(K)
+    A = rng.integers(-128, 128, (M, K), dtype=np.int8)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    s = (rng.random(N) * 0.01).astype(np.float32)
+    want = oracle_mod.gemm_int8_channel(A, B, s, M, K, N, 0.02)
+    C = torch.zeros((M, N), dtype=torch.float32, device=DEV)
+    _mm(sg, "sg_matmul_int8_channel", t(A), t(B), C, M, K, N, scales=t(s), scale_A=0.02)
+    assert np.array_equal(C.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("M,K,N,adt", [(1, 2048, 8192, "bf16"), (2, 1024, 1024, "f32"), (1, 100, 48, "f16")])
+def test_int8_channel_float_activations(sg, oracle_mod, M, K, N, adt):
+    rng = np.random.default_rng(N)
+    x32 = rng.standard_normal((M, K)).astype(np.float32)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    s = (rng.random(N) * 1e-3).astype(np.float32)
+    if adt == "bf16":
+        xo, xt, kw = oracle_mod.f32_to_bf16_bits(x32), bf16_tensor(x32), {"a_bf16": True}
+    elif adt == "f16":
+        xo = x32.astype(np.float16)
+        xt, kw = t(xo), {}
+    else:
+        xo, xt, kw = x32, t(x32), {}
+    want = oracle_mod.gemm_w8_channel(xo, B, s, M, K, N, **kw)
+    C = torch.zeros((M, N), dtype=torch.float32, device=DEV)
+    _mm(sg, "sg_matmul_int8_channel", xt, t(B), C, M, K, N, scales=t(s))
+    close(C.cpu().numpy(), want)
+
+
+def test_fp16_gemv_matches_reference_golden(sg):
+    g = golden("fp16_gemv.npz")
+    K, N = g["B"].shape
+    C = torch.zeros((1, N), dtype=torch.float16, device=DEV)
+    _mm(sg, "sg_matmul_fp16", t(g["A"]).view(1, K), t(g["B"]), C, 1, K, N)
+    close(C.cpu().numpy().ravel(), g["C_neon"])
+    _mm(sg, "sg_matmul_fp16", t(g["A"]).view(1, K), t(g["B"]), C, 1, K, N, bias=t(g["bias"]))
+    close(C.cpu().numpy().ravel(), g["C_neon_bias"])
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 2048, 8192), (2, 333, 64), (1, 64, 40)])
+def test_fp16_gemv_vs_oracle(sg, oracle_mod, M, K, N):
+    rng = np.random.default_rng(M * K)
+    A = rng.standard_normal((M, K)).astype(np.float16)
+    B = (0.02 * rng.standard_normal((K, N))).astype(np.float16)
+    want = oracle_mod.matmul_f16w(A, B, None, M, K, N, c_dt=oracle_mod.DT_F32)
+    C = torch.zeros((M, N), dtype=torch.float32, device=DEV)
+    _mm(sg, "sg_matmul_fp16", t(A), t(B), C, M, K, N)
+    close(C.cpu().numpy(), want)
