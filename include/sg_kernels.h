@@ -108,8 +108,13 @@ const char* sg_last_error(void);
 int32_t sg_version(void);       /* (major << 16) | (minor << 8) | patch */
 /* Number of CUDA devices usable by the library (0 when none). */
 int32_t sg_device_count(void);
+/* Read and clear the device-side error word of the current device (waits on
+ * `stream`).  Kernels whose internal waits are bounded record a timeout there
+ * instead of hanging; returns SG_ERR_RUNTIME with a message if one was set. */
+int32_t sg_device_error_check(void* stream);
 /* Override a launch heuristic (benchmark sweeps).  Keys:
- *   "w4_gemv.groups_per_warp"  INT4 GEMV split-K granularity (0 = heuristic)
+ *   "w4_gemv.groups_per_warp"  INT4 GEMV (CUDA-core path) split-K granularity (0 = heuristic)
+ *   "w4_gemv.path"             INT4 GEMV path: 0 auto, 1 CUDA-core, 2 generic
  * Returns SG_ERR_NOT_FOUND for an unknown key.  No reference counterpart. */
 int32_t sg_set_tuning(const char* key, int32_t value);
 

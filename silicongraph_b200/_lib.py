@@ -87,6 +87,7 @@ _SIGS = {
     "sg_version": (ctypes.c_int32, []),
     "sg_device_count": (ctypes.c_int32, []),
     "sg_set_tuning": (ctypes.c_int32, [ctypes.c_char_p, ctypes.c_int32]),
+    "sg_device_error_check": (ctypes.c_int32, [_P]),
     "sg_matmul_int4_grouped": (ctypes.c_int32, [ctypes.POINTER(SgMatMulParams), _P]),
     "sg_matmul_int4_grouped_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(SgMatMulParams)]),
     "sg_matmul_int8_channel": (ctypes.c_int32, [ctypes.POINTER(SgMatMulParams), _P]),

@@ -131,4 +131,20 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
   return make_float2(__uint_as_float((uint32_t)rd), __uint_as_float((uint32_t)(rd >> 32)));
 }
 
+// Element i of a uint4 / fp16 / int8 lane of packed registers, for indices
+// that are compile-time constants after unrolling (keeps values in registers).
+__device__ __forceinline__ uint32_t u4_get(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+// fp16 number cc (0..15) of 16 packed halves held in (lo: 0..7, hi: 8..15).
+__device__ __forceinline__ float half16_at(const uint4& lo, const uint4& hi, int cc) {
+  const uint32_t w = u4_get(cc < 8 ? lo : hi, (cc & 7) >> 1);
+  return __half2float(__ushort_as_half((unsigned short)(w >> ((cc & 1) * 16))));
+}
+// int8 number cc (0..15) of 16 packed bytes.
+__device__ __forceinline__ int i8x16_at(const uint4& v, int cc) {
+  const uint32_t w = u4_get(v, cc >> 2);
+  return (int)(int8_t)(w >> ((cc & 3) * 8));
+}
+
 }  // namespace sgd

@@ -1,8 +1,11 @@
 // Library runtime: error reporting, device queries, library-owned scratch.
+#include <cudaTypedefs.h>
+
+#include <cstring>
 #include <mutex>
 #include <unordered_map>
 
-#include "sg_common.cuh"
+#include "sm100.cuh"
 
 namespace sg {
 
@@ -28,6 +31,12 @@ std::unordered_map<WsKey, WsBuf, WsKeyHash> g_ws;
 
 std::mutex g_sm_mu;
 std::unordered_map<int, int> g_sm;
+
+std::mutex g_err_mu;
+std::unordered_map<int, int*> g_err_word;
+
+std::mutex g_tm_mu;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 }  // namespace
 
 void set_error(const char* fmt, ...) {
@@ -104,9 +113,82 @@ SgStatus library_workspace(void* stream, size_t bytes, void** out) {
   return SG_OK;
 }
 
+SgStatus device_error_word(int** out) {
+  int dev = 0;
+  SgStatus st = current_device(&dev);
+  if (st != SG_OK) return st;
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  auto it = g_err_word.find(dev);
+  if (it != g_err_word.end()) {
+    *out = it->second;
+    return SG_OK;
+  }
+  int* p = nullptr;
+  SG_CUDA_TRY(cudaMalloc(&p, 256));
+  SG_CUDA_TRY(cudaMemset(p, 0, 256));
+  g_err_word[dev] = p;
+  *out = p;
+  return SG_OK;
+}
+
+SgStatus make_tensor_map(CUtensorMap* out, CUtensorMapDataType dt, int rank, void* base, const uint64_t* dims,
+                         const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz) {
+  {
+    std::lock_guard<std::mutex> lk(g_tm_mu);
+    if (!g_encode) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+      if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
+        cudaGetLastError();
+        set_error("cuTensorMapEncodeTiled unavailable");
+        return SG_ERR_RUNTIME;
+      }
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  }
+  cuuint64_t gdim[5];
+  cuuint64_t gstride[4];
+  cuuint32_t bdim[5];
+  cuuint32_t estride[5];
+  for (int i = 0; i < rank; ++i) {
+    gdim[i] = dims[i];
+    bdim[i] = box[i];
+    estride[i] = 1;
+    if (i + 1 < rank) gstride[i] = strides_bytes[i];
+  }
+  CUresult r = g_encode(out, dt, (cuuint32_t)rank, base, gdim, gstride, bdim, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (code %d)", (int)r);
+    return SG_ERR_INVALID;
+  }
+  return SG_OK;
+}
+
 }  // namespace sg
 
 extern "C" {
+
+int32_t sg_device_error_check(void* stream) {
+  int* w = nullptr;
+  if (sg::device_error_word(&w) != SG_OK) return SG_ERR_RUNTIME;
+  int v = 0;
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(&v, w, sizeof(int), cudaMemcpyDeviceToHost, cs) != cudaSuccess ||
+      cudaStreamSynchronize(cs) != cudaSuccess) {
+    cudaGetLastError();
+    sg::set_error("sg_device_error_check: copy failed");
+    return SG_ERR_RUNTIME;
+  }
+  if (v != 0) {
+    cudaMemsetAsync(w, 0, sizeof(int), cs);
+    cudaStreamSynchronize(cs);
+    sg::set_error("device-side error %d (1 = a bounded wait timed out)", v);
+    return SG_ERR_RUNTIME;
+  }
+  return SG_OK;
+}
 
 const char* sg_last_error(void) { return sg::last_error(); }
 

@@ -28,7 +28,7 @@
 #include <atomic>
 #include <string_view>
 
-#include "sg_common.cuh"
+#include "sm100.cuh"
 
 namespace {
 
@@ -40,6 +40,7 @@ constexpr int kRowsPerChunk = 8;
 constexpr int kMaxRowsPerLaunch = 4;
 
 std::atomic<int> g_tune_groups_per_warp{0};  // 0 = heuristic
+std::atomic<int> g_tune_path{0};              // 0 = auto, 1 = CUDA-core kernel, 2 = generic kernel
 
 struct W4Args {
   const void* A;
@@ -376,9 +377,16 @@ SgStatus launch_fast(const W4Args& a, const Plan& pl, cudaStream_t st) {
 
 }  // namespace
 
-// Core entry with an explicit scratch buffer (NULL -> library scratch).
+namespace sg {
+size_t w4_gemv_mma_scratch_bytes(const SgMatMulParams* p, int sms, bool* applicable);
+SgStatus w4_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, void* ws, size_t ws_bytes,
+                         int* err_word, bool* handled);
+}  // namespace sg
+
+// Core entry.  ws == NULL: library scratch (unless ws_external, then an error
+// if scratch is needed).  err_word == NULL: the library's per-device error word.
 static SgStatus w4_run(const SgMatMulParams* p, void* stream, void* ws, size_t ws_bytes,
-                       bool ws_external) {
+                       bool ws_external, int* err_word) {
   SgStatus st = validate(p);
   if (st != SG_OK) return st;
   if (p->M == 0 || p->N == 0) return SG_OK;
@@ -407,7 +415,31 @@ static SgStatus w4_run(const SgMatMulParams* p, void* stream, void* ws, size_t w
   a.c_dt = p->c_dtype == SG_DT_DEFAULT ? SG_DT_F16 : p->c_dtype;
   a.scale_A = p->scale_A;
 
-  const Plan pl = make_plan(p, sms);
+  const int path = g_tune_path.load();
+  // One activation row and groups of 32k: tensor-core reduction (w4_gemv_mma.cu).
+  bool mma_ok = false;
+  const size_t mma_ws = sg::w4_gemv_mma_scratch_bytes(p, sms, &mma_ok);
+  if (mma_ok && path == 0) {
+    if (ws == nullptr) {
+      if (ws_external) {
+        sg::set_error("sg_matmul_int4_grouped: scratch required (%zu bytes)", mma_ws);
+        return SG_ERR_INVALID;
+      }
+      st = sg::library_workspace(stream, mma_ws, &ws);
+      if (st != SG_OK) return st;
+      ws_bytes = mma_ws;
+    }
+    if (err_word == nullptr) {
+      st = sg::device_error_word(&err_word);
+      if (st != SG_OK) return st;
+    }
+    bool handled = false;
+    st = sg::w4_gemv_mma_run(p, cs, sms, ws, ws_bytes, err_word, &handled);
+    if (handled || st != SG_OK) return st;
+  }
+
+  Plan pl = make_plan(p, sms);
+  if (path == 2) pl.fast = false;
   if (!pl.fast) {
     dim3 grid((p->N + 127) / 128, p->M);
     w4_gemv_generic_kernel<<<grid, 128, 0, cs>>>(a);
@@ -449,9 +481,10 @@ static SgStatus w4_run(const SgMatMulParams* p, void* stream, void* ws, size_t w
 }
 
 namespace sg {
-// Shared with the fixed-scratch entry point.
-SgStatus w4_gemv_run(const SgMatMulParams* p, void* stream, void* ws, size_t ws_bytes, bool ws_external) {
-  return w4_run(p, stream, ws, ws_bytes, ws_external);
+// Entry with caller-chosen scratch and error word (see w4_run).
+SgStatus w4_gemv_run(const SgMatMulParams* p, void* stream, void* ws, size_t ws_bytes, bool ws_external,
+                     int* err_word) {
+  return w4_run(p, stream, ws, ws_bytes, ws_external, err_word);
 }
 size_t w4_gemv_scratch_bytes(const SgMatMulParams* p) {
   if (validate(p) != SG_OK || p->M == 0 || p->N == 0) return 0;
@@ -460,15 +493,21 @@ size_t w4_gemv_scratch_bytes(const SgMatMulParams* p) {
     cudaGetLastError();
     dev = 0;
   }
-  return make_plan(p, sm_count(dev)).ws_bytes;
+  const int sms = sm_count(dev);
+  const int path = g_tune_path.load();
+  bool mma_ok = false;
+  const size_t mws = w4_gemv_mma_scratch_bytes(p, sms, &mma_ok);
+  if (mma_ok && path == 0) return mws;
+  if (path == 2) return 0;
+  return make_plan(p, sms).ws_bytes;
 }
 }  // namespace sg
 
 extern "C" {
 
 SgStatus sg_matmul_int4_grouped(const SgMatMulParams* p, void* stream) {
-  if (p && p->workspace) return w4_run(p, stream, p->workspace, p->workspace_bytes, true);
-  return w4_run(p, stream, nullptr, 0, false);
+  if (p && p->workspace) return w4_run(p, stream, p->workspace, p->workspace_bytes, true, nullptr);
+  return w4_run(p, stream, nullptr, 0, false, nullptr);
 }
 
 size_t sg_matmul_int4_grouped_workspace_size(const SgMatMulParams* p) {
@@ -478,6 +517,10 @@ size_t sg_matmul_int4_grouped_workspace_size(const SgMatMulParams* p) {
 int32_t sg_set_tuning(const char* key, int32_t value) {
   if (key && std::string_view(key) == "w4_gemv.groups_per_warp") {
     g_tune_groups_per_warp.store(value);
+    return SG_OK;
+  }
+  if (key && std::string_view(key) == "w4_gemv.path") {
+    g_tune_path.store(value);
     return SG_OK;
   }
   sg::set_error("sg_set_tuning: unknown key");

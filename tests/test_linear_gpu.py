@@ -67,6 +67,15 @@ def test_int4_generic_path_bitexact(sg, oracle_mod, K, N, gs):
     assert np.array_equal(C.cpu().numpy(), want)
 
 
+@pytest.fixture(params=[0, 1], ids=["auto", "cudacore"])
+def w4_path(sg, request):
+    """Run under the automatic path choice (tensor-core kernel for one row) and
+    with the CUDA-core kernel forced."""
+    sg.set_tuning("w4_gemv.path", request.param)
+    yield request.param
+    sg.set_tuning("w4_gemv.path", 0)
+
+
 @pytest.mark.parametrize("K,N,gs,sym", [
     (4096, 14336, 32, False),   # the INT4 GEMV benchmark shape (x fp32 [1, 4096])
     (2048, 8192, 64, True),
@@ -74,14 +83,58 @@ def test_int4_generic_path_bitexact(sg, oracle_mod, K, N, gs):
     (272, 48, 16, False),       # single split
     (4000, 1024, 32, False),    # partial last group
     (18944, 3584, 128, False),  # Qwen-7B down projection
+    (2048, 1040, 32, False),    # N not a multiple of the 512-column tile
+    (96, 16, 32, False),        # tiny K: one partial chunk
+    (2048, 128256 // 8, 32, False),  # a TP-8 shard of a Llama-3 lm_head
 ])
-def test_int4_fast_path_fp32_activation(sg, oracle_mod, K, N, gs, sym):
+def test_int4_fast_path_fp32_activation(sg, oracle_mod, w4_path, K, N, gs, sym):
     B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=N, sym=sym)
     x = np.random.default_rng(K).standard_normal((1, K)).astype(np.float32)
     want = oracle_mod.matmul_int4_grouped(x, B, S, Z, K, N, gs, c_dt=oracle_mod.DT_F32)
     C = sg.matmul_int4_grouped(t(x), t(B), t(S), t(Z) if Z is not None else None, K, N, gs,
                                out_dtype=torch.float32)
     close(C.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("adt", ["f16", "bf16", "i8"])
+def test_int4_single_row_dtypes_bias(sg, oracle_mod, w4_path, adt):
+    K, N, gs = 3072, 2560, 64
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=21)
+    rng = np.random.default_rng(22)
+    x32 = rng.standard_normal((1, K)).astype(np.float32)
+    bias = (0.1 * rng.standard_normal(N)).astype(np.float16)
+    if adt == "f16":
+        xo = x32.astype(np.float16)
+        xt, kw = t(xo), {}
+    elif adt == "bf16":
+        xo, xt, kw = oracle_mod.f32_to_bf16_bits(x32), bf16_tensor(x32), {"a_bf16": True}
+    else:
+        xo = rng.integers(-128, 128, (1, K), dtype=np.int8)
+        xt, kw = t(xo), {}
+    scale_A = 0.03 if adt == "i8" else 1.0
+    want = oracle_mod.matmul_int4_grouped(xo, B, S, Z, K, N, gs, bias=bias, c_dt=oracle_mod.DT_F32,
+                                          scale_A=scale_A, **kw)
+    C = sg.matmul_int4_grouped(xt, t(B), t(S), t(Z), K, N, gs, out_dtype=torch.float32, bias=t(bias),
+                               scale_A=scale_A)
+    close(C.cpu().numpy(), want)
+
+
+def test_int4_paths_agree_on_reference_golden(sg):
+    """The reference's own output (int8 activations, fp16 out) from every path."""
+    g = golden("int4_gemv_k512_n128_g64.npz")
+    K, N, gs = int(g["K"]), int(g["N"]), int(g["gs"])
+    try:
+        for path in (0, 1, 2):
+            sg.set_tuning("w4_gemv.path", path)
+            C = sg.matmul_int4_grouped(t(g["A"]).view(1, K), t(g["B"]), t(g["S"]), t(g["Z"]), K, N, gs)
+            close(C.cpu().numpy().ravel(), g["C"])
+    finally:
+        sg.set_tuning("w4_gemv.path", 0)
+
+
+def test_no_device_error_recorded(sg):
+    from silicongraph_b200 import _lib
+    _lib.check(_lib.load().sg_device_error_check(torch.cuda.current_stream().cuda_stream))
 
 
 @pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8])
@@ -159,10 +212,12 @@ def test_int4_split_granularity_invariant(sg, oracle_mod, gpw):
     x = np.random.default_rng(8).standard_normal((1, K)).astype(np.float32)
     want = oracle_mod.matmul_int4_grouped(x, B, S, Z, K, N, gs, c_dt=oracle_mod.DT_F32)
     try:
+        sg.set_tuning("w4_gemv.path", 1)
         sg.set_tuning("w4_gemv.groups_per_warp", gpw)
         C = sg.matmul_int4_grouped(t(x), t(B), t(S), t(Z), K, N, gs, out_dtype=torch.float32)
     finally:
         sg.set_tuning("w4_gemv.groups_per_warp", 0)
+        sg.set_tuning("w4_gemv.path", 0)
     close(C.cpu().numpy(), want)
 
 
