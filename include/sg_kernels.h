@@ -139,6 +139,21 @@ SgStatus sg_matmul_int4_grouped(const SgMatMulParams* p, void* stream);
  * this large and zero-filled once before its first use (calls leave it
  * zero-filled).  Returns 0 when no scratch is needed. */
 size_t sg_matmul_int4_grouped_workspace_size(const SgMatMulParams* p);
+/*
+ * Same computation and results as sg_matmul_int4_grouped, for callers that are
+ * not allowed to allocate device memory after start-up: runtimes that fix
+ * their memory budget when a session is admitted and refuse work rather than
+ * allocate later, or host frameworks whose memory pool owns the device and
+ * forbids direct cudaMalloc.  This entry point has no counterpart in the
+ * reference.  It never allocates: its scratch is a fixed 2 MiB array inside
+ * the library, held by every GPU that loads the library until the process
+ * exits.  The first call on a device looks up that array's device address
+ * (make it before any stream capture on that device).  Problems needing more
+ * than 2 MiB of scratch are rejected with SG_ERR_INVALID.  p->workspace is
+ * ignored.  Calls share the array: calls that overlap on the GPU race, so
+ * order them on one stream.
+ */
+SgStatus sg_matmul_int4_grouped_noalloc(const SgMatMulParams* p, void* stream);
 
 /*
  * INT8 per-channel GEMV/GEMM.  Replaces the GLSL gemm_int8 shader

@@ -90,6 +90,7 @@ _SIGS = {
     "sg_device_error_check": (ctypes.c_int32, [_P]),
     "sg_matmul_int4_grouped": (ctypes.c_int32, [ctypes.POINTER(SgMatMulParams), _P]),
     "sg_matmul_int4_grouped_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(SgMatMulParams)]),
+    "sg_matmul_int4_grouped_noalloc": (ctypes.c_int32, [ctypes.POINTER(SgMatMulParams), _P]),
     "sg_matmul_int8_channel": (ctypes.c_int32, [ctypes.POINTER(SgMatMulParams), _P]),
     "sg_matmul_int8_channel_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(SgMatMulParams)]),
     "sg_matmul_fp16": (ctypes.c_int32, [ctypes.POINTER(SgMatMulParams), _P]),
