@@ -115,6 +115,9 @@ int32_t sg_device_error_check(void* stream);
 /* Override a launch heuristic (benchmark sweeps).  Keys:
  *   "w4_gemv.groups_per_warp"  INT4 GEMV (CUDA-core path) split-K granularity (0 = heuristic)
  *   "w4_gemv.path"             INT4 GEMV path: 0 auto, 1 CUDA-core, 2 generic
+ *   "w4_gemv_mma.variant"      tensor-core GEMV launch shape (0 default .. 3)
+ *   "w4_gemv_mma.sleep"        tensor-core GEMV: sleep between stage polls (0/1)
+ *   "w4_gemv_mma.cluster"      tensor-core GEMV: allow the cluster-reduced split (1, default) or not (0)
  * Returns SG_ERR_NOT_FOUND for an unknown key.  No reference counterpart. */
 int32_t sg_set_tuning(const char* key, int32_t value);
 

@@ -381,6 +381,7 @@ namespace sg {
 size_t w4_gemv_mma_scratch_bytes(const SgMatMulParams* p, int sms, bool* applicable);
 SgStatus w4_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, void* ws, size_t ws_bytes,
                          int* err_word, bool* handled);
+bool w4_gemv_mma_tuning(std::string_view key, int value);
 }  // namespace sg
 
 // Core entry.  ws == NULL: library scratch (unless ws_external, then an error
@@ -420,7 +421,7 @@ static SgStatus w4_run(const SgMatMulParams* p, void* stream, void* ws, size_t w
   bool mma_ok = false;
   const size_t mma_ws = sg::w4_gemv_mma_scratch_bytes(p, sms, &mma_ok);
   if (mma_ok && path == 0) {
-    if (ws == nullptr) {
+    if (ws == nullptr && mma_ws > 0) {
       if (ws_external) {
         sg::set_error("sg_matmul_int4_grouped: scratch required (%zu bytes)", mma_ws);
         return SG_ERR_INVALID;
@@ -523,6 +524,7 @@ int32_t sg_set_tuning(const char* key, int32_t value) {
     g_tune_path.store(value);
     return SG_OK;
   }
+  if (key && sg::w4_gemv_mma_tuning(std::string_view(key), value)) return SG_OK;
   sg::set_error("sg_set_tuning: unknown key");
   return SG_ERR_NOT_FOUND;
 }

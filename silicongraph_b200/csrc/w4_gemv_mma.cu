@@ -34,18 +34,18 @@
 //     warp hit 8 distinct 16-byte bank groups (no bank conflicts).
 //   * Blocks reduce their phases in shared memory; a 512-column tile shared by
 //     two blocks is finished by the later one (atomic ticket, fixed order).
+#include <cooperative_groups.h>
+
 #include <algorithm>
+#include <atomic>
 #include <mutex>
+#include <string_view>
 
 #include "sm100.cuh"
 
 namespace {
 
-constexpr int kWarps = 16;
-constexpr int kThreads = kWarps * 32;
 constexpr int kStrips = 4;
-constexpr int kPhases = kWarps / kStrips;
-constexpr int kStages = 2;
 constexpr int kRows = 32;                    // k-pair rows per chunk
 constexpr int kTileCols = kStrips * 128;     // 512
 constexpr int kWBytes = 128 * kRows;         // 4096
@@ -53,10 +53,17 @@ constexpr int kSBytes = 128 * 2 * 2;         // 2 scale rows x 128 fp16
 constexpr int kZBytes = 128 * 2;             // 2 zero rows x 128 int8
 constexpr int kSZBytes = kSBytes + kZBytes;  // 768
 constexpr int kXRowBytes = 32;               // 8 B-fragment words per k-pair row
-constexpr int kOffW = 0;
-constexpr int kOffSZ = kOffW + kWarps * kStages * kWBytes;   // 131072
-constexpr int kOffX = kOffSZ + kWarps * kStages * kSZBytes;  // 155648
 constexpr int kStaticSmemReserve = 2048;
+// Launch shapes: warps per block (4 column strips x warps/4 phases) and TMA
+// stages per warp.  Variant 0 is the default; the others are selectable with
+// sg_set_tuning("w4_gemv_mma.variant", v) for measurement.
+constexpr int kVariantWarps[4] = {16, 8, 12, 8};
+constexpr int kVariantStages[4] = {2, 4, 3, 5};
+constexpr int off_sz(int warps, int stages) { return warps * stages * kWBytes; }
+constexpr int off_x(int warps, int stages) { return off_sz(warps, stages) + warps * stages * kSZBytes; }
+std::atomic<int> g_variant{0};
+std::atomic<int> g_sleep{0};
+std::atomic<int> g_cluster_mode{1};
 
 struct MArgs {
   const void* A;
@@ -67,7 +74,10 @@ struct MArgs {
   float scale_A;
   int has_zeros;
   int n_tiles, cpt, nblocks, flat, total;
+  int ksplit;          // cluster mode: blocks (cluster ranks) per 512-column tile
   int max_chunks;      // x staging capacity (chunks per block)
+  int gs_shift;        // log2(gs) when gs is a power of two, else -1
+  int sleep_wait;      // back off with nanosleep while waiting for a stage
   float* slots;        // [nblocks][2][512]
   unsigned* tickets;   // [n_tiles]
   int* err;
@@ -118,8 +128,6 @@ __device__ __forceinline__ uint32_t pack_h2(__half lo, __half hi) {
   return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
 }
 
-__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 
 // Raw nibble carriers as fp16 pairs (no offset removal): for a word of 4
 // columns x one k pair, lo = 1024 + q (even k), hi = 1024 + 16 q (odd k);
@@ -135,10 +143,17 @@ __device__ __forceinline__ void nibbles_h(uint32_t w, uint32_t& e02, uint32_t& o
   o13 = sgd::lop3_and_or(w8, 0x00F000F0u, MAGIC);
 }
 
-template <bool HAS_Z>
-__global__ void __launch_bounds__(kThreads, 1)
+__device__ __forceinline__ int group_of(const MArgs& a, int k) { return a.gs_shift >= 0 ? (k >> a.gs_shift) : k / a.gs; }
+
+// CLUSTER: grid (ksplit, n_tiles), clusters of ksplit blocks own one tile and
+// reduce their partials through distributed shared memory (no scratch).
+// Otherwise: flat split of all chunks over the blocks, reduced through scratch.
+template <bool HAS_Z, int WARPS, int STAGES, bool CLUSTER>
+__global__ void __launch_bounds__(WARPS * 32, 1)
     w4_gemv_mma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmS,
                        const __grid_constant__ CUtensorMap tmZ, MArgs a) {
+  constexpr int kWarps = WARPS, kThreads = WARPS * 32, kPhases = WARPS / kStrips, kStages = STAGES;
+  constexpr int kOffW = 0, kOffSZ = off_sz(WARPS, STAGES), kOffX = off_x(WARPS, STAGES);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* xst = smem + kOffX;                                             // [chunk][32 rows][32 B]
@@ -153,7 +168,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int strip = warp % kStrips, phase = warp / kStrips;
   const int b = blockIdx.x;
   int cs, ce;
-  block_range(a, b, cs, ce);
+  if (CLUSTER) {
+    const int tile = blockIdx.y, sp = blockIdx.x;
+    cs = tile * a.cpt + (a.cpt * sp) / a.ksplit;
+    ce = tile * a.cpt + (a.cpt * (sp + 1)) / a.ksplit;
+  } else {
+    block_range(a, b, cs, ce);
+  }
   const int t_first = cs / a.cpt;
   const int nchunks = ce - cs;
 
@@ -171,11 +192,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_my = (c_first < ce) ? (ce - c_first + kPhases - 1) / kPhases : 0;
   const uint32_t tx_bytes = kWBytes + kSBytes + (HAS_Z ? kZBytes : 0);
 
+  // chunk position trackers (tile, row-chunk within tile), advanced by kPhases per step
+  int it_tile = c_first / a.cpt, it_crow = c_first - it_tile * a.cpt;  // next chunk to issue
   auto issue = [&](int i) {
-    const int c = c_first + i * kPhases;
-    const int tile = c / a.cpt;
-    const int row0 = (c - tile * a.cpt) * kRows;
-    const int gA = (2 * row0) / a.gs;
+    const int tile = it_tile;
+    const int row0 = it_crow * kRows;
+    it_crow += kPhases;
+    while (it_crow >= a.cpt) {
+      it_crow -= a.cpt;
+      ++it_tile;
+    }
+    const int gA = group_of(a, 2 * row0);
     const int x0 = tile * kTileCols + strip * 128;
     const int s = i % kStages;
     uint8_t* wdst = smem + kOffW + (warp * kStages + s) * kWBytes;
@@ -187,23 +214,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (HAS_Z) sgd::tma_load_2d(szdst + kSBytes, &tmZ, x0, gA, bar);
   };
 
-  // weights do not depend on the previous kernel: start streaming them now
+  // The activation depends on the previous kernel; request it first, so that
+  // its few bytes are not queued behind this block's weight stream.
+  sgd::pdl_wait();
+  constexpr int kPrefetchRows = 2;
+  float xe_pf[kPrefetchRows], xo_pf[kPrefetchRows];
+#pragma unroll
+  for (int j = 0; j < kPrefetchRows; ++j) {
+    const int idx = threadIdx.x + j * kThreads;
+    xe_pf[j] = xo_pf[j] = 0.f;
+    if (idx < nchunks * kRows) {
+      const int cl = idx / kRows, r = idx - cl * kRows;
+      const int k = 2 * (((cs + cl) % a.cpt) * kRows + r);
+      if (k < a.K) xe_pf[j] = load_act(a.A, a.a_dt, k);
+      if (k + 1 < a.K) xo_pf[j] = load_act(a.A, a.a_dt, k + 1);
+    }
+  }
   if (lane == 0) {
     for (int i = 0; i < min(kStages, n_my); ++i) issue(i);
   }
-  sgd::pdl_wait();
 
   // ---- stage the activation as ready-made B fragments.  Per k-pair row:
   //      8 words [hi/lo][column select e][even, odd] with even entries x and odd
   //      entries x/16 (fp16, x split as hi + lo), and per-row sums used to undo
   //      the nibble carriers' constant: X = sum_k x_eff, P = 1024 * sum b.
-  for (int idx = threadIdx.x; idx < nchunks * kRows; idx += kThreads) {
+  for (int idx = threadIdx.x, j = 0; idx < nchunks * kRows; idx += kThreads, ++j) {
     const int cl = idx / kRows, r = idx - cl * kRows;
     const int c = cs + cl;
     const int row = (c % a.cpt) * kRows + r;
     const int k = 2 * row;
-    const float xe = (k < a.K) ? load_act(a.A, a.a_dt, k) : 0.f;
-    const float xo = (k + 1 < a.K) ? load_act(a.A, a.a_dt, k + 1) : 0.f;
+    float xe, xo;
+    if (j < kPrefetchRows) {
+      xe = j == 0 ? xe_pf[0] : xe_pf[1];
+      xo = j == 0 ? xo_pf[0] : xo_pf[1];
+    } else {
+      xe = (k < a.K) ? load_act(a.A, a.a_dt, k) : 0.f;
+      xo = (k + 1 < a.K) ? load_act(a.A, a.a_dt, k + 1) : 0.f;
+    }
     const __half he = __float2half_rn(xe);
     const __half hoF = __float2half_rn(xo);
     const __half le = __float2half_rn(xe - __half2float(he));
@@ -273,11 +320,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   int cur_tile = t_first;
 
   int ok = 1;
+  int tile = c_first / a.cpt, crow = c_first - tile * a.cpt;
   for (int i = 0; i < n_my; ++i) {
-    const int c = c_first + i * kPhases;
-    const int tile = c / a.cpt;
-    const int crow = c - tile * a.cpt;
-    const int cl = c - cs;
+    if (i > 0) {
+      crow += kPhases;
+      while (crow >= a.cpt) {
+        crow -= a.cpt;
+        ++tile;
+      }
+    }
+    const int cl = c_first + i * kPhases - cs;
     const int s = i % kStages;
     if (tile != cur_tile) {  // warp-uniform, at most once
 #pragma unroll
@@ -287,7 +339,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       cur_tile = tile;
     }
-    const bool waited = sgd::mbar_wait(&my_bars[s], (i / kStages) & 1, a.err);
+    const bool waited = a.sleep_wait ? sgd::mbar_wait_sleep(&my_bars[s], (i / kStages) & 1, a.err)
+                                     : sgd::mbar_wait(&my_bars[s], (i / kStages) & 1, a.err);
     if (!__all_sync(0xffffffffu, waited)) {
       ok = 0;
       break;
@@ -314,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- chunk epilogue: acc += scale * (D - P - (8 + zero) * X) for this lane's variant
     const uint8_t* szs = smem + kOffSZ + (warp * kStages + s) * kSZBytes;
     const int k0 = 2 * crow * kRows;
-    const int gA = k0 / a.gs, gB = (k0 + 32) / a.gs;
+    const int gA = group_of(a, k0), gB = group_of(a, k0 + 32);
     const int srow = d_half ? (gB - gA) : 0;
     const uint4 s_lo = *reinterpret_cast<const uint4*>(szs + srow * 256 + g * 32);
     const uint4 s_hi = *reinterpret_cast<const uint4*>(szs + srow * 256 + g * 32 + 16);
@@ -368,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     acc0[q].y += __shfl_xor_sync(0xffffffffu, acc0[q].y, 2);
   }
   __syncthreads();
-  if (s_abort) return;
+  if (!CLUSTER && s_abort) return;
 
   // ---- block reduction over phases: red[seg][phase][512] aliases the weight stages.
   // Column of pair entry: acc[2j+h].x -> 4j+h, .y -> 4j+h+2.  Lane t writes tile j = t.
@@ -387,6 +440,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     r1[0] = s1e.x; r1[2] = s1e.y; r1[1] = s1o.x; r1[3] = s1o.y;
   }
   __syncthreads();
+
+  if (CLUSTER) {
+    // this block's partial of its tile; rank 0 of the cluster sums the ranks in order
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    float* tsum = red + 2 * kPhases * kTileCols;
+    for (int cc = threadIdx.x; cc < kTileCols; cc += kThreads) {
+      float v = 0.f;
+#pragma unroll
+      for (int ph = 0; ph < kPhases; ++ph) v += red[ph * kTileCols + cc];
+      tsum[cc] = v;
+    }
+    cluster.sync();
+    if (cluster.block_rank() == 0) {
+      const int tile = blockIdx.y;
+      int aborted = 0;
+      for (int r = 0; r < a.ksplit; ++r) aborted |= *cluster.map_shared_rank(&s_abort, r);
+      if (!aborted) {
+        for (int cc = threadIdx.x; cc < kTileCols; cc += kThreads) {
+          float v = 0.f;
+          for (int r = 0; r < a.ksplit; ++r) v += cluster.map_shared_rank(tsum, r)[cc];
+          const int col = tile * kTileCols + cc;
+          if (col < a.N) store_out(a.C, a.c_dt, col, finalize(a, col, v));
+        }
+      }
+    }
+    cluster.sync();  // peers keep their shared memory alive until rank 0 has read it
+    return;
+  }
 
   const int t_last = (ce - 1) / a.cpt;
   for (int s2 = 0; s2 < 2 && t_first + s2 <= t_last; ++s2) {
@@ -432,9 +514,41 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 struct MPlan {
   bool ok = false;
+  int variant = 0;
+  int cluster = 0, ksplit = 1;
   int n_tiles = 0, cpt = 0, nblocks = 0, flat = 0, max_chunks = 0, total = 0;
   size_t smem = 0, ws_bytes = 0, tickets_bytes = 0;
 };
+
+// Clusters of k blocks (one per SM: the kernel's shared memory allows one
+// block per SM) that can be resident at once.
+int max_active_clusters(int k) {
+  static std::mutex mu;
+  static int cache[17] = {0};
+  std::lock_guard<std::mutex> lk(mu);
+  if (k < 1 || k > 16) return 0;
+  if (cache[k] != 0) return cache[k];
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(k, 1);
+  cfg.blockDim = dim3(512);
+  cfg.dynamicSmemBytes = 225 * 1024;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = k;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  auto kfn = w4_gemv_mma_kernel<true, 16, 2, true>;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024) != cudaSuccess ||
+      cudaOccupancyMaxActiveClusters(&n, kfn, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = -1;
+  }
+  cache[k] = n;
+  return n;
+}
 
 MPlan make_mplan(const SgMatMulParams* p, int sms) {
   MPlan pl;
@@ -447,7 +561,25 @@ MPlan make_mplan(const SgMatMulParams* p, int sms) {
   const long long total = (long long)pl.n_tiles * pl.cpt;
   if (total >= (1ll << 30)) return pl;
   pl.total = (int)total;
-  if (pl.n_tiles <= sms) {
+  // Cluster mode when a tile-aligned split with <= 8 blocks per tile runs in
+  // one wave (clusters must fit inside a GPC) and fills most SMs.
+  int ks = 0;
+  if (g_cluster_mode.load()) {
+    for (int k = std::min({8, pl.cpt, pl.n_tiles > 0 ? sms / pl.n_tiles : 0}); k >= 2; --k) {
+      if (pl.n_tiles * k < (sms * 3) / 4) break;
+      if (max_active_clusters(k) >= pl.n_tiles) {
+        ks = k;
+        break;
+      }
+    }
+  }
+  if (ks >= 2) {
+    pl.cluster = 1;
+    pl.ksplit = ks;
+    pl.flat = 0;
+    pl.nblocks = pl.n_tiles * ks;
+    pl.max_chunks = (pl.cpt + ks - 1) / ks;
+  } else if (pl.n_tiles <= sms) {
     pl.flat = 1;
     pl.nblocks = (int)std::min<long long>(sms, total);
     pl.max_chunks = (int)((total + pl.nblocks - 1) / pl.nblocks);
@@ -456,12 +588,19 @@ MPlan make_mplan(const SgMatMulParams* p, int sms) {
     pl.nblocks = pl.n_tiles;
     pl.max_chunks = pl.cpt;
   }
-  pl.smem = 1024 + kOffX + (size_t)pl.max_chunks * (kRows * kXRowBytes + kRows * 16 + 2 * 16) + 16 +
-            kWarps * kStages * 8;
+  pl.variant = std::min(3, std::max(0, g_variant.load()));
+  const int vw = kVariantWarps[pl.variant], vs = kVariantStages[pl.variant];
+  pl.smem = 1024 + off_x(vw, vs) + (size_t)pl.max_chunks * (kRows * kXRowBytes + kRows * 16 + 2 * 16) + 16 +
+            vw * vs * 8;
   // opt-in limit per block (227 KB on sm_100) minus this kernel's static shared memory
   if (pl.smem > 227 * 1024 - kStaticSmemReserve) return pl;
-  pl.tickets_bytes = sg::align_up((size_t)pl.n_tiles * sizeof(unsigned), 256);
-  pl.ws_bytes = pl.tickets_bytes + (size_t)pl.nblocks * 2 * kTileCols * sizeof(float);
+  if (pl.cluster) {
+    pl.tickets_bytes = 0;
+    pl.ws_bytes = 0;  // partials stay in distributed shared memory
+  } else {
+    pl.tickets_bytes = sg::align_up((size_t)pl.n_tiles * sizeof(unsigned), 256);
+    pl.ws_bytes = pl.tickets_bytes + (size_t)pl.nblocks * 2 * kTileCols * sizeof(float);
+  }
   pl.ok = true;
   return pl;
 }
@@ -483,7 +622,7 @@ SgStatus w4_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, void
   const MPlan pl = make_mplan(p, sms);
   if (!pl.ok) return SG_OK;
   *handled = true;
-  SG_CHECK_ARG(ws != nullptr && ws_bytes >= pl.ws_bytes && aligned16(ws),
+  SG_CHECK_ARG(pl.ws_bytes == 0 || (ws != nullptr && ws_bytes >= pl.ws_bytes && aligned16(ws)),
                "sg_matmul_int4_grouped: workspace too small (%zu < %zu bytes)", ws_bytes, pl.ws_bytes);
   const int gs = p->group_size > 0 ? p->group_size : 128;
   const int KP = (p->K + 1) / 2;
@@ -531,16 +670,27 @@ SgStatus w4_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, void
   a.flat = pl.flat;
   a.total = pl.total;
   a.max_chunks = pl.max_chunks;
+  a.ksplit = pl.ksplit;
+  a.gs_shift = ((gs & (gs - 1)) == 0) ? __builtin_ctz((unsigned)gs) : -1;
+  a.sleep_wait = g_sleep.load() ? 1 : 0;
   a.tickets = static_cast<unsigned*>(ws);
   a.slots = reinterpret_cast<float*>(static_cast<char*>(ws) + pl.tickets_bytes);
   a.err = err_word;
 
-  auto kfn = a.has_zeros ? w4_gemv_mma_kernel<true> : w4_gemv_mma_kernel<false>;
+  using KFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, MArgs);
+#define SG_W4MMA_KFNS(Z, C)                                                                              \
+  {w4_gemv_mma_kernel<Z, 16, 2, C>, w4_gemv_mma_kernel<Z, 8, 4, C>, w4_gemv_mma_kernel<Z, 12, 3, C>, \
+   w4_gemv_mma_kernel<Z, 8, 5, C>}
+  static const KFn kfns[2][2][4] = {{SG_W4MMA_KFNS(false, false), SG_W4MMA_KFNS(false, true)},
+                                    {SG_W4MMA_KFNS(true, false), SG_W4MMA_KFNS(true, true)}};
+#undef SG_W4MMA_KFNS
+  const int zi = a.has_zeros ? 1 : 0, ci = pl.cluster ? 1 : 0;
+  const KFn kfn = kfns[zi][ci][pl.variant];
   static std::mutex mu;
-  static size_t attr_smem[2] = {0, 0};
+  static size_t attr_smem[2][2][4] = {};
   {
     std::lock_guard<std::mutex> lk(mu);
-    size_t& done = attr_smem[a.has_zeros ? 1 : 0];
+    size_t& done = attr_smem[zi][ci][pl.variant];
     if (done < pl.smem) {
       cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
       if (e != cudaSuccess) {
@@ -552,15 +702,19 @@ SgStatus w4_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, void
     }
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(pl.nblocks);
-  cfg.blockDim = dim3(kThreads);
+  cfg.gridDim = pl.cluster ? dim3(pl.ksplit, pl.n_tiles) : dim3(pl.nblocks);
+  cfg.blockDim = dim3(kVariantWarps[pl.variant] * 32);
   cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = cs;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = pl.ksplit;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pl.cluster ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, tw, ts, tz, a);
   if (e != cudaSuccess) {
     cudaGetLastError();
@@ -568,6 +722,22 @@ SgStatus w4_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, void
     return SG_ERR_RUNTIME;
   }
   return SG_OK;
+}
+
+bool w4_gemv_mma_tuning(std::string_view key, int value) {
+  if (key == "w4_gemv_mma.variant") {
+    g_variant.store(value);
+    return true;
+  }
+  if (key == "w4_gemv_mma.cluster") {
+    g_cluster_mode.store(value);
+    return true;
+  }
+  if (key == "w4_gemv_mma.sleep") {
+    g_sleep.store(value);
+    return true;
+  }
+  return false;
 }
 
 }  // namespace sg

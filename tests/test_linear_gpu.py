@@ -311,3 +311,21 @@ def test_fp16_gemv_vs_oracle(sg, oracle_mod, M, K, N):
     C = torch.zeros((M, N), dtype=torch.float32, device=DEV)
     _mm(sg, "sg_matmul_fp16", t(A), t(B), C, M, K, N)
     close(C.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("cluster", [1, 0])
+@pytest.mark.parametrize("K,N,gs", [(4096, 14336, 32), (2048, 8192, 64), (2048, 128256 // 8, 32)])
+def test_int4_cluster_and_flat_splits(sg, oracle_mod, cluster, K, N, gs):
+    """Tile-aligned cluster split (partials reduced in distributed shared memory)
+    and flat split (partials reduced through scratch) give the oracle's result."""
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=N + 1)
+    x = np.random.default_rng(K + 1).standard_normal((1, K)).astype(np.float32)
+    want = oracle_mod.matmul_int4_grouped(x, B, S, Z, K, N, gs, c_dt=oracle_mod.DT_F32)
+    try:
+        sg.set_tuning("w4_gemv_mma.cluster", cluster)
+        C = sg.matmul_int4_grouped(t(x), t(B), t(S), t(Z), K, N, gs, out_dtype=torch.float32)
+        C2 = sg.matmul_int4_grouped(t(x), t(B), t(S), t(Z), K, N, gs, out_dtype=torch.float32)
+    finally:
+        sg.set_tuning("w4_gemv_mma.cluster", 1)
+    close(C.cpu().numpy(), want)
+    assert torch.equal(C, C2)
