@@ -57,8 +57,8 @@ constexpr int kStaticSmemReserve = 2048;
 // Launch shapes: warps per block (4 column strips x warps/4 phases) and TMA
 // stages per warp.  Variant 0 is the default; the others are selectable with
 // sg_set_tuning("w4_gemv_mma.variant", v) for measurement.
-constexpr int kVariantWarps[4] = {16, 8, 12, 8};
-constexpr int kVariantStages[4] = {2, 4, 3, 5};
+constexpr int kVariantWarps[4] = {16, 20, 12, 8};
+constexpr int kVariantStages[4] = {2, 2, 3, 5};
 constexpr int off_sz(int warps, int stages) { return warps * stages * kWBytes; }
 constexpr int off_x(int warps, int stages) { return off_sz(warps, stages) + warps * stages * kSZBytes; }
 std::atomic<int> g_variant{0};
@@ -311,12 +311,11 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   }
 
   float2 acc[8];    // current tile segment: pairs (4j, 4j+2) -> acc[2j], (4j+1, 4j+3) -> acc[2j+1]
-  float2 acc0[8];   // first tile segment, when the warp's chunks cross a tile boundary
+  float2 acc0[CLUSTER ? 1 : 8];  // first tile segment, when the warp's chunks cross a tile boundary
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    acc[i] = make_float2(0.f, 0.f);
-    acc0[i] = make_float2(0.f, 0.f);
-  }
+  for (int i = 0; i < 8; ++i) acc[i] = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < (CLUSTER ? 1 : 8); ++i) acc0[i] = make_float2(0.f, 0.f);
   int cur_tile = t_first;
 
   int ok = 1;
@@ -331,10 +330,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
     const int cl = c_first + i * kPhases - cs;
     const int s = i % kStages;
-    if (tile != cur_tile) {  // warp-uniform, at most once
+    if (!CLUSTER && tile != cur_tile) {  // warp-uniform, at most once
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        acc0[q] = acc[q];
+        acc0[CLUSTER ? 0 : q] = acc[q];
         acc[q] = make_float2(0.f, 0.f);
       }
       cur_tile = tile;
@@ -415,10 +414,16 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     acc[q].y += __shfl_xor_sync(0xffffffffu, acc[q].y, 1);
     acc[q].x += __shfl_xor_sync(0xffffffffu, acc[q].x, 2);
     acc[q].y += __shfl_xor_sync(0xffffffffu, acc[q].y, 2);
-    acc0[q].x += __shfl_xor_sync(0xffffffffu, acc0[q].x, 1);
-    acc0[q].y += __shfl_xor_sync(0xffffffffu, acc0[q].y, 1);
-    acc0[q].x += __shfl_xor_sync(0xffffffffu, acc0[q].x, 2);
-    acc0[q].y += __shfl_xor_sync(0xffffffffu, acc0[q].y, 2);
+  }
+  if (!CLUSTER) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int qq = CLUSTER ? 0 : q;
+      acc0[qq].x += __shfl_xor_sync(0xffffffffu, acc0[qq].x, 1);
+      acc0[qq].y += __shfl_xor_sync(0xffffffffu, acc0[qq].y, 1);
+      acc0[qq].x += __shfl_xor_sync(0xffffffffu, acc0[qq].x, 2);
+      acc0[qq].y += __shfl_xor_sync(0xffffffffu, acc0[qq].y, 2);
+    }
   }
   __syncthreads();
   if (!CLUSTER && s_abort) return;
@@ -429,8 +434,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   {
     const float2 a0 = t == 0 ? acc[0] : t == 1 ? acc[2] : t == 2 ? acc[4] : acc[6];
     const float2 a1 = t == 0 ? acc[1] : t == 1 ? acc[3] : t == 2 ? acc[5] : acc[7];
-    const float2 b0 = t == 0 ? acc0[0] : t == 1 ? acc0[2] : t == 2 ? acc0[4] : acc0[6];
-    const float2 b1 = t == 0 ? acc0[1] : t == 1 ? acc0[3] : t == 2 ? acc0[5] : acc0[7];
+    const float2 b0 = CLUSTER ? make_float2(0.f, 0.f)
+                              : (t == 0 ? acc0[0] : t == 1 ? acc0[CLUSTER ? 0 : 2] : t == 2 ? acc0[CLUSTER ? 0 : 4]
+                                                                                           : acc0[CLUSTER ? 0 : 6]);
+    const float2 b1 = CLUSTER ? make_float2(0.f, 0.f)
+                              : (t == 0 ? acc0[CLUSTER ? 0 : 1] : t == 1 ? acc0[CLUSTER ? 0 : 3]
+                                         : t == 2 ? acc0[CLUSTER ? 0 : 5] : acc0[CLUSTER ? 0 : 7]);
     // segment 0 = first tile of the block range, segment 1 = second
     const float2 s0e = crossed ? b0 : a0, s0o = crossed ? b1 : a1;
     const float2 s1e = crossed ? a0 : make_float2(0.f, 0.f), s1o = crossed ? a1 : make_float2(0.f, 0.f);
@@ -679,7 +688,7 @@ SgStatus w4_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, void
 
   using KFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, MArgs);
 #define SG_W4MMA_KFNS(Z, C)                                                                              \
-  {w4_gemv_mma_kernel<Z, 16, 2, C>, w4_gemv_mma_kernel<Z, 8, 4, C>, w4_gemv_mma_kernel<Z, 12, 3, C>, \
+  {w4_gemv_mma_kernel<Z, 16, 2, C>, w4_gemv_mma_kernel<Z, 20, 2, C>, w4_gemv_mma_kernel<Z, 12, 3, C>, \
    w4_gemv_mma_kernel<Z, 8, 5, C>}
   static const KFn kfns[2][2][4] = {{SG_W4MMA_KFNS(false, false), SG_W4MMA_KFNS(false, true)},
                                     {SG_W4MMA_KFNS(true, false), SG_W4MMA_KFNS(true, true)}};
