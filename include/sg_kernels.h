@@ -137,10 +137,12 @@ int32_t sg_set_tuning(const char* key, int32_t value);
  * bias).  ldb must be <= 0 or N.  group_size must be even or K <= group_size.
  */
 SgStatus sg_matmul_int4_grouped(const SgMatMulParams* p, void* stream);
-/* Scratch bytes the call needs when p->workspace is NULL the library supplies
- * it from a per-device cache; a caller-supplied workspace must be at least
- * this large and zero-filled once before its first use (calls leave it
- * zero-filled).  Returns 0 when no scratch is needed. */
+/* Scratch bytes the call needs.  When p->workspace is NULL the library
+ * supplies it from a per-(device, stream) cache.  A caller-supplied workspace
+ * must be at least this large and zero-filled before its first use; calls of
+ * the same entry point leave its counters at zero, but a workspace shared with
+ * a different entry point must be zero-filled again before reuse.  Returns 0
+ * when no scratch is needed. */
 size_t sg_matmul_int4_grouped_workspace_size(const SgMatMulParams* p);
 /*
  * Same computation and results as sg_matmul_int4_grouped, for callers that are
@@ -197,6 +199,34 @@ SgStatus sg_quantize_int4_grouped(const float* W, int32_t K, int32_t N, int32_t 
 SgStatus sg_dequantize_int4_grouped(const uint8_t* B, const uint16_t* scales,
                                     const int8_t* zeros, int32_t K, int32_t N,
                                     int32_t group_size, float* W, void* stream);
+
+/* ---------------------------------------------------------------- attention */
+
+/*
+ * Causal (or full) attention.  Replaces flash_attention_fp16 and its per-query
+ * kernel flash_attn_head (compiler/kernels/cpu/flash_attention.h:49-144):
+ *   O[b,h,i] = softmax_j(scale * Q[b,h,i] . K[b,kvh,j]) V[b,kvh,j]
+ *   kvh = h / (num_heads / num_kv_heads)                       (:102,113)
+ *   causal: key j is visible to query i iff j <= q_pos0 + i    (:60)
+ *   scale <= 0 means 1/sqrt(head_dim)                          (:101)
+ * io_dtype: DEFAULT/F16 (reference), F32, BF16; accumulation in fp32.
+ * num_heads must be a multiple of num_kv_heads; head_dim in [1, 256].
+ * K/V may be strided (kv_batch_stride, kv_head_stride; rows of head_dim
+ * elements are contiguous), so a KV cache with more rows than S_kv works.
+ */
+SgStatus sg_flash_attention(const SgFlashAttentionParams* p, void* stream);
+size_t sg_flash_attention_workspace_size(const SgFlashAttentionParams* p);
+
+/*
+ * Decode form (few queries against a long KV cache): the keys are split over
+ * many blocks (flash-decoding) and the partial softmax states are merged in a
+ * fixed order.  Same contract as sg_flash_attention; set S (queries), S_kv
+ * and q_pos0 (position of query 0; < 0 means S_kv - S).  Scratch as for the
+ * linear kernels (library cache, or caller workspace of
+ * sg_flash_decode_workspace_size bytes).
+ */
+SgStatus sg_flash_decode(const SgFlashAttentionParams* p, void* stream);
+size_t sg_flash_decode_workspace_size(const SgFlashAttentionParams* p);
 
 #ifdef __cplusplus
 }

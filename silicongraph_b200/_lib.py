@@ -95,6 +95,10 @@ _SIGS = {
     "sg_matmul_int8_channel_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(SgMatMulParams)]),
     "sg_matmul_fp16": (ctypes.c_int32, [ctypes.POINTER(SgMatMulParams), _P]),
     "sg_matmul_fp16_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(SgMatMulParams)]),
+    "sg_flash_attention": (ctypes.c_int32, [ctypes.POINTER(SgFlashAttentionParams), _P]),
+    "sg_flash_attention_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(SgFlashAttentionParams)]),
+    "sg_flash_decode": (ctypes.c_int32, [ctypes.POINTER(SgFlashAttentionParams), _P]),
+    "sg_flash_decode_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(SgFlashAttentionParams)]),
     "sg_quantize_int4_grouped": (ctypes.c_int32, [_P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                                   ctypes.c_int32, _P, _P, _P, _P]),
     "sg_dequantize_int4_grouped": (ctypes.c_int32, [_P, _P, _P, ctypes.c_int32, ctypes.c_int32,

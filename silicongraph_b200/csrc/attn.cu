@@ -1,0 +1,331 @@
+// Causal flash attention on CUDA cores, and its split-K decode form (sm_100a).
+//
+// Replaces flash_attention_fp16 / flash_attn_head
+// (compiler/kernels/cpu/flash_attention.h:49-144): layout [B, heads, S, D],
+// scale = p.scale > 0 ? p.scale : 1/sqrt(D) (:101), GQA kv_head = h / (H / Hkv)
+// (:102,113), causal: key j visible to the query at position p iff j <= p
+// (:60), online softmax with running max and normaliser (:55-89).
+//
+// Work item = (batch, kv head, block of query positions, key split).  The
+// query heads that share a kv head (GQA group) are processed together, so a
+// K/V tile is read from HBM once per group.  Tiles of 64 keys are staged in
+// shared memory as fp32; each warp owns a few (head, position) rows, lanes
+// split the head dimension, scores come from a warp reduction.
+//   * one split: the normalised output is written directly;
+//   * several splits (decode): each writes (m, l, unnormalised o) to scratch
+//     and a combine kernel merges the splits in fixed order (deterministic).
+// Used for decode (few queries, long KV) and for shapes outside the tensor-core
+// prefill kernel.
+#include <algorithm>
+#include <cmath>
+
+#include "sg_common.cuh"
+
+namespace {
+
+constexpr int kThreads = 128;
+constexpr int kWarps = kThreads / 32;
+constexpr int kKeyTile = 64;
+constexpr int kMaxRowsPerWarp = 8;
+constexpr int kMaxD = 256;
+
+struct AArgs {
+  const void* Q;
+  const void* K;
+  const void* V;
+  void* O;
+  int B, H, Hkv, Sq, Skv, D, G;  // G = query heads per kv head
+  float scale;
+  int causal, q_pos0;
+  int64_t kv_bs, kv_hs;         // element strides of K/V (batch, kv head); row stride = D
+  int io_dt;
+  int qb;                       // query positions per work item
+  int nsplit, keys_per_split;
+  float* part;                  // [B][H][Sq][nsplit][D + 2]  (o..., m, l)
+};
+
+__device__ __forceinline__ float ld_io(const void* p, int dt, int64_t i) {
+  switch (dt) {
+    case SG_DT_F32: return static_cast<const float*>(p)[i];
+    case SG_DT_BF16: return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+    default: return __half2float(static_cast<const __half*>(p)[i]);
+  }
+}
+
+__device__ __forceinline__ void st_io(void* p, int dt, int64_t i, float v) {
+  switch (dt) {
+    case SG_DT_F32: static_cast<float*>(p)[i] = v; break;
+    case SG_DT_BF16: static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v); break;
+    default: static_cast<__half*>(p)[i] = __float2half_rn(v); break;
+  }
+}
+
+template <int DPL>  // head-dim elements per lane (D <= 32 * DPL)
+__global__ void __launch_bounds__(kThreads) attn_cc_kernel(AArgs a) {
+  extern __shared__ float sm[];
+  float* ks = sm;                         // [kKeyTile][D]
+  float* vs = sm + kKeyTile * a.D;        // [kKeyTile][D]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.z, hk = blockIdx.y;
+  const int nqb = (a.Sq + a.qb - 1) / a.qb;
+  const int qblk = blockIdx.x % nqb, split = blockIdx.x / nqb;
+  const int q0 = qblk * a.qb;
+  const int nq = min(a.qb, a.Sq - q0);
+  const int rows = a.G * nq;  // row r: head hk*G + r / nq, position q0 + r % nq
+
+  // key range of this split, clipped to what the causal mask lets any row see
+  int j0 = split * a.keys_per_split;
+  int j1 = min(a.Skv, j0 + a.keys_per_split);
+  if (a.causal) j1 = min(j1, a.q_pos0 + q0 + nq);  // last visible key + 1
+  const int64_t kvbase = (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs;
+
+  float q[kMaxRowsPerWarp][DPL], o[kMaxRowsPerWarp][DPL], m[kMaxRowsPerWarp], l[kMaxRowsPerWarp];
+  int pos[kMaxRowsPerWarp];
+  bool live[kMaxRowsPerWarp];
+#pragma unroll
+  for (int rr = 0; rr < kMaxRowsPerWarp; ++rr) {
+    const int r = warp + rr * kWarps;
+    m[rr] = -INFINITY;
+    l[rr] = 0.f;
+    pos[rr] = 0;
+    live[rr] = r < rows;
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) {
+      q[rr][e] = 0.f;
+      o[rr][e] = 0.f;
+    }
+    if (r < rows) {
+      const int h = hk * a.G + r / nq, qi = q0 + r % nq;
+      pos[rr] = a.q_pos0 + qi;
+      const int64_t qoff = (((int64_t)b * a.H + h) * a.Sq + qi) * a.D;
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) {
+        const int d = lane + 32 * e;
+        if (d < a.D) q[rr][e] = ld_io(a.Q, a.io_dt, qoff + d);
+      }
+    }
+  }
+
+  for (int jt = j0; jt < j1; jt += kKeyTile) {
+    const int nk = min(kKeyTile, j1 - jt);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nk * a.D; i += kThreads) {
+      const int64_t off = kvbase + (int64_t)(jt + i / a.D) * a.D + (i % a.D);
+      ks[i] = ld_io(a.K, a.io_dt, off);
+      vs[i] = ld_io(a.V, a.io_dt, off);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int rr = 0; rr < kMaxRowsPerWarp; ++rr) {
+      if (!live[rr]) continue;  // warp-uniform
+      const int jmax = a.causal ? min(nk, pos[rr] - jt + 1) : nk;
+      for (int jj = 0; jj < jmax; ++jj) {
+        float s = 0.f;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) {
+          const int d = lane + 32 * e;
+          if (d < a.D) s = fmaf(q[rr][e], ks[jj * a.D + d], s);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+        s *= a.scale;
+        const float m_new = fmaxf(m[rr], s);
+        const float e_s = expf(s - m_new);
+        const float c_old = expf(m[rr] - m_new);
+        l[rr] = l[rr] * c_old + e_s;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) {
+          const int d = lane + 32 * e;
+          if (d < a.D) o[rr][e] = fmaf(o[rr][e], c_old, e_s * vs[jj * a.D + d]);
+        }
+        m[rr] = m_new;
+      }
+    }
+  }
+
+#pragma unroll
+  for (int rr = 0; rr < kMaxRowsPerWarp; ++rr) {
+    if (!live[rr]) continue;
+    const int r = warp + rr * kWarps;
+    const int h = hk * a.G + r / nq, qi = q0 + r % nq;
+    if (a.nsplit == 1) {
+      const float inv = l[rr] > 0.f ? 1.0f / l[rr] : 0.f;
+      const int64_t ooff = (((int64_t)b * a.H + h) * a.Sq + qi) * a.D;
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) {
+        const int d = lane + 32 * e;
+        if (d < a.D) st_io(a.O, a.io_dt, ooff + d, o[rr][e] * inv);
+      }
+    } else {
+      float* pp = a.part + ((((int64_t)b * a.H + h) * a.Sq + qi) * a.nsplit + split) * (a.D + 2);
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) {
+        const int d = lane + 32 * e;
+        if (d < a.D) pp[d] = o[rr][e];
+      }
+      if (lane == 0) {
+        pp[a.D] = m[rr];
+        pp[a.D + 1] = l[rr];
+      }
+    }
+  }
+}
+
+// Merge the splits of one (batch, head, query) row: fixed split order.
+__global__ void attn_combine_kernel(AArgs a) {
+  const int row = blockIdx.x;  // (b * H + h) * Sq + qi
+  const float* pp = a.part + (int64_t)row * a.nsplit * (a.D + 2);
+  float M = -INFINITY;
+  for (int sp = 0; sp < a.nsplit; ++sp) M = fmaxf(M, pp[sp * (a.D + 2) + a.D]);
+  float L = 0.f;
+  for (int sp = 0; sp < a.nsplit; ++sp) {
+    const float ms = pp[sp * (a.D + 2) + a.D];
+    if (ms != -INFINITY) L += pp[sp * (a.D + 2) + a.D + 1] * expf(ms - M);
+  }
+  const float inv = L > 0.f ? 1.0f / L : 0.f;
+  for (int d = threadIdx.x; d < a.D; d += blockDim.x) {
+    float acc = 0.f;
+    for (int sp = 0; sp < a.nsplit; ++sp) {
+      const float ms = pp[sp * (a.D + 2) + a.D];
+      if (ms != -INFINITY) acc += pp[sp * (a.D + 2) + d] * expf(ms - M);
+    }
+    st_io(a.O, a.io_dt, (int64_t)row * a.D + d, acc * inv);
+  }
+}
+
+}  // namespace
+
+namespace sg {
+
+SgStatus attn_validate(const SgFlashAttentionParams* p, const char* name) {
+  SG_CHECK_ARG(p != nullptr, "%s: params is NULL", name);
+  SG_CHECK_ARG(p->B >= 0 && p->S >= 0 && p->num_heads >= 0 && p->head_dim >= 0, "%s: negative size", name);
+  if (p->B == 0 || p->S == 0 || p->num_heads == 0) return SG_OK;
+  SG_CHECK_ARG(p->Q && p->K && p->V && p->O, "%s: Q, K, V and O must be non-NULL", name);
+  SG_CHECK_ARG(p->mask == nullptr, "%s: mask is not supported (the reference never reads it)", name);
+  SG_CHECK_ARG(p->head_dim >= 1 && p->head_dim <= kMaxD, "%s: head_dim %d outside [1, %d]", name, p->head_dim,
+               kMaxD);
+  const int hkv = std::max(1, p->num_kv_heads);
+  SG_CHECK_ARG(p->num_heads % hkv == 0, "%s: num_heads %d is not a multiple of num_kv_heads %d", name,
+               p->num_heads, hkv);
+  const int dt = p->io_dtype == SG_DT_DEFAULT ? SG_DT_F16 : p->io_dtype;
+  SG_CHECK_ARG(dt == SG_DT_F16 || dt == SG_DT_F32 || dt == SG_DT_BF16, "%s: io_dtype %d unsupported", name,
+               p->io_dtype);
+  const int skv = p->S_kv > 0 ? p->S_kv : p->S;
+  SG_CHECK_ARG(skv >= 1, "%s: S_kv must be >= 1", name);
+  return SG_OK;
+}
+
+// CUDA-core attention with up to `want_splits` key splits.
+SgStatus attn_cc_run(const SgFlashAttentionParams* p, void* stream, int want_splits, void* ws, size_t ws_bytes,
+                     bool ws_external) {
+  const char* name = "sg_flash_attention";
+  SgStatus st = attn_validate(p, name);
+  if (st != SG_OK) return st;
+  if (p->B == 0 || p->S == 0 || p->num_heads == 0) return SG_OK;
+  int dev = 0;
+  st = current_device(&dev);
+  if (st != SG_OK) return st;
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+
+  AArgs a{};
+  a.Q = p->Q;
+  a.K = p->K;
+  a.V = p->V;
+  a.O = p->O;
+  a.B = p->B;
+  a.H = p->num_heads;
+  a.Hkv = std::max(1, p->num_kv_heads);
+  a.G = a.H / a.Hkv;
+  a.Sq = p->S;
+  a.Skv = p->S_kv > 0 ? p->S_kv : p->S;
+  a.D = p->head_dim;
+  a.scale = p->scale > 0.f ? p->scale : 1.0f / sqrtf((float)p->head_dim);
+  a.causal = p->causal != 0;
+  a.q_pos0 = p->q_pos0 >= 0 ? p->q_pos0 : a.Skv - a.Sq;
+  a.kv_hs = p->kv_head_stride > 0 ? p->kv_head_stride : (int64_t)a.Skv * a.D;
+  a.kv_bs = p->kv_batch_stride > 0 ? p->kv_batch_stride : (int64_t)a.Hkv * a.kv_hs;
+  a.io_dt = p->io_dtype == SG_DT_DEFAULT ? SG_DT_F16 : p->io_dtype;
+  // query positions per work item: at most kWarps * kMaxRowsPerWarp rows (G * qb)
+  a.qb = std::max(1, (kWarps * kMaxRowsPerWarp) / a.G);
+  SG_CHECK_ARG(a.G <= kWarps * kMaxRowsPerWarp, "%s: more than %d query heads per kv head", name,
+               kWarps * kMaxRowsPerWarp);
+  const int nqb = (a.Sq + a.qb - 1) / a.qb;
+  const int sms = sm_count(dev);
+  int nsplit = 1;
+  if (want_splits > 1) {
+    const int items = nqb * a.Hkv * a.B;
+    nsplit = std::max(1, std::min({want_splits, (a.Skv + kKeyTile - 1) / kKeyTile, (4 * sms + items - 1) / items}));
+  }
+  a.nsplit = nsplit;
+  a.keys_per_split = (a.Skv + nsplit - 1) / nsplit;
+  if (nsplit > 1) {
+    const size_t need = (size_t)a.B * a.H * a.Sq * nsplit * (a.D + 2) * sizeof(float);
+    if (ws == nullptr) {
+      if (ws_external) {
+        set_error("%s: scratch required (%zu bytes)", name, need);
+        return SG_ERR_INVALID;
+      }
+      st = library_workspace(stream, need, &ws, kWsAttention);
+      if (st != SG_OK) return st;
+    } else {
+      SG_CHECK_ARG(ws_bytes >= need, "%s: workspace too small (%zu < %zu bytes)", name, ws_bytes, need);
+    }
+    a.part = static_cast<float*>(ws);
+  }
+  const size_t smem = (size_t)2 * kKeyTile * a.D * sizeof(float);
+  dim3 grid(nqb * nsplit, a.Hkv, a.B);
+  const int dpl = (a.D + 31) / 32;
+  auto launch = [&](auto kfn) -> SgStatus {
+    if (smem > 48 * 1024) SG_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kfn<<<grid, kThreads, smem, cs>>>(a);
+    return check_launch("attn_cc_kernel");
+  };
+  if (dpl <= 1) st = launch(attn_cc_kernel<1>);
+  else if (dpl <= 2) st = launch(attn_cc_kernel<2>);
+  else if (dpl <= 4) st = launch(attn_cc_kernel<4>);
+  else st = launch(attn_cc_kernel<8>);
+  if (st != SG_OK || nsplit == 1) return st;
+  attn_combine_kernel<<<a.B * a.H * a.Sq, 64, 0, cs>>>(a);
+  return check_launch("attn_combine_kernel");
+}
+
+size_t attn_cc_scratch_bytes(const SgFlashAttentionParams* p, int want_splits) {
+  if (attn_validate(p, "workspace_size") != SG_OK || p->B == 0 || p->S == 0 || p->num_heads == 0) return 0;
+  if (want_splits <= 1) return 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    dev = 0;
+  }
+  const int hkv = std::max(1, p->num_kv_heads), G = p->num_heads / hkv;
+  const int skv = p->S_kv > 0 ? p->S_kv : p->S;
+  const int qb = std::max(1, (kWarps * kMaxRowsPerWarp) / G);
+  const int nqb = (p->S + qb - 1) / qb;
+  const int items = nqb * hkv * p->B;
+  const int nsplit =
+      std::max(1, std::min({want_splits, (skv + kKeyTile - 1) / kKeyTile, (4 * sm_count(dev) + items - 1) / items}));
+  if (nsplit == 1) return 0;
+  return (size_t)p->B * p->num_heads * p->S * nsplit * (p->head_dim + 2) * sizeof(float);
+}
+
+}  // namespace sg
+
+extern "C" {
+
+SgStatus sg_flash_attention(const SgFlashAttentionParams* p, void* stream) {
+  if (p && p->workspace) return sg::attn_cc_run(p, stream, 8, p->workspace, p->workspace_bytes, true);
+  return sg::attn_cc_run(p, stream, 8, nullptr, 0, false);
+}
+
+size_t sg_flash_attention_workspace_size(const SgFlashAttentionParams* p) { return sg::attn_cc_scratch_bytes(p, 8); }
+
+// Decode: split the keys over many CTAs (flash-decoding) and merge.
+SgStatus sg_flash_decode(const SgFlashAttentionParams* p, void* stream) {
+  if (p && p->workspace) return sg::attn_cc_run(p, stream, 64, p->workspace, p->workspace_bytes, true);
+  return sg::attn_cc_run(p, stream, 64, nullptr, 0, false);
+}
+
+size_t sg_flash_decode_workspace_size(const SgFlashAttentionParams* p) { return sg::attn_cc_scratch_bytes(p, 64); }
+
+}  // extern "C"

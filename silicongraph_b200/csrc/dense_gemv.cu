@@ -326,7 +326,7 @@ Plan make_plan(int kind, const SgMatMulParams* p, int sms) {
   const size_t red_bytes = (size_t)kWarps * kColsPerBlock * 4;
   pl.smem = std::max(xs_bytes, red_bytes);
   if (pl.ksplit > 1) {
-    pl.tickets_bytes = sg::align_up((size_t)pl.n_tiles * 4, 256);
+    pl.tickets_bytes = sg::ticket_bytes(pl.n_tiles);
     pl.ws_bytes = pl.tickets_bytes + (size_t)pl.ksplit * p->N * 4;
   }
   return pl;
@@ -395,7 +395,7 @@ SgStatus dense_run(const char* name, const SgMatMulParams* p, void* stream, bool
   if (pl.ksplit > 1) {
     void* ws = p->workspace;
     if (ws == nullptr) {
-      st = sg::library_workspace(stream, pl.ws_bytes, &ws);
+      st = sg::library_workspace(stream, pl.ws_bytes, &ws, sg::kWsDenseGemv);
       if (st != SG_OK) return st;
     } else {
       SG_CHECK_ARG(p->workspace_bytes >= pl.ws_bytes && sg::aligned16(ws),

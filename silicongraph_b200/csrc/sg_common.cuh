@@ -46,12 +46,24 @@ SgStatus current_device(int* dev);
 int sm_count(int dev);
 
 // ---------------------------------------------------------------- workspace
-// Library-owned scratch, one buffer per (device, stream), grown on demand and
-// zero-filled when (re)allocated.  Growth synchronises the device, so the
-// first call with a larger shape must not run under stream capture.
-SgStatus library_workspace(void* stream, size_t bytes, void** out);
+// Library-owned scratch, one buffer per (device, stream, user), grown on
+// demand and zero-filled when (re)allocated.  Each entry-point family has its
+// own buffer, so ticket counters that a family keeps at zero between calls are
+// never overwritten by another family's partial results.  Growth synchronises
+// the stream, so the first call with a larger shape must not run under stream
+// capture.
+enum WorkspaceUser : int { kWsInt4Gemv = 0, kWsDenseGemv = 1, kWsAttention = 2, kWsUsers = 3 };
+SgStatus library_workspace(void* stream, size_t bytes, void** out, int user);
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Ticket counters (one per column tile) live in a fixed 4 KB prefix of a
+// kernel's scratch (more only beyond 1024 tiles), so partial results of one
+// call never land where another call of the same kernels expects zeros.
+inline size_t ticket_bytes(int n_tiles) {
+  const size_t t = align_up((size_t)n_tiles * sizeof(unsigned), 256);
+  return t < 4096 ? 4096 : t;
+}
 
 // ------------------------------------------------------------------ dtypes
 inline int elem_size(int dt) {

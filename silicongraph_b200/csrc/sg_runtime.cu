@@ -15,11 +15,12 @@ thread_local char g_err[1024] = "";
 struct WsKey {
   int dev;
   void* stream;
-  bool operator==(const WsKey& o) const { return dev == o.dev && stream == o.stream; }
+  int user;
+  bool operator==(const WsKey& o) const { return dev == o.dev && stream == o.stream && user == o.user; }
 };
 struct WsKeyHash {
   size_t operator()(const WsKey& k) const {
-    return std::hash<void*>()(k.stream) * 31u + (size_t)k.dev;
+    return (std::hash<void*>()(k.stream) * 31u + (size_t)k.dev) * 7u + (size_t)k.user;
   }
 };
 struct WsBuf {
@@ -83,12 +84,12 @@ int sm_count(int dev) {
   return n;
 }
 
-SgStatus library_workspace(void* stream, size_t bytes, void** out) {
+SgStatus library_workspace(void* stream, size_t bytes, void** out, int user) {
   int dev = 0;
   SgStatus st = current_device(&dev);
   if (st != SG_OK) return st;
   std::lock_guard<std::mutex> lk(g_ws_mu);
-  WsBuf& b = g_ws[WsKey{dev, stream}];
+  WsBuf& b = g_ws[WsKey{dev, stream, user}];
   if (b.bytes < bytes) {
     size_t want = align_up(bytes < (1u << 20) ? (1u << 20) : bytes, 1u << 20);
     if (b.ptr) {

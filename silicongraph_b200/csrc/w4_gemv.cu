@@ -358,7 +358,7 @@ Plan make_plan(const SgMatMulParams* p, int sms) {
   const size_t red_bytes = (size_t)kWarps * kColsPerBlock * sizeof(float);
   pl.smem = std::max(xs_bytes, red_bytes);
   if (pl.ksplit > 1) {
-    pl.tickets_bytes = sg::align_up((size_t)pl.n_tiles * sizeof(unsigned), 256);
+    pl.tickets_bytes = sg::ticket_bytes(pl.n_tiles);
     pl.ws_bytes = pl.tickets_bytes + (size_t)pl.ksplit * MR * p->N * sizeof(float);
   }
   return pl;
@@ -426,7 +426,7 @@ static SgStatus w4_run(const SgMatMulParams* p, void* stream, void* ws, size_t w
         sg::set_error("sg_matmul_int4_grouped: scratch required (%zu bytes)", mma_ws);
         return SG_ERR_INVALID;
       }
-      st = sg::library_workspace(stream, mma_ws, &ws);
+      st = sg::library_workspace(stream, mma_ws, &ws, sg::kWsInt4Gemv);
       if (st != SG_OK) return st;
       ws_bytes = mma_ws;
     }
@@ -454,7 +454,7 @@ static SgStatus w4_run(const SgMatMulParams* p, void* stream, void* ws, size_t w
         sg::set_error("sg_matmul_int4_grouped: scratch required (%zu bytes)", pl.ws_bytes);
         return SG_ERR_INVALID;
       }
-      st = sg::library_workspace(stream, pl.ws_bytes, &ws);
+      st = sg::library_workspace(stream, pl.ws_bytes, &ws, sg::kWsInt4Gemv);
       if (st != SG_OK) return st;
     } else {
       SG_CHECK_ARG(ws_bytes >= pl.ws_bytes && sg::aligned16(ws),

@@ -607,7 +607,7 @@ MPlan make_mplan(const SgMatMulParams* p, int sms) {
     pl.tickets_bytes = 0;
     pl.ws_bytes = 0;  // partials stay in distributed shared memory
   } else {
-    pl.tickets_bytes = sg::align_up((size_t)pl.n_tiles * sizeof(unsigned), 256);
+    pl.tickets_bytes = sg::ticket_bytes(pl.n_tiles);
     pl.ws_bytes = pl.tickets_bytes + (size_t)pl.nblocks * 2 * kTileCols * sizeof(float);
   }
   pl.ok = true;

@@ -109,7 +109,7 @@ extern "C" SgStatus sg_matmul_int4_grouped_noalloc(const SgMatMulParams* p, void
   }
   if (need > 0) {
     // ticket counters (one per 512-column tile, at the start of the scratch) must start at zero
-    const size_t tickets = sg::align_up((size_t)((q.N + kTileCols - 1) / kTileCols) * sizeof(unsigned), 256);
+    const size_t tickets = sg::ticket_bytes((q.N + kTileCols - 1) / kTileCols);
     const cudaError_t e = cudaMemsetAsync(slot->scratch, 0, tickets < need ? tickets : need,
                                           static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) {

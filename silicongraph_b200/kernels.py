@@ -91,3 +91,31 @@ def matmul_int4_grouped_workspace_size(A, B, scales, zeros, K, N, group_size, ou
 
 def set_tuning(key: str, value: int) -> None:
     check(_lib.load().sg_set_tuning(key.encode(), int(value)))
+
+
+def flash_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, *, causal: bool = True, scale: float = 0.0,
+                    q_pos0: int = 0, decode: bool = False, O: torch.Tensor | None = None, stream=None,
+                    kv_len: int | None = None, workspace=None) -> torch.Tensor:
+    """Q [B,H,Sq,D], K/V [B,Hkv,Smax,D] (only the first kv_len rows are used) --
+    flash_attention_fp16 (flash_attention.h:95-144) on the GPU."""
+    from ._lib import SgFlashAttentionParams
+    Bn, H, Sq, D = Q.shape
+    Hkv, Smax = K.shape[1], K.shape[2]
+    if O is None:
+        O = torch.empty_like(Q)
+    p = SgFlashAttentionParams()
+    p.Q, p.K, p.V, p.O = _ptr(Q), _ptr(K), _ptr(V), _ptr(O)
+    p.B, p.S, p.num_heads, p.num_kv_heads, p.head_dim = Bn, Sq, H, Hkv, D
+    p.scale = scale
+    p.causal = int(causal)
+    p.io_dtype = dtype_code(Q.dtype)
+    p.S_kv = kv_len if kv_len is not None else Smax
+    p.q_pos0 = q_pos0
+    p.kv_head_stride = K.stride(1)
+    p.kv_batch_stride = K.stride(0)
+    if workspace is not None:
+        p.workspace = _ptr(workspace)
+        p.workspace_bytes = workspace.numel() * workspace.element_size()
+    fn = _lib.load().sg_flash_decode if decode else _lib.load().sg_flash_attention
+    check(fn(ctypes.byref(p), _stream(stream)))
+    return O
