@@ -20,7 +20,7 @@
 //   * fp16 B: half2 -> float2 conversion and packed fp32x2 FMAs.
 #include <algorithm>
 
-#include "sg_common.cuh"
+#include "sm100.cuh"
 
 namespace {
 
@@ -380,6 +380,26 @@ SgStatus dense_run(const char* name, const SgMatMulParams* p, void* stream, bool
   a.scale_A = p->scale_A;
   const int kind = kind_of(int8_weights, a.a_dt);
 
+  // Float activations over many rows with INT8 weights: tcgen05 GEMM (gemm_tc.cu).
+  if (int8_weights) {
+    bool tc_ok = false;
+    const size_t tc_ws = sg::gemm_tc_scratch_bytes(p, true, &tc_ok);
+    if (tc_ok) {
+      void* ws = p->workspace;
+      size_t ws_bytes = p->workspace_bytes;
+      if (ws == nullptr && tc_ws > 0) {
+        st = sg::library_workspace(stream, tc_ws, &ws, sg::kWsPrefillGemm);
+        if (st != SG_OK) return st;
+        ws_bytes = tc_ws;
+      }
+      int* err = nullptr;
+      st = sg::device_error_word(&err);
+      if (st != SG_OK) return st;
+      bool handled = false;
+      st = sg::gemm_tc_run(p, true, cs, sg::sm_count(dev), ws, ws_bytes, err, &handled);
+      if (handled || st != SG_OK) return st;
+    }
+  }
   const Plan pl = make_plan(kind, p, sg::sm_count(dev));
   if (!pl.fast) {
     dim3 grid((p->N + 127) / 128, p->M);
@@ -428,6 +448,11 @@ size_t dense_ws(const SgMatMulParams* p, bool int8_weights) {
   if (cudaGetDevice(&dev) != cudaSuccess) {
     cudaGetLastError();
     dev = 0;
+  }
+  if (int8_weights) {
+    bool tc_ok = false;
+    const size_t tws = sg::gemm_tc_scratch_bytes(p, true, &tc_ok);
+    if (tc_ok) return tws;
   }
   const int adt = p->a_dtype == SG_DT_DEFAULT ? (int8_weights ? SG_DT_I8 : SG_DT_F16) : p->a_dtype;
   return make_plan(kind_of(int8_weights, adt), p, sg::sm_count(dev)).ws_bytes;

@@ -1,0 +1,676 @@
+// Prefill dequant-GEMM on the 5th-generation tensor cores (tcgen05 + TMEM):
+//   C[m, n] = sum_k A[m, k] * W[k, n]
+// with W held as the reference's INT4 group-quantized layout
+// (compiler/kernels/cpu/matmul_neon.h:113-147, per-row semantics applied to
+// every row m) or as INT8 per-channel weights with float activations
+// (dense GEMV FA form: C = scales[n] * sum_k A*float(B), opencl_kernels.h:36-52
+// restated for float A).
+//
+// Design (one persistent CTA per SM, 448 threads, warp-specialised):
+//   * The weights are the MMA's A operand and live in TMEM: dequant warps read
+//     the packed bytes that TMA staged in shared memory, expand them in
+//     registers (fp16(scale * (q - 8 - zero)) for INT4, exact integers for
+//     INT8) and write them with tcgen05.st.  The dequantized weights never
+//     touch shared memory, which leaves the shared-memory bandwidth to the
+//     activation operand.
+//   * The activations are the MMA's B operand: TMA copies [BT tokens x 64 k]
+//     tiles (128-byte swizzle, K-major) into shared memory.
+//   * One thread issues tcgen05.mma (M = 128 weight columns, N = BT tokens,
+//     K = 16) into a TMEM accumulator of 128 lanes x BT columns.
+//   * Four epilogue warps (one per TMEM lane quarter) read the accumulator
+//     with tcgen05.ld, apply scale_A / per-channel scales / bias and store C.
+//     With two accumulators the epilogue of one tile overlaps the main loop
+//     of the next.
+//   * Every wait is bounded (2 s); a timed-out wait records an error code in
+//     the device error word, the CTA drains its copies in flight, frees TMEM
+//     and exits.
+//
+// Tile size: 128 weight columns (the TMEM lanes) x BT tokens, K step 64.
+// Operand type: fp16 for INT4 weights (bf16 weights would round
+// scale*(q-8-zero) to 8 significant bits, too coarse for the 2e-3 absolute
+// tolerance at K = 2048); for INT8 weights the integers are exact in either
+// type, so bf16 activations are used as they are.  Activations in other types
+// are first converted to the operand type by a small kernel (exact for int8
+// and for bf16 -> fp16 within fp16's range; fp32 rounds to fp16).
+#include <algorithm>
+#include <atomic>
+#include <string_view>
+
+#include "sm100.cuh"
+
+namespace {
+
+using namespace sgd;
+
+constexpr int kKStep = 64;    // k per pipeline step: one 128-byte swizzle row of 16-bit values
+constexpr int kWCols = 128;   // weight columns per tile = TMEM lanes = UMMA M
+constexpr int kEpiWarps = 4;  // warps 0..3: epilogue, lane quarter = warp
+constexpr int kPrepWarps = 8; // warps 4..11: dequant, lane quarter = warp % 4, k half = (warp - 4) / 4
+constexpr int kWarpTma = kEpiWarps + kPrepWarps;  // 12
+constexpr int kWarpMma = kWarpTma + 1;            // 13
+constexpr int kThreads = (kWarpMma + 1) * 32;     // 448
+constexpr int kTmemCols = 512;
+
+enum WKind : int { kW4Grouped = 0, kW8Channel = 1 };
+
+template <int BT, int WK>
+struct Cfg {
+  static constexpr int kActBytes = BT * 128;                             // BT rows x 64 x 16-bit
+  static constexpr int kWBytes = (WK == kW4Grouped ? kKStep / 2 : kKStep) * kWCols;  // packed rows x 128
+  static constexpr int kSBytes = (WK == kW4Grouped) ? 4 * kWCols * 2 : 0;          // <= 4 scale rows
+  static constexpr int kZBytes = (WK == kW4Grouped) ? 4 * kWCols : 0;              // <= 4 zero rows
+  static constexpr int kStageBytes = kActBytes + kWBytes + kSBytes + kZBytes;
+  static constexpr int kStride = (kStageBytes + 1023) / 1024 * 1024;  // act tile stays 1024-aligned
+  static constexpr int kAcc = (2 * BT + 4 * 32 <= kTmemCols) ? 2 : 1;
+  static constexpr int kStagesTmem = (kTmemCols - kAcc * BT) / 32;
+  static constexpr int kStagesSmem = (227 * 1024 - 2048) / kStride;
+  static constexpr int kStages0 = kStagesTmem < kStagesSmem ? kStagesTmem : kStagesSmem;
+  static constexpr int kStages = kStages0 > 8 ? 8 : kStages0;
+  static constexpr int kBarBytes = (4 * kStages + 2 * 2 + 1) * 8 + 16;
+  static constexpr int kSmem = kStages * kStride + kBarBytes + 1024;  // + alignment slack
+  static_assert(kStages >= 2, "pipeline needs two stages");
+  static_assert(BT % 32 == 0 && BT >= 32 && BT <= 256, "token tile");
+};
+
+struct GArgs {
+  void* C;
+  const __half* bias;    // INT4: fp16 [N] or NULL
+  const float* scales;   // INT8: f32 [N]
+  float scale_A;
+  int apply_scale_A;     // INT4 with int8 activations
+  int c_dt;
+  int ldc;
+  int M, N, K;
+  int gs;                // INT4 group size
+  int ksteps;
+  int n_tiles, m_tiles;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t lop3_and_or_u(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));  // (a & b) | c
+  return d;
+}
+__device__ __forceinline__ uint32_t lop3_xor_or_u(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xBE;" : "=r"(d) : "r"(a), "r"(b), "r"(c));  // (a ^ b) | c
+  return d;
+}
+__device__ __forceinline__ uint32_t h2_as_u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u_as_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+__device__ __forceinline__ uint32_t ld_shared_u8(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_shared_u16(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+// 32 accumulator columns (tokens) of one output column n -> C, rows base, base + ldc, ...
+template <int DT, int WK>
+__device__ __forceinline__ void epi_store(const uint32_t (&r)[32], int cnt, const GArgs& a, int64_t base, float mul,
+                                          float add) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (j < cnt) {
+      float v = __uint_as_float(r[j]);
+      if (WK == kW4Grouped) {
+        if (a.apply_scale_A) v = __fmul_rn(v, a.scale_A);
+        v = __fadd_rn(v, add);
+      } else {
+        v = __fmul_rn(v, mul);
+      }
+      store_from_float<DT>(a.C, base + (int64_t)j * a.ldc, v);
+    }
+  }
+}
+
+// Bounded wait by every lane of a warp with a warp-uniform outcome, so that
+// the .sync.aligned tcgen05 instructions after it see a converged warp.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err) {
+  const bool ok = mbar_wait(bar, parity, err);
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+__device__ __forceinline__ bool warp_wait_sleep(uint64_t* bar, uint32_t parity, int* err) {
+  const bool ok = mbar_wait_sleep(bar, parity, err);
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+
+// BT tokens per tile; WK weight kind; BF16_OP: operand type (INT8 with bf16 activations); HAS_Z: INT4 zeros.
+template <int BT, int WK, bool BF16_OP, bool HAS_Z>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmAct, const __grid_constant__ CUtensorMap tmW,
+                   const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmZ, GArgs a) {
+  using C_ = Cfg<BT, WK>;
+  constexpr int S = C_::kStages, kAcc = C_::kAcc;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * C_::kStride);
+  uint64_t* empty = full + S;
+  uint64_t* afull = empty + S;
+  uint64_t* aempty = afull + S;
+  uint64_t* accfull = aempty + S;
+  uint64_t* accempty = accfull + 2;
+  uint64_t* done = accempty + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&afull[s], kPrepWarps);
+      mbar_init(&aempty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accfull[i], 1);
+      mbar_init(&accempty[i], kEpiWarps);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kWarpMma) {
+    tmem_alloc(tslot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == kWarpTma && lane == 0) {
+    tma_prefetch_desc(&tmAct);
+    tma_prefetch_desc(&tmW);
+    if (WK == kW4Grouped) tma_prefetch_desc(&tmS);
+    if (HAS_Z) tma_prefetch_desc(&tmZ);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  // Inputs written by the preceding kernel on the stream are visible after this.
+  pdl_wait();
+
+  const int tiles = a.n_tiles * a.m_tiles;
+  const int ksteps = a.ksteps;
+
+  if (warp == kWarpTma) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t issued[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      const int gs = a.gs;
+      uint32_t bytes = C_::kActBytes + C_::kWBytes;
+      int srows = 1;
+      if (WK == kW4Grouped) {
+        srows = gs >= kKStep ? 1 : kKStep / gs;
+        bytes += srows * kWCols * 2 + (HAS_Z ? srows * kWCols : 0);
+      }
+      uint32_t g = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        const int n0 = (tile % a.n_tiles) * kWCols, m0 = (tile / a.n_tiles) * BT;
+        for (int ks = 0; ks < ksteps; ++ks, ++g) {
+          const int s = g % S;
+          const uint32_t use = g / S;
+          if (*abort_flag || !mbar_wait(&empty[s], (use & 1) ^ 1, a.err)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          unsigned char* st = smem + s * C_::kStride;
+          mbar_arrive_expect_tx(&full[s], bytes);
+          tma_load_2d(st, &tmAct, ks * kKStep, m0, &full[s]);
+          if (WK == kW4Grouped) {
+            tma_load_2d(st + C_::kActBytes, &tmW, n0, ks * (kKStep / 2), &full[s]);
+            const int grow = (ks * kKStep) / gs;
+            tma_load_2d(st + C_::kActBytes + C_::kWBytes, &tmS, n0, grow, &full[s]);
+            if (HAS_Z) tma_load_2d(st + C_::kActBytes + C_::kWBytes + C_::kSBytes, &tmZ, n0, grow, &full[s]);
+          } else {
+            tma_load_2d(st + C_::kActBytes, &tmW, n0, ks * kKStep, &full[s]);
+          }
+          issued[s] = use + 1;
+        }
+      }
+      // Drain: every copy issued into this CTA's shared memory completes before exit.
+      for (int s = 0; s < S; ++s)
+        if (issued[s]) mbar_wait(&full[s], (issued[s] - 1) & 1, a.err);
+    }
+  } else if (warp == kWarpMma) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(kWCols, BT, BF16_OP ? 1 : 0, 0, 0);
+      uint32_t g = 0;
+      int lt = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++lt) {
+        const int acc = lt % kAcc;
+        const uint32_t ause = lt / kAcc;
+        if (*abort_flag || !mbar_wait(&accempty[acc], (ause & 1) ^ 1, a.err)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t dt = tbase + acc * BT;
+        for (int ks = 0; ks < ksteps; ++ks, ++g) {
+          const int s = g % S;
+          const uint32_t use = g / S;
+          if (*abort_flag || !mbar_wait(&afull[s], use & 1, a.err) || !mbar_wait(&full[s], use & 1, a.err)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t bdesc = umma_smem_desc(smem_u32(smem + s * C_::kStride), 16, 1024, kSwizzle128B);
+          const uint32_t at = tbase + kAcc * BT + s * 32;
+#pragma unroll
+          for (int kk = 0; kk < kKStep / 16; ++kk)
+            umma_f16_ts(dt, at + kk * 8, bdesc + (uint64_t)(kk * 2), idesc, (ks | kk) != 0 ? 1u : 0u);
+          umma_commit(&empty[s]);
+          umma_commit(&aempty[s]);
+        }
+        if (ok) umma_commit(&accfull[acc]);
+      }
+      umma_commit(done);
+      mbar_wait(done, 0, a.err);
+    }
+  } else if (warp >= kEpiWarps) {
+    // ------------------------------------------------------------ dequant warps
+    const int q = warp & 3, h = (warp - kEpiWarps) >> 2;
+    const int col = q * 32 + lane;  // column within the tile = TMEM lane
+    const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    uint32_t g = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+      for (int ks = 0; ks < ksteps; ++ks, ++g) {
+        const int s = g % S;
+        const uint32_t use = g / S;
+        const bool go = __all_sync(0xffffffffu, *abort_flag == 0) && warp_wait(&full[s], use & 1, a.err) &&
+                        warp_wait(&aempty[s], (use & 1) ^ 1, a.err);
+        if (!go) {
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t wbase = smem_u32(smem + s * C_::kStride + C_::kActBytes);
+        uint32_t w[16];
+        if (WK == kW4Grouped) {
+          // rows 16h .. 16h+15 of the packed tile: k = 32h .. 32h+31 of this step
+          const uint32_t sbase = wbase + C_::kWBytes;
+          const uint32_t zbase = sbase + C_::kSBytes;
+          const int gs = a.gs;
+          // group rows used by this half: first 8 rows and last 8 rows
+          const int g0 = gs >= kKStep ? 0 : (32 * h) / gs;
+          const int g1 = gs >= kKStep ? 0 : (32 * h + 16) / gs;
+          const __half2 s0 = __half2half2(__ushort_as_half((unsigned short)ld_shared_u16(sbase + (g0 * kWCols + col) * 2)));
+          const __half2 s1 = __half2half2(__ushort_as_half((unsigned short)ld_shared_u16(sbase + (g1 * kWCols + col) * 2)));
+          int z0 = 0, z1 = 0;
+          if (HAS_Z) {
+            z0 = (int)(int8_t)ld_shared_u8(zbase + g0 * kWCols + col);
+            z1 = (int)(int8_t)ld_shared_u8(zbase + g1 * kWCols + col);
+          }
+          const __half2 c0 = __half2half2(__int2half_rn(1032 + z0));
+          const __half2 c1 = __half2half2(__int2half_rn(1032 + z1));
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const uint32_t b = ld_shared_u8(wbase + (16 * h + i) * kWCols + col);
+            // (1024 + low nibble, 1024 + high nibble) as fp16x2
+            const uint32_t x = lop3_and_or_u(b | (b << 12), 0x000F000Fu, 0x64006400u);
+            const __half2 t = __hsub2(u_as_h2(x), i < 8 ? c0 : c1);  // q - 8 - zero, exact
+            w[i] = h2_as_u(__hmul2(t, i < 8 ? s0 : s1));              // fp16(scale * (q - 8 - zero))
+          }
+        } else {
+          // rows 32h .. 32h+31 of the int8 tile: k = 32h .. 32h+31 of this step, in two passes of 16
+#pragma unroll 1
+          for (int o = 0; o < 2; ++o) {
+            uint32_t w8[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int r = 32 * h + 16 * o + 2 * i;
+              const uint32_t b0 = ld_shared_u8(wbase + r * kWCols + col);
+              const uint32_t b1 = ld_shared_u8(wbase + (r + 1) * kWCols + col);
+              if (BF16_OP) {
+                __nv_bfloat162 v = __floats2bfloat162_rn((float)(int)(int8_t)b0, (float)(int)(int8_t)b1);
+                w8[i] = *reinterpret_cast<uint32_t*>(&v);  // integers: exact
+              } else {
+                // (1024 + (q + 128)) - 1152 = q, exact in fp16
+                const uint32_t x = lop3_xor_or_u(b0 | (b1 << 16), 0x00800080u, 0x64006400u);
+                w8[i] = h2_as_u(__hsub2(u_as_h2(x), __half2half2(__int2half_rn(1152))));
+              }
+            }
+            tmem_st_32x32b_x8(tbase + lane_addr + kAcc * BT + s * 32 + 16 * h + 8 * o, w8);
+          }
+        }
+        if (WK == kW4Grouped) tmem_st_32x32b_x16(tbase + lane_addr + kAcc * BT + s * 32 + 16 * h, w);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&afull[s]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue warps
+    const int q = warp;
+    const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    int lt = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++lt) {
+      const int acc = lt % kAcc;
+      const uint32_t ause = lt / kAcc;
+      const bool go = __all_sync(0xffffffffu, *abort_flag == 0) && warp_wait_sleep(&accfull[acc], ause & 1, a.err);
+      if (!go) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int n = (tile % a.n_tiles) * kWCols + q * 32 + lane;
+      const int m0 = (tile / a.n_tiles) * BT;
+      const bool nvalid = n < a.N;
+      float mul = 1.f, add = 0.f;
+      if (nvalid) {
+        if (WK == kW8Channel) mul = a.scales[n];
+        if (WK == kW4Grouped && a.bias) add = __half2float(a.bias[n]);
+      }
+      const int mrows = min(BT, a.M - m0);
+#pragma unroll 1
+      for (int c = 0; c < BT / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tbase + lane_addr + acc * BT + c * 32, r);
+        tmem_ld_wait();
+        if (c * 32 >= mrows || !nvalid) continue;
+        const int cnt = min(32, mrows - c * 32);
+        const int64_t base = (int64_t)(m0 + c * 32) * a.ldc + n;
+        switch (a.c_dt) {
+          case SG_DT_F32: epi_store<SG_DT_F32, WK>(r, cnt, a, base, mul, add); break;
+          case SG_DT_BF16: epi_store<SG_DT_BF16, WK>(r, cnt, a, base, mul, add); break;
+          default: epi_store<SG_DT_F16, WK>(r, cnt, a, base, mul, add); break;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&accempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
+// Activations -> 16-bit operand type, rows padded to ld_out (zero-filled
+// beyond K).  Grid: x over 8-element chunks of a row, y over rows.
+template <bool TO_BF16>
+__global__ void act_convert_kernel(const void* A, int a_dt, int lda, int M, int K, int ld_out, void* out) {
+  const int k0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (k0 >= ld_out) return;
+  for (int m = blockIdx.y; m < M; m += gridDim.y) {
+    const int64_t j = (int64_t)m * lda + k0;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      v[e] = 0.f;
+      if (k0 + e < K) {
+        switch (a_dt) {
+          case SG_DT_F32: v[e] = load_as_float<SG_DT_F32>(A, j + e); break;
+          case SG_DT_F16: v[e] = load_as_float<SG_DT_F16>(A, j + e); break;
+          case SG_DT_BF16: v[e] = load_as_float<SG_DT_BF16>(A, j + e); break;
+          default: v[e] = load_as_float<SG_DT_I8>(A, j + e); break;
+        }
+      }
+    }
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (TO_BF16) {
+        __nv_bfloat162 t = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+        ow[e] = *reinterpret_cast<uint32_t*>(&t);
+      } else {
+        __half2 t = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+        ow[e] = *reinterpret_cast<uint32_t*>(&t);
+      }
+    }
+    *reinterpret_cast<uint4*>(static_cast<unsigned char*>(out) + ((int64_t)m * ld_out + k0) * 2) = o;
+  }
+}
+
+// The converted activations start this far into the scratch, so that a
+// caller's workspace keeps the zeroed ticket counters of the GEMV kernels at
+// its start.
+constexpr size_t kConvOffset = 64 * 1024;
+
+std::atomic<int> g_tune_bt{0};        // 0 = automatic
+std::atomic<int> g_tune_min_rows{64};  // smallest M sent to the tensor-core GEMM
+
+struct GPlan {
+  bool ok = false;
+  int bt = 128;
+  bool convert = false;
+  bool bf16_op = false;
+  int ld_act = 0;
+  size_t conv_bytes = 0;
+};
+
+int pick_bt(int M, int N, int sms) {
+  const int tune = g_tune_bt.load();
+  if (tune == 128 || tune == 192 || tune == 256) return tune;
+  // Fewest rounds of tiles over the SMs, larger tiles on ties.
+  const int n_tiles = (N + kWCols - 1) / kWCols;
+  int best = 128;
+  double best_cost = 1e30;
+  for (int bt : {256, 192, 128}) {
+    const int m_tiles = (M + bt - 1) / bt;
+    const int tiles = n_tiles * m_tiles;
+    const int rounds = (tiles + sms - 1) / sms;
+    const double cost = (double)rounds * bt;
+    if (cost < best_cost * 0.999) {
+      best_cost = cost;
+      best = bt;
+    }
+  }
+  return best;
+}
+
+GPlan make_plan(const SgMatMulParams* p, int wkind) {
+  GPlan pl;
+  if (p->M < std::max(2, g_tune_min_rows.load()) || p->K <= 0 || p->N <= 0) return pl;
+  if (p->N % 16 != 0 || !sg::aligned16(p->B)) return pl;
+  const int a_dt = p->a_dtype == SG_DT_DEFAULT ? (wkind == kW4Grouped ? SG_DT_I8 : SG_DT_F16) : p->a_dtype;
+  if (wkind == kW4Grouped) {
+    const int gs = p->group_size > 0 ? p->group_size : 128;
+    if (!(gs == 16 || gs == 32 || gs % kKStep == 0)) return pl;
+    if (!sg::aligned16(p->scales_B) || (p->zeros_B && !sg::aligned16(p->zeros_B))) return pl;
+    pl.bf16_op = false;
+  } else {
+    if (a_dt == SG_DT_I8) return pl;  // exact int32 path stays on the GEMV kernels
+    pl.bf16_op = (a_dt == SG_DT_BF16);
+  }
+  const int lda = p->lda > 0 ? p->lda : p->K;
+  const bool direct = ((a_dt == SG_DT_F16 && !pl.bf16_op) || (a_dt == SG_DT_BF16 && pl.bf16_op)) &&
+                      (lda % 8 == 0) && sg::aligned16(p->A);
+  pl.convert = !direct;
+  pl.ld_act = direct ? lda : (int)sg::align_up((size_t)p->K, 8);
+  pl.conv_bytes = pl.convert ? kConvOffset + sg::align_up((size_t)p->M * pl.ld_act * 2, 256) : 0;
+  pl.ok = true;
+  return pl;
+}
+
+template <int BT, int WK, bool BF16_OP, bool HAS_Z>
+SgStatus launch(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tz,
+                const GArgs& a, int grid, cudaStream_t cs) {
+  using C_ = Cfg<BT, WK>;
+  auto kfn = gemm_tc_kernel<BT, WK, BF16_OP, HAS_Z>;
+  static std::atomic<uint64_t> attr_set{0};  // bit per device ordinal
+  int dev = 0;
+  SgStatus dst = sg::current_device(&dev);
+  if (dst != SG_OK) return dst;
+  const uint64_t bit = dev < 64 ? (uint64_t)1 << dev : 0;
+  if (!(attr_set.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::kSmem);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      sg::set_error("gemm_tc_kernel: cannot reserve %d bytes of shared memory: %s", C_::kSmem,
+                    cudaGetErrorString(e));
+      return SG_ERR_RUNTIME;
+    }
+    attr_set.fetch_or(bit);
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C_::kSmem;
+  cfg.stream = cs;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, ta, tw, ts, tz, a);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    sg::set_error("gemm_tc_kernel launch failed: %s", cudaGetErrorString(e));
+    return SG_ERR_RUNTIME;
+  }
+  return SG_OK;
+}
+
+template <int WK, bool BF16_OP, bool HAS_Z>
+SgStatus launch_bt(int bt, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& ts,
+                   const CUtensorMap& tz, const GArgs& a, int grid, cudaStream_t cs) {
+  switch (bt) {
+    case 256: return launch<256, WK, BF16_OP, HAS_Z>(ta, tw, ts, tz, a, grid, cs);
+    case 192: return launch<192, WK, BF16_OP, HAS_Z>(ta, tw, ts, tz, a, grid, cs);
+    default: return launch<128, WK, BF16_OP, HAS_Z>(ta, tw, ts, tz, a, grid, cs);
+  }
+}
+
+}  // namespace
+
+namespace sg {
+
+// Scratch bytes the tensor-core GEMM needs for this problem (0 when it takes
+// the activations as they are); *ok = false when the problem goes elsewhere.
+size_t gemm_tc_scratch_bytes(const SgMatMulParams* p, bool int8_weights, bool* ok) {
+  const GPlan pl = make_plan(p, int8_weights ? kW8Channel : kW4Grouped);
+  *ok = pl.ok;
+  return pl.ok ? pl.conv_bytes : 0;
+}
+
+// Runs the tensor-core GEMM when the problem qualifies (*handled = true).
+SgStatus gemm_tc_run(const SgMatMulParams* p, bool int8_weights, cudaStream_t cs, int sms, void* ws,
+                     size_t ws_bytes, int* err_word, bool* handled) {
+  *handled = false;
+  const int wk = int8_weights ? kW8Channel : kW4Grouped;
+  const GPlan pl = make_plan(p, wk);
+  if (!pl.ok) return SG_OK;
+  if (pl.convert) {
+    SG_CHECK_ARG(ws != nullptr && ws_bytes >= pl.conv_bytes && aligned16(ws),
+                 "tensor-core GEMM: activation scratch too small (%zu < %zu bytes)", ws_bytes, pl.conv_bytes);
+  }
+  const int a_dt = p->a_dtype == SG_DT_DEFAULT ? (wk == kW4Grouped ? SG_DT_I8 : SG_DT_F16) : p->a_dtype;
+  const int lda = p->lda > 0 ? p->lda : p->K;
+  const void* act = p->A;
+  if (pl.convert) {
+    ws = static_cast<unsigned char*>(ws) + kConvOffset;
+    const int chunks = pl.ld_act / 8;
+    const dim3 grid((chunks + 127) / 128, std::min(p->M, 65535));
+    if (pl.bf16_op)
+      act_convert_kernel<true><<<grid, 128, 0, cs>>>(p->A, a_dt, lda, p->M, p->K, pl.ld_act, ws);
+    else
+      act_convert_kernel<false><<<grid, 128, 0, cs>>>(p->A, a_dt, lda, p->M, p->K, pl.ld_act, ws);
+    SgStatus st = check_launch("act_convert_kernel");
+    if (st != SG_OK) return st;
+    act = ws;
+  }
+  const int bt = pick_bt(p->M, p->N, sms);
+  const int gs = p->group_size > 0 ? p->group_size : 128;
+  const int G = (p->K + gs - 1) / gs;
+
+  CUtensorMap ta, tw, ts, tz;
+  SgStatus st;
+  {
+    const uint64_t dims[2] = {(uint64_t)p->K, (uint64_t)p->M};
+    const uint64_t str[1] = {(uint64_t)pl.ld_act * 2};
+    const uint32_t box[2] = {(uint32_t)kKStep, (uint32_t)bt};
+    st = make_tensor_map(&ta, pl.bf16_op ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                         const_cast<void*>(act), dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != SG_OK) return st;
+  }
+  if (wk == kW4Grouped) {
+    const uint64_t dims[2] = {(uint64_t)p->N, (uint64_t)((p->K + 1) / 2)};
+    const uint64_t str[1] = {(uint64_t)p->N};
+    const uint32_t box[2] = {(uint32_t)kWCols, (uint32_t)(kKStep / 2)};
+    st = make_tensor_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(p->B), dims, str, box,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != SG_OK) return st;
+    const uint32_t srows = gs >= kKStep ? 1 : kKStep / gs;
+    const uint64_t sdims[2] = {(uint64_t)p->N, (uint64_t)G};
+    const uint64_t sstr[1] = {(uint64_t)p->N * 2};
+    const uint32_t sbox[2] = {(uint32_t)kWCols, srows};
+    st = make_tensor_map(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(p->scales_B), sdims, sstr, sbox,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != SG_OK) return st;
+    if (p->zeros_B) {
+      const uint64_t zstr[1] = {(uint64_t)p->N};
+      st = make_tensor_map(&tz, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(p->zeros_B), sdims, zstr, sbox,
+                           CU_TENSOR_MAP_SWIZZLE_NONE);
+      if (st != SG_OK) return st;
+    } else {
+      tz = ts;
+    }
+  } else {
+    const uint64_t dims[2] = {(uint64_t)p->N, (uint64_t)p->K};
+    const uint64_t str[1] = {(uint64_t)p->N};
+    const uint32_t box[2] = {(uint32_t)kWCols, (uint32_t)kKStep};
+    st = make_tensor_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(p->B), dims, str, box,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != SG_OK) return st;
+    ts = tw;
+    tz = tw;
+  }
+
+  GArgs a{};
+  a.C = p->C;
+  a.bias = wk == kW4Grouped ? static_cast<const __half*>(p->bias) : nullptr;
+  a.scales = wk == kW8Channel ? static_cast<const float*>(p->scales_B) : nullptr;
+  a.scale_A = p->scale_A;
+  a.apply_scale_A = (wk == kW4Grouped && a_dt == SG_DT_I8) ? 1 : 0;
+  a.c_dt = p->c_dtype == SG_DT_DEFAULT ? (wk == kW4Grouped ? SG_DT_F16 : SG_DT_F32) : p->c_dtype;
+  a.ldc = p->ldc > 0 ? p->ldc : p->N;
+  a.M = p->M;
+  a.N = p->N;
+  a.K = p->K;
+  a.gs = gs;
+  a.ksteps = (p->K + kKStep - 1) / kKStep;
+  a.n_tiles = (p->N + kWCols - 1) / kWCols;
+  a.m_tiles = (p->M + bt - 1) / bt;
+  a.err = err_word;
+  const int tiles = a.n_tiles * a.m_tiles;
+  const int grid = std::min(tiles, sms);
+  *handled = true;
+  if (wk == kW4Grouped) {
+    if (p->zeros_B) return launch_bt<kW4Grouped, false, true>(bt, ta, tw, ts, tz, a, grid, cs);
+    return launch_bt<kW4Grouped, false, false>(bt, ta, tw, ts, tz, a, grid, cs);
+  }
+  if (pl.bf16_op) return launch_bt<kW8Channel, true, false>(bt, ta, tw, ts, tz, a, grid, cs);
+  return launch_bt<kW8Channel, false, false>(bt, ta, tw, ts, tz, a, grid, cs);
+}
+
+bool gemm_tc_tuning(std::string_view key, int value) {
+  if (key == "gemm_tc.bt") {
+    g_tune_bt.store(value);
+    return true;
+  }
+  if (key == "gemm_tc.min_rows") {
+    g_tune_min_rows.store(value);
+    return true;
+  }
+  return false;
+}
+
+}  // namespace sg

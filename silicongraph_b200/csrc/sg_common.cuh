@@ -52,7 +52,7 @@ int sm_count(int dev);
 // never overwritten by another family's partial results.  Growth synchronises
 // the stream, so the first call with a larger shape must not run under stream
 // capture.
-enum WorkspaceUser : int { kWsInt4Gemv = 0, kWsDenseGemv = 1, kWsAttention = 2, kWsUsers = 3 };
+enum WorkspaceUser : int { kWsInt4Gemv = 0, kWsDenseGemv = 1, kWsAttention = 2, kWsPrefillGemm = 3, kWsUsers = 4 };
 SgStatus library_workspace(void* stream, size_t bytes, void** out, int user);
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -60,6 +60,13 @@ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 // Ticket counters (one per column tile) live in a fixed 4 KB prefix of a
 // kernel's scratch (more only beyond 1024 tiles), so partial results of one
 // call never land where another call of the same kernels expects zeros.
+// Tensor-core prefill GEMM (gemm_tc.cu) for INT4-grouped or INT8-per-channel
+// weights.  gemm_tc_scratch_bytes: *ok tells whether the problem qualifies;
+// the result is the scratch it needs (0 when activations are used in place).
+size_t gemm_tc_scratch_bytes(const SgMatMulParams* p, bool int8_weights, bool* ok);
+SgStatus gemm_tc_run(const SgMatMulParams* p, bool int8_weights, cudaStream_t cs, int sms, void* ws,
+                     size_t ws_bytes, int* err_word, bool* handled);
+
 inline size_t ticket_bytes(int n_tiles) {
   const size_t t = align_up((size_t)n_tiles * sizeof(unsigned), 256);
   return t < 4096 ? 4096 : t;

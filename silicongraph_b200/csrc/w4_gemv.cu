@@ -382,6 +382,7 @@ size_t w4_gemv_mma_scratch_bytes(const SgMatMulParams* p, int sms, bool* applica
 SgStatus w4_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, void* ws, size_t ws_bytes,
                          int* err_word, bool* handled);
 bool w4_gemv_mma_tuning(std::string_view key, int value);
+bool gemm_tc_tuning(std::string_view key, int value);
 }  // namespace sg
 
 // Core entry.  ws == NULL: library scratch (unless ws_external, then an error
@@ -417,6 +418,27 @@ static SgStatus w4_run(const SgMatMulParams* p, void* stream, void* ws, size_t w
   a.scale_A = p->scale_A;
 
   const int path = g_tune_path.load();
+  // Many activation rows: tcgen05 GEMM with the weights dequantized into TMEM (gemm_tc.cu).
+  bool tc_ok = false;
+  const size_t tc_ws = path == 0 ? sg::gemm_tc_scratch_bytes(p, false, &tc_ok) : 0;
+  if (tc_ok) {
+    if (ws == nullptr && tc_ws > 0) {
+      if (ws_external) {
+        sg::set_error("sg_matmul_int4_grouped: scratch required (%zu bytes)", tc_ws);
+        return SG_ERR_INVALID;
+      }
+      st = sg::library_workspace(stream, tc_ws, &ws, sg::kWsPrefillGemm);
+      if (st != SG_OK) return st;
+      ws_bytes = tc_ws;
+    }
+    if (err_word == nullptr) {
+      st = sg::device_error_word(&err_word);
+      if (st != SG_OK) return st;
+    }
+    bool handled = false;
+    st = sg::gemm_tc_run(p, false, cs, sms, ws, ws_bytes, err_word, &handled);
+    if (handled || st != SG_OK) return st;
+  }
   // One activation row and groups of 32k: tensor-core reduction (w4_gemv_mma.cu).
   bool mma_ok = false;
   const size_t mma_ws = sg::w4_gemv_mma_scratch_bytes(p, sms, &mma_ok);
@@ -496,6 +518,9 @@ size_t w4_gemv_scratch_bytes(const SgMatMulParams* p) {
   }
   const int sms = sm_count(dev);
   const int path = g_tune_path.load();
+  bool tc_ok = false;
+  const size_t tws = gemm_tc_scratch_bytes(p, false, &tc_ok);
+  if (tc_ok && path == 0) return tws;
   bool mma_ok = false;
   const size_t mws = w4_gemv_mma_scratch_bytes(p, sms, &mma_ok);
   if (mma_ok && path == 0) return mws;
@@ -525,6 +550,7 @@ int32_t sg_set_tuning(const char* key, int32_t value) {
     return SG_OK;
   }
   if (key && sg::w4_gemv_mma_tuning(std::string_view(key), value)) return SG_OK;
+  if (key && sg::gemm_tc_tuning(std::string_view(key), value)) return SG_OK;
   sg::set_error("sg_set_tuning: unknown key");
   return SG_ERR_NOT_FOUND;
 }

@@ -1,0 +1,147 @@
+"""Parity of the tcgen05 prefill GEMM (many activation rows) with the oracle,
+through the C ABI: INT4 group-quantized weights in the reference layout
+(matmul_neon.h:113-147 applied to every row) and INT8 per-channel weights with
+float activations.
+
+Tolerance for floating outputs: |got - want| <= 2e-3 + 1e-2 |want|."""
+import numpy as np
+import pytest
+import torch
+
+from test_linear_gpu import DEV, _mm, bf16_tensor, close, t, w4_problem
+
+pytestmark = pytest.mark.gpu
+
+
+def _acts(oracle_mod, rng, M, K, adt):
+    x32 = rng.standard_normal((M, K)).astype(np.float32)
+    if adt == "f32":
+        return x32, t(x32), {}
+    if adt == "f16":
+        xo = x32.astype(np.float16)
+        return xo, t(xo), {}
+    if adt == "bf16":
+        return oracle_mod.f32_to_bf16_bits(x32), bf16_tensor(x32), {"a_bf16": True}
+    xo = rng.integers(-128, 128, (M, K), dtype=np.int8)
+    return xo, t(xo), {}
+
+
+TDT = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+
+
+@pytest.fixture(params=[0, 128, 192, 256], ids=["bt_auto", "bt128", "bt192", "bt256"])
+def token_tile(sg, request):
+    sg.set_tuning("gemm_tc.bt", request.param)
+    yield request.param
+    sg.set_tuning("gemm_tc.bt", 0)
+
+
+@pytest.mark.parametrize("M,K,N,gs,sym,adt,cdt", [
+    (64, 256, 128, 64, True, "bf16", "bf16"),
+    (130, 2048, 1040, 32, False, "f32", "f32"),     # ragged rows and columns
+    (200, 130, 256, 16, False, "f16", "f16"),       # K not a multiple of the 64-k step, groups of 16
+    (96, 1000, 384, 128, False, "i8", "f16"),       # reference int8 activations, last group partial
+    (257, 512, 640, 256, True, "bf16", "f32"),
+])
+def test_int4_prefill_vs_oracle(sg, oracle_mod, token_tile, M, K, N, gs, sym, adt, cdt):
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=M + K, sym=sym)
+    rng = np.random.default_rng(N)
+    xo, xt, kw = _acts(oracle_mod, rng, M, K, adt)
+    bias = (0.1 * rng.standard_normal(N)).astype(np.float16)
+    scale_A = 0.05 if adt == "i8" else 1.0
+    want = oracle_mod.matmul_int4_grouped(xo, B, S, Z, K, N, gs, M=M, bias=bias, c_dt=oracle_mod.DT_F32,
+                                          scale_A=scale_A, **kw)
+    C = sg.matmul_int4_grouped(xt, t(B), t(S), None if Z is None else t(Z), K, N, gs, out_dtype=TDT[cdt],
+                               bias=t(bias), scale_A=scale_A)
+    close(C.float().cpu().numpy(), want)
+
+
+def test_int4_prefill_agrees_with_row_kernel(sg, oracle_mod):
+    """The tensor-core GEMM and the CUDA-core row kernel on one problem."""
+    M, K, N, gs = 160, 1024, 768, 32
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=7)
+    x = t(np.random.default_rng(8).standard_normal((M, K)).astype(np.float32))
+    args = (x, t(B), t(S), t(Z), K, N, gs)
+    a = sg.matmul_int4_grouped(*args, out_dtype=torch.float32)
+    sg.set_tuning("w4_gemv.path", 1)
+    try:
+        b = sg.matmul_int4_grouped(*args, out_dtype=torch.float32)
+    finally:
+        sg.set_tuning("w4_gemv.path", 0)
+    close(a.cpu().numpy(), b.cpu().numpy())
+    assert torch.equal(a, sg.matmul_int4_grouped(*args, out_dtype=torch.float32))  # deterministic
+
+
+@pytest.mark.parametrize("M,K,N,adt", [
+    (64, 512, 256, "bf16"),
+    (300, 1000, 1040, "f32"),
+    (129, 96, 128, "f16"),
+])
+def test_int8_prefill_vs_oracle(sg, oracle_mod, token_tile, M, K, N, adt):
+    rng = np.random.default_rng(M)
+    xo, xt, kw = _acts(oracle_mod, rng, M, K, adt)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    s = (rng.random(N) * 1e-3).astype(np.float32)
+    want = oracle_mod.gemm_w8_channel(xo, B, s, M, K, N, **kw)
+    C = torch.zeros((M, N), dtype=torch.float32, device=DEV)
+    _mm(sg, "sg_matmul_int8_channel", xt, t(B), C, M, K, N, scales=t(s))
+    close(C.cpu().numpy(), want)
+
+
+def _row_subset(M, seed):
+    rng = np.random.default_rng(seed)
+    return np.unique(np.concatenate([[0, 1, 127, 128, M - 1], rng.integers(0, M, 11)]))
+
+
+def test_prefill_benchmark_shape_int4(sg, oracle_mod):
+    """[2048, 2048] bf16 activations x INT4 symmetric groups of 64 [2048, 8192], bf16 out:
+    16 rows checked against the oracle, all rows finite."""
+    M, K, N, gs = 2048, 2048, 8192, 64
+    B, S, _ = w4_problem(oracle_mod, K, N, gs, seed=31, sym=True)
+    x32 = np.random.default_rng(32).standard_normal((M, K)).astype(np.float32)
+    C = sg.matmul_int4_grouped(bf16_tensor(x32), t(B), t(S), None, K, N, gs, out_dtype=torch.bfloat16)
+    rows = _row_subset(M, 33)
+    xo = oracle_mod.f32_to_bf16_bits(x32[rows])
+    want = oracle_mod.matmul_int4_grouped(xo, B, S, None, K, N, gs, M=len(rows), c_dt=oracle_mod.DT_F32,
+                                          a_bf16=True)
+    got = C.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    close(got[rows], want)
+
+
+def test_prefill_benchmark_shape_int8(sg, oracle_mod):
+    M, K, N = 2048, 2048, 8192
+    rng = np.random.default_rng(41)
+    x32 = rng.standard_normal((M, K)).astype(np.float32)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    s = (rng.random(N) * 1e-3).astype(np.float32)
+    C = torch.zeros((M, N), dtype=torch.bfloat16, device=DEV)
+    _mm(sg, "sg_matmul_int8_channel", bf16_tensor(x32), t(B), C, M, K, N, scales=t(s))
+    rows = _row_subset(M, 42)
+    want = oracle_mod.gemm_w8_channel(oracle_mod.f32_to_bf16_bits(x32[rows]), B, s, len(rows), K, N, a_bf16=True)
+    close(C.float().cpu().numpy()[rows], want)
+
+
+def test_prefill_caller_workspace_keeps_gemv_tickets(sg, oracle_mod):
+    """One caller workspace shared by the prefill GEMM (which converts fp32
+    activations into it) and the single-row GEMV (which keeps zeroed counters
+    at its start)."""
+    K, N, gs = 1024, 2048, 32
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=51)
+    rng = np.random.default_rng(52)
+    xm = t(rng.standard_normal((192, K)).astype(np.float32))
+    x1 = t(rng.standard_normal((1, K)).astype(np.float32))
+    wargs = (t(B), t(S), t(Z), K, N, gs)
+    need = max(sg.matmul_int4_grouped_workspace_size(xm, *wargs, out_dtype=torch.float32),
+               sg.matmul_int4_grouped_workspace_size(x1, *wargs, out_dtype=torch.float32))
+    ws = torch.zeros(need, dtype=torch.uint8, device=DEV)
+    ref_m = sg.matmul_int4_grouped(xm, *wargs, out_dtype=torch.float32)
+    ref_1 = sg.matmul_int4_grouped(x1, *wargs, out_dtype=torch.float32)
+    for _ in range(2):
+        assert torch.equal(sg.matmul_int4_grouped(xm, *wargs, out_dtype=torch.float32, workspace=ws), ref_m)
+        assert torch.equal(sg.matmul_int4_grouped(x1, *wargs, out_dtype=torch.float32, workspace=ws), ref_1)
+
+
+def test_prefill_no_device_error(sg):
+    from silicongraph_b200 import _lib
+    _lib.check(_lib.load().sg_device_error_check(torch.cuda.current_stream().cuda_stream))
