@@ -80,12 +80,12 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, interval_ms: int = 200):
         self.proc = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", str(interval_ms)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, ValueError):
             self.proc = None
@@ -312,6 +312,203 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ----------------------------------------------------------------------------- prefill GEMM workloads
+PF_M, PF_K, PF_N, PF_GS = 2048, 2048, 8192, 64
+PF_WORKLOADS = {
+    "prefill_int4": (f"prefill dequant-GEMM: A bf16 [{PF_M},{PF_K}] x W[{PF_K}x{PF_N}] int4 symmetric group {PF_GS} "
+                     f"(fp16 scales), C bf16 [{PF_M},{PF_N}]"),
+    "prefill_int8": (f"prefill dequant-GEMM: A bf16 [{PF_M},{PF_K}] x W[{PF_K}x{PF_N}] int8 per-channel "
+                     f"(f32 scales), C bf16 [{PF_M},{PF_N}]"),
+}
+
+
+def read_peak_tensor():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            return float(json.load(fh)["bf16_tflops"]), "measured bf16_tflops (burst)"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def prefill_cpu_sample(kind, seconds):
+    """CPU baseline for the prefill GEMM: the reference's own INT4 kernel
+    (one activation row per call, int8 activations) looped over sampled rows,
+    or the oracle's INT8 per-channel restatement; 1 thread."""
+    import oracle
+    M, K, N, gs = PF_M, PF_K, PF_N, PF_GS
+    rng = np.random.default_rng(5)
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+    if kind == "prefill_int4":
+        B = rng.integers(0, 256, (K // 2, N), dtype=np.uint8)
+        S = (rng.random((K // gs, N)) * 0.01).astype(np.float16)
+        A = rng.integers(-128, 128, (M, K), dtype=np.int8)
+        C = np.zeros(N, np.float16)
+        if oracle.ref_available():
+            fn, src = oracle.ref().sgref_neon_matmul_int4_grouped, "reference"
+            call = lambda m: fn(P(A[m]), P(B), P(S), None, P(C), K, N, gs)  # noqa: E731
+        else:
+            src = "port"
+            call = lambda m: oracle.matmul_int4_grouped(A[m:m + 1], B, S, None, K, N, gs)  # noqa: E731
+        what = "reference INT4 kernel (int8 activations, its only activation type), one row per call"
+    else:
+        B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+        s = (rng.random(N) * 1e-3).astype(np.float32)
+        A = oracle.f32_to_bf16_bits(rng.standard_normal((M, K)).astype(np.float32))
+        src = "port"
+        call = lambda m: oracle.gemm_w8_channel(A[m:m + 1], B, s, 1, K, N, a_bf16=True)  # noqa: E731
+        what = "oracle INT8 per-channel GEMM (restated GLSL gemm_int8 for bf16 activations), one row per call"
+    call(0)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        call(n % M)
+        n += 1
+    dt = time.perf_counter() - t0
+    tflops = n * 2.0 * K * N / dt / 1e12
+    return {"value": round(tflops, 6), "unit": "TFLOP/s", "cores": 1, "kind": src,
+            "sample": f"{n} rows of the [{M},{K}]x[{K},{N}] GEMM ({what}) in {dt:.1f} s on 1 host thread"}
+
+
+def run_prefill(args):
+    import torch
+    import torch.distributed as dist
+
+    from silicongraph_b200 import _lib, kernels
+
+    rank, local_rank, world = rank_env()
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    lib = _lib.load()
+    dev = torch.device("cuda", local_rank)
+    M, K, N, gs = PF_M, PF_K, PF_N, PF_GS
+    int4 = args.workload == "prefill_int4"
+    flops = 2.0 * M * K * N
+    rng = np.random.default_rng(4321 + rank)
+    a_host = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).to(torch.bfloat16).pin_memory()
+    W = torch.from_numpy((rng.standard_normal((K, N)) * 0.02).astype(np.float32)).to(dev)
+    stream = torch.cuda.Stream(dev)
+    st = stream.cuda_stream
+    A = a_host.to(dev)
+    A16 = A.half()  # the same activations in the operand type: the GEMM kernel alone
+    C = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    if int4:
+        B = torch.empty((K // 2, N), dtype=torch.uint8, device=dev)
+        S = torch.empty((K // gs, N), dtype=torch.float16, device=dev)
+        _lib.check(lib.sg_quantize_int4_grouped(W.data_ptr(), K, N, gs, 1, B.data_ptr(), S.data_ptr(), None, st))
+        stream.synchronize()
+        p_main = kernels.matmul_params(A, B, C, M=M, K=K, N=N, scales=S, group_size=gs)
+        p_kern = kernels.matmul_params(A16, B, C, M=M, K=K, N=N, scales=S, group_size=gs)
+        fn = lib.sg_matmul_int4_grouped
+        launches = 2  # activation conversion + GEMM
+        dtype = "f16"
+    else:
+        sc = (W.abs().amax(dim=0) / 127.0).clamp_min(1e-12)
+        B = torch.clamp(torch.round(W / sc), -127, 127).to(torch.int8)
+        S = sc.float().contiguous()
+        p_main = kernels.matmul_params(A, B, C, M=M, K=K, N=N, scales=S)
+        p_kern = p_main
+        fn = lib.sg_matmul_int8_channel
+        launches = 1
+        dtype = "bf16"
+    del W
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    flush = torch.empty(max(2 * l2, 256 << 20), dtype=torch.uint8, device=dev)
+
+    def call(p):
+        r = fn(ctypes.byref(p), st)
+        if r != 0:
+            raise _lib.SgError(r, _lib.last_error())
+
+    def timed(p, steps):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        with torch.cuda.stream(stream):
+            for e0, e1 in ev:
+                flush.zero_()  # L2 flushed between timed steps
+                e0.record(stream)
+                call(p)
+                e1.record(stream)
+        stream.synchronize()
+        return sum(e0.elapsed_time(e1) for e0, e1 in ev)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            call(p_main)
+            call(p_kern)
+    stream.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    clocks = ClockSampler(torch.cuda.current_device(), interval_ms=20) if rank == 0 else None
+    barrier()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(timed(p_main, args.steps))
+    ms_kern = max_over_ranks(timed(p_kern, args.steps)) if int4 else ms
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop() if clocks else None
+    value = world * args.steps * flops / (ms / 1e3) / 1e12
+    kern_tflops = args.steps * flops / (ms_kern / 1e3) / 1e12
+
+    # end to end: host activations -> device, GEMM through the C ABI, C -> host, every step
+    e2e_steps = max(1, min(args.steps, 10))
+    c_host = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            A.copy_(a_host, non_blocking=True)
+            call(p_main)
+            c_host.copy_(C, non_blocking=True)
+        e1.record(stream)
+    stream.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = world * e2e_steps * flops / (e2e_ms / 1e3) / 1e12
+    peak, peak_src = read_peak_tensor()
+    line = {
+        "metric": "prefill dequant-GEMM TFLOP/s (" + ("INT4 g64 symmetric" if int4 else "INT8 per-channel") + ")",
+        "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": dtype,
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, host-generated)",
+        "config": {"workload": PF_WORKLOADS[args.workload], "M": M, "K": K, "N": N,
+                   "group_size": gs if int4 else None, "flops_per_step": flops,
+                   "l2": "flushed (256 MB write) before every timed step",
+                   "parallelism": f"replicas x{world} (no data-path collective)",
+                   "timing": "CUDA events around each step, summed; max over ranks"},
+        "roofline": {"bound": "tensor", "achieved": round(kern_tflops, 2), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(kern_tflops / peak, 4), "peak_source": peak_src, "traffic": None,
+                     "achieved_basis": "algorithmic FLOPs / event time of the GEMM kernel alone "
+                     + ("(fp16 activations, no conversion launch)" if int4 else "")},
+        "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "steps": e2e_steps,
+                "h2d_bytes_per_step": int(a_host.numel() * 2), "d2h_bytes_per_step": int(c_host.numel() * 2)},
+        "gpu_launches": args.steps * launches,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            line["cpu_baseline"] = prefill_cpu_sample(args.workload, args.cpu_seconds)
+        except Exception as e:  # the baseline is reported, never required
+            line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args):
     rank, _, world = rank_env()
@@ -395,6 +592,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--ref-budget-s", type=float, default=120.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["gemv_int4", *PF_WORKLOADS], default="gemv_int4",
+                    help="gemv_int4 (default): the decode GEMV; prefill_int4 / prefill_int8: the prefill GEMM")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -403,7 +602,11 @@ def main():
         if args.gpus > 1 and world == 1:
             ap.error("for --gpus N > 1 launch with torch.distributed.run --nproc-per-node N")
     if args.impl == "reference":
+        if args.workload != "gemv_int4":
+            ap.error("--impl reference times the decode GEMV workload")
         run_reference(args)
+    elif args.workload in PF_WORKLOADS:
+        run_prefill(args)
     else:
         run_ours(args)
 

@@ -44,11 +44,24 @@ using namespace sgd;
 
 constexpr int kKStep = 64;    // k per pipeline step: one 128-byte swizzle row of 16-bit values
 constexpr int kWCols = 128;   // weight columns per tile = TMEM lanes = UMMA M
-constexpr int kEpiWarps = 4;  // warps 0..3: epilogue, lane quarter = warp
-constexpr int kPrepWarps = 8; // warps 4..11: dequant, lane quarter = warp % 4, k half = (warp - 4) / 4
-constexpr int kWarpTma = kEpiWarps + kPrepWarps;  // 12
-constexpr int kWarpMma = kWarpTma + 1;            // 13
-constexpr int kThreads = (kWarpMma + 1) * 32;     // 448
+// Warp roles.  Warps 0..3: epilogue, TMEM lane quarter = warp.  Then 8 * PAR
+// dequant warps: lane quarter = warp % 4, k half of the step = bit 2 of the
+// dequant index, and with PAR = 2 the step parity = bit 3 (two steps are
+// dequantized concurrently).  Then two TMA producer warps (activations;
+// weights, scales and zeros) and the MMA warp.  One thread cannot issue
+// tcgen05.mma faster than about one per 105 cycles, and each TMA issue costs
+// on the order of 100 cycles, so every single-thread role gets its own warp.
+constexpr int kEpiWarps = 4;
+constexpr int kStepWarps = 8;  // dequant warps that complete one step (4 quarters x 2 k halves)
+__host__ __device__ constexpr int prep_warps(int par) { return kStepWarps * par; }
+__host__ __device__ constexpr int warp_tma_act(int par) { return kEpiWarps + prep_warps(par); }
+__host__ __device__ constexpr int warp_tma_w(int par) { return warp_tma_act(par) + 1; }
+__host__ __device__ constexpr int warp_mma(int par) { return warp_tma_w(par) + 1; }
+__host__ __device__ constexpr int threads_of(int par) { return (warp_mma(par) + 1) * 32; }
+constexpr int kOutChunk = 32;                         // tokens per epilogue TMA store
+constexpr int kOutBuf = kOutChunk * 128 * 2;          // one 16-bit [32 x 128] staging tile
+constexpr int kOutBufs = 3;                           // staging ring (one barrier per chunk)
+constexpr int kEpiBarrier = 1;                        // named barrier of the epilogue warps
 constexpr int kTmemCols = 512;
 
 enum WKind : int { kW4Grouped = 0, kW8Channel = 1 };
@@ -62,13 +75,17 @@ struct Cfg {
   static constexpr int kStageBytes = kActBytes + kWBytes + kSBytes + kZBytes;
   static constexpr int kStride = (kStageBytes + 1023) / 1024 * 1024;  // act tile stays 1024-aligned
   static constexpr int kAcc = (2 * BT + 4 * 32 <= kTmemCols) ? 2 : 1;
-  static constexpr int kStagesTmem = (kTmemCols - kAcc * BT) / 32;
-  static constexpr int kStagesSmem = (227 * 1024 - 2048) / kStride;
-  static constexpr int kStages0 = kStagesTmem < kStagesSmem ? kStagesTmem : kStagesSmem;
-  static constexpr int kStages = kStages0 > 8 ? 8 : kStages0;
-  static constexpr int kBarBytes = (4 * kStages + 2 * 2 + 1) * 8 + 16;
-  static constexpr int kSmem = kStages * kStride + kBarBytes + 1024;  // + alignment slack
-  static_assert(kStages >= 2, "pipeline needs two stages");
+  // Two rings: shared-memory stages (TMA -> dequant / MMA) and TMEM slots of
+  // dequantized weights (dequant -> MMA), each as deep as its memory allows.
+  static constexpr int kSlots0 = (kTmemCols - kAcc * BT) / 32;
+  static constexpr int kSlots = kSlots0 > 8 ? 8 : kSlots0;
+  static constexpr int kStages0 = (227 * 1024 - 2048 - kOutBufs * kOutBuf) / kStride;
+  static constexpr int kStages = kStages0 > 12 ? 12 : kStages0;
+  static constexpr int kBarBytes = (2 * kStages + 2 * kSlots + 2 * 2 + 1) * 8 + 16;
+  static constexpr int kOutOff = kStages * kStride;  // epilogue staging ring
+  static constexpr int kBarOff = kOutOff + kOutBufs * kOutBuf;
+  static constexpr int kSmem = kBarOff + kBarBytes + 1024;  // + alignment slack
+  static_assert(kStages >= 2 && kSlots >= 2, "pipeline needs two stages");
   static_assert(BT % 32 == 0 && BT >= 32 && BT <= 256, "token tile");
 };
 
@@ -84,6 +101,8 @@ struct GArgs {
   int gs;                // INT4 group size
   int ksteps;
   int n_tiles, m_tiles;
+  int spin;       // 1: single-thread waits spin on test_wait
+  int tma_store;  // 1: 16-bit C written by TMA stores from shared memory
   int* err;
 };
 
@@ -111,51 +130,75 @@ __device__ __forceinline__ uint32_t ld_shared_u16(uint32_t addr) {
   return v;
 }
 
-// 32 accumulator columns (tokens) of one output column n -> C, rows base, base + ldc, ...
-template <int DT, int WK>
-__device__ __forceinline__ void epi_store(const uint32_t (&r)[32], int cnt, const GArgs& a, int64_t base, float mul,
-                                          float add) {
+// 32 finished values (tokens) of one output column -> C rows base, base + ldc, ...
+template <int DT>
+__device__ __forceinline__ void epi_store(const uint32_t (&r)[32], int cnt, const GArgs& a, int64_t base) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    if (j < cnt) {
-      float v = __uint_as_float(r[j]);
-      if (WK == kW4Grouped) {
-        if (a.apply_scale_A) v = __fmul_rn(v, a.scale_A);
-        v = __fadd_rn(v, add);
-      } else {
-        v = __fmul_rn(v, mul);
-      }
-      store_from_float<DT>(a.C, base + (int64_t)j * a.ldc, v);
-    }
-  }
+  for (int j = 0; j < 32; ++j)
+    if (j < cnt) store_from_float<DT>(a.C, base + (int64_t)j * a.ldc, __uint_as_float(r[j]));
 }
 
-// Bounded wait by every lane of a warp with a warp-uniform outcome, so that
-// the .sync.aligned tcgen05 instructions after it see a converged warp.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err) {
-  const bool ok = mbar_wait(bar, parity, err);
-  return __all_sync(0xffffffffu, ok) != 0;
+// Bounded wait by every lane of a warp, then reconvergence.  A lane whose
+// wait times out raises the CTA abort flag; the warp still finishes the
+// current step (its results are then invalid and the device error word says
+// so) and leaves at the next step, where all lanes read the flag together.
+// Every lane waits itself: electing one lane and broadcasting its result
+// costs about three times as much per wait.
+__device__ __forceinline__ void warp_wait(uint64_t* bar, uint32_t parity, int* err, int spin,
+                                          volatile int* abort_flag) {
+  const bool ok = spin ? mbar_wait_spin(bar, parity, err) : mbar_wait(bar, parity, err);
+  if (!ok) *abort_flag = 1;
+  __syncwarp();
 }
-__device__ __forceinline__ bool warp_wait_sleep(uint64_t* bar, uint32_t parity, int* err) {
-  const bool ok = mbar_wait_sleep(bar, parity, err);
-  return __all_sync(0xffffffffu, ok) != 0;
+
+// Named barrier of the 128 epilogue threads; returns the OR of pred over them.
+__device__ __forceinline__ bool epi_bar_or(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n"
+      " barrier.red.or.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "n"(kEpiBarrier), "n"(kEpiWarps * 32)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void epi_bar_sync() {
+  asm volatile("barrier.sync %0, %1;" ::"n"(kEpiBarrier), "n"(kEpiWarps * 32) : "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(smem_u32(smem_src))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_le1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ uint16_t to_out16(float v, int dt) {
+  if (dt == SG_DT_BF16) return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  return __half_as_ushort(__float2half_rn(v));
 }
 
 // BT tokens per tile; WK weight kind; BF16_OP: operand type (INT8 with bf16 activations); HAS_Z: INT4 zeros.
-template <int BT, int WK, bool BF16_OP, bool HAS_Z>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BT, int WK, bool BF16_OP, bool HAS_Z, int PAR>
+__global__ void __launch_bounds__(threads_of(PAR), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmAct, const __grid_constant__ CUtensorMap tmW,
-                   const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmZ, GArgs a) {
+                   const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmZ,
+                   const __grid_constant__ CUtensorMap tmC, GArgs a) {
   using C_ = Cfg<BT, WK>;
-  constexpr int S = C_::kStages, kAcc = C_::kAcc;
+  constexpr int S = C_::kStages, J = C_::kSlots, kAcc = C_::kAcc;
+  constexpr int kWarpAct = warp_tma_act(PAR), kWarpW = warp_tma_w(PAR), kWarpMma = warp_mma(PAR);
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * C_::kStride);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C_::kBarOff);
   uint64_t* empty = full + S;
   uint64_t* afull = empty + S;
-  uint64_t* aempty = afull + S;
-  uint64_t* accfull = aempty + S;
+  uint64_t* aempty = afull + J;
+  uint64_t* accfull = aempty + J;
   uint64_t* accempty = accfull + 2;
   uint64_t* done = accempty + 2;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(done + 1);
@@ -164,10 +207,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 2);  // one expect_tx arrival per producer
       mbar_init(&empty[s], 1);
-      mbar_init(&afull[s], kPrepWarps);
-      mbar_init(&aempty[s], 1);
+    }
+    for (int j = 0; j < J; ++j) {
+      mbar_init(&afull[j], kStepWarps);
+      mbar_init(&aempty[j], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accfull[i], 1);
@@ -181,12 +226,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(tslot, kTmemCols);
     tmem_relinquish();
   }
-  if (warp == kWarpTma && lane == 0) {
-    tma_prefetch_desc(&tmAct);
+  if (warp == kWarpAct && lane == 0) tma_prefetch_desc(&tmAct);
+  if (warp == kWarpW && lane == 0) {
     tma_prefetch_desc(&tmW);
     if (WK == kW4Grouped) tma_prefetch_desc(&tmS);
     if (HAS_Z) tma_prefetch_desc(&tmZ);
   }
+  if (warp == 0 && lane == 0 && a.tma_store) tma_prefetch_desc(&tmC);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -197,15 +243,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tiles = a.n_tiles * a.m_tiles;
   const int ksteps = a.ksteps;
 
-  if (warp == kWarpTma) {
-    // ------------------------------------------------------------ TMA producer
+  if (warp == kWarpAct || warp == kWarpW) {
+    // ------------------------------------------------------------ TMA producers
     if (lane == 0) {
-      uint32_t issued[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      const bool is_act = warp == kWarpAct;
+      uint32_t issued[S];
+      for (int s = 0; s < S; ++s) issued[s] = 0;
       const int gs = a.gs;
-      uint32_t bytes = C_::kActBytes + C_::kWBytes;
-      int srows = 1;
-      if (WK == kW4Grouped) {
-        srows = gs >= kKStep ? 1 : kKStep / gs;
+      uint32_t bytes = is_act ? C_::kActBytes : C_::kWBytes;
+      if (!is_act && WK == kW4Grouped) {
+        const int srows = gs >= kKStep ? 1 : kKStep / gs;
         bytes += srows * kWCols * 2 + (HAS_Z ? srows * kWCols : 0);
       }
       uint32_t g = 0;
@@ -215,15 +262,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int ks = 0; ks < ksteps; ++ks, ++g) {
           const int s = g % S;
           const uint32_t use = g / S;
-          if (*abort_flag || !mbar_wait(&empty[s], (use & 1) ^ 1, a.err)) {
+          if (*abort_flag || !(a.spin ? mbar_wait_spin(&empty[s], (use & 1) ^ 1, a.err)
+                                      : mbar_wait(&empty[s], (use & 1) ^ 1, a.err))) {
             *abort_flag = 1;
             ok = false;
             break;
           }
           unsigned char* st = smem + s * C_::kStride;
           mbar_arrive_expect_tx(&full[s], bytes);
-          tma_load_2d(st, &tmAct, ks * kKStep, m0, &full[s]);
-          if (WK == kW4Grouped) {
+          if (is_act) {
+            tma_load_2d(st, &tmAct, ks * kKStep, m0, &full[s]);
+          } else if (WK == kW4Grouped) {
             tma_load_2d(st + C_::kActBytes, &tmW, n0, ks * (kKStep / 2), &full[s]);
             const int grow = (ks * kKStep) / gs;
             tma_load_2d(st + C_::kActBytes + C_::kWBytes, &tmS, n0, grow, &full[s]);
@@ -255,21 +304,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t dt = tbase + acc * BT;
         for (int ks = 0; ks < ksteps; ++ks, ++g) {
-          const int s = g % S;
-          const uint32_t use = g / S;
-          if (*abort_flag || !mbar_wait(&afull[s], use & 1, a.err) || !mbar_wait(&full[s], use & 1, a.err)) {
+          const int s = g % S, j = g % J;
+          const uint32_t juse = g / J;
+          // The dequant warps arrive on afull[j] only after they observed full[s], which
+          // also covers the activation tile of this stage.
+          if (*abort_flag || !(a.spin ? mbar_wait_spin(&afull[j], juse & 1, a.err)
+                                      : mbar_wait(&afull[j], juse & 1, a.err))) {
             *abort_flag = 1;
             ok = false;
             break;
           }
           tc_fence_after();
           const uint64_t bdesc = umma_smem_desc(smem_u32(smem + s * C_::kStride), 16, 1024, kSwizzle128B);
-          const uint32_t at = tbase + kAcc * BT + s * 32;
+          const uint32_t at = tbase + kAcc * BT + j * 32;
 #pragma unroll
           for (int kk = 0; kk < kKStep / 16; ++kk)
             umma_f16_ts(dt, at + kk * 8, bdesc + (uint64_t)(kk * 2), idesc, (ks | kk) != 0 ? 1u : 0u);
           umma_commit(&empty[s]);
-          umma_commit(&aempty[s]);
+          umma_commit(&aempty[j]);
         }
         if (ok) umma_commit(&accfull[acc]);
       }
@@ -278,31 +330,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= kEpiWarps) {
     // ------------------------------------------------------------ dequant warps
-    const int q = warp & 3, h = (warp - kEpiWarps) >> 2;
+    const int pw = warp - kEpiWarps;
+    const int q = warp & 3, h = (pw >> 2) & 1, par = pw >> 3;
     const int col = q * 32 + lane;  // column within the tile = TMEM lane
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     uint32_t g = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
       for (int ks = 0; ks < ksteps; ++ks, ++g) {
-        const int s = g % S;
-        const uint32_t use = g / S;
-        const bool go = __all_sync(0xffffffffu, *abort_flag == 0) && warp_wait(&full[s], use & 1, a.err) &&
-                        warp_wait(&aempty[s], (use & 1) ^ 1, a.err);
-        if (!go) {
-          *abort_flag = 1;
+        if (PAR > 1 && (int)(g % PAR) != par) continue;
+        __syncwarp();
+        if (*abort_flag) {  // one shared load of a converged warp: the same value in every lane
           ok = false;
           break;
         }
+        const int s = g % S, j = g % J;
+        const uint32_t use = g / S, juse = g / J;
+        warp_wait(&full[s], use & 1, a.err, a.spin, abort_flag);
+        warp_wait(&aempty[j], (juse & 1) ^ 1, a.err, a.spin, abort_flag);
         tc_fence_after();
         const uint32_t wbase = smem_u32(smem + s * C_::kStride + C_::kActBytes);
-        uint32_t w[16];
         if (WK == kW4Grouped) {
           // rows 16h .. 16h+15 of the packed tile: k = 32h .. 32h+31 of this step
+          uint32_t w[16];
           const uint32_t sbase = wbase + C_::kWBytes;
           const uint32_t zbase = sbase + C_::kSBytes;
           const int gs = a.gs;
-          // group rows used by this half: first 8 rows and last 8 rows
+          // scale rows of this half: rows 0..7 and 8..15 (differ only for groups of 16)
           const int g0 = gs >= kKStep ? 0 : (32 * h) / gs;
           const int g1 = gs >= kKStep ? 0 : (32 * h + 16) / gs;
           const __half2 s0 = __half2half2(__ushort_as_half((unsigned short)ld_shared_u16(sbase + (g0 * kWCols + col) * 2)));
@@ -322,6 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const __half2 t = __hsub2(u_as_h2(x), i < 8 ? c0 : c1);  // q - 8 - zero, exact
             w[i] = h2_as_u(__hmul2(t, i < 8 ? s0 : s1));              // fp16(scale * (q - 8 - zero))
           }
+          tmem_st_32x32b_x16(tbase + lane_addr + kAcc * BT + j * 32 + 16 * h, w);
         } else {
           // rows 32h .. 32h+31 of the int8 tile: k = 32h .. 32h+31 of this step, in two passes of 16
 #pragma unroll 1
@@ -341,31 +396,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                 w8[i] = h2_as_u(__hsub2(u_as_h2(x), __half2half2(__int2half_rn(1152))));
               }
             }
-            tmem_st_32x32b_x8(tbase + lane_addr + kAcc * BT + s * 32 + 16 * h + 8 * o, w8);
+            tmem_st_32x32b_x8(tbase + lane_addr + kAcc * BT + j * 32 + 16 * h + 8 * o, w8);
           }
         }
-        if (WK == kW4Grouped) tmem_st_32x32b_x16(tbase + lane_addr + kAcc * BT + s * 32 + 16 * h, w);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&afull[s]);
+        if (lane == 0) mbar_arrive(&afull[j]);
       }
     }
   } else {
     // ------------------------------------------------------------ epilogue warps
     const int q = warp;
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    const int col = q * 32 + lane;
+    unsigned char* out_ring = smem + C_::kOutOff;
+    uint32_t chunk = 0;  // chunks stored so far: staging buffer = chunk % kOutBufs
     int lt = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++lt) {
       const int acc = lt % kAcc;
       const uint32_t ause = lt / kAcc;
-      const bool go = __all_sync(0xffffffffu, *abort_flag == 0) && warp_wait_sleep(&accfull[acc], ause & 1, a.err);
-      if (!go) {
+      const bool ok = *abort_flag == 0 && mbar_wait_sleep(&accfull[acc], ause & 1, a.err);
+      // The four epilogue warps leave together (they share a named barrier below).
+      if (epi_bar_or(!ok)) {
         *abort_flag = 1;
         break;
       }
       tc_fence_after();
-      const int n = (tile % a.n_tiles) * kWCols + q * 32 + lane;
+      const int n0 = (tile % a.n_tiles) * kWCols;
+      const int n = n0 + col;
       const int m0 = (tile / a.n_tiles) * BT;
       const bool nvalid = n < a.N;
       float mul = 1.f, add = 0.f;
@@ -375,23 +434,55 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int mrows = min(BT, a.M - m0);
 #pragma unroll 1
-      for (int c = 0; c < BT / 32; ++c) {
+      for (int c = 0; c < BT / kOutChunk; ++c) {
         uint32_t r[32];
-        tmem_ld_32x32b_x32(tbase + lane_addr + acc * BT + c * 32, r);
+        tmem_ld_32x32b_x32(tbase + lane_addr + acc * BT + c * kOutChunk, r);
         tmem_ld_wait();
-        if (c * 32 >= mrows || !nvalid) continue;
-        const int cnt = min(32, mrows - c * 32);
-        const int64_t base = (int64_t)(m0 + c * 32) * a.ldc + n;
-        switch (a.c_dt) {
-          case SG_DT_F32: epi_store<SG_DT_F32, WK>(r, cnt, a, base, mul, add); break;
-          case SG_DT_BF16: epi_store<SG_DT_BF16, WK>(r, cnt, a, base, mul, add); break;
-          default: epi_store<SG_DT_F16, WK>(r, cnt, a, base, mul, add); break;
+        if (c == BT / kOutChunk - 1) {  // accumulator read out: the MMA may reuse it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&accempty[acc]);
+        }
+        if (c * kOutChunk >= mrows) continue;  // uniform over the epilogue warps
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float v = __uint_as_float(r[j]);
+          if (WK == kW4Grouped) {
+            if (a.apply_scale_A) v = __fmul_rn(v, a.scale_A);
+            v = __fadd_rn(v, add);
+          } else {
+            v = __fmul_rn(v, mul);
+          }
+          r[j] = __float_as_uint(v);
+        }
+        if (a.tma_store) {
+          // [32 tokens x 128 columns] 16-bit tile, then one TMA store (clipped at M and N).
+          // The buffer written now was last read by the store of chunk - 3, which thread 0
+          // waited for before it arrived at the previous chunk's barrier.
+          unsigned char* buf = out_ring + (chunk % kOutBufs) * kOutBuf;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            *reinterpret_cast<uint16_t*>(buf + j * 256 + col * 2) = to_out16(__uint_as_float(r[j]), a.c_dt);
+          fence_proxy_async_smem();
+          epi_bar_sync();
+          if (threadIdx.x == 0) {
+            tma_store_2d(&tmC, buf, n0, m0 + c * kOutChunk);
+            bulk_commit();
+            bulk_wait_read_le1();
+          }
+          ++chunk;
+        } else if (nvalid) {
+          const int cnt = min(32, mrows - c * kOutChunk);
+          const int64_t base = (int64_t)(m0 + c * kOutChunk) * a.ldc + n;
+          switch (a.c_dt) {
+            case SG_DT_F32: epi_store<SG_DT_F32>(r, cnt, a, base); break;
+            case SG_DT_BF16: epi_store<SG_DT_BF16>(r, cnt, a, base); break;
+            default: epi_store<SG_DT_F16>(r, cnt, a, base); break;
+          }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&accempty[acc]);
     }
+    if (threadIdx.x == 0 && a.tma_store) bulk_wait_all();  // stores done before the CTA exits
   }
 
   tc_fence_before();
@@ -446,6 +537,9 @@ constexpr size_t kConvOffset = 64 * 1024;
 
 std::atomic<int> g_tune_bt{0};        // 0 = automatic
 std::atomic<int> g_tune_min_rows{64};  // smallest M sent to the tensor-core GEMM
+std::atomic<int> g_tune_par{2};        // dequant warp groups working on alternate k steps
+std::atomic<int> g_tune_spin{0};       // single-thread waits spin on test_wait
+std::atomic<int> g_tune_tma_store{1};  // 16-bit outputs through TMA stores
 
 struct GPlan {
   bool ok = false;
@@ -459,21 +553,14 @@ struct GPlan {
 int pick_bt(int M, int N, int sms) {
   const int tune = g_tune_bt.load();
   if (tune == 128 || tune == 192 || tune == 256) return tune;
-  // Fewest rounds of tiles over the SMs, larger tiles on ties.
+  // Each activation tile is re-read from L2 for every 128 weight columns, so
+  // the widest token tile moves the fewest bytes per MMA; a narrower one only
+  // pays off when it needs fewer rounds of tiles over the SMs.
   const int n_tiles = (N + kWCols - 1) / kWCols;
-  int best = 128;
-  double best_cost = 1e30;
-  for (int bt : {256, 192, 128}) {
-    const int m_tiles = (M + bt - 1) / bt;
-    const int tiles = n_tiles * m_tiles;
-    const int rounds = (tiles + sms - 1) / sms;
-    const double cost = (double)rounds * bt;
-    if (cost < best_cost * 0.999) {
-      best_cost = cost;
-      best = bt;
-    }
-  }
-  return best;
+  auto rounds = [&](int bt) { return (n_tiles * ((M + bt - 1) / bt) + sms - 1) / sms; };
+  if (M > 192 && rounds(256) <= rounds(192)) return 256;
+  if (M > 128 && rounds(192) <= rounds(128)) return 192;
+  return M > 128 ? 256 : 128;
 }
 
 GPlan make_plan(const SgMatMulParams* p, int wkind) {
@@ -500,11 +587,11 @@ GPlan make_plan(const SgMatMulParams* p, int wkind) {
   return pl;
 }
 
-template <int BT, int WK, bool BF16_OP, bool HAS_Z>
+template <int BT, int WK, bool BF16_OP, bool HAS_Z, int PAR>
 SgStatus launch(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tz,
-                const GArgs& a, int grid, cudaStream_t cs) {
+                const CUtensorMap& tc, const GArgs& a, int grid, cudaStream_t cs) {
   using C_ = Cfg<BT, WK>;
-  auto kfn = gemm_tc_kernel<BT, WK, BF16_OP, HAS_Z>;
+  auto kfn = gemm_tc_kernel<BT, WK, BF16_OP, HAS_Z, PAR>;
   static std::atomic<uint64_t> attr_set{0};  // bit per device ordinal
   int dev = 0;
   SgStatus dst = sg::current_device(&dev);
@@ -522,7 +609,7 @@ SgStatus launch(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap&
   }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(threads_of(PAR));
   cfg.dynamicSmemBytes = C_::kSmem;
   cfg.stream = cs;
   cudaLaunchAttribute attr[1];
@@ -530,7 +617,7 @@ SgStatus launch(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap&
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, ta, tw, ts, tz, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, ta, tw, ts, tz, tc, a);
   if (e != cudaSuccess) {
     cudaGetLastError();
     sg::set_error("gemm_tc_kernel launch failed: %s", cudaGetErrorString(e));
@@ -539,14 +626,21 @@ SgStatus launch(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap&
   return SG_OK;
 }
 
-template <int WK, bool BF16_OP, bool HAS_Z>
+template <int WK, bool BF16_OP, bool HAS_Z, int PAR>
 SgStatus launch_bt(int bt, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& ts,
-                   const CUtensorMap& tz, const GArgs& a, int grid, cudaStream_t cs) {
+                   const CUtensorMap& tz, const CUtensorMap& tc, const GArgs& a, int grid, cudaStream_t cs) {
   switch (bt) {
-    case 256: return launch<256, WK, BF16_OP, HAS_Z>(ta, tw, ts, tz, a, grid, cs);
-    case 192: return launch<192, WK, BF16_OP, HAS_Z>(ta, tw, ts, tz, a, grid, cs);
-    default: return launch<128, WK, BF16_OP, HAS_Z>(ta, tw, ts, tz, a, grid, cs);
+    case 256: return launch<256, WK, BF16_OP, HAS_Z, PAR>(ta, tw, ts, tz, tc, a, grid, cs);
+    case 192: return launch<192, WK, BF16_OP, HAS_Z, PAR>(ta, tw, ts, tz, tc, a, grid, cs);
+    default: return launch<128, WK, BF16_OP, HAS_Z, PAR>(ta, tw, ts, tz, tc, a, grid, cs);
   }
+}
+
+template <int WK, bool BF16_OP, bool HAS_Z>
+SgStatus launch_par(int par, int bt, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& ts,
+                    const CUtensorMap& tz, const CUtensorMap& tc, const GArgs& a, int grid, cudaStream_t cs) {
+  if (par == 1) return launch_bt<WK, BF16_OP, HAS_Z, 1>(bt, ta, tw, ts, tz, tc, a, grid, cs);
+  return launch_bt<WK, BF16_OP, HAS_Z, 2>(bt, ta, tw, ts, tz, tc, a, grid, cs);
 }
 
 }  // namespace
@@ -650,20 +744,47 @@ SgStatus gemm_tc_run(const SgMatMulParams* p, bool int8_weights, cudaStream_t cs
   a.n_tiles = (p->N + kWCols - 1) / kWCols;
   a.m_tiles = (p->M + bt - 1) / bt;
   a.err = err_word;
+  a.spin = g_tune_spin.load() ? 1 : 0;
+  // 16-bit C with 16-byte aligned rows: TMA stores from a shared-memory staging tile.
+  CUtensorMap tc = ta;
+  a.tma_store = 0;
+  if ((a.c_dt == SG_DT_F16 || a.c_dt == SG_DT_BF16) && aligned16(p->C) && ((size_t)a.ldc * 2) % 16 == 0 &&
+      g_tune_tma_store.load()) {
+    const uint64_t dims[2] = {(uint64_t)p->N, (uint64_t)p->M};
+    const uint64_t str[1] = {(uint64_t)a.ldc * 2};
+    const uint32_t box[2] = {(uint32_t)kWCols, (uint32_t)kOutChunk};
+    st = make_tensor_map(&tc, a.c_dt == SG_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                         2, p->C, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != SG_OK) return st;
+    a.tma_store = 1;
+  }
   const int tiles = a.n_tiles * a.m_tiles;
   const int grid = std::min(tiles, sms);
   *handled = true;
+  const int par = g_tune_par.load() == 1 ? 1 : 2;
   if (wk == kW4Grouped) {
-    if (p->zeros_B) return launch_bt<kW4Grouped, false, true>(bt, ta, tw, ts, tz, a, grid, cs);
-    return launch_bt<kW4Grouped, false, false>(bt, ta, tw, ts, tz, a, grid, cs);
+    if (p->zeros_B) return launch_par<kW4Grouped, false, true>(par, bt, ta, tw, ts, tz, tc, a, grid, cs);
+    return launch_par<kW4Grouped, false, false>(par, bt, ta, tw, ts, tz, tc, a, grid, cs);
   }
-  if (pl.bf16_op) return launch_bt<kW8Channel, true, false>(bt, ta, tw, ts, tz, a, grid, cs);
-  return launch_bt<kW8Channel, false, false>(bt, ta, tw, ts, tz, a, grid, cs);
+  if (pl.bf16_op) return launch_par<kW8Channel, true, false>(par, bt, ta, tw, ts, tz, tc, a, grid, cs);
+  return launch_par<kW8Channel, false, false>(par, bt, ta, tw, ts, tz, tc, a, grid, cs);
 }
 
 bool gemm_tc_tuning(std::string_view key, int value) {
   if (key == "gemm_tc.bt") {
     g_tune_bt.store(value);
+    return true;
+  }
+  if (key == "gemm_tc.tma_store") {
+    g_tune_tma_store.store(value);
+    return true;
+  }
+  if (key == "gemm_tc.spin") {
+    g_tune_spin.store(value);
+    return true;
+  }
+  if (key == "gemm_tc.par") {
+    g_tune_par.store(value);
     return true;
   }
   if (key == "gemm_tc.min_rows") {

@@ -29,11 +29,17 @@ def _acts(oracle_mod, rng, M, K, adt):
 TDT = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
 
 
-@pytest.fixture(params=[0, 128, 192, 256], ids=["bt_auto", "bt128", "bt192", "bt256"])
+@pytest.fixture(params=[(0, 2), (128, 1), (128, 2), (192, 1), (192, 2), (256, 2)],
+                ids=["auto", "bt128_par1", "bt128_par2", "bt192_par1", "bt192_par2", "bt256_par2"])
 def token_tile(sg, request):
-    sg.set_tuning("gemm_tc.bt", request.param)
+    """Token tile of the GEMM (0 = automatic) and the number of dequant warp
+    groups working on alternate k steps."""
+    bt, par = request.param
+    sg.set_tuning("gemm_tc.bt", bt)
+    sg.set_tuning("gemm_tc.par", par)
     yield request.param
     sg.set_tuning("gemm_tc.bt", 0)
+    sg.set_tuning("gemm_tc.par", 2)
 
 
 @pytest.mark.parametrize("M,K,N,gs,sym,adt,cdt", [
@@ -145,3 +151,30 @@ def test_prefill_caller_workspace_keeps_gemv_tickets(sg, oracle_mod):
 def test_prefill_no_device_error(sg):
     from silicongraph_b200 import _lib
     _lib.check(_lib.load().sg_device_error_check(torch.cuda.current_stream().cuda_stream))
+
+
+@pytest.mark.parametrize("cdt", [torch.bfloat16, torch.float16])
+def test_prefill_store_paths_identical(sg, oracle_mod, cdt):
+    """The TMA-store epilogue and the direct-store epilogue write the same bits,
+    also into a C with padded rows (ldc > N) and ragged M / N edges."""
+    import ctypes
+    from silicongraph_b200 import _lib
+    M, K, N, gs = 200, 512, 400, 32
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=61)
+    x = t(np.random.default_rng(62).standard_normal((M, K)).astype(np.float32)).to(torch.bfloat16)
+    outs = []
+    for tma in (1, 0):
+        sg.set_tuning("gemm_tc.tma_store", tma)
+        try:
+            Cpad = torch.full((M, N + 24), 7.0, dtype=cdt, device=DEV)
+            p = sg.matmul_params(x, t(B), Cpad, M=M, K=K, N=N, scales=t(S), zeros=t(Z), group_size=gs)
+            p.ldc = N + 24
+            _lib.check(_lib.load().sg_matmul_int4_grouped(ctypes.byref(p), torch.cuda.current_stream().cuda_stream))
+            outs.append(Cpad)
+        finally:
+            sg.set_tuning("gemm_tc.tma_store", 1)
+    assert torch.equal(outs[0], outs[1])
+    assert (outs[0][:, N:] == 7.0).all()  # the padding columns are untouched
+    want = oracle_mod.matmul_int4_grouped(oracle_mod.f32_to_bf16_bits(x.float().cpu().numpy()), B, S, Z, K, N, gs,
+                                          M=M, c_dt=oracle_mod.DT_F32, a_bf16=True)
+    close(outs[0][:, :N].float().cpu().numpy(), want)
