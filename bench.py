@@ -509,6 +509,167 @@ def run_prefill(args):
         dist.destroy_process_group()
 
 
+# ----------------------------------------------------------------------------- attention workloads
+ATTN_WORKLOADS = {
+    # name: (B, H, Hkv, S, D, dtype, description)
+    "attn_prefill": (1, 28, 4, 8192, 128, "bf16",
+                     "causal flash attention, Qwen2.5-7B prefill layer: Q bf16 [1,28,8192,128], "
+                     "K/V bf16 [1,4,8192,128] (GQA 7), scale 1/sqrt(128)"),
+    "attn_small": (1, 32, 32, 512, 64, "f32",
+                   "causal flash attention: Q/K/V fp32 [1,32,512,64], scale 1/8 (CPU-runnable case)"),
+}
+
+
+def attn_flops(H, S, D):
+    """Causal: each query attends to itself and the keys before it; QK^T and PV
+    cost 2 * D each per (query, key) pair."""
+    return 4.0 * H * D * S * (S + 1) / 2
+
+
+def attn_cpu_sample(seconds):
+    """The reference's own flash_attention_fp16 (oracle/_ref) on one head of the
+    long-sequence shape at 2048 tokens (1 thread); the oracle port if it is absent."""
+    import oracle
+    S, D = 2048, 128
+    rng = np.random.default_rng(9)
+    q, k, v = (rng.standard_normal((1, 1, S, D)).astype(np.float16) for _ in range(3))
+    o = np.zeros_like(q)
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+    if oracle.ref_available():
+        fn, kind = oracle.ref().sgref_neon_flash_attention_fp16, "reference"
+        call = lambda: fn(P(q), P(k), P(v), P(o), 1, S, 1, 1, D, 0.0, 1)  # noqa: E731
+    else:
+        kind = "port"
+        call = lambda: oracle.flash_attention(q, k, v, causal=True)  # noqa: E731
+    n, t0 = 0, time.perf_counter()
+    while True:
+        call()
+        n += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(n * attn_flops(1, S, D) / dt / 1e12, 6), "unit": "TFLOP/s", "cores": 1, "kind": kind,
+            "sample": f"{n} calls of flash_attention_fp16 on one head, S={S}, D={D}, causal, fp16, in {dt:.1f} s "
+                      f"on 1 host thread"}
+
+
+def run_attention(args):
+    import torch
+    import torch.distributed as dist
+
+    from silicongraph_b200 import _lib, kernels
+
+    rank, local_rank, world = rank_env()
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    lib = _lib.load()
+    dev = torch.device("cuda", local_rank)
+    B, H, Hkv, S, D, dts, desc = ATTN_WORKLOADS[args.workload]
+    tdt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[dts]
+    flops = attn_flops(H, S, D) * B
+    rng = np.random.default_rng(77 + rank)
+    hq = torch.from_numpy(rng.standard_normal((B, H, S, D)).astype(np.float32)).to(tdt).pin_memory()
+    hk = torch.from_numpy(rng.standard_normal((B, Hkv, S, D)).astype(np.float32)).to(tdt).pin_memory()
+    hv = torch.from_numpy(rng.standard_normal((B, Hkv, S, D)).astype(np.float32)).to(tdt).pin_memory()
+    Q, K, V = hq.to(dev), hk.to(dev), hv.to(dev)
+    O = torch.empty_like(Q)
+    stream = torch.cuda.Stream(dev)
+    st = stream.cuda_stream
+    from silicongraph_b200._lib import SgFlashAttentionParams
+    p = SgFlashAttentionParams()
+    p.Q, p.K, p.V, p.O = Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr()
+    p.B, p.S, p.num_heads, p.num_kv_heads, p.head_dim = B, S, H, Hkv, D
+    p.causal = 1
+    p.io_dtype = kernels.dtype_code(tdt)
+    p.S_kv = S
+    p.q_pos0 = 0
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    flush = torch.empty(max(2 * l2, 256 << 20), dtype=torch.uint8, device=dev)
+
+    def call():
+        r = lib.sg_flash_attention(ctypes.byref(p), st)
+        if r != 0:
+            raise _lib.SgError(r, _lib.last_error())
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            call()
+    stream.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    clocks = ClockSampler(torch.cuda.current_device(), interval_ms=20) if rank == 0 else None
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with torch.cuda.stream(stream):
+        for e0, e1 in ev:
+            flush.zero_()  # L2 flushed between timed steps
+            e0.record(stream)
+            call()
+            e1.record(stream)
+    stream.synchronize()
+    ms = max_over_ranks(sum(e0.elapsed_time(e1) for e0, e1 in ev))
+    clk = clocks.stop() if clocks else None
+    value = world * args.steps * flops / (ms / 1e3) / 1e12
+    per_gpu = args.steps * flops / (ms / 1e3) / 1e12
+    # end to end: host Q/K/V -> device, attention through the C ABI, O -> host, every step
+    e2e_steps = max(1, min(args.steps, 5))
+    ho = torch.empty_like(hq).pin_memory()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            Q.copy_(hq, non_blocking=True)
+            K.copy_(hk, non_blocking=True)
+            V.copy_(hv, non_blocking=True)
+            call()
+            ho.copy_(O, non_blocking=True)
+        e1.record(stream)
+    stream.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    peak, peak_src = read_peak_tensor()
+    esz = Q.element_size()
+    line = {
+        "metric": "flash-attn TFLOP/s (causal, " + dts + ")",
+        "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": dts, "data": "synthetic (seeded N(0,1) Q/K/V, host-generated)",
+        "config": {"workload": desc, "B": B, "H": H, "Hkv": Hkv, "S": S, "D": D,
+                   "flops_per_step": flops, "flop_count": "4*H*D*S*(S+1)/2 (causal)",
+                   "l2": "flushed (256 MB write) before every timed step",
+                   "parallelism": f"replicas x{world} (no data-path collective)",
+                   "timing": "CUDA events around each step, summed; max over ranks"},
+        "roofline": {"bound": "tensor", "achieved": round(per_gpu, 2), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(per_gpu / peak, 4), "peak_source": peak_src, "traffic": None,
+                     "achieved_basis": "algorithmic FLOPs / event time of one sg_flash_attention call"},
+        "e2e": {"value": round(world * e2e_steps * flops / (e2e_ms / 1e3) / 1e12, 3), "unit": "TFLOP/s",
+                "steps": e2e_steps, "h2d_bytes_per_step": int((hq.numel() + hk.numel() + hv.numel()) * esz),
+                "d2h_bytes_per_step": int(ho.numel() * esz)},
+        "gpu_launches": args.steps * (2 if dts == "bf16" else 1),
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            line["cpu_baseline"] = attn_cpu_sample(args.cpu_seconds)
+        except Exception as e:  # the baseline is reported, never required
+            line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args):
     rank, _, world = rank_env()
@@ -592,8 +753,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--ref-budget-s", type=float, default=120.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["gemv_int4", *PF_WORKLOADS], default="gemv_int4",
-                    help="gemv_int4 (default): the decode GEMV; prefill_int4 / prefill_int8: the prefill GEMM")
+    ap.add_argument("--workload", choices=["gemv_int4", *PF_WORKLOADS, *ATTN_WORKLOADS], default="gemv_int4",
+                    help="gemv_int4 (default): the decode GEMV; prefill_int4 / prefill_int8: the prefill GEMM; "
+                         "attn_prefill / attn_small: flash attention")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -607,6 +769,8 @@ def main():
         run_reference(args)
     elif args.workload in PF_WORKLOADS:
         run_prefill(args)
+    elif args.workload in ATTN_WORKLOADS:
+        run_attention(args)
     else:
         run_ours(args)
 

@@ -314,11 +314,22 @@ size_t attn_cc_scratch_bytes(const SgFlashAttentionParams* p, int want_splits) {
 extern "C" {
 
 SgStatus sg_flash_attention(const SgFlashAttentionParams* p, void* stream) {
-  if (p && p->workspace) return sg::attn_cc_run(p, stream, 8, p->workspace, p->workspace_bytes, true);
+  SgStatus st = sg::attn_validate(p, "sg_flash_attention");
+  if (st != SG_OK) return st;
+  if (p->B == 0 || p->S == 0 || p->num_heads == 0) return SG_OK;
+  bool handled = false;
+  st = sg::attn_tc_run(p, static_cast<cudaStream_t>(stream), p->workspace, p->workspace_bytes,
+                       p->workspace != nullptr, &handled);
+  if (st != SG_OK || handled) return st;
+  if (p->workspace) return sg::attn_cc_run(p, stream, 8, p->workspace, p->workspace_bytes, true);
   return sg::attn_cc_run(p, stream, 8, nullptr, 0, false);
 }
 
-size_t sg_flash_attention_workspace_size(const SgFlashAttentionParams* p) { return sg::attn_cc_scratch_bytes(p, 8); }
+size_t sg_flash_attention_workspace_size(const SgFlashAttentionParams* p) {
+  const size_t tc = sg::attn_tc_scratch_bytes(p);
+  const size_t cc = sg::attn_cc_scratch_bytes(p, 8);
+  return tc > cc ? tc : cc;
+}
 
 // Decode: split the keys over many CTAs (flash-decoding) and merge.
 SgStatus sg_flash_decode(const SgFlashAttentionParams* p, void* stream) {

@@ -1,0 +1,553 @@
+// Flash attention on the 5th-generation tensor cores for fp16 / bf16 I/O and
+// head_dim 64 or 128: the batched, GQA, causal driver of
+// flash_attention_fp16 (compiler/kernels/cpu/flash_attention.h:95-144) with
+// the per-query online softmax of flash_attn_head (flash_attention.h:49-90).
+//
+// One CTA per (128-query tile, head, batch).  Per 128-key tile j:
+//   S_j = Q K_j^T        tcgen05.mma, A = Q and B = K_j from shared memory
+//                        (TMA, 128-byte swizzle, K-major), D = S_j in TMEM
+//   softmax              one thread per query row (TMEM lane): its whole score
+//                        row is in its registers after tcgen05.ld, so the row
+//                        max and sum need no shuffles; P_j is written back
+//                        into the first half of S_j's TMEM columns (16-bit)
+//   O += P_j V_j         tcgen05.mma with A = P_j from TMEM and B = V_j from
+//                        shared memory read MN-major (V rows are keys)
+// The running max moves (and O is rescaled) only when a row's max grows by
+// more than 2^8 in exp2 units; otherwise P is taken against the old max, at
+// most 2^8, which the 16-bit P and fp32 sums hold exactly enough.  The final
+// O / l is invariant to the reference point of the max, and l sums the same
+// rounded 16-bit weights that PV multiplies, so O stays a weighted average.
+//
+// Warps: 0..3 softmax + epilogue (TMEM lane quarter = warp), 4: K loader,
+// 5: V loader, 6: MMA issuer.  K and V tiles have separate two-stage rings:
+// a K tile is free as soon as its QK^T finished, a V tile after its PV.
+// TMEM: S/P buffers at columns 0 and 128, O at 256 .. 256 + D.
+// All waits are bounded (2 s) and report through the device error word.
+#include <algorithm>
+#include <atomic>
+#include <string_view>
+#include <type_traits>
+
+#include "sm100.cuh"
+
+namespace {
+
+using namespace sgd;
+
+constexpr int kQT = 128;  // query rows per CTA = TMEM lanes
+constexpr int kKT = 128;  // keys per tile
+constexpr int kWarpK = 4, kWarpV = 5, kWarpMma = 6;
+constexpr int kThreads = 7 * 32;
+constexpr int kTmemCols = 512;
+constexpr int kStages = 2;
+constexpr int kOCol = 256;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+template <int D>
+struct ACfg {
+  static constexpr int kBoxes = D / 64;          // 64-element (128-byte) column blocks per tile
+  static constexpr int kBox = 128 * 128;         // one [128 rows x 128 B] block
+  static constexpr int kTile = kBoxes * kBox;    // one [128 x D] 16-bit tile
+  static constexpr int kQOff = 0;
+  static constexpr int kKOff = kQOff + kTile;
+  static constexpr int kVOff = kKOff + kStages * kTile;
+  static constexpr int kBarOff = kVOff + kStages * kTile;
+  static constexpr int kBars = 1 + 6 * kStages + 2;
+  // At least 120 KB so that one CTA holds an SM (and its 512 TMEM columns).
+  static constexpr int kSmem0 = kBarOff + kBars * 8 + 16 + 1024;
+  static constexpr int kSmem = kSmem0 < 120 * 1024 ? 120 * 1024 : kSmem0;
+};
+
+struct TArgs {
+  void* O;
+  int B, H, G, Sq, Skv;
+  float scale_log2;  // softmax scale * log2(e)
+  int causal, q_pos0;
+  int n_qt;
+  int* err;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// The two 16-bit values of a packed pair, back in fp32.
+template <bool BF16>
+__device__ __forceinline__ float sum2(uint32_t u) {
+  if (BF16) return __uint_as_float(u << 16) + __uint_as_float(u & 0xffff0000u);
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u));
+  return f.x + f.y;
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if (BF16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+  __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ void warp_wait_all(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
+  if (!mbar_wait(bar, parity, err)) *abort_flag = 1;
+  __syncwarp();
+}
+
+// BF16: Q / K / O are bf16 (else fp16).  P and V are always fp16: bf16 inputs
+// have their V copied to fp16 first (exact within fp16's range), so that P
+// keeps 11 significant bits instead of 8.
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, TArgs a) {
+  using C_ = ACfg<D>;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C_::kBarOff);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + kStages;
+  uint64_t* v_full = k_empty + kStages;
+  uint64_t* v_empty = v_full + kStages;
+  uint64_t* s_full = v_empty + kStages;
+  uint64_t* p_full = s_full + kStages;
+  uint64_t* o_ready = p_full + kStages;
+  uint64_t* done = o_ready + 1;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Work item: the heaviest query tiles (most keys under a causal mask) launch first.
+  const int hb_count = a.H * a.B;
+  const int qt = a.n_qt - 1 - (int)(blockIdx.x / hb_count);
+  const int hb = (int)(blockIdx.x % hb_count);
+  const int h = hb % a.H, b = hb / a.H;
+  const int hkv = h / a.G;
+  const int q0 = qt * kQT;
+  const int q_last = min(q0 + kQT, a.Sq) - 1;
+  const int kv_tiles_all = (a.Skv + kKT - 1) / kKT;
+  const int n_kv = a.causal ? min(kv_tiles_all, (a.q_pos0 + q_last) / kKT + 1) : kv_tiles_all;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&p_full[s], 4);
+    }
+    mbar_init(o_ready, 1);
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kWarpMma) {
+    tmem_alloc(tslot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == kWarpK && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+  }
+  if (warp == kWarpV && lane == 0) tma_prefetch_desc(&tmV);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  pdl_wait();
+
+  if (warp == kWarpK || warp == kWarpV) {
+    // ------------------------------------------------------------ loaders
+    if (lane == 0) {
+      const bool is_k = warp == kWarpK;
+      const CUtensorMap* map = is_k ? &tmK : &tmV;
+      uint64_t* fullb = is_k ? k_full : v_full;
+      uint64_t* emptyb = is_k ? k_empty : v_empty;
+      unsigned char* base = smem + (is_k ? C_::kKOff : C_::kVOff);
+      if (is_k) {
+        mbar_arrive_expect_tx(q_full, C_::kTile);
+        for (int bx = 0; bx < C_::kBoxes; ++bx)
+          tma_load_3d(smem + C_::kQOff + bx * C_::kBox, &tmQ, bx * 64, q0, hb, q_full);
+      }
+      uint32_t issued[kStages] = {0, 0};
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % kStages;
+        const uint32_t use = j / kStages;
+        if (*abort_flag || !mbar_wait(&emptyb[st], (use & 1) ^ 1, a.err)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&fullb[st], C_::kTile);
+        for (int bx = 0; bx < C_::kBoxes; ++bx)
+          tma_load_4d(base + st * C_::kTile + bx * C_::kBox, map, bx * 64, j * kKT, hkv, b, &fullb[st]);
+        issued[st] = use + 1;
+      }
+      for (int st = 0; st < kStages; ++st)
+        if (issued[st]) mbar_wait(&fullb[st], (issued[st] - 1) & 1, a.err);
+      if (is_k) mbar_wait(q_full, 0, a.err);
+    }
+  } else if (warp == kWarpMma) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_qk = umma_idesc_f16(kQT, kKT, BF16 ? 1 : 0, 0, 0);
+      const uint32_t idesc_pv = umma_idesc_f16(kQT, D, 0, 0, 1);  // fp16 P x fp16 V, B (= V) MN-major
+      bool ok = mbar_wait(q_full, 0, a.err);
+      auto issue_qk = [&](int t) -> bool {
+        const int st = t % kStages;
+        if (*abort_flag || !mbar_wait(&k_full[st], (t / kStages) & 1, a.err)) return false;
+        tc_fence_after();
+        const uint32_t d = tbase + (t % 2) * kKT;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int bx = kk / 4, off = (kk % 4) * 32;
+          const uint64_t ad = umma_smem_desc(smem_u32(smem + C_::kQOff + bx * C_::kBox + off), 16, 1024, kSwizzle128B);
+          const uint64_t bd =
+              umma_smem_desc(smem_u32(smem + C_::kKOff + st * C_::kTile + bx * C_::kBox + off), 16, 1024, kSwizzle128B);
+          umma_f16_ss(d, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&k_empty[st]);
+        umma_commit(&s_full[t % 2]);
+        return true;
+      };
+      if (ok) ok = issue_qk(0);
+      if (ok && n_kv > 1) ok = issue_qk(1);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = j % kStages;
+        if (*abort_flag || !mbar_wait(&p_full[j % 2], (j / 2) & 1, a.err) ||
+            !mbar_wait(&v_full[st], (j / kStages) & 1, a.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t ap = tbase + (j % 2) * kKT;  // P_j: 128 keys as 64 columns of 16-bit pairs
+#pragma unroll
+        for (int kk = 0; kk < kKT / 16; ++kk) {
+          // 16 keys = two 8-row groups of V: the start moves by 2 x 1024 bytes; LBO steps over
+          // 64-column blocks of V (the second TMA box), SBO over 8-row groups.
+          const uint64_t bd = umma_smem_desc(smem_u32(smem + C_::kVOff + st * C_::kTile + kk * 2048), C_::kBox, 1024,
+                                             kSwizzle128B);
+          umma_f16_ts(tbase + kOCol, ap + kk * 8, bd, idesc_pv, (j | kk) != 0 ? 1u : 0u);
+        }
+        umma_commit(&v_empty[st]);
+        umma_commit(o_ready);
+        if (j + 2 < n_kv) ok = issue_qk(j + 2);
+      }
+      if (!ok) *abort_flag = 1;
+      umma_commit(done);
+      mbar_wait(done, 0, a.err);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int r = warp * 32 + lane;  // query row in the tile = TMEM lane
+    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+    const int q = q0 + r;
+    const int q_pos = a.q_pos0 + q;  // keys 0 .. q_pos are visible under the causal mask
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      __syncwarp();
+      if (*abort_flag) {
+        ok = false;
+        break;
+      }
+      warp_wait_all(&s_full[j % 2], (j / 2) & 1, a.err, abort_flag);
+      tc_fence_after();
+      const uint32_t scol = tbase + lane_addr + (j % 2) * kKT;
+      uint32_t sr[kKT];
+#pragma unroll
+      for (int c = 0; c < kKT / 32; ++c)
+        tmem_ld_32x32b_x32(scol + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+      tmem_ld_wait();
+      const int key0 = j * kKT;
+      const int lim = min(a.causal ? q_pos : 0x7fffffff, a.Skv - 1) - key0;  // keys key0 + i, i <= lim
+      // Only tiles that reach past some row's last visible key need the mask.
+      if (__any_sync(0xffffffffu, lim < kKT - 1)) {
+#pragma unroll
+        for (int i = 0; i < kKT; ++i)
+          if (i > lim) sr[i] = __float_as_uint(-INFINITY);
+      }
+      // Row max on the raw scores (the scale is positive, so it commutes with max).
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < kKT; i += 2) mx = fmax3(mx, __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
+      mx *= a.scale_log2;
+      float alpha = 1.f;
+      const bool rescale = mx > m + kRescaleThreshold;
+      if (rescale) {
+        alpha = ex2(m - mx);  // 0 on the first tile (m = -inf)
+        m = mx;
+        l *= alpha;
+      }
+      const float neg_m = -m;
+      float sum = 0.f;
+      uint32_t pk[kKT / 2];
+#pragma unroll
+      for (int i = 0; i < kKT / 2; ++i) {
+        const float p0 = ex2(fmaf(__uint_as_float(sr[2 * i]), a.scale_log2, neg_m));
+        const float p1 = ex2(fmaf(__uint_as_float(sr[2 * i + 1]), a.scale_log2, neg_m));
+        pk[i] = pack2<false>(p0, p1);
+        sum += sum2<false>(pk[i]);  // l sums the rounded weights that PV multiplies
+      }
+      l += sum;
+      tmem_st_32x32b_x16(scol, *reinterpret_cast<uint32_t(*)[16]>(&pk[0]));
+      tmem_st_32x32b_x16(scol + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[16]));
+      tmem_st_32x32b_x16(scol + 32, *reinterpret_cast<uint32_t(*)[16]>(&pk[32]));
+      tmem_st_32x32b_x16(scol + 48, *reinterpret_cast<uint32_t(*)[16]>(&pk[48]));
+      if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+        // O rows of this warp scale by alpha (1 for rows whose max did not move) once
+        // PV_{j-1} has landed; PV_j waits for p_full below.
+        warp_wait_all(o_ready, (j - 1) & 1, a.err, abort_flag);
+        tc_fence_after();
+#pragma unroll 1
+        for (int dc = 0; dc < D / 32; ++dc) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(tbase + lane_addr + kOCol + dc * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st_32x32b_x16(tbase + lane_addr + kOCol + dc * 32, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
+          tmem_st_32x32b_x16(tbase + lane_addr + kOCol + dc * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[j % 2]);
+    }
+    if (ok && n_kv > 0) {
+      warp_wait_all(o_ready, (n_kv - 1) & 1, a.err, abort_flag);
+      tc_fence_after();
+      const float inv_l = 1.f / l;
+      typedef typename std::conditional<BF16, __nv_bfloat16, __half>::type T;
+      T* orow = static_cast<T*>(a.O) + ((size_t)hb * a.Sq + q) * D;
+#pragma unroll 1
+      for (int dc = 0; dc < D / 32; ++dc) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(tbase + lane_addr + kOCol + dc * 32, o);
+        tmem_ld_wait();
+        uint32_t pkd[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          pkd[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
+        if (q < a.Sq) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + dc * 32);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pkd[4 * v], pkd[4 * v + 1], pkd[4 * v + 2], pkd[4 * v + 3]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
+// V [B, Hkv, Skv, D] bf16 (strided) -> contiguous fp16, 8 values per thread.
+__global__ void v_to_f16_kernel(const __nv_bfloat16* V, int64_t kv_bs, int64_t kv_hs, int Hkv, int Skv, int D,
+                                int64_t total8, __half* out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total8; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = i * 8;
+    const int d = (int)(e % D);
+    const int64_t row = e / D;  // (b * Hkv + hk) * Skv + s
+    const int s = (int)(row % Skv);
+    const int64_t bh = row / Skv;
+    const int hk = (int)(bh % Hkv), b = (int)(bh / Hkv);
+    const uint4 v = *reinterpret_cast<const uint4*>(V + b * kv_bs + hk * kv_hs + (int64_t)s * D + d);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(&v);
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float lo = __uint_as_float(w[k] << 16), hi = __uint_as_float(w[k] & 0xffff0000u);
+      __half2 h = __floats2half2_rn(lo, hi);
+      ow[k] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(out + e) = o;
+  }
+}
+
+template <int D, bool BF16>
+SgStatus launch_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const TArgs& a, int grid,
+                   cudaStream_t cs) {
+  using C_ = ACfg<D>;
+  auto kfn = attn_tc_kernel<D, BF16>;
+  static std::atomic<uint64_t> attr_set{0};
+  int dev = 0;
+  SgStatus st = sg::current_device(&dev);
+  if (st != SG_OK) return st;
+  const uint64_t bit = dev < 64 ? (uint64_t)1 << dev : 0;
+  if (!(attr_set.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::kSmem);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      sg::set_error("attn_tc_kernel: cannot reserve %d bytes of shared memory: %s", C_::kSmem, cudaGetErrorString(e));
+      return SG_ERR_RUNTIME;
+    }
+    attr_set.fetch_or(bit);
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C_::kSmem;
+  cfg.stream = cs;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, tq, tk, tv, a);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    sg::set_error("attn_tc_kernel launch failed: %s", cudaGetErrorString(e));
+    return SG_ERR_RUNTIME;
+  }
+  return SG_OK;
+}
+
+std::atomic<int> g_tune_attn_tc{1};    // 0: tensor-core attention off
+std::atomic<int> g_tune_attn_min_s{256};  // shortest query length sent to it
+
+}  // namespace
+
+namespace sg {
+
+// Runs the tensor-core kernel when the problem qualifies (*handled = true):
+// fp16 / bf16 I/O, head_dim 64 or 128, at least 256 queries, 16-byte aligned
+// tensors and K / V strides.
+namespace {
+bool tc_qualifies(const SgFlashAttentionParams* p) {
+  if (!g_tune_attn_tc.load()) return false;
+  const int io = p->io_dtype == SG_DT_DEFAULT ? SG_DT_F16 : p->io_dtype;
+  const int D = p->head_dim;
+  if ((io != SG_DT_F16 && io != SG_DT_BF16) || (D != 64 && D != 128)) return false;
+  if (p->S < g_tune_attn_min_s.load()) return false;
+  const int Hkv = std::max(1, p->num_kv_heads);
+  const int Skv = p->S_kv > 0 ? p->S_kv : p->S;
+  const int64_t kv_hs = p->kv_head_stride > 0 ? p->kv_head_stride : (int64_t)Skv * D;
+  const int64_t kv_bs = p->kv_batch_stride > 0 ? p->kv_batch_stride : (int64_t)Hkv * kv_hs;
+  if (!aligned16(p->Q) || !aligned16(p->K) || !aligned16(p->V) || !aligned16(p->O)) return false;
+  if ((kv_hs * 2) % 16 != 0 || (kv_bs * 2) % 16 != 0) return false;
+  const int q_pos0 = p->q_pos0 >= 0 ? p->q_pos0 : Skv - p->S;
+  return q_pos0 >= 0;  // queries before the first key: the CUDA-core path reports it
+}
+}  // namespace
+
+// Scratch of the tensor-core path: the fp16 copy of a bf16 V.
+size_t attn_tc_scratch_bytes(const SgFlashAttentionParams* p) {
+  if (!tc_qualifies(p)) return 0;
+  const int io = p->io_dtype == SG_DT_DEFAULT ? SG_DT_F16 : p->io_dtype;
+  if (io != SG_DT_BF16) return 0;
+  const int Skv = p->S_kv > 0 ? p->S_kv : p->S;
+  return align_up((size_t)p->B * std::max(1, p->num_kv_heads) * Skv * p->head_dim * 2, 256);
+}
+
+SgStatus attn_tc_run(const SgFlashAttentionParams* p, cudaStream_t cs, void* ws, size_t ws_bytes, bool ws_external,
+                     bool* handled) {
+  *handled = false;
+  if (!tc_qualifies(p)) return SG_OK;
+  const int io = p->io_dtype == SG_DT_DEFAULT ? SG_DT_F16 : p->io_dtype;
+  const int D = p->head_dim;
+  const int Hkv = std::max(1, p->num_kv_heads);
+  const int Skv = p->S_kv > 0 ? p->S_kv : p->S;
+  int64_t kv_hs = p->kv_head_stride > 0 ? p->kv_head_stride : (int64_t)Skv * D;
+  int64_t kv_bs = p->kv_batch_stride > 0 ? p->kv_batch_stride : (int64_t)Hkv * kv_hs;
+  int* err = nullptr;
+  SgStatus st = device_error_word(&err);
+  if (st != SG_OK) return st;
+  // bf16 V -> contiguous fp16 copy for the PV product
+  const void* vsrc = p->V;
+  int64_t v_hs = kv_hs, v_bs = kv_bs;
+  if (io == SG_DT_BF16) {
+    const size_t need = attn_tc_scratch_bytes(p);
+    if (ws == nullptr) {
+      if (ws_external) {
+        set_error("sg_flash_attention: scratch required (%zu bytes)", need);
+        return SG_ERR_INVALID;
+      }
+      st = library_workspace(cs, need, &ws, kWsAttention);
+      if (st != SG_OK) return st;
+    } else {
+      SG_CHECK_ARG(ws_bytes >= need && aligned16(ws), "sg_flash_attention: workspace too small (%zu < %zu bytes)",
+                   ws_bytes, need);
+    }
+    const int64_t total8 = (int64_t)p->B * Hkv * Skv * D / 8;
+    const int blocks = (int)std::min<int64_t>((total8 + 255) / 256, 148 * 16);
+    v_to_f16_kernel<<<blocks, 256, 0, cs>>>(static_cast<const __nv_bfloat16*>(p->V), kv_bs, kv_hs, Hkv, Skv, D,
+                                            total8, static_cast<__half*>(ws));
+    st = check_launch("v_to_f16_kernel");
+    if (st != SG_OK) return st;
+    vsrc = ws;
+    v_hs = (int64_t)Skv * D;
+    v_bs = (int64_t)Hkv * v_hs;
+  }
+
+  const CUtensorMapDataType dt = io == SG_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap tq, tk, tv;
+  {
+    const uint64_t dims[3] = {(uint64_t)D, (uint64_t)p->S, (uint64_t)p->B * p->num_heads};
+    const uint64_t str[2] = {(uint64_t)D * 2, (uint64_t)p->S * D * 2};
+    const uint32_t box[3] = {64, (uint32_t)kQT, 1};
+    st = make_tensor_map(&tq, dt, 3, const_cast<void*>(p->Q), dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != SG_OK) return st;
+  }
+  {
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)Skv, (uint64_t)Hkv, (uint64_t)p->B};
+    const uint64_t str[3] = {(uint64_t)D * 2, (uint64_t)kv_hs * 2, (uint64_t)kv_bs * 2};
+    const uint32_t box[4] = {64, (uint32_t)kKT, 1, 1};
+    st = make_tensor_map(&tk, dt, 4, const_cast<void*>(p->K), dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != SG_OK) return st;
+    const uint64_t vstr[3] = {(uint64_t)D * 2, (uint64_t)v_hs * 2, (uint64_t)v_bs * 2};
+    st = make_tensor_map(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(vsrc), dims, vstr, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != SG_OK) return st;
+  }
+  TArgs a{};
+  a.O = p->O;
+  a.B = p->B;
+  a.H = p->num_heads;
+  a.G = p->num_heads / Hkv;
+  a.Sq = p->S;
+  a.Skv = Skv;
+  const float scale = p->scale > 0.f ? p->scale : 1.0f / sqrtf((float)D);
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.causal = p->causal != 0;
+  a.q_pos0 = p->q_pos0 >= 0 ? p->q_pos0 : Skv - p->S;
+  a.n_qt = (p->S + kQT - 1) / kQT;
+  a.err = err;
+  const int grid = a.n_qt * a.H * a.B;
+  *handled = true;
+  if (D == 64) return io == SG_DT_BF16 ? launch_tc<64, true>(tq, tk, tv, a, grid, cs)
+                                       : launch_tc<64, false>(tq, tk, tv, a, grid, cs);
+  return io == SG_DT_BF16 ? launch_tc<128, true>(tq, tk, tv, a, grid, cs)
+                          : launch_tc<128, false>(tq, tk, tv, a, grid, cs);
+}
+
+bool attn_tc_tuning(std::string_view key, int value) {
+  if (key == "attn_tc.enable") {
+    g_tune_attn_tc.store(value);
+    return true;
+  }
+  if (key == "attn_tc.min_s") {
+    g_tune_attn_min_s.store(value);
+    return true;
+  }
+  return false;
+}
+
+}  // namespace sg

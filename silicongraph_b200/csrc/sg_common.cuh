@@ -67,6 +67,12 @@ size_t gemm_tc_scratch_bytes(const SgMatMulParams* p, bool int8_weights, bool* o
 SgStatus gemm_tc_run(const SgMatMulParams* p, bool int8_weights, cudaStream_t cs, int sms, void* ws,
                      size_t ws_bytes, int* err_word, bool* handled);
 
+// Tensor-core flash attention (attn_tc.cu): runs the problem when it
+// qualifies (fp16 / bf16, head_dim 64 or 128, long enough), else *handled = false.
+SgStatus attn_tc_run(const SgFlashAttentionParams* p, cudaStream_t cs, void* ws, size_t ws_bytes, bool ws_external,
+                     bool* handled);
+size_t attn_tc_scratch_bytes(const SgFlashAttentionParams* p);
+
 inline size_t ticket_bytes(int n_tiles) {
   const size_t t = align_up((size_t)n_tiles * sizeof(unsigned), 256);
   return t < 4096 ? 4096 : t;

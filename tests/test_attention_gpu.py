@@ -55,13 +55,13 @@ def test_attention_vs_oracle(sg, oracle_mod, dtype, B, H, Hkv, S, D, causal):
         want = oracle_mod.flash_attention(q, k, v, causal=causal)
         got = sg.flash_attention(dev(q), dev(k), dev(v), causal=causal).cpu().numpy()
     elif dtype == "f16":
+        # the oracle in fp32 on the same fp16 input values: one rounding of the output, not two
         q, k, v = (a.astype(np.float16) for a in (q, k, v))
-        want = oracle_mod.flash_attention(q, k, v, causal=causal).astype(np.float32)
+        want = oracle_mod.flash_attention(*(a.astype(np.float32) for a in (q, k, v)), causal=causal)
         got = sg.flash_attention(dev(q), dev(k), dev(v), causal=causal).float().cpu().numpy()
     else:
-        qb, kb, vb = (oracle_mod.f32_to_bf16_bits(a) for a in (q, k, v))
-        want = oracle_mod.bf16_bits_to_f32(
-            oracle_mod.flash_attention(qb, kb, vb, causal=causal, io_dt=oracle_mod.DT_BF16))
+        qb, kb, vb = (oracle_mod.bf16_bits_to_f32(oracle_mod.f32_to_bf16_bits(a)) for a in (q, k, v))
+        want = oracle_mod.flash_attention(qb, kb, vb, causal=causal)
         t = lambda a: torch.from_numpy(a).cuda().to(torch.bfloat16)  # noqa: E731
         got = sg.flash_attention(t(q), t(k), t(v), causal=causal).float().cpu().numpy()
     close(got, want)
