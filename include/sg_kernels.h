@@ -228,6 +228,43 @@ size_t sg_flash_attention_workspace_size(const SgFlashAttentionParams* p);
 SgStatus sg_flash_decode(const SgFlashAttentionParams* p, void* stream);
 size_t sg_flash_decode_workspace_size(const SgFlashAttentionParams* p);
 
+/* ------------------------------------------------------------------ block ops
+ * Element-wise transformer-block ops (compiler/kernels/cpu/matmul_neon.h):
+ * fp32 arithmetic, one rounding to io_dtype (DEFAULT/F16, BF16, F32) at the
+ * end, asynchronous on the stream.
+ */
+
+/* y = x * (1 / sqrt(mean(x^2) + eps)) * w per row of n (rmsnorm_fp16_neon,
+ * :154-190); x, y [rows, n], w [n].  With residual != NULL the row is first
+ * h = round(x + residual), written back to residual (the decoder's residual
+ * stream), and h is normalised. */
+SgStatus sg_rmsnorm(const void* x, void* residual, const void* w, void* y, int32_t rows, int32_t n, float eps,
+                    int32_t io_dtype, void* stream);
+
+/* y = x / (1 + exp(-x)) (silu_fp16_neon, :196-225). */
+SgStatus sg_silu(const void* x, void* y, int64_t n, int32_t io_dtype, void* stream);
+
+/* SwiGLU: y = round(silu(gate)) * up. */
+SgStatus sg_silu_mul(const void* gate, const void* up, void* y, int64_t n, int32_t io_dtype, void* stream);
+
+/* Row softmax in the reference order (softmax_fp16_neon, :230-256): max;
+ * e = round(exp(x - max)); sum of the rounded e; y = round(e * (1 / sum)). */
+SgStatus sg_softmax(const void* x, void* y, int32_t rows, int32_t n, int32_t io_dtype, void* stream);
+
+/* Rotary embedding in place on x [tokens, heads, head_dim] (rope_apply_neon,
+ * :262-275): pairs (i, i + head_dim/2) rotate by theta = pos / base^(2i/head_dim);
+ * pos = positions[t] (device array) or pos0 + t when positions is NULL. */
+SgStatus sg_rope(void* x, int32_t tokens, int32_t heads, int32_t head_dim, const int32_t* positions, int32_t pos0,
+                 float base, int32_t io_dtype, void* stream);
+
+/* out[t, :] = table[ids[t], :] (table [vocab, hidden]); an id outside
+ * [0, vocab) writes zeros and sets the device error word. */
+SgStatus sg_embedding(const void* table, const int32_t* ids, void* out, int32_t tokens, int32_t hidden, int32_t vocab,
+                      int32_t io_dtype, void* stream);
+
+/* out[r] = index of the largest of logits[r, 0 .. n) (first among equals). */
+SgStatus sg_argmax(const float* logits, int32_t rows, int32_t n, int32_t* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -103,6 +103,16 @@ _SIGS = {
                                                   ctypes.c_int32, _P, _P, _P, _P]),
     "sg_dequantize_int4_grouped": (ctypes.c_int32, [_P, _P, _P, ctypes.c_int32, ctypes.c_int32,
                                                     ctypes.c_int32, _P, _P]),
+    "sg_rmsnorm": (ctypes.c_int32, [_P, _P, _P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_float,
+                                    ctypes.c_int32, _P]),
+    "sg_silu": (ctypes.c_int32, [_P, _P, ctypes.c_int64, ctypes.c_int32, _P]),
+    "sg_silu_mul": (ctypes.c_int32, [_P, _P, _P, ctypes.c_int64, ctypes.c_int32, _P]),
+    "sg_softmax": (ctypes.c_int32, [_P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P]),
+    "sg_rope": (ctypes.c_int32, [_P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P, ctypes.c_int32,
+                                 ctypes.c_float, ctypes.c_int32, _P]),
+    "sg_embedding": (ctypes.c_int32, [_P, _P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                      ctypes.c_int32, _P]),
+    "sg_argmax": (ctypes.c_int32, [_P, ctypes.c_int32, ctypes.c_int32, _P, _P]),
 }
 
 

@@ -119,3 +119,60 @@ def flash_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, *, causal
     fn = _lib.load().sg_flash_decode if decode else _lib.load().sg_flash_attention
     check(fn(ctypes.byref(p), _stream(stream)))
     return O
+
+
+# ----------------------------------------------------------------------------- block ops
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-5, residual: torch.Tensor | None = None,
+            out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """rmsnorm_fp16_neon (matmul_neon.h:154-190) per row of x [rows, n]; with a
+    residual: residual += x (rounded to the I/O type) and that is normalised."""
+    n = x.shape[-1]
+    rows = x.numel() // n if n else 0
+    y = torch.empty_like(x) if out is None else out
+    check(_lib.load().sg_rmsnorm(_ptr(x), _ptr(residual), _ptr(w), _ptr(y), rows, n, eps, dtype_code(x.dtype),
+                                 _stream(stream)))
+    return y
+
+
+def silu(x: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    y = torch.empty_like(x) if out is None else out
+    check(_lib.load().sg_silu(_ptr(x), _ptr(y), x.numel(), dtype_code(x.dtype), _stream(stream)))
+    return y
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    y = torch.empty_like(gate) if out is None else out
+    check(_lib.load().sg_silu_mul(_ptr(gate), _ptr(up), _ptr(y), gate.numel(), dtype_code(gate.dtype),
+                                  _stream(stream)))
+    return y
+
+
+def softmax(x: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    n = x.shape[-1]
+    y = torch.empty_like(x) if out is None else out
+    check(_lib.load().sg_softmax(_ptr(x), _ptr(y), x.numel() // n, n, dtype_code(x.dtype), _stream(stream)))
+    return y
+
+
+def rope(x: torch.Tensor, pos0: int = 0, positions: torch.Tensor | None = None, base: float = 10000.0,
+         stream=None) -> torch.Tensor:
+    """In place on x [tokens, heads, head_dim] (rope_apply_neon, matmul_neon.h:262-275)."""
+    t, h, d = x.shape
+    check(_lib.load().sg_rope(_ptr(x), t, h, d, _ptr(positions), pos0, base, dtype_code(x.dtype), _stream(stream)))
+    return x
+
+
+def embedding(table: torch.Tensor, ids: torch.Tensor, stream=None) -> torch.Tensor:
+    vocab, hidden = table.shape
+    out = torch.empty((ids.numel(), hidden), dtype=table.dtype, device=table.device)
+    check(_lib.load().sg_embedding(_ptr(table), _ptr(ids), _ptr(out), ids.numel(), hidden, vocab,
+                                   dtype_code(table.dtype), _stream(stream)))
+    return out
+
+
+def argmax(logits: torch.Tensor, stream=None) -> torch.Tensor:
+    n = logits.shape[-1]
+    rows = logits.numel() // n
+    out = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    check(_lib.load().sg_argmax(_ptr(logits), rows, n, _ptr(out), _stream(stream)))
+    return out
