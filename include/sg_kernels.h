@@ -265,6 +265,28 @@ SgStatus sg_embedding(const void* table, const int32_t* ids, void* out, int32_t 
 /* out[r] = index of the largest of logits[r, 0 .. n) (first among equals). */
 SgStatus sg_argmax(const float* logits, int32_t rows, int32_t n, int32_t* out, void* stream);
 
+/* ------------------------------------------------------------------ decoder glue
+ * qkv [tokens, (heads + 2 kv_heads) * head_dim] (q heads, then k, then v) ->
+ * q_out [heads, tokens, head_dim] rotated; k rotated and v appended to the
+ * layer's cache rows k_cache / v_cache [kv_heads][.. position ..][head_dim]
+ * (kv_head_stride elements between heads) at position positions[t] (device)
+ * or pos0 + t.  io_dtype F16 or BF16. */
+SgStatus sg_qkv_rope_append(const void* qkv, int32_t tokens, int32_t heads, int32_t kv_heads, int32_t head_dim,
+                            const int32_t* positions, int32_t pos0, float base, void* q_out, void* k_cache,
+                            void* v_cache, int64_t kv_head_stride, int32_t io_dtype, void* stream);
+
+/* SwiGLU over the fused projection gate_up [rows, 2 * ffn] (gate columns, then
+ * up columns): y[t, j] = round(silu(gate)) * up. */
+SgStatus sg_swiglu_rows(const void* gate_up, void* y, int32_t rows, int32_t ffn, int32_t io_dtype, void* stream);
+
+/* out[r] = argmax of logits[r, 0 .. n) (first among equals) and, when
+ * logprob != NULL, logprob[r] = its log-softmax value. */
+SgStatus sg_argmax_logprob(const float* logits, int32_t rows, int32_t n, int32_t* out, float* logprob, void* stream);
+
+/* in [heads, tokens, head_dim] -> out [tokens, heads, head_dim]. */
+SgStatus sg_head_transpose(const void* in, void* out, int32_t heads, int32_t tokens, int32_t head_dim,
+                           int32_t io_dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

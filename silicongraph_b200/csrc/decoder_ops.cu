@@ -1,0 +1,200 @@
+// Glue kernels of the decoder layer around the linear and attention kernels:
+//   qkv_rope_append: the fused QKV projection output [T, (H + 2 Hkv) * D] is
+//     split, q and k are rotated (rope_apply_neon, matmul_neon.h:262-275),
+//     q is written head-major [H, T, D] for attention and k / v are appended to
+//     the layer's KV cache rows (kv_cache_layout.cpp:16-53 flat layout
+//     [K|V][kv_head][seq][dim]) at each token's position;
+//   head_transpose: attention output [H, T, D] -> [T, H, D] for the output
+//     projection.
+// Positions come from a device array (so one captured decode step serves
+// every position) or from pos0 + t.
+#include "sm100.cuh"
+
+namespace {
+
+template <typename T>
+__global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, int T_, int H, int Hkv, int D,
+                                       const int32_t* __restrict__ pos, int pos0, float base, T* __restrict__ q_out,
+                                       T* __restrict__ k_cache, T* __restrict__ v_cache, int64_t kv_head_stride) {
+  const int half = D / 2;
+  const int slots = H + 2 * Hkv;  // head slots per token: q heads, k heads, v heads
+  const int64_t total = (int64_t)T_ * slots * half;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int i = (int)(e % half);
+    const int64_t ts = e / half;
+    const int slot = (int)(ts % slots);
+    const int t = (int)(ts / slots);
+    const int p = pos ? pos[t] : pos0 + t;
+    const T* src = qkv + ((int64_t)t * slots + slot) * D;
+    float x0 = (float)src[i], x1 = (float)src[i + half];
+    if (slot < H + Hkv) {  // q and k rotate
+      const float theta = (float)p / powf(base, 2.0f * i / (float)D);
+      const float c = cosf(theta), s = sinf(theta);
+      const float y0 = x0 * c - x1 * s, y1 = x0 * s + x1 * c;
+      x0 = y0;
+      x1 = y1;
+    }
+    T* dst;
+    if (slot < H) dst = q_out + ((int64_t)slot * T_ + t) * D;
+    else if (slot < H + Hkv) dst = k_cache + (slot - H) * kv_head_stride + (int64_t)p * D;
+    else dst = v_cache + (slot - H - Hkv) * kv_head_stride + (int64_t)p * D;
+    dst[i] = (T)x0;
+    dst[i + half] = (T)x1;
+  }
+}
+
+template <typename T>
+__global__ void head_transpose_kernel(const T* __restrict__ in, T* __restrict__ out, int H, int T_, int D) {
+  const int64_t total = (int64_t)H * T_ * D;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int d = (int)(e % D);
+    const int64_t ht = e / D;
+    const int t = (int)(ht % T_);
+    const int h = (int)(ht / T_);
+    out[((int64_t)t * H + h) * D + d] = in[e];
+  }
+}
+
+// y[t, j] = round(silu(gu[t, j])) * gu[t, F + j]  (gate and up halves of the fused projection)
+template <typename T>
+__global__ void swiglu_rows_kernel(const T* __restrict__ gu, T* __restrict__ y, int rows, int F) {
+  const int64_t total = (int64_t)rows * F;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int j = (int)(e % F);
+    const int64_t t = e / F;
+    const float g = (float)gu[t * 2 * F + j];
+    const float s = (float)(T)(g / (1.0f + expf(-g)));  // silu rounded as the reference's silu writes it
+    y[e] = (T)(s * (float)gu[t * 2 * F + F + j]);
+  }
+}
+
+// Greedy token and its log-probability: out = argmax, logprob = x[out] - max - log(sum exp(x - max)).
+__global__ void __launch_bounds__(256) argmax_logprob_kernel(const float* __restrict__ logits, int n,
+                                                             int32_t* __restrict__ out, float* __restrict__ logprob) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  __shared__ float ss[32];
+  const float* row = logits + (int64_t)blockIdx.x * n;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = row[i];
+    if (v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  }
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (lane == 0) {
+    sv[w] = best;
+    si[w] = bi;
+  }
+  __syncthreads();
+  best = lane < nw ? sv[lane] : -INFINITY;
+  bi = lane < nw ? si[lane] : 0x7fffffff;
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  float sum = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) sum += expf(row[i] - best);
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (lane == 0) ss[w] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int k = 0; k < nw; ++k) t += ss[k];
+    const int idx = bi == 0x7fffffff ? 0 : bi;
+    out[blockIdx.x] = idx;
+    if (logprob) logprob[blockIdx.x] = row[idx] - best - logf(t);
+  }
+}
+
+int grid_of(int64_t n) {
+  const int64_t b = (n + 255) / 256;
+  return (int)(b < 1 ? 1 : (b > 148 * 16 ? 148 * 16 : b));
+}
+
+}  // namespace
+
+extern "C" {
+
+SgStatus sg_qkv_rope_append(const void* qkv, int32_t tokens, int32_t heads, int32_t kv_heads, int32_t head_dim,
+                            const int32_t* positions, int32_t pos0, float base, void* q_out, void* k_cache,
+                            void* v_cache, int64_t kv_head_stride, int32_t io_dtype, void* stream) {
+  SG_CHECK_ARG(tokens >= 0 && heads > 0 && kv_heads > 0 && head_dim > 0, "sg_qkv_rope_append: bad size");
+  if (tokens == 0) return SG_OK;
+  SG_CHECK_ARG(qkv && q_out && k_cache && v_cache, "sg_qkv_rope_append: NULL pointer");
+  SG_CHECK_ARG(head_dim % 2 == 0, "sg_qkv_rope_append: head_dim %d is odd", head_dim);
+  SG_CHECK_ARG(kv_head_stride >= head_dim, "sg_qkv_rope_append: kv_head_stride < head_dim");
+  const int dt = io_dtype == SG_DT_DEFAULT ? SG_DT_F16 : io_dtype;
+  SG_CHECK_ARG(dt == SG_DT_F16 || dt == SG_DT_BF16, "sg_qkv_rope_append: io_dtype %d unsupported", io_dtype);
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  const int64_t total = (int64_t)tokens * (heads + 2 * kv_heads) * (head_dim / 2);
+  if (dt == SG_DT_F16)
+    qkv_rope_append_kernel<__half><<<grid_of(total), 256, 0, cs>>>(
+        static_cast<const __half*>(qkv), tokens, heads, kv_heads, head_dim, positions, pos0, base,
+        static_cast<__half*>(q_out), static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), kv_head_stride);
+  else
+    qkv_rope_append_kernel<__nv_bfloat16><<<grid_of(total), 256, 0, cs>>>(
+        static_cast<const __nv_bfloat16*>(qkv), tokens, heads, kv_heads, head_dim, positions, pos0, base,
+        static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_cache),
+        static_cast<__nv_bfloat16*>(v_cache), kv_head_stride);
+  return sg::check_launch("sg_qkv_rope_append");
+}
+
+SgStatus sg_head_transpose(const void* in, void* out, int32_t heads, int32_t tokens, int32_t head_dim,
+                           int32_t io_dtype, void* stream) {
+  SG_CHECK_ARG(heads >= 0 && tokens >= 0 && head_dim >= 0, "sg_head_transpose: bad size");
+  if ((int64_t)heads * tokens * head_dim == 0) return SG_OK;
+  SG_CHECK_ARG(in && out, "sg_head_transpose: NULL pointer");
+  const int dt = io_dtype == SG_DT_DEFAULT ? SG_DT_F16 : io_dtype;
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  const int64_t total = (int64_t)heads * tokens * head_dim;
+  if (dt == SG_DT_F32)
+    head_transpose_kernel<float><<<grid_of(total), 256, 0, cs>>>(static_cast<const float*>(in),
+                                                                 static_cast<float*>(out), heads, tokens, head_dim);
+  else
+    head_transpose_kernel<uint16_t><<<grid_of(total), 256, 0, cs>>>(
+        static_cast<const uint16_t*>(in), static_cast<uint16_t*>(out), heads, tokens, head_dim);
+  return sg::check_launch("sg_head_transpose");
+}
+
+SgStatus sg_swiglu_rows(const void* gate_up, void* y, int32_t rows, int32_t ffn, int32_t io_dtype, void* stream) {
+  SG_CHECK_ARG(rows >= 0 && ffn >= 0, "sg_swiglu_rows: bad size");
+  if ((int64_t)rows * ffn == 0) return SG_OK;
+  SG_CHECK_ARG(gate_up && y, "sg_swiglu_rows: NULL pointer");
+  const int dt = io_dtype == SG_DT_DEFAULT ? SG_DT_F16 : io_dtype;
+  SG_CHECK_ARG(dt == SG_DT_F16 || dt == SG_DT_BF16, "sg_swiglu_rows: io_dtype %d unsupported", io_dtype);
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  const int64_t total = (int64_t)rows * ffn;
+  if (dt == SG_DT_F16)
+    swiglu_rows_kernel<__half><<<grid_of(total), 256, 0, cs>>>(static_cast<const __half*>(gate_up),
+                                                              static_cast<__half*>(y), rows, ffn);
+  else
+    swiglu_rows_kernel<__nv_bfloat16><<<grid_of(total), 256, 0, cs>>>(
+        static_cast<const __nv_bfloat16*>(gate_up), static_cast<__nv_bfloat16*>(y), rows, ffn);
+  return sg::check_launch("sg_swiglu_rows");
+}
+
+SgStatus sg_argmax_logprob(const float* logits, int32_t rows, int32_t n, int32_t* out, float* logprob, void* stream) {
+  SG_CHECK_ARG(rows >= 0 && n >= 1, "sg_argmax_logprob: bad size");
+  if (rows == 0) return SG_OK;
+  SG_CHECK_ARG(logits && out, "sg_argmax_logprob: logits and out must be non-NULL");
+  argmax_logprob_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(logits, n, out, logprob);
+  return sg::check_launch("sg_argmax_logprob");
+}
+
+}  // extern "C"

@@ -1,0 +1,936 @@
+// The armcc SDK (armcc_sdk.h) over the B200 kernels: package loading, graph
+// selection and decoder sessions for graph entries with execution_backend
+// "cuda".  The reference declares this API (compiler/include/armcc_sdk.h:
+// 128-214) without implementing it; the runtime flow follows its documented
+// intent (docs/package_format.md:164-174): load -> select -> session ->
+// prefill / decode.
+//
+// A "cuda" graph entry points at a graph file (format "sg-cuda-decoder")
+// holding the decoder's hyperparameters and a tensor index into one weight
+// file of 4096-aligned tensors: fp16 embeddings and norms, and every linear
+// in the reference's INT4 layout (matmul_neon.h:113-147: u8 [K/2, N], fp16
+// scales and int8 zeros [K/gs, N]), with q/k/v and gate/up fused along N.
+//
+// A session makes one device allocation (the memory planner's arena idea,
+// memory_planner.cpp:172-234, on a single cudaMalloc):
+//   [weights | KV cache [layer][K|V][kv_head][seq][dim] (kv_cache_layout.cpp:
+//    16-53) | activations at planner offsets | linear-kernel scratch |
+//    attention scratch]
+// and runs Llama-style blocks: rmsnorm -> QKV -> rope + KV append -> causal
+// attention -> O -> residual rmsnorm -> gate|up -> SwiGLU -> down, then the
+// final norm, the LM head (fp32 logits) and a greedy argmax.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "armcc_sdk.h"
+#include "sdk_io.h"
+#include "sg_sdk_ext.h"
+#include "sg_kernels.h"
+
+using sgsdk::Json;
+
+namespace {
+
+thread_local std::string g_err;
+
+void set_err(const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+}
+
+uint64_t align_up(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }
+
+struct TensorRef {
+  uint64_t offset = 0, bytes = 0;
+  std::string dtype;
+  std::vector<int64_t> shape;
+};
+
+struct ModelCfg {
+  int layers = 0, hidden = 0, heads = 0, kv_heads = 0, head_dim = 0, ffn = 0, vocab = 0;
+  float rope_theta = 10000.f, rms_eps = 1e-5f;
+  int group_size = 128;
+  bool zeros = true;
+  bool lm_int4 = true;
+  int max_context = 4096, max_chunk = 512;
+  int nqkv() const { return (heads + 2 * kv_heads) * head_dim; }
+};
+
+// ------------------------------------------------------------------ activation plan
+// Greedy best-fit interval colouring (memory_planner.cpp:172-234): buffers in
+// order of first use take the smallest free slot released before their first
+// use, else a new slot at the arena top.
+struct Buf {
+  const char* name;
+  uint64_t bytes;
+  int first, last;
+  uint64_t offset = 0;
+};
+
+uint64_t plan_offsets(std::vector<Buf>& bufs, uint64_t align) {
+  std::vector<Buf*> order;
+  for (auto& b : bufs) order.push_back(&b);
+  std::stable_sort(order.begin(), order.end(), [](const Buf* a, const Buf* b) { return a->first < b->first; });
+  struct Slot {
+    uint64_t offset, size;
+    int freed_at;
+  };
+  std::vector<Slot> slots;
+  uint64_t top = 0;
+  for (Buf* b : order) {
+    const uint64_t need = align_up(std::max<uint64_t>(b->bytes, 1), align);
+    Slot* best = nullptr;
+    for (auto& s : slots)
+      if (s.freed_at <= b->first && s.size >= need && (!best || s.size < best->size)) best = &s;
+    if (best) {
+      b->offset = best->offset;
+      best->freed_at = b->last + 1;
+    } else {
+      top = align_up(top, align);
+      b->offset = top;
+      slots.push_back({top, need, b->last + 1});
+      top += need;
+    }
+  }
+  return top;
+}
+
+// Ops of one decoder step, numbered for the lifetimes below.
+enum : int { kOpEmbed = 0, kOpNorm1 = 1, kOpQkv, kOpRope, kOpAttn, kOpTrans, kOpO, kOpNorm2, kOpGu, kOpSwiglu,
+             kOpDown, kOpNextLayer, kOpFinalNorm, kOpLm, kOpArgmax };
+
+struct Plan {
+  std::vector<Buf> bufs;
+  uint64_t bytes = 0;
+  uint64_t off(const char* n) const {
+    for (auto& b : bufs)
+      if (!strcmp(b.name, n)) return b.offset;
+    return 0;
+  }
+};
+
+Plan make_plan(const ModelCfg& c, int T) {
+  const uint64_t H = c.hidden, e = 2;
+  Plan p;
+  p.bufs = {
+      {"ids", (uint64_t)T * 4, kOpEmbed, kOpArgmax},
+      {"next", 4, kOpEmbed, kOpArgmax},
+      {"logprob", 4, kOpEmbed, kOpArgmax},
+      {"resid", T * H * e, kOpEmbed, kOpFinalNorm},
+      {"x_emb", T * H * e, kOpEmbed, kOpNorm1},
+      {"xnorm", T * H * e, kOpNorm1, kOpLm},
+      {"qkv", (uint64_t)T * c.nqkv() * e, kOpQkv, kOpRope},
+      {"qh", (uint64_t)c.heads * T * c.head_dim * e, kOpRope, kOpAttn},
+      {"attn", (uint64_t)c.heads * T * c.head_dim * e, kOpAttn, kOpO},
+      {"attn_t", (uint64_t)T * c.heads * c.head_dim * e, kOpTrans, kOpO},
+      {"o", T * H * e, kOpO, kOpNorm2},
+      {"gu", (uint64_t)T * 2 * c.ffn * e, kOpGu, kOpSwiglu},
+      {"act", (uint64_t)T * c.ffn * e, kOpSwiglu, kOpDown},
+      {"down", T * H * e, kOpDown, kOpFinalNorm},
+      {"logits", (uint64_t)c.vocab * 4, kOpLm, kOpArgmax},
+  };
+  p.bytes = plan_offsets(p.bufs, 256);
+  return p;
+}
+
+}  // namespace
+
+// ================================================================== handles
+struct ArmPackage_;
+
+struct ArmGraph_ {
+  ArmPackage_* pkg = nullptr;
+  uint32_t index = 0;
+  std::string id, path, backend, description;
+  float ttft_ms = 0, tpot_ms = 0;
+  uint64_t peak_bytes = 0;
+  uint32_t context_length = 0;
+  bool runnable = false;       // a "cuda" graph whose graph file parsed
+  std::string why_not;         // reason when not runnable
+  ModelCfg cfg;
+  std::string weight_path;     // entry of the weight file inside the package
+  std::map<std::string, TensorRef> tensors;
+};
+
+struct ArmPackage_ {
+  sgsdk::Container box;
+  Json manifest;
+  std::string model_id, family, compiler_version;
+  uint32_t num_layers = 0, hidden = 0, vocab = 0;
+  uint32_t num_kernels = 0, num_weight_files = 0;
+  std::vector<std::unique_ptr<ArmGraph_>> graphs;
+};
+
+namespace {
+
+bool parse_cuda_graph(ArmPackage_* pkg, ArmGraph_* g, std::string* why) {
+  std::string text, err;
+  if (!pkg->box.read_text(g->path, &text, &err)) {
+    *why = "graph file: " + err;
+    return false;
+  }
+  Json j;
+  if (!sgsdk::json_parse(text, &j, &err)) {
+    *why = "graph file " + g->path + ": " + err;
+    return false;
+  }
+  if (j["format"].text() != "sg-cuda-decoder") {
+    *why = "graph file " + g->path + " is not an sg-cuda-decoder description";
+    return false;
+  }
+  const Json& m = j["model"];
+  ModelCfg& c = g->cfg;
+  c.layers = (int)m["num_layers"].integer();
+  c.hidden = (int)m["hidden_size"].integer();
+  c.heads = (int)m["num_heads"].integer();
+  c.kv_heads = (int)m["num_kv_heads"].integer(c.heads);
+  c.head_dim = (int)m["head_dim"].integer(c.heads ? c.hidden / c.heads : 0);
+  c.ffn = (int)m["intermediate_size"].integer();
+  c.vocab = (int)m["vocab_size"].integer();
+  c.rope_theta = (float)m["rope_theta"].number(10000.0);
+  c.rms_eps = (float)m["rms_norm_eps"].number(1e-5);
+  const Json& qz = j["quant"];
+  c.group_size = (int)qz["group_size"].integer(128);
+  c.zeros = qz["zero_point"].boolean(true);
+  c.lm_int4 = qz["lm_head"].text("int4") == "int4";
+  c.max_context = (int)j["max_context"].integer(4096);
+  c.max_chunk = (int)j["max_prefill_chunk"].integer(512);
+  if (c.layers <= 0 || c.hidden <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.head_dim <= 0 || c.ffn <= 0 ||
+      c.vocab <= 0 || c.heads % c.kv_heads != 0 || c.head_dim % 2 != 0 || c.max_context <= 0 || c.max_chunk <= 0) {
+    *why = "graph file " + g->path + ": inconsistent model description";
+    return false;
+  }
+  // weight file and its tensor index
+  const std::string wid = j["weights"].text();
+  const Json& ws = pkg->manifest["weights"];
+  for (size_t i = 0; i < ws.size(); ++i)
+    if (ws[i]["id"].text() == wid) g->weight_path = ws[i]["path"].text();
+  if (g->weight_path.empty()) {
+    *why = "weight file '" + wid + "' is not listed in the manifest";
+    return false;
+  }
+  std::string itext;
+  if (!pkg->box.read_text(j["tensor_index"].text(), &itext, &err)) {
+    *why = "tensor index: " + err;
+    return false;
+  }
+  Json idx;
+  if (!sgsdk::json_parse(itext, &idx, &err)) {
+    *why = "tensor index: " + err;
+    return false;
+  }
+  for (auto& kv : idx["tensors"].obj) {
+    TensorRef t;
+    t.offset = (uint64_t)kv.second["offset"].integer();
+    t.bytes = (uint64_t)kv.second["bytes"].integer();
+    t.dtype = kv.second["dtype"].text();
+    for (size_t i = 0; i < kv.second["shape"].size(); ++i) t.shape.push_back(kv.second["shape"][i].integer());
+    g->tensors[kv.first] = t;
+  }
+  return true;
+}
+
+}  // namespace
+
+// ================================================================== session
+struct Linear {
+  const uint8_t* qw = nullptr;
+  const void* scales = nullptr;
+  const int8_t* zeros = nullptr;
+  int K = 0, N = 0;
+};
+
+struct ArmSession_ {
+  ArmGraph_* g = nullptr;
+  ModelCfg c;
+  int dev = 0;
+  cudaStream_t st = nullptr;
+  char* slab = nullptr;
+  uint64_t slab_bytes = 0;
+  // weights
+  const void* embed = nullptr;
+  const void* final_norm = nullptr;
+  std::vector<const void*> in_norm, post_norm;
+  std::vector<Linear> qkv, o, gu, down;
+  Linear lm;
+  const void* lm_f16 = nullptr;
+  // KV cache
+  char* kv = nullptr;
+  int64_t kv_head_stride = 0;  // elements
+  int64_t kv_block = 0;        // elements of one [kv_head][seq][dim] block (K or V of one layer)
+  // activations
+  Plan plan;
+  char* act = nullptr;
+  char* lin_ws = nullptr;
+  uint64_t lin_ws_bytes = 0;
+  char* attn_ws = nullptr;
+  uint64_t attn_ws_bytes = 0;
+  // state
+  int pos = 0;
+  bool emitted = true;
+  int32_t next_host = -1;
+  float logprob_host = 0;
+  uint32_t generated = 0;
+  float ttft_ms = 0, tpot_ms = 0;
+  std::chrono::steady_clock::time_point t_prefill_start;
+  bool ttft_pending = false;
+
+  template <typename T>
+  T* buf(const char* n) { return reinterpret_cast<T*>(act + plan.off(n)); }
+  void* kcache(int l) { return kv + (size_t)(2 * l) * kv_block * 2; }
+  void* vcache(int l) { return kv + (size_t)(2 * l + 1) * kv_block * 2; }
+};
+
+namespace {
+
+ArmStatus fail_sg(SgStatus s, const char* what) {
+  set_err("%s failed: %s", what, sg_last_error());
+  return s == SG_ERR_OOM ? ARMCC_ERR_OOM : ARMCC_ERR_RUNTIME;
+}
+
+#define SG_TRY(call, what)                    \
+  do {                                        \
+    const SgStatus s_ = (call);               \
+    if (s_ != SG_OK) return fail_sg(s_, what); \
+  } while (0)
+
+ArmStatus linear(ArmSession_* S, const Linear& L, const void* A, void* C, int M, int c_dt) {
+  SgMatMulParams p{};
+  p.A = A;
+  p.B = L.qw;
+  p.C = C;
+  p.M = M;
+  p.K = L.K;
+  p.N = L.N;
+  p.scales_B = L.scales;
+  p.zeros_B = L.zeros;
+  p.group_size = S->c.group_size;
+  p.a_dtype = SG_DT_F16;
+  p.c_dtype = c_dt;
+  p.scale_A = 1.0f;
+  p.workspace = S->lin_ws;
+  p.workspace_bytes = S->lin_ws_bytes;
+  SG_TRY(sg_matmul_int4_grouped(&p, S->st), "linear layer");
+  return ARMCC_OK;
+}
+
+// One forward pass over T tokens at positions pos .. pos+T-1 (ids already in
+// the "ids" buffer, or the device-resident next token when from_next).
+ArmStatus forward(ArmSession_* S, int T, bool from_next) {
+  const ModelCfg& c = S->c;
+  cudaStream_t st = S->st;
+  const int H = c.hidden, D = c.head_dim;
+  const int32_t* ids = from_next ? S->buf<int32_t>("next") : S->buf<int32_t>("ids");
+  SG_TRY(sg_embedding(S->embed, ids, S->buf<void>("x_emb"), T, H, c.vocab, SG_DT_F16, st), "embedding");
+  if (cudaMemsetAsync(S->buf<void>("resid"), 0, (size_t)T * H * 2, st) != cudaSuccess) {
+    set_err("cudaMemsetAsync failed");
+    return ARMCC_ERR_RUNTIME;
+  }
+  ArmStatus r;
+  for (int l = 0; l < c.layers; ++l) {
+    const void* x_in = l == 0 ? S->buf<void>("x_emb") : S->buf<void>("down");
+    SG_TRY(sg_rmsnorm(x_in, S->buf<void>("resid"), S->in_norm[l], S->buf<void>("xnorm"), T, H, c.rms_eps, SG_DT_F16,
+                      st),
+           "input rmsnorm");
+    if ((r = linear(S, S->qkv[l], S->buf<void>("xnorm"), S->buf<void>("qkv"), T, SG_DT_F16)) != ARMCC_OK) return r;
+    SG_TRY(sg_qkv_rope_append(S->buf<void>("qkv"), T, c.heads, c.kv_heads, D, nullptr, S->pos, c.rope_theta,
+                              S->buf<void>("qh"), S->kcache(l), S->vcache(l), S->kv_head_stride, SG_DT_F16, st),
+           "rope / KV append");
+    SgFlashAttentionParams a{};
+    a.Q = S->buf<void>("qh");
+    a.K = S->kcache(l);
+    a.V = S->vcache(l);
+    a.O = S->buf<void>("attn");
+    a.B = 1;
+    a.S = T;
+    a.num_heads = c.heads;
+    a.num_kv_heads = c.kv_heads;
+    a.head_dim = D;
+    a.scale = 0.f;
+    a.causal = 1;
+    a.io_dtype = SG_DT_F16;
+    a.S_kv = S->pos + T;
+    a.q_pos0 = S->pos;
+    a.kv_head_stride = S->kv_head_stride;
+    a.kv_batch_stride = S->kv_block;
+    a.workspace = S->attn_ws;
+    a.workspace_bytes = S->attn_ws_bytes;
+    const void* attn_rows = S->buf<void>("attn");
+    if (T == 1) {
+      SG_TRY(sg_flash_decode(&a, st), "decode attention");
+    } else {
+      SG_TRY(sg_flash_attention(&a, st), "prefill attention");
+      SG_TRY(sg_head_transpose(S->buf<void>("attn"), S->buf<void>("attn_t"), c.heads, T, D, SG_DT_F16, st),
+             "head transpose");
+      attn_rows = S->buf<void>("attn_t");
+    }
+    if ((r = linear(S, S->o[l], attn_rows, S->buf<void>("o"), T, SG_DT_F16)) != ARMCC_OK) return r;
+    SG_TRY(sg_rmsnorm(S->buf<void>("o"), S->buf<void>("resid"), S->post_norm[l], S->buf<void>("xnorm"), T, H,
+                      c.rms_eps, SG_DT_F16, st),
+           "post-attention rmsnorm");
+    if ((r = linear(S, S->gu[l], S->buf<void>("xnorm"), S->buf<void>("gu"), T, SG_DT_F16)) != ARMCC_OK) return r;
+    SG_TRY(sg_swiglu_rows(S->buf<void>("gu"), S->buf<void>("act"), T, c.ffn, SG_DT_F16, st), "SwiGLU");
+    if ((r = linear(S, S->down[l], S->buf<void>("act"), S->buf<void>("down"), T, SG_DT_F16)) != ARMCC_OK) return r;
+  }
+  // last token: final norm, LM head, greedy token
+  const size_t last = (size_t)(T - 1) * H * 2;
+  char* down_last = S->buf<char>("down") + last;
+  char* resid_last = S->buf<char>("resid") + last;
+  char* xn_last = S->buf<char>("xnorm") + last;
+  SG_TRY(sg_rmsnorm(down_last, resid_last, S->final_norm, xn_last, 1, H, c.rms_eps, SG_DT_F16, st), "final rmsnorm");
+  if (c.lm_int4) {
+    if ((r = linear(S, S->lm, xn_last, S->buf<void>("logits"), 1, SG_DT_F32)) != ARMCC_OK) return r;
+  } else {
+    SgMatMulParams p{};
+    p.A = xn_last;
+    p.B = S->lm_f16;
+    p.C = S->buf<void>("logits");
+    p.M = 1;
+    p.K = H;
+    p.N = c.vocab;
+    p.a_dtype = SG_DT_F16;
+    p.c_dtype = SG_DT_F32;
+    SG_TRY(sg_matmul_fp16(&p, st), "LM head");
+  }
+  SG_TRY(sg_argmax_logprob(S->buf<float>("logits"), 1, c.vocab, S->buf<int32_t>("next"), S->buf<float>("logprob"),
+                           st),
+         "argmax");
+  S->pos += T;
+  return ARMCC_OK;
+}
+
+// Reads the greedy token (and the kernels' error word) back to the host.
+ArmStatus fetch_next(ArmSession_* S) {
+  int32_t tok = -1;
+  float lp = 0;
+  if (cudaMemcpyAsync(&tok, S->buf<int32_t>("next"), 4, cudaMemcpyDeviceToHost, S->st) != cudaSuccess ||
+      cudaMemcpyAsync(&lp, S->buf<float>("logprob"), 4, cudaMemcpyDeviceToHost, S->st) != cudaSuccess ||
+      cudaStreamSynchronize(S->st) != cudaSuccess) {
+    set_err("device error: %s", cudaGetErrorString(cudaGetLastError()));
+    return ARMCC_ERR_RUNTIME;
+  }
+  const int32_t derr = sg_device_error_check(S->st);
+  if (derr != 0) {
+    set_err("a kernel reported device error %d (%s)", derr, sg_last_error());
+    return ARMCC_ERR_RUNTIME;
+  }
+  S->next_host = tok;
+  S->logprob_host = lp;
+  return ARMCC_OK;
+}
+
+bool bind_linear(ArmGraph_* g, const std::string& name, char* wbase, int K, int N, Linear* out, std::string* why) {
+  auto find = [&](const std::string& n) -> const TensorRef* {
+    auto it = g->tensors.find(n);
+    return it == g->tensors.end() ? nullptr : &it->second;
+  };
+  const TensorRef* q = find(name + ".qweight");
+  const TensorRef* s = find(name + ".scales");
+  const TensorRef* z = find(name + ".zeros");
+  const int gs = g->cfg.group_size;
+  const uint64_t G = (uint64_t)(K + gs - 1) / gs;
+  if (!q || !s || q->bytes != (uint64_t)((K + 1) / 2) * N || s->bytes != G * N * 2) {
+    *why = "tensor " + name + " missing or of the wrong size";
+    return false;
+  }
+  if (g->cfg.zeros && (!z || z->bytes != G * N)) {
+    *why = "tensor " + name + ".zeros missing or of the wrong size";
+    return false;
+  }
+  out->qw = reinterpret_cast<const uint8_t*>(wbase + q->offset);
+  out->scales = wbase + s->offset;
+  out->zeros = g->cfg.zeros ? reinterpret_cast<const int8_t*>(wbase + z->offset) : nullptr;
+  out->K = K;
+  out->N = N;
+  return true;
+}
+
+}  // namespace
+
+// ================================================================== C API
+extern "C" {
+
+const char* armpack_last_error(void) { return g_err.c_str(); }
+
+ArmPackage* armpack_load(const char* path) {
+  if (!path) {
+    set_err("armpack_load: path is NULL");
+    return nullptr;
+  }
+  auto pkg = std::make_unique<ArmPackage_>();
+  std::string err, text;
+  if (!pkg->box.open(path, &err)) {
+    set_err("armpack_load: %s", err.c_str());
+    return nullptr;
+  }
+  if (!pkg->box.read_text("manifest.json", &text, &err)) {
+    set_err("armpack_load: %s", err.c_str());
+    return nullptr;
+  }
+  if (!sgsdk::json_parse(text, &pkg->manifest, &err)) {
+    set_err("armpack_load: manifest.json: %s", err.c_str());
+    return nullptr;
+  }
+  const Json& m = pkg->manifest;
+  pkg->model_id = m["model_id"].text();
+  pkg->family = m["model_family"].text();
+  pkg->compiler_version = m["compiler_version"].text();
+  const Json& arch = m["arch"];
+  pkg->num_layers = (uint32_t)arch["num_layers"].integer();
+  pkg->hidden = (uint32_t)arch["hidden_size"].integer();
+  pkg->vocab = (uint32_t)arch["vocab_size"].integer();
+  pkg->num_kernels = (uint32_t)m["kernels"].size();
+  pkg->num_weight_files = (uint32_t)m["weights"].size();
+  const Json& gs = m["graphs"];
+  if (gs.kind != Json::Array) {
+    set_err("armpack_load: manifest.json has no graphs array");
+    return nullptr;
+  }
+  for (size_t i = 0; i < gs.size(); ++i) {
+    auto g = std::make_unique<ArmGraph_>();
+    const Json& e = gs[i];
+    g->pkg = pkg.get();
+    g->index = (uint32_t)e["index"].integer((int64_t)i);
+    g->id = e["id"].text();
+    g->path = e["path"].text();
+    g->backend = e["execution_backend"].text("cpu");
+    g->ttft_ms = (float)e["estimated_ttft_ms"].number();
+    g->tpot_ms = (float)e["estimated_tpot_ms"].number();
+    g->peak_bytes = (uint64_t)e["peak_memory_bytes"].integer();
+    g->context_length = (uint32_t)e["context_length"].integer();
+    g->description = g->id + " [" + g->backend + ", " + e["quant_dtype"].text("?") + ", context " +
+                     std::to_string(g->context_length) + "]";
+    if (g->backend == "cuda") {
+      g->runnable = parse_cuda_graph(pkg.get(), g.get(), &g->why_not);
+    } else {
+      g->why_not = "execution backend '" + g->backend + "' is not run by this library (only 'cuda')";
+    }
+    pkg->graphs.push_back(std::move(g));
+  }
+  return pkg.release();
+}
+
+void armpack_destroy(ArmPackage* pkg) { delete pkg; }
+
+uint32_t armpack_num_graphs(const ArmPackage* pkg) { return pkg ? (uint32_t)pkg->graphs.size() : 0; }
+
+ArmGraph* armpack_get_graph(ArmPackage* pkg, uint32_t index) {
+  if (!pkg || index >= pkg->graphs.size()) {
+    set_err("armpack_get_graph: index %u out of range", index);
+    return nullptr;
+  }
+  return pkg->graphs[index].get();
+}
+
+ArmGraph* armpack_select_graph(ArmPackage* pkg, const ArmDeviceState* state) {
+  if (!pkg) {
+    set_err("armpack_select_graph: package is NULL");
+    return nullptr;
+  }
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+    cudaGetLastError();
+    set_err("armpack_select_graph: no CUDA device (this library runs only 'cuda' graphs)");
+    return nullptr;
+  }
+  const uint32_t want = state ? state->context_length : 0;
+  ArmGraph_* best = nullptr;
+  for (auto& g : pkg->graphs) {
+    if (!g->runnable) continue;
+    const uint32_t ctx = g->context_length ? g->context_length : (uint32_t)g->cfg.max_context;
+    if (!best) {
+      best = g.get();
+      continue;
+    }
+    const uint32_t bctx = best->context_length ? best->context_length : (uint32_t)best->cfg.max_context;
+    const bool g_fits = ctx >= want, b_fits = bctx >= want;
+    if ((g_fits && !b_fits) || (g_fits == b_fits && (g_fits ? ctx < bctx : ctx > bctx))) best = g.get();
+  }
+  if (!best) {
+    std::string why = "no runnable 'cuda' graph in the package";
+    for (auto& g : pkg->graphs)
+      if (g->backend == "cuda") why += "; " + g->id + ": " + g->why_not;
+    set_err("armpack_select_graph: %s", why.c_str());
+  }
+  return best;
+}
+
+const char* armgraph_description(const ArmGraph* graph) { return graph ? graph->description.c_str() : ""; }
+float armgraph_estimated_tpot_ms(const ArmGraph* graph) { return graph ? graph->tpot_ms : 0.f; }
+uint64_t armgraph_peak_memory_bytes(const ArmGraph* graph) { return graph ? graph->peak_bytes : 0; }
+
+ArmSession* armgraph_create_session(ArmGraph* graph, const ArmSessionOptions* opts) {
+  if (!graph) {
+    set_err("armgraph_create_session: graph is NULL");
+    return nullptr;
+  }
+  if (!graph->runnable) {
+    set_err("armgraph_create_session: %s", graph->why_not.c_str());
+    return nullptr;
+  }
+  if (opts && !opts->use_gpu) {
+    set_err("armgraph_create_session: use_gpu is false, but this library only runs on the GPU");
+    return nullptr;
+  }
+  auto S = std::make_unique<ArmSession_>();
+  S->g = graph;
+  S->c = graph->cfg;
+  const ModelCfg& c = S->c;
+  if (const char* d = getenv("SG_DEVICE")) S->dev = atoi(d);
+  else if (cudaGetDevice(&S->dev) != cudaSuccess) S->dev = 0;
+  if (cudaSetDevice(S->dev) != cudaSuccess) {
+    cudaGetLastError();
+    set_err("armgraph_create_session: cannot use CUDA device %d", S->dev);
+    return nullptr;
+  }
+  if (cudaStreamCreateWithFlags(&S->st, cudaStreamNonBlocking) != cudaSuccess) {
+    set_err("armgraph_create_session: cudaStreamCreate failed");
+    return nullptr;
+  }
+  // weight file
+  const uint8_t* wdata = nullptr;
+  uint64_t wbytes = 0;
+  std::string err;
+  if (!graph->pkg->box.map_entry(graph->weight_path, &wdata, &wbytes, &err)) {
+    set_err("armgraph_create_session: %s", err.c_str());
+    return nullptr;
+  }
+  for (auto& kv : graph->tensors)
+    if (kv.second.offset + kv.second.bytes > wbytes) {
+      set_err("armgraph_create_session: tensor %s lies outside the weight file", kv.first.c_str());
+      return nullptr;
+    }
+  // scratch sizes of the linear kernels (largest over the shapes and token counts used)
+  const int T = c.max_chunk;
+  SgMatMulParams mp{};
+  auto lin_ws = [&](int M, int K, int N, int cdt) {
+    mp = SgMatMulParams{};
+    mp.A = mp.B = mp.scales_B = reinterpret_cast<void*>(256);
+    mp.C = reinterpret_cast<void*>(256);
+    mp.M = M;
+    mp.K = K;
+    mp.N = N;
+    mp.group_size = c.group_size;
+    mp.a_dtype = SG_DT_F16;
+    mp.c_dtype = cdt;
+    return sg_matmul_int4_grouped_workspace_size(&mp);
+  };
+  size_t lws = 0;
+  for (int M : {1, T}) {
+    lws = std::max({lws, lin_ws(M, c.hidden, c.nqkv(), SG_DT_F16), lin_ws(M, c.heads * c.head_dim, c.hidden, SG_DT_F16),
+                    lin_ws(M, c.hidden, 2 * c.ffn, SG_DT_F16), lin_ws(M, c.ffn, c.hidden, SG_DT_F16)});
+  }
+  lws = std::max(lws, lin_ws(1, c.hidden, c.vocab, SG_DT_F32));
+  SgFlashAttentionParams ap{};
+  ap.Q = ap.K = ap.V = ap.O = reinterpret_cast<void*>(256);
+  ap.B = 1;
+  ap.num_heads = c.heads;
+  ap.num_kv_heads = c.kv_heads;
+  ap.head_dim = c.head_dim;
+  ap.causal = 1;
+  ap.io_dtype = SG_DT_F16;
+  ap.S = 1;
+  ap.S_kv = c.max_context;
+  ap.q_pos0 = c.max_context - 1;
+  size_t aws = sg_flash_decode_workspace_size(&ap);
+  ap.S = T;
+  ap.q_pos0 = c.max_context - T;
+  aws = std::max(aws, sg_flash_attention_workspace_size(&ap));
+  // slab layout
+  S->plan = make_plan(c, T);
+  S->kv_head_stride = (int64_t)c.max_context * c.head_dim;
+  S->kv_block = (int64_t)c.kv_heads * S->kv_head_stride;
+  const uint64_t off_w = 0;
+  const uint64_t off_kv = align_up(off_w + wbytes, 4096);
+  const uint64_t kv_bytes = (uint64_t)c.layers * 2 * S->kv_block * 2;
+  const uint64_t off_act = align_up(off_kv + kv_bytes, 4096);
+  const uint64_t off_lws = align_up(off_act + S->plan.bytes, 4096);
+  S->lin_ws_bytes = align_up(std::max<size_t>(lws, 4096), 256);
+  const uint64_t off_aws = align_up(off_lws + S->lin_ws_bytes, 4096);
+  S->attn_ws_bytes = align_up(std::max<size_t>(aws, 256), 256);
+  S->slab_bytes = align_up(off_aws + S->attn_ws_bytes, 4096);
+  if (cudaMalloc(&S->slab, S->slab_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    set_err("armgraph_create_session: cannot allocate %llu bytes on device %d",
+            (unsigned long long)S->slab_bytes, S->dev);
+    return nullptr;
+  }
+  graph->peak_bytes = std::max(graph->peak_bytes, S->slab_bytes);
+  char* wbase = S->slab + off_w;
+  S->kv = S->slab + off_kv;
+  S->act = S->slab + off_act;
+  S->lin_ws = S->slab + off_lws;
+  S->attn_ws = S->slab + off_aws;
+  auto cleanup_fail = [&](const char* what) -> ArmSession* {
+    set_err("armgraph_create_session: %s", what);
+    return nullptr;
+  };
+  if (cudaMemcpyAsync(wbase, wdata, wbytes, cudaMemcpyHostToDevice, S->st) != cudaSuccess ||
+      cudaMemsetAsync(S->kv, 0, kv_bytes, S->st) != cudaSuccess ||
+      cudaMemsetAsync(S->lin_ws, 0, S->lin_ws_bytes, S->st) != cudaSuccess ||
+      cudaMemsetAsync(S->attn_ws, 0, S->attn_ws_bytes, S->st) != cudaSuccess ||
+      cudaStreamSynchronize(S->st) != cudaSuccess) {
+    cudaGetLastError();
+    return cleanup_fail("uploading the weights failed");
+  }
+  // bind tensors
+  auto t = [&](const std::string& n, uint64_t expect) -> const void* {
+    auto it = graph->tensors.find(n);
+    if (it == graph->tensors.end() || it->second.bytes != expect) return nullptr;
+    return wbase + it->second.offset;
+  };
+  const uint64_t H2 = (uint64_t)c.hidden * 2;
+  std::string why;
+  S->embed = t("embed_tokens", (uint64_t)c.vocab * H2);
+  S->final_norm = t("final_norm", H2);
+  if (!S->embed || !S->final_norm) return cleanup_fail("embed_tokens / final_norm missing or of the wrong size");
+  for (int l = 0; l < c.layers; ++l) {
+    const std::string p = "layers." + std::to_string(l) + ".";
+    S->in_norm.push_back(t(p + "input_norm", H2));
+    S->post_norm.push_back(t(p + "post_norm", H2));
+    if (!S->in_norm.back() || !S->post_norm.back()) return cleanup_fail(("norm weights of layer " + std::to_string(l) + " missing").c_str());
+    Linear a, b, g3, d;
+    if (!bind_linear(graph, p + "qkv", wbase, c.hidden, c.nqkv(), &a, &why) ||
+        !bind_linear(graph, p + "o", wbase, c.heads * c.head_dim, c.hidden, &b, &why) ||
+        !bind_linear(graph, p + "gate_up", wbase, c.hidden, 2 * c.ffn, &g3, &why) ||
+        !bind_linear(graph, p + "down", wbase, c.ffn, c.hidden, &d, &why))
+      return cleanup_fail(why.c_str());
+    S->qkv.push_back(a);
+    S->o.push_back(b);
+    S->gu.push_back(g3);
+    S->down.push_back(d);
+  }
+  if (c.lm_int4) {
+    if (!bind_linear(graph, "lm_head", wbase, c.hidden, c.vocab, &S->lm, &why)) return cleanup_fail(why.c_str());
+  } else {
+    S->lm_f16 = t("lm_head.weight", (uint64_t)c.vocab * H2);
+    if (!S->lm_f16) return cleanup_fail("lm_head.weight missing or of the wrong size");
+  }
+  return S.release();
+}
+
+void armsess_destroy(ArmSession* sess) {
+  if (!sess) return;
+  if (sess->st) cudaStreamSynchronize(sess->st);
+  if (sess->slab) cudaFree(sess->slab);
+  if (sess->st) cudaStreamDestroy(sess->st);
+  delete sess;
+}
+
+void armsess_reset(ArmSession* sess) {
+  if (!sess) return;
+  sess->pos = 0;
+  sess->emitted = true;
+  sess->next_host = -1;
+  sess->generated = 0;
+  sess->ttft_ms = sess->tpot_ms = 0;
+}
+
+ArmStatus armsess_prefill(ArmSession* sess, const int32_t* tokens, uint32_t n_tokens) {
+  if (!sess || (!tokens && n_tokens)) {
+    set_err("armsess_prefill: NULL argument");
+    return ARMCC_ERR_RUNTIME;
+  }
+  if (n_tokens == 0) return ARMCC_OK;
+  const ModelCfg& c = sess->c;
+  if ((uint64_t)sess->pos + n_tokens > (uint64_t)c.max_context) {
+    set_err("armsess_prefill: %u tokens after %d exceed the context of %d", n_tokens, sess->pos, c.max_context);
+    return ARMCC_ERR_OOM;
+  }
+  for (uint32_t i = 0; i < n_tokens; ++i)
+    if (tokens[i] < 0 || tokens[i] >= c.vocab) {
+      set_err("armsess_prefill: token %d at %u is outside the vocabulary", tokens[i], i);
+      return ARMCC_ERR_RUNTIME;
+    }
+  if (cudaSetDevice(sess->dev) != cudaSuccess) {
+    set_err("armsess_prefill: cannot use device %d", sess->dev);
+    return ARMCC_ERR_RUNTIME;
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  for (uint32_t done = 0; done < n_tokens;) {
+    const int T = (int)std::min<uint32_t>(n_tokens - done, (uint32_t)c.max_chunk);
+    if (cudaMemcpyAsync(sess->buf<int32_t>("ids"), tokens + done, (size_t)T * 4, cudaMemcpyHostToDevice, sess->st) !=
+        cudaSuccess) {
+      set_err("armsess_prefill: copying token ids failed");
+      return ARMCC_ERR_RUNTIME;
+    }
+    const ArmStatus r = forward(sess, T, false);
+    if (r != ARMCC_OK) return r;
+    done += T;
+  }
+  const ArmStatus r = fetch_next(sess);
+  if (r != ARMCC_OK) return r;
+  sess->emitted = false;
+  sess->t_prefill_start = t0;
+  sess->ttft_pending = true;
+  return ARMCC_OK;
+}
+
+ArmInferenceResult armsess_decode(ArmSession* sess) {
+  ArmInferenceResult res{};
+  res.next_token_id = -1;
+  if (!sess) {
+    set_err("armsess_decode: session is NULL");
+    res.status = ARMCC_ERR_RUNTIME;
+    return res;
+  }
+  if (sess->pos == 0) {
+    set_err("armsess_decode: prefill a prompt first");
+    res.status = ARMCC_ERR_RUNTIME;
+    return res;
+  }
+  cudaSetDevice(sess->dev);
+  const auto t0 = std::chrono::steady_clock::now();
+  if (sess->emitted) {
+    // feed the last emitted token (still on the device) and predict the next one
+    if (sess->pos + 1 > sess->c.max_context) {
+      set_err("armsess_decode: the context of %d tokens is full", sess->c.max_context);
+      res.status = ARMCC_ERR_OOM;
+      return res;
+    }
+    ArmStatus r = forward(sess, 1, true);
+    if (r == ARMCC_OK) r = fetch_next(sess);
+    if (r != ARMCC_OK) {
+      res.status = r;
+      return res;
+    }
+  }
+  const auto t1 = std::chrono::steady_clock::now();
+  sess->emitted = true;
+  sess->generated += 1;
+  const float step_ms = std::chrono::duration<float, std::milli>(t1 - t0).count();
+  if (sess->ttft_pending) {
+    sess->ttft_ms = std::chrono::duration<float, std::milli>(t1 - sess->t_prefill_start).count();
+    sess->ttft_pending = false;
+  } else {
+    sess->tpot_ms = sess->generated > 1 ? (sess->tpot_ms * (sess->generated - 2) + step_ms) / (sess->generated - 1)
+                                        : step_ms;
+  }
+  res.next_token_id = sess->next_host;
+  res.logprob = sess->logprob_host;
+  res.ttft_ms = sess->ttft_ms;
+  res.tpot_ms = sess->tpot_ms;
+  res.tokens_generated = sess->generated;
+  res.status = ARMCC_OK;
+  return res;
+}
+
+ArmStatus armsess_generate(ArmSession* sess, const int32_t* prompt_tokens, uint32_t prompt_len,
+                           uint32_t max_new_tokens, void (*output_cb)(int32_t token_id, void* ctx), void* ctx) {
+  ArmStatus r = armsess_prefill(sess, prompt_tokens, prompt_len);
+  if (r != ARMCC_OK) return r;
+  for (uint32_t i = 0; i < max_new_tokens; ++i) {
+    const ArmInferenceResult res = armsess_decode(sess);
+    if (res.status != ARMCC_OK) return res.status;
+    if (output_cb) output_cb(res.next_token_id, ctx);
+  }
+  return ARMCC_OK;
+}
+
+ArmInferenceResult armgraph_run(ArmGraph* graph, const int32_t* tokens, uint32_t n_tokens) {
+  ArmInferenceResult res{};
+  res.next_token_id = -1;
+  ArmSession* s = armgraph_create_session(graph, nullptr);
+  if (!s) {
+    res.status = ARMCC_ERR_RUNTIME;
+    return res;
+  }
+  const ArmStatus r = armsess_prefill(s, tokens, n_tokens);
+  if (r != ARMCC_OK) {
+    res.status = r;
+  } else {
+    res = armsess_decode(s);
+  }
+  armsess_destroy(s);
+  return res;
+}
+
+ArmStatus armpack_get_info(const ArmPackage* pkg, ArmPackageInfo* info) {
+  if (!pkg || !info) {
+    set_err("armpack_get_info: NULL argument");
+    return ARMCC_ERR_RUNTIME;
+  }
+  memset(info, 0, sizeof *info);
+  snprintf(info->model_id, sizeof info->model_id, "%s", pkg->model_id.c_str());
+  snprintf(info->model_family, sizeof info->model_family, "%s", pkg->family.c_str());
+  snprintf(info->compiler_version, sizeof info->compiler_version, "%s", pkg->compiler_version.c_str());
+  info->num_graphs = (uint32_t)pkg->graphs.size();
+  info->num_kernels = pkg->num_kernels;
+  info->num_weight_files = pkg->num_weight_files;
+  info->num_layers = pkg->num_layers;
+  info->hidden_size = pkg->hidden;
+  info->vocab_size = pkg->vocab;
+  return ARMCC_OK;
+}
+
+void armpack_print_summary(const ArmPackage* pkg) {
+  if (!pkg) return;
+  printf("armpack: %s (%s), compiler %s\n", pkg->model_id.c_str(), pkg->family.c_str(),
+         pkg->compiler_version.c_str());
+  printf("  layers %u, hidden %u, vocab %u, %u weight file(s), %u kernel(s)\n", pkg->num_layers, pkg->hidden,
+         pkg->vocab, pkg->num_weight_files, pkg->num_kernels);
+  for (auto& g : pkg->graphs)
+    printf("  graph %u: %s%s%s\n", g->index, g->description.c_str(), g->runnable ? "" : "  -- not runnable: ",
+           g->runnable ? "" : g->why_not.c_str());
+}
+
+ArmTokenizer* armpack_get_tokenizer(ArmPackage* pkg) {
+  (void)pkg;
+  set_err("armpack_get_tokenizer: not provided by this library (sessions take token ids)");
+  return nullptr;
+}
+int32_t* armtok_encode(ArmTokenizer* tok, const char* text, uint32_t* out_len) {
+  (void)tok;
+  (void)text;
+  if (out_len) *out_len = 0;
+  set_err("armtok_encode: no tokenizer");
+  return nullptr;
+}
+char* armtok_decode(ArmTokenizer* tok, const int32_t* tokens, uint32_t n_tokens) {
+  (void)tok;
+  (void)tokens;
+  (void)n_tokens;
+  set_err("armtok_decode: no tokenizer");
+  return nullptr;
+}
+void armtok_free_text(char* text) { free(text); }
+
+ArmStatus sg_session_last_logits(ArmSession* sess, float* host_out, uint32_t n) {
+  if (!sess || !host_out) {
+    set_err("sg_session_last_logits: NULL argument");
+    return ARMCC_ERR_RUNTIME;
+  }
+  if (sess->pos == 0) {
+    set_err("sg_session_last_logits: no token processed yet");
+    return ARMCC_ERR_RUNTIME;
+  }
+  const size_t count = std::min<size_t>(n, (size_t)sess->c.vocab);
+  cudaSetDevice(sess->dev);
+  if (cudaMemcpyAsync(host_out, sess->buf<float>("logits"), count * 4, cudaMemcpyDeviceToHost, sess->st) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(sess->st) != cudaSuccess) {
+    set_err("sg_session_last_logits: copy failed");
+    return ARMCC_ERR_RUNTIME;
+  }
+  return ARMCC_OK;
+}
+
+uint32_t sg_session_position(const ArmSession* sess) { return sess ? (uint32_t)sess->pos : 0; }
+void armtok_free_tokens(int32_t* tokens) { free(tokens); }
+
+}  // extern "C"

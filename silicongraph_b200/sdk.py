@@ -1,0 +1,218 @@
+"""Python bindings of the armcc SDK C API (include/armcc_sdk.h) exported by
+libsg_b200.so: load a package, select its "cuda" graph, run sessions."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _lib
+
+ARMCC_OK = 0
+
+
+class ArmDeviceState(ctypes.Structure):
+    _fields_ = [("soc_id", ctypes.c_int), ("ram_mb", ctypes.c_uint32), ("battery_pct", ctypes.c_int32),
+                ("thermal_state", ctypes.c_int), ("latency_mode", ctypes.c_int),
+                ("context_length", ctypes.c_uint32), ("gpu_available", ctypes.c_bool),
+                ("npu_available", ctypes.c_bool)]
+
+
+class ArmSessionOptions(ctypes.Structure):
+    _fields_ = [("num_threads", ctypes.c_int32), ("use_gpu", ctypes.c_bool), ("use_npu", ctypes.c_bool),
+                ("seed", ctypes.c_uint32), ("verbose", ctypes.c_bool)]
+
+
+class ArmInferenceResult(ctypes.Structure):
+    _fields_ = [("next_token_id", ctypes.c_int32), ("logprob", ctypes.c_float), ("ttft_ms", ctypes.c_float),
+                ("tpot_ms", ctypes.c_float), ("tokens_generated", ctypes.c_uint32), ("status", ctypes.c_int)]
+
+
+class ArmPackageInfo(ctypes.Structure):
+    _fields_ = [("model_id", ctypes.c_char * 256), ("model_family", ctypes.c_char * 64),
+                ("compiler_version", ctypes.c_char * 32), ("num_graphs", ctypes.c_uint32),
+                ("num_kernels", ctypes.c_uint32), ("num_weight_files", ctypes.c_uint32),
+                ("num_layers", ctypes.c_uint32), ("hidden_size", ctypes.c_uint32),
+                ("vocab_size", ctypes.c_uint32)]
+
+
+_P = ctypes.c_void_p
+_CB = ctypes.CFUNCTYPE(None, ctypes.c_int32, ctypes.c_void_p)
+_SIGS = {
+    "armpack_load": (_P, [ctypes.c_char_p]),
+    "armpack_destroy": (None, [_P]),
+    "armpack_last_error": (ctypes.c_char_p, []),
+    "armpack_select_graph": (_P, [_P, ctypes.POINTER(ArmDeviceState)]),
+    "armpack_num_graphs": (ctypes.c_uint32, [_P]),
+    "armpack_get_graph": (_P, [_P, ctypes.c_uint32]),
+    "armgraph_description": (ctypes.c_char_p, [_P]),
+    "armgraph_estimated_tpot_ms": (ctypes.c_float, [_P]),
+    "armgraph_peak_memory_bytes": (ctypes.c_uint64, [_P]),
+    "armgraph_create_session": (_P, [_P, ctypes.POINTER(ArmSessionOptions)]),
+    "armsess_destroy": (None, [_P]),
+    "armsess_reset": (None, [_P]),
+    "armsess_prefill": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32]),
+    "armsess_decode": (ArmInferenceResult, [_P]),
+    "armsess_generate": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32, ctypes.c_uint32,
+                                        _CB, _P]),
+    "armgraph_run": (ArmInferenceResult, [_P, ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32]),
+    "armpack_get_info": (ctypes.c_int, [_P, ctypes.POINTER(ArmPackageInfo)]),
+    "armpack_print_summary": (None, [_P]),
+    "armpack_get_tokenizer": (_P, [_P]),
+    "sg_session_last_logits": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_float), ctypes.c_uint32]),
+    "sg_session_position": (ctypes.c_uint32, [_P]),
+}
+
+
+class ArmError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"armcc status {status}: {msg}")
+        self.status = status
+
+
+def lib() -> ctypes.CDLL:
+    L = _lib.load()
+    if not getattr(L, "_armcc_sigs", False):
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        L._armcc_sigs = True
+    return L
+
+
+def last_error() -> str:
+    return (lib().armpack_last_error() or b"").decode(errors="replace")
+
+
+def _tokens(tokens) -> tuple[ctypes.Array, int]:
+    a = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), a.size, a
+
+
+class Package:
+    def __init__(self, path: str):
+        self.h = lib().armpack_load(path.encode())
+        if not self.h:
+            raise ArmError(-2, last_error())
+
+    def close(self):
+        if self.h:
+            lib().armpack_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def num_graphs(self) -> int:
+        return lib().armpack_num_graphs(self.h)
+
+    def info(self) -> dict:
+        i = ArmPackageInfo()
+        st = lib().armpack_get_info(self.h, ctypes.byref(i))
+        if st != ARMCC_OK:
+            raise ArmError(st, last_error())
+        return {f: (getattr(i, f).decode() if isinstance(getattr(i, f), bytes) else getattr(i, f))
+                for f, _ in ArmPackageInfo._fields_}
+
+    def graph(self, index: int) -> "Graph":
+        g = lib().armpack_get_graph(self.h, index)
+        if not g:
+            raise ArmError(-1, last_error())
+        return Graph(self, g)
+
+    def select(self, context_length: int = 0) -> "Graph":
+        st = ArmDeviceState(gpu_available=True, context_length=context_length)
+        g = lib().armpack_select_graph(self.h, ctypes.byref(st))
+        if not g:
+            raise ArmError(-1, last_error())
+        return Graph(self, g)
+
+
+class Graph:
+    def __init__(self, pkg: Package, h):
+        self.pkg, self.h = pkg, h
+
+    @property
+    def description(self) -> str:
+        return lib().armgraph_description(self.h).decode()
+
+    @property
+    def peak_memory_bytes(self) -> int:
+        return lib().armgraph_peak_memory_bytes(self.h)
+
+    def session(self) -> "Session":
+        return Session(self)
+
+    def run(self, tokens) -> ArmInferenceResult:
+        p, n, _keep = _tokens(tokens)
+        return lib().armgraph_run(self.h, p, n)
+
+
+class Session:
+    def __init__(self, graph: Graph):
+        self.graph = graph
+        self.h = lib().armgraph_create_session(graph.h, None)
+        if not self.h:
+            raise ArmError(-5, last_error())
+
+    def close(self):
+        if self.h:
+            lib().armsess_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def reset(self):
+        lib().armsess_reset(self.h)
+
+    def prefill(self, tokens):
+        p, n, _keep = _tokens(tokens)
+        st = lib().armsess_prefill(self.h, p, n)
+        if st != ARMCC_OK:
+            raise ArmError(st, last_error())
+
+    def decode(self) -> ArmInferenceResult:
+        r = lib().armsess_decode(self.h)
+        if r.status != ARMCC_OK:
+            raise ArmError(r.status, last_error())
+        return r
+
+    def generate(self, prompt, max_new_tokens: int) -> list[int]:
+        out = []
+        cb = _CB(lambda tok, ctx: out.append(int(tok)))
+        p, n, _keep = _tokens(prompt)
+        st = lib().armsess_generate(self.h, p, n, max_new_tokens, cb, None)
+        if st != ARMCC_OK:
+            raise ArmError(st, last_error())
+        return out
+
+    def last_logits(self, vocab: int) -> np.ndarray:
+        out = np.zeros(vocab, np.float32)
+        st = lib().sg_session_last_logits(self.h, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), vocab)
+        if st != ARMCC_OK:
+            raise ArmError(st, last_error())
+        return out
+
+    @property
+    def position(self) -> int:
+        return lib().sg_session_position(self.h)

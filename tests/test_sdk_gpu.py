@@ -1,0 +1,102 @@
+"""End to end through the armcc SDK on the GPU: a random-init Llama-style INT4
+package, prefill + greedy decode, against the decoder composition oracle
+(oracle/decoder.py: the reference's kernel semantics with fp16 values at op
+boundaries).  Logits within |got - want| <= 2e-3 + 1e-2 |want|; greedy tokens
+equal wherever the oracle's top two logits differ by more than that."""
+import numpy as np
+import pytest
+
+from silicongraph_b200 import armpack
+
+pytestmark = pytest.mark.gpu
+
+SMALL = armpack.llama_config(layers=2, hidden=256, heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=1000,
+                             rope_theta=500000.0, max_pos=4096)
+RTOL, ATOL = 1e-2, 2e-3
+
+
+def close(got, want):
+    err = np.abs(got - want)
+    bad = err > ATOL + RTOL * np.abs(want)
+    assert not bad.any(), f"{bad.sum()} / {bad.size} logits outside tolerance; max err {err.max():.3e}"
+
+
+def check_token(tok, logits_ref):
+    top = np.sort(logits_ref)[-2:]
+    if top[1] - top[0] > ATOL + RTOL * abs(top[1]):
+        assert tok == int(np.argmax(logits_ref))
+
+
+def _package(tmp_path, chunk, ctx=1024, seed=1):
+    w = armpack.random_llama_weights(SMALL, seed=seed)
+    t = armpack.cuda_tensors(SMALL, w, group_size=32)
+    path = armpack.write_package(str(tmp_path / f"m{chunk}.armpack"), SMALL, t, max_context=ctx,
+                                 max_prefill_chunk=chunk)
+    return path, t
+
+
+@pytest.mark.parametrize("prompt_len,chunk", [
+    (37, 128),     # short prompt: CUDA-core attention, row GEMV path below 64 rows
+    (300, 512),    # one 300-token chunk: tensor-core GEMM and tensor-core attention
+    (300, 128),    # chunked prefill: three chunks attending to the earlier ones
+])
+def test_session_matches_decoder_oracle(sg, oracle_mod, tmp_path, prompt_len, chunk):
+    from oracle.decoder import DecoderOracle
+    from silicongraph_b200 import sdk
+    path, t = _package(tmp_path, chunk)
+    rng = np.random.default_rng(prompt_len)
+    prompt = rng.integers(0, SMALL["vocab_size"], prompt_len).astype(np.int32)
+    ref = DecoderOracle(SMALL, t, group_size=32)
+    with sdk.Package(path) as pkg:
+        g = pkg.select(context_length=prompt_len + 8)
+        with g.session() as s:
+            s.prefill(prompt)
+            assert s.position == prompt_len
+            want = ref.forward(prompt)
+            close(s.last_logits(SMALL["vocab_size"]), want)
+            tok = s.decode().next_token_id
+            check_token(tok, want)
+            for step in range(4):
+                want = ref.forward([tok])
+                r = s.decode()
+                close(s.last_logits(SMALL["vocab_size"]), want)
+                check_token(r.next_token_id, want)
+                assert r.tokens_generated == step + 2
+                tok = r.next_token_id
+            assert s.position == prompt_len + 4
+
+
+def test_generate_run_and_reset(sg, tmp_path):
+    from silicongraph_b200 import sdk
+    path, _ = _package(tmp_path, 128)
+    prompt = np.arange(20, dtype=np.int32) * 7 % SMALL["vocab_size"]
+    with sdk.Package(path) as pkg:
+        g = pkg.select()
+        with g.session() as s:
+            a = s.generate(prompt, 6)
+            s.reset()
+            b = s.generate(prompt, 6)
+            assert a == b and len(a) == 6
+            assert s.position == 20 + 5
+        r = g.run(prompt)
+        assert r.status == 0 and r.next_token_id == a[0]
+
+
+def test_session_errors(sg, tmp_path):
+    from silicongraph_b200 import sdk
+    path, _ = _package(tmp_path, 64, ctx=96)
+    with sdk.Package(path) as pkg:
+        with pkg.select().session() as s:
+            with pytest.raises(sdk.ArmError):
+                s.decode()                                   # nothing prefilled
+            with pytest.raises(sdk.ArmError):
+                s.prefill([0, 5, SMALL["vocab_size"]])       # token outside the vocabulary
+            with pytest.raises(sdk.ArmError) as e:
+                s.prefill(np.zeros(97, np.int32))            # longer than the context
+            assert e.value.status == -3
+            s.prefill(np.zeros(95, np.int32))
+            s.decode()                                       # the token predicted by the prompt
+            s.decode()                                       # fills position 96
+            with pytest.raises(sdk.ArmError) as e:
+                s.decode()
+            assert e.value.status == -3
