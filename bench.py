@@ -670,6 +670,145 @@ def run_attention(args):
         dist.destroy_process_group()
 
 
+# ----------------------------------------------------------------------------- end-to-end decode
+DECODE_CFG = dict(layers=16, hidden=2048, heads=32, kv_heads=8, head_dim=64, ffn=8192, vocab=128256,
+                  rope_theta=500000.0)
+DECODE_WORKLOAD = ("Llama-3.2-1B-shape decoder through the armcc SDK: 16 layers, hidden 2048, 32/8 heads, "
+                   "head_dim 64, SwiGLU 8192, vocab 128256, INT4 group-32 weights (lm_head included), fp16 "
+                   "activations and KV cache; prompt of 512 random ids, then greedy decode, batch 1")
+
+
+def build_decode_package(path, cfg, seed=0, gs=32, max_context=1024):
+    """Random N(0, 0.02) weights (norms 1 + N(0, 0.02)) drawn on the GPU and
+    packed by the library's device packer, written as a directory package."""
+    import torch
+
+    from silicongraph_b200 import _lib, armpack
+    lib = _lib.load()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    H, V, F = cfg["hidden_size"], cfg["vocab_size"], cfg["intermediate_size"]
+    Hq, Hkv, D = cfg["num_heads"], cfg["num_kv_heads"], cfg["head_dim"]
+
+    def randn(*shape):
+        return torch.randn(*shape, generator=g, device="cuda", dtype=torch.float32) * 0.02
+
+    def quant(K, N):
+        w = randn(K, N)
+        G = (K + gs - 1) // gs
+        B = torch.empty(((K + 1) // 2, N), dtype=torch.uint8, device="cuda")
+        S = torch.empty((G, N), dtype=torch.float16, device="cuda")
+        Z = torch.empty((G, N), dtype=torch.int8, device="cuda")
+        _lib.check(lib.sg_quantize_int4_grouped(w.data_ptr(), K, N, gs, 0, B.data_ptr(), S.data_ptr(),
+                                                Z.data_ptr(), torch.cuda.current_stream().cuda_stream))
+        return B.cpu().numpy(), S.cpu().numpy(), Z.cpu().numpy()
+
+    t = {"embed_tokens": randn(V, H).half().cpu().numpy()}
+    for i in range(cfg["num_layers"]):
+        q = f"layers.{i}."
+        t[q + "input_norm"] = (1 + randn(H)).half().cpu().numpy()
+        t[q + "post_norm"] = (1 + randn(H)).half().cpu().numpy()
+        for name, K, N in (("qkv", H, (Hq + 2 * Hkv) * D), ("o", Hq * D, H), ("gate_up", H, 2 * F), ("down", F, H)):
+            B, S, Z = quant(K, N)
+            t[q + name + ".qweight"], t[q + name + ".scales"], t[q + name + ".zeros"] = B, S, Z
+    t["final_norm"] = (1 + randn(H)).half().cpu().numpy()
+    t["lm_head.qweight"], t["lm_head.scales"], t["lm_head.zeros"] = quant(H, V)
+    armpack.write_package(path, cfg, t, group_size=gs, max_context=max_context, max_prefill_chunk=512,
+                          as_zip=False, model_id="synthetic/llama-3.2-1b-shape")
+    weight_bytes = sum(a.nbytes for k, a in t.items() if k != "embed_tokens") + H * 2
+    return weight_bytes, t
+
+
+def decode_cpu_sample(cfg, tensors, seconds):
+    """The decoder composition oracle (reference kernel semantics, 1 thread) on
+    the same packed model: a 4-token prompt and greedy steps until `seconds`."""
+    from oracle.decoder import DecoderOracle
+    ref = DecoderOracle(cfg, tensors, group_size=32)
+    ref.forward([1, 2, 3, 4])
+    n, tok, t0 = 0, 5, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        tok = int(np.argmax(ref.forward([tok])))
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 4), "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"{n} greedy decode steps of the full model after a 4-token prompt, decoder composition "
+                      f"of the oracle kernels (fp16 values between ops), {dt:.1f} s on 1 host thread"}
+
+
+def run_decode(args):
+    import tempfile
+
+    import torch
+
+    from silicongraph_b200 import armpack, sdk
+
+    rank, local_rank, world = rank_env()
+    torch.cuda.set_device(local_rank)
+    os.environ["SG_DEVICE"] = str(local_rank)
+    c = DECODE_CFG
+    cfg = armpack.llama_config(layers=c["layers"], hidden=c["hidden"], heads=c["heads"], kv_heads=c["kv_heads"],
+                               head_dim=c["head_dim"], ffn=c["ffn"], vocab=c["vocab"], rope_theta=c["rope_theta"])
+    prompt_len = 512
+    steps = args.steps
+    with tempfile.TemporaryDirectory() as td:
+        pkg_path = os.path.join(td, "llama1b_int4")
+        weight_bytes, tensors = build_decode_package(pkg_path, cfg, seed=11 + rank,
+                                                     max_context=prompt_len + steps + args.warmup + 8)
+        rng = np.random.default_rng(5 + rank)
+        prompt = rng.integers(0, c["vocab"], prompt_len).astype(np.int32)
+        with sdk.Package(pkg_path) as pkg:
+            graph = pkg.select(context_length=prompt_len + steps + args.warmup)
+            with graph.session() as s:
+                # warm-up: a full prompt and a few steps (allocations, tensor maps, caches)
+                s.prefill(prompt)
+                for _ in range(args.warmup):
+                    s.decode()
+                s.reset()
+                clocks = ClockSampler(torch.cuda.current_device(), interval_ms=50) if rank == 0 else None
+                t0 = time.perf_counter()
+                s.prefill(prompt)
+                first = s.decode()                      # the token predicted by the prompt
+                t1 = time.perf_counter()
+                for _ in range(steps):
+                    s.decode()
+                t2 = time.perf_counter()
+                clk = clocks.stop() if clocks else None
+    decode_s = t2 - t1
+    tps = steps / decode_s
+    ctx_mid = prompt_len + steps / 2
+    kv_read = 2 * c["layers"] * c["kv_heads"] * c["head_dim"] * 2 * ctx_mid
+    bytes_per_token = weight_bytes + kv_read
+    peak, peak_src = read_peak_hbm()
+    line = {
+        "metric": "INT4 decode tokens/s (Llama-3.2-1B shape, batch 1)",
+        "value": round(world * tps, 2), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * decode_s / steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (random N(0,0.02) weights drawn on the GPU, random prompt ids)",
+        "config": {"workload": DECODE_WORKLOAD, "prompt": prompt_len, "decode_steps": steps,
+                   "ttft_ms": round(1e3 * (t1 - t0), 3), "prefill_tokens_per_s": round(prompt_len / (t1 - t0), 1),
+                   "bytes_per_token": int(bytes_per_token),
+                   "parallelism": f"replicas x{world} (one session per GPU)",
+                   "timing": "host clock around armsess_decode calls (each returns the token to the host)"},
+        "roofline": {"bound": "hbm", "achieved": round(bytes_per_token * tps / 1e9, 2), "peak": peak,
+                     "unit": "GB/s", "frac": round(bytes_per_token * tps / 1e9 / peak, 4),
+                     "peak_source": f"{peak_src} hbm_gbs", "traffic": None,
+                     "achieved_basis": "weights + KV cache bytes per token x decode tokens/s"},
+        "e2e": {"value": round(world * tps, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 8},
+        "gpu_launches": steps * (10 * c["layers"] + 4),
+        "clocks": clk,
+        "first_token": int(first.next_token_id),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            line["cpu_baseline"] = decode_cpu_sample(cfg, tensors, args.cpu_seconds)
+        except Exception as e:  # the baseline is reported, never required
+            line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args):
     rank, _, world = rank_env()
@@ -753,7 +892,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--ref-budget-s", type=float, default=120.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["gemv_int4", *PF_WORKLOADS, *ATTN_WORKLOADS], default="gemv_int4",
+    ap.add_argument("--workload", choices=["gemv_int4", *PF_WORKLOADS, *ATTN_WORKLOADS, "decode_llama1b"],
+                    default="gemv_int4",
                     help="gemv_int4 (default): the decode GEMV; prefill_int4 / prefill_int8: the prefill GEMM; "
                          "attn_prefill / attn_small: flash attention")
     args = ap.parse_args()
@@ -771,6 +911,8 @@ def main():
         run_prefill(args)
     elif args.workload in ATTN_WORKLOADS:
         run_attention(args)
+    elif args.workload == "decode_llama1b":
+        run_decode(args)
     else:
         run_ours(args)
 

@@ -101,6 +101,11 @@ typedef struct SgFlashAttentionParams {
   int64_t kv_head_stride; /* elements between kv heads of K/V; <= 0 = dense    */
   void* workspace;        /* optional caller scratch (decode split-K)          */
   size_t workspace_bytes;
+  /* Optional device int32: the position of query 0, read by the kernel at run
+   * time (queries then sit at the end: keys = *q_pos_device + S).  S_kv is the
+   * capacity the launch is sized for.  Lets one captured CUDA graph of a decode
+   * step serve every position.  Decode (sg_flash_decode) form only. */
+  const int32_t* q_pos_device;
 } SgFlashAttentionParams;
 
 /* ---------------------------------------------------------------- status */

@@ -75,6 +75,7 @@ class SgFlashAttentionParams(ctypes.Structure):
         ("kv_head_stride", ctypes.c_int64),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
+        ("q_pos_device", ctypes.c_void_p),
     ]
 
 

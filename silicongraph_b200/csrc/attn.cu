@@ -17,7 +17,9 @@
 // Used for decode (few queries, long KV) and for shapes outside the tensor-core
 // prefill kernel.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
+#include <string_view>
 
 #include "sg_common.cuh"
 
@@ -42,6 +44,7 @@ struct AArgs {
   int qb;                       // query positions per work item
   int nsplit, keys_per_split;
   float* part;                  // [B][H][Sq][nsplit][D + 2]  (o..., m, l)
+  const int32_t* q_pos_dev;     // device position of query 0 (Skv is then the capacity)
 };
 
 __device__ __forceinline__ float ld_io(const void* p, int dt, int64_t i) {
@@ -73,10 +76,13 @@ __global__ void __launch_bounds__(kThreads) attn_cc_kernel(AArgs a) {
   const int nq = min(a.qb, a.Sq - q0);
   const int rows = a.G * nq;  // row r: head hk*G + r / nq, position q0 + r % nq
 
+  // positions from the device (a captured decode step) or from the launch
+  const int q_pos0 = a.q_pos_dev ? *a.q_pos_dev : a.q_pos0;
+  const int Skv = a.q_pos_dev ? min(a.Skv, q_pos0 + a.Sq) : a.Skv;
   // key range of this split, clipped to what the causal mask lets any row see
   int j0 = split * a.keys_per_split;
-  int j1 = min(a.Skv, j0 + a.keys_per_split);
-  if (a.causal) j1 = min(j1, a.q_pos0 + q0 + nq);  // last visible key + 1
+  int j1 = min(Skv, j0 + a.keys_per_split);
+  if (a.causal) j1 = min(j1, q_pos0 + q0 + nq);  // last visible key + 1
   const int64_t kvbase = (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs;
 
   float q[kMaxRowsPerWarp][DPL], o[kMaxRowsPerWarp][DPL], m[kMaxRowsPerWarp], l[kMaxRowsPerWarp];
@@ -96,7 +102,7 @@ __global__ void __launch_bounds__(kThreads) attn_cc_kernel(AArgs a) {
     }
     if (r < rows) {
       const int h = hk * a.G + r / nq, qi = q0 + r % nq;
-      pos[rr] = a.q_pos0 + qi;
+      pos[rr] = q_pos0 + qi;
       const int64_t qoff = (((int64_t)b * a.H + h) * a.Sq + qi) * a.D;
 #pragma unroll
       for (int e = 0; e < DPL; ++e) {
@@ -171,6 +177,141 @@ __global__ void __launch_bounds__(kThreads) attn_cc_kernel(AArgs a) {
   }
 }
 
+// Decode form: few query rows per kv head (G * Sq <= 32), head_dim 64 or 128.
+// Per 64-key tile: scores with one key per thread (K tile padded in shared
+// memory, no shuffles per key), online softmax with one warp per row, then
+// O += P V with one (row, dim) per thread.  Scores are prescaled by
+// scale * log2(e) and use exp2; the partial max is written back in natural
+// units for attn_combine_kernel.
+constexpr int kDecRows = 32;
+
+template <int D>
+__global__ void __launch_bounds__(kThreads) attn_decode_kernel(AArgs a) {
+  constexpr int KT = kKeyTile;   // 64 keys per tile
+  constexpr int KS = D + 1;      // padded K row
+  constexpr int OPT = (kDecRows * D + kThreads - 1) / kThreads;  // outputs per thread (max)
+  extern __shared__ float sm[];
+  float* qs = sm;                        // [kDecRows][D]  prescaled queries
+  float* ks = qs + kDecRows * D;         // [KT][KS]
+  float* vs = ks + KT * KS;              // [KT][D]
+  float* ps = vs + KT * D;               // [kDecRows][KT] scores / probabilities
+  float* ms = ps + kDecRows * KT;        // [kDecRows] running max (log2 units)
+  float* ls = ms + kDecRows;             // [kDecRows] running sum
+  float* al = ls + kDecRows;             // [kDecRows] rescale of this tile
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int b = blockIdx.z, hk = blockIdx.y, split = blockIdx.x;
+  const int nq = a.Sq, R = a.G * nq;  // row r: head hk*G + r / nq, query r % nq
+  const int q_pos0 = a.q_pos_dev ? *a.q_pos_dev : a.q_pos0;
+  const int Skv = a.q_pos_dev ? min(a.Skv, q_pos0 + a.Sq) : a.Skv;
+  const int j0 = split * a.keys_per_split;
+  int j1 = min(Skv, j0 + a.keys_per_split);
+  if (a.causal) j1 = min(j1, q_pos0 + nq);
+  const int64_t kvbase = (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs;
+  const float qscale = a.scale * 1.4426950408889634f;
+  for (int i = tid; i < R * D; i += kThreads) {
+    const int r = i / D, d = i % D;
+    const int h = hk * a.G + r / nq, qi = r % nq;
+    qs[i] = ld_io(a.Q, a.io_dt, (((int64_t)b * a.H + h) * a.Sq + qi) * D + d) * qscale;
+  }
+  for (int r = tid; r < kDecRows; r += kThreads) {
+    ms[r] = -INFINITY;
+    ls[r] = 0.f;
+  }
+  float o[OPT];
+#pragma unroll
+  for (int k = 0; k < OPT; ++k) o[k] = 0.f;
+  for (int jt = j0; jt < j1; jt += KT) {
+    const int nk = min(KT, j1 - jt);
+    __syncthreads();  // previous tile's readers are done
+    for (int i = tid; i < KT * D; i += kThreads) {
+      const int j = i / D, d = i % D;
+      float kv = 0.f, vv = 0.f;
+      if (j < nk) {
+        const int64_t off = kvbase + (int64_t)(jt + j) * D + d;
+        kv = ld_io(a.K, a.io_dt, off);
+        vv = ld_io(a.V, a.io_dt, off);
+      }
+      ks[j * KS + d] = kv;
+      vs[j * D + d] = vv;
+    }
+    __syncthreads();
+    // scores: thread -> key j = tid % KT, rows tid / KT, + kThreads / KT, ...
+    {
+      const int j = tid % KT;
+      for (int r = tid / KT; r < R; r += kThreads / KT) {
+        float sdot = 0.f;
+#pragma unroll 8
+        for (int d = 0; d < D; ++d) sdot = fmaf(qs[r * D + d], ks[j * KS + d], sdot);
+        const int key = jt + j;
+        const bool vis = j < nk && (!a.causal || key <= q_pos0 + r % nq);
+        ps[r * KT + j] = vis ? sdot : -INFINITY;
+      }
+    }
+    __syncthreads();
+    // online softmax: one warp per row
+    for (int r = warp; r < R; r += kThreads / 32) {
+      const float s0 = ps[r * KT + lane], s1 = ps[r * KT + lane + 32];
+      float mx = fmaxf(s0, s1);
+#pragma unroll
+      for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_old = ms[r];
+      const float m_new = fmaxf(m_old, mx);
+      const float p0 = m_new == -INFINITY ? 0.f : exp2f(s0 - m_new);
+      const float p1 = m_new == -INFINITY ? 0.f : exp2f(s1 - m_new);
+      ps[r * KT + lane] = p0;
+      ps[r * KT + lane + 32] = p1;
+      float sum = p0 + p1;
+#pragma unroll
+      for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      const float alpha = m_old == -INFINITY ? 0.f : exp2f(m_old - m_new);
+      __syncwarp();
+      if (lane == 0) {
+        ms[r] = m_new;
+        ls[r] = ls[r] * alpha + sum;
+        al[r] = alpha;
+      }
+    }
+    __syncthreads();
+    // O += P V: thread -> outputs i = tid + k * kThreads (row i / D, dim i % D)
+#pragma unroll
+    for (int k = 0; k < OPT; ++k) {
+      const int i = tid + k * kThreads;
+      if (i < R * D) {
+        const int r = i / D, d = i % D;
+        float acc = o[k] * al[r];
+#pragma unroll 8
+        for (int j = 0; j < KT; ++j) acc = fmaf(ps[r * KT + j], vs[j * D + d], acc);
+        o[k] = acc;
+      }
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < OPT; ++k) {
+    const int i = tid + k * kThreads;
+    if (i >= R * D) continue;
+    const int r = i / D, d = i % D;
+    const int h = hk * a.G + r / nq, qi = r % nq;
+    if (a.nsplit == 1) {
+      const float inv = ls[r] > 0.f ? 1.0f / ls[r] : 0.f;
+      st_io(a.O, a.io_dt, (((int64_t)b * a.H + h) * a.Sq + qi) * D + d, o[k] * inv);
+    } else {
+      float* pp = a.part + ((((int64_t)b * a.H + h) * a.Sq + qi) * a.nsplit + split) * (D + 2);
+      pp[d] = o[k];
+      if (d == 0) {
+        pp[D] = ms[r] == -INFINITY ? -INFINITY : ms[r] * 0.6931471805599453f;  // back to natural units
+        pp[D + 1] = ls[r];
+      }
+    }
+  }
+}
+
+template <int D>
+constexpr size_t decode_smem() {
+  return sizeof(float) * ((size_t)kDecRows * D + kKeyTile * (D + 1) + kKeyTile * D + kDecRows * kKeyTile +
+                          3 * kDecRows);
+}
+
 // Merge the splits of one (batch, head, query) row: fixed split order.
 __global__ void attn_combine_kernel(AArgs a) {
   const int row = blockIdx.x;  // (b * H + h) * Sq + qi
@@ -193,9 +334,20 @@ __global__ void attn_combine_kernel(AArgs a) {
   }
 }
 
+std::atomic<int> g_decode_kernel{1};  // key-parallel decode kernel on/off
+
 }  // namespace
 
 namespace sg {
+
+bool attn_tuning(std::string_view key, int value) {
+  if (key == "attn.decode_kernel") {
+    g_decode_kernel.store(value);
+    return true;
+  }
+  return false;
+}
+
 
 SgStatus attn_validate(const SgFlashAttentionParams* p, const char* name) {
   SG_CHECK_ARG(p != nullptr, "%s: params is NULL", name);
@@ -243,6 +395,7 @@ SgStatus attn_cc_run(const SgFlashAttentionParams* p, void* stream, int want_spl
   a.scale = p->scale > 0.f ? p->scale : 1.0f / sqrtf((float)p->head_dim);
   a.causal = p->causal != 0;
   a.q_pos0 = p->q_pos0 >= 0 ? p->q_pos0 : a.Skv - a.Sq;
+  a.q_pos_dev = p->q_pos_device;
   a.kv_hs = p->kv_head_stride > 0 ? p->kv_head_stride : (int64_t)a.Skv * a.D;
   a.kv_bs = p->kv_batch_stride > 0 ? p->kv_batch_stride : (int64_t)a.Hkv * a.kv_hs;
   a.io_dt = p->io_dtype == SG_DT_DEFAULT ? SG_DT_F16 : p->io_dtype;
@@ -272,6 +425,27 @@ SgStatus attn_cc_run(const SgFlashAttentionParams* p, void* stream, int want_spl
       SG_CHECK_ARG(ws_bytes >= need, "%s: workspace too small (%zu < %zu bytes)", name, ws_bytes, need);
     }
     a.part = static_cast<float*>(ws);
+  }
+  // Few query rows per kv head (decode): the key-parallel kernel.
+  if ((a.D == 64 || a.D == 128) && a.G * a.Sq <= kDecRows && g_decode_kernel.load()) {
+    const dim3 dgrid(nsplit, a.Hkv, a.B);
+    // shared-memory attribute set once per (kernel, device)
+    static std::atomic<uint64_t> set_mask[2] = {{0}, {0}};
+    auto launch_dec = [&](void (*kfn)(AArgs), size_t sm, int which) -> SgStatus {
+      const uint64_t bit = dev < 64 ? (uint64_t)1 << dev : 0;
+      if (!(set_mask[which].load() & bit)) {
+        SG_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        set_mask[which].fetch_or(bit);
+      }
+      kfn<<<dgrid, kThreads, sm, cs>>>(a);
+      return check_launch("attn_decode_kernel");
+    };
+    a.qb = a.Sq;
+    st = a.D == 64 ? launch_dec(attn_decode_kernel<64>, decode_smem<64>(), 0)
+                   : launch_dec(attn_decode_kernel<128>, decode_smem<128>(), 1);
+    if (st != SG_OK || nsplit == 1) return st;
+    attn_combine_kernel<<<a.B * a.H * a.Sq, 64, 0, cs>>>(a);
+    return check_launch("attn_combine_kernel");
   }
   const size_t smem = (size_t)2 * kKeyTile * a.D * sizeof(float);
   dim3 grid(nqb * nsplit, a.Hkv, a.B);

@@ -432,7 +432,7 @@ namespace sg {
 // tensors and K / V strides.
 namespace {
 bool tc_qualifies(const SgFlashAttentionParams* p) {
-  if (!g_tune_attn_tc.load()) return false;
+  if (!g_tune_attn_tc.load() || p->q_pos_device) return false;
   const int io = p->io_dtype == SG_DT_DEFAULT ? SG_DT_F16 : p->io_dtype;
   const int D = p->head_dim;
   if ((io != SG_DT_F16 && io != SG_DT_BF16) || (D != 64 && D != 128)) return false;

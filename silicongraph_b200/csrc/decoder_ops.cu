@@ -122,6 +122,89 @@ __global__ void __launch_bounds__(256) argmax_logprob_kernel(const float* __rest
   }
 }
 
+// Parallel form: each block reduces a slice of one row to (max, first index
+// of the max, sum of exp(x - max)); one block per row merges the slices in
+// order (equal maxima keep the lowest index).
+constexpr int kArgSlice = 4096;
+
+__global__ void __launch_bounds__(256) argmax_partial_kernel(const float* __restrict__ logits, int n, int slices,
+                                                             float* __restrict__ part) {
+  __shared__ float sv[8], ssum[8];
+  __shared__ int si[8];
+  const int row = blockIdx.y, sl = blockIdx.x;
+  const float* x = logits + (int64_t)row * n;
+  const int i0 = sl * kArgSlice, i1 = min(n, i0 + kArgSlice);
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    const float v = x[i];
+    if (v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  }
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sv[w] = best;
+    si[w] = bi;
+  }
+  __syncthreads();
+  best = sv[0];
+  bi = si[0];
+  for (int k = 1; k < 8; ++k)
+    if (sv[k] > best || (sv[k] == best && si[k] < bi)) {
+      best = sv[k];
+      bi = si[k];
+    }
+  float sum = 0.f;
+  if (best != -INFINITY)
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) sum += expf(x[i] - best);
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (lane == 0) ssum[w] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int k = 0; k < 8; ++k) t += ssum[k];
+    float* pp = part + ((int64_t)row * slices + sl) * 3;
+    pp[0] = best;
+    pp[1] = __int_as_float(bi);
+    pp[2] = t;
+  }
+}
+
+__global__ void argmax_merge_kernel(const float* __restrict__ logits, int n, int slices,
+                                    const float* __restrict__ part, int32_t* __restrict__ out,
+                                    float* __restrict__ logprob) {
+  if (threadIdx.x != 0) return;
+  const int row = blockIdx.x;
+  const float* pp = part + (int64_t)row * slices * 3;
+  float M = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int k = 0; k < slices; ++k) {
+    const float m = pp[3 * k];
+    const int i = __float_as_int(pp[3 * k + 1]);
+    if (m > M || (m == M && i < idx)) {
+      M = m;
+      idx = i;
+    }
+  }
+  float L = 0.f;
+  if (M != -INFINITY)
+    for (int k = 0; k < slices; ++k)
+      if (pp[3 * k] != -INFINITY) L += pp[3 * k + 2] * expf(pp[3 * k] - M);
+  const int r = idx == 0x7fffffff ? 0 : idx;
+  out[row] = r;
+  if (logprob) logprob[row] = logits[(int64_t)row * n + r] - M - logf(L);
+}
+
 int grid_of(int64_t n) {
   const int64_t b = (n + 255) / 256;
   return (int)(b < 1 ? 1 : (b > 148 * 16 ? 148 * 16 : b));
@@ -193,7 +276,19 @@ SgStatus sg_argmax_logprob(const float* logits, int32_t rows, int32_t n, int32_t
   SG_CHECK_ARG(rows >= 0 && n >= 1, "sg_argmax_logprob: bad size");
   if (rows == 0) return SG_OK;
   SG_CHECK_ARG(logits && out, "sg_argmax_logprob: logits and out must be non-NULL");
-  argmax_logprob_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(logits, n, out, logprob);
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  const int slices = (n + kArgSlice - 1) / kArgSlice;
+  if (slices <= 1 || rows > 65535) {
+    argmax_logprob_kernel<<<rows, 256, 0, cs>>>(logits, n, out, logprob);
+    return sg::check_launch("sg_argmax_logprob");
+  }
+  void* ws = nullptr;
+  SgStatus st = sg::library_workspace(stream, (size_t)rows * slices * 3 * sizeof(float), &ws, sg::kWsArgmax);
+  if (st != SG_OK) return st;
+  argmax_partial_kernel<<<dim3(slices, rows), 256, 0, cs>>>(logits, n, slices, static_cast<float*>(ws));
+  st = sg::check_launch("sg_argmax_logprob");
+  if (st != SG_OK) return st;
+  argmax_merge_kernel<<<rows, 32, 0, cs>>>(logits, n, slices, static_cast<const float*>(ws), out, logprob);
   return sg::check_launch("sg_argmax_logprob");
 }
 

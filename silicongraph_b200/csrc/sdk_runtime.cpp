@@ -131,6 +131,7 @@ Plan make_plan(const ModelCfg& c, int T) {
       {"ids", (uint64_t)T * 4, kOpEmbed, kOpArgmax},
       {"next", 4, kOpEmbed, kOpArgmax},
       {"logprob", 4, kOpEmbed, kOpArgmax},
+      {"pos", 4, kOpEmbed, kOpArgmax},
       {"resid", T * H * e, kOpEmbed, kOpFinalNorm},
       {"x_emb", T * H * e, kOpEmbed, kOpNorm1},
       {"xnorm", T * H * e, kOpNorm1, kOpLm},
@@ -289,6 +290,22 @@ struct ArmSession_ {
   float ttft_ms = 0, tpot_ms = 0;
   std::chrono::steady_clock::time_point t_prefill_start;
   bool ttft_pending = false;
+  // decode step as a CUDA graph: positions come from the device ("pos")
+  bool use_graph = true;
+  bool graph_failed = false;
+  int eager_steps = 0;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t graph_exec = nullptr;
+  int32_t* h_pos = nullptr;  // pinned
+
+  ~ArmSession_() {
+    if (st) cudaStreamSynchronize(st);
+    if (graph_exec) cudaGraphExecDestroy(graph_exec);
+    if (graph) cudaGraphDestroy(graph);
+    if (slab) cudaFree(slab);
+    if (h_pos) cudaFreeHost(h_pos);
+    if (st) cudaStreamDestroy(st);
+  }
 
   template <typename T>
   T* buf(const char* n) { return reinterpret_cast<T*>(act + plan.off(n)); }
@@ -330,8 +347,10 @@ ArmStatus linear(ArmSession_* S, const Linear& L, const void* A, void* C, int M,
 }
 
 // One forward pass over T tokens at positions pos .. pos+T-1 (ids already in
-// the "ids" buffer, or the device-resident next token when from_next).
-ArmStatus forward(ArmSession_* S, int T, bool from_next) {
+// the "ids" buffer, or the device-resident next token when from_next).  With
+// dev_pos (one decode token) the kernels read the position from the "pos"
+// buffer instead of launch arguments, so the launches can be captured once.
+ArmStatus forward(ArmSession_* S, int T, bool from_next, bool dev_pos = false) {
   const ModelCfg& c = S->c;
   cudaStream_t st = S->st;
   const int H = c.hidden, D = c.head_dim;
@@ -348,7 +367,8 @@ ArmStatus forward(ArmSession_* S, int T, bool from_next) {
                       st),
            "input rmsnorm");
     if ((r = linear(S, S->qkv[l], S->buf<void>("xnorm"), S->buf<void>("qkv"), T, SG_DT_F16)) != ARMCC_OK) return r;
-    SG_TRY(sg_qkv_rope_append(S->buf<void>("qkv"), T, c.heads, c.kv_heads, D, nullptr, S->pos, c.rope_theta,
+    SG_TRY(sg_qkv_rope_append(S->buf<void>("qkv"), T, c.heads, c.kv_heads, D,
+                              dev_pos ? S->buf<int32_t>("pos") : nullptr, S->pos, c.rope_theta,
                               S->buf<void>("qh"), S->kcache(l), S->vcache(l), S->kv_head_stride, SG_DT_F16, st),
            "rope / KV append");
     SgFlashAttentionParams a{};
@@ -364,8 +384,9 @@ ArmStatus forward(ArmSession_* S, int T, bool from_next) {
     a.scale = 0.f;
     a.causal = 1;
     a.io_dtype = SG_DT_F16;
-    a.S_kv = S->pos + T;
-    a.q_pos0 = S->pos;
+    a.S_kv = dev_pos ? c.max_context : S->pos + T;
+    a.q_pos0 = dev_pos ? 0 : S->pos;
+    a.q_pos_device = dev_pos ? S->buf<int32_t>("pos") : nullptr;
     a.kv_head_stride = S->kv_head_stride;
     a.kv_batch_stride = S->kv_block;
     a.workspace = S->attn_ws;
@@ -412,6 +433,49 @@ ArmStatus forward(ArmSession_* S, int T, bool from_next) {
          "argmax");
   S->pos += T;
   return ARMCC_OK;
+}
+
+// One decode token through the captured graph (captured on the second step,
+// after an eager step has done every first-use allocation and attribute call).
+ArmStatus decode_step(ArmSession_* S) {
+  *S->h_pos = S->pos;
+  if (cudaMemcpyAsync(S->buf<int32_t>("pos"), S->h_pos, 4, cudaMemcpyHostToDevice, S->st) != cudaSuccess) {
+    set_err("copying the position failed");
+    return ARMCC_ERR_RUNTIME;
+  }
+  if (S->use_graph && S->graph_exec) {
+    if (cudaGraphLaunch(S->graph_exec, S->st) != cudaSuccess) {
+      set_err("cudaGraphLaunch failed: %s", cudaGetErrorString(cudaGetLastError()));
+      return ARMCC_ERR_RUNTIME;
+    }
+    S->pos += 1;
+    return ARMCC_OK;
+  }
+  if (S->use_graph && !S->graph_failed && S->eager_steps > 0) {
+    const int pos_before = S->pos;
+    if (cudaStreamBeginCapture(S->st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+      const ArmStatus r = forward(S, 1, true, true);
+      cudaGraph_t g = nullptr;
+      const cudaError_t e = cudaStreamEndCapture(S->st, &g);
+      cudaGraphExec_t x = nullptr;
+      if (r == ARMCC_OK && e == cudaSuccess && g && cudaGraphInstantiate(&x, g, 0) == cudaSuccess) {
+        S->graph = g;
+        S->graph_exec = x;
+        if (cudaGraphLaunch(x, S->st) != cudaSuccess) {
+          set_err("cudaGraphLaunch failed: %s", cudaGetErrorString(cudaGetLastError()));
+          return ARMCC_ERR_RUNTIME;
+        }
+        return ARMCC_OK;  // forward() advanced pos
+      }
+      if (g) cudaGraphDestroy(g);
+    }
+    cudaGetLastError();
+    S->graph_failed = true;  // run eagerly from now on
+    S->pos = pos_before;
+  }
+  const ArmStatus r = forward(S, 1, true, true);
+  if (r == ARMCC_OK) S->eager_steps += 1;
+  return r;
 }
 
 // Reads the greedy token (and the kernels' error word) back to the host.
@@ -598,10 +662,13 @@ ArmSession* armgraph_create_session(ArmGraph* graph, const ArmSessionOptions* op
     set_err("armgraph_create_session: cannot use CUDA device %d", S->dev);
     return nullptr;
   }
-  if (cudaStreamCreateWithFlags(&S->st, cudaStreamNonBlocking) != cudaSuccess) {
-    set_err("armgraph_create_session: cudaStreamCreate failed");
+  if (cudaStreamCreateWithFlags(&S->st, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMallocHost(&S->h_pos, sizeof(int32_t)) != cudaSuccess) {
+    cudaGetLastError();
+    set_err("armgraph_create_session: cannot create the session's stream");
     return nullptr;
   }
+  if (const char* gflag = getenv("SG_DECODE_GRAPH")) S->use_graph = atoi(gflag) != 0;
   // weight file
   const uint8_t* wdata = nullptr;
   uint64_t wbytes = 0;
@@ -725,11 +792,8 @@ ArmSession* armgraph_create_session(ArmGraph* graph, const ArmSessionOptions* op
 }
 
 void armsess_destroy(ArmSession* sess) {
-  if (!sess) return;
-  if (sess->st) cudaStreamSynchronize(sess->st);
-  if (sess->slab) cudaFree(sess->slab);
-  if (sess->st) cudaStreamDestroy(sess->st);
-  delete sess;
+  if (sess) cudaSetDevice(sess->dev);
+  delete sess;  // the destructor waits for the stream and frees the slab
 }
 
 void armsess_reset(ArmSession* sess) {
@@ -803,7 +867,7 @@ ArmInferenceResult armsess_decode(ArmSession* sess) {
       res.status = ARMCC_ERR_OOM;
       return res;
     }
-    ArmStatus r = forward(sess, 1, true);
+    ArmStatus r = decode_step(sess);
     if (r == ARMCC_OK) r = fetch_next(sess);
     if (r != ARMCC_OK) {
       res.status = r;

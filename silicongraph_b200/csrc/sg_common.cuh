@@ -52,7 +52,8 @@ int sm_count(int dev);
 // never overwritten by another family's partial results.  Growth synchronises
 // the stream, so the first call with a larger shape must not run under stream
 // capture.
-enum WorkspaceUser : int { kWsInt4Gemv = 0, kWsDenseGemv = 1, kWsAttention = 2, kWsPrefillGemm = 3, kWsUsers = 4 };
+enum WorkspaceUser : int { kWsInt4Gemv = 0, kWsDenseGemv = 1, kWsAttention = 2, kWsPrefillGemm = 3, kWsArgmax = 4,
+                           kWsUsers = 5 };
 SgStatus library_workspace(void* stream, size_t bytes, void** out, int user);
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }

@@ -384,6 +384,7 @@ SgStatus w4_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, void
 bool w4_gemv_mma_tuning(std::string_view key, int value);
 bool gemm_tc_tuning(std::string_view key, int value);
 bool attn_tc_tuning(std::string_view key, int value);
+bool attn_tuning(std::string_view key, int value);
 }  // namespace sg
 
 // Core entry.  ws == NULL: library scratch (unless ws_external, then an error
@@ -553,6 +554,7 @@ int32_t sg_set_tuning(const char* key, int32_t value) {
   if (key && sg::w4_gemv_mma_tuning(std::string_view(key), value)) return SG_OK;
   if (key && sg::gemm_tc_tuning(std::string_view(key), value)) return SG_OK;
   if (key && sg::attn_tc_tuning(std::string_view(key), value)) return SG_OK;
+  if (key && sg::attn_tuning(std::string_view(key), value)) return SG_OK;
   sg::set_error("sg_set_tuning: unknown key");
   return SG_ERR_NOT_FOUND;
 }

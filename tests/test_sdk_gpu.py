@@ -100,3 +100,24 @@ def test_session_errors(sg, tmp_path):
             with pytest.raises(sdk.ArmError) as e:
                 s.decode()
             assert e.value.status == -3
+
+
+def test_decode_graph_matches_eager(sg, tmp_path, monkeypatch):
+    """Decode steps replayed from the captured CUDA graph give the same tokens
+    and logits as eager launches."""
+    from silicongraph_b200 import sdk
+    path, _ = _package(tmp_path, 128)
+    prompt = (np.arange(40, dtype=np.int32) * 13) % SMALL["vocab_size"]
+    runs = []
+    for flag in ("1", "0"):
+        monkeypatch.setenv("SG_DECODE_GRAPH", flag)
+        with sdk.Package(path) as pkg:
+            with pkg.select().session() as s:
+                s.prefill(prompt)
+                toks, logits = [], []
+                for _ in range(6):
+                    toks.append(s.decode().next_token_id)
+                    logits.append(s.last_logits(SMALL["vocab_size"]))
+                runs.append((toks, np.stack(logits)))
+    assert runs[0][0] == runs[1][0]
+    assert np.array_equal(runs[0][1], runs[1][1])
