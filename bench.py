@@ -75,48 +75,89 @@ def read_profile_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons, sampled during the timed region."""
+    """SM clocks and throttle reasons, sampled during the timed region.
+
+    NVML (pynvml) is polled from a background thread every interval_ms, so
+    that a timed region of a few milliseconds still gets samples; without
+    pynvml, nvidia-smi -lms does the sampling."""
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, gpu_index: int, interval_ms: int = 200):
+    def __init__(self, gpu_index: int, interval_ms: float = 0.5):
+        import threading
         self.proc = None
+        self.thread = None
+        self.samples = []  # (sm_mhz, sm_max_mhz, reasons)
+        self.stop_flag = threading.Event()
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            pr = torch.cuda.get_device_properties(gpu_index)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            masks = {"hw_slowdown": pynvml.nvmlClocksEventReasonHwSlowdown,
+                     "hw_thermal_slowdown": pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                     "sw_thermal_slowdown": pynvml.nvmlClocksEventReasonSwThermalSlowdown,
+                     "sw_power_cap": pynvml.nvmlClocksEventReasonSwPowerCap}
+            smax = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+
+            def poll():
+                while not self.stop_flag.is_set():
+                    try:
+                        sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                        r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.samples.append((sm, smax, {n for n, m in masks.items() if r & m}))
+                    except pynvml.NVMLError:
+                        return
+                    self.stop_flag.wait(interval_ms / 1e3)
+
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", str(interval_ms)],
+                 "--format=csv,noheader,nounits", "-lms", str(max(20, int(interval_ms)))],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, ValueError):
             self.proc = None
 
     def stop(self):
-        if self.proc is None:
-            return None
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=10)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
-        sm, smax, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 8:
-                continue
+        if self.thread is not None:
+            self.stop_flag.set()
+            self.thread.join(timeout=5)
+            src = "nvml"
+        elif self.proc is not None:
+            self.proc.terminate()
             try:
-                sm.append(float(parts[0]))
-                smax = max(smax, float(parts[1]))
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[4:8]):
-                if v.lower() in ("active", "1", "yes"):
-                    reasons.add(nm)
-        if not sm:
+                out, _ = self.proc.communicate(timeout=10)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            for line in out.strip().splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 8:
+                    continue
+                try:
+                    sm, smax = float(parts[0]), float(parts[1])
+                except ValueError:
+                    continue
+                self.samples.append((sm, smax, {n for n, v in zip(self.NAMES, parts[4:8])
+                                                if v.lower() in ("active", "1", "yes")}))
+            src = "nvidia-smi"
+        else:
             return None
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return None
+        reasons = set().union(*(r for _, _, r in self.samples))
+        return {"sm_mhz": float(np.median([s for s, _, _ in self.samples])),
+                "sm_max_mhz": max(m for _, m, _ in self.samples), "reasons": sorted(reasons),
+                "samples": len(self.samples), "source": src}
 
 
 # ----------------------------------------------------------------------------- CPU baseline
@@ -196,8 +237,10 @@ def run_ours(args):
     del W
     x = x_host.to(dev)
     y = torch.empty((1, N), dtype=torch.float32, device=dev)
-    params = [kernels.matmul_params(x, Bs[i], y, M=1, K=K, N=N, scales=Ss[i], zeros=Zs[i], group_size=gs)
-              for i in range(copies)]
+    # the weights are written once, before the timed launches: they may stream
+    # before each launch's dependency wait
+    params = [kernels.matmul_params(x, Bs[i], y, M=1, K=K, N=N, scales=Ss[i], zeros=Zs[i], group_size=gs,
+                                    flags=_lib.SG_MM_STATIC_WEIGHTS) for i in range(copies)]
     pptr = [ctypes.byref(p) for p in params]
     st = stream.cuda_stream
     fn = lib.sg_matmul_int4_grouped
@@ -450,7 +493,7 @@ def run_prefill(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    clocks = ClockSampler(torch.cuda.current_device(), interval_ms=20) if rank == 0 else None
+    clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
     barrier()
     torch.cuda.synchronize()
     ms = max_over_ranks(timed(p_main, args.steps))
@@ -606,7 +649,7 @@ def run_attention(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    clocks = ClockSampler(torch.cuda.current_device(), interval_ms=20) if rank == 0 else None
+    clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
     if world > 1:
         dist.barrier(device_ids=[local_rank])
     torch.cuda.synchronize()
@@ -764,7 +807,7 @@ def run_decode(args):
                 for _ in range(args.warmup):
                     s.decode()
                 s.reset()
-                clocks = ClockSampler(torch.cuda.current_device(), interval_ms=50) if rank == 0 else None
+                clocks = ClockSampler(torch.cuda.current_device(), interval_ms=5) if rank == 0 else None
                 t0 = time.perf_counter()
                 s.prefill(prompt)
                 first = s.decode()                      # the token predicted by the prompt

@@ -49,6 +49,13 @@ typedef enum {
   SG_DT_I8 = 4
 } SgDType;
 
+/* SgMatMulParams.flags */
+#define SG_MM_STATIC_WEIGHTS 1u /* B, scales_B and zeros_B are not written by the
+                                   kernel launched just before this call on the
+                                   stream: the GEMV may start streaming them before
+                                   it waits for that kernel (programmatic dependent
+                                   launch); A is always read after the wait */
+
 /*
  * Mirrors armcc::kernels::cpu::MatMulParams (matmul_neon.h:32-43).
  * Fields up to group_size keep the reference's names and meanings; the
@@ -72,6 +79,7 @@ typedef struct SgMatMulParams {
   int32_t c_dtype;        /* SgDType of C                                      */
   void* workspace;        /* optional caller scratch, see *_workspace_size()   */
   size_t workspace_bytes;
+  uint32_t flags;         /* SG_MM_* bits; 0 = no assumptions                  */
 } SgMatMulParams;
 
 /*

@@ -48,7 +48,11 @@ class SgMatMulParams(ctypes.Structure):
         ("c_dtype", ctypes.c_int32),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
+        ("flags", ctypes.c_uint32),
     ]
+
+
+SG_MM_STATIC_WEIGHTS = 1
 
 
 class SgFlashAttentionParams(ctypes.Structure):

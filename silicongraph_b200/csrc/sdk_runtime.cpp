@@ -342,6 +342,7 @@ ArmStatus linear(ArmSession_* S, const Linear& L, const void* A, void* C, int M,
   p.scale_A = 1.0f;
   p.workspace = S->lin_ws;
   p.workspace_bytes = S->lin_ws_bytes;
+  p.flags = SG_MM_STATIC_WEIGHTS;  // weights are uploaded once, when the session is created
   SG_TRY(sg_matmul_int4_grouped(&p, S->st), "linear layer");
   return ARMCC_OK;
 }
@@ -698,7 +699,9 @@ ArmSession* armgraph_create_session(ArmGraph* graph, const ArmSessionOptions* op
     return sg_matmul_int4_grouped_workspace_size(&mp);
   };
   size_t lws = 0;
-  for (int M : {1, T}) {
+  // every token count a call can see: the row kernels' scratch depends on M
+  // below the tensor-core GEMM's threshold
+  for (int M = 1; M <= T; M = (M < 64 ? M + 1 : (M == T ? T + 1 : std::min(2 * M, T)))) {
     lws = std::max({lws, lin_ws(M, c.hidden, c.nqkv(), SG_DT_F16), lin_ws(M, c.heads * c.head_dim, c.hidden, SG_DT_F16),
                     lin_ws(M, c.hidden, 2 * c.ffn, SG_DT_F16), lin_ws(M, c.ffn, c.hidden, SG_DT_F16)});
   }

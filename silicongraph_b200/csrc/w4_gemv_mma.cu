@@ -32,8 +32,18 @@
 //   * Rows are assigned to the 4 lanes of a quad so that their (row mod 8)
 //     values differ by 2: with the 128-byte swizzle the 8 lanes of a quarter
 //     warp hit 8 distinct 16-byte bank groups (no bank conflicts).
-//   * Blocks reduce their phases in shared memory; a 512-column tile shared by
-//     two blocks is finished by the later one (atomic ticket, fixed order).
+//   * Scheduling: either clusters of ksplit blocks per 512-column tile that
+//     reduce through distributed shared memory, or a balanced stream-K split
+//     of all (tile, chunk) units over one block per SM.  In the latter a
+//     block's range touches one or more tiles ("segments"); every warp flushes
+//     its quad-reduced sums per segment into a private shared-memory slot, the
+//     block sums its phases, owns interior tiles outright, and hands the
+//     partial of a tile shared with its neighbours to global scratch, where
+//     the last block to arrive (atomic ticket) adds the partials in block
+//     order (deterministic).
+//   * With SG_MM_STATIC_WEIGHTS the first weight stages are requested before
+//     griddepcontrol.wait, so the weight stream overlaps the tail of the
+//     previous kernel on the stream; the activation is read after the wait.
 #include <cooperative_groups.h>
 
 #include <algorithm>
@@ -45,9 +55,9 @@
 
 namespace {
 
-constexpr int kStrips = 4;
 constexpr int kRows = 32;                    // k-pair rows per chunk
-constexpr int kTileCols = kStrips * 128;     // 512
+constexpr int kStreamKStrips = 4;           // stream-K tiles are 512 columns
+constexpr int kStreamKCols = kStreamKStrips * 128;
 constexpr int kWBytes = 128 * kRows;         // 4096
 constexpr int kSBytes = 128 * 2 * 2;         // 2 scale rows x 128 fp16
 constexpr int kZBytes = 128 * 2;             // 2 zero rows x 128 int8
@@ -61,6 +71,16 @@ constexpr int kVariantWarps[4] = {16, 20, 12, 8};
 constexpr int kVariantStages[4] = {2, 2, 3, 5};
 constexpr int off_sz(int warps, int stages) { return warps * stages * kWBytes; }
 constexpr int off_x(int warps, int stages) { return off_sz(warps, stages) + warps * stages * kSZBytes; }
+// Dynamic shared memory after the stages (bytes): B fragments of the staged
+// activation rows, per-half sums, a zero row, the stage barriers, the
+// cluster's [rank][column] partials (rank 0's copy is the one used), then the
+// per-segment, per-phase partial sums.
+constexpr size_t kXSlotBytes = (size_t)kRows * kXRowBytes + 2 * 16;
+inline size_t tail_bytes(int warps, int stages, int strips, int x_slots, int max_segs, int ksplit) {
+  const size_t cols = (size_t)strips * 128;
+  return (size_t)x_slots * kXSlotBytes + 16 + (size_t)warps * stages * 8 + (size_t)ksplit * cols * 4 +
+         (size_t)max_segs * (warps / strips) * cols * 4;
+}
 std::atomic<int> g_variant{0};
 std::atomic<int> g_sleep{0};
 std::atomic<int> g_cluster_mode{1};
@@ -73,32 +93,25 @@ struct MArgs {
   int a_dt, c_dt;
   float scale_A;
   int has_zeros;
-  int n_tiles, cpt, nblocks, flat, total;
+  int n_tiles, cpt, nblocks, total;
+  int q, r;            // stream-K: block b owns chunks [b q + min(b, r), ...); the first r own q + 1
   int ksplit;          // cluster mode: blocks (cluster ranks) per 512-column tile
-  int max_chunks;      // x staging capacity (chunks per block)
+  int x_slots;         // activation staging capacity in 32-row chunks
+  int x_by_row;        // slot of chunk c: c % cpt (range longer than K) or c - range start
+  int max_segs;        // tiles one block's range can touch
   int gs_shift;        // log2(gs) when gs is a power of two, else -1
   int sleep_wait;      // back off with nanosleep while waiting for a stage
-  float* slots;        // [nblocks][2][512]
+  int static_w;        // weights may be requested before the dependency wait
+  float* slots;        // [nblocks][2][512]: first / last segment partials
   unsigned* tickets;   // [n_tiles]
   int* err;
 };
 
-__device__ __forceinline__ void block_range(const MArgs& a, int b, int& cs, int& ce) {
-  if (a.flat) {
-    cs = (int)((long long)a.total * b / a.nblocks);
-    ce = (int)((long long)a.total * (b + 1) / a.nblocks);
-  } else {  // one block per tile
-    cs = b * a.cpt;
-    ce = cs + a.cpt;
-  }
-}
+__device__ __forceinline__ int range_start(const MArgs& a, int b) { return b * a.q + min(b, a.r); }
 
 __device__ __forceinline__ int block_of_chunk(const MArgs& a, int c) {
-  if (!a.flat) return c / a.cpt;
-  int b = (int)((long long)c * a.nblocks / a.total);
-  while (b + 1 < a.nblocks && (long long)a.total * (b + 1) / a.nblocks <= c) ++b;
-  while (b > 0 && (long long)a.total * b / a.nblocks > c) --b;
-  return b;
+  const int big = a.r * (a.q + 1);
+  return c < big ? c / (a.q + 1) : a.r + (c - big) / a.q;
 }
 
 __device__ __forceinline__ float load_act(const void* A, int dt, int i) {
@@ -148,24 +161,29 @@ __device__ __forceinline__ int group_of(const MArgs& a, int k) { return a.gs_shi
 // CLUSTER: grid (ksplit, n_tiles), clusters of ksplit blocks own one tile and
 // reduce their partials through distributed shared memory (no scratch).
 // Otherwise: flat split of all chunks over the blocks, reduced through scratch.
-template <bool HAS_Z, int WARPS, int STAGES, bool CLUSTER>
+// STRIPS: 128-column strips per tile (tile = STRIPS x 128 columns); the
+// block's warps are STRIPS strips x WARPS / STRIPS phases.
+template <bool HAS_Z, int WARPS, int STAGES, bool CLUSTER, int STRIPS>
 __global__ void __launch_bounds__(WARPS * 32, 1)
     w4_gemv_mma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmS,
                        const __grid_constant__ CUtensorMap tmZ, MArgs a) {
-  constexpr int kWarps = WARPS, kThreads = WARPS * 32, kPhases = WARPS / kStrips, kStages = STAGES;
+  constexpr int kWarps = WARPS, kThreads = WARPS * 32, kPhases = WARPS / STRIPS, kStages = STAGES;
+  constexpr int kTC = STRIPS * 128;
   constexpr int kOffW = 0, kOffSZ = off_sz(WARPS, STAGES), kOffX = off_x(WARPS, STAGES);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* xst = smem + kOffX;                                             // [chunk][32 rows][32 B]
-  float4* xrow = reinterpret_cast<float4*>(xst + a.max_chunks * kRows * kXRowBytes);  // [chunk][32]
-  float4* xhalf = xrow + a.max_chunks * kRows;                             // [chunk][2]: Xhi, Phi, Xlo, Plo
-  uint8_t* zrow = reinterpret_cast<uint8_t*>(xhalf + a.max_chunks * 2);   // 16 zero bytes
+  uint8_t* xst = smem + kOffX;                                                  // [slot][32 rows][32 B]
+  float4* xhalf = reinterpret_cast<float4*>(xst + a.x_slots * kRows * kXRowBytes);  // [slot][2]: Xhi, Phi, Xlo, Plo
+  uint8_t* zrow = reinterpret_cast<uint8_t*>(xhalf + a.x_slots * 2);           // 16 zero bytes
   uint64_t* bars = reinterpret_cast<uint64_t*>(zrow + 16);
+  float* csum = reinterpret_cast<float*>(bars + kWarps * kStages);  // cluster: [rank][kTC]
+  float* red = csum + (CLUSTER ? a.ksplit * kTC : 0);                // [seg][phase][kTC]
   __shared__ int s_last;
   __shared__ int s_abort;
+  __shared__ int s_aborts[16];  // cluster: rank r's abort flag, gathered in rank 0
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int strip = warp % kStrips, phase = warp / kStrips;
+  const int strip = warp % STRIPS, phase = warp / STRIPS;
   const int b = blockIdx.x;
   int cs, ce;
   if (CLUSTER) {
@@ -173,10 +191,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     cs = tile * a.cpt + (a.cpt * sp) / a.ksplit;
     ce = tile * a.cpt + (a.cpt * (sp + 1)) / a.ksplit;
   } else {
-    block_range(a, b, cs, ce);
+    cs = range_start(a, b);
+    ce = range_start(a, b + 1);
   }
   const int t_first = cs / a.cpt;
-  const int nchunks = ce - cs;
+  const int nseg = CLUSTER ? 1 : (ce - 1) / a.cpt - t_first + 1;
+  const int nslots = a.x_by_row ? a.cpt : ce - cs;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kWarps * kStages; ++i) sgd::mbar_init(&bars[i], 1);
@@ -185,6 +205,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   }
   if (threadIdx.x < 4) reinterpret_cast<uint32_t*>(zrow)[threadIdx.x] = 0u;
   __syncthreads();
+  // Distributed shared memory is touched only after every block of the
+  // cluster has started: arrive now, wait before the first remote store.
+  if (CLUSTER) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   sgd::pdl_launch_dependents();
 
   uint64_t* my_bars = bars + warp * kStages;
@@ -203,7 +226,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       ++it_tile;
     }
     const int gA = group_of(a, 2 * row0);
-    const int x0 = tile * kTileCols + strip * 128;
+    const int x0 = tile * kTC + strip * 128;
     const int s = i % kStages;
     uint8_t* wdst = smem + kOffW + (warp * kStages + s) * kWBytes;
     uint8_t* szdst = smem + kOffSZ + (warp * kStages + s) * kSZBytes;
@@ -214,23 +237,33 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     if (HAS_Z) sgd::tma_load_2d(szdst + kSBytes, &tmZ, x0, gA, bar);
   };
 
-  // The activation depends on the previous kernel; request it first, so that
-  // its few bytes are not queued behind this block's weight stream.
+  // Weights that no earlier kernel writes stream before the dependency wait.
+  if (a.static_w && lane == 0) {
+    for (int i = 0; i < min(kStages, n_my); ++i) issue(i);
+  }
+  // The activation depends on the previous kernel; without the static-weight
+  // promise it is requested first, so that its few bytes are not queued
+  // behind this block's weight stream.
   sgd::pdl_wait();
+  auto slot_row = [&](int idx, int& k) {  // staging row idx -> k of its even element
+    const int sl = idx / kRows, r = idx - sl * kRows;
+    const int crow = a.x_by_row ? sl : (cs + sl) % a.cpt;
+    k = 2 * (crow * kRows + r);
+  };
   constexpr int kPrefetchRows = 2;
   float xe_pf[kPrefetchRows], xo_pf[kPrefetchRows];
 #pragma unroll
   for (int j = 0; j < kPrefetchRows; ++j) {
     const int idx = threadIdx.x + j * kThreads;
     xe_pf[j] = xo_pf[j] = 0.f;
-    if (idx < nchunks * kRows) {
-      const int cl = idx / kRows, r = idx - cl * kRows;
-      const int k = 2 * (((cs + cl) % a.cpt) * kRows + r);
+    if (idx < nslots * kRows) {
+      int k;
+      slot_row(idx, k);
       if (k < a.K) xe_pf[j] = load_act(a.A, a.a_dt, k);
       if (k + 1 < a.K) xo_pf[j] = load_act(a.A, a.a_dt, k + 1);
     }
   }
-  if (lane == 0) {
+  if (!a.static_w && lane == 0) {
     for (int i = 0; i < min(kStages, n_my); ++i) issue(i);
   }
 
@@ -238,11 +271,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   //      8 words [hi/lo][column select e][even, odd] with even entries x and odd
   //      entries x/16 (fp16, x split as hi + lo), and per-row sums used to undo
   //      the nibble carriers' constant: X = sum_k x_eff, P = 1024 * sum b.
-  for (int idx = threadIdx.x, j = 0; idx < nchunks * kRows; idx += kThreads, ++j) {
-    const int cl = idx / kRows, r = idx - cl * kRows;
-    const int c = cs + cl;
-    const int row = (c % a.cpt) * kRows + r;
-    const int k = 2 * row;
+  for (int idx = threadIdx.x, j = 0; idx < nslots * kRows; idx += kThreads, ++j) {
+    int k;
+    slot_row(idx, k);
     float xe, xo;
     if (j < kPrefetchRows) {
       xe = j == 0 ? xe_pf[0] : xe_pf[1];
@@ -270,21 +301,18 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     uint4* dst = reinterpret_cast<uint4*>(xst + (size_t)idx * kXRowBytes);
     dst[0] = w0;
     dst[1] = w1;
+    // per-row terms, summed over the 16 rows of each half chunk (16 lanes:
+    // the row count per pass is a multiple of 32, so whole warps take part)
     const float bhe = __half2float(he), bho = __half2float(ho), ble = __half2float(le), blo = __half2float(lo);
-    xrow[idx] = make_float4(bhe + 16.f * bho, 1024.f * (bhe + bho), ble + 16.f * blo, 1024.f * (ble + blo));
-  }
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < nchunks * 2; idx += kThreads) {
-    const float4* xr = xrow + idx * 16;
-    float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 v = make_float4(bhe + 16.f * bho, 1024.f * (bhe + bho), ble + 16.f * blo, 1024.f * (ble + blo));
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      s4.x += xr[r].x;
-      s4.y += xr[r].y;
-      s4.z += xr[r].z;
-      s4.w += xr[r].w;
+    for (int o = 1; o < 16; o <<= 1) {
+      v.x += __shfl_xor_sync(0xffffffffu, v.x, o);
+      v.y += __shfl_xor_sync(0xffffffffu, v.y, o);
+      v.z += __shfl_xor_sync(0xffffffffu, v.z, o);
+      v.w += __shfl_xor_sync(0xffffffffu, v.w, o);
     }
-    xhalf[idx] = s4;
+    if ((lane & 15) == 0) xhalf[idx >> 4] = v;
   }
   __syncthreads();
 
@@ -310,13 +338,28 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     xoff[st] = b_live ? (uint32_t)(row * kXRowBytes + b_off) : 0xFFFFFFFFu;
   }
 
-  float2 acc[8];    // current tile segment: pairs (4j, 4j+2) -> acc[2j], (4j+1, 4j+3) -> acc[2j+1]
-  float2 acc0[CLUSTER ? 1 : 8];  // first tile segment, when the warp's chunks cross a tile boundary
+  float2 acc[8];  // pairs (4j, 4j+2) -> acc[2j], (4j+1, 4j+3) -> acc[2j+1]
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = make_float2(0.f, 0.f);
+  // Sums the quad (variants x halves), stores this lane's share of segment
+  // seg into the warp's private slot and clears the accumulators.
+  // Column of pair entry: acc[2j+h].x -> 4j+h, .y -> 4j+h+2; lane t writes j = t.
+  auto flush = [&](int seg) {
 #pragma unroll
-  for (int i = 0; i < (CLUSTER ? 1 : 8); ++i) acc0[i] = make_float2(0.f, 0.f);
-  int cur_tile = t_first;
+    for (int q = 0; q < 8; ++q) {
+      acc[q].x += __shfl_xor_sync(0xffffffffu, acc[q].x, 1);
+      acc[q].y += __shfl_xor_sync(0xffffffffu, acc[q].y, 1);
+      acc[q].x += __shfl_xor_sync(0xffffffffu, acc[q].x, 2);
+      acc[q].y += __shfl_xor_sync(0xffffffffu, acc[q].y, 2);
+    }
+    const float2 e = t == 0 ? acc[0] : t == 1 ? acc[2] : t == 2 ? acc[4] : acc[6];
+    const float2 o = t == 0 ? acc[1] : t == 1 ? acc[3] : t == 2 ? acc[5] : acc[7];
+    float* r0 = red + (seg * kPhases + phase) * kTC + strip * 128 + g * 16 + 4 * t;
+    *reinterpret_cast<float4*>(r0) = make_float4(e.x, o.x, e.y, o.y);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc[q] = make_float2(0.f, 0.f);
+  };
+  int cur_seg = 0;
 
   int ok = 1;
   int tile = c_first / a.cpt, crow = c_first - tile * a.cpt;
@@ -328,15 +371,11 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         ++tile;
       }
     }
-    const int cl = c_first + i * kPhases - cs;
+    const int c = c_first + i * kPhases;
+    const int sl = a.x_by_row ? crow : c - cs;
     const int s = i % kStages;
-    if (!CLUSTER && tile != cur_tile) {  // warp-uniform, at most once
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        acc0[CLUSTER ? 0 : q] = acc[q];
-        acc[q] = make_float2(0.f, 0.f);
-      }
-      cur_tile = tile;
+    if (!CLUSTER) {
+      while (cur_seg < tile - t_first) flush(cur_seg++);  // warp-uniform
     }
     const bool waited = a.sleep_wait ? sgd::mbar_wait_sleep(&my_bars[s], (i / kStages) & 1, a.err)
                                      : sgd::mbar_wait(&my_bars[s], (i / kStages) & 1, a.err);
@@ -345,7 +384,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       break;
     }
     const uint8_t* wst = smem + kOffW + (warp * kStages + s) * kWBytes;
-    const uint8_t* xrows = xst + (size_t)cl * kRows * kXRowBytes;
+    const uint8_t* xrows = xst + (size_t)sl * kRows * kXRowBytes;
     float d[4][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j)
@@ -370,7 +409,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     const int srow = d_half ? (gB - gA) : 0;
     const uint4 s_lo = *reinterpret_cast<const uint4*>(szs + srow * 256 + g * 32);
     const uint4 s_hi = *reinterpret_cast<const uint4*>(szs + srow * 256 + g * 32 + 16);
-    const float4 xp = xhalf[cl * 2 + d_half];
+    const float4 xp = xhalf[sl * 2 + d_half];
     const float X = d_lo ? xp.z : xp.x;
     const float P = d_lo ? xp.w : xp.y;
     uint4 zv = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);  // biased zeros = 0
@@ -404,96 +443,58 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     if (lane == 0 && i + kStages < n_my) issue(i + kStages);
   }
   if (!ok) s_abort = 1;
-  // segment index of the registers: acc0 holds the first tile when the warp crossed into a second
-  const bool crossed = cur_tile != t_first;
-
-  // ---- sum the 4 lanes of a quad (variants x halves)
-#pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    acc[q].x += __shfl_xor_sync(0xffffffffu, acc[q].x, 1);
-    acc[q].y += __shfl_xor_sync(0xffffffffu, acc[q].y, 1);
-    acc[q].x += __shfl_xor_sync(0xffffffffu, acc[q].x, 2);
-    acc[q].y += __shfl_xor_sync(0xffffffffu, acc[q].y, 2);
-  }
-  if (!CLUSTER) {
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const int qq = CLUSTER ? 0 : q;
-      acc0[qq].x += __shfl_xor_sync(0xffffffffu, acc0[qq].x, 1);
-      acc0[qq].y += __shfl_xor_sync(0xffffffffu, acc0[qq].y, 1);
-      acc0[qq].x += __shfl_xor_sync(0xffffffffu, acc0[qq].x, 2);
-      acc0[qq].y += __shfl_xor_sync(0xffffffffu, acc0[qq].y, 2);
-    }
-  }
+  while (cur_seg < nseg) flush(cur_seg++);  // the last touched segment, then zeros for any not reached
   __syncthreads();
   if (!CLUSTER && s_abort) return;
 
-  // ---- block reduction over phases: red[seg][phase][512] aliases the weight stages.
-  // Column of pair entry: acc[2j+h].x -> 4j+h, .y -> 4j+h+2.  Lane t writes tile j = t.
-  float* red = reinterpret_cast<float*>(smem + kOffW);
-  {
-    const float2 a0 = t == 0 ? acc[0] : t == 1 ? acc[2] : t == 2 ? acc[4] : acc[6];
-    const float2 a1 = t == 0 ? acc[1] : t == 1 ? acc[3] : t == 2 ? acc[5] : acc[7];
-    const float2 b0 = CLUSTER ? make_float2(0.f, 0.f)
-                              : (t == 0 ? acc0[0] : t == 1 ? acc0[CLUSTER ? 0 : 2] : t == 2 ? acc0[CLUSTER ? 0 : 4]
-                                                                                           : acc0[CLUSTER ? 0 : 6]);
-    const float2 b1 = CLUSTER ? make_float2(0.f, 0.f)
-                              : (t == 0 ? acc0[CLUSTER ? 0 : 1] : t == 1 ? acc0[CLUSTER ? 0 : 3]
-                                         : t == 2 ? acc0[CLUSTER ? 0 : 5] : acc0[CLUSTER ? 0 : 7]);
-    // segment 0 = first tile of the block range, segment 1 = second
-    const float2 s0e = crossed ? b0 : a0, s0o = crossed ? b1 : a1;
-    const float2 s1e = crossed ? a0 : make_float2(0.f, 0.f), s1o = crossed ? a1 : make_float2(0.f, 0.f);
-    float* r0 = red + (0 * kPhases + phase) * kTileCols + strip * 128 + g * 16 + 4 * t;
-    float* r1 = red + (1 * kPhases + phase) * kTileCols + strip * 128 + g * 16 + 4 * t;
-    r0[0] = s0e.x; r0[2] = s0e.y; r0[1] = s0o.x; r0[3] = s0o.y;
-    r1[0] = s1e.x; r1[2] = s1e.y; r1[1] = s1o.x; r1[3] = s1o.y;
-  }
-  __syncthreads();
-
   if (CLUSTER) {
-    // this block's partial of its tile; rank 0 of the cluster sums the ranks in order
+    // Each rank's phase sum goes straight into rank 0's [rank][column]
+    // buffer; one cluster barrier publishes it, and rank 0 adds the ranks in
+    // order.  No block reads another's shared memory after the barrier.
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
-    float* tsum = red + 2 * kPhases * kTileCols;
-    for (int cc = threadIdx.x; cc < kTileCols; cc += kThreads) {
+    const int rank = (int)cluster.block_rank();
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+    float* csum0 = cluster.map_shared_rank(csum, 0) + rank * kTC;
+    for (int cc = threadIdx.x; cc < kTC; cc += kThreads) {
       float v = 0.f;
 #pragma unroll
-      for (int ph = 0; ph < kPhases; ++ph) v += red[ph * kTileCols + cc];
-      tsum[cc] = v;
+      for (int ph = 0; ph < kPhases; ++ph) v += red[ph * kTC + cc];
+      csum0[cc] = v;
     }
+    if (threadIdx.x == 0) cluster.map_shared_rank(s_aborts, 0)[rank] = s_abort;
     cluster.sync();
-    if (cluster.block_rank() == 0) {
+    if (rank == 0) {
       const int tile = blockIdx.y;
       int aborted = 0;
-      for (int r = 0; r < a.ksplit; ++r) aborted |= *cluster.map_shared_rank(&s_abort, r);
+      for (int r = 0; r < a.ksplit; ++r) aborted |= s_aborts[r];
       if (!aborted) {
-        for (int cc = threadIdx.x; cc < kTileCols; cc += kThreads) {
+        for (int cc = threadIdx.x; cc < kTC; cc += kThreads) {
           float v = 0.f;
-          for (int r = 0; r < a.ksplit; ++r) v += cluster.map_shared_rank(tsum, r)[cc];
-          const int col = tile * kTileCols + cc;
+          for (int r = 0; r < a.ksplit; ++r) v += csum[r * kTC + cc];
+          const int col = tile * kTC + cc;
           if (col < a.N) store_out(a.C, a.c_dt, col, finalize(a, col, v));
         }
       }
     }
-    cluster.sync();  // peers keep their shared memory alive until rank 0 has read it
     return;
   }
 
-  const int t_last = (ce - 1) / a.cpt;
-  for (int s2 = 0; s2 < 2 && t_first + s2 <= t_last; ++s2) {
+  for (int s2 = 0; s2 < nseg; ++s2) {
     const int tile = t_first + s2;
     const int tc0 = tile * a.cpt;
     const int b_lo = block_of_chunk(a, tc0), b_hi = block_of_chunk(a, tc0 + a.cpt - 1);
-    const bool shared_tile = b_lo != b_hi;
-    for (int cc = threadIdx.x; cc < kTileCols; cc += kThreads) {
+    const bool shared_tile = b_lo != b_hi;  // only a first or last segment can be shared
+    const int slot = s2 == 0 ? 0 : 1;
+    for (int cc = threadIdx.x; cc < kTC; cc += kThreads) {
       float v = 0.f;
 #pragma unroll
-      for (int ph = 0; ph < kPhases; ++ph) v += red[(s2 * kPhases + ph) * kTileCols + cc];
-      const int col = tile * kTileCols + cc;
+      for (int ph = 0; ph < kPhases; ++ph) v += red[(s2 * kPhases + ph) * kTC + cc];
+      const int col = tile * kTC + cc;
       if (!shared_tile) {
         if (col < a.N) store_out(a.C, a.c_dt, col, finalize(a, col, v));
       } else {
-        a.slots[((int64_t)b * 2 + s2) * kTileCols + cc] = v;
+        a.slots[((int64_t)b * 2 + slot) * kTC + cc] = v;
       }
     }
     if (!shared_tile) continue;
@@ -506,14 +507,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     __syncthreads();
     if (!s_last) continue;
     __threadfence();
-    for (int cc = threadIdx.x; cc < kTileCols; cc += kThreads) {
-      const int col = tile * kTileCols + cc;
+    for (int cc = threadIdx.x; cc < kTC; cc += kThreads) {
+      const int col = tile * kTC + cc;
       float v = 0.f;
       for (int bb = b_lo; bb <= b_hi; ++bb) {
-        int bcs, bce;
-        block_range(a, bb, bcs, bce);
-        const int sb = tile - bcs / a.cpt;
-        v += __ldcg(&a.slots[((int64_t)bb * 2 + sb) * kTileCols + cc]);
+        const int sb = (range_start(a, bb) / a.cpt == tile) ? 0 : 1;  // the tile is bb's first or last
+        v += __ldcg(&a.slots[((int64_t)bb * 2 + sb) * kTC + cc]);
       }
       if (col < a.N) store_out(a.C, a.c_dt, col, finalize(a, col, v));
     }
@@ -524,8 +523,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 struct MPlan {
   bool ok = false;
   int variant = 0;
-  int cluster = 0, ksplit = 1;
-  int n_tiles = 0, cpt = 0, nblocks = 0, flat = 0, max_chunks = 0, total = 0;
+  int cluster = 0, ksplit = 1, strips = kStreamKStrips;
+  int n_tiles = 0, cpt = 0, nblocks = 0, total = 0, q = 0, r = 0;
+  int x_slots = 0, x_by_row = 0, max_segs = 1;
   size_t smem = 0, ws_bytes = 0, tickets_bytes = 0;
 };
 
@@ -549,7 +549,7 @@ int max_active_clusters(int k) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  auto kfn = w4_gemv_mma_kernel<true, 16, 2, true>;
+  auto kfn = w4_gemv_mma_kernel<true, 16, 2, true, 4>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024) != cudaSuccess ||
       cudaOccupancyMaxActiveClusters(&n, kfn, &cfg) != cudaSuccess) {
     cudaGetLastError();
@@ -565,42 +565,62 @@ MPlan make_mplan(const SgMatMulParams* p, int sms) {
   if (p->M != 1 || p->K <= 0 || (p->N % 16) != 0 || (gs % 32) != 0) return pl;
   if (!sg::aligned16(p->B) || !sg::aligned16(p->scales_B) || (p->zeros_B && !sg::aligned16(p->zeros_B))) return pl;
   const int KP = (p->K + 1) / 2;
-  pl.n_tiles = (p->N + kTileCols - 1) / kTileCols;
   pl.cpt = (KP + kRows - 1) / kRows;
-  const long long total = (long long)pl.n_tiles * pl.cpt;
-  if (total >= (1ll << 30)) return pl;
-  pl.total = (int)total;
-  // Cluster mode when a tile-aligned split with <= 8 blocks per tile runs in
-  // one wave (clusters must fit inside a GPC) and fills most SMs.
-  int ks = 0;
-  if (g_cluster_mode.load()) {
-    for (int k = std::min({8, pl.cpt, pl.n_tiles > 0 ? sms / pl.n_tiles : 0}); k >= 2; --k) {
-      if (pl.n_tiles * k < (sms * 3) / 4) break;
-      if (max_active_clusters(k) >= pl.n_tiles) {
-        ks = k;
-        break;
+  // Cluster split: tiles of 4, 2 or 1 strips (512 / 256 / 128 columns), each
+  // split over k <= 8 blocks that reduce through distributed shared memory
+  // (no global scratch).  The shape that keeps the most SMs busy in one wave
+  // (clusters must fit inside a GPC) wins; ties go to wider tiles.  Mode 1
+  // (default) falls back to the stream-K split when no cluster shape fills at
+  // least half the SMs, mode 2 always takes a cluster shape that fits, mode 0
+  // never does.
+  const int mode = g_cluster_mode.load();
+  int best_blocks = 0, best_strips = 0, best_k = 0;
+  if (mode != 0) {
+    for (int strips : {4, 2, 1}) {
+      const int n_tiles = (p->N + strips * 128 - 1) / (strips * 128);
+      if (n_tiles > sms) continue;
+      for (int k = std::min({8, pl.cpt, sms / n_tiles}); k >= 1; --k) {
+        if (max_active_clusters(k) >= n_tiles) {
+          if (n_tiles * k > best_blocks) {
+            best_blocks = n_tiles * k;
+            best_strips = strips;
+            best_k = k;
+          }
+          break;
+        }
       }
     }
-  }
-  if (ks >= 2) {
-    pl.cluster = 1;
-    pl.ksplit = ks;
-    pl.flat = 0;
-    pl.nblocks = pl.n_tiles * ks;
-    pl.max_chunks = (pl.cpt + ks - 1) / ks;
-  } else if (pl.n_tiles <= sms) {
-    pl.flat = 1;
-    pl.nblocks = (int)std::min<long long>(sms, total);
-    pl.max_chunks = (int)((total + pl.nblocks - 1) / pl.nblocks);
-  } else {
-    pl.flat = 0;
-    pl.nblocks = pl.n_tiles;
-    pl.max_chunks = pl.cpt;
+    if (mode == 1 && 2 * best_blocks < sms) best_blocks = 0;
   }
   pl.variant = std::min(3, std::max(0, g_variant.load()));
+  if (best_blocks > 0) {
+    pl.cluster = 1;
+    pl.strips = best_strips;
+    pl.ksplit = best_k;
+    if (best_strips != 4) pl.variant = 0;  // the narrow tiles come in the default launch shape only
+    pl.n_tiles = (p->N + best_strips * 128 - 1) / (best_strips * 128);
+    pl.total = pl.n_tiles * pl.cpt;
+    pl.nblocks = pl.n_tiles * best_k;
+    pl.x_slots = (pl.cpt + best_k - 1) / best_k;
+    pl.x_by_row = 0;
+    pl.max_segs = 1;
+  } else {
+    pl.strips = kStreamKStrips;
+    pl.n_tiles = (p->N + kStreamKCols - 1) / kStreamKCols;
+    const long long total = (long long)pl.n_tiles * pl.cpt;
+    if (total >= (1ll << 30)) return pl;
+    pl.total = (int)total;
+    pl.nblocks = (int)std::min<long long>(sms, total);
+    pl.q = pl.total / pl.nblocks;
+    pl.r = pl.total % pl.nblocks;
+    const int longest = pl.q + (pl.r > 0 ? 1 : 0);
+    pl.x_by_row = longest > pl.cpt ? 1 : 0;
+    pl.x_slots = pl.x_by_row ? pl.cpt : longest;
+    pl.max_segs = (longest - 1 + pl.cpt - 1) / pl.cpt + 1;
+  }
   const int vw = kVariantWarps[pl.variant], vs = kVariantStages[pl.variant];
-  pl.smem = 1024 + off_x(vw, vs) + (size_t)pl.max_chunks * (kRows * kXRowBytes + kRows * 16 + 2 * 16) + 16 +
-            vw * vs * 8;
+  pl.smem = 1024 + off_x(vw, vs) +
+            tail_bytes(vw, vs, pl.strips, pl.x_slots, pl.max_segs, pl.cluster ? pl.ksplit : 0);
   // opt-in limit per block (227 KB on sm_100) minus this kernel's static shared memory
   if (pl.smem > 227 * 1024 - kStaticSmemReserve) return pl;
   if (pl.cluster) {
@@ -608,7 +628,7 @@ MPlan make_mplan(const SgMatMulParams* p, int sms) {
     pl.ws_bytes = 0;  // partials stay in distributed shared memory
   } else {
     pl.tickets_bytes = sg::ticket_bytes(pl.n_tiles);
-    pl.ws_bytes = pl.tickets_bytes + (size_t)pl.nblocks * 2 * kTileCols * sizeof(float);
+    pl.ws_bytes = pl.tickets_bytes + (size_t)pl.nblocks * 2 * kStreamKCols * sizeof(float);
   }
   pl.ok = true;
   return pl;
@@ -676,30 +696,41 @@ SgStatus w4_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, void
   a.n_tiles = pl.n_tiles;
   a.cpt = pl.cpt;
   a.nblocks = pl.nblocks;
-  a.flat = pl.flat;
   a.total = pl.total;
-  a.max_chunks = pl.max_chunks;
+  a.q = pl.q;
+  a.r = pl.r;
   a.ksplit = pl.ksplit;
+  a.x_slots = pl.x_slots;
+  a.x_by_row = pl.x_by_row;
+  a.max_segs = pl.max_segs;
   a.gs_shift = ((gs & (gs - 1)) == 0) ? __builtin_ctz((unsigned)gs) : -1;
   a.sleep_wait = g_sleep.load() ? 1 : 0;
+  a.static_w = (p->flags & SG_MM_STATIC_WEIGHTS) ? 1 : 0;
   a.tickets = static_cast<unsigned*>(ws);
   a.slots = reinterpret_cast<float*>(static_cast<char*>(ws) + pl.tickets_bytes);
   a.err = err_word;
 
   using KFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, MArgs);
-#define SG_W4MMA_KFNS(Z, C)                                                                              \
-  {w4_gemv_mma_kernel<Z, 16, 2, C>, w4_gemv_mma_kernel<Z, 20, 2, C>, w4_gemv_mma_kernel<Z, 12, 3, C>, \
-   w4_gemv_mma_kernel<Z, 8, 5, C>}
-  static const KFn kfns[2][2][4] = {{SG_W4MMA_KFNS(false, false), SG_W4MMA_KFNS(false, true)},
-                                    {SG_W4MMA_KFNS(true, false), SG_W4MMA_KFNS(true, true)}};
+  // [zeros][variant]: stream-K (512-column tiles), cluster with 512-column
+  // tiles; [zeros][strips 1 / 2]: cluster with narrow tiles, default shape
+#define SG_W4MMA_KFNS(Z, C)                                                                                   \
+  {w4_gemv_mma_kernel<Z, 16, 2, C, 4>, w4_gemv_mma_kernel<Z, 20, 2, C, 4>, w4_gemv_mma_kernel<Z, 12, 3, C, 4>, \
+   w4_gemv_mma_kernel<Z, 8, 5, C, 4>}
+  static const KFn kstream[2][4] = {SG_W4MMA_KFNS(false, false), SG_W4MMA_KFNS(true, false)};
+  static const KFn kcluster[2][4] = {SG_W4MMA_KFNS(false, true), SG_W4MMA_KFNS(true, true)};
 #undef SG_W4MMA_KFNS
-  const int zi = a.has_zeros ? 1 : 0, ci = pl.cluster ? 1 : 0;
-  const KFn kfn = kfns[zi][ci][pl.variant];
+  static const KFn knarrow[2][2] = {{w4_gemv_mma_kernel<false, 16, 2, true, 1>, w4_gemv_mma_kernel<false, 16, 2, true, 2>},
+                                    {w4_gemv_mma_kernel<true, 16, 2, true, 1>, w4_gemv_mma_kernel<true, 16, 2, true, 2>}};
+  const int zi = a.has_zeros ? 1 : 0;
+  const int ki = !pl.cluster ? pl.variant : pl.strips == 4 ? 4 + pl.variant : 8 + (pl.strips == 2 ? 1 : 0);
+  const KFn kfn = !pl.cluster ? kstream[zi][pl.variant]
+                  : pl.strips == 4 ? kcluster[zi][pl.variant]
+                                   : knarrow[zi][pl.strips == 2 ? 1 : 0];
   static std::mutex mu;
-  static size_t attr_smem[2][2][4] = {};
+  static size_t attr_smem[2][10] = {};
   {
     std::lock_guard<std::mutex> lk(mu);
-    size_t& done = attr_smem[zi][ci][pl.variant];
+    size_t& done = attr_smem[zi][ki];
     if (done < pl.smem) {
       cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
       if (e != cudaSuccess) {

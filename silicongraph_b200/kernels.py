@@ -48,8 +48,9 @@ def _stream(stream) -> int | None:
 
 def matmul_params(A, B, C, *, M: int, K: int, N: int, scales=None, zeros=None, bias=None,
                   group_size: int = 0, scale_A: float = 1.0, lda: int = 0, ldc: int = 0,
-                  workspace: torch.Tensor | None = None) -> SgMatMulParams:
+                  workspace: torch.Tensor | None = None, flags: int = 0) -> SgMatMulParams:
     p = SgMatMulParams()
+    p.flags = flags
     p.A = _ptr(A)
     p.B = _ptr(B)
     p.bias = _ptr(bias)
@@ -71,13 +72,13 @@ def matmul_params(A, B, C, *, M: int, K: int, N: int, scales=None, zeros=None, b
 def matmul_int4_grouped(A: torch.Tensor, B: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor | None,
                         K: int, N: int, group_size: int, *, out_dtype=torch.float16, bias=None,
                         scale_A: float = 1.0, C: torch.Tensor | None = None, stream=None,
-                        workspace=None) -> torch.Tensor:
+                        workspace=None, flags: int = 0) -> torch.Tensor:
     """C[M, N] = A[M, K] @ dequant(B) -- the reference INT4 layout (matmul_neon.h:113-143)."""
     M = A.shape[0] if A.dim() == 2 else 1
     if C is None:
         C = torch.empty((M, N), dtype=out_dtype, device=A.device)
     p = matmul_params(A, B, C, M=M, K=K, N=N, scales=scales, zeros=zeros, bias=bias,
-                      group_size=group_size, scale_A=scale_A, workspace=workspace)
+                      group_size=group_size, scale_A=scale_A, workspace=workspace, flags=flags)
     check(_lib.load().sg_matmul_int4_grouped(ctypes.byref(p), _stream(stream)))
     return C
 

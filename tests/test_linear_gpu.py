@@ -193,16 +193,20 @@ def test_int4_caller_workspace(sg, oracle_mod):
     B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=3)
     x = t(np.random.default_rng(4).standard_normal((1, K)).astype(np.float32))
     args = (x, t(B), t(S), t(Z), K, N, gs)
-    need = sg.matmul_int4_grouped_workspace_size(*args, out_dtype=torch.float32)
-    assert need > 0
-    ws = torch.zeros(need, dtype=torch.uint8, device=DEV)
-    a = sg.matmul_int4_grouped(*args, out_dtype=torch.float32, workspace=ws)
-    b = sg.matmul_int4_grouped(*args, out_dtype=torch.float32)
-    assert torch.equal(a, b)
-    a2 = sg.matmul_int4_grouped(*args, out_dtype=torch.float32, workspace=ws)  # tickets were reset
-    assert torch.equal(a, a2)
-    with pytest.raises(SgError):
-        sg.matmul_int4_grouped(*args, out_dtype=torch.float32, workspace=ws[: need // 2])
+    sg.set_tuning("w4_gemv_mma.cluster", 0)  # the stream-K split, whose partials need scratch
+    try:
+        need = sg.matmul_int4_grouped_workspace_size(*args, out_dtype=torch.float32)
+        assert need > 0
+        ws = torch.zeros(need, dtype=torch.uint8, device=DEV)
+        a = sg.matmul_int4_grouped(*args, out_dtype=torch.float32, workspace=ws)
+        b = sg.matmul_int4_grouped(*args, out_dtype=torch.float32)
+        assert torch.equal(a, b)
+        a2 = sg.matmul_int4_grouped(*args, out_dtype=torch.float32, workspace=ws)  # tickets were reset
+        assert torch.equal(a, a2)
+        with pytest.raises(SgError):
+            sg.matmul_int4_grouped(*args, out_dtype=torch.float32, workspace=ws[: need // 2])
+    finally:
+        sg.set_tuning("w4_gemv_mma.cluster", 1)
 
 
 @pytest.mark.parametrize("gpw", [1, 2, 4, 8])
@@ -313,19 +317,33 @@ def test_fp16_gemv_vs_oracle(sg, oracle_mod, M, K, N):
     close(C.cpu().numpy(), want)
 
 
-@pytest.mark.parametrize("cluster", [1, 0])
-@pytest.mark.parametrize("K,N,gs", [(4096, 14336, 32), (2048, 8192, 64), (2048, 128256 // 8, 32)])
-def test_int4_cluster_and_flat_splits(sg, oracle_mod, cluster, K, N, gs):
+@pytest.mark.parametrize("cluster", [2, 1, 0])
+@pytest.mark.parametrize("K,N,gs", [
+    (4096, 14336, 32),        # benchmark shape
+    (2048, 8192, 64),
+    (2048, 128256 // 8, 32),
+    (2048, 3072, 32),         # decoder q|k|v projection: 6 tiles shared by many blocks
+    (8192, 2048, 32),         # decoder down projection
+    (128, 512 * 200, 32),     # ranges longer than K: activation staged by row, 2 tiles per block
+    (64, 512 * 300, 64),      # one chunk per tile: ranges over 3 tiles
+])
+def test_int4_cluster_and_stream_k_splits(sg, oracle_mod, cluster, K, N, gs):
     """Tile-aligned cluster split (partials reduced in distributed shared memory)
-    and flat split (partials reduced through scratch) give the oracle's result."""
+    and the stream-K split (partials of shared tiles reduced through scratch)
+    give the oracle's result, repeatably; the static-weight launch (weights
+    requested before the dependency wait) gives the same bits."""
+    from silicongraph_b200 import _lib
     B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=N + 1)
     x = np.random.default_rng(K + 1).standard_normal((1, K)).astype(np.float32)
     want = oracle_mod.matmul_int4_grouped(x, B, S, Z, K, N, gs, c_dt=oracle_mod.DT_F32)
     try:
         sg.set_tuning("w4_gemv_mma.cluster", cluster)
-        C = sg.matmul_int4_grouped(t(x), t(B), t(S), t(Z), K, N, gs, out_dtype=torch.float32)
-        C2 = sg.matmul_int4_grouped(t(x), t(B), t(S), t(Z), K, N, gs, out_dtype=torch.float32)
+        args = (t(x), t(B), t(S), t(Z), K, N, gs)
+        C = sg.matmul_int4_grouped(*args, out_dtype=torch.float32)
+        C2 = sg.matmul_int4_grouped(*args, out_dtype=torch.float32)
+        C3 = sg.matmul_int4_grouped(*args, out_dtype=torch.float32, flags=_lib.SG_MM_STATIC_WEIGHTS)
     finally:
         sg.set_tuning("w4_gemv_mma.cluster", 1)
     close(C.cpu().numpy(), want)
     assert torch.equal(C, C2)
+    assert torch.equal(C, C3)

@@ -54,16 +54,17 @@ def test_noalloc_matches_allocating_entry_point_twice(sg, oracle_mod, K, N, gs, 
 
 
 def test_noalloc_rejects_scratch_beyond_its_maximum(sg, oracle_mod):
-    """A lm_head-like shape with more 512-column tiles than SMs needs more than
-    2 MiB of split scratch: refused with a message, output untouched."""
+    """A prefill-sized call with fp32 activations (512 x 4096: a 4 MiB fp16
+    copy for the tensor-core GEMM) needs more than the 2 MiB array: refused
+    with a message, output untouched."""
     from silicongraph_b200 import _lib
     lib = _lib.load()
-    K, N, gs = 64, 1 << 19, 32
+    M, K, N, gs = 512, 4096, 512, 32
     B, S, Z = _problem(oracle_mod, K, N, gs, seed=5)
-    x = torch.randn(1, K, device="cuda")
+    x = torch.randn(M, K, device="cuda")
     from silicongraph_b200 import kernels
-    y = torch.full((1, N), 7.0, dtype=torch.float32, device="cuda")
-    p = kernels.matmul_params(x, B, y, M=1, K=K, N=N, scales=S, zeros=Z, group_size=gs)
+    y = torch.full((M, N), 7.0, dtype=torch.float32, device="cuda")
+    p = kernels.matmul_params(x, B, y, M=M, K=K, N=N, scales=S, zeros=Z, group_size=gs)
     need = lib.sg_matmul_int4_grouped_workspace_size(ctypes.byref(p))
     assert need > (2 << 20)
     st = lib.sg_matmul_int4_grouped_noalloc(ctypes.byref(p), torch.cuda.current_stream().cuda_stream)
