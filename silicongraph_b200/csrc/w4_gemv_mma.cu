@@ -4,39 +4,35 @@
 // group_size % 32 == 0.
 //
 // Memory side (HBM-bound):
-//   * Work unit = a chunk of 32 k-pair rows (64 k) x one 512-column tile.
-//     Chunks are split evenly over one block per SM.  A block has 16 warps =
-//     4 column strips (128 columns each) x 4 phases; warp (strip, phase)
-//     takes every 4th chunk of the block's range for its strip.
+//   * Work unit = a chunk of 32 k-pair rows (64 k) x one tile of 1, 2 or 4
+//     128-column strips.  A block has 16 warps = strips x phases; warp
+//     (strip, phase) takes every phases-th chunk of the block's range for its
+//     strip.
 //   * Each warp streams its own 2-stage ring by TMA: a 128-byte x 32-row box
 //     of packed weights (128-byte swizzle), the chunk's two scale rows and two
-//     zero-point rows.  The first stages are issued before griddepcontrol.wait,
-//     so with programmatic dependent launch the next GEMV's weights start
-//     streaming while the previous kernel drains.
+//     zero-point rows.
 // Math side (few instructions per weight):
-//   * A 32-bit word (4 columns x one k pair) becomes four fp16x2 registers
-//     with one shift and four LOP3 (0x6400 magic): 1024 + q for even k and
-//     1024 + 16 q for odd k; pairs hold columns (c0,c2) / (c1,c3) of one k.
-//     Odd-k activations are pre-divided by 16 (exact), and the constant part
-//     (1024 * sum of the B entries) is subtracted after the MMA.
-//   * mma.sync m16n8k16 (fp16 x fp16 -> fp32) reduces over k: A = those
-//     registers (16 column pairs x 16 logical k), B = the activation.  Logical
-//     k 2t+e carries column e of a pair, so B holds x in column n = 2v + e and
-//     zeros elsewhere; the 8 B columns carry 4 "variants" v: the two halves of
-//     the chunk (rows 0-15 and 16-31, each inside one quantisation group) times
-//     x split as fp16 hi + lo (x - hi), which keeps fp32 activation accuracy.
-//     Every lane of the D fragment then holds useful partial sums.
-//   * Per chunk half, variant and column (packed fp32x2 FMAs):
-//     acc += scale * (D - 1024 * sum b - (8 + zero) * sum_k x_k); halves and
-//     variants are summed with two warp shuffles at the end.
+//   * The activation is staged once per block as 16-bit fixed point with one
+//     power-of-two scale per 32 k (x = 2^(E-13) x_q, E the exponent of the
+//     largest |x| there, so |x_q| <= 2^14 and the rounding error is below
+//     2^-15 of that largest value), split as x_q = 256 hi + lo, signed bytes.
+//   * A 32-bit word (4 columns x one k pair, low nibble = even k) gives the
+//     unsigned bytes of both k with one shift and two AND masks.  mma.sync
+//     m16n8k32 (u8 x s8 -> exact int32) reduces over k: A rows are words of
+//     4 columns, A k-slots their columns at 4 k-pair rows x even/odd k, and
+//     B column 2e + v carries hi (v = 0) or lo (v = 1) of x at column slot e
+//     and zero elsewhere, so every D entry is one column's hi or lo partial
+//     dot product and every lane owns 4 columns outright.
+//   * Per 32-k half and column (exact integers until the last step):
+//     acc += scale * 2^(E-13) * (256 D_hi + D_lo - (8 + zero) * sum x_q).
 //   * Rows are assigned to the 4 lanes of a quad so that their (row mod 8)
 //     values differ by 2: with the 128-byte swizzle the 8 lanes of a quarter
 //     warp hit 8 distinct 16-byte bank groups (no bank conflicts).
-//   * Scheduling: either clusters of ksplit blocks per 512-column tile that
-//     reduce through distributed shared memory, or a balanced stream-K split
-//     of all (tile, chunk) units over one block per SM.  In the latter a
+//   * Scheduling: either clusters of ksplit blocks per tile that reduce
+//     through distributed shared memory, or a balanced stream-K split of all
+//     (512-column tile, chunk) units over one block per SM.  In the latter a
 //     block's range touches one or more tiles ("segments"); every warp flushes
-//     its quad-reduced sums per segment into a private shared-memory slot, the
+//     its column sums per segment into a private shared-memory slot, the
 //     block sums its phases, owns interior tiles outright, and hands the
 //     partial of a tile shared with its neighbours to global scratch, where
 //     the last block to arrive (atomic ticket) adds the partials in block
@@ -62,7 +58,6 @@ constexpr int kWBytes = 128 * kRows;         // 4096
 constexpr int kSBytes = 128 * 2 * 2;         // 2 scale rows x 128 fp16
 constexpr int kZBytes = 128 * 2;             // 2 zero rows x 128 int8
 constexpr int kSZBytes = kSBytes + kZBytes;  // 768
-constexpr int kXRowBytes = 32;               // 8 B-fragment words per k-pair row
 constexpr int kStaticSmemReserve = 2048;
 // Launch shapes: warps per block (4 column strips x warps/4 phases) and TMA
 // stages per warp.  Variant 0 is the default; the others are selectable with
@@ -71,14 +66,14 @@ constexpr int kVariantWarps[4] = {16, 20, 12, 8};
 constexpr int kVariantStages[4] = {2, 2, 3, 5};
 constexpr int off_sz(int warps, int stages) { return warps * stages * kWBytes; }
 constexpr int off_x(int warps, int stages) { return off_sz(warps, stages) + warps * stages * kSZBytes; }
-// Dynamic shared memory after the stages (bytes): B fragments of the staged
-// activation rows, per-half sums, a zero row, the stage barriers, the
+// Dynamic shared memory after the stages (bytes): the staged activation (one
+// word per k-pair row, scale and sum per half chunk), the stage barriers, the
 // cluster's [rank][column] partials (rank 0's copy is the one used), then the
 // per-segment, per-phase partial sums.
-constexpr size_t kXSlotBytes = (size_t)kRows * kXRowBytes + 2 * 16;
+constexpr size_t kXSlotBytes = (size_t)kRows * 4 + 2 * 8;
 inline size_t tail_bytes(int warps, int stages, int strips, int x_slots, int max_segs, int ksplit) {
   const size_t cols = (size_t)strips * 128;
-  return (size_t)x_slots * kXSlotBytes + 16 + (size_t)warps * stages * 8 + (size_t)ksplit * cols * 4 +
+  return (size_t)x_slots * kXSlotBytes + (size_t)warps * stages * 8 + (size_t)ksplit * cols * 4 +
          (size_t)max_segs * (warps / strips) * cols * 4;
 }
 std::atomic<int> g_variant{0};
@@ -95,7 +90,7 @@ struct MArgs {
   int has_zeros;
   int n_tiles, cpt, nblocks, total;
   int q, r;            // stream-K: block b owns chunks [b q + min(b, r), ...); the first r own q + 1
-  int ksplit;          // cluster mode: blocks (cluster ranks) per 512-column tile
+  int ksplit;          // cluster mode: blocks (cluster ranks) per tile
   int x_slots;         // activation staging capacity in 32-row chunks
   int x_by_row;        // slot of chunk c: c % cpt (range longer than K) or c - range start
   int max_segs;        // tiles one block's range can touch
@@ -137,25 +132,6 @@ __device__ __forceinline__ float finalize(const MArgs& a, int col, float v) {
   return v;
 }
 
-__device__ __forceinline__ uint32_t pack_h2(__half lo, __half hi) {
-  return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
-}
-
-
-// Raw nibble carriers as fp16 pairs (no offset removal): for a word of 4
-// columns x one k pair, lo = 1024 + q (even k), hi = 1024 + 16 q (odd k);
-// pairs (c0,c2) and (c1,c3).  The constant 1024 (resp. 1024 / 16 with the
-// odd activations pre-divided by 16) is removed after the MMA through a
-// per-chunk correction, so each word costs one shift and four LOP3.
-__device__ __forceinline__ void nibbles_h(uint32_t w, uint32_t& e02, uint32_t& o02, uint32_t& e13, uint32_t& o13) {
-  const uint32_t MAGIC = 0x64006400u;  // fp16 1024 in both halves
-  const uint32_t w8 = w >> 8;
-  e02 = sgd::lop3_and_or(w, 0x000F000Fu, MAGIC);
-  o02 = sgd::lop3_and_or(w, 0x00F000F0u, MAGIC);
-  e13 = sgd::lop3_and_or(w8, 0x000F000Fu, MAGIC);
-  o13 = sgd::lop3_and_or(w8, 0x00F000F0u, MAGIC);
-}
-
 __device__ __forceinline__ int group_of(const MArgs& a, int k) { return a.gs_shift >= 0 ? (k >> a.gs_shift) : k / a.gs; }
 
 // CLUSTER: grid (ksplit, n_tiles), clusters of ksplit blocks own one tile and
@@ -172,10 +148,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   constexpr int kOffW = 0, kOffSZ = off_sz(WARPS, STAGES), kOffX = off_x(WARPS, STAGES);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* xst = smem + kOffX;                                                  // [slot][32 rows][32 B]
-  float4* xhalf = reinterpret_cast<float4*>(xst + a.x_slots * kRows * kXRowBytes);  // [slot][2]: Xhi, Phi, Xlo, Plo
-  uint8_t* zrow = reinterpret_cast<uint8_t*>(xhalf + a.x_slots * 2);           // 16 zero bytes
-  uint64_t* bars = reinterpret_cast<uint64_t*>(zrow + 16);
+  uint32_t* xst = reinterpret_cast<uint32_t*>(smem + kOffX);         // [slot][32 rows]: x_q bytes
+  int2* xgrp = reinterpret_cast<int2*>(xst + a.x_slots * kRows);       // [slot][half]: scale bits, sum x_q
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xgrp + a.x_slots * 2);
   float* csum = reinterpret_cast<float*>(bars + kWarps * kStages);  // cluster: [rank][kTC]
   float* red = csum + (CLUSTER ? a.ksplit * kTC : 0);                // [seg][phase][kTC]
   __shared__ int s_last;
@@ -203,7 +178,6 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     sgd::fence_mbar_init();
     s_abort = 0;
   }
-  if (threadIdx.x < 4) reinterpret_cast<uint32_t*>(zrow)[threadIdx.x] = 0u;
   __syncthreads();
   // Distributed shared memory is touched only after every block of the
   // cluster has started: arrive now, wait before the first remote store.
@@ -267,10 +241,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     for (int i = 0; i < min(kStages, n_my); ++i) issue(i);
   }
 
-  // ---- stage the activation as ready-made B fragments.  Per k-pair row:
-  //      8 words [hi/lo][column select e][even, odd] with even entries x and odd
-  //      entries x/16 (fp16, x split as hi + lo), and per-row sums used to undo
-  //      the nibble carriers' constant: X = sum_k x_eff, P = 1024 * sum b.
+  // ---- stage the activation as 16-bit fixed point, one power-of-two scale
+  //      per half chunk (32 k): x = 2^(E-13) x_q with E the exponent of the
+  //      half's largest |x|, so |x_q| <= 2^14, written as x_q = 256 hi + lo
+  //      with hi, lo signed bytes.  Per k-pair row one word [hi_even, hi_odd,
+  //      lo_even, lo_odd]; per half the scale and sum_k x_q.  A half is 16
+  //      rows = 16 lanes (rows per pass are a multiple of 32: whole warps).
   for (int idx = threadIdx.x, j = 0; idx < nslots * kRows; idx += kThreads, ++j) {
     int k;
     slot_row(idx, k);
@@ -282,82 +258,52 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       xe = (k < a.K) ? load_act(a.A, a.a_dt, k) : 0.f;
       xo = (k + 1 < a.K) ? load_act(a.A, a.a_dt, k + 1) : 0.f;
     }
-    const __half he = __float2half_rn(xe);
-    const __half hoF = __float2half_rn(xo);
-    const __half le = __float2half_rn(xe - __half2float(he));
-    const __half loF = __float2half_rn(xo - __half2float(hoF));
-    const __half ho = __float2half_rn(__half2float(hoF) * 0.0625f);  // exact: power-of-two scaling
-    const __half lo = __float2half_rn(__half2float(loF) * 0.0625f);
-    const __half z = __ushort_as_half(0);
-    uint4 w0, w1;
-    w0.x = pack_h2(he, z);  // hi, e=0 (even, odd)
-    w0.y = pack_h2(ho, z);
-    w0.z = pack_h2(z, he);  // hi, e=1
-    w0.w = pack_h2(z, ho);
-    w1.x = pack_h2(le, z);  // lo, e=0
-    w1.y = pack_h2(lo, z);
-    w1.z = pack_h2(z, le);  // lo, e=1
-    w1.w = pack_h2(z, lo);
-    uint4* dst = reinterpret_cast<uint4*>(xst + (size_t)idx * kXRowBytes);
-    dst[0] = w0;
-    dst[1] = w1;
-    // per-row terms, summed over the 16 rows of each half chunk (16 lanes:
-    // the row count per pass is a multiple of 32, so whole warps take part)
-    const float bhe = __half2float(he), bho = __half2float(ho), ble = __half2float(le), blo = __half2float(lo);
-    float4 v = make_float4(bhe + 16.f * bho, 1024.f * (bhe + bho), ble + 16.f * blo, 1024.f * (ble + blo));
+    float m = fmaxf(fabsf(xe), fabsf(xo));
 #pragma unroll
-    for (int o = 1; o < 16; o <<= 1) {
-      v.x += __shfl_xor_sync(0xffffffffu, v.x, o);
-      v.y += __shfl_xor_sync(0xffffffffu, v.y, o);
-      v.z += __shfl_xor_sync(0xffffffffu, v.z, o);
-      v.w += __shfl_xor_sync(0xffffffffu, v.w, o);
-    }
-    if ((lane & 15) == 0) xhalf[idx >> 4] = v;
+    for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const int E = max((__float_as_int(m) >> 23) - 127, -100);  // m >= 0; tiny halves clamp
+    const float inv = __int_as_float((127 + 13 - E) << 23);      // 2^(13 - E), exact scaling
+    const float sxv = __int_as_float((127 - 13 + E) << 23);      // 2^(E - 13)
+    const int qe = __float2int_rn(xe * inv), qo = __float2int_rn(xo * inv);
+    const int le = ((qe + 128) & 255) - 128, lo = ((qo + 128) & 255) - 128;
+    const int he = (qe - le) >> 8, ho = (qo - lo) >> 8;
+    xst[idx] = (uint32_t)(he & 255) | ((uint32_t)(ho & 255) << 8) | ((uint32_t)(le & 255) << 16) |
+               ((uint32_t)(lo & 255) << 24);
+    int sq = qe + qo;
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    if ((lane & 15) == 0) xgrp[idx >> 4] = make_int2(__float_as_int(sxv), sq);
   }
   __syncthreads();
 
+  // ---- lane roles in mma.sync m16n8k32 (A u8 row-major, B s8 col-major):
+  //      A row m = g (m + 8) is the word of columns 16g + 8jm + 0..3 (+ 4..7)
+  //      of k-pair row r_t, A k-slot 4t + e (16 + 4t + e) its column e at the
+  //      even (odd) k; B column n = 2e + v holds variant v (hi / lo) of x at
+  //      k-slot 4t + e, zero elsewhere.  D[m][2t] / D[m][2t + 1] are then the
+  //      hi / lo partial dot products of column t of the word: every lane
+  //      owns columns 16g + t + 4i, i = 0..3, with no cross-lane reduction.
   const int g = lane >> 2, t = lane & 3;
-  // As a B-operand provider this lane serves variant bv = g / 2 (0 A-hi, 1 A-lo,
-  // 2 B-hi, 3 B-lo) with column select be = g % 2, for the row of quad lane t.
-  const int bv = g >> 1, be = g & 1;
-  const bool b_live = ((bv >= 2) == (t >= 2));
-  const int b_off = ((bv & 1) * 2 + be) * 8;
-  // As a D-fragment holder this lane owns variant t: chunk half t / 2, hi/lo t % 2.
-  const int d_half = t >> 1, d_lo = t & 1;
-  // Per-step shared-memory offsets of this lane (constant over chunks): the
-  // weight row it provides (swizzled 16-byte group g) and its B fragment.
-  uint32_t woff[8], xoff[8];
-#pragma unroll
-  for (int st = 0; st < 8; ++st) {
-    const int h8 = st >> 2;
-    const int p = (st & 1) + ((st & 2) << 1);  // 0, 1, 4, 5
-    const int rA0 = 8 * h8 + p, rA1 = 8 * h8 + p + 2;
-    const int rB0 = 16 + 8 * h8 + ((p + 4) & 7), rB1 = 16 + 8 * h8 + ((p + 6) & 7);
-    const int row = (t == 0) ? rA0 : (t == 1) ? rA1 : (t == 2) ? rB0 : rB1;
-    woff[st] = row * 128 + ((g ^ (row & 7)) << 4);
-    xoff[st] = b_live ? (uint32_t)(row * kXRowBytes + b_off) : 0xFFFFFFFFu;
-  }
+  const int be = g >> 1, bv = g & 1;  // as B provider: column n = g
+  const uint32_t sel_e = (0x4444u & ~(0xFu << (4 * be))) | ((uint32_t)(2 * bv) << (4 * be));
+  const uint32_t sel_o = (0x4444u & ~(0xFu << (4 * be))) | ((uint32_t)(2 * bv + 1) << (4 * be));
+  // Step st covers k-pair rows base(st) + 2t, base = 16 (st / 4) + 8 (st / 2 % 2) + st % 2:
+  // with the 128-byte swizzle the 8 lanes of a quarter warp read 8 distinct
+  // 16-byte bank groups.  Lane offsets for even / odd base:
+  const uint32_t woff0 = 256u * t + ((uint32_t)(g ^ (2 * t)) << 4);
+  const uint32_t woff1 = 256u * t + ((uint32_t)(g ^ (2 * t + 1)) << 4);
 
-  float2 acc[8];  // pairs (4j, 4j+2) -> acc[2j], (4j+1, 4j+3) -> acc[2j+1]
+  float acc[4];  // columns 16g + t + 4i of this warp's strip
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = make_float2(0.f, 0.f);
-  // Sums the quad (variants x halves), stores this lane's share of segment
-  // seg into the warp's private slot and clears the accumulators.
-  // Column of pair entry: acc[2j+h].x -> 4j+h, .y -> 4j+h+2; lane t writes j = t.
+  for (int i = 0; i < 4; ++i) acc[i] = 0.f;
+  // Stores this lane's columns of segment seg into the warp's private slot and clears them.
   auto flush = [&](int seg) {
+    float* r0 = red + (seg * kPhases + phase) * kTC + strip * 128 + 16 * g + t;
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      acc[q].x += __shfl_xor_sync(0xffffffffu, acc[q].x, 1);
-      acc[q].y += __shfl_xor_sync(0xffffffffu, acc[q].y, 1);
-      acc[q].x += __shfl_xor_sync(0xffffffffu, acc[q].x, 2);
-      acc[q].y += __shfl_xor_sync(0xffffffffu, acc[q].y, 2);
+    for (int i = 0; i < 4; ++i) {
+      r0[4 * i] = acc[i];
+      acc[i] = 0.f;
     }
-    const float2 e = t == 0 ? acc[0] : t == 1 ? acc[2] : t == 2 ? acc[4] : acc[6];
-    const float2 o = t == 0 ? acc[1] : t == 1 ? acc[3] : t == 2 ? acc[5] : acc[7];
-    float* r0 = red + (seg * kPhases + phase) * kTC + strip * 128 + g * 16 + 4 * t;
-    *reinterpret_cast<float4*>(r0) = make_float4(e.x, o.x, e.y, o.y);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) acc[q] = make_float2(0.f, 0.f);
   };
   int cur_seg = 0;
 
@@ -384,59 +330,45 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       break;
     }
     const uint8_t* wst = smem + kOffW + (warp * kStages + s) * kWBytes;
-    const uint8_t* xrows = xst + (size_t)sl * kRows * kXRowBytes;
-    float d[4][4];
+    const uint8_t* xr = reinterpret_cast<const uint8_t*>(xst + sl * kRows) + 8 * t;  // row 2t
+    int d[2][2][4];  // [half][jm][fragment]
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int h = 0; h < 2; ++h)
 #pragma unroll
-      for (int q = 0; q < 4; ++q) d[j][q] = 0.f;
+      for (int jm = 0; jm < 2; ++jm)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) d[h][jm][q] = 0;
 #pragma unroll
     for (int st = 0; st < 8; ++st) {
-      const uint4 wv = *reinterpret_cast<const uint4*>(wst + woff[st]);
-      const uint2 bw = *reinterpret_cast<const uint2*>(xoff[st] == 0xFFFFFFFFu ? zrow : xrows + xoff[st]);
-      const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t e02, o02, e13, o13;
-        nibbles_h(words[j], e02, o02, e13, o13);
-        sgd::mma_f16_16816(d[j], e02, e13, o02, o13, bw.x, bw.y);
-      }
+      const int base = 16 * (st >> 2) + 8 * ((st >> 1) & 1) + (st & 1);
+      const uint4 wv = *reinterpret_cast<const uint4*>(wst + base * 128 + ((st & 1) ? woff1 : woff0));
+      const uint32_t X = *reinterpret_cast<const uint32_t*>(xr + base * 4);
+      const uint32_t b0 = __byte_perm(X, 0u, sel_e), b1 = __byte_perm(X, 0u, sel_o);
+      const int h = st >> 2;
+      sgd::mma_u8s8_16832(d[h][0], wv.x & 0x0F0F0F0Fu, wv.y & 0x0F0F0F0Fu, (wv.x >> 4) & 0x0F0F0F0Fu,
+                          (wv.y >> 4) & 0x0F0F0F0Fu, b0, b1);
+      sgd::mma_u8s8_16832(d[h][1], wv.z & 0x0F0F0F0Fu, wv.w & 0x0F0F0F0Fu, (wv.z >> 4) & 0x0F0F0F0Fu,
+                          (wv.w >> 4) & 0x0F0F0F0Fu, b0, b1);
     }
-    // ---- chunk epilogue: acc += scale * (D - P - (8 + zero) * X) for this lane's variant
+    // ---- chunk epilogue per half and column:
+    //      acc += scale * 2^(E-13) * (256 D_hi + D_lo - (8 + zero) * sum x_q)
     const uint8_t* szs = smem + kOffSZ + (warp * kStages + s) * kSZBytes;
     const int k0 = 2 * crow * kRows;
     const int gA = group_of(a, k0), gB = group_of(a, k0 + 32);
-    const int srow = d_half ? (gB - gA) : 0;
-    const uint4 s_lo = *reinterpret_cast<const uint4*>(szs + srow * 256 + g * 32);
-    const uint4 s_hi = *reinterpret_cast<const uint4*>(szs + srow * 256 + g * 32 + 16);
-    const float4 xp = xhalf[sl * 2 + d_half];
-    const float X = d_lo ? xp.z : xp.x;
-    const float P = d_lo ? xp.w : xp.y;
-    uint4 zv = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);  // biased zeros = 0
-    if (HAS_Z) {
-      zv = *reinterpret_cast<const uint4*>(szs + kSBytes + srow * 128 + g * 16);
-      zv.x ^= 0x80808080u;
-      zv.y ^= 0x80808080u;
-      zv.z ^= 0x80808080u;
-      zv.w ^= 0x80808080u;
-    }
-    const float2 mP = make_float2(-P, -P), XX = make_float2(X, X);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int h = 0; h < 2; ++h) {
+      const int srow = h ? (gB - gA) : 0;
+      const int2 xg = xgrp[sl * 2 + h];
+      const float sxh = __int_as_float(xg.x);
+      const __half* sc_row = reinterpret_cast<const __half*>(szs + srow * 256) + 16 * g + t;
+      const int8_t* z_row = reinterpret_cast<const int8_t*>(szs + kSBytes + srow * 128) + 16 * g + t;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        // pair h: d[j][2h], d[j][2h+1] -> columns 4j+h and 4j+h+2
-        const int ca = 4 * j + h, cb = 4 * j + h + 2;
-        const float2 sc = make_float2(sgd::half16_at(s_lo, s_hi, ca), sgd::half16_at(s_lo, s_hi, cb));
-        // 8 + zero: byte (zero ^ 0x80) placed in the mantissa of 2^23, minus (2^23 + 120)
-        const uint32_t zwa = sgd::u4_get(zv, ca >> 2), zwb = sgd::u4_get(zv, cb >> 2);
-        const float za = __uint_as_float(__byte_perm(zwa, 0x4B000000u, 0x7440 | (ca & 3)));
-        const float zb = __uint_as_float(__byte_perm(zwb, 0x4B000000u, 0x7440 | (cb & 3)));
-        const float2 z8 = sgd::ffma2(make_float2(za, zb), make_float2(-1.f, -1.f),
-                                     make_float2(8388728.f, 8388728.f));  // -(z + 8)
-        const float2 dp = sgd::ffma2(make_float2(d[j][2 * h], d[j][2 * h + 1]), make_float2(1.f, 1.f), mP);
-        const float2 tq = sgd::ffma2(z8, XX, dp);
-        acc[2 * j + h] = sgd::ffma2(sc, tq, acc[2 * j + h]);
+      for (int i = 0; i < 4; ++i) {
+        const int jm = i >> 1, fr = (i & 1) * 2;
+        const int y = d[h][jm][fr] * 256 + d[h][jm][fr + 1];
+        const int z8 = HAS_Z ? 8 + (int)z_row[4 * i] : 8;
+        const int tq = y - z8 * xg.y;
+        acc[i] = fmaf(__half2float(sc_row[4 * i]) * sxh, (float)tq, acc[i]);
       }
     }
     __syncwarp();
