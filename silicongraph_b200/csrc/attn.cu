@@ -16,12 +16,14 @@
 //     and a combine kernel merges the splits in fixed order (deterministic).
 // Used for decode (few queries, long KV) and for shapes outside the tensor-core
 // prefill kernel.
+#include <cooperative_groups.h>
+
 #include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <string_view>
 
-#include "sg_common.cuh"
+#include "sm100.cuh"
 
 namespace {
 
@@ -334,7 +336,246 @@ __global__ void attn_combine_kernel(AArgs a) {
   }
 }
 
-std::atomic<int> g_decode_kernel{1};  // key-parallel decode kernel on/off
+// Decode form: few query rows per kv head (R = G * Sq <= 32), head_dim 64 or
+// 128.  The key splits of one (batch, kv head) form one thread-block cluster.
+// Each block streams its 64-key tiles with 16-byte loads straight into
+// registers, one tile ahead: thread t holds half of key t / 2 (K and V).
+// Scores come from the K registers (queries prescaled by scale * log2(e),
+// shared memory, broadcast reads), the online softmax runs one warp per row,
+// and O += P V reads V from shared memory as fp32.  At the end every block
+// stores its (max, sum, unnormalised O) into rank 0's shared memory and rank
+// 0 merges the splits in rank order (deterministic) and writes O: no global
+// scratch and no second kernel.
+constexpr int kDecClusterMax = 16;
+constexpr int kDecTile = 64;
+
+template <int IO>
+struct IoVec;
+template <>
+struct IoVec<SG_DT_F16> {
+  static constexpr int kBytes = 2;
+  __device__ static void to_f32(const uint4& v, float* f) {
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 x = __half22float2(h[i]);
+      f[2 * i] = x.x;
+      f[2 * i + 1] = x.y;
+    }
+  }
+};
+template <>
+struct IoVec<SG_DT_BF16> {
+  static constexpr int kBytes = 2;
+  __device__ static void to_f32(const uint4& v, float* f) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 x = __bfloat1622float2(h[i]);
+      f[2 * i] = x.x;
+      f[2 * i + 1] = x.y;
+    }
+  }
+};
+template <>
+struct IoVec<SG_DT_F32> {
+  static constexpr int kBytes = 4;
+  __device__ static void to_f32(const uint4& v, float* f) {
+    f[0] = __uint_as_float(v.x);
+    f[1] = __uint_as_float(v.y);
+    f[2] = __uint_as_float(v.z);
+    f[3] = __uint_as_float(v.w);
+  }
+};
+
+// shared memory of attn_dec_cluster_kernel<D> for R rows and nsplit ranks (floats)
+inline size_t dec_cluster_smem(int D, int R, int nsplit) {
+  return sizeof(float) * ((size_t)2 * R * (D / 2) + 4 + (size_t)R * kDecTile + (size_t)kDecTile * D + 3 * R +
+                          (size_t)nsplit * R * (D + 2));
+}
+
+template <int D, int IO>
+__global__ void __launch_bounds__(kThreads) attn_dec_cluster_kernel(AArgs a) {
+  namespace cg = cooperative_groups;
+  constexpr int KT = kDecTile, DH = D / 2;
+  constexpr int EPV = 16 / IoVec<IO>::kBytes;  // elements per 16-byte load
+  constexpr int NV = DH / EPV;                 // 16-byte loads per thread per tile (K, and V)
+  extern __shared__ __align__(16) float sm[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int b = blockIdx.z, hk = blockIdx.y, split = blockIdx.x;
+  const int nq = a.Sq, R = a.G * nq;  // row r: head hk*G + r / nq, query r % nq
+  float* qs = sm;                        // [part][R][DH], part 1 offset by 4 floats (banks)
+  float* ps = qs + 2 * R * DH + 4;       // [R][KT] scores, then probabilities
+  float* vsf = ps + R * KT;              // [KT][D] V tile
+  float* ms = vsf + KT * D;              // [R] running max (log2 units)
+  float* ls = ms + R;                    // [R] running sum
+  float* al = ls + R;                    // [R] rescale of this tile
+  float* comb = al + R;                  // rank 0: [rank][R][D + 2]
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  sgd::pdl_wait();  // the newest key and the queries come from the previous kernel
+  sgd::pdl_launch_dependents();
+
+  const int q_pos0 = a.q_pos_dev ? *a.q_pos_dev : a.q_pos0;
+  const int Skv = a.q_pos_dev ? min(a.Skv, q_pos0 + a.Sq) : a.Skv;
+  const int j0 = split * a.keys_per_split;
+  int j1 = min(Skv, j0 + a.keys_per_split);
+  if (a.causal) j1 = min(j1, q_pos0 + nq);
+  const int64_t kvbase = (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs;
+  const float qscale = a.scale * 1.4426950408889634f;
+  const int kk = tid >> 1, part = tid & 1;
+  float* qpart = qs + part * (R * DH + 4);
+  for (int r = tid; r < R; r += kThreads) {
+    ms[r] = -INFINITY;
+    ls[r] = 0.f;
+  }
+  constexpr int kUnits = (kDecRows * D / 4 + kThreads - 1) / kThreads;  // float4 outputs per thread (max)
+  float4 o[kUnits];
+#pragma unroll
+  for (int k = 0; k < kUnits; ++k) o[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+  uint4 kr[NV], vr[NV];
+  auto load_tile = [&](int jt) {
+    const int key = jt + kk;
+    const bool live = key < j1;
+    const uint4* kp = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.K) +
+                                                     ((kvbase + (int64_t)key * D + part * DH) * IoVec<IO>::kBytes));
+    const uint4* vp = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.V) +
+                                                     ((kvbase + (int64_t)key * D + part * DH) * IoVec<IO>::kBytes));
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      kr[i] = live ? __ldg(kp + i) : make_uint4(0u, 0u, 0u, 0u);
+      vr[i] = live ? __ldg(vp + i) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  if (j0 < j1) load_tile(j0);  // in flight together with the query loads
+  for (int i = tid; i < R * D; i += kThreads) {
+    const int r = i / D, d = i % D;
+    const int h = hk * a.G + r / nq, qi = r % nq;
+    const float v = ld_io(a.Q, a.io_dt, (((int64_t)b * a.H + h) * a.Sq + qi) * D + d) * qscale;
+    qs[(d / DH) * (R * DH + 4) + r * DH + (d % DH)] = v;
+  }
+  __syncthreads();
+  for (int jt = j0; jt < j1; jt += KT) {
+    // V tile into shared memory; scores of this thread's key half for every row
+    float kf[DH];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      float vf[EPV];
+      IoVec<IO>::to_f32(vr[i], vf);
+#pragma unroll
+      for (int e = 0; e < EPV; e += 4)
+        *reinterpret_cast<float4*>(vsf + kk * D + part * DH + i * EPV + e) =
+            make_float4(vf[e], vf[e + 1], vf[e + 2], vf[e + 3]);
+      IoVec<IO>::to_f32(kr[i], kf + i * EPV);
+    }
+    const int key = jt + kk;
+    const bool vis_key = key < j1;
+    for (int r = 0; r < R; ++r) {
+      const float* qr = qpart + r * DH;
+      float sdot = 0.f;
+#pragma unroll
+      for (int d = 0; d < DH; d += 4) {
+        const float4 q4 = *reinterpret_cast<const float4*>(qr + d);
+        sdot = fmaf(q4.x, kf[d], sdot);
+        sdot = fmaf(q4.y, kf[d + 1], sdot);
+        sdot = fmaf(q4.z, kf[d + 2], sdot);
+        sdot = fmaf(q4.w, kf[d + 3], sdot);
+      }
+      sdot += __shfl_xor_sync(0xffffffffu, sdot, 1);
+      const bool vis = vis_key && (!a.causal || key <= q_pos0 + r % nq);
+      if (part == 0) ps[r * KT + kk] = vis ? sdot : -INFINITY;
+    }
+    if (jt + KT < j1) load_tile(jt + KT);  // next tile in flight during this one's softmax and P V
+    __syncthreads();
+    // online softmax: one warp per row
+    for (int r = warp; r < R; r += kThreads / 32) {
+      const float s0 = ps[r * KT + lane], s1 = ps[r * KT + lane + 32];
+      float mx = fmaxf(s0, s1);
+#pragma unroll
+      for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_old = ms[r];
+      const float m_new = fmaxf(m_old, mx);
+      const float p0 = m_new == -INFINITY ? 0.f : exp2f(s0 - m_new);
+      const float p1 = m_new == -INFINITY ? 0.f : exp2f(s1 - m_new);
+      ps[r * KT + lane] = p0;
+      ps[r * KT + lane + 32] = p1;
+      float sum = p0 + p1;
+#pragma unroll
+      for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      const float alpha = m_old == -INFINITY ? 0.f : exp2f(m_old - m_new);
+      __syncwarp();
+      if (lane == 0) {
+        ms[r] = m_new;
+        ls[r] = ls[r] * alpha + sum;
+        al[r] = alpha;
+      }
+    }
+    __syncthreads();
+    // O += P V: thread -> float4 units u = tid + k * kThreads (row u / (D/4), dims 4 (u % (D/4)))
+#pragma unroll
+    for (int k = 0; k < kUnits; ++k) {
+      const int u = tid + k * kThreads;
+      if (u < R * (D / 4)) {
+        const int r = u / (D / 4), d = 4 * (u % (D / 4));
+        const float alr = al[r];
+        float4 acc = make_float4(o[k].x * alr, o[k].y * alr, o[k].z * alr, o[k].w * alr);
+#pragma unroll 8
+        for (int j = 0; j < KT; ++j) {
+          const float p = ps[r * KT + j];
+          const float4 v = *reinterpret_cast<const float4*>(vsf + j * D + d);
+          acc.x = fmaf(p, v.x, acc.x);
+          acc.y = fmaf(p, v.y, acc.y);
+          acc.z = fmaf(p, v.z, acc.z);
+          acc.w = fmaf(p, v.w, acc.w);
+        }
+        o[k] = acc;
+      }
+    }
+    __syncthreads();  // ps, vsf and al are rewritten by the next tile
+  }
+
+  // ---- merge the splits in rank 0 (cluster rank == split)
+  cg::cluster_group cluster = cg::this_cluster();
+  const int nsplit = a.nsplit;
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+  float* dst = cluster.map_shared_rank(comb, 0) + (size_t)split * R * (D + 2);
+#pragma unroll
+  for (int k = 0; k < kUnits; ++k) {
+    const int u = tid + k * kThreads;
+    if (u < R * (D / 4)) {
+      const int r = u / (D / 4), d = 4 * (u % (D / 4));
+      float* pr = dst + r * (D + 2) + d;
+      pr[0] = o[k].x;
+      pr[1] = o[k].y;
+      pr[2] = o[k].z;
+      pr[3] = o[k].w;
+    }
+  }
+  for (int r = tid; r < R; r += kThreads) {
+    dst[r * (D + 2) + D] = ms[r];
+    dst[r * (D + 2) + D + 1] = ls[r];
+  }
+  cluster.sync();
+  if (split != 0) return;
+  for (int i = tid; i < R * D; i += kThreads) {
+    const int r = i / D, d = i % D;
+    float M = -INFINITY;
+    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, comb[((size_t)sp * R + r) * (D + 2) + D]);
+    float L = 0.f, acc = 0.f;
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float* pr = comb + ((size_t)sp * R + r) * (D + 2);
+      if (pr[D] == -INFINITY) continue;
+      const float w = exp2f(pr[D] - M);
+      L = fmaf(pr[D + 1], w, L);
+      acc = fmaf(pr[d], w, acc);
+    }
+    const int h = hk * a.G + r / nq, qi = r % nq;
+    st_io(a.O, a.io_dt, (((int64_t)b * a.H + h) * a.Sq + qi) * D + d, L > 0.f ? acc / L : 0.f);
+  }
+}
+
+std::atomic<int> g_decode_kernel{1};  // decode kernel: 1 cluster, 2 key-parallel + combine, 0 generic
+std::atomic<int> g_decode_cluster_max{kDecClusterMax};  // largest cluster of key splits
 
 }  // namespace
 
@@ -343,6 +584,10 @@ namespace sg {
 bool attn_tuning(std::string_view key, int value) {
   if (key == "attn.decode_kernel") {
     g_decode_kernel.store(value);
+    return true;
+  }
+  if (key == "attn.decode_cluster_max") {
+    g_decode_cluster_max.store(value);
     return true;
   }
   return false;
@@ -426,8 +671,50 @@ SgStatus attn_cc_run(const SgFlashAttentionParams* p, void* stream, int want_spl
     }
     a.part = static_cast<float*>(ws);
   }
-  // Few query rows per kv head (decode): the key-parallel kernel.
-  if ((a.D == 64 || a.D == 128) && a.G * a.Sq <= kDecRows && g_decode_kernel.load()) {
+  // Few query rows per kv head (decode): one cluster of key splits per (batch, kv head).
+  const int R = a.G * a.Sq;
+  const int eb = a.io_dt == SG_DT_F32 ? 4 : 2;
+  const bool vec_ok = aligned16(a.K) && aligned16(a.V) && (a.kv_hs * eb) % 16 == 0 && (a.kv_bs * eb) % 16 == 0;
+  if ((a.D == 64 || (a.D == 128 && eb == 2)) && R <= kDecRows && vec_ok && g_decode_kernel.load() == 1) {
+    const int tiles = (a.Skv + kDecTile - 1) / kDecTile;
+    const int items = a.Hkv * a.B;
+    const int cmax = std::max(1, std::min(kDecClusterMax, g_decode_cluster_max.load()));
+    int ns = std::max(1, std::min({cmax, tiles, (2 * sms + items - 1) / items}));
+    while (ns > 1 && dec_cluster_smem(a.D, R, ns) > 200 * 1024) --ns;
+    const int tiles_per = (tiles + ns - 1) / ns;
+    a.keys_per_split = tiles_per * kDecTile;
+    a.nsplit = (tiles + tiles_per - 1) / tiles_per;
+    const size_t smem = dec_cluster_smem(a.D, R, a.nsplit);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.nsplit, a.Hkv, a.B);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = cs;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = a.nsplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    auto launch_cl = [&](void (*kfn)(AArgs)) -> SgStatus {
+      SG_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      if (a.nsplit > 8) SG_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+      SG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kfn, a));
+      return SG_OK;
+    };
+    if (a.D == 64) {
+      if (a.io_dt == SG_DT_F32) return launch_cl(attn_dec_cluster_kernel<64, SG_DT_F32>);
+      if (a.io_dt == SG_DT_BF16) return launch_cl(attn_dec_cluster_kernel<64, SG_DT_BF16>);
+      return launch_cl(attn_dec_cluster_kernel<64, SG_DT_F16>);
+    }
+    if (a.io_dt == SG_DT_BF16) return launch_cl(attn_dec_cluster_kernel<128, SG_DT_BF16>);
+    return launch_cl(attn_dec_cluster_kernel<128, SG_DT_F16>);
+  }
+  // The key-parallel kernel with a separate combine.
+  if ((a.D == 64 || a.D == 128) && R <= kDecRows && g_decode_kernel.load() != 0) {
     const dim3 dgrid(nsplit, a.Hkv, a.B);
     // shared-memory attribute set once per (kernel, device)
     static std::atomic<uint64_t> set_mask[2] = {{0}, {0}};

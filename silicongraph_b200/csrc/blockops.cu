@@ -72,6 +72,8 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 // residual (I/O type) and normalised; without: h = x.
 __global__ void __launch_bounds__(kRowThreads) rmsnorm_kernel(const void* x, void* residual, const void* w, void* y,
                                                               int n, float eps, int dt) {
+  sgd::pdl_wait();  // inputs come from the previous kernel on the stream
+  sgd::pdl_launch_dependents();
   __shared__ float red[32];
   const int64_t base = (int64_t)blockIdx.x * n;
   float ss = 0.f;
@@ -115,6 +117,8 @@ template <typename T>
 __global__ void __launch_bounds__(kRowThreads) rmsnorm_vec_kernel(const T* __restrict__ x, T* __restrict__ residual,
                                                                   const T* __restrict__ w, T* __restrict__ y, int n,
                                                                   float eps) {
+  sgd::pdl_wait();  // inputs come from the previous kernel on the stream
+  sgd::pdl_launch_dependents();
   __shared__ float red[32];
   const int64_t base = (int64_t)blockIdx.x * n;
   const int nv = n / 8;
@@ -153,6 +157,8 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_vec_kernel(const T* __res
 
 // y = silu(g) (* u when u != NULL)
 __global__ void silu_kernel(const void* g, const void* u, void* y, int64_t n, int dt) {
+  sgd::pdl_wait();  // inputs come from the previous kernel on the stream
+  sgd::pdl_launch_dependents();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const float xi = ld(g, dt, i);
     float v = xi / (1.0f + expf(-xi));
@@ -164,6 +170,8 @@ __global__ void silu_kernel(const void* g, const void* u, void* y, int64_t n, in
 // One CTA per row (reference order: max; y = round(exp(x - max)); sum of the
 // rounded values; y = round(y * (1 / sum))).
 __global__ void __launch_bounds__(kRowThreads) softmax_kernel(const void* x, void* y, int n, int dt) {
+  sgd::pdl_wait();  // inputs come from the previous kernel on the stream
+  sgd::pdl_launch_dependents();
   __shared__ float red[32];
   const int64_t base = (int64_t)blockIdx.x * n;
   float mx = -FLT_MAX;
@@ -182,6 +190,8 @@ __global__ void __launch_bounds__(kRowThreads) softmax_kernel(const void* x, voi
 
 // In place on x [tokens, heads, D]: token t is at position pos[t] (or pos0 + t).
 __global__ void rope_kernel(void* x, int tokens, int heads, int D, const int32_t* pos, int pos0, float base, int dt) {
+  sgd::pdl_wait();  // inputs come from the previous kernel on the stream
+  sgd::pdl_launch_dependents();
   const int half = D / 2;
   const int64_t total = (int64_t)tokens * heads * half;
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
@@ -201,6 +211,8 @@ __global__ void rope_kernel(void* x, int tokens, int heads, int D, const int32_t
 // out[t, :] = table[ids[t], :]; ids outside [0, vocab) give zeros and the error word.
 __global__ void embedding_kernel(const void* table, const int32_t* ids, void* out, int tokens, int hidden, int vocab,
                                  int esz, int* bad) {
+  sgd::pdl_wait();  // inputs come from the previous kernel on the stream
+  sgd::pdl_launch_dependents();
   const int t = blockIdx.y;
   if (t >= tokens) return;
   const int id = ids[t];
@@ -225,6 +237,8 @@ __global__ void embedding_kernel(const void* table, const int32_t* ids, void* ou
 
 // Greedy argmax per row of fp32 logits (first index among equal maxima; NaN never wins).
 __global__ void __launch_bounds__(kRowThreads) argmax_kernel(const float* logits, int n, int32_t* out) {
+  sgd::pdl_wait();  // inputs come from the previous kernel on the stream
+  sgd::pdl_launch_dependents();
   __shared__ float sv[32];
   __shared__ int si[32];
   const float* row = logits + (int64_t)blockIdx.x * n;
@@ -295,14 +309,13 @@ SgStatus sg_rmsnorm(const void* x, void* residual, const void* w, void* y, int32
   const bool vec = dt != SG_DT_F32 && n % 8 == 0 && n <= 8 * kRowThreads * kVecPerThread && sg::aligned16(x) &&
                    sg::aligned16(w) && sg::aligned16(y) && (residual == nullptr || sg::aligned16(residual));
   if (vec && dt == SG_DT_F16)
-    rmsnorm_vec_kernel<__half><<<rows, kRowThreads, 0, cs>>>(static_cast<const __half*>(x),
-                                                             static_cast<__half*>(residual),
-                                                             static_cast<const __half*>(w), static_cast<__half*>(y),
-                                                             n, eps);
+    SG_CUDA_TRY(sgd::launch_pdl(rmsnorm_vec_kernel<__half>, dim3(rows), dim3(kRowThreads), 0, cs,
+                                static_cast<const __half*>(x), static_cast<__half*>(residual),
+                                static_cast<const __half*>(w), static_cast<__half*>(y), n, eps));
   else if (vec)
-    rmsnorm_vec_kernel<__nv_bfloat16><<<rows, kRowThreads, 0, cs>>>(
-        static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(residual),
-        static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(y), n, eps);
+    SG_CUDA_TRY(sgd::launch_pdl(rmsnorm_vec_kernel<__nv_bfloat16>, dim3(rows), dim3(kRowThreads), 0, cs,
+                                static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(residual),
+                                static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(y), n, eps));
   else
     rmsnorm_kernel<<<rows, kRowThreads, 0, cs>>>(x, residual, w, y, n, eps, dt);
   return sg::check_launch("sg_rmsnorm");
@@ -371,8 +384,8 @@ SgStatus sg_embedding(const void* table, const int32_t* ids, void* out, int32_t 
   if (s != SG_OK) return s;
   const int64_t row_bytes = (int64_t)hidden * sg::elem_size(dt);
   const dim3 grid((unsigned)std::max<int64_t>(1, std::min<int64_t>(8, (row_bytes / 16 + 255) / 256)), tokens);
-  embedding_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(table, ids, out, tokens, hidden, vocab,
-                                                                        sg::elem_size(dt), err);
+  SG_CUDA_TRY(sgd::launch_pdl(embedding_kernel, grid, dim3(256), 0, static_cast<cudaStream_t>(stream), table, ids,
+                              out, tokens, hidden, vocab, (int)sg::elem_size(dt), err));
   return sg::check_launch("sg_embedding");
 }
 

@@ -16,6 +16,8 @@ template <typename T>
 __global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, int T_, int H, int Hkv, int D,
                                        const int32_t* __restrict__ pos, int pos0, float base, T* __restrict__ q_out,
                                        T* __restrict__ k_cache, T* __restrict__ v_cache, int64_t kv_head_stride) {
+  sgd::pdl_wait();  // inputs come from the previous kernel on the stream
+  sgd::pdl_launch_dependents();
   const int half = D / 2;
   const int slots = H + 2 * Hkv;  // head slots per token: q heads, k heads, v heads
   const int64_t total = (int64_t)T_ * slots * half;
@@ -45,6 +47,8 @@ __global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, int T_, int H,
 
 template <typename T>
 __global__ void head_transpose_kernel(const T* __restrict__ in, T* __restrict__ out, int H, int T_, int D) {
+  sgd::pdl_wait();  // inputs come from the previous kernel on the stream
+  sgd::pdl_launch_dependents();
   const int64_t total = (int64_t)H * T_ * D;
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
     const int d = (int)(e % D);
@@ -58,6 +62,8 @@ __global__ void head_transpose_kernel(const T* __restrict__ in, T* __restrict__ 
 // y[t, j] = round(silu(gu[t, j])) * gu[t, F + j]  (gate and up halves of the fused projection)
 template <typename T>
 __global__ void swiglu_rows_kernel(const T* __restrict__ gu, T* __restrict__ y, int rows, int F) {
+  sgd::pdl_wait();  // inputs come from the previous kernel on the stream
+  sgd::pdl_launch_dependents();
   const int64_t total = (int64_t)rows * F;
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
     const int j = (int)(e % F);
@@ -71,6 +77,8 @@ __global__ void swiglu_rows_kernel(const T* __restrict__ gu, T* __restrict__ y, 
 // Greedy token and its log-probability: out = argmax, logprob = x[out] - max - log(sum exp(x - max)).
 __global__ void __launch_bounds__(256) argmax_logprob_kernel(const float* __restrict__ logits, int n,
                                                              int32_t* __restrict__ out, float* __restrict__ logprob) {
+  sgd::pdl_wait();  // inputs come from the previous kernel on the stream
+  sgd::pdl_launch_dependents();
   __shared__ float sv[32];
   __shared__ int si[32];
   __shared__ float ss[32];
@@ -129,6 +137,8 @@ constexpr int kArgSlice = 4096;
 
 __global__ void __launch_bounds__(256) argmax_partial_kernel(const float* __restrict__ logits, int n, int slices,
                                                              float* __restrict__ part) {
+  sgd::pdl_wait();  // inputs come from the previous kernel on the stream
+  sgd::pdl_launch_dependents();
   __shared__ float sv[8], ssum[8];
   __shared__ int si[8];
   const int row = blockIdx.y, sl = blockIdx.x;
@@ -183,6 +193,8 @@ __global__ void __launch_bounds__(256) argmax_partial_kernel(const float* __rest
 __global__ void argmax_merge_kernel(const float* __restrict__ logits, int n, int slices,
                                     const float* __restrict__ part, int32_t* __restrict__ out,
                                     float* __restrict__ logprob) {
+  sgd::pdl_wait();  // inputs come from the previous kernel on the stream
+  sgd::pdl_launch_dependents();
   if (threadIdx.x != 0) return;
   const int row = blockIdx.x;
   const float* pp = part + (int64_t)row * slices * 3;
@@ -227,14 +239,16 @@ SgStatus sg_qkv_rope_append(const void* qkv, int32_t tokens, int32_t heads, int3
   cudaStream_t cs = static_cast<cudaStream_t>(stream);
   const int64_t total = (int64_t)tokens * (heads + 2 * kv_heads) * (head_dim / 2);
   if (dt == SG_DT_F16)
-    qkv_rope_append_kernel<__half><<<grid_of(total), 256, 0, cs>>>(
-        static_cast<const __half*>(qkv), tokens, heads, kv_heads, head_dim, positions, pos0, base,
-        static_cast<__half*>(q_out), static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), kv_head_stride);
+    SG_CUDA_TRY(sgd::launch_pdl(qkv_rope_append_kernel<__half>, dim3(grid_of(total)), dim3(256), 0, cs,
+                                static_cast<const __half*>(qkv), (int)tokens, (int)heads, (int)kv_heads,
+                                (int)head_dim, positions, (int)pos0, base, static_cast<__half*>(q_out),
+                                static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), kv_head_stride));
   else
-    qkv_rope_append_kernel<__nv_bfloat16><<<grid_of(total), 256, 0, cs>>>(
-        static_cast<const __nv_bfloat16*>(qkv), tokens, heads, kv_heads, head_dim, positions, pos0, base,
-        static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_cache),
-        static_cast<__nv_bfloat16*>(v_cache), kv_head_stride);
+    SG_CUDA_TRY(sgd::launch_pdl(qkv_rope_append_kernel<__nv_bfloat16>, dim3(grid_of(total)), dim3(256), 0, cs,
+                                static_cast<const __nv_bfloat16*>(qkv), (int)tokens, (int)heads, (int)kv_heads,
+                                (int)head_dim, positions, (int)pos0, base, static_cast<__nv_bfloat16*>(q_out),
+                                static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache),
+                                kv_head_stride));
   return sg::check_launch("sg_qkv_rope_append");
 }
 
@@ -264,11 +278,12 @@ SgStatus sg_swiglu_rows(const void* gate_up, void* y, int32_t rows, int32_t ffn,
   cudaStream_t cs = static_cast<cudaStream_t>(stream);
   const int64_t total = (int64_t)rows * ffn;
   if (dt == SG_DT_F16)
-    swiglu_rows_kernel<__half><<<grid_of(total), 256, 0, cs>>>(static_cast<const __half*>(gate_up),
-                                                              static_cast<__half*>(y), rows, ffn);
+    SG_CUDA_TRY(sgd::launch_pdl(swiglu_rows_kernel<__half>, dim3(grid_of(total)), dim3(256), 0, cs,
+                                static_cast<const __half*>(gate_up), static_cast<__half*>(y), (int)rows, (int)ffn));
   else
-    swiglu_rows_kernel<__nv_bfloat16><<<grid_of(total), 256, 0, cs>>>(
-        static_cast<const __nv_bfloat16*>(gate_up), static_cast<__nv_bfloat16*>(y), rows, ffn);
+    SG_CUDA_TRY(sgd::launch_pdl(swiglu_rows_kernel<__nv_bfloat16>, dim3(grid_of(total)), dim3(256), 0, cs,
+                                static_cast<const __nv_bfloat16*>(gate_up), static_cast<__nv_bfloat16*>(y),
+                                (int)rows, (int)ffn));
   return sg::check_launch("sg_swiglu_rows");
 }
 
@@ -285,11 +300,11 @@ SgStatus sg_argmax_logprob(const float* logits, int32_t rows, int32_t n, int32_t
   void* ws = nullptr;
   SgStatus st = sg::library_workspace(stream, (size_t)rows * slices * 3 * sizeof(float), &ws, sg::kWsArgmax);
   if (st != SG_OK) return st;
-  argmax_partial_kernel<<<dim3(slices, rows), 256, 0, cs>>>(logits, n, slices, static_cast<float*>(ws));
-  st = sg::check_launch("sg_argmax_logprob");
-  if (st != SG_OK) return st;
-  argmax_merge_kernel<<<rows, 32, 0, cs>>>(logits, n, slices, static_cast<const float*>(ws), out, logprob);
-  return sg::check_launch("sg_argmax_logprob");
+  SG_CUDA_TRY(sgd::launch_pdl(argmax_partial_kernel, dim3(slices, rows), dim3(256), 0, cs, logits, (int)n, slices,
+                              static_cast<float*>(ws)));
+  SG_CUDA_TRY(sgd::launch_pdl(argmax_merge_kernel, dim3(rows), dim3(32), 0, cs, logits, (int)n, slices,
+                              static_cast<const float*>(ws), out, logprob));
+  return SG_OK;
 }
 
 }  // extern "C"

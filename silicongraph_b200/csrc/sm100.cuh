@@ -10,6 +10,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <utility>
 #include <stdint.h>
 
 #include "sg_common.cuh"
@@ -135,6 +136,25 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 // Allow the next grid on the stream to begin launching.
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Host: launch kfn so that it may start while the previous grid on the stream
+// drains (programmatic dependent launch).  The kernel must call pdl_wait()
+// before it reads anything that grid wrote.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kfn)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kfn, std::forward<Args>(args)...);
 }
 
 // ------------------------------------------------------------------ TMA (no multicast)

@@ -62,8 +62,10 @@ constexpr int kStaticSmemReserve = 2048;
 // Launch shapes: warps per block (4 column strips x warps/4 phases) and TMA
 // stages per warp.  Variant 0 is the default; the others are selectable with
 // sg_set_tuning("w4_gemv_mma.variant", v) for measurement.
-constexpr int kVariantWarps[4] = {16, 20, 12, 8};
-constexpr int kVariantStages[4] = {2, 2, 3, 5};
+constexpr int kVariantWarps[5] = {16, 20, 12, 8, 8};
+constexpr int kVariantStages[5] = {2, 2, 3, 5, 2};
+constexpr int kPairVariant = 4;                // 8 warps: two blocks per SM
+constexpr size_t kPairSmemLimit = 110 * 1024;  // dynamic shared memory that lets two blocks share an SM
 constexpr int off_sz(int warps, int stages) { return warps * stages * kWBytes; }
 constexpr int off_x(int warps, int stages) { return off_sz(warps, stages) + warps * stages * kSZBytes; }
 // Dynamic shared memory after the stages (bytes): the staged activation (one
@@ -79,6 +81,7 @@ inline size_t tail_bytes(int warps, int stages, int strips, int x_slots, int max
 std::atomic<int> g_variant{0};
 std::atomic<int> g_sleep{0};
 std::atomic<int> g_cluster_mode{1};
+std::atomic<int> g_pair{1};  // allow two 8-warp blocks per SM
 
 struct MArgs {
   const void* A;
@@ -140,7 +143,7 @@ __device__ __forceinline__ int group_of(const MArgs& a, int k) { return a.gs_shi
 // STRIPS: 128-column strips per tile (tile = STRIPS x 128 columns); the
 // block's warps are STRIPS strips x WARPS / STRIPS phases.
 template <bool HAS_Z, int WARPS, int STAGES, bool CLUSTER, int STRIPS>
-__global__ void __launch_bounds__(WARPS * 32, 1)
+__global__ void __launch_bounds__(WARPS * 32, WARPS <= 8 ? 2 : 1)
     w4_gemv_mma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmS,
                        const __grid_constant__ CUtensorMap tmZ, MArgs a) {
   constexpr int kWarps = WARPS, kThreads = WARPS * 32, kPhases = WARPS / STRIPS, kStages = STAGES;
@@ -441,10 +444,24 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     __threadfence();
     for (int cc = threadIdx.x; cc < kTC; cc += kThreads) {
       const int col = tile * kTC + cc;
+      // Partials in block order; loads batched so that they are in flight
+      // together.  The tile is block bb's first segment (slot 0) when bb
+      // starts inside it, else its last (slot 1).
       float v = 0.f;
-      for (int bb = b_lo; bb <= b_hi; ++bb) {
-        const int sb = (range_start(a, bb) / a.cpt == tile) ? 0 : 1;  // the tile is bb's first or last
-        v += __ldcg(&a.slots[((int64_t)bb * 2 + sb) * kTC + cc]);
+      for (int b0 = b_lo; b0 <= b_hi; b0 += 8) {
+        float pv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int bb = b0 + u;
+          pv[u] = 0.f;
+          if (bb <= b_hi) {
+            const int sb = range_start(a, bb) >= tc0 ? 0 : 1;
+            pv[u] = __ldcg(&a.slots[((int64_t)bb * 2 + sb) * kTC + cc]);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (b0 + u <= b_hi) v += pv[u];
       }
       if (col < a.N) store_out(a.C, a.c_dt, col, finalize(a, col, v));
     }
@@ -461,18 +478,19 @@ struct MPlan {
   size_t smem = 0, ws_bytes = 0, tickets_bytes = 0;
 };
 
-// Clusters of k blocks (one per SM: the kernel's shared memory allows one
-// block per SM) that can be resident at once.
-int max_active_clusters(int k) {
+// Clusters of k blocks that can be resident at once: one 16-warp block per
+// SM, or (pair) two 8-warp blocks per SM.
+int max_active_clusters(int k, int pair) {
   static std::mutex mu;
-  static int cache[17] = {0};
+  static int cache[2][17] = {};
   std::lock_guard<std::mutex> lk(mu);
   if (k < 1 || k > 16) return 0;
-  if (cache[k] != 0) return cache[k];
+  if (cache[pair][k] != 0) return cache[pair][k];
+  const int smem = pair ? (int)kPairSmemLimit : 225 * 1024;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(k, 1);
-  cfg.blockDim = dim3(512);
-  cfg.dynamicSmemBytes = 225 * 1024;
+  cfg.blockDim = dim3(pair ? 256 : 512);
+  cfg.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = k;
@@ -481,13 +499,13 @@ int max_active_clusters(int k) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  auto kfn = w4_gemv_mma_kernel<true, 16, 2, true, 4>;
-  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024) != cudaSuccess ||
+  auto kfn = pair ? w4_gemv_mma_kernel<true, 8, 2, true, 2> : w4_gemv_mma_kernel<true, 16, 2, true, 4>;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
       cudaOccupancyMaxActiveClusters(&n, kfn, &cfg) != cudaSuccess) {
     cudaGetLastError();
     n = -1;
   }
-  cache[k] = n;
+  cache[pair][k] = n;
   return n;
 }
 
@@ -500,36 +518,53 @@ MPlan make_mplan(const SgMatMulParams* p, int sms) {
   pl.cpt = (KP + kRows - 1) / kRows;
   // Cluster split: tiles of 4, 2 or 1 strips (512 / 256 / 128 columns), each
   // split over k <= 8 blocks that reduce through distributed shared memory
-  // (no global scratch).  The shape that keeps the most SMs busy in one wave
-  // (clusters must fit inside a GPC) wins; ties go to wider tiles.  Mode 1
-  // (default) falls back to the stream-K split when no cluster shape fills at
-  // least half the SMs, mode 2 always takes a cluster shape that fits, mode 0
-  // never does.
+  // (no global scratch), with one 16-warp block per SM or, when no such
+  // shape fits, two 8-warp blocks per SM.  The shape that keeps the most
+  // warps busy in one wave (clusters must fit inside a GPC) wins; ties go to
+  // wider tiles.  Mode 1 (default) falls back to the stream-K split when no cluster
+  // shape fills at least half the SMs, mode 2 always takes a cluster shape
+  // that fits, mode 0 never does.
   const int mode = g_cluster_mode.load();
-  int best_blocks = 0, best_strips = 0, best_k = 0;
+  long long best_score = 0;
+  int best_strips = 0, best_k = 0, best_pair = 0;
   if (mode != 0) {
-    for (int strips : {4, 2, 1}) {
-      const int n_tiles = (p->N + strips * 128 - 1) / (strips * 128);
-      if (n_tiles > sms) continue;
-      for (int k = std::min({8, pl.cpt, sms / n_tiles}); k >= 1; --k) {
-        if (max_active_clusters(k) >= n_tiles) {
-          if (n_tiles * k > best_blocks) {
-            best_blocks = n_tiles * k;
+    for (int pair : {0, 1}) {
+      // two blocks per SM only when the tiles outnumber the SMs: with fewer
+      // tiles they measured slower than one 16-warp block per SM
+      if (pair && (!g_pair.load() || best_score > 0)) continue;
+      const int slots = sms * (pair ? 2 : 1);
+      const int vv = pair ? kPairVariant : 0;
+      for (int strips : {4, 2, 1}) {
+        const int n_tiles = (p->N + strips * 128 - 1) / (strips * 128);
+        if (n_tiles > slots) continue;
+        for (int k = std::min({8, pl.cpt, slots / n_tiles}); k >= 1; --k) {
+          if (max_active_clusters(k, pair) < n_tiles) continue;
+          const size_t smem = 1024 + off_x(kVariantWarps[vv], kVariantStages[vv]) +
+                              tail_bytes(kVariantWarps[vv], kVariantStages[vv], strips, (pl.cpt + k - 1) / k, 1, k);
+          if (pair && smem > kPairSmemLimit) continue;
+          const long long score = (long long)n_tiles * k * kVariantWarps[vv];
+          if (score > best_score) {
+            best_score = score;
             best_strips = strips;
             best_k = k;
+            best_pair = pair;
           }
           break;
         }
       }
     }
-    if (mode == 1 && 2 * best_blocks < sms) best_blocks = 0;
+    if (mode == 1 && 2 * best_score < (long long)sms * 16) best_score = 0;
   }
   pl.variant = std::min(3, std::max(0, g_variant.load()));
-  if (best_blocks > 0) {
+  if (best_score > 0) {
     pl.cluster = 1;
     pl.strips = best_strips;
     pl.ksplit = best_k;
-    if (best_strips != 4) pl.variant = 0;  // the narrow tiles come in the default launch shape only
+    if (best_pair) {
+      pl.variant = kPairVariant;
+    } else if (best_strips != 4) {
+      pl.variant = 0;  // the narrow tiles come in the default launch shape only
+    }
     pl.n_tiles = (p->N + best_strips * 128 - 1) / (best_strips * 128);
     pl.total = pl.n_tiles * pl.cpt;
     pl.nblocks = pl.n_tiles * best_k;
@@ -653,13 +688,29 @@ SgStatus w4_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, void
 #undef SG_W4MMA_KFNS
   static const KFn knarrow[2][2] = {{w4_gemv_mma_kernel<false, 16, 2, true, 1>, w4_gemv_mma_kernel<false, 16, 2, true, 2>},
                                     {w4_gemv_mma_kernel<true, 16, 2, true, 1>, w4_gemv_mma_kernel<true, 16, 2, true, 2>}};
+  static const KFn kpair[2][3] = {{w4_gemv_mma_kernel<false, 8, 2, true, 1>, w4_gemv_mma_kernel<false, 8, 2, true, 2>,
+                                   w4_gemv_mma_kernel<false, 8, 2, true, 4>},
+                                  {w4_gemv_mma_kernel<true, 8, 2, true, 1>, w4_gemv_mma_kernel<true, 8, 2, true, 2>,
+                                   w4_gemv_mma_kernel<true, 8, 2, true, 4>}};
   const int zi = a.has_zeros ? 1 : 0;
-  const int ki = !pl.cluster ? pl.variant : pl.strips == 4 ? 4 + pl.variant : 8 + (pl.strips == 2 ? 1 : 0);
-  const KFn kfn = !pl.cluster ? kstream[zi][pl.variant]
-                  : pl.strips == 4 ? kcluster[zi][pl.variant]
-                                   : knarrow[zi][pl.strips == 2 ? 1 : 0];
+  const int si = pl.strips == 4 ? 2 : pl.strips == 2 ? 1 : 0;
+  int ki;
+  KFn kfn;
+  if (!pl.cluster) {
+    ki = pl.variant;
+    kfn = kstream[zi][pl.variant];
+  } else if (pl.variant == kPairVariant) {
+    ki = 10 + si;
+    kfn = kpair[zi][si];
+  } else if (pl.strips == 4) {
+    ki = 4 + pl.variant;
+    kfn = kcluster[zi][pl.variant];
+  } else {
+    ki = 8 + si;
+    kfn = knarrow[zi][si];
+  }
   static std::mutex mu;
-  static size_t attr_smem[2][10] = {};
+  static size_t attr_smem[2][13] = {};
   {
     std::lock_guard<std::mutex> lk(mu);
     size_t& done = attr_smem[zi][ki];
@@ -703,6 +754,10 @@ bool w4_gemv_mma_tuning(std::string_view key, int value) {
   }
   if (key == "w4_gemv_mma.cluster") {
     g_cluster_mode.store(value);
+    return true;
+  }
+  if (key == "w4_gemv_mma.pair") {
+    g_pair.store(value);
     return true;
   }
   if (key == "w4_gemv_mma.sleep") {

@@ -67,10 +67,14 @@ def test_attention_vs_oracle(sg, oracle_mod, dtype, B, H, Hkv, S, D, causal):
     close(got, want)
 
 
+@pytest.mark.parametrize("kernel", [1, 2, 0], ids=["cluster", "key-parallel", "generic"])
 @pytest.mark.parametrize("Skv,Sq,H,Hkv,D", [(768, 1, 32, 8, 64), (4096, 1, 28, 4, 128), (1000, 3, 8, 8, 64),
-                                            (64, 1, 4, 2, 32)])
-def test_decode_against_kv_cache(sg, oracle_mod, Skv, Sq, H, Hkv, D):
-    """Queries at the end of a strided KV cache (capacity > S_kv), split-K."""
+                                            (64, 1, 4, 2, 32), (8192, 1, 28, 4, 128), (37, 2, 16, 2, 64),
+                                            (300, 4, 28, 4, 128)])
+def test_decode_against_kv_cache(sg, oracle_mod, kernel, Skv, Sq, H, Hkv, D):
+    """Queries at the end of a strided KV cache (capacity > S_kv), split-K, with
+    each decode kernel: the cluster of key splits merged in distributed shared
+    memory, the key-parallel kernel plus a combine kernel, the generic one."""
     rng = np.random.default_rng(Skv)
     cap = Skv + 37
     q = rng.standard_normal((2, H, Sq, D)).astype(np.float16)
@@ -78,7 +82,32 @@ def test_decode_against_kv_cache(sg, oracle_mod, Skv, Sq, H, Hkv, D):
     vc = rng.standard_normal((2, Hkv, cap, D)).astype(np.float16)
     want = oracle_mod.flash_attention(q, np.ascontiguousarray(kc[:, :, :Skv]), np.ascontiguousarray(vc[:, :, :Skv]),
                                       causal=True, q_pos0=Skv - Sq).astype(np.float32)
-    got = sg.flash_attention(dev(q), dev(kc), dev(vc), causal=True, q_pos0=-1, decode=True, kv_len=Skv)
+    try:
+        sg.set_tuning("attn.decode_kernel", kernel)
+        got = sg.flash_attention(dev(q), dev(kc), dev(vc), causal=True, q_pos0=-1, decode=True, kv_len=Skv)
+        got2 = sg.flash_attention(dev(q), dev(kc), dev(vc), causal=True, q_pos0=-1, decode=True, kv_len=Skv)
+    finally:
+        sg.set_tuning("attn.decode_kernel", 1)
+    close(got.float().cpu().numpy(), want)
+    assert torch.equal(got, got2)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_decode_cluster_kernel_io_types(sg, oracle_mod, dtype):
+    """fp32 and bf16 caches through the cluster decode kernel (head_dim 64)."""
+    rng = np.random.default_rng(7)
+    Skv, Sq, H, Hkv, D = 700, 1, 32, 8, 64
+    q = rng.standard_normal((1, H, Sq, D)).astype(np.float32)
+    kc = rng.standard_normal((1, Hkv, Skv, D)).astype(np.float32)
+    vc = rng.standard_normal((1, Hkv, Skv, D)).astype(np.float32)
+    if dtype == "f32":
+        want = oracle_mod.flash_attention(q, kc, vc, causal=True, q_pos0=Skv - Sq)
+        t = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    else:
+        q, kc, vc = (oracle_mod.bf16_bits_to_f32(oracle_mod.f32_to_bf16_bits(a)) for a in (q, kc, vc))
+        want = oracle_mod.flash_attention(q, kc, vc, causal=True, q_pos0=Skv - Sq)
+        t = lambda a: torch.from_numpy(a).cuda().to(torch.bfloat16)  # noqa: E731
+    got = sg.flash_attention(t(q), t(kc), t(vc), causal=True, q_pos0=-1, decode=True)
     close(got.float().cpu().numpy(), want)
 
 

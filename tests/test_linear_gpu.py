@@ -317,7 +317,7 @@ def test_fp16_gemv_vs_oracle(sg, oracle_mod, M, K, N):
     close(C.cpu().numpy(), want)
 
 
-@pytest.mark.parametrize("cluster", [2, 1, 0])
+@pytest.mark.parametrize("cluster", [2, 1, 0, "one-block-per-sm"])
 @pytest.mark.parametrize("K,N,gs", [
     (4096, 14336, 32),        # benchmark shape
     (2048, 8192, 64),
@@ -328,8 +328,9 @@ def test_fp16_gemv_vs_oracle(sg, oracle_mod, M, K, N):
     (64, 512 * 300, 64),      # one chunk per tile: ranges over 3 tiles
 ])
 def test_int4_cluster_and_stream_k_splits(sg, oracle_mod, cluster, K, N, gs):
-    """Tile-aligned cluster split (partials reduced in distributed shared memory)
-    and the stream-K split (partials of shared tiles reduced through scratch)
+    """Tile-aligned cluster split (partials reduced in distributed shared memory;
+    one 16-warp or two 8-warp blocks per SM) and the stream-K split (partials
+    of shared tiles reduced through scratch)
     give the oracle's result, repeatably; the static-weight launch (weights
     requested before the dependency wait) gives the same bits."""
     from silicongraph_b200 import _lib
@@ -337,6 +338,9 @@ def test_int4_cluster_and_stream_k_splits(sg, oracle_mod, cluster, K, N, gs):
     x = np.random.default_rng(K + 1).standard_normal((1, K)).astype(np.float32)
     want = oracle_mod.matmul_int4_grouped(x, B, S, Z, K, N, gs, c_dt=oracle_mod.DT_F32)
     try:
+        if cluster == "one-block-per-sm":  # no two-blocks-per-SM cluster shapes
+            sg.set_tuning("w4_gemv_mma.pair", 0)
+            cluster = 1
         sg.set_tuning("w4_gemv_mma.cluster", cluster)
         args = (t(x), t(B), t(S), t(Z), K, N, gs)
         C = sg.matmul_int4_grouped(*args, out_dtype=torch.float32)
@@ -344,6 +348,7 @@ def test_int4_cluster_and_stream_k_splits(sg, oracle_mod, cluster, K, N, gs):
         C3 = sg.matmul_int4_grouped(*args, out_dtype=torch.float32, flags=_lib.SG_MM_STATIC_WEIGHTS)
     finally:
         sg.set_tuning("w4_gemv_mma.cluster", 1)
+        sg.set_tuning("w4_gemv_mma.pair", 1)
     close(C.cpu().numpy(), want)
     assert torch.equal(C, C2)
     assert torch.equal(C, C3)
