@@ -785,29 +785,45 @@ def run_decode(args):
 
     from silicongraph_b200 import armpack, sdk
 
+    import datetime
+
+    import torch.distributed as dist
+
     rank, local_rank, world = rank_env()
+    tp = args.workload == "decode_llama1b_tp"
     torch.cuda.set_device(local_rank)
     os.environ["SG_DEVICE"] = str(local_rank)
+    if world > 1:  # host-side group: the NCCL id of a tensor-parallel session, and max-over-ranks timing
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
     c = DECODE_CFG
     cfg = armpack.llama_config(layers=c["layers"], hidden=c["hidden"], heads=c["heads"], kv_heads=c["kv_heads"],
                                head_dim=c["head_dim"], ffn=c["ffn"], vocab=c["vocab"], rope_theta=c["rope_theta"])
     prompt_len = 512
     steps = args.steps
+    seed_rank = 0 if tp else rank  # the ranks of one tensor-parallel model share its weights and prompt
+    tp_arg = None
+    if tp:
+        uid = [sdk.tp_unique_id() if rank == 0 else None]
+        if world > 1:
+            dist.broadcast_object_list(uid, src=0)
+        tp_arg = (rank, world, uid[0])
     with tempfile.TemporaryDirectory() as td:
         pkg_path = os.path.join(td, "llama1b_int4")
-        weight_bytes, tensors = build_decode_package(pkg_path, cfg, seed=11 + rank,
+        weight_bytes, tensors = build_decode_package(pkg_path, cfg, seed=11 + seed_rank,
                                                      max_context=prompt_len + steps + args.warmup + 8)
-        rng = np.random.default_rng(5 + rank)
+        rng = np.random.default_rng(5 + seed_rank)
         prompt = rng.integers(0, c["vocab"], prompt_len).astype(np.int32)
         with sdk.Package(pkg_path) as pkg:
             graph = pkg.select(context_length=prompt_len + steps + args.warmup)
-            with graph.session() as s:
+            with graph.session(tp=tp_arg) as s:
                 # warm-up: a full prompt and a few steps (allocations, tensor maps, caches)
                 s.prefill(prompt)
                 for _ in range(args.warmup):
                     s.decode()
                 s.reset()
                 clocks = ClockSampler(torch.cuda.current_device(), interval_ms=5) if rank == 0 else None
+                if world > 1:
+                    dist.barrier()
                 t0 = time.perf_counter()
                 s.prefill(prompt)
                 first = s.decode()                      # the token predicted by the prompt
@@ -816,28 +832,38 @@ def run_decode(args):
                     s.decode()
                 t2 = time.perf_counter()
                 clk = clocks.stop() if clocks else None
-    decode_s = t2 - t1
+    decode_s, ttft_s = t2 - t1, t1 - t0
+    if world > 1:  # the slowest rank
+        tmax = torch.tensor([decode_s, ttft_s], dtype=torch.float64)
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        decode_s, ttft_s = float(tmax[0]), float(tmax[1])
+        dist.destroy_process_group()
     tps = steps / decode_s
+    seqs = 1 if tp else world  # sequences decoded at once over the whole job
     ctx_mid = prompt_len + steps / 2
     kv_read = 2 * c["layers"] * c["kv_heads"] * c["head_dim"] * 2 * ctx_mid
     bytes_per_token = weight_bytes + kv_read
     peak, peak_src = read_peak_hbm()
     line = {
         "metric": "INT4 decode tokens/s (Llama-3.2-1B shape, batch 1)",
-        "value": round(world * tps, 2), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "value": round(seqs * tps, 2), "unit": "tokens/s", "n_gpus": world, "steps": steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * decode_s / steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (random N(0,0.02) weights drawn on the GPU, random prompt ids)",
         "config": {"workload": DECODE_WORKLOAD, "prompt": prompt_len, "decode_steps": steps,
-                   "ttft_ms": round(1e3 * (t1 - t0), 3), "prefill_tokens_per_s": round(prompt_len / (t1 - t0), 1),
+                   "ttft_ms": round(1e3 * ttft_s, 3), "prefill_tokens_per_s": round(prompt_len / ttft_s, 1),
                    "bytes_per_token": int(bytes_per_token),
-                   "parallelism": f"replicas x{world} (one session per GPU)",
-                   "timing": "host clock around armsess_decode calls (each returns the token to the host)"},
-        "roofline": {"bound": "hbm", "achieved": round(bytes_per_token * tps / 1e9, 2), "peak": peak,
-                     "unit": "GB/s", "frac": round(bytes_per_token * tps / 1e9 / peak, 4),
+                   "parallelism": (f"tensor-parallel x{world} (one session over {world} GPUs, NCCL all-reduce "
+                                   "after the o and down projections)") if tp else
+                                  f"replicas x{world} (one session per GPU)",
+                   "timing": "host clock around armsess_decode calls (each returns the token to the host), "
+                             "max over ranks"},
+        "roofline": {"bound": "hbm", "achieved": round(bytes_per_token * tps / 1e9 / (world if tp else 1), 2),
+                     "peak": peak, "unit": "GB/s",
+                     "frac": round(bytes_per_token * tps / 1e9 / (world if tp else 1) / peak, 4),
                      "peak_source": f"{peak_src} hbm_gbs", "traffic": None,
-                     "achieved_basis": "weights + KV cache bytes per token x decode tokens/s"},
-        "e2e": {"value": round(world * tps, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                     "achieved_basis": "weights + KV cache bytes per token x decode tokens/s, per GPU"},
+        "e2e": {"value": round(seqs * tps, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 8},
         "gpu_launches": steps * (10 * c["layers"] + 4),
         "clocks": clk,
@@ -935,10 +961,13 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--ref-budget-s", type=float, default=120.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["gemv_int4", *PF_WORKLOADS, *ATTN_WORKLOADS, "decode_llama1b"],
+    ap.add_argument("--workload", choices=["gemv_int4", *PF_WORKLOADS, *ATTN_WORKLOADS, "decode_llama1b",
+                                           "decode_llama1b_tp"],
                     default="gemv_int4",
                     help="gemv_int4 (default): the decode GEMV; prefill_int4 / prefill_int8: the prefill GEMM; "
-                         "attn_prefill / attn_small: flash attention")
+                         "attn_prefill / attn_small: flash attention; decode_llama1b: Llama-1B-shape decode "
+                         "through the SDK (one session per GPU); decode_llama1b_tp: the same model "
+                         "tensor-parallel over all GPUs")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -954,7 +983,7 @@ def main():
         run_prefill(args)
     elif args.workload in ATTN_WORKLOADS:
         run_attention(args)
-    elif args.workload == "decode_llama1b":
+    elif args.workload in ("decode_llama1b", "decode_llama1b_tp"):
         run_decode(args)
     else:
         run_ours(args)

@@ -296,6 +296,16 @@ SgStatus sg_swiglu_rows(const void* gate_up, void* y, int32_t rows, int32_t ffn,
  * logprob != NULL, logprob[r] = its log-softmax value. */
 SgStatus sg_argmax_logprob(const float* logits, int32_t rows, int32_t n, int32_t* out, float* logprob, void* stream);
 
+/* Greedy token across a vocabulary split over ranks (tensor parallelism).
+ * pack: from this rank's logits shard, its local argmax idx and local
+ * log-prob, writes out3 = {max logit, local log-sum-exp, vocab0 + idx}.
+ * pick: from the ranks' triples in rank order ([world][3]), writes the
+ * global greedy token (first rank among equal maxima, i.e. the lowest
+ * vocabulary index) and its log-prob over the whole vocabulary. */
+SgStatus sg_tp_argmax_pack(const float* logits, const int32_t* idx, const float* logprob, int32_t vocab0,
+                           float* out3, void* stream);
+SgStatus sg_tp_argmax_pick(const float* all3, int32_t world, int32_t* next, float* logprob, void* stream);
+
 /* in [heads, tokens, head_dim] -> out [tokens, heads, head_dim]. */
 SgStatus sg_head_transpose(const void* in, void* out, int32_t heads, int32_t tokens, int32_t head_dim,
                            int32_t io_dtype, void* stream);

@@ -5,6 +5,8 @@
 #ifndef SG_SDK_EXT_H_
 #define SG_SDK_EXT_H_
 
+#include <stdint.h>
+
 #include "armcc_sdk.h"
 
 #ifdef __cplusplus
@@ -19,6 +21,49 @@ ArmStatus sg_session_last_logits(ArmSession* sess, float* host_out, uint32_t n);
 
 /* Number of tokens in the session's KV cache. */
 uint32_t sg_session_position(const ArmSession* sess);
+
+/* ---- tensor parallelism --------------------------------------------------
+ * One session spread over `world` processes, one GPU each, in the Megatron
+ * layout: the q|k|v and gate|up projections are split by output columns
+ * (query heads with their kv heads, FFN columns), the output and down
+ * projections by input rows, the LM head by vocabulary columns; embedding
+ * and norms are replicated.  After each row-split projection the partial
+ * hidden states are summed with an NCCL all-reduce; the greedy token is
+ * picked from the ranks' (max, log-sum-exp, index) triples after an NCCL
+ * all-gather, so every rank emits the same token. */
+typedef struct SgTpModel {
+  int32_t hidden, heads, kv_heads, head_dim, ffn, vocab, group_size;
+} SgTpModel;
+
+typedef struct SgTpShard {
+  int32_t q_head0, q_head1;   /* query heads [q_head0, q_head1)                       */
+  int32_t kv_head0, kv_head1; /* kv heads [kv_head0, kv_head1); with more ranks than
+                                 kv heads each rank holds one kv head, replicated    */
+  int32_t ffn0, ffn1;         /* gate / up columns and down rows [ffn0, ffn1)        */
+  int32_t vocab0, vocab1;     /* LM head columns [vocab0, vocab1)                    */
+} SgTpShard;
+
+/* The shard of `rank` in a group of `world` (host only, no device needed).
+ * ARMCC_ERR_UNSUPPORTED when the shapes do not split: heads must divide
+ * among the ranks through their kv heads, FFN and vocabulary splits fall on
+ * group (resp. 16-column) boundaries, and every o / down row split on a
+ * quantisation group boundary. */
+ArmStatus sg_tp_shard(const SgTpModel* model, int32_t rank, int32_t world, SgTpShard* out);
+
+/* A fresh 128-byte NCCL unique id: create it on one rank and give the same
+ * bytes to every rank's sg_session_create_tp. */
+ArmStatus sg_tp_unique_id(uint8_t id_out[128]);
+
+/* This rank's session of a tensor-parallel group.  Collective: every rank
+ * of the group calls it with the same id and world, each on its own GPU
+ * (SG_DEVICE, else the current device).  NCCL is loaded at run time
+ * (libnccl.so.2, or the path in SG_NCCL_LIBRARY). */
+ArmSession* sg_session_create_tp(ArmGraph* graph, const ArmSessionOptions* opts, int32_t rank, int32_t world,
+                                 const uint8_t id[128]);
+
+/* The vocabulary range [lo, hi) whose logits sg_session_last_logits returns
+ * (the whole vocabulary unless the session is tensor-parallel). */
+void sg_session_vocab_range(const ArmSession* sess, uint32_t* lo, uint32_t* hi);
 
 #ifdef __cplusplus
 }

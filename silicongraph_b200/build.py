@@ -89,7 +89,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
     newest = max(os.path.getmtime(o) for o in objs)
     if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < newest:
         tmp = LIB + ".tmp"
-        cmd = [nvcc(), *ARCH, "-shared", "-o", tmp, *objs, "-cudart", "static", "-lcuda", "-lz",
+        cmd = [nvcc(), *ARCH, "-shared", "-o", tmp, *objs, "-cudart", "static", "-lcuda", "-lz", "-ldl",
                "-L/usr/local/cuda/lib64/stubs"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:

@@ -222,6 +222,41 @@ int grid_of(int64_t n) {
   return (int)(b < 1 ? 1 : (b > 148 * 16 ? 148 * 16 : b));
 }
 
+// Tensor-parallel greedy token: per-rank triple, then the pick over ranks.
+__global__ void tp_argmax_pack_kernel(const float* __restrict__ logits, const int32_t* __restrict__ idx,
+                                      const float* __restrict__ logprob, int vocab0, float* __restrict__ out) {
+  sgd::pdl_wait();
+  sgd::pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    const int i = *idx;
+    const float m = logits[i];
+    out[0] = m;
+    out[1] = m - *logprob;  // log-sum-exp of this rank's shard
+    out[2] = (float)(vocab0 + i);
+  }
+}
+
+__global__ void tp_argmax_pick_kernel(const float* __restrict__ all, int world, int32_t* __restrict__ next,
+                                      float* __restrict__ logprob) {
+  sgd::pdl_wait();
+  sgd::pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    int best = 0;
+    float M = all[0], Lmax = all[1];
+    for (int r = 1; r < world; ++r) {
+      if (all[3 * r] > M) {
+        M = all[3 * r];
+        best = r;
+      }
+      Lmax = fmaxf(Lmax, all[3 * r + 1]);
+    }
+    float s = 0.f;
+    for (int r = 0; r < world; ++r) s += expf(all[3 * r + 1] - Lmax);
+    *next = (int32_t)all[3 * best + 2];
+    if (logprob) *logprob = M - (Lmax + logf(s));
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -304,6 +339,21 @@ SgStatus sg_argmax_logprob(const float* logits, int32_t rows, int32_t n, int32_t
                               static_cast<float*>(ws)));
   SG_CUDA_TRY(sgd::launch_pdl(argmax_merge_kernel, dim3(rows), dim3(32), 0, cs, logits, (int)n, slices,
                               static_cast<const float*>(ws), out, logprob));
+  return SG_OK;
+}
+
+SgStatus sg_tp_argmax_pack(const float* logits, const int32_t* idx, const float* logprob, int32_t vocab0,
+                           float* out3, void* stream) {
+  SG_CHECK_ARG(logits && idx && logprob && out3, "sg_tp_argmax_pack: NULL pointer");
+  SG_CUDA_TRY(sgd::launch_pdl(tp_argmax_pack_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), logits,
+                              idx, logprob, (int)vocab0, out3));
+  return SG_OK;
+}
+
+SgStatus sg_tp_argmax_pick(const float* all3, int32_t world, int32_t* next, float* logprob, void* stream) {
+  SG_CHECK_ARG(all3 && next && world >= 1, "sg_tp_argmax_pick: bad argument");
+  SG_CUDA_TRY(sgd::launch_pdl(tp_argmax_pick_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), all3,
+                              (int)world, next, logprob));
   return SG_OK;
 }
 

@@ -19,7 +19,16 @@
 // and runs Llama-style blocks: rmsnorm -> QKV -> rope + KV append -> causal
 // attention -> O -> residual rmsnorm -> gate|up -> SwiGLU -> down, then the
 // final norm, the LM head (fp32 logits) and a greedy argmax.
+//
+// A tensor-parallel session (sg_session_create_tp) holds one rank's shard of
+// every linear, cut out of the full weight image on the device with strided
+// copies: q|k|v and gate|up by output columns, o and down by input rows on
+// quantisation-group boundaries, the LM head by vocabulary columns.  NCCL
+// (loaded with dlopen, so the library never pins an NCCL version of its own)
+// sums the row-split outputs and gathers the ranks' greedy candidates.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <chrono>
@@ -68,8 +77,90 @@ struct ModelCfg {
   bool zeros = true;
   bool lm_int4 = true;
   int max_context = 4096, max_chunk = 512;
+  int vocab_global = 0;  // rows of the embedding table (vocab is the LM head's columns here)
   int nqkv() const { return (heads + 2 * kv_heads) * head_dim; }
 };
+
+// ------------------------------------------------------------------ NCCL at run time
+struct NcclApi {
+  bool ok = false;
+  std::string why;
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+// The NCCL the host process already loaded (e.g. PyTorch's), else SG_NCCL_LIBRARY, else libnccl.so.2.
+const NcclApi& nccl_api() {
+  static const NcclApi api = [] {
+    NcclApi a;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) {
+      const char* path = getenv("SG_NCCL_LIBRARY");
+      h = dlopen(path && *path ? path : "libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    }
+    if (!h) {
+      const char* e = dlerror();
+      a.why = std::string("cannot load NCCL: ") + (e ? e : "unknown error");
+      return a;
+    }
+    a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    a.comm_init_rank = reinterpret_cast<decltype(a.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    a.all_gather = reinterpret_cast<decltype(a.all_gather)>(dlsym(h, "ncclAllGather"));
+    a.comm_destroy = reinterpret_cast<decltype(a.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
+    a.ok = a.get_unique_id && a.comm_init_rank && a.all_reduce && a.all_gather && a.comm_destroy && a.error_string;
+    if (!a.ok) a.why = "the loaded NCCL library lacks a required symbol";
+    return a;
+  }();
+  return api;
+}
+
+// ------------------------------------------------------------------ tensor-parallel shard
+bool tp_plan(const SgTpModel& m, int rank, int world, SgTpShard* s, std::string* why) {
+  auto fail = [&](const std::string& w) {
+    *why = w;
+    return false;
+  };
+  if (world < 1 || rank < 0 || rank >= world) return fail("rank outside [0, world)");
+  if (m.heads <= 0 || m.kv_heads <= 0 || m.heads % m.kv_heads != 0 || m.head_dim <= 0 || m.ffn <= 0 ||
+      m.vocab <= 0 || m.group_size <= 0 || m.hidden <= 0)
+    return fail("bad model dimensions");
+  const int G = m.heads / m.kv_heads, D = m.head_dim, gs = m.group_size;
+  if (world <= m.kv_heads) {
+    if (m.kv_heads % world != 0) return fail("kv heads do not divide among the ranks");
+    s->kv_head0 = (int)((int64_t)rank * m.kv_heads / world);
+    s->kv_head1 = (int)((int64_t)(rank + 1) * m.kv_heads / world);
+    s->q_head0 = s->kv_head0 * G;
+    s->q_head1 = s->kv_head1 * G;
+  } else {
+    if (world % m.kv_heads != 0) return fail("ranks do not divide among the kv heads");
+    const int R = world / m.kv_heads, kv = rank / R, sub = rank % R;
+    if (G < R) return fail("fewer query heads per kv head than ranks sharing it");
+    s->kv_head0 = kv;
+    s->kv_head1 = kv + 1;
+    s->q_head0 = kv * G + sub * G / R;
+    s->q_head1 = kv * G + (sub + 1) * G / R;
+  }
+  if ((s->q_head0 * D) % gs != 0 || (s->q_head1 * D) % gs != 0)
+    return fail("the output projection's row split falls inside a quantisation group");
+  if (((s->q_head1 - s->q_head0 + 2 * (s->kv_head1 - s->kv_head0)) * D) % 16 != 0)
+    return fail("the q|k|v shard is not a multiple of 16 columns");
+  if (m.ffn % gs != 0 || m.ffn / gs < world) return fail("the FFN does not split on quantisation groups");
+  const int64_t gf = m.ffn / gs;
+  s->ffn0 = (int)(rank * gf / world * gs);
+  s->ffn1 = (int)((rank + 1) * gf / world * gs);
+  if (m.vocab % 16 != 0 || m.vocab / 16 < world) return fail("the vocabulary does not split on 16 columns");
+  const int64_t vb = m.vocab / 16;
+  s->vocab0 = (int)(rank * vb / world * 16);
+  s->vocab1 = (int)((rank + 1) * vb / world * 16);
+  return true;
+}
 
 // ------------------------------------------------------------------ activation plan
 // Greedy best-fit interval colouring (memory_planner.cpp:172-234): buffers in
@@ -144,6 +235,8 @@ Plan make_plan(const ModelCfg& c, int T) {
       {"act", (uint64_t)T * c.ffn * e, kOpSwiglu, kOpDown},
       {"down", T * H * e, kOpDown, kOpFinalNorm},
       {"logits", (uint64_t)c.vocab * 4, kOpLm, kOpArgmax},
+      {"tp_mine", 16, kOpArgmax, kOpArgmax},
+      {"tp_all", 16 * 64, kOpArgmax, kOpArgmax},
   };
   p.bytes = plan_offsets(p.bufs, 256);
   return p;
@@ -203,6 +296,7 @@ bool parse_cuda_graph(ArmPackage_* pkg, ArmGraph_* g, std::string* why) {
   c.head_dim = (int)m["head_dim"].integer(c.heads ? c.hidden / c.heads : 0);
   c.ffn = (int)m["intermediate_size"].integer();
   c.vocab = (int)m["vocab_size"].integer();
+  c.vocab_global = c.vocab;
   c.rope_theta = (float)m["rope_theta"].number(10000.0);
   c.rms_eps = (float)m["rms_norm_eps"].number(1e-5);
   const Json& qz = j["quant"];
@@ -297,11 +391,18 @@ struct ArmSession_ {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t graph_exec = nullptr;
   int32_t* h_pos = nullptr;  // pinned
+  // tensor parallelism (tp_world == 1: a whole-model session)
+  int tp_rank = 0, tp_world = 1;
+  SgTpShard shard{};
+  ncclComm_t comm = nullptr;
+  int* tp_flag = nullptr;  // device word for the ranks' agreement on setup
 
   ~ArmSession_() {
     if (st) cudaStreamSynchronize(st);
     if (graph_exec) cudaGraphExecDestroy(graph_exec);
     if (graph) cudaGraphDestroy(graph);
+    if (comm) nccl_api().comm_destroy(comm);  // after the graphs that hold its calls
+    if (tp_flag) cudaFree(tp_flag);
     if (slab) cudaFree(slab);
     if (h_pos) cudaFreeHost(h_pos);
     if (st) cudaStreamDestroy(st);
@@ -325,6 +426,17 @@ ArmStatus fail_sg(SgStatus s, const char* what) {
     const SgStatus s_ = (call);               \
     if (s_ != SG_OK) return fail_sg(s_, what); \
   } while (0)
+
+// Sums a row-split projection's fp16 output over the ranks (in place).
+ArmStatus tp_sum(ArmSession_* S, void* buf, size_t count) {
+  if (S->tp_world == 1) return ARMCC_OK;
+  const ncclResult_t e = nccl_api().all_reduce(buf, buf, count, ncclHalf, ncclSum, S->comm, S->st);
+  if (e != ncclSuccess) {
+    set_err("ncclAllReduce failed: %s", nccl_api().error_string(e));
+    return ARMCC_ERR_RUNTIME;
+  }
+  return ARMCC_OK;
+}
 
 ArmStatus linear(ArmSession_* S, const Linear& L, const void* A, void* C, int M, int c_dt) {
   SgMatMulParams p{};
@@ -356,7 +468,7 @@ ArmStatus forward(ArmSession_* S, int T, bool from_next, bool dev_pos = false) {
   cudaStream_t st = S->st;
   const int H = c.hidden, D = c.head_dim;
   const int32_t* ids = from_next ? S->buf<int32_t>("next") : S->buf<int32_t>("ids");
-  SG_TRY(sg_embedding(S->embed, ids, S->buf<void>("x_emb"), T, H, c.vocab, SG_DT_F16, st), "embedding");
+  SG_TRY(sg_embedding(S->embed, ids, S->buf<void>("x_emb"), T, H, c.vocab_global, SG_DT_F16, st), "embedding");
   if (cudaMemsetAsync(S->buf<void>("resid"), 0, (size_t)T * H * 2, st) != cudaSuccess) {
     set_err("cudaMemsetAsync failed");
     return ARMCC_ERR_RUNTIME;
@@ -402,12 +514,14 @@ ArmStatus forward(ArmSession_* S, int T, bool from_next, bool dev_pos = false) {
       attn_rows = S->buf<void>("attn_t");
     }
     if ((r = linear(S, S->o[l], attn_rows, S->buf<void>("o"), T, SG_DT_F16)) != ARMCC_OK) return r;
+    if ((r = tp_sum(S, S->buf<void>("o"), (size_t)T * H)) != ARMCC_OK) return r;
     SG_TRY(sg_rmsnorm(S->buf<void>("o"), S->buf<void>("resid"), S->post_norm[l], S->buf<void>("xnorm"), T, H,
                       c.rms_eps, SG_DT_F16, st),
            "post-attention rmsnorm");
     if ((r = linear(S, S->gu[l], S->buf<void>("xnorm"), S->buf<void>("gu"), T, SG_DT_F16)) != ARMCC_OK) return r;
     SG_TRY(sg_swiglu_rows(S->buf<void>("gu"), S->buf<void>("act"), T, c.ffn, SG_DT_F16, st), "SwiGLU");
     if ((r = linear(S, S->down[l], S->buf<void>("act"), S->buf<void>("down"), T, SG_DT_F16)) != ARMCC_OK) return r;
+    if ((r = tp_sum(S, S->buf<void>("down"), (size_t)T * H)) != ARMCC_OK) return r;
   }
   // last token: final norm, LM head, greedy token
   const size_t last = (size_t)(T - 1) * H * 2;
@@ -432,6 +546,21 @@ ArmStatus forward(ArmSession_* S, int T, bool from_next, bool dev_pos = false) {
   SG_TRY(sg_argmax_logprob(S->buf<float>("logits"), 1, c.vocab, S->buf<int32_t>("next"), S->buf<float>("logprob"),
                            st),
          "argmax");
+  if (S->tp_world > 1) {
+    // every rank's (max, log-sum-exp, index), gathered in rank order, then the global pick
+    SG_TRY(sg_tp_argmax_pack(S->buf<float>("logits"), S->buf<int32_t>("next"), S->buf<float>("logprob"),
+                             S->shard.vocab0, S->buf<float>("tp_mine"), st),
+           "tensor-parallel argmax");
+    const ncclResult_t e = nccl_api().all_gather(S->buf<float>("tp_mine"), S->buf<float>("tp_all"), 3, ncclFloat,
+                                                 S->comm, st);
+    if (e != ncclSuccess) {
+      set_err("ncclAllGather failed: %s", nccl_api().error_string(e));
+      return ARMCC_ERR_RUNTIME;
+    }
+    SG_TRY(sg_tp_argmax_pick(S->buf<float>("tp_all"), S->tp_world, S->buf<int32_t>("next"), S->buf<float>("logprob"),
+                             st),
+           "tensor-parallel argmax");
+  }
   S->pos += T;
   return ARMCC_OK;
 }
@@ -523,6 +652,357 @@ bool bind_linear(ArmGraph_* g, const std::string& name, char* wbase, int K, int 
   out->K = K;
   out->N = N;
   return true;
+}
+
+// One rank's cut of a linear in the reference INT4 layout: input rows
+// [r0, r1) (on quantisation-group boundaries) and the listed output column
+// ranges, packed side by side.  With dry only the space is reserved.
+struct ColRange {
+  int c0, c1;
+};
+
+bool shard_linear(ArmGraph_* g, const std::string& name, int K, int N, int r0, int r1,
+                  std::initializer_list<ColRange> cols, const char* full, char* wbase, uint64_t* cursor, bool dry,
+                  cudaStream_t st, Linear* out, std::string* why) {
+  Linear whole;
+  if (!bind_linear(g, name, const_cast<char*>(full), K, N, &whole, why)) return false;
+  const int gs = g->cfg.group_size;
+  const int Kl = r1 - r0;
+  int Nl = 0;
+  for (const ColRange& c : cols) Nl += c.c1 - c.c0;
+  const uint64_t KPl = (uint64_t)(Kl + 1) / 2, Gl = (uint64_t)(Kl + gs - 1) / gs;
+  const uint64_t p0 = (uint64_t)r0 / 2, g0 = (uint64_t)r0 / gs;
+  const uint64_t offB = *cursor;
+  *cursor = align_up(*cursor + KPl * Nl, 256);
+  const uint64_t offS = *cursor;
+  *cursor = align_up(*cursor + Gl * Nl * 2, 256);
+  uint64_t offZ = 0;
+  if (whole.zeros) {
+    offZ = *cursor;
+    *cursor = align_up(*cursor + Gl * Nl, 256);
+  }
+  out->qw = reinterpret_cast<const uint8_t*>(wbase + offB);
+  out->scales = wbase + offS;
+  out->zeros = whole.zeros ? reinterpret_cast<const int8_t*>(wbase + offZ) : nullptr;
+  out->K = Kl;
+  out->N = Nl;
+  if (dry) return true;
+  const char* qsrc = reinterpret_cast<const char*>(whole.qw);
+  const char* ssrc = static_cast<const char*>(whole.scales);
+  const char* zsrc = reinterpret_cast<const char*>(whole.zeros);
+  uint64_t dc = 0;
+  for (const ColRange& c : cols) {
+    const size_t w = (size_t)(c.c1 - c.c0);
+    if (cudaMemcpy2DAsync(wbase + offB + dc, Nl, qsrc + p0 * N + c.c0, N, w, KPl, cudaMemcpyDeviceToDevice, st) !=
+            cudaSuccess ||
+        cudaMemcpy2DAsync(wbase + offS + dc * 2, (size_t)Nl * 2, ssrc + (g0 * N + c.c0) * 2, (size_t)N * 2, w * 2, Gl,
+                          cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+        (zsrc && cudaMemcpy2DAsync(wbase + offZ + dc, Nl, zsrc + g0 * N + c.c0, N, w, Gl, cudaMemcpyDeviceToDevice,
+                                   st) != cudaSuccess)) {
+      cudaGetLastError();
+      *why = "copying the shard of " + name + " failed";
+      return false;
+    }
+    dc += w;
+  }
+  return true;
+}
+
+// Session of rank `rank` in a group of `world` (world 1: the whole model, no NCCL).
+ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int rank, int world, const uint8_t* id) {
+  const char* fn = world > 1 ? "sg_session_create_tp" : "armgraph_create_session";
+  if (!graph) {
+    set_err("%s: graph is NULL", fn);
+    return nullptr;
+  }
+  if (!graph->runnable) {
+    set_err("%s: %s", fn, graph->why_not.c_str());
+    return nullptr;
+  }
+  if (opts && !opts->use_gpu) {
+    set_err("%s: use_gpu is false, but this library only runs on the GPU", fn);
+    return nullptr;
+  }
+  auto S = std::make_unique<ArmSession_>();
+  S->g = graph;
+  S->c = graph->cfg;
+  S->tp_rank = rank;
+  S->tp_world = world;
+  const ModelCfg& gc = graph->cfg;
+  std::string why;
+  if (world > 1) {
+    if (!gc.lm_int4) {
+      set_err("%s: tensor parallelism needs an INT4 LM head", fn);
+      return nullptr;
+    }
+    if (world > 64) {
+      set_err("%s: at most 64 ranks", fn);
+      return nullptr;
+    }
+    const SgTpModel m{gc.hidden, gc.heads, gc.kv_heads, gc.head_dim, gc.ffn, gc.vocab, gc.group_size};
+    if (!tp_plan(m, rank, world, &S->shard, &why)) {
+      set_err("%s: %s", fn, why.c_str());
+      return nullptr;
+    }
+    if (!nccl_api().ok) {
+      set_err("%s: %s", fn, nccl_api().why.c_str());
+      return nullptr;
+    }
+    S->c.heads = S->shard.q_head1 - S->shard.q_head0;
+    S->c.kv_heads = S->shard.kv_head1 - S->shard.kv_head0;
+    S->c.ffn = S->shard.ffn1 - S->shard.ffn0;
+    S->c.vocab = S->shard.vocab1 - S->shard.vocab0;
+  } else {
+    S->shard = SgTpShard{0, gc.heads, 0, gc.kv_heads, 0, gc.ffn, 0, gc.vocab};
+  }
+  const ModelCfg& c = S->c;
+  if (const char* d = getenv("SG_DEVICE")) S->dev = atoi(d);
+  else if (cudaGetDevice(&S->dev) != cudaSuccess) S->dev = 0;
+  if (cudaSetDevice(S->dev) != cudaSuccess) {
+    cudaGetLastError();
+    set_err("%s: cannot use CUDA device %d", fn, S->dev);
+    return nullptr;
+  }
+  if (cudaStreamCreateWithFlags(&S->st, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMallocHost(&S->h_pos, sizeof(int32_t)) != cudaSuccess) {
+    cudaGetLastError();
+    set_err("%s: cannot create the session's stream", fn);
+    return nullptr;
+  }
+  if (const char* gflag = getenv("SG_DECODE_GRAPH")) S->use_graph = atoi(gflag) != 0;
+  if (world > 1) {
+    ncclUniqueId uid;
+    memcpy(uid.internal, id, sizeof uid.internal);
+    if (cudaMalloc(&S->tp_flag, 256) != cudaSuccess) {
+      cudaGetLastError();
+      set_err("%s: cannot allocate device memory", fn);
+      return nullptr;
+    }
+    const ncclResult_t e = nccl_api().comm_init_rank(&S->comm, world, uid, rank);
+    if (e != ncclSuccess) {
+      S->comm = nullptr;
+      set_err("%s: ncclCommInitRank failed: %s", fn, nccl_api().error_string(e));
+      return nullptr;
+    }
+  }
+  // weight file
+  const uint8_t* wdata = nullptr;
+  uint64_t wbytes = 0;
+  std::string err;
+  if (!graph->pkg->box.map_entry(graph->weight_path, &wdata, &wbytes, &err)) {
+    set_err("%s: %s", fn, err.c_str());
+    return nullptr;
+  }
+  for (auto& kv : graph->tensors)
+    if (kv.second.offset + kv.second.bytes > wbytes) {
+      set_err("%s: tensor %s lies outside the weight file", fn, kv.first.c_str());
+      return nullptr;
+    }
+  // scratch sizes of the linear kernels (largest over the shapes and token counts used)
+  const int T = c.max_chunk;
+  SgMatMulParams mp{};
+  auto lin_ws = [&](int M, int K, int N, int cdt) {
+    mp = SgMatMulParams{};
+    mp.A = mp.B = mp.scales_B = reinterpret_cast<void*>(256);
+    mp.C = reinterpret_cast<void*>(256);
+    mp.M = M;
+    mp.K = K;
+    mp.N = N;
+    mp.group_size = c.group_size;
+    mp.a_dtype = SG_DT_F16;
+    mp.c_dtype = cdt;
+    return sg_matmul_int4_grouped_workspace_size(&mp);
+  };
+  size_t lws = 0;
+  // every token count a call can see: the row kernels' scratch depends on M
+  // below the tensor-core GEMM's threshold
+  for (int M = 1; M <= T; M = (M < 64 ? M + 1 : (M == T ? T + 1 : std::min(2 * M, T)))) {
+    lws = std::max({lws, lin_ws(M, c.hidden, c.nqkv(), SG_DT_F16), lin_ws(M, c.heads * c.head_dim, c.hidden, SG_DT_F16),
+                    lin_ws(M, c.hidden, 2 * c.ffn, SG_DT_F16), lin_ws(M, c.ffn, c.hidden, SG_DT_F16)});
+  }
+  lws = std::max(lws, lin_ws(1, c.hidden, c.vocab, SG_DT_F32));
+  SgFlashAttentionParams ap{};
+  ap.Q = ap.K = ap.V = ap.O = reinterpret_cast<void*>(256);
+  ap.B = 1;
+  ap.num_heads = c.heads;
+  ap.num_kv_heads = c.kv_heads;
+  ap.head_dim = c.head_dim;
+  ap.causal = 1;
+  ap.io_dtype = SG_DT_F16;
+  ap.S = 1;
+  ap.S_kv = c.max_context;
+  ap.q_pos0 = c.max_context - 1;
+  size_t aws = sg_flash_decode_workspace_size(&ap);
+  ap.S = T;
+  ap.q_pos0 = c.max_context - T;
+  aws = std::max(aws, sg_flash_attention_workspace_size(&ap));
+
+  // weights: the whole file (one rank), or this rank's shards (several)
+  const SgTpShard& sh = S->shard;
+  const int H = gc.hidden, D = gc.head_dim, Hq = gc.heads, Hkv = gc.kv_heads, F = gc.ffn;
+  const uint64_t H2 = (uint64_t)H * 2;
+  auto find = [&](const std::string& n, uint64_t expect) -> const TensorRef* {
+    auto it = graph->tensors.find(n);
+    return (it == graph->tensors.end() || it->second.bytes != expect) ? nullptr : &it->second;
+  };
+  // Places (dry: sizes only) the replicated tensors and every linear shard at
+  // offsets from wbase; returns the bytes used or 0 with `why` set.
+  auto place = [&](const char* full, char* wbase, bool dry) -> uint64_t {
+    uint64_t cur = 0;
+    auto replicate = [&](const std::string& n, uint64_t bytes, const void** dst) -> bool {
+      const TensorRef* r = find(n, bytes);
+      if (!r) {
+        why = "tensor " + n + " missing or of the wrong size";
+        return false;
+      }
+      const uint64_t off = cur;
+      cur = align_up(cur + bytes, 256);
+      *dst = wbase + off;
+      if (!dry && cudaMemcpyAsync(wbase + off, full + r->offset, bytes, cudaMemcpyDeviceToDevice, S->st) != cudaSuccess) {
+        cudaGetLastError();
+        why = "copying " + n + " failed";
+        return false;
+      }
+      return true;
+    };
+    S->in_norm.assign(gc.layers, nullptr);
+    S->post_norm.assign(gc.layers, nullptr);
+    S->qkv.assign(gc.layers, Linear{});
+    S->o.assign(gc.layers, Linear{});
+    S->gu.assign(gc.layers, Linear{});
+    S->down.assign(gc.layers, Linear{});
+    if (!replicate("embed_tokens", (uint64_t)gc.vocab_global * H2, &S->embed) ||
+        !replicate("final_norm", H2, &S->final_norm))
+      return 0;
+    for (int l = 0; l < gc.layers; ++l) {
+      const std::string p = "layers." + std::to_string(l) + ".";
+      if (!replicate(p + "input_norm", H2, &S->in_norm[l]) || !replicate(p + "post_norm", H2, &S->post_norm[l]))
+        return 0;
+      const int nq = gc.nqkv();
+      if (!shard_linear(graph, p + "qkv", H, nq, 0, H,
+                        {{sh.q_head0 * D, sh.q_head1 * D},
+                         {(Hq + sh.kv_head0) * D, (Hq + sh.kv_head1) * D},
+                         {(Hq + Hkv + sh.kv_head0) * D, (Hq + Hkv + sh.kv_head1) * D}},
+                        full, wbase, &cur, dry, S->st, &S->qkv[l], &why) ||
+          !shard_linear(graph, p + "o", Hq * D, H, sh.q_head0 * D, sh.q_head1 * D, {{0, H}}, full, wbase, &cur, dry,
+                        S->st, &S->o[l], &why) ||
+          !shard_linear(graph, p + "gate_up", H, 2 * F, 0, H, {{sh.ffn0, sh.ffn1}, {F + sh.ffn0, F + sh.ffn1}}, full,
+                        wbase, &cur, dry, S->st, &S->gu[l], &why) ||
+          !shard_linear(graph, p + "down", F, H, sh.ffn0, sh.ffn1, {{0, H}}, full, wbase, &cur, dry, S->st,
+                        &S->down[l], &why))
+        return 0;
+    }
+    if (!shard_linear(graph, "lm_head", H, gc.vocab, 0, H, {{sh.vocab0, sh.vocab1}}, full, wbase, &cur, dry, S->st,
+                      &S->lm, &why))
+      return 0;
+    return std::max<uint64_t>(cur, 256);
+  };
+  uint64_t w_region = wbytes;
+  if (world > 1) {
+    w_region = place(nullptr, nullptr, true);
+    if (w_region == 0) {
+      set_err("%s: %s", fn, why.c_str());
+      return nullptr;
+    }
+  }
+  // slab layout
+  S->plan = make_plan(c, T);
+  S->kv_head_stride = (int64_t)c.max_context * c.head_dim;
+  S->kv_block = (int64_t)c.kv_heads * S->kv_head_stride;
+  const uint64_t off_w = 0;
+  const uint64_t off_kv = align_up(off_w + w_region, 4096);
+  const uint64_t kv_bytes = (uint64_t)c.layers * 2 * S->kv_block * 2;
+  const uint64_t off_act = align_up(off_kv + kv_bytes, 4096);
+  const uint64_t off_lws = align_up(off_act + S->plan.bytes, 4096);
+  S->lin_ws_bytes = align_up(std::max<size_t>(lws, 4096), 256);
+  const uint64_t off_aws = align_up(off_lws + S->lin_ws_bytes, 4096);
+  S->attn_ws_bytes = align_up(std::max<size_t>(aws, 256), 256);
+  S->slab_bytes = align_up(off_aws + S->attn_ws_bytes, 4096);
+  char* full = nullptr;  // the whole weight image, while the shards are cut (several ranks)
+  bool ok = cudaMalloc(&S->slab, S->slab_bytes) == cudaSuccess;
+  if (ok && world > 1) ok = cudaMalloc(&full, wbytes) == cudaSuccess;
+  if (!ok) cudaGetLastError();
+  if (world > 1) {
+    // every rank learns whether all ranks got their memory before any goes on
+    int bad = ok ? 0 : 1;
+    ncclResult_t e = ncclSuccess;
+    if (cudaMemcpyAsync(S->tp_flag, &bad, 4, cudaMemcpyHostToDevice, S->st) != cudaSuccess ||
+        (e = nccl_api().all_reduce(S->tp_flag, S->tp_flag, 1, ncclInt32, ncclMax, S->comm, S->st)) != ncclSuccess ||
+        cudaMemcpyAsync(&bad, S->tp_flag, 4, cudaMemcpyDeviceToHost, S->st) != cudaSuccess ||
+        cudaStreamSynchronize(S->st) != cudaSuccess)
+      bad = 1;
+    if (bad) ok = false;
+  }
+  if (!ok) {
+    if (full) cudaFree(full);
+    set_err("%s: cannot allocate %llu bytes on device %d (or another rank could not)", fn,
+            (unsigned long long)S->slab_bytes, S->dev);
+    return nullptr;
+  }
+  graph->peak_bytes = std::max(graph->peak_bytes, S->slab_bytes);
+  char* wbase = S->slab + off_w;
+  S->kv = S->slab + off_kv;
+  S->act = S->slab + off_act;
+  S->lin_ws = S->slab + off_lws;
+  S->attn_ws = S->slab + off_aws;
+  auto cleanup_fail = [&](const char* what) -> ArmSession* {
+    if (full) {
+      cudaStreamSynchronize(S->st);
+      cudaFree(full);
+    }
+    set_err("%s: %s", fn, what);
+    return nullptr;
+  };
+  char* image = world > 1 ? full : wbase;
+  if (cudaMemcpyAsync(image, wdata, wbytes, cudaMemcpyHostToDevice, S->st) != cudaSuccess ||
+      cudaMemsetAsync(S->kv, 0, kv_bytes, S->st) != cudaSuccess ||
+      cudaMemsetAsync(S->lin_ws, 0, S->lin_ws_bytes, S->st) != cudaSuccess ||
+      cudaMemsetAsync(S->attn_ws, 0, S->attn_ws_bytes, S->st) != cudaSuccess) {
+    cudaGetLastError();
+    return cleanup_fail("uploading the weights failed");
+  }
+  if (world > 1) {
+    if (place(full, wbase, false) == 0) return cleanup_fail(why.c_str());
+    if (cudaStreamSynchronize(S->st) != cudaSuccess) return cleanup_fail("cutting the weight shards failed");
+    cudaFree(full);
+    full = nullptr;
+    return S.release();
+  }
+  if (cudaStreamSynchronize(S->st) != cudaSuccess) {
+    cudaGetLastError();
+    return cleanup_fail("uploading the weights failed");
+  }
+  // bind tensors of the whole image
+  auto t = [&](const std::string& n, uint64_t expect) -> const void* {
+    const TensorRef* r = find(n, expect);
+    return r ? wbase + r->offset : nullptr;
+  };
+  S->embed = t("embed_tokens", (uint64_t)c.vocab * H2);
+  S->final_norm = t("final_norm", H2);
+  if (!S->embed || !S->final_norm) return cleanup_fail("embed_tokens / final_norm missing or of the wrong size");
+  for (int l = 0; l < c.layers; ++l) {
+    const std::string p = "layers." + std::to_string(l) + ".";
+    S->in_norm.push_back(t(p + "input_norm", H2));
+    S->post_norm.push_back(t(p + "post_norm", H2));
+    if (!S->in_norm.back() || !S->post_norm.back()) return cleanup_fail(("norm weights of layer " + std::to_string(l) + " missing").c_str());
+    Linear a, b, g3, d;
+    if (!bind_linear(graph, p + "qkv", wbase, c.hidden, c.nqkv(), &a, &why) ||
+        !bind_linear(graph, p + "o", wbase, c.heads * c.head_dim, c.hidden, &b, &why) ||
+        !bind_linear(graph, p + "gate_up", wbase, c.hidden, 2 * c.ffn, &g3, &why) ||
+        !bind_linear(graph, p + "down", wbase, c.ffn, c.hidden, &d, &why))
+      return cleanup_fail(why.c_str());
+    S->qkv.push_back(a);
+    S->o.push_back(b);
+    S->gu.push_back(g3);
+    S->down.push_back(d);
+  }
+  if (c.lm_int4) {
+    if (!bind_linear(graph, "lm_head", wbase, c.hidden, c.vocab, &S->lm, &why)) return cleanup_fail(why.c_str());
+  } else {
+    S->lm_f16 = t("lm_head.weight", (uint64_t)c.vocab * H2);
+    if (!S->lm_f16) return cleanup_fail("lm_head.weight missing or of the wrong size");
+  }
+  return S.release();
 }
 
 }  // namespace
@@ -640,158 +1120,7 @@ float armgraph_estimated_tpot_ms(const ArmGraph* graph) { return graph ? graph->
 uint64_t armgraph_peak_memory_bytes(const ArmGraph* graph) { return graph ? graph->peak_bytes : 0; }
 
 ArmSession* armgraph_create_session(ArmGraph* graph, const ArmSessionOptions* opts) {
-  if (!graph) {
-    set_err("armgraph_create_session: graph is NULL");
-    return nullptr;
-  }
-  if (!graph->runnable) {
-    set_err("armgraph_create_session: %s", graph->why_not.c_str());
-    return nullptr;
-  }
-  if (opts && !opts->use_gpu) {
-    set_err("armgraph_create_session: use_gpu is false, but this library only runs on the GPU");
-    return nullptr;
-  }
-  auto S = std::make_unique<ArmSession_>();
-  S->g = graph;
-  S->c = graph->cfg;
-  const ModelCfg& c = S->c;
-  if (const char* d = getenv("SG_DEVICE")) S->dev = atoi(d);
-  else if (cudaGetDevice(&S->dev) != cudaSuccess) S->dev = 0;
-  if (cudaSetDevice(S->dev) != cudaSuccess) {
-    cudaGetLastError();
-    set_err("armgraph_create_session: cannot use CUDA device %d", S->dev);
-    return nullptr;
-  }
-  if (cudaStreamCreateWithFlags(&S->st, cudaStreamNonBlocking) != cudaSuccess ||
-      cudaMallocHost(&S->h_pos, sizeof(int32_t)) != cudaSuccess) {
-    cudaGetLastError();
-    set_err("armgraph_create_session: cannot create the session's stream");
-    return nullptr;
-  }
-  if (const char* gflag = getenv("SG_DECODE_GRAPH")) S->use_graph = atoi(gflag) != 0;
-  // weight file
-  const uint8_t* wdata = nullptr;
-  uint64_t wbytes = 0;
-  std::string err;
-  if (!graph->pkg->box.map_entry(graph->weight_path, &wdata, &wbytes, &err)) {
-    set_err("armgraph_create_session: %s", err.c_str());
-    return nullptr;
-  }
-  for (auto& kv : graph->tensors)
-    if (kv.second.offset + kv.second.bytes > wbytes) {
-      set_err("armgraph_create_session: tensor %s lies outside the weight file", kv.first.c_str());
-      return nullptr;
-    }
-  // scratch sizes of the linear kernels (largest over the shapes and token counts used)
-  const int T = c.max_chunk;
-  SgMatMulParams mp{};
-  auto lin_ws = [&](int M, int K, int N, int cdt) {
-    mp = SgMatMulParams{};
-    mp.A = mp.B = mp.scales_B = reinterpret_cast<void*>(256);
-    mp.C = reinterpret_cast<void*>(256);
-    mp.M = M;
-    mp.K = K;
-    mp.N = N;
-    mp.group_size = c.group_size;
-    mp.a_dtype = SG_DT_F16;
-    mp.c_dtype = cdt;
-    return sg_matmul_int4_grouped_workspace_size(&mp);
-  };
-  size_t lws = 0;
-  // every token count a call can see: the row kernels' scratch depends on M
-  // below the tensor-core GEMM's threshold
-  for (int M = 1; M <= T; M = (M < 64 ? M + 1 : (M == T ? T + 1 : std::min(2 * M, T)))) {
-    lws = std::max({lws, lin_ws(M, c.hidden, c.nqkv(), SG_DT_F16), lin_ws(M, c.heads * c.head_dim, c.hidden, SG_DT_F16),
-                    lin_ws(M, c.hidden, 2 * c.ffn, SG_DT_F16), lin_ws(M, c.ffn, c.hidden, SG_DT_F16)});
-  }
-  lws = std::max(lws, lin_ws(1, c.hidden, c.vocab, SG_DT_F32));
-  SgFlashAttentionParams ap{};
-  ap.Q = ap.K = ap.V = ap.O = reinterpret_cast<void*>(256);
-  ap.B = 1;
-  ap.num_heads = c.heads;
-  ap.num_kv_heads = c.kv_heads;
-  ap.head_dim = c.head_dim;
-  ap.causal = 1;
-  ap.io_dtype = SG_DT_F16;
-  ap.S = 1;
-  ap.S_kv = c.max_context;
-  ap.q_pos0 = c.max_context - 1;
-  size_t aws = sg_flash_decode_workspace_size(&ap);
-  ap.S = T;
-  ap.q_pos0 = c.max_context - T;
-  aws = std::max(aws, sg_flash_attention_workspace_size(&ap));
-  // slab layout
-  S->plan = make_plan(c, T);
-  S->kv_head_stride = (int64_t)c.max_context * c.head_dim;
-  S->kv_block = (int64_t)c.kv_heads * S->kv_head_stride;
-  const uint64_t off_w = 0;
-  const uint64_t off_kv = align_up(off_w + wbytes, 4096);
-  const uint64_t kv_bytes = (uint64_t)c.layers * 2 * S->kv_block * 2;
-  const uint64_t off_act = align_up(off_kv + kv_bytes, 4096);
-  const uint64_t off_lws = align_up(off_act + S->plan.bytes, 4096);
-  S->lin_ws_bytes = align_up(std::max<size_t>(lws, 4096), 256);
-  const uint64_t off_aws = align_up(off_lws + S->lin_ws_bytes, 4096);
-  S->attn_ws_bytes = align_up(std::max<size_t>(aws, 256), 256);
-  S->slab_bytes = align_up(off_aws + S->attn_ws_bytes, 4096);
-  if (cudaMalloc(&S->slab, S->slab_bytes) != cudaSuccess) {
-    cudaGetLastError();
-    set_err("armgraph_create_session: cannot allocate %llu bytes on device %d",
-            (unsigned long long)S->slab_bytes, S->dev);
-    return nullptr;
-  }
-  graph->peak_bytes = std::max(graph->peak_bytes, S->slab_bytes);
-  char* wbase = S->slab + off_w;
-  S->kv = S->slab + off_kv;
-  S->act = S->slab + off_act;
-  S->lin_ws = S->slab + off_lws;
-  S->attn_ws = S->slab + off_aws;
-  auto cleanup_fail = [&](const char* what) -> ArmSession* {
-    set_err("armgraph_create_session: %s", what);
-    return nullptr;
-  };
-  if (cudaMemcpyAsync(wbase, wdata, wbytes, cudaMemcpyHostToDevice, S->st) != cudaSuccess ||
-      cudaMemsetAsync(S->kv, 0, kv_bytes, S->st) != cudaSuccess ||
-      cudaMemsetAsync(S->lin_ws, 0, S->lin_ws_bytes, S->st) != cudaSuccess ||
-      cudaMemsetAsync(S->attn_ws, 0, S->attn_ws_bytes, S->st) != cudaSuccess ||
-      cudaStreamSynchronize(S->st) != cudaSuccess) {
-    cudaGetLastError();
-    return cleanup_fail("uploading the weights failed");
-  }
-  // bind tensors
-  auto t = [&](const std::string& n, uint64_t expect) -> const void* {
-    auto it = graph->tensors.find(n);
-    if (it == graph->tensors.end() || it->second.bytes != expect) return nullptr;
-    return wbase + it->second.offset;
-  };
-  const uint64_t H2 = (uint64_t)c.hidden * 2;
-  std::string why;
-  S->embed = t("embed_tokens", (uint64_t)c.vocab * H2);
-  S->final_norm = t("final_norm", H2);
-  if (!S->embed || !S->final_norm) return cleanup_fail("embed_tokens / final_norm missing or of the wrong size");
-  for (int l = 0; l < c.layers; ++l) {
-    const std::string p = "layers." + std::to_string(l) + ".";
-    S->in_norm.push_back(t(p + "input_norm", H2));
-    S->post_norm.push_back(t(p + "post_norm", H2));
-    if (!S->in_norm.back() || !S->post_norm.back()) return cleanup_fail(("norm weights of layer " + std::to_string(l) + " missing").c_str());
-    Linear a, b, g3, d;
-    if (!bind_linear(graph, p + "qkv", wbase, c.hidden, c.nqkv(), &a, &why) ||
-        !bind_linear(graph, p + "o", wbase, c.heads * c.head_dim, c.hidden, &b, &why) ||
-        !bind_linear(graph, p + "gate_up", wbase, c.hidden, 2 * c.ffn, &g3, &why) ||
-        !bind_linear(graph, p + "down", wbase, c.ffn, c.hidden, &d, &why))
-      return cleanup_fail(why.c_str());
-    S->qkv.push_back(a);
-    S->o.push_back(b);
-    S->gu.push_back(g3);
-    S->down.push_back(d);
-  }
-  if (c.lm_int4) {
-    if (!bind_linear(graph, "lm_head", wbase, c.hidden, c.vocab, &S->lm, &why)) return cleanup_fail(why.c_str());
-  } else {
-    S->lm_f16 = t("lm_head.weight", (uint64_t)c.vocab * H2);
-    if (!S->lm_f16) return cleanup_fail("lm_head.weight missing or of the wrong size");
-  }
-  return S.release();
+  return create_session(graph, opts, 0, 1, nullptr);
 }
 
 void armsess_destroy(ArmSession* sess) {
@@ -820,7 +1149,7 @@ ArmStatus armsess_prefill(ArmSession* sess, const int32_t* tokens, uint32_t n_to
     return ARMCC_ERR_OOM;
   }
   for (uint32_t i = 0; i < n_tokens; ++i)
-    if (tokens[i] < 0 || tokens[i] >= c.vocab) {
+    if (tokens[i] < 0 || tokens[i] >= c.vocab_global) {
       set_err("armsess_prefill: token %d at %u is outside the vocabulary", tokens[i], i);
       return ARMCC_ERR_RUNTIME;
     }
@@ -998,6 +1327,57 @@ ArmStatus sg_session_last_logits(ArmSession* sess, float* host_out, uint32_t n) 
 }
 
 uint32_t sg_session_position(const ArmSession* sess) { return sess ? (uint32_t)sess->pos : 0; }
+
+ArmStatus sg_tp_shard(const SgTpModel* model, int32_t rank, int32_t world, SgTpShard* out) {
+  if (!model || !out) {
+    set_err("sg_tp_shard: NULL argument");
+    return ARMCC_ERR_RUNTIME;
+  }
+  std::string why;
+  if (!tp_plan(*model, rank, world, out, &why)) {
+    set_err("sg_tp_shard: %s", why.c_str());
+    return ARMCC_ERR_UNSUPPORTED;
+  }
+  return ARMCC_OK;
+}
+
+ArmStatus sg_tp_unique_id(uint8_t id_out[128]) {
+  if (!id_out) {
+    set_err("sg_tp_unique_id: NULL argument");
+    return ARMCC_ERR_RUNTIME;
+  }
+  if (!nccl_api().ok) {
+    set_err("sg_tp_unique_id: %s", nccl_api().why.c_str());
+    return ARMCC_ERR_UNSUPPORTED;
+  }
+  ncclUniqueId uid;
+  const ncclResult_t e = nccl_api().get_unique_id(&uid);
+  if (e != ncclSuccess) {
+    set_err("sg_tp_unique_id: ncclGetUniqueId failed: %s", nccl_api().error_string(e));
+    return ARMCC_ERR_RUNTIME;
+  }
+  static_assert(sizeof uid.internal == 128, "NCCL unique id size");
+  memcpy(id_out, uid.internal, 128);
+  return ARMCC_OK;
+}
+
+ArmSession* sg_session_create_tp(ArmGraph* graph, const ArmSessionOptions* opts, int32_t rank, int32_t world,
+                                 const uint8_t id[128]) {
+  if (world > 1 && !id) {
+    set_err("sg_session_create_tp: id is NULL");
+    return nullptr;
+  }
+  if (world < 1 || rank < 0 || rank >= world) {
+    set_err("sg_session_create_tp: rank %d outside a group of %d", rank, world);
+    return nullptr;
+  }
+  return create_session(graph, opts, rank, world, id);
+}
+
+void sg_session_vocab_range(const ArmSession* sess, uint32_t* lo, uint32_t* hi) {
+  if (lo) *lo = sess ? (uint32_t)sess->shard.vocab0 : 0;
+  if (hi) *hi = sess ? (uint32_t)sess->shard.vocab1 : 0;
+}
 void armtok_free_tokens(int32_t* tokens) { free(tokens); }
 
 }  // extern "C"

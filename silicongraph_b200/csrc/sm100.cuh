@@ -1,4 +1,4 @@
-// sm_100a building blocks: mbarriers with bounded waits, TMA (no multicast),
+// sm_100a building blocks: mbarriers with bounded waits, TMA into this CTA only,
 // programmatic dependent launch, tcgen05 (TMEM alloc, MMA, loads/stores) and
 // the UMMA shared-memory / instruction descriptors.
 //
@@ -157,7 +157,7 @@ inline cudaError_t launch_pdl(void (*kfn)(KArgs...), dim3 grid, dim3 block, size
   return cudaLaunchKernelEx(&cfg, kfn, std::forward<Args>(args)...);
 }
 
-// ------------------------------------------------------------------ TMA (no multicast)
+// ------------------------------------------------------------------ TMA (into this CTA only)
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int32_t x, int32_t y,
                                             uint64_t* bar) {
   asm volatile(

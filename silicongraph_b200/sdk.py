@@ -36,6 +36,15 @@ class ArmPackageInfo(ctypes.Structure):
                 ("vocab_size", ctypes.c_uint32)]
 
 
+class SgTpModel(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("hidden", "heads", "kv_heads", "head_dim", "ffn", "vocab", "group_size")]
+
+
+class SgTpShard(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("q_head0", "q_head1", "kv_head0", "kv_head1", "ffn0", "ffn1",
+                                              "vocab0", "vocab1")]
+
+
 _P = ctypes.c_void_p
 _CB = ctypes.CFUNCTYPE(None, ctypes.c_int32, ctypes.c_void_p)
 _SIGS = {
@@ -61,6 +70,12 @@ _SIGS = {
     "armpack_get_tokenizer": (_P, [_P]),
     "sg_session_last_logits": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_float), ctypes.c_uint32]),
     "sg_session_position": (ctypes.c_uint32, [_P]),
+    "sg_tp_shard": (ctypes.c_int, [ctypes.POINTER(SgTpModel), ctypes.c_int32, ctypes.c_int32,
+                                   ctypes.POINTER(SgTpShard)]),
+    "sg_tp_unique_id": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint8)]),
+    "sg_session_create_tp": (_P, [_P, ctypes.POINTER(ArmSessionOptions), ctypes.c_int32, ctypes.c_int32,
+                                  ctypes.POINTER(ctypes.c_uint8)]),
+    "sg_session_vocab_range": (None, [_P, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32)]),
 }
 
 
@@ -88,6 +103,27 @@ def last_error() -> str:
 def _tokens(tokens) -> tuple[ctypes.Array, int]:
     a = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
     return a.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), a.size, a
+
+
+def tp_shard(cfg: dict, rank: int, world: int, group_size: int) -> dict:
+    """The tensor-parallel shard of `rank` among `world` for a model config
+    (silicongraph_b200.armpack.llama_config keys); host only."""
+    m = SgTpModel(cfg["hidden_size"], cfg["num_heads"], cfg["num_kv_heads"], cfg["head_dim"],
+                  cfg["intermediate_size"], cfg["vocab_size"], group_size)
+    out = SgTpShard()
+    st = lib().sg_tp_shard(ctypes.byref(m), rank, world, ctypes.byref(out))
+    if st != ARMCC_OK:
+        raise ArmError(st, last_error())
+    return {f: getattr(out, f) for f, _ in SgTpShard._fields_}
+
+
+def tp_unique_id() -> bytes:
+    """A fresh NCCL unique id (128 bytes) for sessions of one tensor-parallel group."""
+    buf = (ctypes.c_uint8 * 128)()
+    st = lib().sg_tp_unique_id(buf)
+    if st != ARMCC_OK:
+        raise ArmError(st, last_error())
+    return bytes(buf)
 
 
 class Package:
@@ -150,8 +186,9 @@ class Graph:
     def peak_memory_bytes(self) -> int:
         return lib().armgraph_peak_memory_bytes(self.h)
 
-    def session(self) -> "Session":
-        return Session(self)
+    def session(self, tp: tuple[int, int, bytes] | None = None) -> "Session":
+        """A session; tp = (rank, world, unique id) joins a tensor-parallel group."""
+        return Session(self, tp)
 
     def run(self, tokens) -> ArmInferenceResult:
         p, n, _keep = _tokens(tokens)
@@ -159,9 +196,14 @@ class Graph:
 
 
 class Session:
-    def __init__(self, graph: Graph):
+    def __init__(self, graph: Graph, tp: tuple[int, int, bytes] | None = None):
         self.graph = graph
-        self.h = lib().armgraph_create_session(graph.h, None)
+        if tp is None:
+            self.h = lib().armgraph_create_session(graph.h, None)
+        else:
+            rank, world, uid = tp
+            buf = (ctypes.c_uint8 * 128).from_buffer_copy(uid)
+            self.h = lib().sg_session_create_tp(graph.h, None, rank, world, buf)
         if not self.h:
             raise ArmError(-5, last_error())
 
@@ -206,7 +248,12 @@ class Session:
             raise ArmError(st, last_error())
         return out
 
-    def last_logits(self, vocab: int) -> np.ndarray:
+    def last_logits(self, vocab: int | None = None) -> np.ndarray:
+        """fp32 logits of the last processed token over vocab_range (the first
+        `vocab` of them when given)."""
+        if vocab is None:
+            lo, hi = self.vocab_range
+            vocab = hi - lo
         out = np.zeros(vocab, np.float32)
         st = lib().sg_session_last_logits(self.h, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), vocab)
         if st != ARMCC_OK:
@@ -216,3 +263,10 @@ class Session:
     @property
     def position(self) -> int:
         return lib().sg_session_position(self.h)
+
+    @property
+    def vocab_range(self) -> tuple[int, int]:
+        """[lo, hi) of the logits last_logits returns (a shard on a tensor-parallel session)."""
+        lo, hi = ctypes.c_uint32(), ctypes.c_uint32()
+        lib().sg_session_vocab_range(self.h, ctypes.byref(lo), ctypes.byref(hi))
+        return lo.value, hi.value

@@ -1,0 +1,80 @@
+"""A tensor-parallel session over two GPUs (sg_session_create_tp): each rank
+holds its shard of every linear, NCCL sums the row-split projections and
+picks the greedy token across the vocabulary shards.  The gathered logits
+and the tokens must match the decoder composition oracle like a one-GPU
+session does (|got - want| <= 2e-3 + 1e-2 |want|), and every rank must emit
+the same tokens.  Skipped with fewer than two GPUs."""
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from silicongraph_b200 import armpack
+
+pytestmark = pytest.mark.gpu
+
+SMALL = armpack.llama_config(layers=2, hidden=256, heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=1008,
+                             rope_theta=500000.0, max_pos=4096)
+RTOL, ATOL = 1e-2, 2e-3
+STEPS = 4
+
+
+def _worker(rank, world, uid, path, prompt, out_dir):
+    os.environ["SG_DEVICE"] = str(rank)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    from silicongraph_b200 import sdk
+    with sdk.Package(path) as pkg:
+        g = pkg.select(context_length=len(prompt) + STEPS + 4)
+        with g.session(tp=(rank, world, uid)) as s:
+            s.prefill(prompt)
+            logits = [s.last_logits()]
+            toks = [s.decode().next_token_id]  # predicted by the prompt
+            for _ in range(STEPS):
+                toks.append(s.decode().next_token_id)
+                logits.append(s.last_logits())
+            lo, hi = s.vocab_range
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), logits=np.stack(logits), toks=np.array(toks), lo=lo, hi=hi)
+
+
+@pytest.mark.parametrize("world", [2])
+def test_tp_session_matches_decoder_oracle(sg, oracle_mod, tmp_path, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from oracle.decoder import DecoderOracle
+    from silicongraph_b200 import sdk
+    w = armpack.random_llama_weights(SMALL, seed=4)
+    t = armpack.cuda_tensors(SMALL, w, group_size=32)
+    path = armpack.write_package(str(tmp_path / "tp.armpack"), SMALL, t, max_context=256, max_prefill_chunk=64)
+    prompt = np.random.default_rng(9).integers(0, SMALL["vocab_size"], 90).astype(np.int32)  # two prefill chunks
+    uid = sdk.tp_unique_id()
+    mp.start_processes(_worker, args=(world, uid, path, prompt, str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    ranks = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
+    assert [int(r["lo"]) for r in ranks] == sorted(int(r["lo"]) for r in ranks)
+    assert int(ranks[-1]["hi"]) == SMALL["vocab_size"]
+    for r in ranks[1:]:
+        assert np.array_equal(r["toks"], ranks[0]["toks"])  # every rank emits the same tokens
+    logits = np.concatenate([r["logits"] for r in ranks], axis=1)
+    toks = ranks[0]["toks"]
+    ref = DecoderOracle(SMALL, t, group_size=32)
+
+    def close(got, want):
+        err = np.abs(got - want)
+        bad = err > ATOL + RTOL * np.abs(want)
+        assert not bad.any(), f"{bad.sum()} / {bad.size} logits outside tolerance; max err {err.max():.3e}"
+
+    def check_token(tok, want):
+        top = np.sort(want)[-2:]
+        if top[1] - top[0] > ATOL + RTOL * abs(top[1]):
+            assert tok == int(np.argmax(want))
+
+    want = ref.forward(prompt)
+    close(logits[0], want)
+    check_token(int(toks[0]), want)
+    for i in range(STEPS):
+        want = ref.forward([int(toks[i])])
+        close(logits[i + 1], want)
+        check_token(int(toks[i + 1]), want)
