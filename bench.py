@@ -721,7 +721,8 @@ DECODE_WORKLOAD = ("Llama-3.2-1B-shape decoder through the armcc SDK: 16 layers,
                    "activations and KV cache; prompt of 512 random ids, then greedy decode, batch 1")
 
 
-def build_decode_package(path, cfg, seed=0, gs=32, max_context=1024):
+def build_decode_package(path, cfg, seed=0, gs=32, max_context=1024, max_prefill_chunk=512,
+                         model_id="synthetic/llama-3.2-1b-shape"):
     """Random N(0, 0.02) weights (norms 1 + N(0, 0.02)) drawn on the GPU and
     packed by the library's device packer, written as a directory package."""
     import torch
@@ -756,8 +757,8 @@ def build_decode_package(path, cfg, seed=0, gs=32, max_context=1024):
             t[q + name + ".qweight"], t[q + name + ".scales"], t[q + name + ".zeros"] = B, S, Z
     t["final_norm"] = (1 + randn(H)).half().cpu().numpy()
     t["lm_head.qweight"], t["lm_head.scales"], t["lm_head.zeros"] = quant(H, V)
-    armpack.write_package(path, cfg, t, group_size=gs, max_context=max_context, max_prefill_chunk=512,
-                          as_zip=False, model_id="synthetic/llama-3.2-1b-shape")
+    armpack.write_package(path, cfg, t, group_size=gs, max_context=max_context, max_prefill_chunk=max_prefill_chunk,
+                          as_zip=False, model_id=model_id)
     weight_bytes = sum(a.nbytes for k, a in t.items() if k != "embed_tokens") + H * 2
     return weight_bytes, t
 
@@ -878,6 +879,119 @@ def run_decode(args):
         print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- Qwen-7B shape, tensor-parallel
+QWEN_CFG = dict(layers=28, hidden=3584, heads=28, kv_heads=4, head_dim=128, ffn=18944, vocab=152064,
+                rope_theta=1000000.0)
+QWEN_GS = 128
+QWEN_PROMPT = 8192
+QWEN_WORKLOAD = ("Qwen2.5-7B-shape decoder through the armcc SDK, tensor-parallel over all ranks: 28 layers, "
+                 "hidden 3584, 28/4 heads, head_dim 128, SwiGLU 18944, vocab 152064, INT4 group-128 weights "
+                 "(lm_head included); one 8192-token prefill of random ids, then greedy decode, batch 1")
+
+
+def run_qwen(args):
+    import datetime
+    import shutil
+
+    import torch
+    import torch.distributed as dist
+
+    from silicongraph_b200 import armpack, sdk
+
+    rank, local_rank, world = rank_env()
+    torch.cuda.set_device(local_rank)
+    os.environ["SG_DEVICE"] = str(local_rank)
+    if world > 1:
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
+    c = QWEN_CFG
+    cfg = armpack.llama_config(layers=c["layers"], hidden=c["hidden"], heads=c["heads"], kv_heads=c["kv_heads"],
+                               head_dim=c["head_dim"], ffn=c["ffn"], vocab=c["vocab"], rope_theta=c["rope_theta"])
+    steps = args.steps
+    ctx = QWEN_PROMPT + steps + args.warmup + 8
+    # one package on the host's disk, written by rank 0, read by every rank
+    root = os.environ.get("SG_BENCH_TMP", "/tmp")
+    pkg_path = [os.path.join(root, f"sg_qwen7b_{os.getpid()}") if rank == 0 else None]
+    uid = [sdk.tp_unique_id() if rank == 0 else None]
+    if world > 1:
+        dist.broadcast_object_list(pkg_path, src=0)
+        dist.broadcast_object_list(uid, src=0)
+    pkg_path = pkg_path[0]
+    try:
+        if rank == 0:
+            weight_bytes, _ = build_decode_package(pkg_path, cfg, seed=21, gs=QWEN_GS, max_context=ctx,
+                                                   max_prefill_chunk=QWEN_PROMPT,
+                                                   model_id="synthetic/qwen2.5-7b-shape")
+            torch.cuda.empty_cache()
+        else:
+            weight_bytes = 0
+        if world > 1:
+            wb = [weight_bytes]
+            dist.broadcast_object_list(wb, src=0)
+            weight_bytes = wb[0]
+        prompt = np.random.default_rng(6).integers(0, c["vocab"], QWEN_PROMPT).astype(np.int32)
+        with sdk.Package(pkg_path) as pkg:
+            graph = pkg.select(context_length=ctx)
+            with graph.session(tp=(rank, world, uid[0])) as s:
+                s.prefill(prompt[:1024])           # warm-up: allocations, tensor maps, graph capture
+                for _ in range(args.warmup):
+                    s.decode()
+                s.reset()
+                clocks = ClockSampler(torch.cuda.current_device(), interval_ms=5) if rank == 0 else None
+                if world > 1:
+                    dist.barrier()
+                t0 = time.perf_counter()
+                s.prefill(prompt)
+                first = s.decode()
+                t1 = time.perf_counter()
+                for _ in range(steps):
+                    s.decode()
+                t2 = time.perf_counter()
+                clk = clocks.stop() if clocks else None
+    finally:
+        if world > 1:
+            dist.barrier()
+        if rank == 0:
+            shutil.rmtree(pkg_path, ignore_errors=True)
+    ttft_s, decode_s = t1 - t0, t2 - t1
+    if world > 1:
+        tmax = torch.tensor([ttft_s, decode_s], dtype=torch.float64)
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        ttft_s, decode_s = float(tmax[0]), float(tmax[1])
+        dist.destroy_process_group()
+    H, L, F, V, D = c["hidden"], c["layers"], c["ffn"], c["vocab"], c["head_dim"]
+    Hq, Hkv = c["heads"], c["kv_heads"]
+    lin_params = L * (H * (Hq + 2 * Hkv) * D + Hq * D * H + H * 2 * F + F * H)
+    S = QWEN_PROMPT
+    flops = 2.0 * lin_params * S + L * 4.0 * Hq * D * S * (S + 1) / 2 + 2.0 * H * V  # linears, causal attention, LM head
+    prefill_tps = S / ttft_s
+    achieved = flops / ttft_s / 1e12 / world
+    peak, peak_src = read_peak_tensor()
+    dec_tps = steps / decode_s
+    line = {
+        "metric": "Qwen-7B-shape INT4 prefill tokens/s (8192-token prompt, tensor-parallel)",
+        "value": round(prefill_tps, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * decode_s / steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (random N(0,0.02) weights drawn on the GPU, random prompt ids)",
+        "config": {"workload": QWEN_WORKLOAD, "prompt": S, "ttft_ms": round(1e3 * ttft_s, 2),
+                   "decode_steps": steps, "decode_tokens_per_s": round(dec_tps, 2),
+                   "decode_ms_per_token": round(1e3 * decode_s / steps, 3),
+                   "weight_bytes": int(weight_bytes), "flops_prefill": flops,
+                   "parallelism": f"tensor-parallel x{world} (NCCL all-reduce after o and down)",
+                   "timing": "host clock around armsess_prefill / armsess_decode, max over ranks"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_src, "traffic": None,
+                     "achieved_basis": "prefill FLOPs (linears + causal attention + LM head) / TTFT, per GPU"},
+        "e2e": {"value": round(prefill_tps, 1), "unit": "tokens/s", "h2d_bytes_per_step": S * 4,
+                "d2h_bytes_per_step": 8},
+        "gpu_launches": None,
+        "clocks": clk,
+        "first_token": int(first.next_token_id),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args):
     rank, _, world = rank_env()
@@ -962,11 +1076,12 @@ def main():
     ap.add_argument("--ref-budget-s", type=float, default=120.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["gemv_int4", *PF_WORKLOADS, *ATTN_WORKLOADS, "decode_llama1b",
-                                           "decode_llama1b_tp"],
+                                           "decode_llama1b_tp", "qwen7b_tp"],
                     default="gemv_int4",
                     help="gemv_int4 (default): the decode GEMV; prefill_int4 / prefill_int8: the prefill GEMM; "
                          "attn_prefill / attn_small: flash attention; decode_llama1b: Llama-1B-shape decode "
                          "through the SDK (one session per GPU); decode_llama1b_tp: the same model "
+                         "tensor-parallel over all GPUs; qwen7b_tp: Qwen-7B-shape 8192-token prefill + decode, "
                          "tensor-parallel over all GPUs")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -985,6 +1100,8 @@ def main():
         run_attention(args)
     elif args.workload in ("decode_llama1b", "decode_llama1b_tp"):
         run_decode(args)
+    elif args.workload == "qwen7b_tp":
+        run_qwen(args)
     else:
         run_ours(args)
 
