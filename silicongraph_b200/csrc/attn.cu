@@ -574,7 +574,252 @@ __global__ void __launch_bounds__(kThreads) attn_dec_cluster_kernel(AArgs a) {
   }
 }
 
-std::atomic<int> g_decode_kernel{1};  // decode kernel: 1 cluster, 2 key-parallel + combine, 0 generic
+// Decode form on tensor cores: up to 16 query rows per kv head (R = G * Sq),
+// head_dim 64 or 128, fp16 or bf16 I/O (bf16 values go to fp16 for the MMAs,
+// so that P keeps 11 significant bits).  Same cluster-of-splits structure as
+// attn_dec_cluster_kernel; per 64-key tile:
+//   * S = Q K^T with mma.sync m16n8k16 (queries = the 16 A rows, kept in
+//     registers as fragments; warp w takes keys 16w .. 16w+15, K row-major in
+//     shared memory with 16 bytes of padding per row, so the B fragments are
+//     conflict-free 32-bit loads);
+//   * online softmax on the scores in shared memory, one warp per row;
+//   * O += P V with mma.sync (P rebuilt as fp16 A fragments, V fragments by
+//     ldmatrix.trans from row-major V; warp w owns a quarter of the head dims).
+// The next tile's K and V are in flight in registers during each tile.
+constexpr int kDecMmaRows = 16;
+
+__device__ __forceinline__ void ldmatrix_x2_trans(uint32_t& r0, uint32_t& r1, const void* smem_row) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
+               : "=r"(r0), "=r"(r1)
+               : "r"(sgd::smem_u32(smem_row)));
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// 8 elements of a 16-byte load as fp16 (bf16 input converted).
+template <int IO>
+__device__ __forceinline__ uint4 to_f16x8(const uint4& v) {
+  if (IO == SG_DT_F16) return v;
+  float f[8];
+  IoVec<SG_DT_BF16>::to_f32(v, f);
+  uint4 o;
+  o.x = pack_half2(f[0], f[1]);
+  o.y = pack_half2(f[2], f[3]);
+  o.z = pack_half2(f[4], f[5]);
+  o.w = pack_half2(f[6], f[7]);
+  return o;
+}
+
+inline size_t dec_mma_smem(int D, int R, int nsplit) {
+  const size_t kvrow = (size_t)(D + 8) * 2;  // bytes per padded fp16 row
+  return 2 * kDecTile * kvrow + sizeof(float) * ((size_t)kDecMmaRows * kDecTile + 3 * kDecMmaRows +
+                                                 (size_t)nsplit * R * (D + 2));
+}
+
+template <int D, int IO>
+__global__ void __launch_bounds__(kThreads) attn_dec_mma_kernel(AArgs a) {
+  namespace cg = cooperative_groups;
+  constexpr int KT = kDecTile, KP = D + 8;  // padded row (halves)
+  constexpr int NV = (D / 2) * 2 / 16;      // 16-byte loads per thread per tile (K, and V): half a row
+  constexpr int DW = D / 4;                 // head dims per warp in P V
+  constexpr int NT = DW / 8;                // n-tiles per warp in P V
+  extern __shared__ __align__(16) uint8_t smb[];
+  __half* ks = reinterpret_cast<__half*>(smb);         // [KT][KP]
+  __half* vs = ks + KT * KP;                           // [KT][KP]
+  float* ps = reinterpret_cast<float*>(vs + KT * KP);  // [16][KT] scores, then probabilities
+  float* ms = ps + kDecMmaRows * KT;                   // [16] running max (log2 units)
+  float* ls = ms + kDecMmaRows;                        // [16] running sum
+  float* al = ls + kDecMmaRows;                        // [16] rescale of this tile
+  float* comb = al + kDecMmaRows;                      // rank 0: [rank][R][D + 2]
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  sgd::pdl_wait();  // the newest key and the queries come from the previous kernel
+  sgd::pdl_launch_dependents();
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int b = blockIdx.z, hk = blockIdx.y, split = blockIdx.x;
+  const int nq = a.Sq, R = a.G * nq;  // row r: head hk*G + r / nq, query r % nq
+  const int q_pos0 = a.q_pos_dev ? *a.q_pos_dev : a.q_pos0;
+  const int Skv = a.q_pos_dev ? min(a.Skv, q_pos0 + a.Sq) : a.Skv;
+  const int j0 = split * a.keys_per_split;
+  int j1 = min(Skv, j0 + a.keys_per_split);
+  if (a.causal) j1 = min(j1, q_pos0 + nq);
+  const int64_t kvbase = (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs;
+  const int kk = tid >> 1, part = tid & 1;  // loader role: half `part` of key kk
+
+  uint4 kr[NV], vr[NV];
+  auto load_tile = [&](int jt) {
+    const int key = jt + kk;
+    const bool live = key < j1;
+    const int64_t e0 = kvbase + (int64_t)key * D + part * (D / 2);
+    const uint4* kp = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.K) + e0);
+    const uint4* vp = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.V) + e0);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      kr[i] = live ? __ldg(kp + i) : make_uint4(0u, 0u, 0u, 0u);
+      vr[i] = live ? __ldg(vp + i) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  if (j0 < j1) load_tile(j0);  // in flight together with the query loads
+
+  // Q fragments (A of S = Q K^T), prescaled by scale * log2(e); rows >= R are zero.
+  const float qscale = a.scale * 1.4426950408889634f;
+  auto q_at = [&](int r, int d) -> float {
+    if (r >= R) return 0.f;
+    const int h = hk * a.G + r / nq, qi = r % nq;
+    return ld_io(a.Q, a.io_dt, (((int64_t)b * a.H + h) * a.Sq + qi) * D + d) * qscale;
+  };
+  uint32_t qf[D / 16][4];
+#pragma unroll
+  for (int s = 0; s < D / 16; ++s) {
+    const int d0 = 16 * s + 2 * t;
+    qf[s][0] = pack_half2(q_at(g, d0), q_at(g, d0 + 1));
+    qf[s][1] = pack_half2(q_at(g + 8, d0), q_at(g + 8, d0 + 1));
+    qf[s][2] = pack_half2(q_at(g, d0 + 8), q_at(g, d0 + 9));
+    qf[s][3] = pack_half2(q_at(g + 8, d0 + 8), q_at(g + 8, d0 + 9));
+  }
+  for (int r = tid; r < kDecMmaRows; r += kThreads) {
+    ms[r] = -INFINITY;
+    ls[r] = 0.f;
+  }
+  float o[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) o[n][q] = 0.f;
+
+  for (int jt = j0; jt < j1; jt += KT) {
+    __syncthreads();  // the previous tile's readers of ks, vs, ps and al are done
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      *reinterpret_cast<uint4*>(ks + kk * KP + part * (D / 2) + 8 * i) = to_f16x8<IO>(kr[i]);
+      *reinterpret_cast<uint4*>(vs + kk * KP + part * (D / 2) + 8 * i) = to_f16x8<IO>(vr[i]);
+    }
+    if (jt + KT < j1) load_tile(jt + KT);  // next tile in flight during this one
+    __syncthreads();
+    // ---- S = Q K^T for this warp's 16 keys (two n-tiles of 8)
+    float sc[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) sc[j][q] = 0.f;
+      const __half* krow = ks + (16 * warp + 8 * j + g) * KP + 2 * t;
+#pragma unroll
+      for (int s = 0; s < D / 16; ++s) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow + 16 * s);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(krow + 16 * s + 8);
+        sgd::mma_f16_16816(sc[j], qf[s][0], qf[s][1], qf[s][2], qf[s][3], b0, b1);
+      }
+    }
+    // scores to shared memory with the visibility mask (rows >= R are never read)
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int r = g + 8 * (q >> 1);
+        const int kl = 16 * warp + 8 * j + 2 * t + (q & 1);
+        const int key = jt + kl;
+        const bool vis = key < j1 && (!a.causal || key <= q_pos0 + r % nq);
+        ps[r * KT + kl] = vis ? sc[j][q] : -INFINITY;
+      }
+    __syncthreads();
+    // ---- online softmax: one warp per row
+    for (int r = warp; r < R; r += kThreads / 32) {
+      const float s0 = ps[r * KT + lane], s1 = ps[r * KT + lane + 32];
+      float mx = fmaxf(s0, s1);
+#pragma unroll
+      for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_old = ms[r];
+      const float m_new = fmaxf(m_old, mx);
+      const float p0 = m_new == -INFINITY ? 0.f : exp2f(s0 - m_new);
+      const float p1 = m_new == -INFINITY ? 0.f : exp2f(s1 - m_new);
+      ps[r * KT + lane] = p0;
+      ps[r * KT + lane + 32] = p1;
+      float sum = p0 + p1;
+#pragma unroll
+      for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      const float alpha = m_old == -INFINITY ? 0.f : exp2f(m_old - m_new);
+      __syncwarp();
+      if (lane == 0) {
+        ms[r] = m_new;
+        ls[r] = ls[r] * alpha + sum;
+        al[r] = alpha;
+      }
+    }
+    __syncthreads();
+    // ---- O += P V for this warp's dims [DW * warp, DW * (warp + 1))
+    const float a_lo = g < R ? al[g] : 0.f, a_hi = g + 8 < R ? al[g + 8] : 0.f;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      o[n][0] *= a_lo;
+      o[n][1] *= a_lo;
+      o[n][2] *= a_hi;
+      o[n][3] *= a_hi;
+    }
+    auto p_at = [&](int r, int kl) -> float { return r < R ? ps[r * KT + kl] : 0.f; };
+#pragma unroll
+    for (int s = 0; s < KT / 16; ++s) {
+      const int k0 = 16 * s + 2 * t;
+      const uint32_t pa0 = pack_half2(p_at(g, k0), p_at(g, k0 + 1));
+      const uint32_t pa1 = pack_half2(p_at(g + 8, k0), p_at(g + 8, k0 + 1));
+      const uint32_t pa2 = pack_half2(p_at(g, k0 + 8), p_at(g, k0 + 9));
+      const uint32_t pa3 = pack_half2(p_at(g + 8, k0 + 8), p_at(g + 8, k0 + 9));
+      // ldmatrix rows: lanes 0-7 keys 16s + lane, lanes 8-15 keys 16s + 8 + (lane - 8)
+      const __half* vrow = vs + (16 * s + (lane & 15)) * KP + DW * warp;
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        uint32_t b0, b1;
+        ldmatrix_x2_trans(b0, b1, vrow + 8 * n);
+        sgd::mma_f16_16816(o[n], pa0, pa1, pa2, pa3, b0, b1);
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- merge the splits in rank 0 (cluster rank == split)
+  cg::cluster_group cluster = cg::this_cluster();
+  const int nsplit = a.nsplit;
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+  float* dst = cluster.map_shared_rank(comb, 0) + (size_t)split * R * (D + 2);
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    const int d = DW * warp + 8 * n + 2 * t;
+    if (g < R) {
+      dst[g * (D + 2) + d] = o[n][0];
+      dst[g * (D + 2) + d + 1] = o[n][1];
+    }
+    if (g + 8 < R) {
+      dst[(g + 8) * (D + 2) + d] = o[n][2];
+      dst[(g + 8) * (D + 2) + d + 1] = o[n][3];
+    }
+  }
+  for (int r = tid; r < R; r += kThreads) {
+    dst[r * (D + 2) + D] = ms[r];
+    dst[r * (D + 2) + D + 1] = ls[r];
+  }
+  cluster.sync();
+  if (split != 0) return;
+  for (int i = tid; i < R * D; i += kThreads) {
+    const int r = i / D, d = i % D;
+    float M = -INFINITY;
+    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, comb[((size_t)sp * R + r) * (D + 2) + D]);
+    float L = 0.f, acc = 0.f;
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float* pr = comb + ((size_t)sp * R + r) * (D + 2);
+      if (pr[D] == -INFINITY) continue;
+      const float w = exp2f(pr[D] - M);
+      L = fmaf(pr[D + 1], w, L);
+      acc = fmaf(pr[d], w, acc);
+    }
+    const int h = hk * a.G + r / nq, qi = r % nq;
+    st_io(a.O, a.io_dt, (((int64_t)b * a.H + h) * a.Sq + qi) * D + d, L > 0.f ? acc / L : 0.f);
+  }
+}
+
+std::atomic<int> g_decode_kernel{3};  // decode kernel: 3 tensor-core cluster, 1 CUDA-core cluster, 2 key-parallel + combine, 0 generic
 std::atomic<int> g_decode_cluster_max{kDecClusterMax};  // largest cluster of key splits
 
 }  // namespace
@@ -675,16 +920,20 @@ SgStatus attn_cc_run(const SgFlashAttentionParams* p, void* stream, int want_spl
   const int R = a.G * a.Sq;
   const int eb = a.io_dt == SG_DT_F32 ? 4 : 2;
   const bool vec_ok = aligned16(a.K) && aligned16(a.V) && (a.kv_hs * eb) % 16 == 0 && (a.kv_bs * eb) % 16 == 0;
-  if ((a.D == 64 || (a.D == 128 && eb == 2)) && R <= kDecRows && vec_ok && g_decode_kernel.load() == 1) {
+  const int mode = g_decode_kernel.load();
+  const bool use_mma = mode == 3 && eb == 2 && (a.D == 64 || a.D == 128) && R <= kDecMmaRows && vec_ok;
+  const bool use_cl = (mode == 3 || mode == 1) && (a.D == 64 || (a.D == 128 && eb == 2)) && R <= kDecRows && vec_ok;
+  if (use_mma || use_cl) {
+    auto smem_of = [&](int ns) { return use_mma ? dec_mma_smem(a.D, R, ns) : dec_cluster_smem(a.D, R, ns); };
     const int tiles = (a.Skv + kDecTile - 1) / kDecTile;
     const int items = a.Hkv * a.B;
     const int cmax = std::max(1, std::min(kDecClusterMax, g_decode_cluster_max.load()));
     int ns = std::max(1, std::min({cmax, tiles, (2 * sms + items - 1) / items}));
-    while (ns > 1 && dec_cluster_smem(a.D, R, ns) > 200 * 1024) --ns;
+    while (ns > 1 && smem_of(ns) > 200 * 1024) --ns;
     const int tiles_per = (tiles + ns - 1) / ns;
     a.keys_per_split = tiles_per * kDecTile;
     a.nsplit = (tiles + tiles_per - 1) / tiles_per;
-    const size_t smem = dec_cluster_smem(a.D, R, a.nsplit);
+    const size_t smem = smem_of(a.nsplit);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.nsplit, a.Hkv, a.B);
     cfg.blockDim = dim3(kThreads);
@@ -705,6 +954,12 @@ SgStatus attn_cc_run(const SgFlashAttentionParams* p, void* stream, int want_spl
       SG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kfn, a));
       return SG_OK;
     };
+    if (use_mma) {
+      if (a.D == 64)
+        return launch_cl(a.io_dt == SG_DT_BF16 ? attn_dec_mma_kernel<64, SG_DT_BF16> : attn_dec_mma_kernel<64, SG_DT_F16>);
+      return launch_cl(a.io_dt == SG_DT_BF16 ? attn_dec_mma_kernel<128, SG_DT_BF16>
+                                             : attn_dec_mma_kernel<128, SG_DT_F16>);
+    }
     if (a.D == 64) {
       if (a.io_dt == SG_DT_F32) return launch_cl(attn_dec_cluster_kernel<64, SG_DT_F32>);
       if (a.io_dt == SG_DT_BF16) return launch_cl(attn_dec_cluster_kernel<64, SG_DT_BF16>);

@@ -67,14 +67,15 @@ def test_attention_vs_oracle(sg, oracle_mod, dtype, B, H, Hkv, S, D, causal):
     close(got, want)
 
 
-@pytest.mark.parametrize("kernel", [1, 2, 0], ids=["cluster", "key-parallel", "generic"])
+@pytest.mark.parametrize("kernel", [3, 1, 2, 0], ids=["tensor-core-cluster", "cluster", "key-parallel", "generic"])
 @pytest.mark.parametrize("Skv,Sq,H,Hkv,D", [(768, 1, 32, 8, 64), (4096, 1, 28, 4, 128), (1000, 3, 8, 8, 64),
                                             (64, 1, 4, 2, 32), (8192, 1, 28, 4, 128), (37, 2, 16, 2, 64),
                                             (300, 4, 28, 4, 128)])
 def test_decode_against_kv_cache(sg, oracle_mod, kernel, Skv, Sq, H, Hkv, D):
     """Queries at the end of a strided KV cache (capacity > S_kv), split-K, with
     each decode kernel: the cluster of key splits merged in distributed shared
-    memory, the key-parallel kernel plus a combine kernel, the generic one."""
+    memory (scores and P V on tensor cores, or on CUDA cores), the
+    key-parallel kernel plus a combine kernel, the generic one."""
     rng = np.random.default_rng(Skv)
     cap = Skv + 37
     q = rng.standard_normal((2, H, Sq, D)).astype(np.float16)
@@ -87,16 +88,18 @@ def test_decode_against_kv_cache(sg, oracle_mod, kernel, Skv, Sq, H, Hkv, D):
         got = sg.flash_attention(dev(q), dev(kc), dev(vc), causal=True, q_pos0=-1, decode=True, kv_len=Skv)
         got2 = sg.flash_attention(dev(q), dev(kc), dev(vc), causal=True, q_pos0=-1, decode=True, kv_len=Skv)
     finally:
-        sg.set_tuning("attn.decode_kernel", 1)
+        sg.set_tuning("attn.decode_kernel", 3)
     close(got.float().cpu().numpy(), want)
     assert torch.equal(got, got2)
 
 
+@pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
-def test_decode_cluster_kernel_io_types(sg, oracle_mod, dtype):
-    """fp32 and bf16 caches through the cluster decode kernel (head_dim 64)."""
+def test_decode_cluster_kernel_io_types(sg, oracle_mod, dtype, D):
+    """fp32 caches (CUDA-core cluster kernel at head_dim 64, key-parallel at 128)
+    and bf16 caches (tensor-core cluster kernel, fp16 inside)."""
     rng = np.random.default_rng(7)
-    Skv, Sq, H, Hkv, D = 700, 1, 32, 8, 64
+    Skv, Sq, H, Hkv = 700, 1, 32, 8
     q = rng.standard_normal((1, H, Sq, D)).astype(np.float32)
     kc = rng.standard_normal((1, Hkv, Skv, D)).astype(np.float32)
     vc = rng.standard_normal((1, Hkv, Skv, D)).astype(np.float32)
