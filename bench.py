@@ -718,7 +718,7 @@ DECODE_CFG = dict(layers=16, hidden=2048, heads=32, kv_heads=8, head_dim=64, ffn
                   rope_theta=500000.0)
 DECODE_WORKLOAD = ("Llama-3.2-1B-shape decoder through the armcc SDK: 16 layers, hidden 2048, 32/8 heads, "
                    "head_dim 64, SwiGLU 8192, vocab 128256, INT4 group-32 weights (lm_head included), fp16 "
-                   "activations and KV cache; prompt of 512 random ids, then greedy decode, batch 1")
+                   "activations and KV cache; a prompt of 512 random ids per sequence, then greedy decode")
 
 
 def build_decode_package(path, cfg, seed=0, gs=32, max_context=1024, max_prefill_chunk=512,
@@ -813,24 +813,29 @@ def run_decode(args):
         weight_bytes, tensors = build_decode_package(pkg_path, cfg, seed=11 + seed_rank,
                                                      max_context=prompt_len + steps + args.warmup + 8)
         rng = np.random.default_rng(5 + seed_rank)
-        prompt = rng.integers(0, c["vocab"], prompt_len).astype(np.int32)
+        B = args.batch
+        prompt = rng.integers(0, c["vocab"], (B, prompt_len)).astype(np.int32)
         with sdk.Package(pkg_path) as pkg:
             graph = pkg.select(context_length=prompt_len + steps + args.warmup)
-            with graph.session(tp=tp_arg) as s:
+            with graph.session(tp=tp_arg, batch=B) as s:
+                if B == 1:
+                    prefill, decode = (lambda: s.prefill(prompt[0])), (lambda: s.decode().next_token_id)
+                else:
+                    prefill, decode = (lambda: s.batch_prefill(prompt)), (lambda: int(s.batch_decode()[0]))
                 # warm-up: a full prompt and a few steps (allocations, tensor maps, caches)
-                s.prefill(prompt)
+                prefill()
                 for _ in range(args.warmup):
-                    s.decode()
+                    decode()
                 s.reset()
                 clocks = ClockSampler(torch.cuda.current_device(), interval_ms=5) if rank == 0 else None
                 if world > 1:
                     dist.barrier()
                 t0 = time.perf_counter()
-                s.prefill(prompt)
-                first = s.decode()                      # the token predicted by the prompt
+                prefill()
+                first = decode()                        # the token predicted by the prompt
                 t1 = time.perf_counter()
                 for _ in range(steps):
-                    s.decode()
+                    decode()
                 t2 = time.perf_counter()
                 clk = clocks.stop() if clocks else None
     decode_s, ttft_s = t2 - t1, t1 - t0
@@ -840,18 +845,19 @@ def run_decode(args):
         decode_s, ttft_s = float(tmax[0]), float(tmax[1])
         dist.destroy_process_group()
     tps = steps / decode_s
-    seqs = 1 if tp else world  # sequences decoded at once over the whole job
+    seqs = args.batch * (1 if tp else world)  # sequences decoded at once over the whole job
     ctx_mid = prompt_len + steps / 2
     kv_read = 2 * c["layers"] * c["kv_heads"] * c["head_dim"] * 2 * ctx_mid
     bytes_per_token = weight_bytes + kv_read
+    bytes_per_step = weight_bytes + args.batch * kv_read  # one step reads the weights once for the whole batch
     peak, peak_src = read_peak_hbm()
     line = {
-        "metric": "INT4 decode tokens/s (Llama-3.2-1B shape, batch 1)",
+        "metric": f"INT4 decode tokens/s (Llama-3.2-1B shape, batch {args.batch})",
         "value": round(seqs * tps, 2), "unit": "tokens/s", "n_gpus": world, "steps": steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * decode_s / steps, "higher_is_better": True,
         "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (random N(0,0.02) weights drawn on the GPU, random prompt ids)",
-        "config": {"workload": DECODE_WORKLOAD, "prompt": prompt_len, "decode_steps": steps,
+        "config": {"workload": DECODE_WORKLOAD, "batch": args.batch, "prompt": prompt_len, "decode_steps": steps,
                    "ttft_ms": round(1e3 * ttft_s, 3), "prefill_tokens_per_s": round(prompt_len / ttft_s, 1),
                    "bytes_per_token": int(bytes_per_token),
                    "parallelism": (f"tensor-parallel x{world} (one session over {world} GPUs, NCCL all-reduce "
@@ -859,16 +865,16 @@ def run_decode(args):
                                   f"replicas x{world} (one session per GPU)",
                    "timing": "host clock around armsess_decode calls (each returns the token to the host), "
                              "max over ranks"},
-        "roofline": {"bound": "hbm", "achieved": round(bytes_per_token * tps / 1e9 / (world if tp else 1), 2),
+        "roofline": {"bound": "hbm", "achieved": round(bytes_per_step * tps / 1e9 / (world if tp else 1), 2),
                      "peak": peak, "unit": "GB/s",
-                     "frac": round(bytes_per_token * tps / 1e9 / (world if tp else 1) / peak, 4),
+                     "frac": round(bytes_per_step * tps / 1e9 / (world if tp else 1) / peak, 4),
                      "peak_source": f"{peak_src} hbm_gbs", "traffic": None,
-                     "achieved_basis": "weights + KV cache bytes per token x decode tokens/s, per GPU"},
+                     "achieved_basis": "(weights + KV cache of every sequence) bytes per step x steps/s, per GPU"},
         "e2e": {"value": round(seqs * tps, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 8},
         "gpu_launches": steps * (10 * c["layers"] + 4),
         "clocks": clk,
-        "first_token": int(first.next_token_id),
+        "first_token": int(first),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -1075,6 +1081,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--ref-budget-s", type=float, default=120.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="decode workloads: sequences decoded in lockstep by one session (config: 1 and 16)")
     ap.add_argument("--workload", choices=["gemv_int4", *PF_WORKLOADS, *ATTN_WORKLOADS, "decode_llama1b",
                                            "decode_llama1b_tp", "qwen7b_tp"],
                     default="gemv_int4",

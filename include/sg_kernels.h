@@ -288,6 +288,15 @@ SgStatus sg_qkv_rope_append(const void* qkv, int32_t tokens, int32_t heads, int3
                             const int32_t* positions, int32_t pos0, float base, void* q_out, void* k_cache,
                             void* v_cache, int64_t kv_head_stride, int32_t io_dtype, void* stream);
 
+/* The same for `batch` sequences of seq_tokens tokens each (token t of the
+ * input is token t % seq_tokens of sequence t / seq_tokens): q goes to
+ * q_out [batch, heads, seq_tokens, head_dim], k / v of sequence b to the
+ * caches at b * kv_batch_stride (elements). */
+SgStatus sg_qkv_rope_append_batched(const void* qkv, int32_t batch, int32_t seq_tokens, int32_t heads,
+                                    int32_t kv_heads, int32_t head_dim, const int32_t* positions, int32_t pos0,
+                                    float base, void* q_out, void* k_cache, void* v_cache, int64_t kv_head_stride,
+                                    int64_t kv_batch_stride, int32_t io_dtype, void* stream);
+
 /* SwiGLU over the fused projection gate_up [rows, 2 * ffn] (gate columns, then
  * up columns): y[t, j] = round(silu(gate)) * up. */
 SgStatus sg_swiglu_rows(const void* gate_up, void* y, int32_t rows, int32_t ffn, int32_t io_dtype, void* stream);
@@ -296,15 +305,17 @@ SgStatus sg_swiglu_rows(const void* gate_up, void* y, int32_t rows, int32_t ffn,
  * logprob != NULL, logprob[r] = its log-softmax value. */
 SgStatus sg_argmax_logprob(const float* logits, int32_t rows, int32_t n, int32_t* out, float* logprob, void* stream);
 
-/* Greedy token across a vocabulary split over ranks (tensor parallelism).
- * pack: from this rank's logits shard, its local argmax idx and local
- * log-prob, writes out3 = {max logit, local log-sum-exp, vocab0 + idx}.
- * pick: from the ranks' triples in rank order ([world][3]), writes the
+/* Greedy token across a vocabulary split over ranks (tensor parallelism),
+ * one row per sequence.  pack: from this rank's logits shard [rows,
+ * vocab_local], its local argmax idx[rows] and local log-probs, writes
+ * out3[rows][3] = {max logit, local log-sum-exp, vocab0 + idx}.  pick: from
+ * the ranks' triples in rank order ([world][rows][3]), writes each row's
  * global greedy token (first rank among equal maxima, i.e. the lowest
  * vocabulary index) and its log-prob over the whole vocabulary. */
-SgStatus sg_tp_argmax_pack(const float* logits, const int32_t* idx, const float* logprob, int32_t vocab0,
-                           float* out3, void* stream);
-SgStatus sg_tp_argmax_pick(const float* all3, int32_t world, int32_t* next, float* logprob, void* stream);
+SgStatus sg_tp_argmax_pack(const float* logits, int32_t rows, int32_t vocab_local, const int32_t* idx,
+                           const float* logprob, int32_t vocab0, float* out3, void* stream);
+SgStatus sg_tp_argmax_pick(const float* all3, int32_t world, int32_t rows, int32_t* next, float* logprob,
+                           void* stream);
 
 /* in [heads, tokens, head_dim] -> out [tokens, heads, head_dim]. */
 SgStatus sg_head_transpose(const void* in, void* out, int32_t heads, int32_t tokens, int32_t head_dim,

@@ -15,8 +15,9 @@ extern "C" {
 
 /* Copies the fp32 logits of the last processed token (after
  * armsess_prefill, or after a armsess_decode that ran a step) into host
- * memory: min(n, vocab) values.  Returns ARMCC_OK, or an error status with
- * armpack_last_error() set. */
+ * memory: min(n, vocab) values, or for a batched session min(n, batch *
+ * vocab) values, sequence by sequence.  Returns ARMCC_OK, or an error
+ * status with armpack_last_error() set. */
 ArmStatus sg_session_last_logits(ArmSession* sess, float* host_out, uint32_t n);
 
 /* Number of tokens in the session's KV cache. */
@@ -64,6 +65,28 @@ ArmSession* sg_session_create_tp(ArmGraph* graph, const ArmSessionOptions* opts,
 /* The vocabulary range [lo, hi) whose logits sg_session_last_logits returns
  * (the whole vocabulary unless the session is tensor-parallel). */
 void sg_session_vocab_range(const ArmSession* sess, uint32_t* lo, uint32_t* hi);
+
+/* ---- batched greedy decoding ----------------------------------------------
+ * A session of `batch` sequences decoded in lockstep (one position for all):
+ * every linear runs on batch rows, attention on batch sequences of the
+ * session's KV cache [sequence][layer][K|V][kv_head][seq][dim].  rank /
+ * world / id as for sg_session_create_tp (world 1: no NCCL, id unused).
+ * armsess_prefill / armsess_decode serve batch-1 sessions; batched ones use
+ * the two calls below. */
+ArmSession* sg_session_create_ex(ArmGraph* graph, const ArmSessionOptions* opts, uint32_t batch, int32_t rank,
+                                 int32_t world, const uint8_t id[128]);
+
+/* Prefills every sequence with n_tokens tokens (tokens[b * n_tokens + i] is
+ * token i of sequence b). */
+ArmStatus sg_batch_prefill(ArmSession* sess, const int32_t* tokens, uint32_t n_tokens);
+
+/* Greedy tokens of all sequences into next_tokens[batch]: the first call
+ * after a prefill returns the tokens the prompts predict, later calls run
+ * one decode step each. */
+ArmStatus sg_batch_decode(ArmSession* sess, int32_t* next_tokens);
+
+/* Sequences of the session. */
+uint32_t sg_session_batch(const ArmSession* sess);
 
 #ifdef __cplusplus
 }

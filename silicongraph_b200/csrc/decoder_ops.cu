@@ -13,9 +13,10 @@
 namespace {
 
 template <typename T>
-__global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, int T_, int H, int Hkv, int D,
+__global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, int T_, int Ts, int H, int Hkv, int D,
                                        const int32_t* __restrict__ pos, int pos0, float base, T* __restrict__ q_out,
-                                       T* __restrict__ k_cache, T* __restrict__ v_cache, int64_t kv_head_stride) {
+                                       T* __restrict__ k_cache, T* __restrict__ v_cache, int64_t kv_head_stride,
+                                       int64_t kv_batch_stride) {
   sgd::pdl_wait();  // inputs come from the previous kernel on the stream
   sgd::pdl_launch_dependents();
   const int half = D / 2;
@@ -26,7 +27,8 @@ __global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, int T_, int H,
     const int64_t ts = e / half;
     const int slot = (int)(ts % slots);
     const int t = (int)(ts / slots);
-    const int p = pos ? pos[t] : pos0 + t;
+    const int b = t / Ts, tl = t - b * Ts;  // sequence, token within it
+    const int p = pos ? pos[tl] : pos0 + tl;
     const T* src = qkv + ((int64_t)t * slots + slot) * D;
     float x0 = (float)src[i], x1 = (float)src[i + half];
     if (slot < H + Hkv) {  // q and k rotate
@@ -37,9 +39,9 @@ __global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, int T_, int H,
       x1 = y1;
     }
     T* dst;
-    if (slot < H) dst = q_out + ((int64_t)slot * T_ + t) * D;
-    else if (slot < H + Hkv) dst = k_cache + (slot - H) * kv_head_stride + (int64_t)p * D;
-    else dst = v_cache + (slot - H - Hkv) * kv_head_stride + (int64_t)p * D;
+    if (slot < H) dst = q_out + (((int64_t)b * H + slot) * Ts + tl) * D;
+    else if (slot < H + Hkv) dst = k_cache + b * kv_batch_stride + (slot - H) * kv_head_stride + (int64_t)p * D;
+    else dst = v_cache + b * kv_batch_stride + (slot - H - Hkv) * kv_head_stride + (int64_t)p * D;
     dst[i] = (T)x0;
     dst[i + half] = (T)x1;
   }
@@ -222,38 +224,39 @@ int grid_of(int64_t n) {
   return (int)(b < 1 ? 1 : (b > 148 * 16 ? 148 * 16 : b));
 }
 
-// Tensor-parallel greedy token: per-rank triple, then the pick over ranks.
-__global__ void tp_argmax_pack_kernel(const float* __restrict__ logits, const int32_t* __restrict__ idx,
-                                      const float* __restrict__ logprob, int vocab0, float* __restrict__ out) {
+// Tensor-parallel greedy token: per-rank triples, then the pick over ranks (one row per sequence).
+__global__ void tp_argmax_pack_kernel(const float* __restrict__ logits, int vocab_local, const int32_t* __restrict__ idx,
+                                      const float* __restrict__ logprob, int vocab0, int rows, float* __restrict__ out) {
   sgd::pdl_wait();
   sgd::pdl_launch_dependents();
-  if (threadIdx.x == 0) {
-    const int i = *idx;
-    const float m = logits[i];
-    out[0] = m;
-    out[1] = m - *logprob;  // log-sum-exp of this rank's shard
-    out[2] = (float)(vocab0 + i);
+  for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+    const int i = idx[r];
+    const float m = logits[(int64_t)r * vocab_local + i];
+    out[3 * r] = m;
+    out[3 * r + 1] = m - logprob[r];  // log-sum-exp of this rank's shard
+    out[3 * r + 2] = (float)(vocab0 + i);
   }
 }
 
-__global__ void tp_argmax_pick_kernel(const float* __restrict__ all, int world, int32_t* __restrict__ next,
+__global__ void tp_argmax_pick_kernel(const float* __restrict__ all, int world, int rows, int32_t* __restrict__ next,
                                       float* __restrict__ logprob) {
   sgd::pdl_wait();
   sgd::pdl_launch_dependents();
-  if (threadIdx.x == 0) {
+  for (int r = threadIdx.x; r < rows; r += blockDim.x) {
     int best = 0;
-    float M = all[0], Lmax = all[1];
-    for (int r = 1; r < world; ++r) {
-      if (all[3 * r] > M) {
-        M = all[3 * r];
-        best = r;
+    float M = all[3 * r], Lmax = all[3 * r + 1];
+    for (int w = 1; w < world; ++w) {
+      const float* tw = all + 3 * ((int64_t)w * rows + r);
+      if (tw[0] > M) {
+        M = tw[0];
+        best = w;
       }
-      Lmax = fmaxf(Lmax, all[3 * r + 1]);
+      Lmax = fmaxf(Lmax, tw[1]);
     }
     float s = 0.f;
-    for (int r = 0; r < world; ++r) s += expf(all[3 * r + 1] - Lmax);
-    *next = (int32_t)all[3 * best + 2];
-    if (logprob) *logprob = M - (Lmax + logf(s));
+    for (int w = 0; w < world; ++w) s += expf(all[3 * ((int64_t)w * rows + r) + 1] - Lmax);
+    next[r] = (int32_t)all[3 * ((int64_t)best * rows + r) + 2];
+    if (logprob) logprob[r] = M - (Lmax + logf(s));
   }
 }
 
@@ -261,30 +264,45 @@ __global__ void tp_argmax_pick_kernel(const float* __restrict__ all, int world, 
 
 extern "C" {
 
-SgStatus sg_qkv_rope_append(const void* qkv, int32_t tokens, int32_t heads, int32_t kv_heads, int32_t head_dim,
-                            const int32_t* positions, int32_t pos0, float base, void* q_out, void* k_cache,
-                            void* v_cache, int64_t kv_head_stride, int32_t io_dtype, void* stream) {
-  SG_CHECK_ARG(tokens >= 0 && heads > 0 && kv_heads > 0 && head_dim > 0, "sg_qkv_rope_append: bad size");
+SgStatus sg_qkv_rope_append_batched(const void* qkv, int32_t batch, int32_t seq_tokens, int32_t heads,
+                                    int32_t kv_heads, int32_t head_dim, const int32_t* positions, int32_t pos0,
+                                    float base, void* q_out, void* k_cache, void* v_cache, int64_t kv_head_stride,
+                                    int64_t kv_batch_stride, int32_t io_dtype, void* stream) {
+  SG_CHECK_ARG(batch >= 0 && seq_tokens >= 0 && heads > 0 && kv_heads > 0 && head_dim > 0,
+               "sg_qkv_rope_append: bad size");
+  const int64_t tokens = (int64_t)batch * seq_tokens;
   if (tokens == 0) return SG_OK;
+  SG_CHECK_ARG(tokens <= INT32_MAX, "sg_qkv_rope_append: too many tokens");
   SG_CHECK_ARG(qkv && q_out && k_cache && v_cache, "sg_qkv_rope_append: NULL pointer");
   SG_CHECK_ARG(head_dim % 2 == 0, "sg_qkv_rope_append: head_dim %d is odd", head_dim);
   SG_CHECK_ARG(kv_head_stride >= head_dim, "sg_qkv_rope_append: kv_head_stride < head_dim");
+  SG_CHECK_ARG(batch == 1 || kv_batch_stride >= kv_heads * kv_head_stride,
+               "sg_qkv_rope_append: kv_batch_stride smaller than one sequence's cache");
   const int dt = io_dtype == SG_DT_DEFAULT ? SG_DT_F16 : io_dtype;
   SG_CHECK_ARG(dt == SG_DT_F16 || dt == SG_DT_BF16, "sg_qkv_rope_append: io_dtype %d unsupported", io_dtype);
   cudaStream_t cs = static_cast<cudaStream_t>(stream);
-  const int64_t total = (int64_t)tokens * (heads + 2 * kv_heads) * (head_dim / 2);
+  const int64_t total = tokens * (heads + 2 * kv_heads) * (head_dim / 2);
   if (dt == SG_DT_F16)
     SG_CUDA_TRY(sgd::launch_pdl(qkv_rope_append_kernel<__half>, dim3(grid_of(total)), dim3(256), 0, cs,
-                                static_cast<const __half*>(qkv), (int)tokens, (int)heads, (int)kv_heads,
-                                (int)head_dim, positions, (int)pos0, base, static_cast<__half*>(q_out),
-                                static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), kv_head_stride));
+                                static_cast<const __half*>(qkv), (int)tokens, (int)seq_tokens, (int)heads,
+                                (int)kv_heads, (int)head_dim, positions, (int)pos0, base, static_cast<__half*>(q_out),
+                                static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), kv_head_stride,
+                                kv_batch_stride));
   else
     SG_CUDA_TRY(sgd::launch_pdl(qkv_rope_append_kernel<__nv_bfloat16>, dim3(grid_of(total)), dim3(256), 0, cs,
-                                static_cast<const __nv_bfloat16*>(qkv), (int)tokens, (int)heads, (int)kv_heads,
-                                (int)head_dim, positions, (int)pos0, base, static_cast<__nv_bfloat16*>(q_out),
-                                static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache),
-                                kv_head_stride));
-  return sg::check_launch("sg_qkv_rope_append");
+                                static_cast<const __nv_bfloat16*>(qkv), (int)tokens, (int)seq_tokens, (int)heads,
+                                (int)kv_heads, (int)head_dim, positions, (int)pos0, base,
+                                static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_cache),
+                                static_cast<__nv_bfloat16*>(v_cache), kv_head_stride, kv_batch_stride));
+  return SG_OK;
+}
+
+SgStatus sg_qkv_rope_append(const void* qkv, int32_t tokens, int32_t heads, int32_t kv_heads, int32_t head_dim,
+                            const int32_t* positions, int32_t pos0, float base, void* q_out, void* k_cache,
+                            void* v_cache, int64_t kv_head_stride, int32_t io_dtype, void* stream) {
+  SG_CHECK_ARG(tokens >= 0, "sg_qkv_rope_append: bad size");
+  return sg_qkv_rope_append_batched(qkv, 1, tokens, heads, kv_heads, head_dim, positions, pos0, base, q_out, k_cache,
+                                    v_cache, kv_head_stride, 0, io_dtype, stream);
 }
 
 SgStatus sg_head_transpose(const void* in, void* out, int32_t heads, int32_t tokens, int32_t head_dim,
@@ -342,18 +360,19 @@ SgStatus sg_argmax_logprob(const float* logits, int32_t rows, int32_t n, int32_t
   return SG_OK;
 }
 
-SgStatus sg_tp_argmax_pack(const float* logits, const int32_t* idx, const float* logprob, int32_t vocab0,
-                           float* out3, void* stream) {
-  SG_CHECK_ARG(logits && idx && logprob && out3, "sg_tp_argmax_pack: NULL pointer");
-  SG_CUDA_TRY(sgd::launch_pdl(tp_argmax_pack_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), logits,
-                              idx, logprob, (int)vocab0, out3));
+SgStatus sg_tp_argmax_pack(const float* logits, int32_t rows, int32_t vocab_local, const int32_t* idx,
+                           const float* logprob, int32_t vocab0, float* out3, void* stream) {
+  SG_CHECK_ARG(logits && idx && logprob && out3 && rows >= 1 && vocab_local >= 1, "sg_tp_argmax_pack: bad argument");
+  SG_CUDA_TRY(sgd::launch_pdl(tp_argmax_pack_kernel, dim3(1), dim3(128), 0, static_cast<cudaStream_t>(stream), logits,
+                              (int)vocab_local, idx, logprob, (int)vocab0, (int)rows, out3));
   return SG_OK;
 }
 
-SgStatus sg_tp_argmax_pick(const float* all3, int32_t world, int32_t* next, float* logprob, void* stream) {
-  SG_CHECK_ARG(all3 && next && world >= 1, "sg_tp_argmax_pick: bad argument");
-  SG_CUDA_TRY(sgd::launch_pdl(tp_argmax_pick_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), all3,
-                              (int)world, next, logprob));
+SgStatus sg_tp_argmax_pick(const float* all3, int32_t world, int32_t rows, int32_t* next, float* logprob,
+                           void* stream) {
+  SG_CHECK_ARG(all3 && next && world >= 1 && rows >= 1, "sg_tp_argmax_pick: bad argument");
+  SG_CUDA_TRY(sgd::launch_pdl(tp_argmax_pick_kernel, dim3(1), dim3(128), 0, static_cast<cudaStream_t>(stream), all3,
+                              (int)world, (int)rows, next, logprob));
   return SG_OK;
 }
 

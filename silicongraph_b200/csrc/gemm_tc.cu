@@ -536,7 +536,7 @@ __global__ void act_convert_kernel(const void* A, int a_dt, int lda, int M, int 
 constexpr size_t kConvOffset = 64 * 1024;
 
 std::atomic<int> g_tune_bt{0};        // 0 = automatic
-std::atomic<int> g_tune_min_rows{64};  // smallest M sent to the tensor-core GEMM
+std::atomic<int> g_tune_min_rows{5};  // smallest M sent to the tensor-core GEMM (4 rows and fewer: GEMV kernels)
 std::atomic<int> g_tune_par{2};        // dequant warp groups working on alternate k steps
 std::atomic<int> g_tune_spin{0};       // single-thread waits spin on test_wait
 std::atomic<int> g_tune_tma_store{1};  // 16-bit outputs through TMA stores

@@ -215,13 +215,14 @@ struct Plan {
   }
 };
 
-Plan make_plan(const ModelCfg& c, int T) {
+// T = rows of one forward pass (sequences x tokens per sequence), B = sequences.
+Plan make_plan(const ModelCfg& c, int T, int B, int world) {
   const uint64_t H = c.hidden, e = 2;
   Plan p;
   p.bufs = {
       {"ids", (uint64_t)T * 4, kOpEmbed, kOpArgmax},
-      {"next", 4, kOpEmbed, kOpArgmax},
-      {"logprob", 4, kOpEmbed, kOpArgmax},
+      {"next", (uint64_t)B * 4, kOpEmbed, kOpArgmax},
+      {"logprob", (uint64_t)B * 4, kOpEmbed, kOpArgmax},
       {"pos", 4, kOpEmbed, kOpArgmax},
       {"resid", T * H * e, kOpEmbed, kOpFinalNorm},
       {"x_emb", T * H * e, kOpEmbed, kOpNorm1},
@@ -234,9 +235,12 @@ Plan make_plan(const ModelCfg& c, int T) {
       {"gu", (uint64_t)T * 2 * c.ffn * e, kOpGu, kOpSwiglu},
       {"act", (uint64_t)T * c.ffn * e, kOpSwiglu, kOpDown},
       {"down", T * H * e, kOpDown, kOpFinalNorm},
-      {"logits", (uint64_t)c.vocab * 4, kOpLm, kOpArgmax},
-      {"tp_mine", 16, kOpArgmax, kOpArgmax},
-      {"tp_all", 16 * 64, kOpArgmax, kOpArgmax},
+      {"last_x", (uint64_t)B * H * e, kOpFinalNorm, kOpLm},  // each sequence's last row
+      {"last_r", (uint64_t)B * H * e, kOpFinalNorm, kOpLm},
+      {"last_n", (uint64_t)B * H * e, kOpFinalNorm, kOpLm},
+      {"logits", (uint64_t)B * c.vocab * 4, kOpLm, kOpArgmax},
+      {"tp_mine", (uint64_t)B * 12, kOpArgmax, kOpArgmax},
+      {"tp_all", (uint64_t)world * B * 12, kOpArgmax, kOpArgmax},
   };
   p.bytes = plan_offsets(p.bufs, 256);
   return p;
@@ -391,6 +395,9 @@ struct ArmSession_ {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t graph_exec = nullptr;
   int32_t* h_pos = nullptr;  // pinned
+  // sequences decoded together (sg_session_create_ex), in lockstep at one position
+  int batch = 1;
+  std::vector<int32_t> next_all;  // host copy of every sequence's greedy token
   // tensor parallelism (tp_world == 1: a whole-model session)
   int tp_rank = 0, tp_world = 1;
   SgTpShard shard{};
@@ -410,6 +417,8 @@ struct ArmSession_ {
 
   template <typename T>
   T* buf(const char* n) { return reinterpret_cast<T*>(act + plan.off(n)); }
+  // KV cache [sequence][layer][K|V][kv_head][seq][dim]
+  int64_t kv_bstride() const { return (int64_t)c.layers * 2 * kv_block; }  // elements per sequence
   void* kcache(int l) { return kv + (size_t)(2 * l) * kv_block * 2; }
   void* vcache(int l) { return kv + (size_t)(2 * l + 1) * kv_block * 2; }
 };
@@ -459,13 +468,15 @@ ArmStatus linear(ArmSession_* S, const Linear& L, const void* A, void* C, int M,
   return ARMCC_OK;
 }
 
-// One forward pass over T tokens at positions pos .. pos+T-1 (ids already in
-// the "ids" buffer, or the device-resident next token when from_next).  With
-// dev_pos (one decode token) the kernels read the position from the "pos"
+// One forward pass over Ts tokens of each of the session's B sequences, at
+// positions pos .. pos+Ts-1 (ids already in the "ids" buffer, sequence-major,
+// or the device-resident next tokens when from_next).  With dev_pos (one
+// decode token per sequence) the kernels read the position from the "pos"
 // buffer instead of launch arguments, so the launches can be captured once.
-ArmStatus forward(ArmSession_* S, int T, bool from_next, bool dev_pos = false) {
+ArmStatus forward(ArmSession_* S, int Ts, bool from_next, bool dev_pos = false) {
   const ModelCfg& c = S->c;
   cudaStream_t st = S->st;
+  const int B = S->batch, T = B * Ts;
   const int H = c.hidden, D = c.head_dim;
   const int32_t* ids = from_next ? S->buf<int32_t>("next") : S->buf<int32_t>("ids");
   SG_TRY(sg_embedding(S->embed, ids, S->buf<void>("x_emb"), T, H, c.vocab_global, SG_DT_F16, st), "embedding");
@@ -480,37 +491,41 @@ ArmStatus forward(ArmSession_* S, int T, bool from_next, bool dev_pos = false) {
                       st),
            "input rmsnorm");
     if ((r = linear(S, S->qkv[l], S->buf<void>("xnorm"), S->buf<void>("qkv"), T, SG_DT_F16)) != ARMCC_OK) return r;
-    SG_TRY(sg_qkv_rope_append(S->buf<void>("qkv"), T, c.heads, c.kv_heads, D,
-                              dev_pos ? S->buf<int32_t>("pos") : nullptr, S->pos, c.rope_theta,
-                              S->buf<void>("qh"), S->kcache(l), S->vcache(l), S->kv_head_stride, SG_DT_F16, st),
+    SG_TRY(sg_qkv_rope_append_batched(S->buf<void>("qkv"), B, Ts, c.heads, c.kv_heads, D,
+                                      dev_pos ? S->buf<int32_t>("pos") : nullptr, S->pos, c.rope_theta,
+                                      S->buf<void>("qh"), S->kcache(l), S->vcache(l), S->kv_head_stride,
+                                      S->kv_bstride(), SG_DT_F16, st),
            "rope / KV append");
     SgFlashAttentionParams a{};
     a.Q = S->buf<void>("qh");
     a.K = S->kcache(l);
     a.V = S->vcache(l);
     a.O = S->buf<void>("attn");
-    a.B = 1;
-    a.S = T;
+    a.B = B;
+    a.S = Ts;
     a.num_heads = c.heads;
     a.num_kv_heads = c.kv_heads;
     a.head_dim = D;
     a.scale = 0.f;
     a.causal = 1;
     a.io_dtype = SG_DT_F16;
-    a.S_kv = dev_pos ? c.max_context : S->pos + T;
+    a.S_kv = dev_pos ? c.max_context : S->pos + Ts;
     a.q_pos0 = dev_pos ? 0 : S->pos;
     a.q_pos_device = dev_pos ? S->buf<int32_t>("pos") : nullptr;
     a.kv_head_stride = S->kv_head_stride;
-    a.kv_batch_stride = S->kv_block;
+    a.kv_batch_stride = S->kv_bstride();
     a.workspace = S->attn_ws;
     a.workspace_bytes = S->attn_ws_bytes;
     const void* attn_rows = S->buf<void>("attn");
-    if (T == 1) {
-      SG_TRY(sg_flash_decode(&a, st), "decode attention");
+    if (Ts == 1) {
+      SG_TRY(sg_flash_decode(&a, st), "decode attention");  // [B, H, 1, D] = B rows of H * D
     } else {
       SG_TRY(sg_flash_attention(&a, st), "prefill attention");
-      SG_TRY(sg_head_transpose(S->buf<void>("attn"), S->buf<void>("attn_t"), c.heads, T, D, SG_DT_F16, st),
-             "head transpose");
+      const size_t seq = (size_t)c.heads * Ts * D * 2;  // bytes of one sequence's [H, Ts, D]
+      for (int b = 0; b < B; ++b)
+        SG_TRY(sg_head_transpose(S->buf<char>("attn") + b * seq, S->buf<char>("attn_t") + b * seq, c.heads, Ts, D,
+                                 SG_DT_F16, st),
+               "head transpose");
       attn_rows = S->buf<void>("attn_t");
     }
     if ((r = linear(S, S->o[l], attn_rows, S->buf<void>("o"), T, SG_DT_F16)) != ARMCC_OK) return r;
@@ -523,45 +538,56 @@ ArmStatus forward(ArmSession_* S, int T, bool from_next, bool dev_pos = false) {
     if ((r = linear(S, S->down[l], S->buf<void>("act"), S->buf<void>("down"), T, SG_DT_F16)) != ARMCC_OK) return r;
     if ((r = tp_sum(S, S->buf<void>("down"), (size_t)T * H)) != ARMCC_OK) return r;
   }
-  // last token: final norm, LM head, greedy token
-  const size_t last = (size_t)(T - 1) * H * 2;
-  char* down_last = S->buf<char>("down") + last;
-  char* resid_last = S->buf<char>("resid") + last;
-  char* xn_last = S->buf<char>("xnorm") + last;
-  SG_TRY(sg_rmsnorm(down_last, resid_last, S->final_norm, xn_last, 1, H, c.rms_eps, SG_DT_F16, st), "final rmsnorm");
+  // each sequence's last token: final norm, LM head, greedy token
+  const void *x_last = S->buf<void>("down"), *r_last = S->buf<void>("resid");
+  if (Ts > 1) {
+    const size_t row = (size_t)H * 2, pitch = (size_t)Ts * row, off = (size_t)(Ts - 1) * row;
+    if (cudaMemcpy2DAsync(S->buf<void>("last_x"), row, S->buf<char>("down") + off, pitch, row, B,
+                          cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+        cudaMemcpy2DAsync(S->buf<void>("last_r"), row, S->buf<char>("resid") + off, pitch, row, B,
+                          cudaMemcpyDeviceToDevice, st) != cudaSuccess) {
+      set_err("gathering the last rows failed");
+      return ARMCC_ERR_RUNTIME;
+    }
+    x_last = S->buf<void>("last_x");
+    r_last = S->buf<void>("last_r");
+  }
+  SG_TRY(sg_rmsnorm(x_last, const_cast<void*>(r_last), S->final_norm, S->buf<void>("last_n"), B, H, c.rms_eps,
+                    SG_DT_F16, st),
+         "final rmsnorm");
   if (c.lm_int4) {
-    if ((r = linear(S, S->lm, xn_last, S->buf<void>("logits"), 1, SG_DT_F32)) != ARMCC_OK) return r;
+    if ((r = linear(S, S->lm, S->buf<void>("last_n"), S->buf<void>("logits"), B, SG_DT_F32)) != ARMCC_OK) return r;
   } else {
     SgMatMulParams p{};
-    p.A = xn_last;
+    p.A = S->buf<void>("last_n");
     p.B = S->lm_f16;
     p.C = S->buf<void>("logits");
-    p.M = 1;
+    p.M = B;
     p.K = H;
     p.N = c.vocab;
     p.a_dtype = SG_DT_F16;
     p.c_dtype = SG_DT_F32;
     SG_TRY(sg_matmul_fp16(&p, st), "LM head");
   }
-  SG_TRY(sg_argmax_logprob(S->buf<float>("logits"), 1, c.vocab, S->buf<int32_t>("next"), S->buf<float>("logprob"),
+  SG_TRY(sg_argmax_logprob(S->buf<float>("logits"), B, c.vocab, S->buf<int32_t>("next"), S->buf<float>("logprob"),
                            st),
          "argmax");
   if (S->tp_world > 1) {
-    // every rank's (max, log-sum-exp, index), gathered in rank order, then the global pick
-    SG_TRY(sg_tp_argmax_pack(S->buf<float>("logits"), S->buf<int32_t>("next"), S->buf<float>("logprob"),
+    // every rank's (max, log-sum-exp, index) per sequence, gathered in rank order, then the global pick
+    SG_TRY(sg_tp_argmax_pack(S->buf<float>("logits"), B, c.vocab, S->buf<int32_t>("next"), S->buf<float>("logprob"),
                              S->shard.vocab0, S->buf<float>("tp_mine"), st),
            "tensor-parallel argmax");
-    const ncclResult_t e = nccl_api().all_gather(S->buf<float>("tp_mine"), S->buf<float>("tp_all"), 3, ncclFloat,
-                                                 S->comm, st);
+    const ncclResult_t e = nccl_api().all_gather(S->buf<float>("tp_mine"), S->buf<float>("tp_all"), (size_t)3 * B,
+                                                 ncclFloat, S->comm, st);
     if (e != ncclSuccess) {
       set_err("ncclAllGather failed: %s", nccl_api().error_string(e));
       return ARMCC_ERR_RUNTIME;
     }
-    SG_TRY(sg_tp_argmax_pick(S->buf<float>("tp_all"), S->tp_world, S->buf<int32_t>("next"), S->buf<float>("logprob"),
-                             st),
+    SG_TRY(sg_tp_argmax_pick(S->buf<float>("tp_all"), S->tp_world, B, S->buf<int32_t>("next"),
+                             S->buf<float>("logprob"), st),
            "tensor-parallel argmax");
   }
-  S->pos += T;
+  S->pos += Ts;
   return ARMCC_OK;
 }
 
@@ -608,11 +634,12 @@ ArmStatus decode_step(ArmSession_* S) {
   return r;
 }
 
-// Reads the greedy token (and the kernels' error word) back to the host.
+// Reads every sequence's greedy token (and the kernels' error word) back to the host.
 ArmStatus fetch_next(ArmSession_* S) {
-  int32_t tok = -1;
+  S->next_all.assign(S->batch, -1);
   float lp = 0;
-  if (cudaMemcpyAsync(&tok, S->buf<int32_t>("next"), 4, cudaMemcpyDeviceToHost, S->st) != cudaSuccess ||
+  if (cudaMemcpyAsync(S->next_all.data(), S->buf<int32_t>("next"), (size_t)S->batch * 4, cudaMemcpyDeviceToHost,
+                      S->st) != cudaSuccess ||
       cudaMemcpyAsync(&lp, S->buf<float>("logprob"), 4, cudaMemcpyDeviceToHost, S->st) != cudaSuccess ||
       cudaStreamSynchronize(S->st) != cudaSuccess) {
     set_err("device error: %s", cudaGetErrorString(cudaGetLastError()));
@@ -623,8 +650,86 @@ ArmStatus fetch_next(ArmSession_* S) {
     set_err("a kernel reported device error %d (%s)", derr, sg_last_error());
     return ARMCC_ERR_RUNTIME;
   }
-  S->next_host = tok;
+  S->next_host = S->next_all[0];
   S->logprob_host = lp;
+  return ARMCC_OK;
+}
+
+// Prefill of n tokens per sequence (tokens sequence-major: sequence b's
+// token i at tokens[b * n + i]), in chunks of at most max_chunk per sequence.
+ArmStatus prefill_tokens(ArmSession_* S, const int32_t* tokens, uint32_t n, const char* fn) {
+  const ModelCfg& c = S->c;
+  if ((uint64_t)S->pos + n > (uint64_t)c.max_context) {
+    set_err("%s: %u tokens after %d exceed the context of %d", fn, n, S->pos, c.max_context);
+    return ARMCC_ERR_OOM;
+  }
+  for (uint64_t i = 0; i < (uint64_t)n * S->batch; ++i)
+    if (tokens[i] < 0 || tokens[i] >= c.vocab_global) {
+      set_err("%s: token %d at %llu is outside the vocabulary", fn, tokens[i], (unsigned long long)i);
+      return ARMCC_ERR_RUNTIME;
+    }
+  if (cudaSetDevice(S->dev) != cudaSuccess) {
+    set_err("%s: cannot use device %d", fn, S->dev);
+    return ARMCC_ERR_RUNTIME;
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  std::vector<int32_t> chunk;
+  for (uint32_t done = 0; done < n;) {
+    const int T = (int)std::min<uint32_t>(n - done, (uint32_t)c.max_chunk);
+    const int32_t* src = tokens + done;
+    if (S->batch > 1) {  // gather this chunk of every sequence
+      chunk.resize((size_t)S->batch * T);
+      for (int b = 0; b < S->batch; ++b)
+        memcpy(chunk.data() + (size_t)b * T, tokens + (size_t)b * n + done, (size_t)T * 4);
+      src = chunk.data();
+    }
+    if (cudaMemcpyAsync(S->buf<int32_t>("ids"), src, (size_t)S->batch * T * 4, cudaMemcpyHostToDevice, S->st) !=
+            cudaSuccess ||
+        (S->batch > 1 && cudaStreamSynchronize(S->st) != cudaSuccess)) {  // the gather buffer is reused
+      set_err("%s: copying token ids failed", fn);
+      return ARMCC_ERR_RUNTIME;
+    }
+    const ArmStatus r = forward(S, T, false);
+    if (r != ARMCC_OK) return r;
+    done += T;
+  }
+  const ArmStatus r = fetch_next(S);
+  if (r != ARMCC_OK) return r;
+  S->emitted = false;
+  S->t_prefill_start = t0;
+  S->ttft_pending = true;
+  return ARMCC_OK;
+}
+
+// Emits the pending greedy tokens, running one decode step first when the
+// previous ones were already emitted.
+ArmStatus step_tokens(ArmSession_* S, const char* fn, float* step_ms) {
+  if (S->pos == 0) {
+    set_err("%s: prefill a prompt first", fn);
+    return ARMCC_ERR_RUNTIME;
+  }
+  cudaSetDevice(S->dev);
+  const auto t0 = std::chrono::steady_clock::now();
+  if (S->emitted) {
+    // feed the last emitted tokens (still on the device) and predict the next ones
+    if (S->pos + 1 > S->c.max_context) {
+      set_err("%s: the context of %d tokens is full", fn, S->c.max_context);
+      return ARMCC_ERR_OOM;
+    }
+    ArmStatus r = decode_step(S);
+    if (r == ARMCC_OK) r = fetch_next(S);
+    if (r != ARMCC_OK) return r;
+  }
+  const auto t1 = std::chrono::steady_clock::now();
+  S->emitted = true;
+  S->generated += 1;
+  *step_ms = std::chrono::duration<float, std::milli>(t1 - t0).count();
+  if (S->ttft_pending) {
+    S->ttft_ms = std::chrono::duration<float, std::milli>(t1 - S->t_prefill_start).count();
+    S->ttft_pending = false;
+  } else {
+    S->tpot_ms = S->generated > 1 ? (S->tpot_ms * (S->generated - 2) + *step_ms) / (S->generated - 1) : *step_ms;
+  }
   return ARMCC_OK;
 }
 
@@ -709,7 +814,8 @@ bool shard_linear(ArmGraph_* g, const std::string& name, int K, int N, int r0, i
 }
 
 // Session of rank `rank` in a group of `world` (world 1: the whole model, no NCCL).
-ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int rank, int world, const uint8_t* id) {
+ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int rank, int world, const uint8_t* id,
+                           int batch) {
   const char* fn = world > 1 ? "sg_session_create_tp" : "armgraph_create_session";
   if (!graph) {
     set_err("%s: graph is NULL", fn);
@@ -723,11 +829,16 @@ ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int r
     set_err("%s: use_gpu is false, but this library only runs on the GPU", fn);
     return nullptr;
   }
+  if (batch < 1 || batch > 1024) {
+    set_err("%s: batch %d outside [1, 1024]", fn, batch);
+    return nullptr;
+  }
   auto S = std::make_unique<ArmSession_>();
   S->g = graph;
   S->c = graph->cfg;
   S->tp_rank = rank;
   S->tp_world = world;
+  S->batch = batch;
   const ModelCfg& gc = graph->cfg;
   std::string why;
   if (world > 1) {
@@ -816,14 +927,15 @@ ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int r
   size_t lws = 0;
   // every token count a call can see: the row kernels' scratch depends on M
   // below the tensor-core GEMM's threshold
-  for (int M = 1; M <= T; M = (M < 64 ? M + 1 : (M == T ? T + 1 : std::min(2 * M, T)))) {
+  const int TB = T * batch;  // rows of the largest forward pass
+  for (int M = 1; M <= TB; M = (M < 64 ? M + 1 : (M == TB ? TB + 1 : std::min(2 * M, TB)))) {
     lws = std::max({lws, lin_ws(M, c.hidden, c.nqkv(), SG_DT_F16), lin_ws(M, c.heads * c.head_dim, c.hidden, SG_DT_F16),
                     lin_ws(M, c.hidden, 2 * c.ffn, SG_DT_F16), lin_ws(M, c.ffn, c.hidden, SG_DT_F16)});
   }
-  lws = std::max(lws, lin_ws(1, c.hidden, c.vocab, SG_DT_F32));
+  lws = std::max(lws, lin_ws(batch, c.hidden, c.vocab, SG_DT_F32));
   SgFlashAttentionParams ap{};
   ap.Q = ap.K = ap.V = ap.O = reinterpret_cast<void*>(256);
-  ap.B = 1;
+  ap.B = batch;
   ap.num_heads = c.heads;
   ap.num_kv_heads = c.kv_heads;
   ap.head_dim = c.head_dim;
@@ -906,12 +1018,12 @@ ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int r
     }
   }
   // slab layout
-  S->plan = make_plan(c, T);
+  S->plan = make_plan(c, T * batch, batch, world);
   S->kv_head_stride = (int64_t)c.max_context * c.head_dim;
   S->kv_block = (int64_t)c.kv_heads * S->kv_head_stride;
   const uint64_t off_w = 0;
   const uint64_t off_kv = align_up(off_w + w_region, 4096);
-  const uint64_t kv_bytes = (uint64_t)c.layers * 2 * S->kv_block * 2;
+  const uint64_t kv_bytes = (uint64_t)batch * c.layers * 2 * S->kv_block * 2;
   const uint64_t off_act = align_up(off_kv + kv_bytes, 4096);
   const uint64_t off_lws = align_up(off_act + S->plan.bytes, 4096);
   S->lin_ws_bytes = align_up(std::max<size_t>(lws, 4096), 256);
@@ -1120,7 +1232,7 @@ float armgraph_estimated_tpot_ms(const ArmGraph* graph) { return graph ? graph->
 uint64_t armgraph_peak_memory_bytes(const ArmGraph* graph) { return graph ? graph->peak_bytes : 0; }
 
 ArmSession* armgraph_create_session(ArmGraph* graph, const ArmSessionOptions* opts) {
-  return create_session(graph, opts, 0, 1, nullptr);
+  return create_session(graph, opts, 0, 1, nullptr, 1);
 }
 
 void armsess_destroy(ArmSession* sess) {
@@ -1142,39 +1254,12 @@ ArmStatus armsess_prefill(ArmSession* sess, const int32_t* tokens, uint32_t n_to
     set_err("armsess_prefill: NULL argument");
     return ARMCC_ERR_RUNTIME;
   }
+  if (sess->batch != 1) {
+    set_err("armsess_prefill: the session decodes %d sequences; use sg_batch_prefill", sess->batch);
+    return ARMCC_ERR_UNSUPPORTED;
+  }
   if (n_tokens == 0) return ARMCC_OK;
-  const ModelCfg& c = sess->c;
-  if ((uint64_t)sess->pos + n_tokens > (uint64_t)c.max_context) {
-    set_err("armsess_prefill: %u tokens after %d exceed the context of %d", n_tokens, sess->pos, c.max_context);
-    return ARMCC_ERR_OOM;
-  }
-  for (uint32_t i = 0; i < n_tokens; ++i)
-    if (tokens[i] < 0 || tokens[i] >= c.vocab_global) {
-      set_err("armsess_prefill: token %d at %u is outside the vocabulary", tokens[i], i);
-      return ARMCC_ERR_RUNTIME;
-    }
-  if (cudaSetDevice(sess->dev) != cudaSuccess) {
-    set_err("armsess_prefill: cannot use device %d", sess->dev);
-    return ARMCC_ERR_RUNTIME;
-  }
-  const auto t0 = std::chrono::steady_clock::now();
-  for (uint32_t done = 0; done < n_tokens;) {
-    const int T = (int)std::min<uint32_t>(n_tokens - done, (uint32_t)c.max_chunk);
-    if (cudaMemcpyAsync(sess->buf<int32_t>("ids"), tokens + done, (size_t)T * 4, cudaMemcpyHostToDevice, sess->st) !=
-        cudaSuccess) {
-      set_err("armsess_prefill: copying token ids failed");
-      return ARMCC_ERR_RUNTIME;
-    }
-    const ArmStatus r = forward(sess, T, false);
-    if (r != ARMCC_OK) return r;
-    done += T;
-  }
-  const ArmStatus r = fetch_next(sess);
-  if (r != ARMCC_OK) return r;
-  sess->emitted = false;
-  sess->t_prefill_start = t0;
-  sess->ttft_pending = true;
-  return ARMCC_OK;
+  return prefill_tokens(sess, tokens, n_tokens, "armsess_prefill");
 }
 
 ArmInferenceResult armsess_decode(ArmSession* sess) {
@@ -1185,37 +1270,16 @@ ArmInferenceResult armsess_decode(ArmSession* sess) {
     res.status = ARMCC_ERR_RUNTIME;
     return res;
   }
-  if (sess->pos == 0) {
-    set_err("armsess_decode: prefill a prompt first");
-    res.status = ARMCC_ERR_RUNTIME;
+  if (sess->batch != 1) {
+    set_err("armsess_decode: the session decodes %d sequences; use sg_batch_decode", sess->batch);
+    res.status = ARMCC_ERR_UNSUPPORTED;
     return res;
   }
-  cudaSetDevice(sess->dev);
-  const auto t0 = std::chrono::steady_clock::now();
-  if (sess->emitted) {
-    // feed the last emitted token (still on the device) and predict the next one
-    if (sess->pos + 1 > sess->c.max_context) {
-      set_err("armsess_decode: the context of %d tokens is full", sess->c.max_context);
-      res.status = ARMCC_ERR_OOM;
-      return res;
-    }
-    ArmStatus r = decode_step(sess);
-    if (r == ARMCC_OK) r = fetch_next(sess);
-    if (r != ARMCC_OK) {
-      res.status = r;
-      return res;
-    }
-  }
-  const auto t1 = std::chrono::steady_clock::now();
-  sess->emitted = true;
-  sess->generated += 1;
-  const float step_ms = std::chrono::duration<float, std::milli>(t1 - t0).count();
-  if (sess->ttft_pending) {
-    sess->ttft_ms = std::chrono::duration<float, std::milli>(t1 - sess->t_prefill_start).count();
-    sess->ttft_pending = false;
-  } else {
-    sess->tpot_ms = sess->generated > 1 ? (sess->tpot_ms * (sess->generated - 2) + step_ms) / (sess->generated - 1)
-                                        : step_ms;
+  float step_ms = 0;
+  const ArmStatus r = step_tokens(sess, "armsess_decode", &step_ms);
+  if (r != ARMCC_OK) {
+    res.status = r;
+    return res;
   }
   res.next_token_id = sess->next_host;
   res.logprob = sess->logprob_host;
@@ -1315,7 +1379,7 @@ ArmStatus sg_session_last_logits(ArmSession* sess, float* host_out, uint32_t n) 
     set_err("sg_session_last_logits: no token processed yet");
     return ARMCC_ERR_RUNTIME;
   }
-  const size_t count = std::min<size_t>(n, (size_t)sess->c.vocab);
+  const size_t count = std::min<size_t>(n, (size_t)sess->batch * sess->c.vocab);
   cudaSetDevice(sess->dev);
   if (cudaMemcpyAsync(host_out, sess->buf<float>("logits"), count * 4, cudaMemcpyDeviceToHost, sess->st) !=
           cudaSuccess ||
@@ -1361,6 +1425,42 @@ ArmStatus sg_tp_unique_id(uint8_t id_out[128]) {
   return ARMCC_OK;
 }
 
+ArmSession* sg_session_create_ex(ArmGraph* graph, const ArmSessionOptions* opts, uint32_t batch, int32_t rank,
+                                 int32_t world, const uint8_t id[128]) {
+  if (world > 1 && !id) {
+    set_err("sg_session_create_ex: id is NULL");
+    return nullptr;
+  }
+  if (world < 1 || rank < 0 || rank >= world) {
+    set_err("sg_session_create_ex: rank %d outside a group of %d", rank, world);
+    return nullptr;
+  }
+  return create_session(graph, opts, rank, world, id, (int)std::min<uint32_t>(batch, 1u << 20));
+}
+
+ArmStatus sg_batch_prefill(ArmSession* sess, const int32_t* tokens, uint32_t n_tokens) {
+  if (!sess || (!tokens && n_tokens)) {
+    set_err("sg_batch_prefill: NULL argument");
+    return ARMCC_ERR_RUNTIME;
+  }
+  if (n_tokens == 0) return ARMCC_OK;
+  return prefill_tokens(sess, tokens, n_tokens, "sg_batch_prefill");
+}
+
+ArmStatus sg_batch_decode(ArmSession* sess, int32_t* next_tokens) {
+  if (!sess || !next_tokens) {
+    set_err("sg_batch_decode: NULL argument");
+    return ARMCC_ERR_RUNTIME;
+  }
+  float step_ms = 0;
+  const ArmStatus r = step_tokens(sess, "sg_batch_decode", &step_ms);
+  if (r != ARMCC_OK) return r;
+  memcpy(next_tokens, sess->next_all.data(), (size_t)sess->batch * 4);
+  return ARMCC_OK;
+}
+
+uint32_t sg_session_batch(const ArmSession* sess) { return sess ? (uint32_t)sess->batch : 0; }
+
 ArmSession* sg_session_create_tp(ArmGraph* graph, const ArmSessionOptions* opts, int32_t rank, int32_t world,
                                  const uint8_t id[128]) {
   if (world > 1 && !id) {
@@ -1371,7 +1471,7 @@ ArmSession* sg_session_create_tp(ArmGraph* graph, const ArmSessionOptions* opts,
     set_err("sg_session_create_tp: rank %d outside a group of %d", rank, world);
     return nullptr;
   }
-  return create_session(graph, opts, rank, world, id);
+  return create_session(graph, opts, rank, world, id, 1);
 }
 
 void sg_session_vocab_range(const ArmSession* sess, uint32_t* lo, uint32_t* hi) {

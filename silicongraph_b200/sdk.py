@@ -76,6 +76,11 @@ _SIGS = {
     "sg_session_create_tp": (_P, [_P, ctypes.POINTER(ArmSessionOptions), ctypes.c_int32, ctypes.c_int32,
                                   ctypes.POINTER(ctypes.c_uint8)]),
     "sg_session_vocab_range": (None, [_P, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32)]),
+    "sg_session_create_ex": (_P, [_P, ctypes.POINTER(ArmSessionOptions), ctypes.c_uint32, ctypes.c_int32,
+                                  ctypes.c_int32, ctypes.POINTER(ctypes.c_uint8)]),
+    "sg_batch_prefill": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32]),
+    "sg_batch_decode": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_int32)]),
+    "sg_session_batch": (ctypes.c_uint32, [_P]),
 }
 
 
@@ -186,9 +191,10 @@ class Graph:
     def peak_memory_bytes(self) -> int:
         return lib().armgraph_peak_memory_bytes(self.h)
 
-    def session(self, tp: tuple[int, int, bytes] | None = None) -> "Session":
-        """A session; tp = (rank, world, unique id) joins a tensor-parallel group."""
-        return Session(self, tp)
+    def session(self, tp: tuple[int, int, bytes] | None = None, batch: int = 1) -> "Session":
+        """A session; tp = (rank, world, unique id) joins a tensor-parallel group;
+        batch > 1 decodes that many sequences in lockstep."""
+        return Session(self, tp, batch)
 
     def run(self, tokens) -> ArmInferenceResult:
         p, n, _keep = _tokens(tokens)
@@ -196,14 +202,14 @@ class Graph:
 
 
 class Session:
-    def __init__(self, graph: Graph, tp: tuple[int, int, bytes] | None = None):
+    def __init__(self, graph: Graph, tp: tuple[int, int, bytes] | None = None, batch: int = 1):
         self.graph = graph
-        if tp is None:
+        if tp is None and batch == 1:
             self.h = lib().armgraph_create_session(graph.h, None)
         else:
-            rank, world, uid = tp
+            rank, world, uid = tp if tp is not None else (0, 1, bytes(128))
             buf = (ctypes.c_uint8 * 128).from_buffer_copy(uid)
-            self.h = lib().sg_session_create_tp(graph.h, None, rank, world, buf)
+            self.h = lib().sg_session_create_ex(graph.h, None, batch, rank, world, buf)
         if not self.h:
             raise ArmError(-5, last_error())
 
@@ -248,12 +254,33 @@ class Session:
             raise ArmError(st, last_error())
         return out
 
+    @property
+    def batch(self) -> int:
+        return lib().sg_session_batch(self.h)
+
+    def batch_prefill(self, tokens) -> None:
+        """tokens [batch, n]: one prompt per sequence, all of length n."""
+        a = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        if a.ndim != 2 or a.shape[0] != self.batch:
+            raise ValueError(f"tokens must be [{self.batch}, n]")
+        st = lib().sg_batch_prefill(self.h, a.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), a.shape[1])
+        if st != ARMCC_OK:
+            raise ArmError(st, last_error())
+
+    def batch_decode(self) -> np.ndarray:
+        """Every sequence's next greedy token."""
+        out = np.zeros(self.batch, np.int32)
+        st = lib().sg_batch_decode(self.h, out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)))
+        if st != ARMCC_OK:
+            raise ArmError(st, last_error())
+        return out
+
     def last_logits(self, vocab: int | None = None) -> np.ndarray:
         """fp32 logits of the last processed token over vocab_range (the first
         `vocab` of them when given)."""
         if vocab is None:
             lo, hi = self.vocab_range
-            vocab = hi - lo
+            vocab = (hi - lo) * self.batch
         out = np.zeros(vocab, np.float32)
         st = lib().sg_session_last_logits(self.h, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), vocab)
         if st != ARMCC_OK:

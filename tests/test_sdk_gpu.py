@@ -36,7 +36,7 @@ def _package(tmp_path, chunk, ctx=1024, seed=1):
 
 
 @pytest.mark.parametrize("prompt_len,chunk", [
-    (37, 128),     # short prompt: CUDA-core attention, row GEMV path below 64 rows
+    (37, 128),     # short prompt: CUDA-core attention
     (300, 512),    # one 300-token chunk: tensor-core GEMM and tensor-core attention
     (300, 128),    # chunked prefill: three chunks attending to the earlier ones
 ])
@@ -121,3 +121,35 @@ def test_decode_graph_matches_eager(sg, tmp_path, monkeypatch):
                 runs.append((toks, np.stack(logits)))
     assert runs[0][0] == runs[1][0]
     assert np.array_equal(runs[0][1], runs[1][1])
+
+
+def test_batched_session_matches_each_sequence(sg, oracle_mod, tmp_path):
+    """Three sequences prefilled and decoded in lockstep through one session
+    (sg_session_create_ex / sg_batch_prefill / sg_batch_decode): each
+    sequence's logits and tokens match the oracle run on that sequence alone."""
+    from oracle.decoder import DecoderOracle
+    from silicongraph_b200 import sdk
+    path, t = _package(tmp_path, 64)
+    B, n, steps, V = 3, 70, 3, SMALL["vocab_size"]  # 70 tokens: two prefill chunks of up to 64
+    prompts = np.random.default_rng(17).integers(0, V, (B, n)).astype(np.int32)
+    with sdk.Package(path) as pkg:
+        with pkg.select().session(batch=B) as s:
+            assert s.batch == B
+            with pytest.raises(sdk.ArmError):
+                s.prefill(prompts[0])  # the single-sequence calls refuse a batched session
+            s.batch_prefill(prompts)
+            logits = [s.last_logits().reshape(B, V)]
+            toks = [s.batch_decode()]
+            for _ in range(steps):
+                toks.append(s.batch_decode())
+                logits.append(s.last_logits().reshape(B, V))
+            assert s.position == n + steps
+    for b in range(B):
+        ref = DecoderOracle(SMALL, t, group_size=32)
+        want = ref.forward(prompts[b])
+        close(logits[0][b], want)
+        check_token(int(toks[0][b]), want)
+        for i in range(steps):
+            want = ref.forward([int(toks[i][b])])
+            close(logits[i + 1][b], want)
+            check_token(int(toks[i + 1][b]), want)

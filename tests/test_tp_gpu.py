@@ -21,26 +21,36 @@ RTOL, ATOL = 1e-2, 2e-3
 STEPS = 4
 
 
-def _worker(rank, world, uid, path, prompt, out_dir):
+def _worker(rank, world, uid, path, prompt, batch, out_dir):
     os.environ["SG_DEVICE"] = str(rank)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     torch.cuda.set_device(rank)
     from silicongraph_b200 import sdk
     with sdk.Package(path) as pkg:
-        g = pkg.select(context_length=len(prompt) + STEPS + 4)
-        with g.session(tp=(rank, world, uid)) as s:
-            s.prefill(prompt)
-            logits = [s.last_logits()]
-            toks = [s.decode().next_token_id]  # predicted by the prompt
-            for _ in range(STEPS):
-                toks.append(s.decode().next_token_id)
-                logits.append(s.last_logits())
+        g = pkg.select(context_length=prompt.shape[1] + STEPS + 4)
+        with g.session(tp=(rank, world, uid), batch=batch) as s:
             lo, hi = s.vocab_range
-    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), logits=np.stack(logits), toks=np.array(toks), lo=lo, hi=hi)
+            if batch == 1:
+                s.prefill(prompt[0])
+                logits = [s.last_logits()]
+                toks = [[s.decode().next_token_id]]  # predicted by the prompt
+                for _ in range(STEPS):
+                    toks.append([s.decode().next_token_id])
+                    logits.append(s.last_logits())
+            else:
+                s.batch_prefill(prompt)
+                logits = [s.last_logits()]
+                toks = [s.batch_decode()]
+                for _ in range(STEPS):
+                    toks.append(s.batch_decode())
+                    logits.append(s.last_logits())
+    # logits [steps + 1, batch, shard], toks [steps + 1, batch]
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), logits=np.stack(logits).reshape(STEPS + 1, batch, hi - lo),
+             toks=np.array(toks), lo=lo, hi=hi)
 
 
-@pytest.mark.parametrize("world", [2])
-def test_tp_session_matches_decoder_oracle(sg, oracle_mod, tmp_path, world):
+@pytest.mark.parametrize("world,batch", [(2, 1), (2, 2)])
+def test_tp_session_matches_decoder_oracle(sg, oracle_mod, tmp_path, world, batch):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     from oracle.decoder import DecoderOracle
@@ -48,18 +58,17 @@ def test_tp_session_matches_decoder_oracle(sg, oracle_mod, tmp_path, world):
     w = armpack.random_llama_weights(SMALL, seed=4)
     t = armpack.cuda_tensors(SMALL, w, group_size=32)
     path = armpack.write_package(str(tmp_path / "tp.armpack"), SMALL, t, max_context=256, max_prefill_chunk=64)
-    prompt = np.random.default_rng(9).integers(0, SMALL["vocab_size"], 90).astype(np.int32)  # two prefill chunks
+    prompt = np.random.default_rng(9).integers(0, SMALL["vocab_size"], (batch, 90)).astype(np.int32)  # 2 chunks
     uid = sdk.tp_unique_id()
-    mp.start_processes(_worker, args=(world, uid, path, prompt, str(tmp_path)), nprocs=world, join=True,
+    mp.start_processes(_worker, args=(world, uid, path, prompt, batch, str(tmp_path)), nprocs=world, join=True,
                        start_method="spawn")
     ranks = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
     assert [int(r["lo"]) for r in ranks] == sorted(int(r["lo"]) for r in ranks)
     assert int(ranks[-1]["hi"]) == SMALL["vocab_size"]
     for r in ranks[1:]:
         assert np.array_equal(r["toks"], ranks[0]["toks"])  # every rank emits the same tokens
-    logits = np.concatenate([r["logits"] for r in ranks], axis=1)
+    logits = np.concatenate([r["logits"] for r in ranks], axis=2)  # [steps + 1, batch, vocab]
     toks = ranks[0]["toks"]
-    ref = DecoderOracle(SMALL, t, group_size=32)
 
     def close(got, want):
         err = np.abs(got - want)
@@ -71,10 +80,12 @@ def test_tp_session_matches_decoder_oracle(sg, oracle_mod, tmp_path, world):
         if top[1] - top[0] > ATOL + RTOL * abs(top[1]):
             assert tok == int(np.argmax(want))
 
-    want = ref.forward(prompt)
-    close(logits[0], want)
-    check_token(int(toks[0]), want)
-    for i in range(STEPS):
-        want = ref.forward([int(toks[i])])
-        close(logits[i + 1], want)
-        check_token(int(toks[i + 1]), want)
+    for b in range(batch):
+        ref = DecoderOracle(SMALL, t, group_size=32)
+        want = ref.forward(prompt[b])
+        close(logits[0, b], want)
+        check_token(int(toks[0][b]), want)
+        for i in range(STEPS):
+            want = ref.forward([int(toks[i][b])])
+            close(logits[i + 1, b], want)
+            check_token(int(toks[i + 1][b]), want)
