@@ -317,6 +317,19 @@ SgStatus sg_tp_argmax_pack(const float* logits, int32_t rows, int32_t vocab_loca
 SgStatus sg_tp_argmax_pick(const float* all3, int32_t world, int32_t rows, int32_t* next, float* logprob,
                            void* stream);
 
+/* One-shot all-reduce (sum) of n fp16 values over the `world` ranks of a
+ * tensor-parallel group through NVLink peer memory, for decode-sized vectors.
+ * regions[q] is rank q's region of sg_tp_allreduce_region_bytes(world, max_n)
+ * bytes (zero-filled once, mapped into this process, e.g. through CUDA IPC);
+ * regions[rank] is this rank's own.  Every rank calls it with the same n, in
+ * the same order; n and max_n are multiples of 8, n <= max_n, world <= 8.
+ * The result (summed in rank order in fp32, rounded once) replaces data on
+ * every rank.  A peer that does not arrive within 2 s leaves data unreduced
+ * and sets the device error word (sg_device_error_check). */
+size_t sg_tp_allreduce_region_bytes(int32_t world, int32_t max_n);
+SgStatus sg_tp_allreduce_f16(void* data, int32_t n, int32_t rank, int32_t world, void* const* regions, int32_t max_n,
+                             void* stream);
+
 /* in [heads, tokens, head_dim] -> out [tokens, heads, head_dim]. */
 SgStatus sg_head_transpose(const void* in, void* out, int32_t heads, int32_t tokens, int32_t head_dim,
                            int32_t io_dtype, void* stream);

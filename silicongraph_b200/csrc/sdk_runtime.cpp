@@ -403,11 +403,18 @@ struct ArmSession_ {
   SgTpShard shard{};
   ncclComm_t comm = nullptr;
   int* tp_flag = nullptr;  // device word for the ranks' agreement on setup
+  // peer-memory all-reduce of decode-sized sums (sg_tp_allreduce_f16); NCCL otherwise
+  void* ar_region = nullptr;
+  int ar_max = 0;
+  std::vector<void*> ar_regions;  // every rank's region as mapped here (own one at tp_rank)
 
   ~ArmSession_() {
     if (st) cudaStreamSynchronize(st);
     if (graph_exec) cudaGraphExecDestroy(graph_exec);
     if (graph) cudaGraphDestroy(graph);
+    for (size_t q = 0; q < ar_regions.size(); ++q)
+      if ((int)q != tp_rank && ar_regions[q]) cudaIpcCloseMemHandle(ar_regions[q]);
+    if (ar_region) cudaFree(ar_region);
     if (comm) nccl_api().comm_destroy(comm);  // after the graphs that hold its calls
     if (tp_flag) cudaFree(tp_flag);
     if (slab) cudaFree(slab);
@@ -439,6 +446,11 @@ ArmStatus fail_sg(SgStatus s, const char* what) {
 // Sums a row-split projection's fp16 output over the ranks (in place).
 ArmStatus tp_sum(ArmSession_* S, void* buf, size_t count) {
   if (S->tp_world == 1) return ARMCC_OK;
+  if (S->ar_region && count <= (size_t)S->ar_max && count % 8 == 0) {
+    SG_TRY(sg_tp_allreduce_f16(buf, (int32_t)count, S->tp_rank, S->tp_world, S->ar_regions.data(), S->ar_max, S->st),
+           "peer all-reduce");
+    return ARMCC_OK;
+  }
   const ncclResult_t e = nccl_api().all_reduce(buf, buf, count, ncclHalf, ncclSum, S->comm, S->st);
   if (e != ncclSuccess) {
     set_err("ncclAllReduce failed: %s", nccl_api().error_string(e));
@@ -813,6 +825,75 @@ bool shard_linear(ArmGraph_* g, const std::string& name, int K, int N, int r0, i
   return true;
 }
 
+// Maps every rank's peer all-reduce region into this process (CUDA IPC
+// handles exchanged with one NCCL all-gather).  Collective and symmetric: if
+// any rank cannot set it up (or SG_TP_P2P=0 on any rank), every rank keeps
+// NCCL for all sums.  Returns false only when a collective itself failed.
+bool setup_peer_allreduce(ArmSession_* S, int max_n) {
+  const int world = S->tp_world, rank = S->tp_rank;
+  const char* env = getenv("SG_TP_P2P");
+  bool ok = world <= 8 && !(env && atoi(env) == 0);
+  const size_t bytes = sg_tp_allreduce_region_bytes(world, max_n);
+  cudaIpcMemHandle_t mine{};
+  if (ok) ok = bytes > 0 && cudaMalloc(&S->ar_region, bytes) == cudaSuccess;
+  if (ok) ok = cudaMemset(S->ar_region, 0, bytes) == cudaSuccess && cudaIpcGetMemHandle(&mine, S->ar_region) == cudaSuccess;
+  if (!ok) cudaGetLastError();
+  // [world][handle | status] on the device, gathered in place
+  struct Slot {
+    cudaIpcMemHandle_t h;
+    int32_t ok;
+    int32_t pad[3];
+  };
+  Slot* dslots = nullptr;
+  std::vector<Slot> slots(world);
+  slots[rank].h = mine;
+  slots[rank].ok = ok ? 1 : 0;
+  if (cudaMalloc(&dslots, sizeof(Slot) * world) != cudaSuccess ||
+      cudaMemcpy(dslots + rank, &slots[rank], sizeof(Slot), cudaMemcpyHostToDevice) != cudaSuccess ||
+      nccl_api().all_gather(dslots + rank, dslots, sizeof(Slot), ncclChar, S->comm, S->st) != ncclSuccess ||
+      cudaMemcpyAsync(slots.data(), dslots, sizeof(Slot) * world, cudaMemcpyDeviceToHost, S->st) != cudaSuccess ||
+      cudaStreamSynchronize(S->st) != cudaSuccess) {
+    cudaGetLastError();
+    if (dslots) cudaFree(dslots);
+    return false;
+  }
+  cudaFree(dslots);
+  bool all = true;
+  for (const Slot& x : slots) all = all && x.ok;
+  S->ar_regions.assign(world, nullptr);
+  int opened = 1;
+  if (all) {
+    S->ar_regions[rank] = S->ar_region;
+    for (int q = 0; q < world && opened; ++q) {
+      if (q == rank) continue;
+      if (cudaIpcOpenMemHandle(&S->ar_regions[q], slots[q].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        S->ar_regions[q] = nullptr;
+        opened = 0;
+      }
+    }
+  }
+  // every rank learns whether every rank mapped every peer
+  int bad = (all && opened) ? 0 : 1;
+  if (cudaMemcpyAsync(S->tp_flag, &bad, 4, cudaMemcpyHostToDevice, S->st) != cudaSuccess ||
+      nccl_api().all_reduce(S->tp_flag, S->tp_flag, 1, ncclInt32, ncclMax, S->comm, S->st) != ncclSuccess ||
+      cudaMemcpyAsync(&bad, S->tp_flag, 4, cudaMemcpyDeviceToHost, S->st) != cudaSuccess ||
+      cudaStreamSynchronize(S->st) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (bad) {  // NCCL for every sum on every rank
+    for (int q = 0; q < world; ++q)
+      if (q != rank && S->ar_regions[q]) cudaIpcCloseMemHandle(S->ar_regions[q]);
+    S->ar_regions.clear();
+    if (S->ar_region) cudaFree(S->ar_region);
+    S->ar_region = nullptr;
+    return true;
+  }
+  S->ar_max = max_n;
+  return true;
+}
+
 // Session of rank `rank` in a group of `world` (world 1: the whole model, no NCCL).
 ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int rank, int world, const uint8_t* id,
                            int batch) {
@@ -893,6 +974,10 @@ ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int r
     if (e != ncclSuccess) {
       S->comm = nullptr;
       set_err("%s: ncclCommInitRank failed: %s", fn, nccl_api().error_string(e));
+      return nullptr;
+    }
+    if (!setup_peer_allreduce(S.get(), (int)align_up((uint64_t)batch * gc.hidden, 8))) {
+      set_err("%s: a collective of the peer all-reduce setup failed", fn);
       return nullptr;
     }
   }

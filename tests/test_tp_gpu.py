@@ -1,6 +1,7 @@
 """A tensor-parallel session over two GPUs (sg_session_create_tp): each rank
-holds its shard of every linear, NCCL sums the row-split projections and
-picks the greedy token across the vocabulary shards.  The gathered logits
+holds its shard of every linear; the row-split projections are summed by the
+peer-memory all-reduce (decode) or NCCL (prefill, or everywhere with
+SG_TP_P2P=0), and NCCL picks the greedy token across the vocabulary shards.  The gathered logits
 and the tokens must match the decoder composition oracle like a one-GPU
 session does (|got - want| <= 2e-3 + 1e-2 |want|), and every rank must emit
 the same tokens.  Skipped with fewer than two GPUs."""
@@ -21,9 +22,10 @@ RTOL, ATOL = 1e-2, 2e-3
 STEPS = 4
 
 
-def _worker(rank, world, uid, path, prompt, batch, out_dir):
+def _worker(rank, world, uid, path, prompt, batch, p2p, out_dir):
     os.environ["SG_DEVICE"] = str(rank)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["SG_TP_P2P"] = "1" if p2p else "0"
     torch.cuda.set_device(rank)
     from silicongraph_b200 import sdk
     with sdk.Package(path) as pkg:
@@ -49,8 +51,9 @@ def _worker(rank, world, uid, path, prompt, batch, out_dir):
              toks=np.array(toks), lo=lo, hi=hi)
 
 
-@pytest.mark.parametrize("world,batch", [(2, 1), (2, 2)])
-def test_tp_session_matches_decoder_oracle(sg, oracle_mod, tmp_path, world, batch):
+@pytest.mark.parametrize("world,batch,p2p", [(2, 1, True), (2, 2, True), (2, 2, False)],
+                         ids=["peer-allreduce", "batch2-peer-allreduce", "batch2-nccl"])
+def test_tp_session_matches_decoder_oracle(sg, oracle_mod, tmp_path, world, batch, p2p):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     from oracle.decoder import DecoderOracle
@@ -60,8 +63,8 @@ def test_tp_session_matches_decoder_oracle(sg, oracle_mod, tmp_path, world, batc
     path = armpack.write_package(str(tmp_path / "tp.armpack"), SMALL, t, max_context=256, max_prefill_chunk=64)
     prompt = np.random.default_rng(9).integers(0, SMALL["vocab_size"], (batch, 90)).astype(np.int32)  # 2 chunks
     uid = sdk.tp_unique_id()
-    mp.start_processes(_worker, args=(world, uid, path, prompt, batch, str(tmp_path)), nprocs=world, join=True,
-                       start_method="spawn")
+    mp.start_processes(_worker, args=(world, uid, path, prompt, batch, p2p, str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
     ranks = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
     assert [int(r["lo"]) for r in ranks] == sorted(int(r["lo"]) for r in ranks)
     assert int(ranks[-1]["hi"]) == SMALL["vocab_size"]
@@ -89,3 +92,4 @@ def test_tp_session_matches_decoder_oracle(sg, oracle_mod, tmp_path, world, batc
             want = ref.forward([int(toks[i][b])])
             close(logits[i + 1, b], want)
             check_token(int(toks[i + 1][b]), want)
+
