@@ -579,13 +579,14 @@ __global__ void __launch_bounds__(kThreads) attn_dec_cluster_kernel(AArgs a) {
 // so that P keeps 11 significant bits).  Same cluster-of-splits structure as
 // attn_dec_cluster_kernel; per 64-key tile:
 //   * S = Q K^T with mma.sync m16n8k16 (queries = the 16 A rows, kept in
-//     registers as fragments; warp w takes keys 16w .. 16w+15, K row-major in
+//     registers as fragments; warp w of 8 takes keys 8w .. 8w+7, K row-major in
 //     shared memory with 16 bytes of padding per row, so the B fragments are
 //     conflict-free 32-bit loads);
 //   * online softmax on the scores in shared memory, one warp per row;
 //   * O += P V with mma.sync (P rebuilt as fp16 A fragments, V fragments by
-//     ldmatrix.trans from row-major V; warp w owns a quarter of the head dims).
-// The next tile's K and V are in flight in registers during each tile.
+//     ldmatrix.trans from row-major V; warp w owns an eighth of the head dims).
+// K and V tiles stream through a 3-stage cp.async ring (two tiles in flight
+// while one is computed; bf16 tiles are converted to fp16 in place).
 constexpr int kDecMmaRows = 16;
 
 __device__ __forceinline__ void ldmatrix_x2_trans(uint32_t& r0, uint32_t& r1, const void* smem_row) {
@@ -613,23 +614,26 @@ __device__ __forceinline__ uint4 to_f16x8(const uint4& v) {
   return o;
 }
 
+constexpr int kDecMmaStages = 3;     // K/V tiles in flight per block
+constexpr int kDecMmaThreads = 256;  // 8 warps: 8 keys each in Q K^T, an eighth of the head dims in P V
+
 inline size_t dec_mma_smem(int D, int R, int nsplit) {
   const size_t kvrow = (size_t)(D + 8) * 2;  // bytes per padded fp16 row
-  return 2 * kDecTile * kvrow + sizeof(float) * ((size_t)kDecMmaRows * kDecTile + 3 * kDecMmaRows +
-                                                 (size_t)nsplit * R * (D + 2));
+  return kDecMmaStages * 2 * kDecTile * kvrow +
+         sizeof(float) * ((size_t)kDecMmaRows * kDecTile + 3 * kDecMmaRows + (size_t)nsplit * R * (D + 2));
 }
 
 template <int D, int IO>
-__global__ void __launch_bounds__(kThreads) attn_dec_mma_kernel(AArgs a) {
+__global__ void __launch_bounds__(kDecMmaThreads) attn_dec_mma_kernel(AArgs a) {
   namespace cg = cooperative_groups;
   constexpr int KT = kDecTile, KP = D + 8;  // padded row (halves)
-  constexpr int NV = (D / 2) * 2 / 16;      // 16-byte loads per thread per tile (K, and V): half a row
-  constexpr int DW = D / 4;                 // head dims per warp in P V
+  constexpr int kW = kDecMmaThreads / 32;   // 8 warps
+  constexpr int NV = (D / 4) * 2 / 16;      // 16-byte loads per thread per tile (K, and V): a quarter row
+  constexpr int DW = D / kW;                // head dims per warp in P V
   constexpr int NT = DW / 8;                // n-tiles per warp in P V
   extern __shared__ __align__(16) uint8_t smb[];
-  __half* ks = reinterpret_cast<__half*>(smb);         // [KT][KP]
-  __half* vs = ks + KT * KP;                           // [KT][KP]
-  float* ps = reinterpret_cast<float*>(vs + KT * KP);  // [16][KT] scores, then probabilities
+  __half* kvs = reinterpret_cast<__half*>(smb);        // [stage][K | V][KT][KP]
+  float* ps = reinterpret_cast<float*>(kvs + kDecMmaStages * 2 * KT * KP);  // [16][KT] scores, probabilities
   float* ms = ps + kDecMmaRows * KT;                   // [16] running max (log2 units)
   float* ls = ms + kDecMmaRows;                        // [16] running sum
   float* al = ls + kDecMmaRows;                        // [16] rescale of this tile
@@ -648,22 +652,28 @@ __global__ void __launch_bounds__(kThreads) attn_dec_mma_kernel(AArgs a) {
   int j1 = min(Skv, j0 + a.keys_per_split);
   if (a.causal) j1 = min(j1, q_pos0 + nq);
   const int64_t kvbase = (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs;
-  const int kk = tid >> 1, part = tid & 1;  // loader role: half `part` of key kk
+  const int kk = tid >> 2, part = tid & 3;  // loader role: quarter `part` of key kk
 
-  uint4 kr[NV], vr[NV];
-  auto load_tile = [&](int jt) {
-    const int key = jt + kk;
+  const int ntiles = j1 > j0 ? (j1 - j0 + KT - 1) / KT : 0;
+  // this thread's 16-byte pieces of tile `it` into stage it % kDecMmaStages (zeros past the last key)
+  auto issue_tile = [&](int it) {
+    const int key = j0 + it * KT + kk;
     const bool live = key < j1;
-    const int64_t e0 = kvbase + (int64_t)key * D + part * (D / 2);
-    const uint4* kp = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.K) + e0);
-    const uint4* vp = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.V) + e0);
+    const int64_t e0 = kvbase + (int64_t)(live ? key : j0) * D + part * (D / 4);
+    const uint16_t* kp = static_cast<const uint16_t*>(a.K) + e0;
+    const uint16_t* vp = static_cast<const uint16_t*>(a.V) + e0;
+    __half* kd = kvs + (size_t)(it % kDecMmaStages) * 2 * KT * KP + kk * KP + part * (D / 4);
+    __half* vd = kd + KT * KP;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      kr[i] = live ? __ldg(kp + i) : make_uint4(0u, 0u, 0u, 0u);
-      vr[i] = live ? __ldg(vp + i) : make_uint4(0u, 0u, 0u, 0u);
+      sgd::cp_async_16(kd + 8 * i, kp + 8 * i, live);
+      sgd::cp_async_16(vd + 8 * i, vp + 8 * i, live);
     }
   };
-  if (j0 < j1) load_tile(j0);  // in flight together with the query loads
+  for (int s = 0; s < kDecMmaStages - 1; ++s) {  // in flight together with the query loads
+    if (s < ntiles) issue_tile(s);
+    sgd::cp_async_commit();
+  }
 
   // Q fragments (A of S = Q K^T), prescaled by scale * log2(e); rows >= R are zero.
   const float qscale = a.scale * 1.4426950408889634f;
@@ -681,7 +691,7 @@ __global__ void __launch_bounds__(kThreads) attn_dec_mma_kernel(AArgs a) {
     qf[s][2] = pack_half2(q_at(g, d0 + 8), q_at(g, d0 + 9));
     qf[s][3] = pack_half2(q_at(g + 8, d0 + 8), q_at(g + 8, d0 + 9));
   }
-  for (int r = tid; r < kDecMmaRows; r += kThreads) {
+  for (int r = tid; r < kDecMmaRows; r += kDecMmaThreads) {
     ms[r] = -INFINITY;
     ls[r] = 0.f;
   }
@@ -691,43 +701,46 @@ __global__ void __launch_bounds__(kThreads) attn_dec_mma_kernel(AArgs a) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) o[n][q] = 0.f;
 
-  for (int jt = j0; jt < j1; jt += KT) {
-    __syncthreads();  // the previous tile's readers of ks, vs, ps and al are done
+  for (int it = 0; it < ntiles; ++it) {
+    const int jt = j0 + it * KT;
+    sgd::cp_async_wait<kDecMmaStages - 2>();  // this thread's pieces of tile `it` have landed
+    __half* ks = kvs + (size_t)(it % kDecMmaStages) * 2 * KT * KP;
+    __half* vs = ks + KT * KP;
+    if (IO == SG_DT_BF16) {  // this thread's own pieces, bf16 -> fp16 in place
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      *reinterpret_cast<uint4*>(ks + kk * KP + part * (D / 2) + 8 * i) = to_f16x8<IO>(kr[i]);
-      *reinterpret_cast<uint4*>(vs + kk * KP + part * (D / 2) + 8 * i) = to_f16x8<IO>(vr[i]);
+      for (int i = 0; i < NV; ++i) {
+        uint4* kq = reinterpret_cast<uint4*>(ks + kk * KP + part * (D / 4) + 8 * i);
+        uint4* vq = reinterpret_cast<uint4*>(vs + kk * KP + part * (D / 4) + 8 * i);
+        *kq = to_f16x8<IO>(*kq);
+        *vq = to_f16x8<IO>(*vq);
+      }
     }
-    if (jt + KT < j1) load_tile(jt + KT);  // next tile in flight during this one
-    __syncthreads();
-    // ---- S = Q K^T for this warp's 16 keys (two n-tiles of 8)
-    float sc[2][4];
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) sc[j][q] = 0.f;
-      const __half* krow = ks + (16 * warp + 8 * j + g) * KP + 2 * t;
+    __syncthreads();  // every piece of tile `it` is in; tile it - 1's readers are done
+    if (it + kDecMmaStages - 1 < ntiles) issue_tile(it + kDecMmaStages - 1);  // into tile it - 1's stage
+    sgd::cp_async_commit();
+    // ---- S = Q K^T for this warp's 8 keys (one n-tile)
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+      const __half* krow = ks + (8 * warp + g) * KP + 2 * t;
 #pragma unroll
       for (int s = 0; s < D / 16; ++s) {
         const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow + 16 * s);
         const uint32_t b1 = *reinterpret_cast<const uint32_t*>(krow + 16 * s + 8);
-        sgd::mma_f16_16816(sc[j], qf[s][0], qf[s][1], qf[s][2], qf[s][3], b0, b1);
+        sgd::mma_f16_16816(sc, qf[s][0], qf[s][1], qf[s][2], qf[s][3], b0, b1);
       }
     }
     // scores to shared memory with the visibility mask (rows >= R are never read)
 #pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int r = g + 8 * (q >> 1);
-        const int kl = 16 * warp + 8 * j + 2 * t + (q & 1);
-        const int key = jt + kl;
-        const bool vis = key < j1 && (!a.causal || key <= q_pos0 + r % nq);
-        ps[r * KT + kl] = vis ? sc[j][q] : -INFINITY;
-      }
+    for (int q = 0; q < 4; ++q) {
+      const int r = g + 8 * (q >> 1);
+      const int kl = 8 * warp + 2 * t + (q & 1);
+      const int key = jt + kl;
+      const bool vis = key < j1 && (!a.causal || key <= q_pos0 + r % nq);
+      ps[r * KT + kl] = vis ? sc[q] : -INFINITY;
+    }
     __syncthreads();
     // ---- online softmax: one warp per row
-    for (int r = warp; r < R; r += kThreads / 32) {
+    for (int r = warp; r < R; r += kW) {
       const float s0 = ps[r * KT + lane], s1 = ps[r * KT + lane + 32];
       float mx = fmaxf(s0, s1);
 #pragma unroll
@@ -796,13 +809,13 @@ __global__ void __launch_bounds__(kThreads) attn_dec_mma_kernel(AArgs a) {
       dst[(g + 8) * (D + 2) + d + 1] = o[n][3];
     }
   }
-  for (int r = tid; r < R; r += kThreads) {
+  for (int r = tid; r < R; r += kDecMmaThreads) {
     dst[r * (D + 2) + D] = ms[r];
     dst[r * (D + 2) + D + 1] = ls[r];
   }
   cluster.sync();
   if (split != 0) return;
-  for (int i = tid; i < R * D; i += kThreads) {
+  for (int i = tid; i < R * D; i += kDecMmaThreads) {
     const int r = i / D, d = i % D;
     float M = -INFINITY;
     for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, comb[((size_t)sp * R + r) * (D + 2) + D]);
@@ -936,7 +949,7 @@ SgStatus attn_cc_run(const SgFlashAttentionParams* p, void* stream, int want_spl
     const size_t smem = smem_of(a.nsplit);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.nsplit, a.Hkv, a.B);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(use_mma ? kDecMmaThreads : kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = cs;
     cudaLaunchAttribute attr[2];

@@ -157,6 +157,21 @@ inline cudaError_t launch_pdl(void (*kfn)(KArgs...), dim3 grid, dim3 block, size
   return cudaLaunchKernelEx(&cfg, kfn, std::forward<Args>(args)...);
 }
 
+// ------------------------------------------------------------------ cp.async (16 bytes, L2 only)
+// Copies 16 bytes from global to shared memory asynchronously; with valid ==
+// false nothing is read and the 16 bytes are zero-filled (gmem must still be
+// a mapped address).
+__device__ __forceinline__ void cp_async_16(void* smem, const void* gmem, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // ------------------------------------------------------------------ TMA (into this CTA only)
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int32_t x, int32_t y,
                                             uint64_t* bar) {
