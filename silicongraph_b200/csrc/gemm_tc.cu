@@ -192,8 +192,7 @@ __global__ void __launch_bounds__(threads_of(PAR), 1)
   constexpr int S = C_::kStages, J = C_::kSlots, kAcc = C_::kAcc;
   constexpr int kWarpAct = warp_tma_act(PAR), kWarpW = warp_tma_w(PAR), kWarpMma = warp_mma(PAR);
   extern __shared__ unsigned char smem_raw[];
-  unsigned char* smem =
-      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* smem = sgd::align_smem_1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C_::kBarOff);
   uint64_t* empty = full + S;
   uint64_t* afull = empty + S;

@@ -39,6 +39,13 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// The first 1024-byte aligned byte at or after p (dynamic shared memory),
+// derived from p itself so the compiler keeps its shared-space provenance
+// (rounding through an integer makes every later access a generic load).
+__device__ __forceinline__ uint8_t* align_smem_1024(uint8_t* p) {
+  return p + ((1024u - (smem_u32(p) & 1023u)) & 1023u);
+}
+
 // ------------------------------------------------------------------ mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
@@ -323,6 +330,16 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ldmatrix: four 8x8 b16 matrices; lane i gives the (16-byte aligned) address
+// of row i % 8 of matrix i / 8, and receives elements (i / 4, 2 (i % 4) + {0, 1})
+// of matrix j in register j.
+__device__ __forceinline__ void ldmatrix_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3,
+                                            const void* smem_row) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_u32(smem_row)));
 }
 
 // mma.sync m16n8k32, A unsigned 8-bit (row), B signed 8-bit (col), exact

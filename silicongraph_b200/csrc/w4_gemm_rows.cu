@@ -1,0 +1,602 @@
+// INT4 group-quantised GEMM for a few activation rows (2..16: batched decode)
+// on the tensor cores (sm_100a).  Same contract and weight layout as
+// w4_gemv.cu (compiler/kernels/cpu/matmul_neon.h:113-143); used when
+// 2 <= M <= 16, group_size % 32 == 0 and N % 16 == 0 (measured faster than
+// both the tcgen05 GEMM and the GEMV kernels on every decoder shape there).
+//
+//   * Tile = 128 output columns.  Few tiles: a cluster of ksplit blocks shares
+//     a tile's K range, and each rank adds the ranks' partials of 1/ksplit of
+//     the tile's outputs in rank order from their shared memory
+//     (deterministic, no scratch).  Many tiles: persistent blocks (one or two
+//     per SM) stage the activations once and take every blocks-th tile, the
+//     weight ring running on across tiles; results go straight from the
+//     accumulators to C.
+//   * One producer warp streams 32 k-pair rows x 128 columns of packed weights
+//     (128-byte swizzled TMA box) plus the chunk's two scale and zero-point
+//     rows through a ring of 8 to 32 stages (as deep as shared memory allows:
+//     the kernel is bound by the weight bytes in flight per SM).  Two sets of
+//     8 consumer warps take alternate chunks; in a set each warp owns 16
+//     columns, and the two sets' partials are added in set order at the end.
+//   * A warp's 16 columns are the 16 rows of the mma.sync m16n8k16 A operand
+//     (A row g = column 2g, row g + 8 = column 2g + 1); a lane's byte of two
+//     k gives both halves of one A register: (byte & 0x0F) | 0x6400 is
+//     1024 + q_lo and (byte & 0xF0) | 0x5400 is 64 + q_hi (the fp16 ulp at 64
+//     is 1/16), so subtracting (1032 + zero, 72 + zero) is exact and one
+//     multiply by the scale rounds once: the fp16 weight scale * (q - 8 - zero).
+//   * The activation rows, staged once per block in fp16, are the B columns
+//     (8 rows per n-tile); D accumulates in fp32 over the block's whole range.
+#include <cooperative_groups.h>
+
+#include <algorithm>
+#include <atomic>
+#include <mutex>
+#include <string_view>
+
+#include "sm100.cuh"
+
+namespace {
+
+constexpr int kRowsPerChunk = 32;  // k-pair rows per chunk (64 k)
+constexpr int kTileCols = 128;
+constexpr int kColWarps = 8;                         // warps per chunk: 16 columns each
+constexpr int kConsumerWarps = 2 * kColWarps;        // two sets, taking alternate chunks
+constexpr int kThreads = (kConsumerWarps + 1) * 32;  // + the producer warp
+constexpr int kMinStages = 8;  // ring depth: 8, 16 or 32 chunks (the most that fit shared memory)
+constexpr int kMaxSmem = 227 * 1024 - 2048;  // opt-in limit minus this kernel's static shared memory
+constexpr int kWBytes = 128 * kRowsPerChunk;      // 4096
+constexpr int kSBytes = 128 * 2 * 2;              // 2 scale rows x 128 fp16
+constexpr int kZBytes = 128 * 2;                  // 2 zero rows x 128 int8
+constexpr int kSZBytes = kSBytes + kZBytes;       // 768
+constexpr int kStageBytes = kWBytes + kSZBytes;   // 4864: weights [stage][4096] (1024-aligned for the swizzle), then [stage][768]
+
+struct RArgs {
+  const void* A;
+  const __half* bias;
+  void* C;
+  int M, K, N, lda, ldc, gs, gs_shift;
+  int a_dt, c_dt;
+  float scale_A;
+  int n_tiles, cpt, ksplit, x_slots;
+  int static_w;
+  int stage_shift;  // log2 of the ring depth
+  int x_vec;  // A 16-byte aligned, lda and K multiples of 8: rows staged 8 values at a time
+  int* err;
+};
+
+__device__ __forceinline__ float load_act(const void* A, int dt, int64_t i) {
+  switch (dt) {
+    case SG_DT_F32: return static_cast<const float*>(A)[i];
+    case SG_DT_F16: return __half2float(static_cast<const __half*>(A)[i]);
+    case SG_DT_BF16: return __bfloat162float(static_cast<const __nv_bfloat16*>(A)[i]);
+    default: return (float)static_cast<const int8_t*>(A)[i];
+  }
+}
+
+// 8 consecutive activations (fp16) of element i; i % 8 == 0 and A 16-byte aligned
+__device__ __forceinline__ uint4 load_act8(const void* A, int dt, int64_t i) {
+  uint4 o;
+  __half2* oh = reinterpret_cast<__half2*>(&o);
+  switch (dt) {
+    case SG_DT_F16: return *reinterpret_cast<const uint4*>(static_cast<const __half*>(A) + i);
+    case SG_DT_F32: {
+      const float4 u = reinterpret_cast<const float4*>(static_cast<const float*>(A) + i)[0];
+      const float4 v = reinterpret_cast<const float4*>(static_cast<const float*>(A) + i)[1];
+      oh[0] = __floats2half2_rn(u.x, u.y);
+      oh[1] = __floats2half2_rn(u.z, u.w);
+      oh[2] = __floats2half2_rn(v.x, v.y);
+      oh[3] = __floats2half2_rn(v.z, v.w);
+      return o;
+    }
+    case SG_DT_BF16: {
+      const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(A) + i);
+      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(b[j]);
+        oh[j] = __floats2half2_rn(f.x, f.y);
+      }
+      return o;
+    }
+    default: {
+      const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const int8_t*>(A) + i);
+      const int8_t* b = reinterpret_cast<const int8_t*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) oh[j] = __floats2half2_rn((float)b[2 * j], (float)b[2 * j + 1]);
+      return o;
+    }
+  }
+}
+
+__device__ __forceinline__ int group_of(const RArgs& a, int k) { return a.gs_shift >= 0 ? (k >> a.gs_shift) : k / a.gs; }
+
+// (1024 + q_lo, 64 + q_hi) of the byte at `sel` (0x4040: byte 0, 0x4141: byte 1) of w
+__device__ __forceinline__ __half2 nibble_pair(uint32_t w, uint32_t sel) {
+  const uint32_t x = __byte_perm(w, 0u, sel);
+  const uint32_t v = (x & 0x00F0000Fu) | 0x54006400u;
+  return *reinterpret_cast<const __half2*>(&v);
+}
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
+
+template <bool HAS_Z, int MT>
+__global__ void __launch_bounds__(kThreads, 1)
+    w4_rows_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmS,
+                   const __grid_constant__ CUtensorMap tmZ, RArgs a) {
+  namespace cg = cooperative_groups;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = sgd::align_smem_1024(smem_raw);
+  const int nst = 1 << a.stage_shift;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + nst * kStageBytes);
+  uint64_t* empty = full + nst;
+  const int XP = a.x_slots * 64 + 8;  // staged k per row, padded (bank spread)
+  __half* xs = reinterpret_cast<__half*>(empty + nst);  // [MT][XP]
+  float* red = reinterpret_cast<float*>(xs + MT * XP);      // [2 sets][MT][128] this block's partials
+  __shared__ int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sp = blockIdx.x;
+  const bool split = a.ksplit > 1;  // then gridDim.y == n_tiles: one tile per cluster
+  const int cr0 = (a.cpt * sp) / a.ksplit;                // first chunk (of every tile) of this block
+  const int nch = (a.cpt * (sp + 1)) / a.ksplit - cr0;    // chunks per tile
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < nst; ++i) {
+      sgd::mbar_init(&full[i], 1);
+      sgd::mbar_init(&empty[i], kColWarps);
+    }
+    sgd::fence_mbar_init();
+    s_abort = 0;
+  }
+  __syncthreads();
+  if (split) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  sgd::pdl_launch_dependents();
+
+  if (warp == kConsumerWarps) {
+    // ---- producer: weights that no earlier kernel writes stream before the dependency wait
+    if (!a.static_w) sgd::pdl_wait();
+    if (lane == 0) {
+      const uint32_t tx = kWBytes + kSBytes + (HAS_Z ? kZBytes : 0);
+      int it = 0;  // chunks issued, over all tiles of this block
+      bool stop = false;
+      for (int tile = blockIdx.y; tile < a.n_tiles && !stop; tile += gridDim.y) {
+        for (int i = 0; i < nch; ++i, ++it) {
+          const int s = it & (nst - 1);
+          if (it >= nst && !sgd::mbar_wait(&empty[s], ((it >> a.stage_shift) - 1) & 1, a.err)) {
+            s_abort = 1;
+            stop = true;
+            break;
+          }
+          const int row0 = (cr0 + i) * kRowsPerChunk;
+          const int gA = group_of(a, 2 * row0);
+          uint8_t* wst = smem + s * kWBytes;
+          uint8_t* szst = smem + nst * kWBytes + s * kSZBytes;
+          sgd::mbar_arrive_expect_tx(&full[s], tx);
+          sgd::tma_load_2d(wst, &tmW, tile * kTileCols, row0, &full[s]);
+          sgd::tma_load_2d(szst, &tmS, tile * kTileCols, gA, &full[s]);
+          if (HAS_Z) sgd::tma_load_2d(szst + kSBytes, &tmZ, tile * kTileCols, gA, &full[s]);
+        }
+      }
+    }
+  } else {
+    // ---- consumers: stage the activation rows once (fp16, zero past M and K), then the chunks
+    sgd::pdl_wait();
+    const int span = nch * 64;
+    if (a.x_vec) {
+      // 8 values per thread and access, 4 accesses in flight per thread
+      constexpr int kU = 4, kT = kConsumerWarps * 32;
+      const int nv = span / 8, total = MT * nv;
+      for (int base = threadIdx.x; base < total; base += kU * kT) {
+        uint4 v[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int idx = base + u * kT;
+          const int m = idx / nv, k = cr0 * 64 + 8 * (idx - m * nv);
+          v[u] = make_uint4(0u, 0u, 0u, 0u);
+          if (idx < total && m < a.M && k < a.K) v[u] = load_act8(a.A, a.a_dt, (int64_t)m * a.lda + k);
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int idx = base + u * kT;
+          if (idx < total) {
+            const int m = idx / nv;
+            *reinterpret_cast<uint4*>(xs + m * XP + 8 * (idx - m * nv)) = v[u];
+          }
+        }
+      }
+    } else {
+      for (int idx = threadIdx.x; idx < MT * span; idx += kConsumerWarps * 32) {
+        const int m = idx / span, kk = idx - m * span;
+        const int k = cr0 * 64 + kk;
+        const float v = (m < a.M && k < a.K) ? load_act(a.A, a.a_dt, (int64_t)m * a.lda + k) : 0.f;
+        xs[m * XP + kk] = __float2half_rn(v);
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+    const int cw = warp % kColWarps, cp = warp / kColWarps;  // column group; chunk parity of this set
+    const int g = lane >> 2, t = lane & 3;
+    const int c0 = 16 * cw + 2 * g;  // A row g: column c0; row g + 8: column c0 + 1
+    // ldmatrix row of this lane: MT 16: matrices (n-tile j / 2, k half j % 2) of one 16-k step;
+    // MT 8: matrices (k half j % 2) of steps 2p + j / 2
+    const int lj = lane >> 3, lr = lane & 7;
+    const __half* xrow = MT == 16 ? xs + (8 * (lj >> 1) + lr) * XP + 8 * (lj & 1) : xs + lr * XP + 8 * lj;
+    float* myred = red + cp * MT * kTileCols;
+    bool dead = false;  // a wait of this warp ran out: skip the rest, keep to the barriers
+    int it0 = 0;
+    for (int tile = blockIdx.y; tile < a.n_tiles; tile += gridDim.y) {
+      float acc[MT / 8][4];
+#pragma unroll
+      for (int n = 0; n < MT / 8; ++n)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[n][q] = 0.f;
+      for (int i = (cp - it0) & 1; i < nch && !dead; i += 2) {
+        const int it = it0 + i;
+        const int s = it & (nst - 1);
+        const bool ok = sgd::mbar_wait(&full[s], (it >> a.stage_shift) & 1, a.err);
+        if (!__all_sync(0xffffffffu, ok)) {
+          s_abort = 1;
+          dead = true;
+          break;
+        }
+        const uint8_t* W = smem + s * kWBytes;
+        const uint8_t* SZ = smem + nst * kWBytes + s * kSZBytes;
+        const int k0 = (cr0 + i) * 64;
+        const int srowB = group_of(a, k0 + 32) - group_of(a, k0);
+        __half2 sc[2][2], off[2][2];  // [half of the chunk][column c0 / c0 + 1]
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int srow = h ? srowB : 0;
+          const uint32_t s2 = *reinterpret_cast<const uint32_t*>(SZ + (srow * 128 + c0) * 2);  // scales c0, c0 + 1
+          const uint32_t sd0 = __byte_perm(s2, 0u, 0x1010u), sd1 = __byte_perm(s2, 0u, 0x3232u);
+          sc[h][0] = *reinterpret_cast<const __half2*>(&sd0);
+          sc[h][1] = *reinterpret_cast<const __half2*>(&sd1);
+          if (HAS_Z) {
+            // zero byte z -> fp16 pair (1152 + z, 1152 + z) by bits, minus (120, 1080): (1032 + z, 72 + z), exact
+            const uint32_t zz = *reinterpret_cast<const uint16_t*>(SZ + kSBytes + srow * 128 + c0);
+            const __half2 bias = __halves2half2(__ushort_as_half(0x5780), __ushort_as_half(0x6438));  // 120, 1080
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              const uint32_t m = (__byte_perm(zz, 0u, c ? 0x4141u : 0x4040u) ^ 0x00800080u) | 0x64006400u;
+              off[h][c] = __hsub2(*reinterpret_cast<const __half2*>(&m), bias);
+            }
+          } else {
+            off[h][0] = off[h][1] = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x5480));  // 1032, 72
+          }
+        }
+        uint32_t bx[4][MT / 8][2];  // B fragments [16-k step][n-tile][k half]
+#pragma unroll
+        for (int q = 0; q < 4; q += (MT == 16 ? 1 : 2)) {
+          uint32_t r0, r1, r2, r3;
+          sgd::ldmatrix_x4(r0, r1, r2, r3, xrow + i * 64 + 16 * q);
+          if (MT == 16) {
+            bx[q][0][0] = r0;
+            bx[q][0][1] = r1;
+            bx[q][MT / 8 - 1][0] = r2;
+            bx[q][MT / 8 - 1][1] = r3;
+          } else {
+            bx[q][0][0] = r0;
+            bx[q][0][1] = r1;
+            bx[q + 1][0][0] = r2;
+            bx[q + 1][0][1] = r3;
+          }
+        }
+#pragma unroll
+        for (int st = 0; st < 4; ++st) {
+          const int h = st >> 1;
+          const int r0 = 8 * st + t, r1 = r0 + 4;  // k-pair rows of k-slots (2t, 2t+1) and (2t+8, 2t+9)
+          const uint32_t w0 = *reinterpret_cast<const uint16_t*>(W + r0 * 128 + ((cw ^ (r0 & 7)) << 4) + 2 * g);
+          const uint32_t w1 = *reinterpret_cast<const uint16_t*>(W + r1 * 128 + ((cw ^ (r1 & 7)) << 4) + 2 * g);
+          const uint32_t a0 = h2_bits(__hmul2(__hsub2(nibble_pair(w0, 0x4040u), off[h][0]), sc[h][0]));
+          const uint32_t a1 = h2_bits(__hmul2(__hsub2(nibble_pair(w0, 0x4141u), off[h][1]), sc[h][1]));
+          const uint32_t a2 = h2_bits(__hmul2(__hsub2(nibble_pair(w1, 0x4040u), off[h][0]), sc[h][0]));
+          const uint32_t a3 = h2_bits(__hmul2(__hsub2(nibble_pair(w1, 0x4141u), off[h][1]), sc[h][1]));
+#pragma unroll
+          for (int n = 0; n < MT / 8; ++n) sgd::mma_f16_16816(acc[n], a0, a1, a2, a3, bx[st][n][0], bx[st][n][1]);
+        }
+        __syncwarp();
+        if (lane == 0) sgd::mbar_arrive(&empty[s]);
+      }
+      it0 += nch;
+      // D: [n][0] row 8n + 2t, column c0; [1] row 8n + 2t + 1, c0; [2] row 8n + 2t, c0 + 1; [3] row 8n + 2t + 1, c0 + 1
+#pragma unroll
+      for (int n = 0; n < MT / 8; ++n) {
+        const int m = 8 * n + 2 * t;
+        myred[m * kTileCols + c0] = acc[n][0];
+        myred[(m + 1) * kTileCols + c0] = acc[n][1];
+        myred[m * kTileCols + c0 + 1] = acc[n][2];
+        myred[(m + 1) * kTileCols + c0 + 1] = acc[n][3];
+      }
+      if (!split) {
+        // both sets' partials of this tile, added in set order, go out coalesced
+        asm volatile("bar.sync 2, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+        if (!s_abort) {
+          for (int idx = threadIdx.x; idx < a.M * kTileCols; idx += kConsumerWarps * 32) {
+            const int m = idx / kTileCols, cc = idx - m * kTileCols;
+            const int col = tile * kTileCols + cc;
+            if (col >= a.N) continue;
+            float v = red[idx] + red[MT * kTileCols + idx];
+            if (a.a_dt == SG_DT_I8) v *= a.scale_A;
+            if (a.bias) v += __half2float(a.bias[col]);
+            const int64_t o = (int64_t)m * a.ldc + col;
+            switch (a.c_dt) {
+              case SG_DT_F32: sgd::store_from_float<SG_DT_F32>(a.C, o, v); break;
+              case SG_DT_BF16: sgd::store_from_float<SG_DT_BF16>(a.C, o, v); break;
+              default: sgd::store_from_float<SG_DT_F16>(a.C, o, v); break;
+            }
+          }
+        }
+        asm volatile("bar.sync 2, %0;" ::"n"(kConsumerWarps * 32) : "memory");  // red is free for the next tile
+      }
+    }
+  }
+  if (!split) return;
+  __syncthreads();
+  // ---- split K: rank r adds the ranks' partials (in rank order) of its 1/ksplit of the tile's outputs
+  cg::cluster_group cluster = cg::this_cluster();
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+  cluster.sync();
+  int aborted = 0;
+  for (int r = 0; r < a.ksplit; ++r) aborted |= *cluster.map_shared_rank(&s_abort, r);
+  if (!aborted) {
+    const float* parts[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) parts[q] = cluster.map_shared_rank(red, q < a.ksplit ? q : 0);
+    const int tile = blockIdx.y;
+    const int tot = a.M * kTileCols, per = (tot + a.ksplit - 1) / a.ksplit;
+    const int hi = min(tot, (sp + 1) * per);
+    for (int idx = sp * per + threadIdx.x; idx < hi; idx += kThreads) {
+      const int m = idx / kTileCols, cc = idx - m * kTileCols;
+      const int col = tile * kTileCols + cc;
+      if (col >= a.N) continue;
+      float pv[8][2];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        pv[q][0] = q < a.ksplit ? parts[q][idx] : 0.f;
+        pv[q][1] = q < a.ksplit ? parts[q][MT * kTileCols + idx] : 0.f;
+      }
+      float v = 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (q < a.ksplit) v += pv[q][0] + pv[q][1];
+      if (a.a_dt == SG_DT_I8) v *= a.scale_A;
+      if (a.bias) v += __half2float(a.bias[col]);
+      const int64_t o = (int64_t)m * a.ldc + col;
+      switch (a.c_dt) {
+        case SG_DT_F32: sgd::store_from_float<SG_DT_F32>(a.C, o, v); break;
+        case SG_DT_BF16: sgd::store_from_float<SG_DT_BF16>(a.C, o, v); break;
+        default: sgd::store_from_float<SG_DT_F16>(a.C, o, v); break;
+      }
+    }
+  }
+  cluster.sync();  // peers keep their shared memory until every rank has read it
+}
+
+struct RPlan {
+  bool ok = false;
+  int mt = 8, n_tiles = 0, cpt = 0, ksplit = 1, x_slots = 0;
+  int blocks = 0;  // ksplit == 1: persistent blocks, each taking every blocks-th tile
+  int stages = kMinStages;
+  size_t smem = 0;
+};
+
+size_t rows_smem(int mt, int x_slots, int stages) {
+  return 1024 + (size_t)stages * kStageBytes + 2 * stages * 8 + (size_t)mt * (x_slots * 64 + 8) * 2 +
+         2 * (size_t)mt * kTileCols * 4;
+}
+
+// Blocks of this kernel (at the given shared memory, no cluster) resident per SM.
+int rows_blocks_per_sm(size_t smem) {
+  static std::mutex mu;
+  static int cache[8] = {};  // [smem bucket of 32 KB]
+  const int bucket = (int)std::min<size_t>(7, smem / (32 * 1024));
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache[bucket] != 0) return cache[bucket];
+  int n = 0;
+  auto kfn = w4_rows_kernel<true, 16>;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kfn, kThreads, (size_t)(bucket + 1) * 32 * 1024) !=
+          cudaSuccess) {
+    cudaGetLastError();
+    n = -1;
+  }
+  cache[bucket] = n;
+  return n;
+}
+
+// Clusters of k blocks of this kernel (at the given shared memory) resident at once.
+int rows_active_clusters(int k, size_t smem) {
+  static std::mutex mu;
+  static int cache[9][8] = {};  // [k][smem bucket of 32 KB]
+  const int bucket = (int)std::min<size_t>(7, smem / (32 * 1024));
+  std::lock_guard<std::mutex> lk(mu);
+  if (k < 1 || k > 8) return 0;
+  if (cache[k][bucket] != 0) return cache[k][bucket];
+  const int bytes = (int)((size_t)(bucket + 1) * 32 * 1024);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(k, 1);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = bytes;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = k;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  auto kfn = w4_rows_kernel<true, 16>;
+  // the attribute only ever grows (a launch may already rely on a larger value)
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) != cudaSuccess ||
+      cudaOccupancyMaxActiveClusters(&n, kfn, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = -1;
+  }
+  cache[k][bucket] = n;
+  return n;
+}
+
+std::atomic<int> g_rows_enable{1};
+std::atomic<int> g_rows_max_tiles{1 << 30};  // widest output (in 128-column tiles) taken
+std::atomic<int> g_rows_stages{0};  // 0: deepest ring that fits
+
+RPlan make_rplan(const SgMatMulParams* p, int sms) {
+  RPlan pl;
+  const int gs = p->group_size > 0 ? p->group_size : 128;
+  if (p->M < 2 || p->M > 16 || p->K <= 0 || p->N <= 0 || (p->N % 16) != 0 || (gs % 32) != 0) return pl;
+  if ((p->N + kTileCols - 1) / kTileCols > g_rows_max_tiles.load()) return pl;
+  if (!sg::aligned16(p->B) || !sg::aligned16(p->scales_B) || (p->zeros_B && !sg::aligned16(p->zeros_B))) return pl;
+  pl.mt = p->M <= 8 ? 8 : 16;
+  pl.n_tiles = (p->N + kTileCols - 1) / kTileCols;
+  pl.cpt = ((p->K + 1) / 2 + kRowsPerChunk - 1) / kRowsPerChunk;
+  // the largest split that keeps every cluster resident in one wave; many tiles: one block each
+  int ks = 1;
+  for (int k = std::min({8, pl.cpt, std::max(1, (2 * sms) / pl.n_tiles)}); k >= 2; --k) {
+    const size_t smem = rows_smem(pl.mt, (pl.cpt + k - 1) / k, kMinStages);
+    if (smem <= 200 * 1024 && rows_active_clusters(k, smem) >= pl.n_tiles) {
+      ks = k;
+      break;
+    }
+  }
+  pl.ksplit = ks;
+  pl.x_slots = (pl.cpt + ks - 1) / ks;
+  // the deepest ring that fits (more weight bytes in flight per SM)
+  // (no deeper than the chunks one block streams)
+  const int want = g_rows_stages.load();
+  const long chunks = (long)pl.x_slots * (ks > 1 ? 1 : (pl.n_tiles + sms - 1) / sms);
+  pl.stages = kMinStages;
+  for (int st = kMinStages * 2; st <= 32; st *= 2)
+    if ((want == 0 ? st / 2 < chunks : st <= want) && rows_smem(pl.mt, pl.x_slots, st) <= (size_t)kMaxSmem)
+      pl.stages = st;
+  while (ks > 1 && pl.stages > kMinStages && rows_active_clusters(ks, rows_smem(pl.mt, pl.x_slots, pl.stages)) < pl.n_tiles)
+    pl.stages /= 2;
+  pl.smem = rows_smem(pl.mt, pl.x_slots, pl.stages);
+  if (pl.smem > (size_t)kMaxSmem) return pl;
+  if (ks > 1) {
+    pl.blocks = pl.n_tiles;
+  } else {
+    // persistent blocks stage the activations once; one per SM unless two per
+    // SM finish the tiles in fewer rounds (two blocks share an SM's issue slots)
+    const int bps = rows_blocks_per_sm(pl.smem);
+    if (bps < 1) return pl;
+    const int r1 = (pl.n_tiles + sms - 1) / sms;
+    const int r2 = bps >= 2 ? 2 * ((pl.n_tiles + 2 * sms - 1) / (2 * sms)) : 1 << 30;
+    pl.blocks = std::min(pl.n_tiles, r2 <= r1 ? 2 * sms : sms);
+  }
+  pl.ok = true;
+  return pl;
+}
+
+}  // namespace
+
+namespace sg {
+
+bool w4_rows_tuning(std::string_view key, int value) {
+  if (key == "w4_rows.enable") {
+    g_rows_enable.store(value);
+    return true;
+  }
+  if (key == "w4_rows.stages") {
+    g_rows_stages.store(value);
+    return true;
+  }
+  if (key == "w4_rows.max_tiles") {
+    g_rows_max_tiles.store(std::max(1, value));
+    return true;
+  }
+  return false;
+}
+
+SgStatus w4_rows_run(const SgMatMulParams* p, cudaStream_t cs, int sms, int* err_word, bool* handled) {
+  *handled = false;
+  if (!g_rows_enable.load()) return SG_OK;
+  const RPlan pl = make_rplan(p, sms);
+  if (!pl.ok) return SG_OK;
+  *handled = true;
+  const int gs = p->group_size > 0 ? p->group_size : 128;
+  const int KP = (p->K + 1) / 2;
+  const int G = (p->K + gs - 1) / gs;
+  CUtensorMap tw, ts, tz;
+  SgStatus st;
+  {
+    const uint64_t dims[2] = {(uint64_t)p->N, (uint64_t)KP};
+    const uint64_t strides[1] = {(uint64_t)p->N};
+    const uint32_t box[2] = {128, (uint32_t)kRowsPerChunk};
+    st = make_tensor_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(p->B), dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != SG_OK) return st;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)p->N, (uint64_t)G};
+    const uint64_t sstr[1] = {(uint64_t)p->N * 2};
+    const uint32_t box[2] = {128, 2};
+    st = make_tensor_map(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(p->scales_B), dims, sstr, box,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != SG_OK) return st;
+    if (p->zeros_B) {
+      const uint64_t zstr[1] = {(uint64_t)p->N};
+      st = make_tensor_map(&tz, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(p->zeros_B), dims, zstr, box,
+                           CU_TENSOR_MAP_SWIZZLE_NONE);
+      if (st != SG_OK) return st;
+    } else {
+      tz = ts;  // never read
+    }
+  }
+  RArgs a{};
+  a.A = p->A;
+  a.bias = static_cast<const __half*>(p->bias);
+  a.C = p->C;
+  a.M = p->M;
+  a.K = p->K;
+  a.N = p->N;
+  a.lda = p->lda > 0 ? p->lda : p->K;
+  a.ldc = p->ldc > 0 ? p->ldc : p->N;
+  a.gs = gs;
+  a.gs_shift = ((gs & (gs - 1)) == 0) ? __builtin_ctz((unsigned)gs) : -1;
+  a.a_dt = p->a_dtype == SG_DT_DEFAULT ? SG_DT_I8 : p->a_dtype;
+  a.c_dt = p->c_dtype == SG_DT_DEFAULT ? SG_DT_F16 : p->c_dtype;
+  a.scale_A = p->scale_A;
+  a.n_tiles = pl.n_tiles;
+  a.cpt = pl.cpt;
+  a.ksplit = pl.ksplit;
+  a.x_slots = pl.x_slots;
+  a.static_w = (p->flags & SG_MM_STATIC_WEIGHTS) ? 1 : 0;
+  a.stage_shift = __builtin_ctz((unsigned)pl.stages);
+  a.x_vec = sg::aligned16(p->A) && a.lda % 8 == 0 && p->K % 8 == 0;
+  a.err = err_word;
+  using KFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, RArgs);
+  static const KFn kfns[2][2] = {{w4_rows_kernel<false, 8>, w4_rows_kernel<false, 16>},
+                                 {w4_rows_kernel<true, 8>, w4_rows_kernel<true, 16>}};
+  const int zi = p->zeros_B ? 1 : 0, mi = pl.mt == 8 ? 0 : 1;
+  const KFn kfn = kfns[zi][mi];
+  // every instantiation gets the largest shared-memory opt-in once; the
+  // occupancy query above relies on the same value
+  static std::once_flag once[2][2];
+  cudaError_t ae = cudaSuccess;
+  std::call_once(once[zi][mi], [&] { ae = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem); });
+  if (ae != cudaSuccess) {
+    cudaGetLastError();
+    set_error("w4_rows: cudaFuncSetAttribute(%d) failed: %s", kMaxSmem, cudaGetErrorString(ae));
+    return SG_ERR_RUNTIME;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.ksplit, pl.blocks);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = cs;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = pl.ksplit;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pl.ksplit > 1 ? 2 : 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, tw, ts, tz, a);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("w4_rows_kernel launch failed: %s", cudaGetErrorString(e));
+    return SG_ERR_RUNTIME;
+  }
+  return SG_OK;
+}
+
+}  // namespace sg

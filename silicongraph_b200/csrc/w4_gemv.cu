@@ -382,6 +382,8 @@ size_t w4_gemv_mma_scratch_bytes(const SgMatMulParams* p, int sms, bool* applica
 SgStatus w4_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, void* ws, size_t ws_bytes,
                          int* err_word, bool* handled);
 bool w4_gemv_mma_tuning(std::string_view key, int value);
+SgStatus w4_rows_run(const SgMatMulParams* p, cudaStream_t cs, int sms, int* err_word, bool* handled);
+bool w4_rows_tuning(std::string_view key, int value);
 bool gemm_tc_tuning(std::string_view key, int value);
 bool attn_tc_tuning(std::string_view key, int value);
 bool attn_tuning(std::string_view key, int value);
@@ -420,6 +422,16 @@ static SgStatus w4_run(const SgMatMulParams* p, void* stream, void* ws, size_t w
   a.scale_A = p->scale_A;
 
   const int path = g_tune_path.load();
+  // 2..16 activation rows (batched decode): fp16-dequant mma.sync GEMM (w4_gemm_rows.cu).
+  if (path == 0 && p->M >= 2 && p->M <= 16) {
+    if (err_word == nullptr) {
+      st = sg::device_error_word(&err_word);
+      if (st != SG_OK) return st;
+    }
+    bool handled = false;
+    st = sg::w4_rows_run(p, cs, sms, err_word, &handled);
+    if (handled || st != SG_OK) return st;
+  }
   // Many activation rows: tcgen05 GEMM with the weights dequantized into TMEM (gemm_tc.cu).
   bool tc_ok = false;
   const size_t tc_ws = path == 0 ? sg::gemm_tc_scratch_bytes(p, false, &tc_ok) : 0;
@@ -552,6 +564,7 @@ int32_t sg_set_tuning(const char* key, int32_t value) {
     return SG_OK;
   }
   if (key && sg::w4_gemv_mma_tuning(std::string_view(key), value)) return SG_OK;
+  if (key && sg::w4_rows_tuning(std::string_view(key), value)) return SG_OK;
   if (key && sg::gemm_tc_tuning(std::string_view(key), value)) return SG_OK;
   if (key && sg::attn_tc_tuning(std::string_view(key), value)) return SG_OK;
   if (key && sg::attn_tuning(std::string_view(key), value)) return SG_OK;

@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS <= 8 ? 2 : 1)
   constexpr int kTC = STRIPS * 128;
   constexpr int kOffW = 0, kOffSZ = off_sz(WARPS, STAGES), kOffX = off_x(WARPS, STAGES);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = sgd::align_smem_1024(smem_raw);
   uint32_t* xst = reinterpret_cast<uint32_t*>(smem + kOffX);         // [slot][32 rows]: x_q bytes
   int2* xgrp = reinterpret_cast<int2*>(xst + a.x_slots * kRows);       // [slot][half]: scale bits, sum x_q
   uint64_t* bars = reinterpret_cast<uint64_t*>(xgrp + a.x_slots * 2);

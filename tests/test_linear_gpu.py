@@ -352,3 +352,62 @@ def test_int4_cluster_and_stream_k_splits(sg, oracle_mod, cluster, K, N, gs):
     close(C.cpu().numpy(), want)
     assert torch.equal(C, C2)
     assert torch.equal(C, C3)
+
+
+@pytest.mark.parametrize("M,K,N,gs,sym", [
+    (16, 2048, 3072, 32, False),   # batch-16 decode, q|k|v shape
+    (13, 8192, 2048, 32, False),   # odd row count, long K (clusters of K splits)
+    (7, 1024, 4096, 128, True),    # symmetric, group 128
+    (2, 2048, 8192, 32, False),    # 64 tiles
+    (9, 130, 48, 32, False),       # ragged K and a partial tile
+])
+def test_int4_few_rows_kernel(sg, oracle_mod, M, K, N, gs, sym):
+    """2..16 activation rows on the fp16-dequant mma.sync kernel: the oracle's
+    result within tolerance, repeatable bit for bit, with and without the
+    static-weight launch."""
+    from silicongraph_b200 import _lib
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=M * 7 + K, sym=sym)
+    x = np.random.default_rng(M + N).standard_normal((M, K)).astype(np.float32)
+    xh = x.astype(np.float16)
+    want = oracle_mod.matmul_int4_grouped(xh, B, S, Z, K, N, gs, M=M, c_dt=oracle_mod.DT_F32)
+    args = (t(xh), t(B), t(S), None if Z is None else t(Z), K, N, gs)
+    C = sg.matmul_int4_grouped(*args, out_dtype=torch.float32)
+    C2 = sg.matmul_int4_grouped(*args, out_dtype=torch.float32, flags=_lib.SG_MM_STATIC_WEIGHTS)
+    close(C.cpu().numpy(), want)
+    assert torch.equal(C, C2)
+
+
+@pytest.mark.parametrize("xdt", ["f32", "bf16"])
+def test_int4_few_rows_activation_types(sg, oracle_mod, xdt):
+    """fp32 and bf16 activation rows on the few-rows kernel (staged as fp16,
+    8 values per load): the oracle's result on the same activations within
+    tolerance."""
+    M, K, N, gs = 6, 2048, 1024, 32
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=21)
+    x = np.random.default_rng(5).standard_normal((M, K)).astype(np.float32)
+    if xdt == "bf16":
+        xt = bf16_tensor(x)
+        x = xt.float().cpu().numpy()
+    else:
+        xt = t(x)
+    want = oracle_mod.matmul_int4_grouped(x, B, S, Z, K, N, gs, M=M, c_dt=oracle_mod.DT_F32)
+    C = sg.matmul_int4_grouped(xt, t(B), t(S), t(Z), K, N, gs, out_dtype=torch.float32)
+    close(C.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("M,K,N,sym", [
+    (5, 1024, 40960, False),   # 320 tiles: persistent blocks take two or three tiles each
+    (16, 2048, 20480, True),   # 160 tiles: one tile per block, no K split
+])
+def test_int4_few_rows_persistent(sg, oracle_mod, M, K, N, sym):
+    """Wide outputs on the few-rows kernel: persistent blocks without a K
+    split; the oracle's result within tolerance and repeatable bit for bit."""
+    gs = 32
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=M + 3, sym=sym)
+    x = np.random.default_rng(N).standard_normal((M, K)).astype(np.float32).astype(np.float16)
+    want = oracle_mod.matmul_int4_grouped(x, B, S, Z, K, N, gs, M=M, c_dt=oracle_mod.DT_F32)
+    args = (t(x), t(B), t(S), None if Z is None else t(Z), K, N, gs)
+    C = sg.matmul_int4_grouped(*args, out_dtype=torch.float32)
+    C2 = sg.matmul_int4_grouped(*args, out_dtype=torch.float32)
+    close(C.cpu().numpy(), want)
+    assert torch.equal(C, C2)
