@@ -1,20 +1,19 @@
 // INT4 group-quantised GEMM for a few activation rows (2..16: batched decode)
 // on the tensor cores (sm_100a).  Same contract and weight layout as
 // w4_gemv.cu (compiler/kernels/cpu/matmul_neon.h:113-143); used when
-// 2 <= M <= 16, group_size % 32 == 0 and N % 16 == 0 (measured faster than
-// both the tcgen05 GEMM and the GEMV kernels on every decoder shape there).
+// 2 <= M <= 16, the group size is a power of two >= 32 and N % 16 == 0
+// (measured faster than both the tcgen05 GEMM and the GEMV kernels on every
+// decoder shape there).
 //
 //   * Tile = 128 output columns.  Few tiles: a cluster of ksplit blocks shares
 //     a tile's K range, and each rank adds the ranks' partials of 1/ksplit of
 //     the tile's outputs in rank order from their shared memory
 //     (deterministic, no scratch).  Many tiles: persistent blocks (one or two
 //     per SM) stage the activations once and take every blocks-th tile, the
-//     weight ring running on across tiles; results go straight from the
-//     accumulators to C.
-//   * One producer warp streams 32 k-pair rows x 128 columns of packed weights
-//     (128-byte swizzled TMA box) plus the chunk's two scale and zero-point
-//     rows through a ring of 8 to 32 stages (as deep as shared memory allows:
-//     the kernel is bound by the weight bytes in flight per SM).  Two sets of
+//     weight ring running on across tiles.
+//   * One producer warp streams chunks of 64 k-pair rows (128 k) x 128
+//     columns of packed weights (128-byte swizzled TMA box) plus the chunk's
+//     scale and zero-point rows through a ring of 4 to 16 stages.  Two sets of
 //     8 consumer warps take alternate chunks; in a set each warp owns 16
 //     columns, and the two sets' partials are added in set order at the end.
 //   * A warp's 16 columns are the 16 rows of the mma.sync m16n8k16 A operand
@@ -24,7 +23,8 @@
 //     is 1/16), so subtracting (1032 + zero, 72 + zero) is exact and one
 //     multiply by the scale rounds once: the fp16 weight scale * (q - 8 - zero).
 //   * The activation rows, staged once per block in fp16, are the B columns
-//     (8 rows per n-tile); D accumulates in fp32 over the block's whole range.
+//     (8 rows per n-tile, fetched with ldmatrix); D accumulates in fp32 over
+//     the block's whole range.
 #include <cooperative_groups.h>
 
 #include <algorithm>
@@ -36,24 +36,25 @@
 
 namespace {
 
-constexpr int kRowsPerChunk = 32;  // k-pair rows per chunk (64 k)
+constexpr int kRowsPerChunk = 64;  // k-pair rows per chunk (128 k)
 constexpr int kTileCols = 128;
 constexpr int kColWarps = 8;                         // warps per chunk: 16 columns each
 constexpr int kConsumerWarps = 2 * kColWarps;        // two sets, taking alternate chunks
 constexpr int kThreads = (kConsumerWarps + 1) * 32;  // + the producer warp
-constexpr int kMinStages = 8;  // ring depth: 8, 16 or 32 chunks (the most that fit shared memory)
+constexpr int kMinStages = 4;  // ring depth: 4, 8 or 16 chunks (the most that fit shared memory)
+constexpr int kMaxStages = 16;
 constexpr int kMaxSmem = 227 * 1024 - 2048;  // opt-in limit minus this kernel's static shared memory
-constexpr int kWBytes = 128 * kRowsPerChunk;      // 4096
-constexpr int kSBytes = 128 * 2 * 2;              // 2 scale rows x 128 fp16
-constexpr int kZBytes = 128 * 2;                  // 2 zero rows x 128 int8
-constexpr int kSZBytes = kSBytes + kZBytes;       // 768
-constexpr int kStageBytes = kWBytes + kSZBytes;   // 4864: weights [stage][4096] (1024-aligned for the swizzle), then [stage][768]
+constexpr int kWBytes = 128 * kRowsPerChunk;      // 8192
+constexpr int kSBytes = 128 * 4 * 2;              // up to 4 scale rows (group 32) x 128 fp16
+constexpr int kZBytes = 128 * 4;                  // up to 4 zero rows x 128 int8
+constexpr int kSZBytes = kSBytes + kZBytes;       // 1536
+constexpr int kStageBytes = kWBytes + kSZBytes;   // weights [stage][8192] (1024-aligned for the swizzle), then [stage][1536]
 
 struct RArgs {
   const void* A;
   const __half* bias;
   void* C;
-  int M, K, N, lda, ldc, gs, gs_shift;
+  int M, K, N, lda, ldc, gs_shift;
   int a_dt, c_dt;
   float scale_A;
   int n_tiles, cpt, ksplit, x_slots;
@@ -107,8 +108,6 @@ __device__ __forceinline__ uint4 load_act8(const void* A, int dt, int64_t i) {
   }
 }
 
-__device__ __forceinline__ int group_of(const RArgs& a, int k) { return a.gs_shift >= 0 ? (k >> a.gs_shift) : k / a.gs; }
-
 // (1024 + q_lo, 64 + q_hi) of the byte at `sel` (0x4040: byte 0, 0x4141: byte 1) of w
 __device__ __forceinline__ __half2 nibble_pair(uint32_t w, uint32_t sel) {
   const uint32_t x = __byte_perm(w, 0u, sel);
@@ -118,7 +117,8 @@ __device__ __forceinline__ __half2 nibble_pair(uint32_t w, uint32_t sel) {
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
 
-template <bool HAS_Z, int MT>
+// GPC: groups per chunk (128 k): 4 for group 32, 2 for group 64, 1 for larger groups.
+template <bool HAS_Z, int MT, int GPC>
 __global__ void __launch_bounds__(kThreads, 1)
     w4_rows_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmS,
                    const __grid_constant__ CUtensorMap tmZ, RArgs a) {
@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nst = 1 << a.stage_shift;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + nst * kStageBytes);
   uint64_t* empty = full + nst;
-  const int XP = a.x_slots * 64 + 8;  // staged k per row, padded (bank spread)
+  const int XP = a.x_slots * 128 + 8;  // staged k per row, padded (bank spread)
   __half* xs = reinterpret_cast<__half*>(empty + nst);  // [MT][XP]
   float* red = reinterpret_cast<float*>(xs + MT * XP);      // [2 sets][MT][128] this block's partials
   __shared__ int s_abort;
@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- producer: weights that no earlier kernel writes stream before the dependency wait
     if (!a.static_w) sgd::pdl_wait();
     if (lane == 0) {
-      const uint32_t tx = kWBytes + kSBytes + (HAS_Z ? kZBytes : 0);
+      constexpr uint32_t tx = kWBytes + GPC * (256 + (HAS_Z ? 128 : 0));
       int it = 0;  // chunks issued, over all tiles of this block
       bool stop = false;
       for (int tile = blockIdx.y; tile < a.n_tiles && !stop; tile += gridDim.y) {
@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const int row0 = (cr0 + i) * kRowsPerChunk;
-          const int gA = group_of(a, 2 * row0);
+          const int gA = (2 * row0) >> a.gs_shift;
           uint8_t* wst = smem + s * kWBytes;
           uint8_t* szst = smem + nst * kWBytes + s * kSZBytes;
           sgd::mbar_arrive_expect_tx(&full[s], tx);
@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---- consumers: stage the activation rows once (fp16, zero past M and K), then the chunks
     sgd::pdl_wait();
-    const int span = nch * 64;
+    const int span = nch * 128;
     if (a.x_vec) {
       // 8 values per thread and access, 4 accesses in flight per thread
       constexpr int kU = 4, kT = kConsumerWarps * 32;
@@ -189,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
           const int idx = base + u * kT;
-          const int m = idx / nv, k = cr0 * 64 + 8 * (idx - m * nv);
+          const int m = idx / nv, k = cr0 * 128 + 8 * (idx - m * nv);
           v[u] = make_uint4(0u, 0u, 0u, 0u);
           if (idx < total && m < a.M && k < a.K) v[u] = load_act8(a.A, a.a_dt, (int64_t)m * a.lda + k);
         }
@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
       for (int idx = threadIdx.x; idx < MT * span; idx += kConsumerWarps * 32) {
         const int m = idx / span, kk = idx - m * span;
-        const int k = cr0 * 64 + kk;
+        const int k = cr0 * 128 + kk;
         const float v = (m < a.M && k < a.K) ? load_act(a.A, a.a_dt, (int64_t)m * a.lda + k) : 0.f;
         xs[m * XP + kk] = __float2half_rn(v);
       }
@@ -218,6 +218,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // MT 8: matrices (k half j % 2) of steps 2p + j / 2
     const int lj = lane >> 3, lr = lane & 7;
     const __half* xrow = MT == 16 ? xs + (8 * (lj >> 1) + lr) * XP + 8 * (lj & 1) : xs + lr * XP + 8 * lj;
+    // this lane's weight bytes in a stage: k-pair rows 8 st + t (+ 4), 16-byte column group cw (swizzled)
+    const int wl0 = t * 128 + ((cw ^ t) << 4) + 2 * g, wl1 = (t + 4) * 128 + ((cw ^ (t + 4)) << 4) + 2 * g;
     float* myred = red + cp * MT * kTileCols;
     bool dead = false;  // a wait of this warp ran out: skip the rest, keep to the barriers
     int it0 = 0;
@@ -238,58 +240,59 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const uint8_t* W = smem + s * kWBytes;
         const uint8_t* SZ = smem + nst * kWBytes + s * kSZBytes;
-        const int k0 = (cr0 + i) * 64;
-        const int srowB = group_of(a, k0 + 32) - group_of(a, k0);
-        __half2 sc[2][2], off[2][2];  // [half of the chunk][column c0 / c0 + 1]
+        const __half* xi = xrow + i * 128;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int srow = h ? srowB : 0;
-          const uint32_t s2 = *reinterpret_cast<const uint32_t*>(SZ + (srow * 128 + c0) * 2);  // scales c0, c0 + 1
+        for (int gi = 0; gi < GPC; ++gi) {
+          // scale and zero of columns c0, c0 + 1 for group gi of the chunk
+          const uint32_t s2 = *reinterpret_cast<const uint32_t*>(SZ + (gi * 128 + c0) * 2);
           const uint32_t sd0 = __byte_perm(s2, 0u, 0x1010u), sd1 = __byte_perm(s2, 0u, 0x3232u);
-          sc[h][0] = *reinterpret_cast<const __half2*>(&sd0);
-          sc[h][1] = *reinterpret_cast<const __half2*>(&sd1);
+          const __half2 sc0 = *reinterpret_cast<const __half2*>(&sd0), sc1 = *reinterpret_cast<const __half2*>(&sd1);
+          __half2 off0, off1;
           if (HAS_Z) {
             // zero byte z -> fp16 pair (1152 + z, 1152 + z) by bits, minus (120, 1080): (1032 + z, 72 + z), exact
-            const uint32_t zz = *reinterpret_cast<const uint16_t*>(SZ + kSBytes + srow * 128 + c0);
+            const uint32_t zz = *reinterpret_cast<const uint16_t*>(SZ + kSBytes + gi * 128 + c0);
             const __half2 bias = __halves2half2(__ushort_as_half(0x5780), __ushort_as_half(0x6438));  // 120, 1080
+            const uint32_t m0 = (__byte_perm(zz, 0u, 0x4040u) ^ 0x00800080u) | 0x64006400u;
+            const uint32_t m1 = (__byte_perm(zz, 0u, 0x4141u) ^ 0x00800080u) | 0x64006400u;
+            off0 = __hsub2(*reinterpret_cast<const __half2*>(&m0), bias);
+            off1 = __hsub2(*reinterpret_cast<const __half2*>(&m1), bias);
+          } else {
+            off0 = off1 = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x5480));  // 1032, 72
+          }
+          constexpr int kSteps = 8 / GPC;  // 16-k steps in the group's part of the chunk
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-              const uint32_t m = (__byte_perm(zz, 0u, c ? 0x4141u : 0x4040u) ^ 0x00800080u) | 0x64006400u;
-              off[h][c] = __hsub2(*reinterpret_cast<const __half2*>(&m), bias);
+          for (int j = 0; j < kSteps; j += (MT == 16 ? 1 : 2)) {
+            const int st0 = gi * kSteps + j;
+            uint32_t bx[2][2][2];  // [step][n-tile][k half]
+            {
+              uint32_t r0, r1, r2, r3;
+              sgd::ldmatrix_x4(r0, r1, r2, r3, xi + 16 * st0);
+              if (MT == 16) {
+                bx[0][0][0] = r0;
+                bx[0][0][1] = r1;
+                bx[0][1][0] = r2;
+                bx[0][1][1] = r3;
+              } else {
+                bx[0][0][0] = r0;
+                bx[0][0][1] = r1;
+                bx[1][0][0] = r2;
+                bx[1][0][1] = r3;
+              }
             }
-          } else {
-            off[h][0] = off[h][1] = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x5480));  // 1032, 72
+#pragma unroll
+            for (int u = 0; u < (MT == 16 ? 1 : 2); ++u) {
+              const int st = st0 + u;
+              const uint32_t w0 = *reinterpret_cast<const uint16_t*>(W + st * 1024 + wl0);
+              const uint32_t w1 = *reinterpret_cast<const uint16_t*>(W + st * 1024 + wl1);
+              const uint32_t a0 = h2_bits(__hmul2(__hsub2(nibble_pair(w0, 0x4040u), off0), sc0));
+              const uint32_t a1 = h2_bits(__hmul2(__hsub2(nibble_pair(w0, 0x4141u), off1), sc1));
+              const uint32_t a2 = h2_bits(__hmul2(__hsub2(nibble_pair(w1, 0x4040u), off0), sc0));
+              const uint32_t a3 = h2_bits(__hmul2(__hsub2(nibble_pair(w1, 0x4141u), off1), sc1));
+#pragma unroll
+              for (int n = 0; n < MT / 8; ++n)
+                sgd::mma_f16_16816(acc[n], a0, a1, a2, a3, bx[MT == 16 ? 0 : u][n][0], bx[MT == 16 ? 0 : u][n][1]);
+            }
           }
-        }
-        uint32_t bx[4][MT / 8][2];  // B fragments [16-k step][n-tile][k half]
-#pragma unroll
-        for (int q = 0; q < 4; q += (MT == 16 ? 1 : 2)) {
-          uint32_t r0, r1, r2, r3;
-          sgd::ldmatrix_x4(r0, r1, r2, r3, xrow + i * 64 + 16 * q);
-          if (MT == 16) {
-            bx[q][0][0] = r0;
-            bx[q][0][1] = r1;
-            bx[q][MT / 8 - 1][0] = r2;
-            bx[q][MT / 8 - 1][1] = r3;
-          } else {
-            bx[q][0][0] = r0;
-            bx[q][0][1] = r1;
-            bx[q + 1][0][0] = r2;
-            bx[q + 1][0][1] = r3;
-          }
-        }
-#pragma unroll
-        for (int st = 0; st < 4; ++st) {
-          const int h = st >> 1;
-          const int r0 = 8 * st + t, r1 = r0 + 4;  // k-pair rows of k-slots (2t, 2t+1) and (2t+8, 2t+9)
-          const uint32_t w0 = *reinterpret_cast<const uint16_t*>(W + r0 * 128 + ((cw ^ (r0 & 7)) << 4) + 2 * g);
-          const uint32_t w1 = *reinterpret_cast<const uint16_t*>(W + r1 * 128 + ((cw ^ (r1 & 7)) << 4) + 2 * g);
-          const uint32_t a0 = h2_bits(__hmul2(__hsub2(nibble_pair(w0, 0x4040u), off[h][0]), sc[h][0]));
-          const uint32_t a1 = h2_bits(__hmul2(__hsub2(nibble_pair(w0, 0x4141u), off[h][1]), sc[h][1]));
-          const uint32_t a2 = h2_bits(__hmul2(__hsub2(nibble_pair(w1, 0x4040u), off[h][0]), sc[h][0]));
-          const uint32_t a3 = h2_bits(__hmul2(__hsub2(nibble_pair(w1, 0x4141u), off[h][1]), sc[h][1]));
-#pragma unroll
-          for (int n = 0; n < MT / 8; ++n) sgd::mma_f16_16816(acc[n], a0, a1, a2, a3, bx[st][n][0], bx[st][n][1]);
         }
         __syncwarp();
         if (lane == 0) sgd::mbar_arrive(&empty[s]);
@@ -378,7 +381,7 @@ struct RPlan {
 };
 
 size_t rows_smem(int mt, int x_slots, int stages) {
-  return 1024 + (size_t)stages * kStageBytes + 2 * stages * 8 + (size_t)mt * (x_slots * 64 + 8) * 2 +
+  return 1024 + (size_t)stages * kStageBytes + 2 * stages * 8 + (size_t)mt * (x_slots * 128 + 8) * 2 +
          2 * (size_t)mt * kTileCols * 4;
 }
 
@@ -390,7 +393,7 @@ int rows_blocks_per_sm(size_t smem) {
   std::lock_guard<std::mutex> lk(mu);
   if (cache[bucket] != 0) return cache[bucket];
   int n = 0;
-  auto kfn = w4_rows_kernel<true, 16>;
+  auto kfn = w4_rows_kernel<true, 16, 4>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) != cudaSuccess ||
       cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kfn, kThreads, (size_t)(bucket + 1) * 32 * 1024) !=
           cudaSuccess) {
@@ -422,7 +425,7 @@ int rows_active_clusters(int k, size_t smem) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  auto kfn = w4_rows_kernel<true, 16>;
+  auto kfn = w4_rows_kernel<true, 16, 4>;
   // the attribute only ever grows (a launch may already rely on a larger value)
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) != cudaSuccess ||
       cudaOccupancyMaxActiveClusters(&n, kfn, &cfg) != cudaSuccess) {
@@ -440,7 +443,8 @@ std::atomic<int> g_rows_stages{0};  // 0: deepest ring that fits
 RPlan make_rplan(const SgMatMulParams* p, int sms) {
   RPlan pl;
   const int gs = p->group_size > 0 ? p->group_size : 128;
-  if (p->M < 2 || p->M > 16 || p->K <= 0 || p->N <= 0 || (p->N % 16) != 0 || (gs % 32) != 0) return pl;
+  if (p->M < 2 || p->M > 16 || p->K <= 0 || p->N <= 0 || (p->N % 16) != 0 || gs < 32 || (gs & (gs - 1)) != 0)
+    return pl;
   if ((p->N + kTileCols - 1) / kTileCols > g_rows_max_tiles.load()) return pl;
   if (!sg::aligned16(p->B) || !sg::aligned16(p->scales_B) || (p->zeros_B && !sg::aligned16(p->zeros_B))) return pl;
   pl.mt = p->M <= 8 ? 8 : 16;
@@ -462,7 +466,7 @@ RPlan make_rplan(const SgMatMulParams* p, int sms) {
   const int want = g_rows_stages.load();
   const long chunks = (long)pl.x_slots * (ks > 1 ? 1 : (pl.n_tiles + sms - 1) / sms);
   pl.stages = kMinStages;
-  for (int st = kMinStages * 2; st <= 32; st *= 2)
+  for (int st = kMinStages * 2; st <= kMaxStages; st *= 2)
     if ((want == 0 ? st / 2 < chunks : st <= want) && rows_smem(pl.mt, pl.x_slots, st) <= (size_t)kMaxSmem)
       pl.stages = st;
   while (ks > 1 && pl.stages > kMinStages && rows_active_clusters(ks, rows_smem(pl.mt, pl.x_slots, pl.stages)) < pl.n_tiles)
@@ -513,12 +517,13 @@ SgStatus w4_rows_run(const SgMatMulParams* p, cudaStream_t cs, int sms, int* err
   const int gs = p->group_size > 0 ? p->group_size : 128;
   const int KP = (p->K + 1) / 2;
   const int G = (p->K + gs - 1) / gs;
+  const int gpc = gs == 32 ? 4 : gs == 64 ? 2 : 1;  // groups per 128-k chunk
   CUtensorMap tw, ts, tz;
   SgStatus st;
   {
     const uint64_t dims[2] = {(uint64_t)p->N, (uint64_t)KP};
     const uint64_t strides[1] = {(uint64_t)p->N};
-    const uint32_t box[2] = {128, (uint32_t)kRowsPerChunk};
+    const uint32_t box[2] = {128, (uint32_t)kRowsPerChunk};  // 64 k-pair rows
     st = make_tensor_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(p->B), dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_128B);
     if (st != SG_OK) return st;
@@ -526,7 +531,7 @@ SgStatus w4_rows_run(const SgMatMulParams* p, cudaStream_t cs, int sms, int* err
   {
     const uint64_t dims[2] = {(uint64_t)p->N, (uint64_t)G};
     const uint64_t sstr[1] = {(uint64_t)p->N * 2};
-    const uint32_t box[2] = {128, 2};
+    const uint32_t box[2] = {128, (uint32_t)gpc};  // the chunk's group rows
     st = make_tensor_map(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(p->scales_B), dims, sstr, box,
                          CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st != SG_OK) return st;
@@ -548,8 +553,7 @@ SgStatus w4_rows_run(const SgMatMulParams* p, cudaStream_t cs, int sms, int* err
   a.N = p->N;
   a.lda = p->lda > 0 ? p->lda : p->K;
   a.ldc = p->ldc > 0 ? p->ldc : p->N;
-  a.gs = gs;
-  a.gs_shift = ((gs & (gs - 1)) == 0) ? __builtin_ctz((unsigned)gs) : -1;
+  a.gs_shift = __builtin_ctz((unsigned)gs);
   a.a_dt = p->a_dtype == SG_DT_DEFAULT ? SG_DT_I8 : p->a_dtype;
   a.c_dt = p->c_dtype == SG_DT_DEFAULT ? SG_DT_F16 : p->c_dtype;
   a.scale_A = p->scale_A;
@@ -562,15 +566,18 @@ SgStatus w4_rows_run(const SgMatMulParams* p, cudaStream_t cs, int sms, int* err
   a.x_vec = sg::aligned16(p->A) && a.lda % 8 == 0 && p->K % 8 == 0;
   a.err = err_word;
   using KFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, RArgs);
-  static const KFn kfns[2][2] = {{w4_rows_kernel<false, 8>, w4_rows_kernel<false, 16>},
-                                 {w4_rows_kernel<true, 8>, w4_rows_kernel<true, 16>}};
-  const int zi = p->zeros_B ? 1 : 0, mi = pl.mt == 8 ? 0 : 1;
-  const KFn kfn = kfns[zi][mi];
+  static const KFn kfns[2][2][3] = {
+      {{w4_rows_kernel<false, 8, 4>, w4_rows_kernel<false, 8, 2>, w4_rows_kernel<false, 8, 1>},
+       {w4_rows_kernel<false, 16, 4>, w4_rows_kernel<false, 16, 2>, w4_rows_kernel<false, 16, 1>}},
+      {{w4_rows_kernel<true, 8, 4>, w4_rows_kernel<true, 8, 2>, w4_rows_kernel<true, 8, 1>},
+       {w4_rows_kernel<true, 16, 4>, w4_rows_kernel<true, 16, 2>, w4_rows_kernel<true, 16, 1>}}};
+  const int zi = p->zeros_B ? 1 : 0, mi = pl.mt == 8 ? 0 : 1, gi = gpc == 4 ? 0 : gpc == 2 ? 1 : 2;
+  const KFn kfn = kfns[zi][mi][gi];
   // every instantiation gets the largest shared-memory opt-in once; the
   // occupancy query above relies on the same value
-  static std::once_flag once[2][2];
+  static std::once_flag once[2][2][3];
   cudaError_t ae = cudaSuccess;
-  std::call_once(once[zi][mi], [&] { ae = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem); });
+  std::call_once(once[zi][mi][gi], [&] { ae = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem); });
   if (ae != cudaSuccess) {
     cudaGetLastError();
     set_error("w4_rows: cudaFuncSetAttribute(%d) failed: %s", kMaxSmem, cudaGetErrorString(ae));
