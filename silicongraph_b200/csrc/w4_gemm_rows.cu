@@ -15,7 +15,10 @@
 //     columns of packed weights (128-byte swizzled TMA box) plus the chunk's
 //     scale and zero-point rows through a ring of 4 to 16 stages.  Two sets of
 //     8 consumer warps take alternate chunks; in a set each warp owns 16
-//     columns, and the two sets' partials are added in set order at the end.
+//     columns, and the sets' partials are added in set order at the end.
+//   * The nibble unpacking is written as explicit prmt + lop3 (one three-input
+//     logic op with both constants in registers); the same expression in C
+//     compiled to two logic ops per weight pair.
 //   * A warp's 16 columns are the 16 rows of the mma.sync m16n8k16 A operand
 //     (A row g = column 2g, row g + 8 = column 2g + 1); a lane's byte of two
 //     k gives both halves of one A register: (byte & 0x0F) | 0x6400 is
@@ -39,7 +42,8 @@ namespace {
 constexpr int kRowsPerChunk = 64;  // k-pair rows per chunk (128 k)
 constexpr int kTileCols = 128;
 constexpr int kColWarps = 8;                         // warps per chunk: 16 columns each
-constexpr int kConsumerWarps = 2 * kColWarps;        // two sets, taking alternate chunks
+constexpr int kSets = 2;                             // consumer sets, taking every kSets-th chunk (3 measured slower)
+constexpr int kConsumerWarps = kSets * kColWarps;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;  // + the producer warp
 constexpr int kMinStages = 4;  // ring depth: 4, 8 or 16 chunks (the most that fit shared memory)
 constexpr int kMaxStages = 16;
@@ -60,6 +64,7 @@ struct RArgs {
   int n_tiles, cpt, ksplit, x_slots;
   int static_w;
   int stage_shift;  // log2 of the ring depth
+  int psleep;       // producer backs off with nanosleep while the ring is full
   int x_vec;  // A 16-byte aligned, lda and K multiples of 8: rows staged 8 values at a time
   int* err;
 };
@@ -108,11 +113,34 @@ __device__ __forceinline__ uint4 load_act8(const void* A, int dt, int64_t i) {
   }
 }
 
-// (1024 + q_lo, 64 + q_hi) of the byte at `sel` (0x4040: byte 0, 0x4141: byte 1) of w
-__device__ __forceinline__ __half2 nibble_pair(uint32_t w, uint32_t sel) {
-  const uint32_t x = __byte_perm(w, 0u, sel);
-  const uint32_t v = (x & 0x00F0000Fu) | 0x54006400u;
+// A constant the compiler keeps in a register (opaque to constant folding).
+__device__ __forceinline__ uint32_t opaque_u32(uint32_t v) {
+  uint32_t r;
+  asm volatile("mov.b32 %0, %1;" : "=r"(r) : "r"(v));
+  return r;
+}
+
+// (1024 + q_lo, 64 + q_hi) of the byte at `sel` (0x4040: byte 0, 0x4141: byte 1)
+// of w: one byte permute and one three-input logic op, (x & mask) | magic with
+// mask = 0x00F0000F and magic = 0x54006400 in registers.
+template <uint32_t SEL>
+__device__ __forceinline__ __half2 nibble_pair(uint32_t w, uint32_t mask, uint32_t magic) {
+  uint32_t v;
+  asm("{\n .reg .b32 t;\n prmt.b32 t, %1, 0, %2;\n lop3.b32 %0, t, %3, %4, 0xEA;\n}"
+      : "=r"(v)
+      : "r"(w), "n"(SEL), "r"(mask), "r"(magic));
   return *reinterpret_cast<const __half2*>(&v);
+}
+
+// fp16 pair (1152 + z, 1152 + z) of the signed zero byte z at `sel` of zz:
+// ((z, 0, z, 0) ^ flip) | magic with flip = 0x00800080, magic = 0x64006400.
+template <uint32_t SEL>
+__device__ __forceinline__ uint32_t zero_pair(uint32_t zz, uint32_t flip, uint32_t magic) {
+  uint32_t v;
+  asm("{\n .reg .b32 t;\n prmt.b32 t, %1, 0, %2;\n lop3.b32 %0, t, %3, %4, 0xBE;\n}"
+      : "=r"(v)
+      : "r"(zz), "n"(SEL), "r"(flip), "r"(magic));
+  return v;
 }
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
@@ -130,7 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + nst;
   const int XP = a.x_slots * 128 + 8;  // staged k per row, padded (bank spread)
   __half* xs = reinterpret_cast<__half*>(empty + nst);  // [MT][XP]
-  float* red = reinterpret_cast<float*>(xs + MT * XP);      // [2 sets][MT][128] this block's partials
+  float* red = reinterpret_cast<float*>(xs + MT * XP);      // [kSets][MT][128] this block's partials
   __shared__ int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -160,7 +188,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = blockIdx.y; tile < a.n_tiles && !stop; tile += gridDim.y) {
         for (int i = 0; i < nch; ++i, ++it) {
           const int s = it & (nst - 1);
-          if (it >= nst && !sgd::mbar_wait(&empty[s], ((it >> a.stage_shift) - 1) & 1, a.err)) {
+          // the ring is usually full: a sleeping poll keeps this warp's issue slots for the consumers
+          if (it >= nst && !(a.psleep ? sgd::mbar_wait_sleep(&empty[s], ((it >> a.stage_shift) - 1) & 1, a.err)
+                                      : sgd::mbar_wait(&empty[s], ((it >> a.stage_shift) - 1) & 1, a.err))) {
             s_abort = 1;
             stop = true;
             break;
@@ -221,6 +251,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // this lane's weight bytes in a stage: k-pair rows 8 st + t (+ 4), 16-byte column group cw (swizzled)
     const int wl0 = t * 128 + ((cw ^ t) << 4) + 2 * g, wl1 = (t + 4) * 128 + ((cw ^ (t + 4)) << 4) + 2 * g;
     float* myred = red + cp * MT * kTileCols;
+    const uint32_t kMaskW = opaque_u32(0x00F0000Fu), kMagicW = opaque_u32(0x54006400u);
+    const uint32_t kFlipZ = opaque_u32(0x00800080u), kMagicZ = opaque_u32(0x64006400u);
     bool dead = false;  // a wait of this warp ran out: skip the rest, keep to the barriers
     int it0 = 0;
     for (int tile = blockIdx.y; tile < a.n_tiles; tile += gridDim.y) {
@@ -229,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int n = 0; n < MT / 8; ++n)
 #pragma unroll
         for (int q = 0; q < 4; ++q) acc[n][q] = 0.f;
-      for (int i = (cp - it0) & 1; i < nch && !dead; i += 2) {
+      for (int i = ((cp - it0) % kSets + kSets) % kSets; i < nch && !dead; i += kSets) {
         const int it = it0 + i;
         const int s = it & (nst - 1);
         const bool ok = sgd::mbar_wait(&full[s], (it >> a.stage_shift) & 1, a.err);
@@ -252,8 +284,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             // zero byte z -> fp16 pair (1152 + z, 1152 + z) by bits, minus (120, 1080): (1032 + z, 72 + z), exact
             const uint32_t zz = *reinterpret_cast<const uint16_t*>(SZ + kSBytes + gi * 128 + c0);
             const __half2 bias = __halves2half2(__ushort_as_half(0x5780), __ushort_as_half(0x6438));  // 120, 1080
-            const uint32_t m0 = (__byte_perm(zz, 0u, 0x4040u) ^ 0x00800080u) | 0x64006400u;
-            const uint32_t m1 = (__byte_perm(zz, 0u, 0x4141u) ^ 0x00800080u) | 0x64006400u;
+            const uint32_t m0 = zero_pair<0x4040u>(zz, kFlipZ, kMagicZ);
+            const uint32_t m1 = zero_pair<0x4141u>(zz, kFlipZ, kMagicZ);
             off0 = __hsub2(*reinterpret_cast<const __half2*>(&m0), bias);
             off1 = __hsub2(*reinterpret_cast<const __half2*>(&m1), bias);
           } else {
@@ -284,10 +316,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int st = st0 + u;
               const uint32_t w0 = *reinterpret_cast<const uint16_t*>(W + st * 1024 + wl0);
               const uint32_t w1 = *reinterpret_cast<const uint16_t*>(W + st * 1024 + wl1);
-              const uint32_t a0 = h2_bits(__hmul2(__hsub2(nibble_pair(w0, 0x4040u), off0), sc0));
-              const uint32_t a1 = h2_bits(__hmul2(__hsub2(nibble_pair(w0, 0x4141u), off1), sc1));
-              const uint32_t a2 = h2_bits(__hmul2(__hsub2(nibble_pair(w1, 0x4040u), off0), sc0));
-              const uint32_t a3 = h2_bits(__hmul2(__hsub2(nibble_pair(w1, 0x4141u), off1), sc1));
+              const uint32_t a0 = h2_bits(__hmul2(__hsub2(nibble_pair<0x4040u>(w0, kMaskW, kMagicW), off0), sc0));
+              const uint32_t a1 = h2_bits(__hmul2(__hsub2(nibble_pair<0x4141u>(w0, kMaskW, kMagicW), off1), sc1));
+              const uint32_t a2 = h2_bits(__hmul2(__hsub2(nibble_pair<0x4040u>(w1, kMaskW, kMagicW), off0), sc0));
+              const uint32_t a3 = h2_bits(__hmul2(__hsub2(nibble_pair<0x4141u>(w1, kMaskW, kMagicW), off1), sc1));
 #pragma unroll
               for (int n = 0; n < MT / 8; ++n)
                 sgd::mma_f16_16816(acc[n], a0, a1, a2, a3, bx[MT == 16 ? 0 : u][n][0], bx[MT == 16 ? 0 : u][n][1]);
@@ -308,14 +340,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         myred[(m + 1) * kTileCols + c0 + 1] = acc[n][3];
       }
       if (!split) {
-        // both sets' partials of this tile, added in set order, go out coalesced
+        // the sets' partials of this tile, added in set order, go out coalesced
         asm volatile("bar.sync 2, %0;" ::"n"(kConsumerWarps * 32) : "memory");
         if (!s_abort) {
           for (int idx = threadIdx.x; idx < a.M * kTileCols; idx += kConsumerWarps * 32) {
             const int m = idx / kTileCols, cc = idx - m * kTileCols;
             const int col = tile * kTileCols + cc;
             if (col >= a.N) continue;
-            float v = red[idx] + red[MT * kTileCols + idx];
+            float v = red[idx];
+#pragma unroll
+            for (int q = 1; q < kSets; ++q) v += red[q * MT * kTileCols + idx];
             if (a.a_dt == SG_DT_I8) v *= a.scale_A;
             if (a.bias) v += __half2float(a.bias[col]);
             const int64_t o = (int64_t)m * a.ldc + col;
@@ -349,16 +383,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = idx / kTileCols, cc = idx - m * kTileCols;
       const int col = tile * kTileCols + cc;
       if (col >= a.N) continue;
-      float pv[8][2];
+      float pv[8][kSets];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        pv[q][0] = q < a.ksplit ? parts[q][idx] : 0.f;
-        pv[q][1] = q < a.ksplit ? parts[q][MT * kTileCols + idx] : 0.f;
-      }
+      for (int q = 0; q < 8; ++q)
+#pragma unroll
+        for (int c = 0; c < kSets; ++c) pv[q][c] = q < a.ksplit ? parts[q][c * MT * kTileCols + idx] : 0.f;
       float v = 0.f;
 #pragma unroll
       for (int q = 0; q < 8; ++q)
-        if (q < a.ksplit) v += pv[q][0] + pv[q][1];
+        if (q < a.ksplit) {
+          float t = pv[q][0];
+#pragma unroll
+          for (int c = 1; c < kSets; ++c) t += pv[q][c];
+          v += t;
+        }
       if (a.a_dt == SG_DT_I8) v *= a.scale_A;
       if (a.bias) v += __half2float(a.bias[col]);
       const int64_t o = (int64_t)m * a.ldc + col;
@@ -382,7 +420,7 @@ struct RPlan {
 
 size_t rows_smem(int mt, int x_slots, int stages) {
   return 1024 + (size_t)stages * kStageBytes + 2 * stages * 8 + (size_t)mt * (x_slots * 128 + 8) * 2 +
-         2 * (size_t)mt * kTileCols * 4;
+         (size_t)kSets * mt * kTileCols * 4;
 }
 
 // Blocks of this kernel (at the given shared memory, no cluster) resident per SM.
@@ -439,6 +477,7 @@ int rows_active_clusters(int k, size_t smem) {
 std::atomic<int> g_rows_enable{1};
 std::atomic<int> g_rows_max_tiles{1 << 30};  // widest output (in 128-column tiles) taken
 std::atomic<int> g_rows_stages{0};  // 0: deepest ring that fits
+std::atomic<int> g_rows_psleep{1};
 
 RPlan make_rplan(const SgMatMulParams* p, int sms) {
   RPlan pl;
@@ -495,6 +534,10 @@ namespace sg {
 bool w4_rows_tuning(std::string_view key, int value) {
   if (key == "w4_rows.enable") {
     g_rows_enable.store(value);
+    return true;
+  }
+  if (key == "w4_rows.producer_sleep") {
+    g_rows_psleep.store(value);
     return true;
   }
   if (key == "w4_rows.stages") {
@@ -563,6 +606,7 @@ SgStatus w4_rows_run(const SgMatMulParams* p, cudaStream_t cs, int sms, int* err
   a.x_slots = pl.x_slots;
   a.static_w = (p->flags & SG_MM_STATIC_WEIGHTS) ? 1 : 0;
   a.stage_shift = __builtin_ctz((unsigned)pl.stages);
+  a.psleep = g_rows_psleep.load() ? 1 : 0;
   a.x_vec = sg::aligned16(p->A) && a.lda % 8 == 0 && p->K % 8 == 0;
   a.err = err_word;
   using KFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, RArgs);
