@@ -1091,7 +1091,14 @@ def main():
                          "through the SDK (one session per GPU); decode_llama1b_tp: the same model "
                          "tensor-parallel over all GPUs; qwen7b_tp: Qwen-7B-shape 8192-token prefill + decode, "
                          "tensor-parallel over all GPUs")
+    ap.add_argument("--tuning", action="append", default=[], metavar="KEY=VALUE",
+                    help="kernel tuning knob (sg_set_tuning) applied before the run; repeatable")
     args = ap.parse_args()
+    if args.tuning:
+        from silicongraph_b200 import kernels
+        for kv in args.tuning:
+            key, _, val = kv.partition("=")
+            kernels.set_tuning(key, int(val))
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     _, _, world = rank_env()

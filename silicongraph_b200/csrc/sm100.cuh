@@ -332,6 +332,27 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// ---------------------------------------------- cluster shared-memory pushes
+// The shared::cluster address of `p` (this CTA's shared memory) in CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+// Asynchronous 16-byte store into another CTA's shared memory (addresses from
+// cluster_addr); its bytes complete_tx on that CTA's mbarrier `rbar`.
+__device__ __forceinline__ void st_async_v4(uint32_t raddr, float4 v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(raddr),
+               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(rbar)
+               : "memory");
+}
+__device__ __forceinline__ void st_async_u32(uint32_t raddr, uint32_t v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(raddr), "r"(v),
+               "r"(rbar)
+               : "memory");
+}
+
 // ldmatrix: four 8x8 b16 matrices; lane i gives the (16-byte aligned) address
 // of row i % 8 of matrix i / 8, and receives elements (i / 4, 2 (i % 4) + {0, 1})
 // of matrix j in register j.

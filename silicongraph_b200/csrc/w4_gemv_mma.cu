@@ -82,6 +82,7 @@ std::atomic<int> g_variant{0};
 std::atomic<int> g_sleep{0};
 std::atomic<int> g_cluster_mode{1};
 std::atomic<int> g_pair{1};  // allow two 8-warp blocks per SM
+std::atomic<int> g_strips{0};  // 0: any tile width; 1, 2, 4: only that many 128-column strips
 
 struct MArgs {
   const void* A;
@@ -158,7 +159,8 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS <= 8 ? 2 : 1)
   float* red = csum + (CLUSTER ? a.ksplit * kTC : 0);                // [seg][phase][kTC]
   __shared__ int s_last;
   __shared__ int s_abort;
-  __shared__ int s_aborts[16];  // cluster: rank r's abort flag, gathered in rank 0
+  __shared__ int s_aborts[16];  // cluster: rank r's abort flag, pushed to every rank
+  __shared__ __align__(8) uint64_t s_rbar;  // cluster: the other ranks' pushes have landed
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int strip = warp % STRIPS, phase = warp / STRIPS;
@@ -176,8 +178,18 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS <= 8 ? 2 : 1)
   const int nseg = CLUSTER ? 1 : (ce - 1) / a.cpt - t_first + 1;
   const int nslots = a.x_by_row ? a.cpt : ce - cs;
 
+  // cluster reduction: rank r owns columns [r * per, r * per + own) of the
+  // tile and receives the other ranks' partials of them (plus their abort
+  // flags) by st.async on s_rbar
+  const int per = CLUSTER ? ((kTC + a.ksplit - 1) / a.ksplit + 3) & ~3 : 1;
+  const int own_lo = CLUSTER ? min(kTC, (int)blockIdx.x * per) : 0;
+  const int own = CLUSTER ? min(kTC, own_lo + per) - own_lo : 0;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kWarps * kStages; ++i) sgd::mbar_init(&bars[i], 1);
+    if (CLUSTER && a.ksplit > 1) {
+      sgd::mbar_init(&s_rbar, 1);
+      sgd::mbar_arrive_expect_tx(&s_rbar, (uint32_t)((a.ksplit - 1) * (own * 4 + 4)));
+    }
     sgd::fence_mbar_init();
     s_abort = 0;
   }
@@ -383,33 +395,48 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS <= 8 ? 2 : 1)
   if (!CLUSTER && s_abort) return;
 
   if (CLUSTER) {
-    // Each rank's phase sum goes straight into rank 0's [rank][column]
-    // buffer; one cluster barrier publishes it, and rank 0 adds the ranks in
-    // order.  No block reads another's shared memory after the barrier.
-    namespace cg = cooperative_groups;
-    cg::cluster_group cluster = cg::this_cluster();
-    const int rank = (int)cluster.block_rank();
-    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
-    float* csum0 = cluster.map_shared_rank(csum, 0) + rank * kTC;
-    for (int cc = threadIdx.x; cc < kTC; cc += kThreads) {
-      float v = 0.f;
+    // Each rank adds its phases and pushes the sums of the columns that
+    // another rank owns straight into that rank's [rank][column] buffer with
+    // st.async (completion counted on the owner's s_rbar), keeps its own, and
+    // then adds the ranks' partials of its columns in rank order and stores
+    // them.  One-sided: no cluster-wide barrier after the pushes.
+    const int rank = blockIdx.x;  // cluster dims (ksplit, 1, 1): rank == blockIdx.x
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every rank has started
+    for (int c4 = threadIdx.x; c4 < kTC / 4; c4 += kThreads) {
+      const int cc = 4 * c4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int ph = 0; ph < kPhases; ++ph) v += red[ph * kTC + cc];
-      csum0[cc] = v;
+      for (int ph = 0; ph < kPhases; ++ph) {
+        const float4 r = *reinterpret_cast<const float4*>(&red[ph * kTC + cc]);
+        v.x += r.x;
+        v.y += r.y;
+        v.z += r.z;
+        v.w += r.w;
+      }
+      const int owner = cc / per;
+      if (owner == rank || a.ksplit == 1) {
+        *reinterpret_cast<float4*>(&csum[rank * kTC + cc]) = v;
+      } else {
+        sgd::st_async_v4(sgd::cluster_addr(&csum[rank * kTC + cc], owner), v, sgd::cluster_addr(&s_rbar, owner));
+      }
     }
-    if (threadIdx.x == 0) cluster.map_shared_rank(s_aborts, 0)[rank] = s_abort;
-    cluster.sync();
-    if (rank == 0) {
+    if (a.ksplit > 1 && threadIdx.x < a.ksplit && threadIdx.x != rank) {
+      const uint32_t q = threadIdx.x;
+      sgd::st_async_u32(sgd::cluster_addr(&s_aborts[rank], q), (uint32_t)s_abort, sgd::cluster_addr(&s_rbar, q));
+    }
+    int ok_wait = 1;
+    if (a.ksplit > 1) ok_wait = sgd::mbar_wait(&s_rbar, 0, a.err) ? 1 : 0;
+    __syncthreads();  // the local partial and (through s_rbar) the pushed ones are visible
+    int aborted = s_abort || !ok_wait;
+    for (int r = 0; r < a.ksplit; ++r)
+      if (r != rank) aborted |= s_aborts[r];
+    if (!aborted) {
       const int tile = blockIdx.y;
-      int aborted = 0;
-      for (int r = 0; r < a.ksplit; ++r) aborted |= s_aborts[r];
-      if (!aborted) {
-        for (int cc = threadIdx.x; cc < kTC; cc += kThreads) {
-          float v = 0.f;
-          for (int r = 0; r < a.ksplit; ++r) v += csum[r * kTC + cc];
-          const int col = tile * kTC + cc;
-          if (col < a.N) store_out(a.C, a.c_dt, col, finalize(a, col, v));
-        }
+      for (int cc = own_lo + threadIdx.x; cc < own_lo + own; cc += kThreads) {
+        float v = 0.f;
+        for (int r = 0; r < a.ksplit; ++r) v += csum[r * kTC + cc];
+        const int col = tile * kTC + cc;
+        if (col < a.N) store_out(a.C, a.c_dt, col, finalize(a, col, v));
       }
     }
     return;
@@ -535,6 +562,7 @@ MPlan make_mplan(const SgMatMulParams* p, int sms) {
       const int slots = sms * (pair ? 2 : 1);
       const int vv = pair ? kPairVariant : 0;
       for (int strips : {4, 2, 1}) {
+        if (g_strips.load() != 0 && strips != g_strips.load()) continue;
         const int n_tiles = (p->N + strips * 128 - 1) / (strips * 128);
         if (n_tiles > slots) continue;
         for (int k = std::min({8, pl.cpt, slots / n_tiles}); k >= 1; --k) {
@@ -555,7 +583,7 @@ MPlan make_mplan(const SgMatMulParams* p, int sms) {
     }
     if (mode == 1 && 2 * best_score < (long long)sms * 16) best_score = 0;
   }
-  pl.variant = std::min(3, std::max(0, g_variant.load()));
+  pl.variant = std::min(kPairVariant, std::max(0, g_variant.load()));
   if (best_score > 0) {
     pl.cluster = 1;
     pl.strips = best_strips;
@@ -754,6 +782,10 @@ bool w4_gemv_mma_tuning(std::string_view key, int value) {
   }
   if (key == "w4_gemv_mma.cluster") {
     g_cluster_mode.store(value);
+    return true;
+  }
+  if (key == "w4_gemv_mma.strips") {
+    g_strips.store(value);
     return true;
   }
   if (key == "w4_gemv_mma.pair") {
