@@ -872,7 +872,10 @@ def run_decode(args):
                      "achieved_basis": "(weights + KV cache of every sequence) bytes per step x steps/s, per GPU"},
         "e2e": {"value": round(seqs * tps, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 8},
-        "gpu_launches": steps * (10 * c["layers"] + 4),
+        # per layer: 2 rmsnorm, q|k|v, rope + KV append, attention, o, gate|up, down,
+        # SwiGLU unless fused into down (one sequence), 2 all-reduces (tensor-parallel);
+        # per step: embedding, final rmsnorm, LM head, greedy pick (2 kernels)
+        "gpu_launches": steps * (c["layers"] * (8 + (0 if args.batch == 1 else 1) + (2 if tp else 0)) + 5),
         "clocks": clk,
         "first_token": int(first),
     }

@@ -55,6 +55,13 @@ typedef enum {
                                    stream: the GEMV may start streaming them before
                                    it waits for that kernel (programmatic dependent
                                    launch); A is always read after the wait */
+#define SG_MM_A_SWIGLU 2u       /* A holds rows of [gate | up] (2K values each, row
+                                   stride lda >= 2K, fp16 or bf16): the GEMM consumes
+                                   silu(gate) * up rounded to A's type exactly as
+                                   sg_swiglu_rows writes it (the SwiGLU of
+                                   ops_swiglu, fused into the down projection).
+                                   INT4 only, on the one-row and 2..16-row
+                                   kernels; other shapes return SG_ERR_UNSUPPORTED */
 
 /*
  * Mirrors armcc::kernels::cpu::MatMulParams (matmul_neon.h:32-43).

@@ -53,6 +53,7 @@ class SgMatMulParams(ctypes.Structure):
 
 
 SG_MM_STATIC_WEIGHTS = 1
+SG_MM_A_SWIGLU = 2
 
 
 class SgFlashAttentionParams(ctypes.Structure):
@@ -112,6 +113,7 @@ _SIGS = {
                                     ctypes.c_int32, _P]),
     "sg_silu": (ctypes.c_int32, [_P, _P, ctypes.c_int64, ctypes.c_int32, _P]),
     "sg_silu_mul": (ctypes.c_int32, [_P, _P, _P, ctypes.c_int64, ctypes.c_int32, _P]),
+    "sg_swiglu_rows": (ctypes.c_int32, [_P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P]),
     "sg_softmax": (ctypes.c_int32, [_P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P]),
     "sg_rope": (ctypes.c_int32, [_P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P, ctypes.c_int32,
                                  ctypes.c_float, ctypes.c_int32, _P]),

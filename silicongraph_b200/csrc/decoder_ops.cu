@@ -70,9 +70,8 @@ __global__ void swiglu_rows_kernel(const T* __restrict__ gu, T* __restrict__ y, 
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
     const int j = (int)(e % F);
     const int64_t t = e / F;
-    const float g = (float)gu[t * 2 * F + j];
-    const float s = (float)(T)(g / (1.0f + expf(-g)));  // silu rounded as the reference's silu writes it
-    y[e] = (T)(s * (float)gu[t * 2 * F + F + j]);
+    // silu rounded as the reference's silu writes it, then the product
+    y[e] = sgd::swiglu_value<T>((float)gu[t * 2 * F + j], (float)gu[t * 2 * F + F + j]);
   }
 }
 

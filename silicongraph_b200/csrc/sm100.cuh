@@ -332,6 +332,14 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// SwiGLU of one element as the decoder writes it: silu(g) rounded to T, times
+// u, rounded to T (sg_swiglu_rows and the GEMMs that fuse it share this code).
+template <typename T>
+__device__ __forceinline__ T swiglu_value(float g, float u) {
+  const float s = (float)(T)(g / (1.0f + expf(-g)));
+  return (T)(s * u);
+}
+
 // ---------------------------------------------- cluster shared-memory pushes
 // The shared::cluster address of `p` (this CTA's shared memory) in CTA `rank`.
 __device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {

@@ -66,6 +66,7 @@ struct RArgs {
   int stage_shift;  // log2 of the ring depth
   int psleep;       // producer backs off with nanosleep while the ring is full
   int x_vec;  // A 16-byte aligned, lda and K multiples of 8: rows staged 8 values at a time
+  int swiglu; // A rows are [gate | up]: x = SwiGLU(A[m][k], A[m][K + k]) (SG_MM_A_SWIGLU)
   int* err;
 };
 
@@ -118,6 +119,40 @@ __device__ __forceinline__ uint32_t opaque_u32(uint32_t v) {
   uint32_t r;
   asm volatile("mov.b32 %0, %1;" : "=r"(r) : "r"(v));
   return r;
+}
+
+// SwiGLU of gate element i and up element i + K, rounded to A's type, as fp32.
+__device__ __forceinline__ float load_swiglu(const void* A, int dt, int64_t i, int K) {
+  if (dt == SG_DT_BF16) {
+    const __nv_bfloat16* p = static_cast<const __nv_bfloat16*>(A);
+    return __bfloat162float(sgd::swiglu_value<__nv_bfloat16>(__bfloat162float(p[i]), __bfloat162float(p[i + K])));
+  }
+  const __half* p = static_cast<const __half*>(A);
+  return __half2float(sgd::swiglu_value<__half>(__half2float(p[i]), __half2float(p[i + K])));
+}
+
+// 8 SwiGLU activations (fp16) from gate elements i.. and up elements i + K..; 16-byte aligned
+__device__ __forceinline__ uint4 load_swiglu8(const void* A, int dt, int64_t i, int K) {
+  uint4 o;
+  __half* oh = reinterpret_cast<__half*>(&o);
+  if (dt == SG_DT_BF16) {
+    const uint4 g = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(A) + i);
+    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(A) + i + K);
+    const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&g);
+    const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      oh[j] = __float2half_rn(__bfloat162float(
+          sgd::swiglu_value<__nv_bfloat16>(__bfloat162float(gb[j]), __bfloat162float(ub[j]))));
+  } else {
+    const uint4 g = *reinterpret_cast<const uint4*>(static_cast<const __half*>(A) + i);
+    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const __half*>(A) + i + K);
+    const __half* gh = reinterpret_cast<const __half*>(&g);
+    const __half* uh = reinterpret_cast<const __half*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) oh[j] = sgd::swiglu_value<__half>(__half2float(gh[j]), __half2float(uh[j]));
+  }
+  return o;
 }
 
 // (1024 + q_lo, 64 + q_hi) of the byte at `sel` (0x4040: byte 0, 0x4141: byte 1)
@@ -221,7 +256,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int idx = base + u * kT;
           const int m = idx / nv, k = cr0 * 128 + 8 * (idx - m * nv);
           v[u] = make_uint4(0u, 0u, 0u, 0u);
-          if (idx < total && m < a.M && k < a.K) v[u] = load_act8(a.A, a.a_dt, (int64_t)m * a.lda + k);
+          if (idx < total && m < a.M && k < a.K)
+            v[u] = a.swiglu ? load_swiglu8(a.A, a.a_dt, (int64_t)m * a.lda + k, a.K)
+                            : load_act8(a.A, a.a_dt, (int64_t)m * a.lda + k);
         }
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
@@ -236,7 +273,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int idx = threadIdx.x; idx < MT * span; idx += kConsumerWarps * 32) {
         const int m = idx / span, kk = idx - m * span;
         const int k = cr0 * 128 + kk;
-        const float v = (m < a.M && k < a.K) ? load_act(a.A, a.a_dt, (int64_t)m * a.lda + k) : 0.f;
+        const int64_t e = (int64_t)m * a.lda + k;
+        const float v = (m < a.M && k < a.K) ? (a.swiglu ? load_swiglu(a.A, a.a_dt, e, a.K) : load_act(a.A, a.a_dt, e))
+                                             : 0.f;
         xs[m * XP + kk] = __float2half_rn(v);
       }
     }
@@ -594,7 +633,8 @@ SgStatus w4_rows_run(const SgMatMulParams* p, cudaStream_t cs, int sms, int* err
   a.M = p->M;
   a.K = p->K;
   a.N = p->N;
-  a.lda = p->lda > 0 ? p->lda : p->K;
+  a.swiglu = (p->flags & SG_MM_A_SWIGLU) ? 1 : 0;
+  a.lda = p->lda > 0 ? p->lda : (a.swiglu ? 2 * p->K : p->K);
   a.ldc = p->ldc > 0 ? p->ldc : p->N;
   a.gs_shift = __builtin_ctz((unsigned)gs);
   a.a_dt = p->a_dtype == SG_DT_DEFAULT ? SG_DT_I8 : p->a_dtype;

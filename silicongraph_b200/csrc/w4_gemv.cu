@@ -316,6 +316,11 @@ SgStatus validate(const SgMatMulParams* p) {
   const int adt = p->a_dtype == SG_DT_DEFAULT ? SG_DT_I8 : p->a_dtype;
   const int cdt = p->c_dtype == SG_DT_DEFAULT ? SG_DT_F16 : p->c_dtype;
   SG_CHECK_ARG(adt >= SG_DT_F32 && adt <= SG_DT_I8, "sg_matmul_int4_grouped: bad a_dtype %d", p->a_dtype);
+  if (p->flags & SG_MM_A_SWIGLU) {
+    SG_CHECK_ARG(adt == SG_DT_F16 || adt == SG_DT_BF16, "sg_matmul_int4_grouped: SG_MM_A_SWIGLU needs fp16 or bf16 A");
+    SG_CHECK_ARG(p->lda <= 0 || p->lda >= 2 * p->K, "sg_matmul_int4_grouped: SG_MM_A_SWIGLU needs lda >= 2K (got %d)",
+                 p->lda);
+  }
   SG_CHECK_ARG(cdt == SG_DT_F32 || cdt == SG_DT_F16 || cdt == SG_DT_BF16,
                "sg_matmul_int4_grouped: bad c_dtype %d", p->c_dtype);
   return SG_OK;
@@ -387,6 +392,7 @@ bool w4_rows_tuning(std::string_view key, int value);
 bool gemm_tc_tuning(std::string_view key, int value);
 bool attn_tc_tuning(std::string_view key, int value);
 bool attn_tuning(std::string_view key, int value);
+bool sdk_tuning(std::string_view key, int value);
 }  // namespace sg
 
 // Core entry.  ws == NULL: library scratch (unless ws_external, then an error
@@ -432,9 +438,10 @@ static SgStatus w4_run(const SgMatMulParams* p, void* stream, void* ws, size_t w
     st = sg::w4_rows_run(p, cs, sms, err_word, &handled);
     if (handled || st != SG_OK) return st;
   }
+  const bool swiglu = (p->flags & SG_MM_A_SWIGLU) != 0;
   // Many activation rows: tcgen05 GEMM with the weights dequantized into TMEM (gemm_tc.cu).
   bool tc_ok = false;
-  const size_t tc_ws = path == 0 ? sg::gemm_tc_scratch_bytes(p, false, &tc_ok) : 0;
+  const size_t tc_ws = path == 0 && !swiglu ? sg::gemm_tc_scratch_bytes(p, false, &tc_ok) : 0;
   if (tc_ok) {
     if (ws == nullptr && tc_ws > 0) {
       if (ws_external) {
@@ -473,6 +480,11 @@ static SgStatus w4_run(const SgMatMulParams* p, void* stream, void* ws, size_t w
     bool handled = false;
     st = sg::w4_gemv_mma_run(p, cs, sms, ws, ws_bytes, err_word, &handled);
     if (handled || st != SG_OK) return st;
+  }
+  if (swiglu) {
+    sg::set_error("sg_matmul_int4_grouped: SG_MM_A_SWIGLU is fused only on the one-row and 2..16-row kernels "
+                  "(M=%d K=%d N=%d group %d)", p->M, p->K, p->N, p->group_size);
+    return SG_ERR_UNSUPPORTED;
   }
 
   Plan pl = make_plan(p, sms);
@@ -568,6 +580,7 @@ int32_t sg_set_tuning(const char* key, int32_t value) {
   if (key && sg::gemm_tc_tuning(std::string_view(key), value)) return SG_OK;
   if (key && sg::attn_tc_tuning(std::string_view(key), value)) return SG_OK;
   if (key && sg::attn_tuning(std::string_view(key), value)) return SG_OK;
+  if (key && sg::sdk_tuning(std::string_view(key), value)) return SG_OK;
   sg::set_error("sg_set_tuning: unknown key");
   return SG_ERR_NOT_FOUND;
 }

@@ -101,6 +101,7 @@ struct MArgs {
   int gs_shift;        // log2(gs) when gs is a power of two, else -1
   int sleep_wait;      // back off with nanosleep while waiting for a stage
   int static_w;        // weights may be requested before the dependency wait
+  int swiglu;          // A is [gate | up]: x = SwiGLU(A[k], A[K + k]) (SG_MM_A_SWIGLU)
   float* slots;        // [nblocks][2][512]: first / last segment partials
   unsigned* tickets;   // [n_tiles]
   int* err;
@@ -120,6 +121,20 @@ __device__ __forceinline__ float load_act(const void* A, int dt, int i) {
     case SG_DT_BF16: return __bfloat162float(static_cast<const __nv_bfloat16*>(A)[i]);
     default: return (float)static_cast<const int8_t*>(A)[i];
   }
+}
+
+// Activation k of the row: A[k], or with SG_MM_A_SWIGLU the SwiGLU of gate
+// A[k] and up A[K + k] rounded to A's type, as sg_swiglu_rows writes it.
+__device__ __forceinline__ float load_x(const MArgs& a, int k) {
+  if (a.swiglu) {
+    if (a.a_dt == SG_DT_BF16) {
+      const __nv_bfloat16* p = static_cast<const __nv_bfloat16*>(a.A);
+      return __bfloat162float(sgd::swiglu_value<__nv_bfloat16>(__bfloat162float(p[k]), __bfloat162float(p[a.K + k])));
+    }
+    const __half* p = static_cast<const __half*>(a.A);
+    return __half2float(sgd::swiglu_value<__half>(__half2float(p[k]), __half2float(p[a.K + k])));
+  }
+  return load_act(a.A, a.a_dt, k);
 }
 
 __device__ __forceinline__ void store_out(void* C, int dt, int64_t i, float v) {
@@ -248,8 +263,8 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS <= 8 ? 2 : 1)
     if (idx < nslots * kRows) {
       int k;
       slot_row(idx, k);
-      if (k < a.K) xe_pf[j] = load_act(a.A, a.a_dt, k);
-      if (k + 1 < a.K) xo_pf[j] = load_act(a.A, a.a_dt, k + 1);
+      if (k < a.K) xe_pf[j] = load_x(a, k);
+      if (k + 1 < a.K) xo_pf[j] = load_x(a, k + 1);
     }
   }
   if (!a.static_w && lane == 0) {
@@ -270,8 +285,8 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS <= 8 ? 2 : 1)
       xe = j == 0 ? xe_pf[0] : xe_pf[1];
       xo = j == 0 ? xo_pf[0] : xo_pf[1];
     } else {
-      xe = (k < a.K) ? load_act(a.A, a.a_dt, k) : 0.f;
-      xo = (k + 1 < a.K) ? load_act(a.A, a.a_dt, k + 1) : 0.f;
+      xe = (k < a.K) ? load_x(a, k) : 0.f;
+      xo = (k + 1 < a.K) ? load_x(a, k + 1) : 0.f;
     }
     float m = fmaxf(fabsf(xe), fabsf(xo));
 #pragma unroll
@@ -701,6 +716,7 @@ SgStatus w4_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, void
   a.gs_shift = ((gs & (gs - 1)) == 0) ? __builtin_ctz((unsigned)gs) : -1;
   a.sleep_wait = g_sleep.load() ? 1 : 0;
   a.static_w = (p->flags & SG_MM_STATIC_WEIGHTS) ? 1 : 0;
+  a.swiglu = (p->flags & SG_MM_A_SWIGLU) ? 1 : 0;
   a.tickets = static_cast<unsigned*>(ws);
   a.slots = reinterpret_cast<float*>(static_cast<char*>(ws) + pl.tickets_bytes);
   a.err = err_word;

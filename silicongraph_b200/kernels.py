@@ -90,6 +90,15 @@ def matmul_int4_grouped_workspace_size(A, B, scales, zeros, K, N, group_size, ou
     return int(_lib.load().sg_matmul_int4_grouped_workspace_size(ctypes.byref(p)))
 
 
+def swiglu_rows(gate_up: torch.Tensor, ffn: int, stream=None) -> torch.Tensor:
+    """[rows, 2 ffn] gate | up -> [rows, ffn] silu(gate) * up, each product rounded
+    as the decoder writes it (ops_swiglu)."""
+    rows = gate_up.shape[0]
+    y = torch.empty((rows, ffn), dtype=gate_up.dtype, device=gate_up.device)
+    check(_lib.load().sg_swiglu_rows(_ptr(gate_up), _ptr(y), rows, ffn, dtype_code(gate_up.dtype), _stream(stream)))
+    return y
+
+
 def set_tuning(key: str, value: int) -> None:
     check(_lib.load().sg_set_tuning(key.encode(), int(value)))
 

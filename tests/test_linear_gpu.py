@@ -411,3 +411,30 @@ def test_int4_few_rows_persistent(sg, oracle_mod, M, K, N, sym):
     C2 = sg.matmul_int4_grouped(*args, out_dtype=torch.float32)
     close(C.cpu().numpy(), want)
     assert torch.equal(C, C2)
+
+
+@pytest.mark.parametrize("M,dt", [(1, torch.float16), (2, torch.float16), (5, torch.float16), (16, torch.float16),
+                                  (1, torch.bfloat16), (4, torch.bfloat16)])
+def test_int4_swiglu_fused_matches_two_kernels(sg, oracle_mod, M, dt):
+    """SG_MM_A_SWIGLU: the down projection staging silu(gate) * up itself gives
+    the same bits as sg_swiglu_rows followed by the plain GEMM."""
+    from silicongraph_b200 import _lib
+    K, N, gs = 2048, 1024, 32
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=M + 40)
+    gu = torch.from_numpy(np.random.default_rng(M).standard_normal((M, 2 * K)).astype(np.float32) * 2).to(dt).to(DEV)
+    act = sg.swiglu_rows(gu, K)
+    want = sg.matmul_int4_grouped(act, t(B), t(S), t(Z), K, N, gs, out_dtype=torch.float32)
+    got = sg.matmul_int4_grouped(gu, t(B), t(S), t(Z), K, N, gs, out_dtype=torch.float32,
+                                 flags=_lib.SG_MM_A_SWIGLU)
+    assert torch.equal(got, want)
+
+
+def test_int4_swiglu_fused_refuses_many_rows(sg, oracle_mod):
+    """The fused SwiGLU exists on the few-row kernels only; a prefill-sized call
+    is refused with SG_ERR_UNSUPPORTED instead of computing something else."""
+    from silicongraph_b200 import _lib
+    K, N, gs = 256, 256, 32
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=3)
+    gu = torch.zeros((64, 2 * K), dtype=torch.float16, device=DEV)
+    with pytest.raises(Exception, match="SG_MM_A_SWIGLU"):
+        sg.matmul_int4_grouped(gu, t(B), t(S), t(Z), K, N, gs, flags=_lib.SG_MM_A_SWIGLU)
