@@ -65,6 +65,17 @@ __device__ __forceinline__ void st_io(void* p, int dt, int64_t i, float v) {
   }
 }
 
+// Keys per split.  With the position in device memory (a captured decode step
+// launched for the cache's capacity) the live keys are spread evenly over the
+// splits in whole 64-key tiles, so every split works whatever the position;
+// otherwise the host's split.
+__device__ __forceinline__ int split_keys(const AArgs& a, int q_pos0, int Skv) {
+  if (!a.q_pos_dev) return a.keys_per_split;
+  const int live = a.causal ? min(Skv, q_pos0 + a.Sq) : Skv;
+  const int per = (live + a.nsplit - 1) / a.nsplit;
+  return max(64, (per + 63) / 64 * 64);
+}
+
 template <int DPL>  // head-dim elements per lane (D <= 32 * DPL)
 __global__ void __launch_bounds__(kThreads) attn_cc_kernel(AArgs a) {
   extern __shared__ float sm[];
@@ -82,8 +93,9 @@ __global__ void __launch_bounds__(kThreads) attn_cc_kernel(AArgs a) {
   const int q_pos0 = a.q_pos_dev ? *a.q_pos_dev : a.q_pos0;
   const int Skv = a.q_pos_dev ? min(a.Skv, q_pos0 + a.Sq) : a.Skv;
   // key range of this split, clipped to what the causal mask lets any row see
-  int j0 = split * a.keys_per_split;
-  int j1 = min(Skv, j0 + a.keys_per_split);
+  const int kps = split_keys(a, q_pos0, Skv);
+  int j0 = split * kps;
+  int j1 = min(Skv, j0 + kps);
   if (a.causal) j1 = min(j1, q_pos0 + q0 + nq);  // last visible key + 1
   const int64_t kvbase = (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs;
 
@@ -205,8 +217,9 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(AArgs a) {
   const int nq = a.Sq, R = a.G * nq;  // row r: head hk*G + r / nq, query r % nq
   const int q_pos0 = a.q_pos_dev ? *a.q_pos_dev : a.q_pos0;
   const int Skv = a.q_pos_dev ? min(a.Skv, q_pos0 + a.Sq) : a.Skv;
-  const int j0 = split * a.keys_per_split;
-  int j1 = min(Skv, j0 + a.keys_per_split);
+  const int kps = split_keys(a, q_pos0, Skv);
+  const int j0 = split * kps;
+  int j1 = min(Skv, j0 + kps);
   if (a.causal) j1 = min(j1, q_pos0 + nq);
   const int64_t kvbase = (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs;
   const float qscale = a.scale * 1.4426950408889634f;
@@ -417,8 +430,9 @@ __global__ void __launch_bounds__(kThreads) attn_dec_cluster_kernel(AArgs a) {
 
   const int q_pos0 = a.q_pos_dev ? *a.q_pos_dev : a.q_pos0;
   const int Skv = a.q_pos_dev ? min(a.Skv, q_pos0 + a.Sq) : a.Skv;
-  const int j0 = split * a.keys_per_split;
-  int j1 = min(Skv, j0 + a.keys_per_split);
+  const int kps = split_keys(a, q_pos0, Skv);
+  const int j0 = split * kps;
+  int j1 = min(Skv, j0 + kps);
   if (a.causal) j1 = min(j1, q_pos0 + nq);
   const int64_t kvbase = (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs;
   const float qscale = a.scale * 1.4426950408889634f;
@@ -648,8 +662,9 @@ __global__ void __launch_bounds__(kDecMmaThreads) attn_dec_mma_kernel(AArgs a) {
   const int nq = a.Sq, R = a.G * nq;  // row r: head hk*G + r / nq, query r % nq
   const int q_pos0 = a.q_pos_dev ? *a.q_pos_dev : a.q_pos0;
   const int Skv = a.q_pos_dev ? min(a.Skv, q_pos0 + a.Sq) : a.Skv;
-  const int j0 = split * a.keys_per_split;
-  int j1 = min(Skv, j0 + a.keys_per_split);
+  const int kps = split_keys(a, q_pos0, Skv);
+  const int j0 = split * kps;
+  int j1 = min(Skv, j0 + kps);
   if (a.causal) j1 = min(j1, q_pos0 + nq);
   const int64_t kvbase = (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs;
   const int kk = tid >> 2, part = tid & 3;  // loader role: quarter `part` of key kk
@@ -832,7 +847,260 @@ __global__ void __launch_bounds__(kDecMmaThreads) attn_dec_mma_kernel(AArgs a) {
   }
 }
 
-std::atomic<int> g_decode_kernel{3};  // decode kernel: 3 tensor-core cluster, 1 CUDA-core cluster, 2 key-parallel + combine, 0 generic
+// ---------------------------------------------------------------------------
+// Decode attention with the key range split over the warps (flash-decoding
+// inside the block).  One block per (key split, kv head, batch), a cluster of
+// the splits as in attn_dec_mma_kernel, but no block barrier per tile:
+//   * warp w takes the 16-key groups w, w + 8, w + 16, ... of the block's range
+//     and streams each group's K and V rows through its own cp.async ring;
+//   * S = Q K^T (mma.sync m16n8k16, two 8-key n-tiles) stays in registers; the
+//     warp keeps its own running max, sum and O for the 16 (padded) rows; the
+//     score fragment is already the A fragment of O += P V (keys as k), V
+//     fragments by ldmatrix.trans;
+//   * at the end the 8 warps' (max, sum, O) are merged in shared memory in
+//     warp order, and the block's result goes to rank 0 of the cluster, which
+//     merges the splits in rank order (as attn_dec_mma_kernel).
+constexpr int kDecWarpThreads = 256;
+constexpr int kDecWarpGroup = 16;  // keys per warp step
+
+template <int D>
+constexpr int dec_warp_stages() { return 2; }  // groups in flight per warp
+
+inline size_t dec_warp_smem(int D, int R, int nsplit) {
+  const int st = dec_warp_stages<64>();
+  const size_t ring = (size_t)8 * st * 2 * kDecWarpGroup * (D + 8) * 2;  // [warp][stage][K | V][16][D + 8] fp16
+  const size_t merge = (size_t)8 * kDecMmaRows * (D + 2) * 4;           // [warp][16][D + 2] fp32
+  return std::max(ring, merge) + sizeof(float) * (size_t)nsplit * R * (D + 2);
+}
+
+template <int D, int IO>
+__global__ void __launch_bounds__(kDecWarpThreads) attn_dec_warp_kernel(AArgs a) {
+  namespace cg = cooperative_groups;
+  constexpr int KG = kDecWarpGroup, KP = D + 8;  // padded row (halves)
+  constexpr int kW = kDecWarpThreads / 32;
+  constexpr int ST = dec_warp_stages<D>();
+  constexpr int NP = KG * D / 8 / 32;  // 16-byte pieces per lane per group (K, and V)
+  constexpr int NT = D / 8;            // n-tiles of O
+  extern __shared__ __align__(16) uint8_t smb[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  __half* ring = reinterpret_cast<__half*>(smb) + (size_t)warp * ST * 2 * KG * KP;  // this warp's [stage][K | V][KG][KP]
+  const size_t main_bytes = std::max((size_t)kW * ST * 2 * KG * KP * 2, (size_t)kW * kDecMmaRows * (D + 2) * 4);
+  float* wm = reinterpret_cast<float*>(smb);                  // after the loop: [warp][16][D + 2]
+  float* comb = reinterpret_cast<float*>(smb + main_bytes);  // rank 0: [rank][R][D + 2]
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  sgd::pdl_wait();  // the newest key and the queries come from the previous kernel
+  sgd::pdl_launch_dependents();
+
+  const int b = blockIdx.z, hk = blockIdx.y, split = blockIdx.x;
+  const int nq = a.Sq, R = a.G * nq;  // row r: head hk*G + r / nq, query r % nq
+  const int q_pos0 = a.q_pos_dev ? *a.q_pos_dev : a.q_pos0;
+  const int Skv = a.q_pos_dev ? min(a.Skv, q_pos0 + a.Sq) : a.Skv;
+  const int kps = split_keys(a, q_pos0, Skv);
+  const int j0 = split * kps;
+  int j1 = min(Skv, j0 + kps);
+  if (a.causal) j1 = min(j1, q_pos0 + nq);
+  const int64_t kvbase = (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs;
+  const int ngroups = j1 > j0 ? (j1 - j0 + KG - 1) / KG : 0;
+  const int nmine = ngroups > warp ? (ngroups - warp + kW - 1) / kW : 0;  // groups warp, warp + kW, ...
+
+  // lane's pieces of group i (the warp's i-th) into stage i % ST; zeros past the last key
+  auto issue = [&](int i) {
+    const int key0 = j0 + (warp + kW * i) * KG;
+    __half* kd = ring + (size_t)(i % ST) * 2 * KG * KP;
+    __half* vd = kd + KG * KP;
+#pragma unroll
+    for (int u = 0; u < NP; ++u) {
+      const int pc = lane + 32 * u;
+      const int kl = pc / (D / 8), part = pc % (D / 8);
+      const int key = key0 + kl;
+      const bool live = key < j1;
+      const int64_t e0 = kvbase + (int64_t)(live ? key : j0) * D + part * 8;
+      sgd::cp_async_16(kd + kl * KP + part * 8, static_cast<const uint16_t*>(a.K) + e0, live);
+      sgd::cp_async_16(vd + kl * KP + part * 8, static_cast<const uint16_t*>(a.V) + e0, live);
+    }
+  };
+  for (int i = 0; i < ST - 1; ++i) {
+    if (i < nmine) issue(i);
+    sgd::cp_async_commit();
+  }
+
+  // Q fragments (A of S = Q K^T), prescaled by scale * log2(e); rows >= R are zero.
+  const float qscale = a.scale * 1.4426950408889634f;
+  auto q_at = [&](int r, int d) -> float {
+    if (r >= R) return 0.f;
+    const int h = hk * a.G + r / nq, qi = r % nq;
+    return ld_io(a.Q, a.io_dt, (((int64_t)b * a.H + h) * a.Sq + qi) * D + d) * qscale;
+  };
+  uint32_t qf[D / 16][4];
+#pragma unroll
+  for (int s2 = 0; s2 < D / 16; ++s2) {
+    const int d0 = 16 * s2 + 2 * t;
+    qf[s2][0] = pack_half2(q_at(g, d0), q_at(g, d0 + 1));
+    qf[s2][1] = pack_half2(q_at(g + 8, d0), q_at(g + 8, d0 + 1));
+    qf[s2][2] = pack_half2(q_at(g, d0 + 8), q_at(g, d0 + 9));
+    qf[s2][3] = pack_half2(q_at(g + 8, d0 + 8), q_at(g + 8, d0 + 9));
+  }
+  float o[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) o[n][q] = 0.f;
+  float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;  // rows g and g + 8
+  const int r_lo = g, r_hi = g + 8;
+  const int qlo = r_lo % nq, qhi = r_hi % nq;
+
+  for (int i = 0; i < nmine; ++i) {
+    sgd::cp_async_wait<ST - 2>();  // this lane's pieces of group i have landed
+    __half* ks = ring + (size_t)(i % ST) * 2 * KG * KP;
+    __half* vs = ks + KG * KP;
+    if (IO == SG_DT_BF16) {  // this lane's own pieces, bf16 -> fp16 in place
+#pragma unroll
+      for (int u = 0; u < NP; ++u) {
+        const int pc = lane + 32 * u;
+        const int kl = pc / (D / 8), part = pc % (D / 8);
+        uint4* kq = reinterpret_cast<uint4*>(ks + kl * KP + part * 8);
+        uint4* vq = reinterpret_cast<uint4*>(vs + kl * KP + part * 8);
+        *kq = to_f16x8<IO>(*kq);
+        *vq = to_f16x8<IO>(*vq);
+      }
+    }
+    __syncwarp();  // the group is in for every lane; group i - 1's stage is free
+    if (i + ST - 1 < nmine) issue(i + ST - 1);
+    sgd::cp_async_commit();
+    const int key0 = j0 + (warp + kW * i) * KG;
+    // ---- S = Q K^T: n-tile h covers keys key0 + 8h .. + 7
+    float sc[2][4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) sc[h][q] = 0.f;
+      const __half* krow = ks + (8 * h + g) * KP + 2 * t;
+#pragma unroll
+      for (int s2 = 0; s2 < D / 16; ++s2) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow + 16 * s2);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(krow + 16 * s2 + 8);
+        sgd::mma_f16_16816(sc[h], qf[s2][0], qf[s2][1], qf[s2][2], qf[s2][3], b0, b1);
+      }
+    }
+    // mask: keys past the range or (causal) past the row's query position
+    float mx_lo = -INFINITY, mx_hi = -INFINITY;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int key = key0 + 8 * h + 2 * t + (q & 1);
+        const int qi = q < 2 ? qlo : qhi;
+        const bool vis = key < j1 && (!a.causal || key <= q_pos0 + qi);
+        sc[h][q] = vis ? sc[h][q] : -INFINITY;
+        if (q < 2) mx_lo = fmaxf(mx_lo, sc[h][q]);
+        else mx_hi = fmaxf(mx_hi, sc[h][q]);
+      }
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, off));
+      mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, off));
+    }
+    const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
+    const float al_lo = m_lo == -INFINITY ? 0.f : exp2f(m_lo - mn_lo);
+    const float al_hi = m_hi == -INFINITY ? 0.f : exp2f(m_hi - mn_hi);
+    float p[2][4], s_lo = 0.f, s_hi = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float mn = q < 2 ? mn_lo : mn_hi;
+        p[h][q] = mn == -INFINITY ? 0.f : exp2f(sc[h][q] - mn);
+        if (q < 2) s_lo += p[h][q];
+        else s_hi += p[h][q];
+      }
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      s_lo += __shfl_xor_sync(0xffffffffu, s_lo, off);
+      s_hi += __shfl_xor_sync(0xffffffffu, s_hi, off);
+    }
+    m_lo = mn_lo;
+    m_hi = mn_hi;
+    l_lo = l_lo * al_lo + s_lo;
+    l_hi = l_hi * al_hi + s_hi;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      o[n][0] *= al_lo;
+      o[n][1] *= al_lo;
+      o[n][2] *= al_hi;
+      o[n][3] *= al_hi;
+    }
+    // ---- O += P V: P [16 rows x 16 keys] as the A fragment straight from the scores
+    const uint32_t pa0 = pack_half2(p[0][0], p[0][1]), pa1 = pack_half2(p[0][2], p[0][3]);
+    const uint32_t pa2 = pack_half2(p[1][0], p[1][1]), pa3 = pack_half2(p[1][2], p[1][3]);
+    const __half* vrow = vs + (lane & 15) * KP;  // ldmatrix rows: keys 0-15
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      uint32_t b0, b1;
+      ldmatrix_x2_trans(b0, b1, vrow + 8 * n);
+      sgd::mma_f16_16816(o[n], pa0, pa1, pa2, pa3, b0, b1);
+    }
+  }
+  sgd::cp_async_wait<0>();
+  __syncthreads();  // every warp is done with its ring: the merge buffer reuses it
+
+  // ---- the warps' partials into [warp][row][D + 2]: O, then max, sum
+  float* mine = wm + (size_t)warp * kDecMmaRows * (D + 2);
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    const int d = 8 * n + 2 * t;
+    mine[r_lo * (D + 2) + d] = o[n][0];
+    mine[r_lo * (D + 2) + d + 1] = o[n][1];
+    mine[r_hi * (D + 2) + d] = o[n][2];
+    mine[r_hi * (D + 2) + d + 1] = o[n][3];
+  }
+  if (t == 0) {
+    mine[r_lo * (D + 2) + D] = m_lo;
+    mine[r_lo * (D + 2) + D + 1] = l_lo;
+    mine[r_hi * (D + 2) + D] = m_hi;
+    mine[r_hi * (D + 2) + D + 1] = l_hi;
+  }
+  __syncthreads();
+  // ---- block merge (warp order) straight into rank 0's [split][row][D + 2]
+  cg::cluster_group cluster = cg::this_cluster();
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+  float* dst = cluster.map_shared_rank(comb, 0) + (size_t)split * R * (D + 2);
+  for (int i = tid; i < R * (D + 2); i += kDecWarpThreads) {
+    const int r = i / (D + 2), d = i % (D + 2);
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kW; ++w) M = fmaxf(M, wm[((size_t)w * kDecMmaRows + r) * (D + 2) + D]);
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kW; ++w) {
+      const float* pr = wm + ((size_t)w * kDecMmaRows + r) * (D + 2);
+      if (pr[D] == -INFINITY) continue;
+      const float wt = exp2f(pr[D] - M);
+      acc = fmaf(d == D ? 0.f : (d == D + 1 ? pr[D + 1] : pr[d]), wt, acc);
+    }
+    dst[i] = d == D ? M : acc;
+  }
+  cluster.sync();
+  if (split != 0) return;
+  const int nsplit = a.nsplit;
+  for (int i = tid; i < R * D; i += kDecWarpThreads) {
+    const int r = i / D, d = i % D;
+    float M = -INFINITY;
+    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, comb[((size_t)sp * R + r) * (D + 2) + D]);
+    float L = 0.f, acc = 0.f;
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float* pr = comb + ((size_t)sp * R + r) * (D + 2);
+      if (pr[D] == -INFINITY) continue;
+      const float wt = exp2f(pr[D] - M);
+      L = fmaf(pr[D + 1], wt, L);
+      acc = fmaf(pr[d], wt, acc);
+    }
+    const int h = hk * a.G + r / nq, qi = r % nq;
+    st_io(a.O, a.io_dt, (((int64_t)b * a.H + h) * a.Sq + qi) * D + d, L > 0.f ? acc / L : 0.f);
+  }
+}
+
+std::atomic<int> g_decode_kernel{4};  // decode kernel: 4 warp-split tensor-core cluster, 3 tensor-core cluster, 1 CUDA-core cluster, 2 key-parallel + combine, 0 generic
 std::atomic<int> g_decode_cluster_max{kDecClusterMax};  // largest cluster of key splits
 
 }  // namespace
@@ -934,8 +1202,50 @@ SgStatus attn_cc_run(const SgFlashAttentionParams* p, void* stream, int want_spl
   const int eb = a.io_dt == SG_DT_F32 ? 4 : 2;
   const bool vec_ok = aligned16(a.K) && aligned16(a.V) && (a.kv_hs * eb) % 16 == 0 && (a.kv_bs * eb) % 16 == 0;
   const int mode = g_decode_kernel.load();
-  const bool use_mma = mode == 3 && eb == 2 && (a.D == 64 || a.D == 128) && R <= kDecMmaRows && vec_ok;
-  const bool use_cl = (mode == 3 || mode == 1) && (a.D == 64 || (a.D == 128 && eb == 2)) && R <= kDecRows && vec_ok;
+  const bool use_warp = mode == 4 && eb == 2 && (a.D == 64 || a.D == 128) && R <= kDecMmaRows && vec_ok;
+  if (use_warp) {
+    // splits: as many as the capacity of one wave allows (blocks per SM from shared memory)
+    const int tiles = (a.Skv + kDecTile - 1) / kDecTile;
+    const int items = a.Hkv * a.B;
+    int cmax = std::max(1, std::min(kDecClusterMax, g_decode_cluster_max.load()));
+    while (cmax > 1 && dec_warp_smem(a.D, R, cmax) > 200 * 1024) --cmax;  // rank 0 holds every split's rows
+    void (*kfn)(AArgs) = a.D == 64 ? (a.io_dt == SG_DT_BF16 ? attn_dec_warp_kernel<64, SG_DT_BF16>
+                                                            : attn_dec_warp_kernel<64, SG_DT_F16>)
+                                   : (a.io_dt == SG_DT_BF16 ? attn_dec_warp_kernel<128, SG_DT_BF16>
+                                                            : attn_dec_warp_kernel<128, SG_DT_F16>);
+    const size_t smem_max = dec_warp_smem(a.D, R, cmax);
+    SG_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_max));
+    int per_sm = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kDecWarpThreads, smem_max) != cudaSuccess) {
+      cudaGetLastError();
+      per_sm = 1;
+    }
+    const int ns = std::max(1, std::min({cmax, tiles, (std::max(1, per_sm) * sms) / items}));
+    const int tiles_per = (tiles + ns - 1) / ns;
+    a.keys_per_split = tiles_per * kDecTile;
+    a.nsplit = (tiles + tiles_per - 1) / tiles_per;
+    const size_t smem = dec_warp_smem(a.D, R, a.nsplit);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.nsplit, a.Hkv, a.B);
+    cfg.blockDim = dim3(kDecWarpThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = cs;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = a.nsplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    if (a.nsplit > 8) SG_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    SG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kfn, a));
+    return SG_OK;
+  }
+  const bool use_mma = (mode == 3 || mode == 4) && eb == 2 && (a.D == 64 || a.D == 128) && R <= kDecMmaRows && vec_ok;
+  const bool use_cl = (mode == 4 || mode == 3 || mode == 1) && (a.D == 64 || (a.D == 128 && eb == 2)) && R <= kDecRows &&
+                      vec_ok;
   if (use_mma || use_cl) {
     auto smem_of = [&](int ns) { return use_mma ? dec_mma_smem(a.D, R, ns) : dec_cluster_smem(a.D, R, ns); };
     const int tiles = (a.Skv + kDecTile - 1) / kDecTile;

@@ -105,9 +105,12 @@ def set_tuning(key: str, value: int) -> None:
 
 def flash_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, *, causal: bool = True, scale: float = 0.0,
                     q_pos0: int = 0, decode: bool = False, O: torch.Tensor | None = None, stream=None,
-                    kv_len: int | None = None, workspace=None) -> torch.Tensor:
+                    kv_len: int | None = None, workspace=None, q_pos_device: torch.Tensor | None = None
+                    ) -> torch.Tensor:
     """Q [B,H,Sq,D], K/V [B,Hkv,Smax,D] (only the first kv_len rows are used) --
-    flash_attention_fp16 (flash_attention.h:95-144) on the GPU."""
+    flash_attention_fp16 (flash_attention.h:95-144) on the GPU.  With q_pos_device
+    (an int32 device scalar) the position of query 0 is read on the device and the
+    keys used are min(kv_len, position + Sq), as a captured decode step does."""
     from ._lib import SgFlashAttentionParams
     Bn, H, Sq, D = Q.shape
     Hkv, Smax = K.shape[1], K.shape[2]
@@ -123,6 +126,8 @@ def flash_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, *, causal
     p.q_pos0 = q_pos0
     p.kv_head_stride = K.stride(1)
     p.kv_batch_stride = K.stride(0)
+    if q_pos_device is not None:
+        p.q_pos_device = _ptr(q_pos_device)
     if workspace is not None:
         p.workspace = _ptr(workspace)
         p.workspace_bytes = workspace.numel() * workspace.element_size()

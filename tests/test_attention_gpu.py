@@ -67,7 +67,8 @@ def test_attention_vs_oracle(sg, oracle_mod, dtype, B, H, Hkv, S, D, causal):
     close(got, want)
 
 
-@pytest.mark.parametrize("kernel", [3, 1, 2, 0], ids=["tensor-core-cluster", "cluster", "key-parallel", "generic"])
+@pytest.mark.parametrize("kernel", [4, 3, 1, 2, 0],
+                         ids=["warp-split", "tensor-core-cluster", "cluster", "key-parallel", "generic"])
 @pytest.mark.parametrize("Skv,Sq,H,Hkv,D", [(768, 1, 32, 8, 64), (4096, 1, 28, 4, 128), (1000, 3, 8, 8, 64),
                                             (64, 1, 4, 2, 32), (8192, 1, 28, 4, 128), (37, 2, 16, 2, 64),
                                             (300, 4, 28, 4, 128)])
@@ -88,7 +89,7 @@ def test_decode_against_kv_cache(sg, oracle_mod, kernel, Skv, Sq, H, Hkv, D):
         got = sg.flash_attention(dev(q), dev(kc), dev(vc), causal=True, q_pos0=-1, decode=True, kv_len=Skv)
         got2 = sg.flash_attention(dev(q), dev(kc), dev(vc), causal=True, q_pos0=-1, decode=True, kv_len=Skv)
     finally:
-        sg.set_tuning("attn.decode_kernel", 3)
+        sg.set_tuning("attn.decode_kernel", 4)
     close(got.float().cpu().numpy(), want)
     assert torch.equal(got, got2)
 
@@ -153,3 +154,46 @@ def test_library_scratch_shared_safely_between_kernels(sg, oracle_mod):
             close(o.float().cpu().numpy(), want_a)
     finally:
         sg.set_tuning("w4_gemv_mma.cluster", 1)
+
+
+@pytest.mark.parametrize("kernel", [4, 3, 1, 2, 0])
+@pytest.mark.parametrize("B,pos", [(1, 0), (1, 63), (1, 600), (1, 1500), (16, 600), (4, 2046)])
+def test_decode_position_on_device(sg, oracle_mod, kernel, B, pos):
+    """A captured decode step launches for the cache's capacity and reads the
+    position from device memory: the live keys are spread over the splits at run
+    time.  Every kernel matches the oracle on the live prefix at short, long and
+    tile-boundary positions, with one and with many sequences."""
+    rng = np.random.default_rng(pos + B)
+    cap, H, Hkv, D = 2048, 32, 8, 64
+    q = rng.standard_normal((B, H, 1, D)).astype(np.float16)
+    kc = rng.standard_normal((B, Hkv, cap, D)).astype(np.float16)
+    vc = rng.standard_normal((B, Hkv, cap, D)).astype(np.float16)
+    n = pos + 1
+    want = oracle_mod.flash_attention(q, np.ascontiguousarray(kc[:, :, :n]), np.ascontiguousarray(vc[:, :, :n]),
+                                      causal=True, q_pos0=pos).astype(np.float32)
+    p = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    try:
+        sg.set_tuning("attn.decode_kernel", kernel)
+        got = sg.flash_attention(dev(q), dev(kc), dev(vc), causal=True, decode=True, kv_len=cap, q_pos_device=p)
+    finally:
+        sg.set_tuning("attn.decode_kernel", 4)
+    close(got.float().cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("D,H,Hkv", [(64, 32, 8), (128, 28, 4)])
+def test_decode_warp_split_bf16(sg, oracle_mod, D, H, Hkv):
+    """bf16 KV caches on the warp-split kernel (fp16 inside), GQA 4 and 7."""
+    rng = np.random.default_rng(D)
+    Skv = 1000
+    q = rng.standard_normal((2, H, 1, D)).astype(np.float32)
+    kc = rng.standard_normal((2, Hkv, Skv, D)).astype(np.float32)
+    vc = rng.standard_normal((2, Hkv, Skv, D)).astype(np.float32)
+    q, kc, vc = (oracle_mod.bf16_bits_to_f32(oracle_mod.f32_to_bf16_bits(a)) for a in (q, kc, vc))
+    want = oracle_mod.flash_attention(q, kc, vc, causal=True, q_pos0=Skv - 1)
+    t = lambda a: torch.from_numpy(a).cuda().to(torch.bfloat16)  # noqa: E731
+    try:
+        sg.set_tuning("attn.decode_kernel", 4)
+        got = sg.flash_attention(t(q), t(kc), t(vc), causal=True, q_pos0=-1, decode=True)
+    finally:
+        sg.set_tuning("attn.decode_kernel", 4)
+    close(got.float().cpu().numpy(), want)
