@@ -81,3 +81,42 @@ def test_no_cpu_fallback_without_device(lib):
     p.M, p.K, p.N, p.group_size = 1, 32, 16, 32
     assert lib.sg_matmul_int4_grouped(ctypes.byref(p), None) == SG_ERR_RUNTIME
     assert b"no CUDA device" in lib.sg_last_error()
+
+
+def test_flag_values_match_header():
+    """The Python binding's SG_MM_* flag values are the header's."""
+    from silicongraph_b200 import _lib
+    src = open(os.path.join(ROOT, "include", "sg_kernels.h")).read()
+    for name in ("SG_MM_STATIC_WEIGHTS", "SG_MM_A_SWIGLU"):
+        m = re.search(rf"#define {name} (\d+)u", src)
+        assert m, name
+        assert int(m.group(1)) == getattr(_lib, name)
+
+
+@pytest.mark.parametrize("key,value", [
+    ("w4_rows.enable", 1), ("w4_rows.stages", 0), ("w4_rows.producer_sleep", 1), ("w4_rows.max_tiles", 1 << 30),
+    ("w4_gemv_mma.strips", 0), ("w4_gemv_mma.variant", 0), ("attn.decode_kernel", 4), ("sdk.fuse_swiglu", 1),
+])
+def test_tuning_keys_known(lib, key, value):
+    """Every tuning knob the kernels and the SDK read is reachable through
+    sg_set_tuning (host-only; the values set are the defaults)."""
+    from silicongraph_b200._lib import SG_OK
+    assert lib.sg_set_tuning(key.encode(), value) == SG_OK
+
+
+def test_swiglu_flag_argument_checks(lib):
+    """SG_MM_A_SWIGLU is refused for int8 / fp32 activations and for an lda
+    shorter than the gate | up row, before any device work."""
+    from silicongraph_b200._lib import SG_DT_F32, SG_ERR_INVALID, SG_MM_A_SWIGLU, SgMatMulParams
+    buf = (ctypes.c_uint8 * 4096)()
+    p = SgMatMulParams()
+    p.A = p.B = p.C = p.scales_B = ctypes.addressof(buf)
+    p.M, p.K, p.N, p.group_size = 1, 64, 16, 32
+    p.flags = SG_MM_A_SWIGLU
+    p.a_dtype = SG_DT_F32
+    assert lib.sg_matmul_int4_grouped(ctypes.byref(p), None) == SG_ERR_INVALID
+    assert b"SG_MM_A_SWIGLU" in lib.sg_last_error()
+    p.a_dtype = 2  # fp16
+    p.lda = 64     # < 2K
+    assert lib.sg_matmul_int4_grouped(ctypes.byref(p), None) == SG_ERR_INVALID
+    assert b"lda" in lib.sg_last_error()
