@@ -895,7 +895,8 @@ QWEN_GS = 128
 QWEN_PROMPT = 8192
 QWEN_WORKLOAD = ("Qwen2.5-7B-shape decoder through the armcc SDK, tensor-parallel over all ranks: 28 layers, "
                  "hidden 3584, 28/4 heads, head_dim 128, SwiGLU 18944, vocab 152064, INT4 group-128 weights "
-                 "(lm_head included); one 8192-token prefill of random ids, then greedy decode, batch 1")
+                 "(lm_head included); an 8192-token prefill of random ids per sequence, then greedy decode "
+                 "of every sequence in lockstep (--batch sequences, 32 in the configuration)")
 
 
 def run_qwen(args):
@@ -916,7 +917,11 @@ def run_qwen(args):
     cfg = armpack.llama_config(layers=c["layers"], hidden=c["hidden"], heads=c["heads"], kv_heads=c["kv_heads"],
                                head_dim=c["head_dim"], ffn=c["ffn"], vocab=c["vocab"], rope_theta=c["rope_theta"])
     steps = args.steps
+    B = args.batch
     ctx = QWEN_PROMPT + steps + args.warmup + 8
+    # prompt chunk per forward pass: the whole prompt for one sequence; about 32 K tokens per
+    # pass when batched (the activation buffers scale with sequences x chunk)
+    chunk = QWEN_PROMPT if B == 1 else max(256, (32768 // B) // 256 * 256)
     # one package on the host's disk, written by rank 0, read by every rank
     root = os.environ.get("SG_BENCH_TMP", "/tmp")
     pkg_path = [os.path.join(root, f"sg_qwen7b_{os.getpid()}") if rank == 0 else None]
@@ -928,7 +933,7 @@ def run_qwen(args):
     try:
         if rank == 0:
             weight_bytes, _ = build_decode_package(pkg_path, cfg, seed=21, gs=QWEN_GS, max_context=ctx,
-                                                   max_prefill_chunk=QWEN_PROMPT,
+                                                   max_prefill_chunk=chunk,
                                                    model_id="synthetic/qwen2.5-7b-shape")
             torch.cuda.empty_cache()
         else:
@@ -937,23 +942,27 @@ def run_qwen(args):
             wb = [weight_bytes]
             dist.broadcast_object_list(wb, src=0)
             weight_bytes = wb[0]
-        prompt = np.random.default_rng(6).integers(0, c["vocab"], QWEN_PROMPT).astype(np.int32)
+        prompt = np.random.default_rng(6).integers(0, c["vocab"], (B, QWEN_PROMPT)).astype(np.int32)
         with sdk.Package(pkg_path) as pkg:
             graph = pkg.select(context_length=ctx)
-            with graph.session(tp=(rank, world, uid[0])) as s:
-                s.prefill(prompt[:1024])           # warm-up: allocations, tensor maps, graph capture
+            with graph.session(tp=(rank, world, uid[0]), batch=B) as s:
+                if B == 1:
+                    prefill, decode = (lambda p: s.prefill(p[0])), (lambda: s.decode().next_token_id)
+                else:
+                    prefill, decode = s.batch_prefill, (lambda: int(s.batch_decode()[0]))
+                prefill(prompt[:, :1024])          # warm-up: allocations, tensor maps, graph capture
                 for _ in range(args.warmup):
-                    s.decode()
+                    decode()
                 s.reset()
                 clocks = ClockSampler(torch.cuda.current_device(), interval_ms=5) if rank == 0 else None
                 if world > 1:
                     dist.barrier()
                 t0 = time.perf_counter()
-                s.prefill(prompt)
-                first = s.decode()
+                prefill(prompt)
+                first = decode()
                 t1 = time.perf_counter()
                 for _ in range(steps):
-                    s.decode()
+                    decode()
                 t2 = time.perf_counter()
                 clk = clocks.stop() if clocks else None
     finally:
@@ -971,18 +980,21 @@ def run_qwen(args):
     Hq, Hkv = c["heads"], c["kv_heads"]
     lin_params = L * (H * (Hq + 2 * Hkv) * D + Hq * D * H + H * 2 * F + F * H)
     S = QWEN_PROMPT
-    flops = 2.0 * lin_params * S + L * 4.0 * Hq * D * S * (S + 1) / 2 + 2.0 * H * V  # linears, causal attention, LM head
-    prefill_tps = S / ttft_s
+    # linears, causal attention, LM head (last token), per sequence
+    flops = B * (2.0 * lin_params * S + L * 4.0 * Hq * D * S * (S + 1) / 2 + 2.0 * H * V)
+    prefill_tps = B * S / ttft_s
     achieved = flops / ttft_s / 1e12 / world
     peak, peak_src = read_peak_tensor()
-    dec_tps = steps / decode_s
+    dec_tps = B * steps / decode_s
     line = {
-        "metric": "Qwen-7B-shape INT4 prefill tokens/s (8192-token prompt, tensor-parallel)",
+        "metric": f"Qwen-7B-shape INT4 prefill tokens/s (8192-token prompt{'s x ' + str(B) if B > 1 else ''}, "
+                  "tensor-parallel)",
         "value": round(prefill_tps, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * decode_s / steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (random N(0,0.02) weights drawn on the GPU, random prompt ids)",
-        "config": {"workload": QWEN_WORKLOAD, "prompt": S, "ttft_ms": round(1e3 * ttft_s, 2),
+        "config": {"workload": QWEN_WORKLOAD, "batch": B, "prompt": S, "prefill_chunk": chunk,
+                   "ttft_ms": round(1e3 * ttft_s, 2),
                    "decode_steps": steps, "decode_tokens_per_s": round(dec_tps, 2),
                    "decode_ms_per_token": round(1e3 * decode_s / steps, 3),
                    "weight_bytes": int(weight_bytes), "flops_prefill": flops,
@@ -991,11 +1003,11 @@ def run_qwen(args):
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_src, "traffic": None,
                      "achieved_basis": "prefill FLOPs (linears + causal attention + LM head) / TTFT, per GPU"},
-        "e2e": {"value": round(prefill_tps, 1), "unit": "tokens/s", "h2d_bytes_per_step": S * 4,
-                "d2h_bytes_per_step": 8},
+        "e2e": {"value": round(prefill_tps, 1), "unit": "tokens/s", "h2d_bytes_per_step": B * S * 4,
+                "d2h_bytes_per_step": 8 if B == 1 else 4 * B},
         "gpu_launches": None,
         "clocks": clk,
-        "first_token": int(first.next_token_id),
+        "first_token": int(first),
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -1073,6 +1085,91 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+INT8_WORKLOAD = (f"int8_gemv: x fp32 [1,{K_DIM}] x W[{K_DIM}x{N_DIM}] int8 per-channel (fp32 column scales), "
+                 f"y fp32 [1,{N_DIM}] (weight-only variant of the gemm_int8 shader, vulkan_shaders.h:53-82)")
+
+
+def run_int8(args):
+    """The INT8 per-channel decode GEMV (row a3): same timing rules as the INT4
+    line; the reference has no CPU kernel for this layout (its only INT8 path
+    is a GLSL/OpenCL shader), so there is no CPU baseline on this line."""
+    import torch
+
+    from silicongraph_b200 import _lib, kernels
+
+    rank, local_rank, world = rank_env()
+    if world > 1:
+        raise SystemExit("--workload gemv_int8 runs on one GPU")
+    torch.cuda.set_device(local_rank)
+    lib = _lib.load()
+    dev = torch.device("cuda", local_rank)
+    K, N = K_DIM, N_DIM
+    nbytes = K * N + 4 * N + 4 * K + 4 * N
+    rng = np.random.default_rng(4321)
+    W = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+    sc = (np.abs(W).max(axis=0) / 127.0).astype(np.float32)
+    Wq = np.clip(np.rint(W / sc), -127, 127).astype(np.int8)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    copies = max(2, math.ceil(2.0 * l2 / (K * N)))
+    Bs = [torch.from_numpy(Wq).to(dev) for _ in range(copies)]
+    S = torch.from_numpy(sc).to(dev)
+    x = torch.from_numpy(rng.standard_normal((1, K)).astype(np.float32)).to(dev)
+    y = torch.empty((1, N), dtype=torch.float32, device=dev)
+    params = [kernels.matmul_params(x, Bs[i], y, M=1, K=K, N=N, scales=S) for i in range(copies)]
+    pptr = [ctypes.byref(p) for p in params]
+    stream = torch.cuda.Stream(dev)
+    st = stream.cuda_stream
+    fn = lib.sg_matmul_int8_channel
+
+    def launch(i):
+        r = fn(pptr[i % copies], st)
+        if r != 0:
+            raise _lib.SgError(r, _lib.last_error())
+
+    for i in range(args.warmup):
+        launch(i)
+    stream.synchronize()
+    graph_len = max(copies, (min(args.graph_len, args.steps) // copies) * copies)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(graph_len):
+            launch(i)
+    g.replay()
+    stream.synchronize()
+    clocks = ClockSampler(torch.cuda.current_device())
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps // graph_len):
+            g.replay()
+        for i in range(args.steps % graph_len):
+            launch(i)
+        e1.record(stream)
+    stream.synchronize()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    value = args.steps * nbytes / (ms / 1e3) / 1e9
+    peak, peak_src = read_peak_hbm()
+    line = {
+        "metric": "INT8 per-channel GEMV HBM GB/s", "value": round(value, 2), "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights quantised per column on the host)",
+        "config": {"workload": INT8_WORKLOAD, "weight_copies": copies,
+                   "l2": f"{copies} weight copies rotate ({copies * K * N / 1e6:.0f} MB > L2)"},
+        "roofline": {"bound": "hbm", "achieved": round(value, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(value / peak, 4), "peak_source": f"{peak_src} hbm_gbs", "traffic": None,
+                     "achieved_basis": "algorithmic bytes per launch x launches / event time of back-to-back launches"},
+        "cpu_baseline": None,
+        "gpu_launches": args.steps,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -1086,7 +1183,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=1,
                     help="decode workloads: sequences decoded in lockstep by one session (config: 1 and 16)")
-    ap.add_argument("--workload", choices=["gemv_int4", *PF_WORKLOADS, *ATTN_WORKLOADS, "decode_llama1b",
+    ap.add_argument("--workload", choices=["gemv_int4", "gemv_int8", *PF_WORKLOADS, *ATTN_WORKLOADS, "decode_llama1b",
                                            "decode_llama1b_tp", "qwen7b_tp"],
                     default="gemv_int4",
                     help="gemv_int4 (default): the decode GEMV; prefill_int4 / prefill_int8: the prefill GEMM; "
@@ -1112,6 +1209,8 @@ def main():
         if args.workload != "gemv_int4":
             ap.error("--impl reference times the decode GEMV workload")
         run_reference(args)
+    elif args.workload == "gemv_int8":
+        run_int8(args)
     elif args.workload in PF_WORKLOADS:
         run_prefill(args)
     elif args.workload in ATTN_WORKLOADS:
