@@ -144,10 +144,10 @@ __global__ void __launch_bounds__(kThreads, 2) dense_gemv_kernel(DArgs a) {
     acci[c] = 0;
   }
 
-  if (col_ok) {
+  if (col_ok && KIND == W_F16) {
     const uint8_t* Bcol = a.B + (int64_t)col0 * ESZ;
     for (int ch = warp * kRowsPerChunk; ch < nrows_pad; ch += kWarps * kRowsPerChunk) {
-      if (KIND == W_F16) {
+      {
         uint4 wv[kRowsPerChunk][2];
 #pragma unroll
         for (int r = 0; r < kRowsPerChunk; ++r) {
@@ -174,50 +174,64 @@ __global__ void __launch_bounds__(kThreads, 2) dense_gemv_kernel(DArgs a) {
             accf[2 * q + 1] = acc2.y;
           }
         }
+      }
+    }
+  }
+  if (col_ok && KIND != W_F16) {
+    // int8 weights: the next chunk's rows are requested before this chunk is
+    // consumed (two chunks of loads in flight per warp)
+    const uint8_t* Bcol = a.B + (int64_t)col0;
+    constexpr int kStep = kWarps * kRowsPerChunk;
+    auto load_chunk = [&](int ch, uint4 (&dst)[kRowsPerChunk]) {
+#pragma unroll
+      for (int r = 0; r < kRowsPerChunk; ++r) {
+        const int k = r_begin + ch + r;
+        dst[r] = (k < r_end) ? sgd::ldg_stream(Bcol + (int64_t)k * a.N) : make_uint4(0u, 0u, 0u, 0u);
+      }
+    };
+    uint4 wv[kRowsPerChunk], nx[kRowsPerChunk];
+    int ch = warp * kRowsPerChunk;
+    if (ch < nrows_pad) load_chunk(ch, wv);
+    for (; ch < nrows_pad; ch += kStep) {
+      if (ch + kStep < nrows_pad) load_chunk(ch + kStep, nx);
+      if (KIND == W_INT8_IA) {
+        const int32_t* xq = reinterpret_cast<const int32_t*>(xs_f);
+#pragma unroll
+        for (int r4 = 0; r4 < kRowsPerChunk; r4 += 4) {
+          const int32_t a4 = xq[(ch + r4) / 4];
+          const uint32_t rows[4][4] = {{wv[r4].x, wv[r4].y, wv[r4].z, wv[r4].w},
+                                       {wv[r4 + 1].x, wv[r4 + 1].y, wv[r4 + 1].z, wv[r4 + 1].w},
+                                       {wv[r4 + 2].x, wv[r4 + 2].y, wv[r4 + 2].z, wv[r4 + 2].w},
+                                       {wv[r4 + 3].x, wv[r4 + 3].y, wv[r4 + 3].z, wv[r4 + 3].w}};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t cw[4];
+            transpose4x4(rows[0][q], rows[1][q], rows[2][q], rows[3][q], cw);
+#pragma unroll
+            for (int b = 0; b < 4; ++b) acci[4 * q + b] = __dp4a((int)cw[b], a4, acci[4 * q + b]);
+          }
+        }
       } else {
-        uint4 wv[kRowsPerChunk];
 #pragma unroll
         for (int r = 0; r < kRowsPerChunk; ++r) {
-          const int k = r_begin + ch + r;
-          wv[r] = (k < r_end) ? sgd::ldg_stream(Bcol + (int64_t)k * a.N) : make_uint4(0u, 0u, 0u, 0u);
-        }
-        if (KIND == W_INT8_IA) {
-          const int32_t* xq = reinterpret_cast<const int32_t*>(xs_f);
+          const float x = xs_f[ch + r];
+          const float2 xx = make_float2(x, x);
+          const uint32_t words[4] = {wv[r].x, wv[r].y, wv[r].z, wv[r].w};
 #pragma unroll
-          for (int r4 = 0; r4 < kRowsPerChunk; r4 += 4) {
-            const int32_t a4 = xq[(ch + r4) / 4];
-            const uint32_t rows[4][4] = {{wv[r4].x, wv[r4].y, wv[r4].z, wv[r4].w},
-                                         {wv[r4 + 1].x, wv[r4 + 1].y, wv[r4 + 1].z, wv[r4 + 1].w},
-                                         {wv[r4 + 2].x, wv[r4 + 2].y, wv[r4 + 2].z, wv[r4 + 2].w},
-                                         {wv[r4 + 3].x, wv[r4 + 3].y, wv[r4 + 3].z, wv[r4 + 3].w}};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint32_t cw[4];
-              transpose4x4(rows[0][q], rows[1][q], rows[2][q], rows[3][q], cw);
-#pragma unroll
-              for (int b = 0; b < 4; ++b) acci[4 * q + b] = __dp4a((int)cw[b], a4, acci[4 * q + b]);
-            }
-          }
-        } else {
-#pragma unroll
-          for (int r = 0; r < kRowsPerChunk; ++r) {
-            const float x = xs_f[ch + r];
-            const float2 xx = make_float2(x, x);
-            const uint32_t words[4] = {wv[r].x, wv[r].y, wv[r].z, wv[r].w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              float2 p01, p23;
-              i8word_to_f32(words[q], p01, p23);
-              float2 a01 = sgd::ffma2(p01, xx, make_float2(accf[4 * q], accf[4 * q + 1]));
-              float2 a23 = sgd::ffma2(p23, xx, make_float2(accf[4 * q + 2], accf[4 * q + 3]));
-              accf[4 * q] = a01.x;
-              accf[4 * q + 1] = a01.y;
-              accf[4 * q + 2] = a23.x;
-              accf[4 * q + 3] = a23.y;
-            }
+          for (int q = 0; q < 4; ++q) {
+            float2 p01, p23;
+            i8word_to_f32(words[q], p01, p23);
+            float2 a01 = sgd::ffma2(p01, xx, make_float2(accf[4 * q], accf[4 * q + 1]));
+            float2 a23 = sgd::ffma2(p23, xx, make_float2(accf[4 * q + 2], accf[4 * q + 3]));
+            accf[4 * q] = a01.x;
+            accf[4 * q + 1] = a01.y;
+            accf[4 * q + 2] = a23.x;
+            accf[4 * q + 3] = a23.y;
           }
         }
       }
+#pragma unroll
+      for (int r = 0; r < kRowsPerChunk; ++r) wv[r] = nx[r];
     }
   }
 
@@ -316,9 +330,17 @@ Plan make_plan(int kind, const SgMatMulParams* p, int sms) {
   pl.n_tiles = (p->N + kColsPerBlock - 1) / kColsPerBlock;
   // chunks of 8 rows are the unit of work of one warp step
   const long chunks = (p->K + kRowsPerChunk - 1) / kRowsPerChunk;
-  const long units = (long)pl.n_tiles * chunks;
-  const long target = (long)sms * 4 * kWarps * 2;  // ~2 chunks per warp, ~4 blocks per SM
-  long chunks_per_split = std::max<long>(kWarps, (units + target - 1) / target * kWarps);
+  long chunks_per_split;
+  if (kind == W_F16) {
+    const long units = (long)pl.n_tiles * chunks;
+    const long target = (long)sms * 4 * kWarps * 2;  // ~2 chunks per warp, ~4 blocks per SM
+    chunks_per_split = std::max<long>(kWarps, (units + target - 1) / target * kWarps);
+  } else {
+    // int8: about two blocks per SM, each warp streaming several chunks with the
+    // next one in flight (fewer, longer splits than one round trip per warp)
+    const long ks = std::max<long>(1, std::min<long>(chunks / kWarps, (2L * sms + pl.n_tiles - 1) / pl.n_tiles));
+    chunks_per_split = std::max<long>(kWarps, ((chunks + ks - 1) / ks + kWarps - 1) / kWarps * kWarps);
+  }
   chunks_per_split = std::min<long>(chunks_per_split, 4096 / kRowsPerChunk);  // x stage <= 16 KB
   pl.rows_per_split = (int)(chunks_per_split * kRowsPerChunk);
   pl.ksplit = (p->K + pl.rows_per_split - 1) / pl.rows_per_split;
