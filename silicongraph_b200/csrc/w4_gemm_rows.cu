@@ -532,7 +532,7 @@ RPlan make_rplan(const SgMatMulParams* p, int sms) {
   int ks = 1;
   for (int k = std::min({8, pl.cpt, std::max(1, (2 * sms) / pl.n_tiles)}); k >= 2; --k) {
     const size_t smem = rows_smem(pl.mt, (pl.cpt + k - 1) / k, kMinStages);
-    if (smem <= 200 * 1024 && rows_active_clusters(k, smem) >= pl.n_tiles) {
+    if (smem <= (size_t)kMaxSmem && rows_active_clusters(k, smem) >= pl.n_tiles) {
       ks = k;
       break;
     }

@@ -438,3 +438,15 @@ def test_int4_swiglu_fused_refuses_many_rows(sg, oracle_mod):
     gu = torch.zeros((64, 2 * K), dtype=torch.float16, device=DEV)
     with pytest.raises(Exception, match="SG_MM_A_SWIGLU"):
         sg.matmul_int4_grouped(gu, t(B), t(S), t(Z), K, N, gs, flags=_lib.SG_MM_A_SWIGLU)
+
+
+@pytest.mark.parametrize("M,K,N,gs", [(17, 2048, 3072, 32), (24, 3584, 4608, 128), (32, 1024, 40960, 32),
+                                      (32, 2368, 3584, 128)])
+def test_int4_two_pass_rows(sg, oracle_mod, M, K, N, gs):
+    """17..32 activation rows run as two passes of the few-row kernel (the
+    second over rows 16..M-1): the oracle's result within tolerance."""
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=M + K)
+    x = np.random.default_rng(M * 3).standard_normal((M, K)).astype(np.float32).astype(np.float16)
+    want = oracle_mod.matmul_int4_grouped(x, B, S, Z, K, N, gs, M=M, c_dt=oracle_mod.DT_F32)
+    C = sg.matmul_int4_grouped(t(x), t(B), t(S), t(Z), K, N, gs, out_dtype=torch.float32)
+    close(C.cpu().numpy(), want)
