@@ -338,7 +338,8 @@ Plan make_plan(int kind, const SgMatMulParams* p, int sms) {
   } else {
     // int8: about two blocks per SM, each warp streaming several chunks with the
     // next one in flight (fewer, longer splits than one round trip per warp)
-    const long ks = std::max<long>(1, std::min<long>(chunks / kWarps, (2L * sms + pl.n_tiles - 1) / pl.n_tiles));
+    // (rounded down: a partial second wave of blocks would nearly double the time)
+    const long ks = std::max<long>(1, std::min<long>(chunks / kWarps, (2L * sms) / pl.n_tiles));
     chunks_per_split = std::max<long>(kWarps, ((chunks + ks - 1) / ks + kWarps - 1) / kWarps * kWarps);
   }
   chunks_per_split = std::min<long>(chunks_per_split, 4096 / kRowsPerChunk);  // x stage <= 16 KB
