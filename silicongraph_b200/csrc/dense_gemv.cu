@@ -19,6 +19,7 @@
 //     byte of 2^23 (PRMT) minus (2^23 + 128), then packed fp32x2 FMAs.
 //   * fp16 B: half2 -> float2 conversion and packed fp32x2 FMAs.
 #include <algorithm>
+#include <mutex>
 
 #include "sm100.cuh"
 
@@ -29,6 +30,8 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kColsPerLane = 16;
 constexpr int kColsPerBlock = 32 * kColsPerLane;  // 512
 constexpr int kRowsPerChunk = 8;                   // rows per warp step (multiple of 4)
+constexpr int kChunkBytes = kRowsPerChunk * kColsPerBlock;  // int8: one warp step, 4 KB
+constexpr int kI8Stages = 6;                       // int8: chunks in flight per warp (cp.async ring)
 
 enum WKind { W_INT8_IA = 0, W_INT8_FA = 1, W_F16 = 2 };
 
@@ -42,6 +45,7 @@ struct DArgs {
   int a_dt, c_dt;
   float scale_A;
   int rows_per_split, ksplit;
+  int ring_off;        // int8: byte offset of the per-warp cp.async rings in dynamic shared memory
   float* partial;      // [ksplit][M][N] (float)  or int32 for W_INT8_IA
   unsigned* tickets;
 };
@@ -102,7 +106,7 @@ __device__ __forceinline__ void i8word_to_f32(uint32_t w, float2& p01, float2& p
 }
 
 template <int KIND>
-__global__ void __launch_bounds__(kThreads, 2) dense_gemv_kernel(DArgs a) {
+__global__ void __launch_bounds__(kThreads, KIND == W_F16 ? 2 : 1) dense_gemv_kernel(DArgs a) {
   extern __shared__ float xs_f[];  // staged activations for this block's rows
   const int tile = blockIdx.x, split = blockIdx.y;
   const int r_begin = split * a.rows_per_split;
@@ -178,22 +182,37 @@ __global__ void __launch_bounds__(kThreads, 2) dense_gemv_kernel(DArgs a) {
     }
   }
   if (col_ok && KIND != W_F16) {
-    // int8 weights: the next chunk's rows are requested before this chunk is
-    // consumed (two chunks of loads in flight per warp)
+    // int8 weights: every lane streams its own 16 bytes of each row of its warp's
+    // chunks through a cp.async ring in shared memory (kI8Stages chunks in flight
+    // per warp); a lane reads back only what it copied, so no warp barrier
+    uint8_t* ring = reinterpret_cast<uint8_t*>(xs_f) + a.ring_off + (size_t)warp * kI8Stages * kChunkBytes + lane * 16;
     const uint8_t* Bcol = a.B + (int64_t)col0;
     constexpr int kStep = kWarps * kRowsPerChunk;
-    auto load_chunk = [&](int ch, uint4 (&dst)[kRowsPerChunk]) {
+    const int first = warp * kRowsPerChunk;
+    const int nmy = first < nrows_pad ? (nrows_pad - first + kStep - 1) / kStep : 0;
+    auto issue = [&](int i) {
+      const int ch = first + i * kStep;
+      uint8_t* dst = ring + (i % kI8Stages) * kChunkBytes;
 #pragma unroll
       for (int r = 0; r < kRowsPerChunk; ++r) {
         const int k = r_begin + ch + r;
-        dst[r] = (k < r_end) ? sgd::ldg_stream(Bcol + (int64_t)k * a.N) : make_uint4(0u, 0u, 0u, 0u);
+        const bool live = k < r_end;
+        sgd::cp_async_16(dst + r * kColsPerBlock, Bcol + (int64_t)(live ? k : r_begin) * a.N, live);
       }
     };
-    uint4 wv[kRowsPerChunk], nx[kRowsPerChunk];
-    int ch = warp * kRowsPerChunk;
-    if (ch < nrows_pad) load_chunk(ch, wv);
-    for (; ch < nrows_pad; ch += kStep) {
-      if (ch + kStep < nrows_pad) load_chunk(ch + kStep, nx);
+    for (int i = 0; i < kI8Stages - 1; ++i) {
+      if (i < nmy) issue(i);
+      sgd::cp_async_commit();
+    }
+    for (int i = 0; i < nmy; ++i) {
+      sgd::cp_async_wait<kI8Stages - 2>();  // this lane's copies of chunk i have landed
+      if (i + kI8Stages - 1 < nmy) issue(i + kI8Stages - 1);  // into chunk i - 1's stage (read already)
+      sgd::cp_async_commit();
+      const int ch = first + i * kStep;
+      const uint8_t* src = ring + (i % kI8Stages) * kChunkBytes;
+      uint4 wv[kRowsPerChunk];
+#pragma unroll
+      for (int r = 0; r < kRowsPerChunk; ++r) wv[r] = *reinterpret_cast<const uint4*>(src + r * kColsPerBlock);
       if (KIND == W_INT8_IA) {
         const int32_t* xq = reinterpret_cast<const int32_t*>(xs_f);
 #pragma unroll
@@ -230,9 +249,8 @@ __global__ void __launch_bounds__(kThreads, 2) dense_gemv_kernel(DArgs a) {
           }
         }
       }
-#pragma unroll
-      for (int r = 0; r < kRowsPerChunk; ++r) wv[r] = nx[r];
     }
+    sgd::cp_async_wait<0>();
   }
 
   // ---- reduce the 8 warps (fixed order), then split-K
@@ -317,7 +335,7 @@ __global__ void dense_gemv_generic_kernel(DArgs a) {
 
 struct Plan {
   bool fast = false;
-  int rows_per_split = 0, ksplit = 1, n_tiles = 0;
+  int rows_per_split = 0, ksplit = 1, n_tiles = 0, ring_off = 0;
   size_t smem = 0, ws_bytes = 0, tickets_bytes = 0;
 };
 
@@ -336,10 +354,9 @@ Plan make_plan(int kind, const SgMatMulParams* p, int sms) {
     const long target = (long)sms * 4 * kWarps * 2;  // ~2 chunks per warp, ~4 blocks per SM
     chunks_per_split = std::max<long>(kWarps, (units + target - 1) / target * kWarps);
   } else {
-    // int8: about two blocks per SM, each warp streaming several chunks with the
-    // next one in flight (fewer, longer splits than one round trip per warp)
-    // (rounded down: a partial second wave of blocks would nearly double the time)
-    const long ks = std::max<long>(1, std::min<long>(chunks / kWarps, (2L * sms) / pl.n_tiles));
+    // int8: one block per SM (its warps' cp.async rings fill the shared memory),
+    // each warp streaming several chunks; rounded down so that the grid is one wave
+    const long ks = std::max<long>(1, std::min<long>(chunks / kWarps, (long)sms / pl.n_tiles));
     chunks_per_split = std::max<long>(kWarps, ((chunks + ks - 1) / ks + kWarps - 1) / kWarps * kWarps);
   }
   chunks_per_split = std::min<long>(chunks_per_split, 4096 / kRowsPerChunk);  // x stage <= 16 KB
@@ -348,6 +365,10 @@ Plan make_plan(int kind, const SgMatMulParams* p, int sms) {
   const size_t xs_bytes = (size_t)pl.rows_per_split * 4;
   const size_t red_bytes = (size_t)kWarps * kColsPerBlock * 4;
   pl.smem = std::max(xs_bytes, red_bytes);
+  if (kind != W_F16) {
+    pl.ring_off = (int)sg::align_up(pl.smem, (size_t)16);
+    pl.smem = (size_t)pl.ring_off + (size_t)kWarps * kI8Stages * kChunkBytes;
+  }
   if (pl.ksplit > 1) {
     pl.tickets_bytes = sg::ticket_bytes(pl.n_tiles);
     pl.ws_bytes = pl.tickets_bytes + (size_t)pl.ksplit * p->N * 4;
@@ -435,6 +456,20 @@ SgStatus dense_run(const char* name, const SgMatMulParams* p, void* stream, bool
   }
   a.rows_per_split = pl.rows_per_split;
   a.ksplit = pl.ksplit;
+  a.ring_off = pl.ring_off;
+  if (kind != W_F16) {  // the int8 rings need the shared-memory opt-in (once per kernel)
+    static std::once_flag once[2];
+    cudaError_t ae = cudaSuccess;
+    auto kfn = kind == W_INT8_IA ? dense_gemv_kernel<W_INT8_IA> : dense_gemv_kernel<W_INT8_FA>;
+    std::call_once(once[kind == W_INT8_IA ? 0 : 1], [&] {
+      ae = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 2048);
+    });
+    if (ae != cudaSuccess) {
+      cudaGetLastError();
+      sg::set_error("%s: cudaFuncSetAttribute failed: %s", name, cudaGetErrorString(ae));
+      return SG_ERR_RUNTIME;
+    }
+  }
   if (pl.ksplit > 1) {
     void* ws = p->workspace;
     if (ws == nullptr) {
