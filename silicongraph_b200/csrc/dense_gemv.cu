@@ -15,8 +15,11 @@
 //   * int8 A: four rows of a lane are transposed 4x4 bytes with PRMT so each
 //     32-bit word holds one column's four k values, then dp4a accumulates in
 //     int32 -- exact, hence bit-identical to the shader for any split.
-//   * float A: int8 bytes become exact fp32 via (b ^ 0x80) placed in the low
-//     byte of 2^23 (PRMT) minus (2^23 + 128), then packed fp32x2 FMAs.
+//   * float A (int8 weights): x is staged as 16-bit fixed point per 8-row chunk
+//     (one power-of-two scale per chunk, |error| below 2^-14 of the chunk's
+//     largest |x|), split into signed hi / lo bytes; the weights meet both in
+//     dp4a (exact int32) after the same 4x4 transpose, and each chunk adds
+//     scale * (256 hi_sum + lo_sum) to the fp32 accumulators.
 //   * fp16 B: half2 -> float2 conversion and packed fp32x2 FMAs.
 #include <algorithm>
 #include <mutex>
@@ -92,19 +95,6 @@ __device__ __forceinline__ void transpose4x4(const uint32_t w0, const uint32_t w
   c[3] = __byte_perm(t2, t3, 0x7632);
 }
 
-// Exact fp32 values of the 4 signed bytes of w as two pairs (b0,b1), (b2,b3).
-__device__ __forceinline__ void i8word_to_f32(uint32_t w, float2& p01, float2& p23) {
-  const uint32_t u = w ^ 0x80808080u;  // biased: byte + 128 in [0, 255]
-  const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440));
-  const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441));
-  const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442));
-  const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443));
-  constexpr float OFF = -8388736.0f;  // -(2^23 + 128)
-  const float2 one = make_float2(1.f, 1.f), off = make_float2(OFF, OFF);
-  p01 = sgd::ffma2(make_float2(f0, f1), one, off);
-  p23 = sgd::ffma2(make_float2(f2, f3), one, off);
-}
-
 template <int KIND>
 __global__ void __launch_bounds__(kThreads, KIND == W_F16 ? 2 : 1) dense_gemv_kernel(DArgs a) {
   extern __shared__ float xs_f[];  // staged activations for this block's rows
@@ -126,6 +116,29 @@ __global__ void __launch_bounds__(kThreads, KIND == W_F16 ? 2 : 1) dense_gemv_ke
         v |= (uint32_t)(uint8_t)x << (8 * j);
       }
       xq[i] = (int32_t)v;
+    }
+  } else if (KIND == W_INT8_FA) {
+    // float activations as 16-bit fixed point per 8-row chunk: x = 2^(E-13) q, E the
+    // exponent of the chunk's largest |x| (|q| <= 2^14, error below 2^-14 of that
+    // value), q = 256 hi + lo in signed bytes, so the weights meet them in dp4a
+    int8_t* xhi = reinterpret_cast<int8_t*>(xs_f);
+    int8_t* xlo = xhi + nrows_pad;
+    float* sx = reinterpret_cast<float*>(xhi + 2 * nrows_pad);
+    const int lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < (nrows_pad + kThreads - 1) / kThreads * kThreads; i += kThreads) {
+      const int k = r_begin + i;
+      const float x = (i < nrows_pad && k < r_end) ? load_act(a.A, a.a_dt, k) : 0.f;
+      float m = fabsf(x);
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const int E = max((__float_as_int(m) >> 23) - 127, -100);
+      const int q = __float2int_rn(x * __int_as_float((127 + 13 - E) << 23));
+      const int lo = ((q + 128) & 255) - 128, hi = (q - lo) >> 8;
+      if (i < nrows_pad) {
+        xhi[i] = (int8_t)hi;
+        xlo[i] = (int8_t)lo;
+        if ((lane & 7) == 0) sx[i / 8] = __int_as_float((127 - 13 + E) << 23);  // 2^(E - 13)
+      }
     }
   } else {
     for (int i = threadIdx.x; i < nrows_pad; i += kThreads) {
@@ -231,23 +244,34 @@ __global__ void __launch_bounds__(kThreads, KIND == W_F16 ? 2 : 1) dense_gemv_ke
           }
         }
       } else {
+        // exact int32 dot products with the hi and lo bytes of this chunk's fixed-point x
+        const int32_t* xh = reinterpret_cast<const int32_t*>(xs_f);
+        const int32_t* xl = reinterpret_cast<const int32_t*>(reinterpret_cast<const int8_t*>(xs_f) + nrows_pad);
+        const float* sx = reinterpret_cast<const float*>(reinterpret_cast<const int8_t*>(xs_f) + 2 * nrows_pad);
+        int ah[16], al[16];
 #pragma unroll
-        for (int r = 0; r < kRowsPerChunk; ++r) {
-          const float x = xs_f[ch + r];
-          const float2 xx = make_float2(x, x);
-          const uint32_t words[4] = {wv[r].x, wv[r].y, wv[r].z, wv[r].w};
+        for (int c = 0; c < 16; ++c) ah[c] = al[c] = 0;
+#pragma unroll
+        for (int r4 = 0; r4 < kRowsPerChunk; r4 += 4) {
+          const int32_t h4 = xh[(ch + r4) / 4], l4 = xl[(ch + r4) / 4];
+          const uint32_t rows[4][4] = {{wv[r4].x, wv[r4].y, wv[r4].z, wv[r4].w},
+                                       {wv[r4 + 1].x, wv[r4 + 1].y, wv[r4 + 1].z, wv[r4 + 1].w},
+                                       {wv[r4 + 2].x, wv[r4 + 2].y, wv[r4 + 2].z, wv[r4 + 2].w},
+                                       {wv[r4 + 3].x, wv[r4 + 3].y, wv[r4 + 3].z, wv[r4 + 3].w}};
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            float2 p01, p23;
-            i8word_to_f32(words[q], p01, p23);
-            float2 a01 = sgd::ffma2(p01, xx, make_float2(accf[4 * q], accf[4 * q + 1]));
-            float2 a23 = sgd::ffma2(p23, xx, make_float2(accf[4 * q + 2], accf[4 * q + 3]));
-            accf[4 * q] = a01.x;
-            accf[4 * q + 1] = a01.y;
-            accf[4 * q + 2] = a23.x;
-            accf[4 * q + 3] = a23.y;
+            uint32_t cw[4];
+            transpose4x4(rows[0][q], rows[1][q], rows[2][q], rows[3][q], cw);
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              ah[4 * q + b] = __dp4a((int)cw[b], h4, ah[4 * q + b]);
+              al[4 * q + b] = __dp4a((int)cw[b], l4, al[4 * q + b]);
+            }
           }
         }
+        const float sc = sx[ch / kRowsPerChunk];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) accf[c] = fmaf((float)(ah[c] * 256 + al[c]), sc, accf[c]);
       }
     }
     sgd::cp_async_wait<0>();
