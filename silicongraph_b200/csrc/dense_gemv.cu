@@ -34,7 +34,8 @@ constexpr int kColsPerLane = 16;
 constexpr int kColsPerBlock = 32 * kColsPerLane;  // 512
 constexpr int kRowsPerChunk = 8;                   // rows per warp step (multiple of 4)
 constexpr int kChunkBytes = kRowsPerChunk * kColsPerBlock;  // int8: one warp step, 4 KB
-constexpr int kI8Stages = 6;                       // int8: chunks in flight per warp (cp.async ring)
+constexpr int kI8Warps = 16;                       // int8: warps per block (one block per SM)
+constexpr int kI8Stages = 3;                       // int8: chunks in flight per warp (cp.async ring)
 
 enum WKind { W_INT8_IA = 0, W_INT8_FA = 1, W_F16 = 2 };
 
@@ -96,7 +97,9 @@ __device__ __forceinline__ void transpose4x4(const uint32_t w0, const uint32_t w
 }
 
 template <int KIND>
-__global__ void __launch_bounds__(kThreads, KIND == W_F16 ? 2 : 1) dense_gemv_kernel(DArgs a) {
+__global__ void __launch_bounds__(KIND == W_F16 ? kThreads : kI8Warps * 32, KIND == W_F16 ? 2 : 1) dense_gemv_kernel(DArgs a) {
+  constexpr int W = KIND == W_F16 ? kWarps : kI8Warps;  // warps per block
+  constexpr int T = W * 32;
   extern __shared__ float xs_f[];  // staged activations for this block's rows
   const int tile = blockIdx.x, split = blockIdx.y;
   const int r_begin = split * a.rows_per_split;
@@ -107,7 +110,7 @@ __global__ void __launch_bounds__(kThreads, KIND == W_F16 ? 2 : 1) dense_gemv_ke
   // stage x (zero padded to a whole number of chunks)
   if (KIND == W_INT8_IA) {
     int32_t* xq = reinterpret_cast<int32_t*>(xs_f);  // packed int8 quads
-    for (int i = threadIdx.x; i < nrows_pad / 4; i += kThreads) {
+    for (int i = threadIdx.x; i < nrows_pad / 4; i += T) {
       uint32_t v = 0;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -125,7 +128,7 @@ __global__ void __launch_bounds__(kThreads, KIND == W_F16 ? 2 : 1) dense_gemv_ke
     int8_t* xlo = xhi + nrows_pad;
     float* sx = reinterpret_cast<float*>(xhi + 2 * nrows_pad);
     const int lane = threadIdx.x & 31;
-    for (int i = threadIdx.x; i < (nrows_pad + kThreads - 1) / kThreads * kThreads; i += kThreads) {
+    for (int i = threadIdx.x; i < (nrows_pad + T - 1) / T * T; i += T) {
       const int k = r_begin + i;
       const float x = (i < nrows_pad && k < r_end) ? load_act(a.A, a.a_dt, k) : 0.f;
       float m = fabsf(x);
@@ -141,7 +144,7 @@ __global__ void __launch_bounds__(kThreads, KIND == W_F16 ? 2 : 1) dense_gemv_ke
       }
     }
   } else {
-    for (int i = threadIdx.x; i < nrows_pad; i += kThreads) {
+    for (int i = threadIdx.x; i < nrows_pad; i += T) {
       const int k = r_begin + i;
       xs_f[i] = (k < r_end) ? load_act(a.A, a.a_dt, k) : 0.f;
     }
@@ -163,7 +166,7 @@ __global__ void __launch_bounds__(kThreads, KIND == W_F16 ? 2 : 1) dense_gemv_ke
 
   if (col_ok && KIND == W_F16) {
     const uint8_t* Bcol = a.B + (int64_t)col0 * ESZ;
-    for (int ch = warp * kRowsPerChunk; ch < nrows_pad; ch += kWarps * kRowsPerChunk) {
+    for (int ch = warp * kRowsPerChunk; ch < nrows_pad; ch += W * kRowsPerChunk) {
       {
         uint4 wv[kRowsPerChunk][2];
 #pragma unroll
@@ -200,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, KIND == W_F16 ? 2 : 1) dense_gemv_ke
     // per warp); a lane reads back only what it copied, so no warp barrier
     uint8_t* ring = reinterpret_cast<uint8_t*>(xs_f) + a.ring_off + (size_t)warp * kI8Stages * kChunkBytes + lane * 16;
     const uint8_t* Bcol = a.B + (int64_t)col0;
-    constexpr int kStep = kWarps * kRowsPerChunk;
+    constexpr int kStep = W * kRowsPerChunk;
     const int first = warp * kRowsPerChunk;
     const int nmy = first < nrows_pad ? (nrows_pad - first + kStep - 1) / kStep : 0;
     auto issue = [&](int i) {
@@ -280,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, KIND == W_F16 ? 2 : 1) dense_gemv_ke
   // ---- reduce the 8 warps (fixed order), then split-K
   __syncthreads();
   __shared__ bool s_last;
-  float* red = xs_f;  // [kWarps][512] (int32 bits for W_INT8_IA)
+  float* red = xs_f;  // [W][512] (int32 bits for W_INT8_IA)
   if (col_ok) {
 #pragma unroll
     for (int c = 0; c < 16; ++c)
@@ -288,19 +291,19 @@ __global__ void __launch_bounds__(kThreads, KIND == W_F16 ? 2 : 1) dense_gemv_ke
           (KIND == W_INT8_IA) ? __int_as_float(acci[c]) : accf[c];
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < kColsPerBlock; c += kThreads) {
+  for (int c = threadIdx.x; c < kColsPerBlock; c += T) {
     const int col = tile * kColsPerBlock + c;
     if (col >= a.N) continue;
     if (KIND == W_INT8_IA) {
       int v = 0;
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) v += __float_as_int(red[w * kColsPerBlock + c]);
+      for (int w = 0; w < W; ++w) v += __float_as_int(red[w * kColsPerBlock + c]);
       if (a.ksplit == 1) store_out(a.C, a.c_dt, col, finalize_i(a, col, v));
       else reinterpret_cast<int*>(a.partial)[(int64_t)split * a.N + col] = v;
     } else {
       float v = 0.f;
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) v += red[w * kColsPerBlock + c];
+      for (int w = 0; w < W; ++w) v += red[w * kColsPerBlock + c];
       if (a.ksplit == 1) store_out(a.C, a.c_dt, col, finalize_f<KIND>(a, col, v));
       else a.partial[(int64_t)split * a.N + col] = v;
     }
@@ -315,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, KIND == W_F16 ? 2 : 1) dense_gemv_ke
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  for (int c = threadIdx.x; c < kColsPerBlock; c += kThreads) {
+  for (int c = threadIdx.x; c < kColsPerBlock; c += T) {
     const int col = tile * kColsPerBlock + c;
     if (col >= a.N) continue;
     if (KIND == W_INT8_IA) {
@@ -378,20 +381,20 @@ Plan make_plan(int kind, const SgMatMulParams* p, int sms) {
     const long target = (long)sms * 4 * kWarps * 2;  // ~2 chunks per warp, ~4 blocks per SM
     chunks_per_split = std::max<long>(kWarps, (units + target - 1) / target * kWarps);
   } else {
-    // int8: one block per SM (its warps' cp.async rings fill the shared memory),
-    // each warp streaming several chunks; rounded down so that the grid is one wave
-    const long ks = std::max<long>(1, std::min<long>(chunks / kWarps, (long)sms / pl.n_tiles));
-    chunks_per_split = std::max<long>(kWarps, ((chunks + ks - 1) / ks + kWarps - 1) / kWarps * kWarps);
+    // int8: one 16-warp block per SM (its warps' cp.async rings fill the shared
+    // memory), each warp streaming several chunks; rounded down to one wave
+    const long ks = std::max<long>(1, std::min<long>(chunks / kI8Warps, (long)sms / pl.n_tiles));
+    chunks_per_split = std::max<long>(kI8Warps, ((chunks + ks - 1) / ks + kI8Warps - 1) / kI8Warps * kI8Warps);
   }
   chunks_per_split = std::min<long>(chunks_per_split, 4096 / kRowsPerChunk);  // x stage <= 16 KB
   pl.rows_per_split = (int)(chunks_per_split * kRowsPerChunk);
   pl.ksplit = (p->K + pl.rows_per_split - 1) / pl.rows_per_split;
   const size_t xs_bytes = (size_t)pl.rows_per_split * 4;
-  const size_t red_bytes = (size_t)kWarps * kColsPerBlock * 4;
+  const size_t red_bytes = (size_t)(kind == W_F16 ? kWarps : kI8Warps) * kColsPerBlock * 4;
   pl.smem = std::max(xs_bytes, red_bytes);
   if (kind != W_F16) {
     pl.ring_off = (int)sg::align_up(pl.smem, (size_t)16);
-    pl.smem = (size_t)pl.ring_off + (size_t)kWarps * kI8Stages * kChunkBytes;
+    pl.smem = (size_t)pl.ring_off + (size_t)kI8Warps * kI8Stages * kChunkBytes;
   }
   if (pl.ksplit > 1) {
     pl.tickets_bytes = sg::ticket_bytes(pl.n_tiles);
@@ -514,8 +517,8 @@ SgStatus dense_run(const char* name, const SgMatMulParams* p, void* stream, bool
     ar.A = static_cast<const char*>(p->A) + (size_t)m * a.lda * sg::elem_size(a.a_dt);
     ar.C = static_cast<char*>(p->C) + (size_t)m * a.ldc * sg::elem_size(a.c_dt);
     switch (kind) {
-      case W_INT8_IA: dense_gemv_kernel<W_INT8_IA><<<grid, kThreads, pl.smem, cs>>>(ar); break;
-      case W_INT8_FA: dense_gemv_kernel<W_INT8_FA><<<grid, kThreads, pl.smem, cs>>>(ar); break;
+      case W_INT8_IA: dense_gemv_kernel<W_INT8_IA><<<grid, kI8Warps * 32, pl.smem, cs>>>(ar); break;
+      case W_INT8_FA: dense_gemv_kernel<W_INT8_FA><<<grid, kI8Warps * 32, pl.smem, cs>>>(ar); break;
       default: dense_gemv_kernel<W_F16><<<grid, kThreads, pl.smem, cs>>>(ar); break;
     }
     st = sg::check_launch(name);
