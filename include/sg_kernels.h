@@ -189,7 +189,11 @@ SgStatus sg_matmul_int4_grouped_noalloc(const SgMatMulParams* p, void* stream);
  * a_dtype DEFAULT/I8: C[m,n] = float(sum_k A*B as int32) * scale_A * scales_B[n]
  *                     (the shader's exact arithmetic; c_dtype DEFAULT = F32)
  * a_dtype F32/F16/BF16: weight-only variant C[m,n] = scales_B[n] * sum_k A*B
- *                     in fp32 (scale_A unused).
+ *                     in fp32 (scale_A unused).  Few rows (decode): each row's
+ *                     activations are taken as 16-bit fixed point with one
+ *                     power-of-two scale per 8 consecutive k (error below 2^-14
+ *                     of the largest |A| among them) and reduced exactly in
+ *                     int32; many rows: the tcgen05 GEMM in fp32 accumulation.
  */
 SgStatus sg_matmul_int8_channel(const SgMatMulParams* p, void* stream);
 size_t sg_matmul_int8_channel_workspace_size(const SgMatMulParams* p);
