@@ -192,7 +192,8 @@ SgStatus sg_matmul_int4_grouped_noalloc(const SgMatMulParams* p, void* stream);
  *                     in fp32 (scale_A unused).  Few rows (decode): each row's
  *                     activations are taken as 16-bit fixed point with one
  *                     power-of-two scale per 8 consecutive k (error below 2^-14
- *                     of the largest |A| among them) and reduced exactly in
+ *                     of the largest |A| among them, or 2^-114 absolute where
+ *                     that is below 2^-100) and reduced exactly in
  *                     int32; many rows: the tcgen05 GEMM in fp32 accumulation.
  */
 SgStatus sg_matmul_int8_channel(const SgMatMulParams* p, void* stream);

@@ -17,7 +17,8 @@
 //     int32 -- exact, hence bit-identical to the shader for any split.
 //   * float A (int8 weights): x is staged as 16-bit fixed point per 8-row chunk
 //     (one power-of-two scale per chunk, |error| below 2^-14 of the chunk's
-//     largest |x|), split into signed hi / lo bytes; the weights meet both in
+//     largest |x|, or 2^-114 when that is below 2^-100 and the exponent is
+//     clamped), split into signed hi / lo bytes; the weights meet both in
 //     dp4a (exact int32) after the same 4x4 transpose, and each chunk adds
 //     scale * (256 hi_sum + lo_sum) to the fp32 accumulators.
 //   * fp16 B: half2 -> float2 conversion and packed fp32x2 FMAs.
