@@ -23,7 +23,7 @@
 //     scale * (256 hi_sum + lo_sum) to the fp32 accumulators.
 //   * fp16 B: half2 -> float2 conversion and packed fp32x2 FMAs.
 #include <algorithm>
-#include <mutex>
+#include <atomic>
 
 #include "sm100.cuh"
 
@@ -485,17 +485,19 @@ SgStatus dense_run(const char* name, const SgMatMulParams* p, void* stream, bool
   a.rows_per_split = pl.rows_per_split;
   a.ksplit = pl.ksplit;
   a.ring_off = pl.ring_off;
-  if (kind != W_F16) {  // the int8 rings need the shared-memory opt-in (once per kernel)
-    static std::once_flag once[2];
-    cudaError_t ae = cudaSuccess;
-    auto kfn = kind == W_INT8_IA ? dense_gemv_kernel<W_INT8_IA> : dense_gemv_kernel<W_INT8_FA>;
-    std::call_once(once[kind == W_INT8_IA ? 0 : 1], [&] {
-      ae = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 2048);
-    });
-    if (ae != cudaSuccess) {
-      cudaGetLastError();
-      sg::set_error("%s: cudaFuncSetAttribute failed: %s", name, cudaGetErrorString(ae));
-      return SG_ERR_RUNTIME;
+  if (kind != W_F16) {  // the int8 rings need the shared-memory opt-in (once per kernel and device)
+    static std::atomic<uint64_t> attr_set[2] = {};
+    const int ki = kind == W_INT8_IA ? 0 : 1;
+    const uint64_t bit = dev < 64 ? (uint64_t)1 << dev : 0;
+    if (!(attr_set[ki].load() & bit)) {
+      auto kfn = kind == W_INT8_IA ? dense_gemv_kernel<W_INT8_IA> : dense_gemv_kernel<W_INT8_FA>;
+      const cudaError_t ae = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 2048);
+      if (ae != cudaSuccess) {
+        cudaGetLastError();
+        sg::set_error("%s: cudaFuncSetAttribute failed: %s", name, cudaGetErrorString(ae));
+        return SG_ERR_RUNTIME;
+      }
+      attr_set[ki].fetch_or(bit);
     }
   }
   if (pl.ksplit > 1) {

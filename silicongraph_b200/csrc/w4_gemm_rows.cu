@@ -657,15 +657,22 @@ SgStatus w4_rows_run(const SgMatMulParams* p, cudaStream_t cs, int sms, int* err
        {w4_rows_kernel<true, 16, 4>, w4_rows_kernel<true, 16, 2>, w4_rows_kernel<true, 16, 1>}}};
   const int zi = p->zeros_B ? 1 : 0, mi = pl.mt == 8 ? 0 : 1, gi = gpc == 4 ? 0 : gpc == 2 ? 1 : 2;
   const KFn kfn = kfns[zi][mi][gi];
-  // every instantiation gets the largest shared-memory opt-in once; the
-  // occupancy query above relies on the same value
-  static std::once_flag once[2][2][3];
-  cudaError_t ae = cudaSuccess;
-  std::call_once(once[zi][mi][gi], [&] { ae = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem); });
-  if (ae != cudaSuccess) {
-    cudaGetLastError();
-    set_error("w4_rows: cudaFuncSetAttribute(%d) failed: %s", kMaxSmem, cudaGetErrorString(ae));
-    return SG_ERR_RUNTIME;
+  // every instantiation gets the largest shared-memory opt-in once per device
+  // (the attribute belongs to the device's copy of the kernel); the occupancy
+  // query above relies on the same value
+  static std::atomic<uint64_t> attr_set[2][2][3] = {};
+  int dev = 0;
+  st = sg::current_device(&dev);
+  if (st != SG_OK) return st;
+  const uint64_t bit = dev < 64 ? (uint64_t)1 << dev : 0;
+  if (!(attr_set[zi][mi][gi].load() & bit)) {
+    const cudaError_t ae = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+    if (ae != cudaSuccess) {
+      cudaGetLastError();
+      set_error("w4_rows: cudaFuncSetAttribute(%d) failed: %s", kMaxSmem, cudaGetErrorString(ae));
+      return SG_ERR_RUNTIME;
+    }
+    attr_set[zi][mi][gi].fetch_or(bit);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.ksplit, pl.blocks);

@@ -753,11 +753,16 @@ SgStatus w4_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, void
     ki = 8 + si;
     kfn = knarrow[zi][si];
   }
+  // the shared-memory opt-in belongs to each device's copy of the kernel
   static std::mutex mu;
-  static size_t attr_smem[2][13] = {};
+  static size_t attr_smem[64][2][13] = {};
   {
+    int dev = 0;
+    const SgStatus dst = sg::current_device(&dev);
+    if (dst != SG_OK) return dst;
     std::lock_guard<std::mutex> lk(mu);
-    size_t& done = attr_smem[zi][ki];
+    size_t scratch = 0;
+    size_t& done = dev >= 0 && dev < 64 ? attr_smem[dev][zi][ki] : scratch;
     if (done < pl.smem) {
       cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
       if (e != cudaSuccess) {
