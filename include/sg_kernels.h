@@ -128,9 +128,11 @@ const char* sg_last_error(void);
 int32_t sg_version(void);       /* (major << 16) | (minor << 8) | patch */
 /* Number of CUDA devices usable by the library (0 when none). */
 int32_t sg_device_count(void);
-/* Read and clear the device-side error word of the current device (waits on
- * `stream`).  Kernels whose internal waits are bounded record a timeout there
- * instead of hanging; returns SG_ERR_RUNTIME with a message if one was set. */
+/* Read and clear the device-side error words of the current device (waits on
+ * `stream`): the library's own and the one sg_matmul_int4_grouped_noalloc
+ * gives its kernels.  Kernels whose internal waits are bounded record a timeout
+ * there instead of hanging; returns SG_ERR_RUNTIME with a message if one was
+ * set.  Allocates no device memory. */
 int32_t sg_device_error_check(void* stream);
 /* Override a launch heuristic (benchmark sweeps).  Keys:
  *   "w4_gemv.groups_per_warp"  INT4 GEMV (CUDA-core path) split-K granularity (0 = heuristic)
@@ -176,7 +178,8 @@ size_t sg_matmul_int4_grouped_workspace_size(const SgMatMulParams* p);
  * (make it before any stream capture on that device).  Problems needing more
  * than 2 MiB of scratch are rejected with SG_ERR_INVALID.  p->workspace is
  * ignored.  Calls share the array: calls that overlap on the GPU race, so
- * order them on one stream.
+ * order them on one stream.  A bounded wait that runs out inside it is
+ * reported by sg_device_error_check, like any other kernel's.
  */
 SgStatus sg_matmul_int4_grouped_noalloc(const SgMatMulParams* p, void* stream);
 

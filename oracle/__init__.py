@@ -38,12 +38,17 @@ _lib = None
 _ref = None
 
 
-def build(ref: bool | None = None) -> None:
-    """Compile the restatement (and the reference kernels when the reference
-    checkout is present, or when ``ref`` is True)."""
+def build(ref: bool | None = None, refdir: str | None = None) -> None:
+    """Compile the restatement, and the reference's own kernels when a
+    reference checkout is named (``refdir``, else the ``SG_REFERENCE_DIR``
+    environment variable) and present, or when ``ref`` is True (then a missing
+    checkout is an error)."""
     subprocess.run(["make", "-s", "-C", _HERE], check=True)
-    refdir = os.environ.get("SG_REFERENCE_DIR", "/root/reference")
-    if ref or (ref is None and os.path.isdir(os.path.join(refdir, "compiler", "kernels", "cpu"))):
+    refdir = refdir or os.environ.get("SG_REFERENCE_DIR")
+    present = bool(refdir) and os.path.isdir(os.path.join(refdir, "compiler", "kernels", "cpu"))
+    if ref and not present:
+        raise FileNotFoundError("the reference checkout is needed: pass refdir or set SG_REFERENCE_DIR")
+    if present and ref is not False:
         subprocess.run(["make", "-s", "-C", _HERE, "ref", f"REF={refdir}"], check=True)
 
 

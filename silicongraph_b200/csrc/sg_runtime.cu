@@ -132,6 +132,12 @@ SgStatus device_error_word(int** out) {
   return SG_OK;
 }
 
+int* existing_device_error_word(int dev) {
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  auto it = g_err_word.find(dev);
+  return it == g_err_word.end() ? nullptr : it->second;
+}
+
 SgStatus make_tensor_map(CUtensorMap* out, CUtensorMapDataType dt, int rank, void* base, const uint64_t* dims,
                          const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz) {
   {
@@ -172,20 +178,32 @@ SgStatus make_tensor_map(CUtensorMap* out, CUtensorMapDataType dt, int rank, voi
 extern "C" {
 
 int32_t sg_device_error_check(void* stream) {
-  int* w = nullptr;
-  if (sg::device_error_word(&w) != SG_OK) return SG_ERR_RUNTIME;
-  int v = 0;
+  // Two words can hold a device-side error: the library's own (created on a
+  // device's first launch that needs it) and the one the allocation-free GEMV
+  // passes its kernels.  A word that does not exist yet has recorded nothing,
+  // so this check allocates no device memory.
+  int dev = 0;
+  if (sg::current_device(&dev) != SG_OK) return SG_ERR_RUNTIME;
+  int* words[2] = {sg::existing_device_error_word(dev), sg::noalloc_error_word(dev)};
   cudaStream_t cs = static_cast<cudaStream_t>(stream);
-  if (cudaMemcpyAsync(&v, w, sizeof(int), cudaMemcpyDeviceToHost, cs) != cudaSuccess ||
-      cudaStreamSynchronize(cs) != cudaSuccess) {
-    cudaGetLastError();
-    sg::set_error("sg_device_error_check: copy failed");
-    return SG_ERR_RUNTIME;
+  int first = 0;
+  for (int* w : words) {
+    if (!w) continue;
+    int v = 0;
+    if (cudaMemcpyAsync(&v, w, sizeof(int), cudaMemcpyDeviceToHost, cs) != cudaSuccess ||
+        cudaStreamSynchronize(cs) != cudaSuccess) {
+      cudaGetLastError();
+      sg::set_error("sg_device_error_check: copy failed");
+      return SG_ERR_RUNTIME;
+    }
+    if (v != 0) {
+      cudaMemsetAsync(w, 0, sizeof(int), cs);
+      cudaStreamSynchronize(cs);
+      if (first == 0) first = v;
+    }
   }
-  if (v != 0) {
-    cudaMemsetAsync(w, 0, sizeof(int), cs);
-    cudaStreamSynchronize(cs);
-    sg::set_error("device-side error %d (1 = a bounded wait timed out)", v);
+  if (first != 0) {
+    sg::set_error("device-side error %d (1 = a bounded wait timed out)", first);
     return SG_ERR_RUNTIME;
   }
   return SG_OK;

@@ -387,6 +387,11 @@ __device__ __forceinline__ void mma_u8s8_16832(int (&d)[4], uint32_t a0, uint32_
 namespace sg {
 // Per-device error word written by bounded waits (allocated on first use).
 SgStatus device_error_word(int** out);
+// The library's error word on `dev` if it exists yet, else nullptr (no allocation).
+int* existing_device_error_word(int dev);
+// The allocation-free GEMV's error word on `dev` once that device has served its
+// first call, else nullptr (w4_gemv_noalloc.cu).
+int* noalloc_error_word(int dev);
 // Host: encode a 2D/3D tiled tensor map through the driver entry point.
 // dims in elements (innermost first), strides in bytes, box in elements.
 SgStatus make_tensor_map(CUtensorMap* out, CUtensorMapDataType dt, int rank, void* base, const uint64_t* dims,

@@ -24,7 +24,9 @@
 // ticket counters it relies on before its kernel runs, and calls that overlap
 // on the GPU (for example on two streams at once) race on the array -- order
 // them on one stream.  No cudaMalloc, cudaFree or allocating library routine
-// is called.
+// is called.  A bounded wait that runs out in these kernels sets this file's
+// own error word, which sg_device_error_check reads and clears together with
+// the library's (that check allocates nothing either).
 #include <mutex>
 
 #include "sm100.cuh"
@@ -82,6 +84,12 @@ SgStatus device_slot(int dev, DeviceSlot** out) {
 }  // namespace
 
 namespace sg {
+int* noalloc_error_word(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mu);
+  return g_slots[dev].ready ? g_slots[dev].err : nullptr;
+}
+
 SgStatus w4_gemv_run(const SgMatMulParams* p, void* stream, void* ws, size_t ws_bytes, bool ws_external,
                      int* err_word);
 size_t w4_gemv_scratch_bytes(const SgMatMulParams* p);

@@ -159,9 +159,12 @@ def gen_block_ops(R):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("SG_REFERENCE_DIR", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("SG_REFERENCE_DIR"),
+                    help="the reference checkout (default: $SG_REFERENCE_DIR)")
     args = ap.parse_args()
-    oracle.build(ref=True)
+    if not args.reference:
+        ap.error("name the reference checkout with --reference or SG_REFERENCE_DIR")
+    oracle.build(ref=True, refdir=args.reference)
     R = oracle.ref()
     gen_int4_gemv(R)
     gen_quant_params(args.reference)

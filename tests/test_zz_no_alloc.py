@@ -47,6 +47,8 @@ def test_noalloc_matches_allocating_entry_point_twice(sg, oracle_mod, K, N, gs, 
         assert st_ref == 0, _lib.last_error()
         st, got = _call(lib, "sg_matmul_int4_grouped_noalloc", x, B, S, Z, K, N, gs, M)
         assert st == 0, _lib.last_error()
+        # a timed-out wait inside the allocation-free kernels is reported here
+        assert lib.sg_device_error_check(torch.cuda.current_stream().cuda_stream) == 0, _lib.last_error()
         torch.cuda.synchronize()
         g, w = got.cpu().numpy(), want.cpu().numpy()
         err = np.abs(g - w)
