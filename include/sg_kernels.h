@@ -193,10 +193,10 @@ SgStatus sg_matmul_int4_grouped_noalloc(const SgMatMulParams* p, void* stream);
  *                     (the shader's exact arithmetic; c_dtype DEFAULT = F32)
  * a_dtype F32/F16/BF16: weight-only variant C[m,n] = scales_B[n] * sum_k A*B
  *                     in fp32 (scale_A unused).  Few rows (decode): each row's
- *                     activations are taken as 16-bit fixed point with one
- *                     power-of-two scale per 8 consecutive k (error below 2^-14
- *                     of the largest |A| among them, or 2^-114 absolute where
- *                     that is below 2^-100) and reduced exactly in
+ *                     activations are taken as 24-bit fixed point with one
+ *                     power-of-two scale per 8 consecutive k (error at most
+ *                     2^-22 of the largest |A| among them, or 2^-122 absolute
+ *                     where that is below 2^-100) and reduced exactly in
  *                     int32; many rows: the tcgen05 GEMM in fp32 accumulation.
  */
 SgStatus sg_matmul_int8_channel(const SgMatMulParams* p, void* stream);

@@ -96,6 +96,8 @@ def ref() -> ctypes.CDLL:
             getattr(R, pre + "rope").argtypes = [_P, _I, _I, _F]
             getattr(R, pre + "flash_attn_head").argtypes = [_P, _P, _P, _P, _I, _I, _F, _I, _I]
             getattr(R, pre + "flash_attention_fp16").argtypes = [_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _I]
+        # the OpenCL-C gemm_int8_m1 kernel run as host C (ref_opencl.c)
+        R.sgref_cl_gemm_int8_m1.argtypes = [_P, _P, _P, _P, _I, _I, _F]
         _ref = R
     return _ref
 

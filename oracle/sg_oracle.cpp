@@ -92,24 +92,46 @@ void orc_matmul_int4_grouped(const void* A, int a_dt, const uint8_t* B, const ui
   const int32_t gs = (group_size > 0) ? group_size : 128;
   if (lda <= 0) lda = K;
   if (ldc <= 0) ldc = N;
+  // Every column n gets the reference's sequence of fp32 operations in
+  // ascending k (per k pair: acc += a0 * w0f, then acc += a1 * w1f, or + 0.0f
+  // past an odd K); the loops only visit the columns side by side (k outer,
+  // n inner) so that the oracle streams its rows and vectorises.  Each
+  // column's accumulator is independent, so the results are the same bits.
+  std::vector<float> acc((size_t)N), sc((size_t)N), zf((size_t)N);
   for (int32_t m = 0; m < M; ++m) {
-    for (int32_t n = 0; n < N; ++n) {
-      float acc = 0.0f;
-      for (int32_t k = 0; k < K; k += 2) {
-        const uint8_t packed = B[(int64_t)(k / 2) * N + n];
-        const int8_t w0 = (int8_t)((packed & 0x0F) - 8);
-        const int8_t w1 = (int8_t)((packed >> 4) - 8);
-        const int32_t group = k / gs;
-        const float scale = h2f(scales[(int64_t)group * N + n]);
-        const int8_t zero = zeros ? zeros[(int64_t)group * N + n] : 0;
-        const float w0f = scale * (float)(w0 - zero);
-        const float w1f = scale * (float)(w1 - zero);
-        acc += load_act(A, a_dt, (int64_t)m * lda + k) * w0f;
-        acc += (k + 1 < K) ? (load_act(A, a_dt, (int64_t)m * lda + k + 1) * w1f) : 0.0f;
+    std::fill(acc.begin(), acc.end(), 0.0f);
+    int32_t cur_group = -1;
+    for (int32_t k = 0; k < K; k += 2) {
+      const int32_t group = k / gs;
+      if (group != cur_group) {
+        cur_group = group;
+        for (int32_t n = 0; n < N; ++n) {
+          sc[n] = h2f(scales[(int64_t)group * N + n]);
+          zf[n] = zeros ? (float)zeros[(int64_t)group * N + n] : 0.0f;
+        }
       }
-      if (a_dt == DT_DEFAULT || a_dt == DT_I8) acc = acc * scale_A;
-      if (bias) acc = acc + h2f(bias[n]);
-      store_out(C, c_dt, (int64_t)m * ldc + n, acc);
+      const uint8_t* row = B + (int64_t)(k / 2) * N;
+      const float a0 = load_act(A, a_dt, (int64_t)m * lda + k);
+      const bool odd = k + 1 < K;
+      const float a1 = odd ? load_act(A, a_dt, (int64_t)m * lda + k + 1) : 0.0f;
+      float* ac = acc.data();
+      const float* scp = sc.data();
+      const float* zp = zf.data();
+      for (int32_t n = 0; n < N; ++n) {
+        const uint8_t packed = row[n];
+        // (w - zero) is an exact small integer either way: (float)(int) == float - float
+        const float w0f = scp[n] * ((float)((int)(packed & 0x0F) - 8) - zp[n]);
+        const float w1f = scp[n] * ((float)((int)(packed >> 4) - 8) - zp[n]);
+        float v = ac[n] + a0 * w0f;
+        v = v + (odd ? a1 * w1f : 0.0f);
+        ac[n] = v;
+      }
+    }
+    for (int32_t n = 0; n < N; ++n) {
+      float v = acc[n];
+      if (a_dt == DT_DEFAULT || a_dt == DT_I8) v = v * scale_A;
+      if (bias) v = v + h2f(bias[n]);
+      store_out(C, c_dt, (int64_t)m * ldc + n, v);
     }
   }
 }

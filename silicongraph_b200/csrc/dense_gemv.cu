@@ -15,12 +15,15 @@
 //   * int8 A: four rows of a lane are transposed 4x4 bytes with PRMT so each
 //     32-bit word holds one column's four k values, then dp4a accumulates in
 //     int32 -- exact, hence bit-identical to the shader for any split.
-//   * float A (int8 weights): x is staged as 16-bit fixed point per 8-row chunk
-//     (one power-of-two scale per chunk, |error| below 2^-14 of the chunk's
-//     largest |x|, or 2^-114 when that is below 2^-100 and the exponent is
-//     clamped), split into signed hi / lo bytes; the weights meet both in
-//     dp4a (exact int32) after the same 4x4 transpose, and each chunk adds
-//     scale * (256 hi_sum + lo_sum) to the fp32 accumulators.
+//   * float A (int8 weights): x is staged as 24-bit fixed point per 8-row chunk
+//     (one power-of-two scale per chunk, |error| at most 2^-22 of the chunk's
+//     largest |x|, or 2^-122 when that is below 2^-100 and the exponent is
+//     clamped), split into signed hi / mid / lo bytes; the weights meet all
+//     three in dp4a (exact int32) after the same 4x4 transpose, and each
+//     chunk adds scale * (256 (256 hi_sum + mid_sum) + lo_sum) to the fp32
+//     accumulators.  (16 bits were not enough: with one outlier of 100..1000
+//     among the activations, columns whose sum nearly cancels missed
+//     2e-3 + 1e-2 |y|.)
 //   * fp16 B: half2 -> float2 conversion and packed fp32x2 FMAs.
 #include <algorithm>
 #include <atomic>
@@ -122,12 +125,13 @@ __global__ void __launch_bounds__(KIND == W_F16 ? kThreads : kI8Warps * 32, KIND
       xq[i] = (int32_t)v;
     }
   } else if (KIND == W_INT8_FA) {
-    // float activations as 16-bit fixed point per 8-row chunk: x = 2^(E-13) q, E the
-    // exponent of the chunk's largest |x| (|q| <= 2^14, error below 2^-14 of that
-    // value), q = 256 hi + lo in signed bytes, so the weights meet them in dp4a
+    // float activations as 24-bit fixed point per 8-row chunk: x = 2^(E-21) q, E the
+    // exponent of the chunk's largest |x| (|q| <= 2^22, error at most 2^-22 of that
+    // value), q = 65536 hi + 256 mid + lo in signed bytes, so the weights meet them in dp4a
     int8_t* xhi = reinterpret_cast<int8_t*>(xs_f);
-    int8_t* xlo = xhi + nrows_pad;
-    float* sx = reinterpret_cast<float*>(xhi + 2 * nrows_pad);
+    int8_t* xmid = xhi + nrows_pad;
+    int8_t* xlo = xhi + 2 * nrows_pad;
+    float* sx = reinterpret_cast<float*>(xhi + 3 * nrows_pad);
     const int lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < (nrows_pad + T - 1) / T * T; i += T) {
       const int k = r_begin + i;
@@ -136,12 +140,14 @@ __global__ void __launch_bounds__(KIND == W_F16 ? kThreads : kI8Warps * 32, KIND
 #pragma unroll
       for (int o = 1; o < 8; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
       const int E = max((__float_as_int(m) >> 23) - 127, -100);
-      const int q = __float2int_rn(x * __int_as_float((127 + 13 - E) << 23));
-      const int lo = ((q + 128) & 255) - 128, hi = (q - lo) >> 8;
+      const int q = __float2int_rn(x * __int_as_float((127 + 21 - E) << 23));
+      const int lo = ((q + 128) & 255) - 128, r = (q - lo) >> 8;
+      const int mid = ((r + 128) & 255) - 128, hi = (r - mid) >> 8;
       if (i < nrows_pad) {
         xhi[i] = (int8_t)hi;
+        xmid[i] = (int8_t)mid;
         xlo[i] = (int8_t)lo;
-        if ((lane & 7) == 0) sx[i / 8] = __int_as_float((127 - 13 + E) << 23);  // 2^(E - 13)
+        if ((lane & 7) == 0) sx[i / 8] = __int_as_float((127 - 21 + E) << 23);  // 2^(E - 21)
       }
     }
   } else {
@@ -248,16 +254,17 @@ __global__ void __launch_bounds__(KIND == W_F16 ? kThreads : kI8Warps * 32, KIND
           }
         }
       } else {
-        // exact int32 dot products with the hi and lo bytes of this chunk's fixed-point x
+        // exact int32 dot products with the hi, mid and lo bytes of this chunk's fixed-point x
         const int32_t* xh = reinterpret_cast<const int32_t*>(xs_f);
-        const int32_t* xl = reinterpret_cast<const int32_t*>(reinterpret_cast<const int8_t*>(xs_f) + nrows_pad);
-        const float* sx = reinterpret_cast<const float*>(reinterpret_cast<const int8_t*>(xs_f) + 2 * nrows_pad);
-        int ah[16], al[16];
+        const int32_t* xm = reinterpret_cast<const int32_t*>(reinterpret_cast<const int8_t*>(xs_f) + nrows_pad);
+        const int32_t* xl = reinterpret_cast<const int32_t*>(reinterpret_cast<const int8_t*>(xs_f) + 2 * nrows_pad);
+        const float* sx = reinterpret_cast<const float*>(reinterpret_cast<const int8_t*>(xs_f) + 3 * nrows_pad);
+        int ah[16], am[16], al[16];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) ah[c] = al[c] = 0;
+        for (int c = 0; c < 16; ++c) ah[c] = am[c] = al[c] = 0;
 #pragma unroll
         for (int r4 = 0; r4 < kRowsPerChunk; r4 += 4) {
-          const int32_t h4 = xh[(ch + r4) / 4], l4 = xl[(ch + r4) / 4];
+          const int32_t h4 = xh[(ch + r4) / 4], m4 = xm[(ch + r4) / 4], l4 = xl[(ch + r4) / 4];
           const uint32_t rows[4][4] = {{wv[r4].x, wv[r4].y, wv[r4].z, wv[r4].w},
                                        {wv[r4 + 1].x, wv[r4 + 1].y, wv[r4 + 1].z, wv[r4 + 1].w},
                                        {wv[r4 + 2].x, wv[r4 + 2].y, wv[r4 + 2].z, wv[r4 + 2].w},
@@ -269,13 +276,15 @@ __global__ void __launch_bounds__(KIND == W_F16 ? kThreads : kI8Warps * 32, KIND
 #pragma unroll
             for (int b = 0; b < 4; ++b) {
               ah[4 * q + b] = __dp4a((int)cw[b], h4, ah[4 * q + b]);
+              am[4 * q + b] = __dp4a((int)cw[b], m4, am[4 * q + b]);
               al[4 * q + b] = __dp4a((int)cw[b], l4, al[4 * q + b]);
             }
           }
         }
         const float sc = sx[ch / kRowsPerChunk];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) accf[c] = fmaf((float)(ah[c] * 256 + al[c]), sc, accf[c]);
+        for (int c = 0; c < 16; ++c)  // |256 ah + am| <= 2^24 + 2^16: int32, one rounding as a float
+          accf[c] = fmaf(fmaf(256.f, (float)(ah[c] * 256 + am[c]), (float)al[c]), sc, accf[c]);
       }
     }
     sgd::cp_async_wait<0>();

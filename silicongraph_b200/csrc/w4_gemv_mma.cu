@@ -12,19 +12,24 @@
 //     of packed weights (128-byte swizzle), the chunk's two scale rows and two
 //     zero-point rows.
 // Math side (few instructions per weight):
-//   * The activation is staged once per block as 16-bit fixed point with one
-//     power-of-two scale per 32 k (x = 2^(E-13) x_q, E the exponent of the
-//     largest |x| there, so |x_q| <= 2^14 and the rounding error is below
-//     2^-15 of that largest value), split as x_q = 256 hi + lo, signed bytes.
+//   * The activation is staged once per block as 24-bit fixed point with one
+//     power-of-two scale per 32 k (x = 2^(E-21) x_q, E the exponent of the
+//     largest |x| there, so |x_q| <= 2^22 and the rounding error is below
+//     2^-23 of that largest value), split as x_q = 65536 hi + 256 mid + lo,
+//     signed bytes.  (16 bits were not enough: with one outlier of 100..1000
+//     per 32 k, columns whose sum nearly cancels missed 2e-3 + 1e-2 |y|.)
 //   * A 32-bit word (4 columns x one k pair, low nibble = even k) gives the
 //     unsigned bytes of both k with one shift and two AND masks.  mma.sync
 //     m16n8k32 (u8 x s8 -> exact int32) reduces over k: A rows are words of
 //     4 columns, A k-slots their columns at 4 k-pair rows x even/odd k, and
-//     B column 2e + v carries hi (v = 0) or lo (v = 1) of x at column slot e
-//     and zero elsewhere, so every D entry is one column's hi or lo partial
-//     dot product and every lane owns 4 columns outright.
-//   * Per 32-k half and column (exact integers until the last step):
-//     acc += scale * 2^(E-13) * (256 D_hi + D_lo - (8 + zero) * sum x_q).
+//     B column 2e + v carries hi (v = 0) or mid (v = 1) of x at column slot
+//     e and zero elsewhere, so every D entry is one column's hi or mid
+//     partial dot product and every lane owns 4 columns outright; a second
+//     MMA on the same A fragments takes lo (v = 0; v = 1 is zero).
+//   * Per 32-k half and column, with S_hm = sum (x_q >> 8) and S_lo = sum lo
+//     (integers exact in int32 until the last two roundings):
+//     acc += scale * 2^(E-21) * (256 (256 D_hi + D_mid - (8 + zero) S_hm)
+//                                + D_lo - (8 + zero) S_lo).
 //   * Rows are assigned to the 4 lanes of a quad so that their (row mod 8)
 //     values differ by 2: with the 128-byte swizzle the 8 lanes of a quarter
 //     warp hit 8 distinct 16-byte bank groups (no bank conflicts).
@@ -72,7 +77,7 @@ constexpr int off_x(int warps, int stages) { return off_sz(warps, stages) + warp
 // word per k-pair row, scale and sum per half chunk), the stage barriers, the
 // cluster's [rank][column] partials (rank 0's copy is the one used), then the
 // per-segment, per-phase partial sums.
-constexpr size_t kXSlotBytes = (size_t)kRows * 4 + 2 * 8;
+constexpr size_t kXSlotBytes = (size_t)kRows * 8 + 2 * 16;
 inline size_t tail_bytes(int warps, int stages, int strips, int x_slots, int max_segs, int ksplit) {
   const size_t cols = (size_t)strips * 128;
   return (size_t)x_slots * kXSlotBytes + (size_t)warps * stages * 8 + (size_t)ksplit * cols * 4 +
@@ -167,8 +172,8 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS <= 8 ? 2 : 1)
   constexpr int kOffW = 0, kOffSZ = off_sz(WARPS, STAGES), kOffX = off_x(WARPS, STAGES);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = sgd::align_smem_1024(smem_raw);
-  uint32_t* xst = reinterpret_cast<uint32_t*>(smem + kOffX);         // [slot][32 rows]: x_q bytes
-  int2* xgrp = reinterpret_cast<int2*>(xst + a.x_slots * kRows);       // [slot][half]: scale bits, sum x_q
+  uint2* xst = reinterpret_cast<uint2*>(smem + kOffX);               // [slot][32 rows]: x_q bytes
+  int4* xgrp = reinterpret_cast<int4*>(xst + a.x_slots * kRows);     // [slot][half]: scale bits, S_hm, S_lo
   uint64_t* bars = reinterpret_cast<uint64_t*>(xgrp + a.x_slots * 2);
   float* csum = reinterpret_cast<float*>(bars + kWarps * kStages);  // cluster: [rank][kTC]
   float* red = csum + (CLUSTER ? a.ksplit * kTC : 0);                // [seg][phase][kTC]
@@ -271,12 +276,13 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS <= 8 ? 2 : 1)
     for (int i = 0; i < min(kStages, n_my); ++i) issue(i);
   }
 
-  // ---- stage the activation as 16-bit fixed point, one power-of-two scale
-  //      per half chunk (32 k): x = 2^(E-13) x_q with E the exponent of the
-  //      half's largest |x|, so |x_q| <= 2^14, written as x_q = 256 hi + lo
-  //      with hi, lo signed bytes.  Per k-pair row one word [hi_even, hi_odd,
-  //      lo_even, lo_odd]; per half the scale and sum_k x_q.  A half is 16
-  //      rows = 16 lanes (rows per pass are a multiple of 32: whole warps).
+  // ---- stage the activation as 24-bit fixed point, one power-of-two scale
+  //      per half chunk (32 k): x = 2^(E-21) x_q with E the exponent of the
+  //      half's largest |x|, so |x_q| <= 2^22, written as x_q = 65536 hi +
+  //      256 mid + lo with hi, mid, lo signed bytes.  Per k-pair row two words
+  //      [hi_even, hi_odd, mid_even, mid_odd], [lo_even, lo_odd, 0, 0]; per
+  //      half the scale, S_hm = sum_k (x_q >> 8) and S_lo = sum_k lo.  A half
+  //      is 16 rows = 16 lanes (rows per pass are a multiple of 32: whole warps).
   for (int idx = threadIdx.x, j = 0; idx < nslots * kRows; idx += kThreads, ++j) {
     int k;
     slot_row(idx, k);
@@ -291,28 +297,36 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS <= 8 ? 2 : 1)
     float m = fmaxf(fabsf(xe), fabsf(xo));
 #pragma unroll
     for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const int E = max((__float_as_int(m) >> 23) - 127, -100);  // m >= 0; tiny halves clamp
-    const float inv = __int_as_float((127 + 13 - E) << 23);      // 2^(13 - E), exact scaling
-    const float sxv = __int_as_float((127 - 13 + E) << 23);      // 2^(E - 13)
+    // m >= 0; tiny halves clamp (2^(21+100) and 2^(-100-21) are normal floats)
+    const int E = max((__float_as_int(m) >> 23) - 127, -100);
+    const float inv = __int_as_float((127 + 21 - E) << 23);      // 2^(21 - E), exact scaling
+    const float sxv = __int_as_float((127 - 21 + E) << 23);      // 2^(E - 21)
     const int qe = __float2int_rn(xe * inv), qo = __float2int_rn(xo * inv);
     const int le = ((qe + 128) & 255) - 128, lo = ((qo + 128) & 255) - 128;
-    const int he = (qe - le) >> 8, ho = (qo - lo) >> 8;
-    xst[idx] = (uint32_t)(he & 255) | ((uint32_t)(ho & 255) << 8) | ((uint32_t)(le & 255) << 16) |
-               ((uint32_t)(lo & 255) << 24);
-    int sq = qe + qo;
+    const int re = (qe - le) >> 8, ro = (qo - lo) >> 8;  // 256 hi + mid, exact
+    const int me = ((re + 128) & 255) - 128, mo = ((ro + 128) & 255) - 128;
+    const int he = (re - me) >> 8, ho = (ro - mo) >> 8;
+    xst[idx] = make_uint2((uint32_t)(he & 255) | ((uint32_t)(ho & 255) << 8) | ((uint32_t)(me & 255) << 16) |
+                              ((uint32_t)(mo & 255) << 24),
+                          (uint32_t)(le & 255) | ((uint32_t)(lo & 255) << 8));
+    int shm = re + ro, slo = le + lo;
 #pragma unroll
-    for (int o = 1; o < 16; o <<= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    if ((lane & 15) == 0) xgrp[idx >> 4] = make_int2(__float_as_int(sxv), sq);
+    for (int o = 1; o < 16; o <<= 1) {
+      shm += __shfl_xor_sync(0xffffffffu, shm, o);
+      slo += __shfl_xor_sync(0xffffffffu, slo, o);
+    }
+    if ((lane & 15) == 0) xgrp[idx >> 4] = make_int4(__float_as_int(sxv), shm, slo, 0);
   }
   __syncthreads();
 
   // ---- lane roles in mma.sync m16n8k32 (A u8 row-major, B s8 col-major):
   //      A row m = g (m + 8) is the word of columns 16g + 8jm + 0..3 (+ 4..7)
   //      of k-pair row r_t, A k-slot 4t + e (16 + 4t + e) its column e at the
-  //      even (odd) k; B column n = 2e + v holds variant v (hi / lo) of x at
-  //      k-slot 4t + e, zero elsewhere.  D[m][2t] / D[m][2t + 1] are then the
-  //      hi / lo partial dot products of column t of the word: every lane
-  //      owns columns 16g + t + 4i, i = 0..3, with no cross-lane reduction.
+  //      even (odd) k; B column n = 2e + v holds byte v of a staged word of
+  //      x at k-slot 4t + e, zero elsewhere: hi / mid from the first word,
+  //      lo / zero from the second.  D[m][2t] / D[m][2t + 1] are then those
+  //      partial dot products of column t of the word: every lane owns
+  //      columns 16g + t + 4i, i = 0..3, with no cross-lane reduction.
   const int g = lane >> 2, t = lane & 3;
   const int be = g >> 1, bv = g & 1;  // as B provider: column n = g
   const uint32_t sel_e = (0x4444u & ~(0xFu << (4 * be))) | ((uint32_t)(2 * bv) << (4 * be));
@@ -360,45 +374,52 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS <= 8 ? 2 : 1)
       break;
     }
     const uint8_t* wst = smem + kOffW + (warp * kStages + s) * kWBytes;
-    const uint8_t* xr = reinterpret_cast<const uint8_t*>(xst + sl * kRows) + 8 * t;  // row 2t
-    int d[2][2][4];  // [half][jm][fragment]
+    const uint8_t* xr = reinterpret_cast<const uint8_t*>(xst + sl * kRows) + 16 * t;  // row 2t
+    int d[2][2][4];  // [half][jm][fragment]: hi, mid
+    int e[2][2][4];  // [half][jm][fragment]: lo, zero
 #pragma unroll
     for (int h = 0; h < 2; ++h)
 #pragma unroll
       for (int jm = 0; jm < 2; ++jm)
 #pragma unroll
-        for (int q = 0; q < 4; ++q) d[h][jm][q] = 0;
+        for (int q = 0; q < 4; ++q) d[h][jm][q] = e[h][jm][q] = 0;
 #pragma unroll
     for (int st = 0; st < 8; ++st) {
       const int base = 16 * (st >> 2) + 8 * ((st >> 1) & 1) + (st & 1);
       const uint4 wv = *reinterpret_cast<const uint4*>(wst + base * 128 + ((st & 1) ? woff1 : woff0));
-      const uint32_t X = *reinterpret_cast<const uint32_t*>(xr + base * 4);
-      const uint32_t b0 = __byte_perm(X, 0u, sel_e), b1 = __byte_perm(X, 0u, sel_o);
+      const uint2 X = *reinterpret_cast<const uint2*>(xr + base * 8);
+      const uint32_t b0 = __byte_perm(X.x, 0u, sel_e), b1 = __byte_perm(X.x, 0u, sel_o);
+      const uint32_t c0 = __byte_perm(X.y, 0u, sel_e), c1 = __byte_perm(X.y, 0u, sel_o);
       const int h = st >> 2;
-      sgd::mma_u8s8_16832(d[h][0], wv.x & 0x0F0F0F0Fu, wv.y & 0x0F0F0F0Fu, (wv.x >> 4) & 0x0F0F0F0Fu,
-                          (wv.y >> 4) & 0x0F0F0F0Fu, b0, b1);
-      sgd::mma_u8s8_16832(d[h][1], wv.z & 0x0F0F0F0Fu, wv.w & 0x0F0F0F0Fu, (wv.z >> 4) & 0x0F0F0F0Fu,
-                          (wv.w >> 4) & 0x0F0F0F0Fu, b0, b1);
+      const uint32_t a0 = wv.x & 0x0F0F0F0Fu, a1 = wv.y & 0x0F0F0F0Fu, a2 = (wv.x >> 4) & 0x0F0F0F0Fu,
+                     a3 = (wv.y >> 4) & 0x0F0F0F0Fu;
+      const uint32_t a4 = wv.z & 0x0F0F0F0Fu, a5 = wv.w & 0x0F0F0F0Fu, a6 = (wv.z >> 4) & 0x0F0F0F0Fu,
+                     a7 = (wv.w >> 4) & 0x0F0F0F0Fu;
+      sgd::mma_u8s8_16832(d[h][0], a0, a1, a2, a3, b0, b1);
+      sgd::mma_u8s8_16832(d[h][1], a4, a5, a6, a7, b0, b1);
+      sgd::mma_u8s8_16832(e[h][0], a0, a1, a2, a3, c0, c1);
+      sgd::mma_u8s8_16832(e[h][1], a4, a5, a6, a7, c0, c1);
     }
     // ---- chunk epilogue per half and column:
-    //      acc += scale * 2^(E-13) * (256 D_hi + D_lo - (8 + zero) * sum x_q)
+    //      acc += scale * 2^(E-21) * (256 (256 D_hi + D_mid - (8 + zero) S_hm) + D_lo - (8 + zero) S_lo)
+    //      |256 D_hi + D_mid - (8 + zero) S_hm| < 2^24: exact in int32 and as a float
     const uint8_t* szs = smem + kOffSZ + (warp * kStages + s) * kSZBytes;
     const int k0 = 2 * crow * kRows;
     const int gA = group_of(a, k0), gB = group_of(a, k0 + 32);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int srow = h ? (gB - gA) : 0;
-      const int2 xg = xgrp[sl * 2 + h];
+      const int4 xg = xgrp[sl * 2 + h];
       const float sxh = __int_as_float(xg.x);
       const __half* sc_row = reinterpret_cast<const __half*>(szs + srow * 256) + 16 * g + t;
       const int8_t* z_row = reinterpret_cast<const int8_t*>(szs + kSBytes + srow * 128) + 16 * g + t;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int jm = i >> 1, fr = (i & 1) * 2;
-        const int y = d[h][jm][fr] * 256 + d[h][jm][fr + 1];
         const int z8 = HAS_Z ? 8 + (int)z_row[4 * i] : 8;
-        const int tq = y - z8 * xg.y;
-        acc[i] = fmaf(__half2float(sc_row[4 * i]) * sxh, (float)tq, acc[i]);
+        const int hm = d[h][jm][fr] * 256 + d[h][jm][fr + 1] - z8 * xg.y;
+        const int lw = e[h][jm][fr] - z8 * xg.z;
+        acc[i] = fmaf(__half2float(sc_row[4 * i]) * sxh, fmaf(256.f, (float)hm, (float)lw), acc[i]);
       }
     }
     __syncwarp();

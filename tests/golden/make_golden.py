@@ -11,6 +11,9 @@ Every expected output here comes from the reference's own code:
     into oracle/_ref/libsg_ref.so -- NEON branches through oracle/neon_shim
     (the INT4 loop exists only there, matmul_neon.h:114-142) and the scalar
     branches;
+  * INT8 per-channel GEMV: the reference's OpenCL-C kernel gemm_int8_m1
+    (compiler/kernels/gpu/opencl_kernels.h:36-52), cut out of its string
+    literal and compiled as host C into the same library (oracle/ref_opencl.c);
   * INT4 quantisation parameters: python/armcc/calibration.py's
     CalibrationStats.computeQuantParams (imported from the reference).
 Inputs are seeded numpy draws (default_rng(seed)); the INT4 weight bytes are
@@ -135,6 +138,32 @@ def gen_attention(R):
     np.savez_compressed(os.path.join(HERE, "attn_f32_head.npz"), Q=Q, K=K, V=V, O=O, scale=1.0 / 8.0)
 
 
+def gen_int8_channel(R):
+    cases = [
+        # name, K, N, scale_A
+        ("k37_n20", 37, 20, 0.5),
+        ("k256_n64", 256, 64, 0.02),
+        ("k1000_n40", 1000, 40, 1.0),
+        ("k2048_n24", 2048, 24, 0.0078125),
+    ]
+    d = {}
+    for i, (name, K, N, scale_A) in enumerate(cases):
+        rng = np.random.default_rng(500 + i)
+        A = rng.integers(-128, 128, K, dtype=np.int8)
+        B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+        if i == 3:  # extremes: every product at its largest magnitude in some columns
+            A[:] = -128
+            B[:, :8] = -128
+            B[:, 8:16] = 127
+        s = (rng.random(N) * 0.01).astype(np.float32)
+        C = np.zeros(N, np.float32)
+        R.sgref_cl_gemm_int8_m1(p(A), p(B), p(s), p(C), K, N, scale_A)
+        d.update({f"{name}_A": A, f"{name}_B": B, f"{name}_s": s, f"{name}_C": C,
+                  f"{name}_scale_A": np.float32(scale_A)})
+    d["cases"] = np.array([c[0] for c in cases])
+    np.savez_compressed(os.path.join(HERE, "int8_channel.npz"), **d)
+
+
 def gen_block_ops(R):
     rng = np.random.default_rng(33)
     n = 100
@@ -161,16 +190,19 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SG_REFERENCE_DIR"),
                     help="the reference checkout (default: $SG_REFERENCE_DIR)")
+    ap.add_argument("--only", action="append", default=[],
+                    help="generate only these sets (int4_gemv, quant_params, fp16_gemv, attention, block_ops, "
+                         "int8_channel); repeatable; default all")
     args = ap.parse_args()
     if not args.reference:
         ap.error("name the reference checkout with --reference or SG_REFERENCE_DIR")
     oracle.build(ref=True, refdir=args.reference)
     R = oracle.ref()
-    gen_int4_gemv(R)
-    gen_quant_params(args.reference)
-    gen_fp16_gemv(R)
-    gen_attention(R)
-    gen_block_ops(R)
+    gens = {"int4_gemv": lambda: gen_int4_gemv(R), "quant_params": lambda: gen_quant_params(args.reference),
+            "fp16_gemv": lambda: gen_fp16_gemv(R), "attention": lambda: gen_attention(R),
+            "block_ops": lambda: gen_block_ops(R), "int8_channel": lambda: gen_int8_channel(R)}
+    for name in args.only or gens:
+        gens[name]()
     print("golden vectors written to", HERE)
 
 

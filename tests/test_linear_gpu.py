@@ -96,6 +96,32 @@ def test_int4_fast_path_fp32_activation(sg, oracle_mod, w4_path, K, N, gs, sym):
     close(C.cpu().numpy(), want)
 
 
+def outlier_activations(K, amp, seed, rows=1, group=32):
+    """x ~ N(0,1) with one value of magnitude amp..1.5 amp, random sign, in
+    every group of `group` k: the heavy-tailed activations real decoders feed
+    their linears."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((rows, K)).astype(np.float32)
+    for r in range(rows):
+        for g0 in range(0, K, group):
+            n = min(group, K - g0)
+            x[r, g0 + int(rng.integers(0, n))] = np.float32(amp * (1.0 + 0.5 * rng.random())
+                                                              * np.sign(rng.standard_normal()))
+    return x
+
+
+@pytest.mark.parametrize("amp", [100.0, 1000.0])
+@pytest.mark.parametrize("K,N,gs", [(4096, 14336, 32), (18944, 3584, 128), (2048, 3072, 32)])
+def test_int4_fast_path_outlier_activations(sg, oracle_mod, w4_path, K, N, gs, amp):
+    """One large activation per 32 k through the fp32-activation GEMV,
+    against the oracle at the same elementwise bar."""
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=N + 1)
+    x = outlier_activations(K, amp, seed=K + int(amp))
+    want = oracle_mod.matmul_int4_grouped(x, B, S, Z, K, N, gs, c_dt=oracle_mod.DT_F32)
+    C = sg.matmul_int4_grouped(t(x), t(B), t(S), t(Z), K, N, gs, out_dtype=torch.float32)
+    close(C.cpu().numpy(), want)
+
+
 @pytest.mark.parametrize("adt", ["f16", "bf16", "i8"])
 def test_int4_single_row_dtypes_bias(sg, oracle_mod, w4_path, adt):
     K, N, gs = 3072, 2560, 64
@@ -277,6 +303,23 @@ def test_int8_channel_int8_activations_bitexact(sg, oracle_mod, M, K, N):
     assert np.array_equal(C.cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("M", [1, 2])
+def test_int8_channel_matches_reference_golden(sg, M):
+    """Bit for bit against the reference's own OpenCL-C gemm_int8_m1
+    (opencl_kernels.h:36-52) run as host C; M = 2 repeats the row so that the
+    multi-row kernel is held to the same reference output."""
+    g = golden("int8_channel.npz")
+    for name in g["cases"]:
+        A, B, s, want = (g[f"{name}_{k}"] for k in ("A", "B", "s", "C"))
+        K, N = B.shape
+        C = torch.zeros((M, N), dtype=torch.float32, device=DEV)
+        _mm(sg, "sg_matmul_int8_channel", t(np.repeat(A[None, :], M, 0)), t(B), C, M, K, N, scales=t(s),
+            scale_A=float(g[f"{name}_scale_A"]))
+        got = C.cpu().numpy()
+        for m in range(M):
+            assert np.array_equal(got[m].view(np.uint32), want.view(np.uint32)), (name, m)
+
+
 @pytest.mark.parametrize("M,K,N,adt", [(1, 2048, 8192, "bf16"), (2, 1024, 1024, "f32"), (1, 100, 48, "f16")])
 def test_int8_channel_float_activations(sg, oracle_mod, M, K, N, adt):
     rng = np.random.default_rng(N)
@@ -293,6 +336,20 @@ def test_int8_channel_float_activations(sg, oracle_mod, M, K, N, adt):
     want = oracle_mod.gemm_w8_channel(xo, B, s, M, K, N, **kw)
     C = torch.zeros((M, N), dtype=torch.float32, device=DEV)
     _mm(sg, "sg_matmul_int8_channel", xt, t(B), C, M, K, N, scales=t(s))
+    close(C.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("amp", [100.0, 1000.0])
+@pytest.mark.parametrize("M,K,N", [(1, 4096, 14336), (2, 2048, 1024)])
+def test_int8_channel_outlier_activations(sg, oracle_mod, M, K, N, amp):
+    """INT8 weights, fp32 activations with one large value per 32 k."""
+    rng = np.random.default_rng(K + int(amp))
+    x = outlier_activations(K, amp, seed=N + int(amp), rows=M)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    s = (rng.random(N) * 1e-3).astype(np.float32)
+    want = oracle_mod.gemm_w8_channel(x, B, s, M, K, N)
+    C = torch.zeros((M, N), dtype=torch.float32, device=DEV)
+    _mm(sg, "sg_matmul_int8_channel", t(x), t(B), C, M, K, N, scales=t(s))
     close(C.cpu().numpy(), want)
 
 

@@ -118,3 +118,14 @@ def test_bf16_helpers_roundtrip(oracle_mod):
     b = oracle_mod.f32_to_bf16_bits(x)
     y = oracle_mod.bf16_bits_to_f32(b)
     np.testing.assert_allclose(y, x, rtol=4e-3)
+
+
+def test_int8_channel_matches_reference_golden(oracle_mod):
+    """The restated INT8 per-channel kernel against the reference's own
+    OpenCL-C gemm_int8_m1 (opencl_kernels.h:36-52) run as host C: bit for bit."""
+    g = golden("int8_channel.npz")
+    for name in g["cases"]:
+        A, B, s, C = (g[f"{name}_{k}"] for k in ("A", "B", "s", "C"))
+        K, N = B.shape
+        got = oracle_mod.gemm_int8_channel(A[None, :], B, s, 1, K, N, float(g[f"{name}_scale_A"]))
+        assert np.array_equal(got[0].view(np.uint32), C.view(np.uint32)), name
