@@ -294,6 +294,10 @@ def run_ours(args):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
+        # a bounded device delay (about 1 ms) ahead of the start event, so that the
+        # host has queued the graph launches before the timed region begins and
+        # the GPU does not idle on host launch latency inside it
+        torch.cuda._sleep(2_000_000)
         e0.record(stream)
         for _ in range(n_rep):
             g.replay()
@@ -747,40 +751,11 @@ def build_decode_package(path, cfg, seed=0, gs=32, max_context=1024, max_prefill
                          model_id="synthetic/llama-3.2-1b-shape"):
     """Random N(0, 0.02) weights (norms 1 + N(0, 0.02)) drawn on the GPU and
     packed by the library's device packer, written as a directory package."""
-    import torch
-
-    from silicongraph_b200 import _lib, armpack
-    lib = _lib.load()
-    g = torch.Generator(device="cuda")
-    g.manual_seed(seed)
-    H, V, F = cfg["hidden_size"], cfg["vocab_size"], cfg["intermediate_size"]
-    Hq, Hkv, D = cfg["num_heads"], cfg["num_kv_heads"], cfg["head_dim"]
-
-    def randn(*shape):
-        return torch.randn(*shape, generator=g, device="cuda", dtype=torch.float32) * 0.02
-
-    def quant(K, N):
-        w = randn(K, N)
-        G = (K + gs - 1) // gs
-        B = torch.empty(((K + 1) // 2, N), dtype=torch.uint8, device="cuda")
-        S = torch.empty((G, N), dtype=torch.float16, device="cuda")
-        Z = torch.empty((G, N), dtype=torch.int8, device="cuda")
-        _lib.check(lib.sg_quantize_int4_grouped(w.data_ptr(), K, N, gs, 0, B.data_ptr(), S.data_ptr(),
-                                                Z.data_ptr(), torch.cuda.current_stream().cuda_stream))
-        return B.cpu().numpy(), S.cpu().numpy(), Z.cpu().numpy()
-
-    t = {"embed_tokens": randn(V, H).half().cpu().numpy()}
-    for i in range(cfg["num_layers"]):
-        q = f"layers.{i}."
-        t[q + "input_norm"] = (1 + randn(H)).half().cpu().numpy()
-        t[q + "post_norm"] = (1 + randn(H)).half().cpu().numpy()
-        for name, K, N in (("qkv", H, (Hq + 2 * Hkv) * D), ("o", Hq * D, H), ("gate_up", H, 2 * F), ("down", F, H)):
-            B, S, Z = quant(K, N)
-            t[q + name + ".qweight"], t[q + name + ".scales"], t[q + name + ".zeros"] = B, S, Z
-    t["final_norm"] = (1 + randn(H)).half().cpu().numpy()
-    t["lm_head.qweight"], t["lm_head.scales"], t["lm_head.zeros"] = quant(H, V)
+    from silicongraph_b200 import armpack
+    t = armpack.random_cuda_tensors_on_device(cfg, seed=seed, group_size=gs)
     armpack.write_package(path, cfg, t, group_size=gs, max_context=max_context, max_prefill_chunk=max_prefill_chunk,
                           as_zip=False, model_id=model_id)
+    H = cfg["hidden_size"]
     weight_bytes = sum(a.nbytes for k, a in t.items() if k != "embed_tokens") + H * 2
     return weight_bytes, t
 
@@ -1163,6 +1138,7 @@ def run_int8(args):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
+        torch.cuda._sleep(2_000_000)  # host queues the launches while the GPU waits (outside the timed region)
         e0.record(stream)
         for _ in range(args.steps // graph_len):
             g.replay()

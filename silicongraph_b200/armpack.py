@@ -240,3 +240,47 @@ def pack_random_llama(path: str, cfg: dict | None = None, seed: int = 0, **kw) -
     t = cuda_tensors(cfg, w, group_size=gs, symmetric=sym)
     write_package(path, cfg, t, **kw)
     return path, cfg, t
+
+
+def random_cuda_tensors_on_device(cfg: dict, seed: int = 0, group_size: int = 32, std: float = 0.02) -> dict:
+    """The "cuda" profile's tensors of a random-init Llama-style model, drawn
+    on the current CUDA device (N(0, std) matrices, 1 + N(0, std) norms) and
+    packed there by the library's own INT4 packer (sg_quantize_int4_grouped,
+    the same convention as quantize_int4_grouped); returned as host arrays in
+    file order.  For models too large to draw and quantise on the host in
+    reasonable time (the Llama-3.2-1B and Qwen2.5-7B shapes)."""
+    import torch
+
+    from . import _lib
+    lib = _lib.load()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    H, V, F = cfg["hidden_size"], cfg["vocab_size"], cfg["intermediate_size"]
+    Hq, Hkv, D = cfg["num_heads"], cfg["num_kv_heads"], cfg["head_dim"]
+    gs = group_size
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def randn(*shape):
+        return torch.randn(*shape, generator=g, device="cuda", dtype=torch.float32) * std
+
+    def quant(K, N):
+        w = randn(K, N)
+        G = (K + gs - 1) // gs
+        B = torch.empty(((K + 1) // 2, N), dtype=torch.uint8, device="cuda")
+        S = torch.empty((G, N), dtype=torch.float16, device="cuda")
+        Z = torch.empty((G, N), dtype=torch.int8, device="cuda")
+        _lib.check(lib.sg_quantize_int4_grouped(w.data_ptr(), K, N, gs, 0, B.data_ptr(), S.data_ptr(),
+                                                Z.data_ptr(), stream))
+        return B.cpu().numpy(), S.cpu().numpy(), Z.cpu().numpy()
+
+    t = {"embed_tokens": randn(V, H).half().cpu().numpy()}
+    for i in range(cfg["num_layers"]):
+        q = f"layers.{i}."
+        t[q + "input_norm"] = (1 + randn(H)).half().cpu().numpy()
+        t[q + "post_norm"] = (1 + randn(H)).half().cpu().numpy()
+        for name, K, N in (("qkv", H, (Hq + 2 * Hkv) * D), ("o", Hq * D, H), ("gate_up", H, 2 * F), ("down", F, H)):
+            B, S, Z = quant(K, N)
+            t[q + name + ".qweight"], t[q + name + ".scales"], t[q + name + ".zeros"] = B, S, Z
+    t["final_norm"] = (1 + randn(H)).half().cpu().numpy()
+    t["lm_head.qweight"], t["lm_head.scales"], t["lm_head.zeros"] = quant(H, V)
+    return t
