@@ -23,6 +23,23 @@ ArmStatus sg_session_last_logits(ArmSession* sess, float* host_out, uint32_t n);
 /* Number of tokens in the session's KV cache. */
 uint32_t sg_session_position(const ArmSession* sess);
 
+/* ---- memory-aware graph selection -----------------------------------------
+ * armpack_select_graph scores the package's runnable "cuda" graphs as the
+ * reference's GraphSelector::score does (compiler/lib/generator/
+ * graph_selector.cpp:34-94) and refuses before allocating: a graph whose
+ * session would need more than 95 % of the device memory available (free
+ * memory of the session's device now, capped by ArmDeviceState.ram_mb when
+ * that is non-zero) is rejected (:45-51); NULL when none fits, with the
+ * reason in armpack_last_error().  The call below does the same against a
+ * stated number of available bytes (no device query: a caller that manages
+ * its own device budget, or a test). */
+ArmGraph* sg_select_graph_within(ArmPackage* pkg, const ArmDeviceState* state, uint64_t device_bytes_available);
+
+/* Device bytes a session of `batch` sequences on `graph` allocates (its one
+ * slab: weights, KV cache for the graph's context, activations, scratch); 0
+ * for a graph this library cannot run. */
+uint64_t sg_graph_session_bytes(const ArmGraph* graph, uint32_t batch);
+
 /* ---- tensor parallelism --------------------------------------------------
  * One session spread over `world` processes, one GPU each, in the Megatron
  * layout: the q|k|v and gate|up projections are split by output columns

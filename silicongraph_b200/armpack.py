@@ -147,14 +147,18 @@ def cuda_tensors(cfg: dict, weights: dict, group_size: int = 32, symmetric: bool
 
 # ----------------------------------------------------------------------------- writer
 def write_package(path: str, cfg: dict, tensors: dict, *, model_id: str = "synthetic/llama-style",
-                  group_size: int = 32, symmetric: bool = False, max_context: int = 4096,
-                  max_prefill_chunk: int = 512, as_zip: bool = True) -> str:
-    """Writes a package (ZIP file, or a directory with the same layout) whose
-    single graph entry has execution_backend "cuda"; returns `path`."""
+                  group_size: int = 32, symmetric: bool = False, max_context=4096,
+                  max_prefill_chunk: int = 512, as_zip: bool = True, graph_conditions=None) -> str:
+    """Writes a package (ZIP file, or a directory with the same layout) with
+    execution_backend "cuda" graph entries sharing one weight file: one graph
+    per context length in `max_context` (an int or a list).  graph_conditions
+    (a list of dicts, one per graph) overrides manifest fields of the entries,
+    e.g. thermal_state / latency_mode / estimated_tpot_ms.  Returns `path`."""
+    contexts = [max_context] if isinstance(max_context, int) else list(max_context)
+    conds = list(graph_conditions) if graph_conditions else [{} for _ in contexts]
+    assert len(conds) == len(contexts)
     wid = f"weights_int4_g{group_size}"
     wpath, ipath = f"weights/{wid}.bin", f"weights/{wid}.index.json"
-    gid = f"cuda_int4_g{group_size}_ctx{max_context}"
-    gpath = f"graphs/{gid}.json"
     index, offset = {}, 0
     for name, arr in tensors.items():
         arr = np.ascontiguousarray(arr)
@@ -165,29 +169,34 @@ def write_package(path: str, cfg: dict, tensors: dict, *, model_id: str = "synth
     total = (offset + ALIGN - 1) // ALIGN * ALIGN
     H, L = cfg["hidden_size"], cfg["num_layers"]
     kv_per_token = 2 * L * cfg["num_kv_heads"] * cfg["head_dim"] * 2
-    graph = {
-        "format": GRAPH_FORMAT, "version": 1,
-        "model": {"family": "llama_style", **{k: cfg[k] for k in (
-            "num_layers", "hidden_size", "num_heads", "num_kv_heads", "head_dim", "intermediate_size",
-            "vocab_size", "rope_theta", "rms_norm_eps")}},
-        "quant": {"scheme": "int4_grouped", "group_size": group_size, "zero_point": not symmetric,
-                  "lm_head": "int4"},
-        "weights": wid, "tensor_index": ipath,
-        "max_context": max_context, "max_prefill_chunk": max_prefill_chunk,
-    }
+    graphs, entries = {}, []
+    for gi, (ctx, cond) in enumerate(zip(contexts, conds)):
+        gid = f"cuda_int4_g{group_size}_ctx{ctx}" + (f"_{gi}" if len(contexts) > 1 else "")
+        gpath = f"graphs/{gid}.json"
+        graphs[gpath] = {
+            "format": GRAPH_FORMAT, "version": 1,
+            "model": {"family": "llama_style", **{k: cfg[k] for k in (
+                "num_layers", "hidden_size", "num_heads", "num_kv_heads", "head_dim", "intermediate_size",
+                "vocab_size", "rope_theta", "rms_norm_eps")}},
+            "quant": {"scheme": "int4_grouped", "group_size": group_size, "zero_point": not symmetric,
+                      "lm_head": "int4"},
+            "weights": wid, "tensor_index": ipath,
+            "max_context": ctx, "max_prefill_chunk": max_prefill_chunk,
+        }
+        entries.append({
+            "index": gi, "id": gid, "path": gpath, "soc_name": "nvidia_b200", "quant_dtype": f"int4_g{group_size}",
+            "memory_budget_mb": 0, "context_length": ctx, "thermal_state": "nominal",
+            "latency_mode": "interactive", "execution_backend": "cuda", "estimated_ttft_ms": 0.0,
+            "estimated_tpot_ms": 0.0, "peak_memory_bytes": total + kv_per_token * ctx,
+            "weight_bytes": total, "activation_bytes": 0, "kv_cache_bytes": kv_per_token * ctx,
+            "kv_bytes_per_token": kv_per_token, "kernel_ids": [], **cond})
     manifest = {
         "armpack_version": "1.0", "compiler_version": "sg-b200-0.1.0", "model_id": model_id,
         "model_family": "llama_style", "created_at": time.strftime("%Y-%m-%dT%H:%M:%SZ", time.gmtime()),
         "arch": {"num_layers": L, "hidden_size": H, "num_heads": cfg["num_heads"],
                  "num_kv_heads": cfg["num_kv_heads"], "vocab_size": cfg["vocab_size"],
-                 "max_position_embeddings": cfg.get("max_position_embeddings", max_context)},
-        "graphs": [{
-            "index": 0, "id": gid, "path": gpath, "soc_name": "nvidia_b200", "quant_dtype": f"int4_g{group_size}",
-            "memory_budget_mb": 0, "context_length": max_context, "thermal_state": "nominal",
-            "latency_mode": "interactive", "execution_backend": "cuda", "estimated_ttft_ms": 0.0,
-            "estimated_tpot_ms": 0.0, "peak_memory_bytes": total + kv_per_token * max_context,
-            "weight_bytes": total, "activation_bytes": 0, "kv_cache_bytes": kv_per_token * max_context,
-            "kv_bytes_per_token": kv_per_token, "kernel_ids": []}],
+                 "max_position_embeddings": cfg.get("max_position_embeddings", max(contexts))},
+        "graphs": entries,
         "kernels": [],
         "weights": [{"id": wid, "path": wpath, "dtype": "int4", "size_bytes": total, "mmap_safe": True,
                      "page_alignment": ALIGN}],
@@ -210,7 +219,8 @@ def write_package(path: str, cfg: dict, tensors: dict, *, model_id: str = "synth
         if total > pos:
             fh.write(b"\0" * (total - pos))
 
-    texts = {"manifest.json": json.dumps(manifest, indent=2), gpath: json.dumps(graph, indent=2),
+    texts = {"manifest.json": json.dumps(manifest, indent=2),
+             **{gp: json.dumps(g, indent=2) for gp, g in graphs.items()},
              ipath: json.dumps({"tensors": index}), "runtime_config.json": json.dumps(runtime_config, indent=2)}
     if not as_zip:
         os.makedirs(os.path.join(path, "weights"), exist_ok=True)

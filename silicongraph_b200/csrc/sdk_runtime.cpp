@@ -260,6 +260,8 @@ struct ArmGraph_ {
   float ttft_ms = 0, tpot_ms = 0;
   uint64_t peak_bytes = 0;
   uint32_t context_length = 0;
+  int thermal = 0;             // manifest thermal_state: 0 nominal, 1 warm, 2 hot, 3 critical
+  int latency = 0;             // manifest latency_mode: 0 interactive, 1 batch, 2 background
   bool runnable = false;       // a "cuda" graph whose graph file parsed
   std::string why_not;         // reason when not runnable
   ModelCfg cfg;
@@ -937,6 +939,52 @@ bool setup_peer_allreduce(ArmSession_* S, int max_n) {
 }
 
 // Session of rank `rank` in a group of `world` (world 1: the whole model, no NCCL).
+// Scratch of the linear kernels (largest over the shapes and token counts a
+// session of `batch` sequences uses) and of the attention kernels.
+void session_scratch(const ModelCfg& c, int batch, size_t* lws_out, size_t* aws_out) {
+  const int T = c.max_chunk;
+  SgMatMulParams mp{};
+  auto lin_ws = [&](int M, int K, int N, int cdt) {
+    mp = SgMatMulParams{};
+    mp.A = mp.B = mp.scales_B = reinterpret_cast<void*>(256);
+    mp.C = reinterpret_cast<void*>(256);
+    mp.M = M;
+    mp.K = K;
+    mp.N = N;
+    mp.group_size = c.group_size;
+    mp.a_dtype = SG_DT_F16;
+    mp.c_dtype = cdt;
+    return sg_matmul_int4_grouped_workspace_size(&mp);
+  };
+  size_t lws = 0;
+  // every token count a call can see: the row kernels' scratch depends on M
+  // below the tensor-core GEMM's threshold
+  const int TB = T * batch;  // rows of the largest forward pass
+  for (int M = 1; M <= TB; M = (M < 64 ? M + 1 : (M == TB ? TB + 1 : std::min(2 * M, TB)))) {
+    lws = std::max({lws, lin_ws(M, c.hidden, c.nqkv(), SG_DT_F16), lin_ws(M, c.heads * c.head_dim, c.hidden, SG_DT_F16),
+                    lin_ws(M, c.hidden, 2 * c.ffn, SG_DT_F16), lin_ws(M, c.ffn, c.hidden, SG_DT_F16)});
+  }
+  lws = std::max(lws, lin_ws(batch, c.hidden, c.vocab, SG_DT_F32));
+  SgFlashAttentionParams ap{};
+  ap.Q = ap.K = ap.V = ap.O = reinterpret_cast<void*>(256);
+  ap.B = batch;
+  ap.num_heads = c.heads;
+  ap.num_kv_heads = c.kv_heads;
+  ap.head_dim = c.head_dim;
+  ap.causal = 1;
+  ap.io_dtype = SG_DT_F16;
+  ap.S = 1;
+  ap.S_kv = c.max_context;
+  ap.q_pos0 = c.max_context - 1;
+  size_t aws = sg_flash_decode_workspace_size(&ap);
+  ap.S = T;
+  ap.q_pos0 = c.max_context - T;
+  aws = std::max(aws, sg_flash_attention_workspace_size(&ap));
+
+  *lws_out = lws;
+  *aws_out = aws;
+}
+
 ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int rank, int world, const uint8_t* id,
                            int batch) {
   const char* fn = world > 1 ? "sg_session_create_tp" : "armgraph_create_session";
@@ -1038,43 +1086,8 @@ ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int r
     }
   // scratch sizes of the linear kernels (largest over the shapes and token counts used)
   const int T = c.max_chunk;
-  SgMatMulParams mp{};
-  auto lin_ws = [&](int M, int K, int N, int cdt) {
-    mp = SgMatMulParams{};
-    mp.A = mp.B = mp.scales_B = reinterpret_cast<void*>(256);
-    mp.C = reinterpret_cast<void*>(256);
-    mp.M = M;
-    mp.K = K;
-    mp.N = N;
-    mp.group_size = c.group_size;
-    mp.a_dtype = SG_DT_F16;
-    mp.c_dtype = cdt;
-    return sg_matmul_int4_grouped_workspace_size(&mp);
-  };
-  size_t lws = 0;
-  // every token count a call can see: the row kernels' scratch depends on M
-  // below the tensor-core GEMM's threshold
-  const int TB = T * batch;  // rows of the largest forward pass
-  for (int M = 1; M <= TB; M = (M < 64 ? M + 1 : (M == TB ? TB + 1 : std::min(2 * M, TB)))) {
-    lws = std::max({lws, lin_ws(M, c.hidden, c.nqkv(), SG_DT_F16), lin_ws(M, c.heads * c.head_dim, c.hidden, SG_DT_F16),
-                    lin_ws(M, c.hidden, 2 * c.ffn, SG_DT_F16), lin_ws(M, c.ffn, c.hidden, SG_DT_F16)});
-  }
-  lws = std::max(lws, lin_ws(batch, c.hidden, c.vocab, SG_DT_F32));
-  SgFlashAttentionParams ap{};
-  ap.Q = ap.K = ap.V = ap.O = reinterpret_cast<void*>(256);
-  ap.B = batch;
-  ap.num_heads = c.heads;
-  ap.num_kv_heads = c.kv_heads;
-  ap.head_dim = c.head_dim;
-  ap.causal = 1;
-  ap.io_dtype = SG_DT_F16;
-  ap.S = 1;
-  ap.S_kv = c.max_context;
-  ap.q_pos0 = c.max_context - 1;
-  size_t aws = sg_flash_decode_workspace_size(&ap);
-  ap.S = T;
-  ap.q_pos0 = c.max_context - T;
-  aws = std::max(aws, sg_flash_attention_workspace_size(&ap));
+  size_t lws = 0, aws = 0;
+  session_scratch(c, batch, &lws, &aws);
 
   // weights: the whole file (one rank), or this rank's shards (several)
   const SgTpShard& sh = S->shard;
@@ -1310,6 +1323,11 @@ ArmPackage* armpack_load(const char* path) {
     g->tpot_ms = (float)e["estimated_tpot_ms"].number();
     g->peak_bytes = (uint64_t)e["peak_memory_bytes"].integer();
     g->context_length = (uint32_t)e["context_length"].integer();
+    {
+      const std::string th = e["thermal_state"].text("nominal"), lm = e["latency_mode"].text("interactive");
+      g->thermal = th == "warm" ? 1 : th == "hot" ? 2 : th == "critical" ? 3 : 0;
+      g->latency = lm == "batch" ? 1 : lm == "background" ? 2 : 0;
+    }
     g->description = g->id + " [" + g->backend + ", " + e["quant_dtype"].text("?") + ", context " +
                      std::to_string(g->context_length) + "]";
     if (g->backend == "cuda") {
@@ -1334,6 +1352,78 @@ ArmGraph* armpack_get_graph(ArmPackage* pkg, uint32_t index) {
   return pkg->graphs[index].get();
 }
 
+// Device memory a one-sequence session of `g` allocates: the weight image,
+// the KV cache for the graph's full context, the planned activations and the
+// kernels' scratch -- the slab armgraph_create_session asks cudaMalloc for.
+static uint64_t planned_session_bytes(const ArmGraph_* g, int batch) {
+  const ModelCfg& c = g->cfg;
+  uint64_t w = 0;
+  for (const auto& kv : g->tensors) w = std::max(w, kv.second.offset + kv.second.bytes);
+  size_t lws = 0, aws = 0;
+  session_scratch(c, batch, &lws, &aws);
+  const Plan plan = make_plan(c, c.max_chunk * batch, batch, 1);
+  const uint64_t kv_bytes = (uint64_t)batch * c.layers * 2 * (uint64_t)c.kv_heads * c.max_context * c.head_dim * 2;
+  uint64_t off = align_up(w, 4096);
+  off = align_up(off + kv_bytes, 4096);
+  off = align_up(off + plan.bytes, 4096);
+  off = align_up(off + align_up(std::max<size_t>(lws, 4096), 256), 4096);
+  return align_up(off + align_up(std::max<size_t>(aws, 256), 256), 4096);
+}
+
+// GraphSelector::score (compiler/lib/generator/graph_selector.cpp:34-94) for
+// "cuda" graphs, lower is better: a graph whose peak memory exceeds 95 % of
+// the available device memory is rejected (:45-51); latency-mode mismatch
+// +20, thermal mismatch +10 per step, a context shorter than requested
+// +500 + 0.1 per missing token, a longer one +0.001 per extra token, memory
+// use above 85 % of the budget +50 and below 30 % +10, and half the
+// estimated TPOT.  The SoC and precision rules do not apply to a CUDA graph,
+// and there is no Vulkan penalty (no Vulkan candidate is run here).
+static bool score_graph(const ArmGraph_* g, const ArmDeviceState* st, uint64_t avail, uint64_t need, float* out) {
+  if (need > avail / 100 * 95) return false;
+  float s = 0.f;
+  const int lat = st ? (int)st->latency_mode : 0, th = st ? (int)st->thermal_state : 0;
+  if (g->latency != lat) s += 20.f;
+  if (g->thermal != th) s += 10.f * (float)std::abs(g->thermal - th);
+  const uint32_t ctx = g->context_length ? g->context_length : (uint32_t)g->cfg.max_context;
+  const int64_t diff = (int64_t)ctx - (int64_t)(st ? st->context_length : 0);
+  s += diff < 0 ? 500.f + (float)(-diff) * 0.1f : (float)diff * 0.001f;
+  const float use = avail ? (float)need / (float)avail : 1.f;
+  if (use > 0.85f) s += 50.f;
+  else if (use < 0.3f) s += 10.f;
+  s += g->tpot_ms * 0.5f;
+  *out = s;
+  return true;
+}
+
+static ArmGraph* select_within(ArmPackage* pkg, const ArmDeviceState* state, uint64_t avail, const char* fn) {
+  ArmGraph_* best = nullptr;
+  float best_score = 0.f;
+  std::string refused;
+  for (auto& g : pkg->graphs) {
+    if (!g->runnable) continue;
+    const uint64_t need = std::max(g->peak_bytes, planned_session_bytes(g.get(), 1));
+    float sc = 0.f;
+    if (!score_graph(g.get(), state, avail, need, &sc)) {
+      char buf[256];
+      snprintf(buf, sizeof buf, "; %s needs %llu bytes, more than 95%% of the %llu available", g->id.c_str(),
+               (unsigned long long)need, (unsigned long long)avail);
+      refused += buf;
+      continue;
+    }
+    if (!best || sc < best_score) {
+      best = g.get();
+      best_score = sc;
+    }
+  }
+  if (!best) {
+    std::string why = refused.empty() ? std::string("; no runnable 'cuda' graph in the package") : refused;
+    for (auto& g : pkg->graphs)
+      if (g->backend == "cuda" && !g->runnable) why += "; " + g->id + ": " + g->why_not;
+    set_err("%s: no graph fits%s", fn, why.c_str());
+  }
+  return best;
+}
+
 ArmGraph* armpack_select_graph(ArmPackage* pkg, const ArmDeviceState* state) {
   if (!pkg) {
     set_err("armpack_select_graph: package is NULL");
@@ -1345,26 +1435,37 @@ ArmGraph* armpack_select_graph(ArmPackage* pkg, const ArmDeviceState* state) {
     set_err("armpack_select_graph: no CUDA device (this library runs only 'cuda' graphs)");
     return nullptr;
   }
-  const uint32_t want = state ? state->context_length : 0;
-  ArmGraph_* best = nullptr;
-  for (auto& g : pkg->graphs) {
-    if (!g->runnable) continue;
-    const uint32_t ctx = g->context_length ? g->context_length : (uint32_t)g->cfg.max_context;
-    if (!best) {
-      best = g.get();
-      continue;
-    }
-    const uint32_t bctx = best->context_length ? best->context_length : (uint32_t)best->cfg.max_context;
-    const bool g_fits = ctx >= want, b_fits = bctx >= want;
-    if ((g_fits && !b_fits) || (g_fits == b_fits && (g_fits ? ctx < bctx : ctx > bctx))) best = g.get();
+  // the device a session would run on (SG_DEVICE, else the current one) and its free memory now:
+  // the selection refuses before allocating, as the reference's execution policy requires
+  int prev = 0, dev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) prev = 0;
+  dev = prev;
+  if (const char* d = getenv("SG_DEVICE")) dev = atoi(d);
+  size_t free_b = 0, total_b = 0;
+  const bool ok = cudaSetDevice(dev) == cudaSuccess && cudaMemGetInfo(&free_b, &total_b) == cudaSuccess;
+  cudaSetDevice(prev);
+  if (!ok) {
+    cudaGetLastError();
+    set_err("armpack_select_graph: cannot query the memory of CUDA device %d", dev);
+    return nullptr;
   }
-  if (!best) {
-    std::string why = "no runnable 'cuda' graph in the package";
-    for (auto& g : pkg->graphs)
-      if (g->backend == "cuda") why += "; " + g->id + ": " + g->why_not;
-    set_err("armpack_select_graph: %s", why.c_str());
+  uint64_t avail = free_b;
+  // a caller-stated budget (ArmDeviceState.ram_mb, the reference's ram_available_mb) caps it
+  if (state && state->ram_mb > 0) avail = std::min<uint64_t>(avail, (uint64_t)state->ram_mb << 20);
+  return select_within(pkg, state, avail, "armpack_select_graph");
+}
+
+ArmGraph* sg_select_graph_within(ArmPackage* pkg, const ArmDeviceState* state, uint64_t device_bytes_available) {
+  if (!pkg) {
+    set_err("sg_select_graph_within: package is NULL");
+    return nullptr;
   }
-  return best;
+  return select_within(pkg, state, device_bytes_available, "sg_select_graph_within");
+}
+
+uint64_t sg_graph_session_bytes(const ArmGraph* graph, uint32_t batch) {
+  if (!graph || !graph->runnable || batch == 0) return 0;
+  return planned_session_bytes(graph, (int)std::min<uint32_t>(batch, 1u << 20));
 }
 
 const char* armgraph_description(const ArmGraph* graph) { return graph ? graph->description.c_str() : ""; }

@@ -70,6 +70,8 @@ _SIGS = {
     "armpack_get_tokenizer": (_P, [_P]),
     "sg_session_last_logits": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_float), ctypes.c_uint32]),
     "sg_session_position": (ctypes.c_uint32, [_P]),
+    "sg_select_graph_within": (_P, [_P, ctypes.POINTER(ArmDeviceState), ctypes.c_uint64]),
+    "sg_graph_session_bytes": (ctypes.c_uint64, [_P, ctypes.c_uint32]),
     "sg_tp_shard": (ctypes.c_int, [ctypes.POINTER(SgTpModel), ctypes.c_int32, ctypes.c_int32,
                                    ctypes.POINTER(SgTpShard)]),
     "sg_tp_unique_id": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint8)]),
@@ -171,9 +173,18 @@ class Package:
             raise ArmError(-1, last_error())
         return Graph(self, g)
 
-    def select(self, context_length: int = 0) -> "Graph":
-        st = ArmDeviceState(gpu_available=True, context_length=context_length)
-        g = lib().armpack_select_graph(self.h, ctypes.byref(st))
+    def select(self, context_length: int = 0, *, ram_mb: int = 0, thermal: int = 0, latency: int = 0,
+               device_bytes_available: int | None = None) -> "Graph":
+        """armpack_select_graph: the best-scoring graph whose session fits in
+        95 % of the device memory available (free memory now, capped by
+        ram_mb when given); with device_bytes_available, against that figure
+        instead (sg_select_graph_within, no device query)."""
+        st = ArmDeviceState(gpu_available=True, context_length=context_length, ram_mb=ram_mb,
+                            thermal_state=thermal, latency_mode=latency)
+        if device_bytes_available is None:
+            g = lib().armpack_select_graph(self.h, ctypes.byref(st))
+        else:
+            g = lib().sg_select_graph_within(self.h, ctypes.byref(st), device_bytes_available)
         if not g:
             raise ArmError(-1, last_error())
         return Graph(self, g)
@@ -190,6 +201,10 @@ class Graph:
     @property
     def peak_memory_bytes(self) -> int:
         return lib().armgraph_peak_memory_bytes(self.h)
+
+    def session_bytes(self, batch: int = 1) -> int:
+        """Device bytes a session of `batch` sequences allocates (one slab)."""
+        return lib().sg_graph_session_bytes(self.h, batch)
 
     def session(self, tp: tuple[int, int, bytes] | None = None, batch: int = 1) -> "Session":
         """A session; tp = (rank, world, unique id) joins a tensor-parallel group;

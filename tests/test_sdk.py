@@ -104,3 +104,51 @@ def test_malformed_packages(tmp_path):
         assert "cpu" in pkg.graph(0).description
         with pytest.raises(sdk.ArmError):
             pkg.graph(0).session()
+
+
+# ------------------------------------------------------------------ memory-aware selection
+def _multi_graph_package(tmp_path, contexts, conditions=None):
+    from silicongraph_b200 import armpack
+    cfg = armpack.llama_config(layers=2, hidden=256, heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=1000,
+                               rope_theta=500000.0, max_pos=65536)
+    t = armpack.cuda_tensors(cfg, armpack.random_llama_weights(cfg, seed=2), group_size=32)
+    return armpack.write_package(str(tmp_path / "multi.armpack"), cfg, t, max_context=contexts,
+                                 max_prefill_chunk=128, graph_conditions=conditions)
+
+
+def test_select_prefers_fitting_context_and_refuses_before_allocation(tmp_path):
+    """graph_selector.cpp:34-94 with device memory as the budget: the graph
+    with a long-enough context wins, a graph over 95 % of the budget is
+    rejected (:45-51), and with nothing fitting the call refuses with the
+    reason instead of allocating."""
+    from silicongraph_b200 import sdk
+    path = _multi_graph_package(tmp_path, [1024, 4096, 16384])
+    with sdk.Package(path) as pkg:
+        need = [pkg.graph(i).session_bytes() for i in range(3)]
+        assert need[0] < need[1] < need[2]               # the KV cache grows with the context
+        big = 100 * need[2]
+        assert "ctx4096" in pkg.select(2000, device_bytes_available=big).description
+        assert "ctx16384" in pkg.select(10000, device_bytes_available=big).description
+        # the 4096-token graph exactly over 95 %: the shorter one is taken despite its context
+        just_under = need[1] * 100 // 95 + 200
+        assert "ctx4096" in pkg.select(2000, device_bytes_available=just_under).description
+        assert "ctx1024" in pkg.select(2000, device_bytes_available=need[1]).description
+        with pytest.raises(sdk.ArmError) as e:
+            pkg.select(2000, device_bytes_available=need[0])   # nothing fits in 95 %
+        assert "95%" in str(e.value) and "needs" in str(e.value)
+
+
+def test_select_penalises_thermal_and_latency_mismatch(tmp_path):
+    from silicongraph_b200 import sdk
+    conds = [{"thermal_state": "hot", "latency_mode": "interactive"},
+             {"thermal_state": "nominal", "latency_mode": "background"},
+             {"thermal_state": "nominal", "latency_mode": "interactive"}]
+    path = _multi_graph_package(tmp_path, [4096, 4096, 4096], conds)
+    with sdk.Package(path) as pkg:
+        big = 100 * pkg.graph(0).session_bytes()
+        assert pkg.select(4096, device_bytes_available=big).description.startswith("cuda_int4_g32_ctx4096_2")
+        # a hot device prefers the graph built for it (10 per thermal step outweighs nothing else)
+        assert pkg.select(4096, thermal=2, device_bytes_available=big).description.startswith(
+            "cuda_int4_g32_ctx4096_0")
+        assert pkg.select(4096, latency=2, device_bytes_available=big).description.startswith(
+            "cuda_int4_g32_ctx4096_1")

@@ -153,3 +153,22 @@ def test_batched_session_matches_each_sequence(sg, oracle_mod, tmp_path):
             want = ref.forward([int(toks[i][b])])
             close(logits[i + 1][b], want)
             check_token(int(toks[i + 1][b]), want)
+
+
+def test_select_graph_refuses_before_allocation(sg, tmp_path):
+    """armpack_select_graph sizes a graph's session exactly (the slab the
+    session then allocates) and refuses when it exceeds 95 % of the budget:
+    the device's free memory, capped by ArmDeviceState.ram_mb."""
+    from silicongraph_b200 import sdk
+    path, _ = _package(tmp_path, 128)
+    with sdk.Package(path) as pkg:
+        g = pkg.select(64)
+        need = g.session_bytes()
+        manifest_peak = g.peak_memory_bytes
+        with g.session():
+            assert g.peak_memory_bytes == max(manifest_peak, need)   # the slab is what was planned
+        budget_mb = (need * 100 // 95) // (1 << 20)                  # just under what 95 % needs
+        with pytest.raises(sdk.ArmError) as e:
+            pkg.select(64, ram_mb=max(1, budget_mb))
+        assert "95%" in str(e.value)
+        assert pkg.select(64, ram_mb=budget_mb + 2) is not None

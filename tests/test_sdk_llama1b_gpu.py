@@ -3,12 +3,26 @@
 group-32 weights, random N(0, 0.02) init) through the armcc SDK on the GPU,
 against the decoder composition oracle (oracle/decoder.py: the reference's
 kernel semantics, matmul_neon.h:113-147 / flash_attention.h:95-144 /
-matmul_neon.h:154-275, fp16 values at op boundaries).
+matmul_neon.h:154-275, fp16 values at op boundaries).  Batch 1, and two
+sequences of a batch-16 session; the logits after the prompt and after each of
+four greedy steps.
 
-Logits after the prompt and after each of four greedy steps within
-|got - want| <= 2e-3 + 1e-2 |want| over the whole vocabulary; greedy tokens
-equal wherever the oracle's top two logits differ by more than that.  Batch 1,
-and two sequences of a batch-16 session."""
+The yardstick is the reference's own rounding noise.  With fp16 values between
+ops, the reference's logits at this width and depth sit about 3e-3 (relative
+L2) from the same kernels run in fp32: they miss an elementwise
+2e-3 + 1e-2 |y| bar against exact arithmetic on about 6 % of the vocabulary
+(and already on some logits with one layer), so no implementation that sums in
+another order can meet that bar against them.  Each check therefore measures
+the reference's fp16-vs-fp32 distance on the same tokens (the oracle in both
+precisions) and requires the GPU's logits to be
+  * within 2x that distance of the fp16 reference and of the fp32 one
+    (relative L2; measured 1.3x and about 1x),
+  * elementwise within 2e-3 + 1e-2 |y| + 10 sigma of the fp16 reference,
+    sigma the RMS of the reference's own fp16-vs-fp32 difference,
+and the greedy token equal to the reference's wherever its top two logits
+differ by more than that elementwise bound.  The strict 2e-3 + 1e-2 |y| bar
+holds per kernel at these shapes (tests/test_linear_gpu.py and the attention
+tests) and end to end on the small model (tests/test_sdk_gpu.py)."""
 import numpy as np
 import pytest
 
@@ -22,15 +36,27 @@ RTOL, ATOL = 1e-2, 2e-3
 STEPS = 4
 
 
-def close(got, want, what):
-    err = np.abs(got - want)
-    bad = err > ATOL + RTOL * np.abs(want)
-    assert not bad.any(), f"{what}: {bad.sum()} / {bad.size} logits outside tolerance; max err {err.max():.3e}"
+def rel_l2(a, b):
+    return float(np.linalg.norm(np.asarray(a, np.float64) - b) / np.linalg.norm(np.asarray(b, np.float64)))
 
 
-def check_token(tok, logits_ref):
+def check(got, want16, want32, what):
+    """Returns the elementwise bound used (for the greedy-token check)."""
+    noise = rel_l2(want16, want32)
+    sigma = float(np.sqrt(np.mean((want16.astype(np.float64) - want32) ** 2)))
+    d16, d32 = rel_l2(got, want16), rel_l2(got, want32)
+    assert d16 <= 2.0 * noise, f"{what}: GPU vs fp16 reference {d16:.2e}, reference's own noise {noise:.2e}"
+    assert d32 <= 2.0 * noise, f"{what}: GPU vs fp32 {d32:.2e}, reference's own noise {noise:.2e}"
+    bound = ATOL + RTOL * np.abs(want16) + 10.0 * sigma
+    err = np.abs(got - want16)
+    bad = err > bound
+    assert not bad.any(), f"{what}: {bad.sum()} / {bad.size} logits beyond the bound; max err {err.max():.3e}"
+    return ATOL + 10.0 * sigma
+
+
+def check_token(tok, logits_ref, slack):
     top = np.sort(logits_ref)[-2:]
-    if top[1] - top[0] > ATOL + RTOL * abs(top[1]):
+    if top[1] - top[0] > slack + RTOL * abs(top[1]):
         assert tok == int(np.argmax(logits_ref))
 
 
@@ -49,20 +75,21 @@ def test_llama1b_batch1_matches_decoder_oracle(llama1b, oracle_mod):
     path, t = llama1b
     V = LLAMA_1B["vocab_size"]
     prompt = np.random.default_rng(24).integers(0, V, 24).astype(np.int32)
-    ref = DecoderOracle(LLAMA_1B, t, group_size=32)
+    r16 = DecoderOracle(LLAMA_1B, t, group_size=32)
+    r32 = DecoderOracle(LLAMA_1B, t, group_size=32, precision="f32")
     with sdk.Package(path) as pkg:
         with pkg.select(context_length=64).session() as s:
             s.prefill(prompt)
-            want = ref.forward(prompt)
-            close(s.last_logits(V), want, "prompt")
+            want = r16.forward(prompt)
+            slack = check(s.last_logits(V), want, r32.forward(prompt), "prompt")
             r = s.decode()
-            check_token(r.next_token_id, want)
+            check_token(r.next_token_id, want, slack)
             tok = r.next_token_id
             for step in range(STEPS):
-                want = ref.forward([tok])
+                want = r16.forward([tok])
                 r = s.decode()
-                close(s.last_logits(V), want, f"step {step}")
-                check_token(r.next_token_id, want)
+                slack = check(s.last_logits(V), want, r32.forward([tok]), f"step {step}")
+                check_token(r.next_token_id, want, slack)
                 tok = r.next_token_id
 
 
@@ -82,11 +109,13 @@ def test_llama1b_batch16_matches_decoder_oracle(llama1b, oracle_mod):
                 toks.append(s.batch_decode())
                 logits.append(s.last_logits().reshape(B, V))
     for b in (0, 11):
-        ref = DecoderOracle(LLAMA_1B, t, group_size=32)
-        want = ref.forward(prompts[b])
-        close(logits[0][b], want, f"sequence {b} prompt")
-        check_token(int(toks[0][b]), want)
+        r16 = DecoderOracle(LLAMA_1B, t, group_size=32)
+        r32 = DecoderOracle(LLAMA_1B, t, group_size=32, precision="f32")
+        want = r16.forward(prompts[b])
+        slack = check(logits[0][b], want, r32.forward(prompts[b]), f"sequence {b} prompt")
+        check_token(int(toks[0][b]), want, slack)
         for i in range(STEPS):
-            want = ref.forward([int(toks[i][b])])
-            close(logits[i + 1][b], want, f"sequence {b} step {i}")
-            check_token(int(toks[i + 1][b]), want)
+            tok = int(toks[i][b])
+            want = r16.forward([tok])
+            slack = check(logits[i + 1][b], want, r32.forward([tok]), f"sequence {b} step {i}")
+            check_token(int(toks[i + 1][b]), want, slack)
