@@ -93,6 +93,28 @@ typedef struct SgMatMulParams {
  * Mirrors armcc::kernels::cpu::FlashAttentionParams (flash_attention.h:25-42),
  * layouts [B, heads, S, head_dim] (flash_attention.h:116,124,137).
  */
+/* Paged KV cache (the reference's planPagedLayout,
+ * compiler/lib/memory/kv_cache_layout.cpp:65-102): a pool of pages
+ * [page][K|V][kv_head][page_size][head_dim] and a table of int32 physical
+ * page ids.  The token at position j of sequence b lives in page
+ * table[b * table_batch_stride + (j / page_size) * table_page_stride], row
+ * j % page_size.  With paging, the K and V pointers of the calls below are
+ * the K and V halves of physical page 0 (V = K + kv_heads * page_size *
+ * head_dim elements in the reference layout), and head h of page p starts
+ * page_stride * p + h * page_size * head_dim elements after them.  A table
+ * entry outside [0, num_pages) is never dereferenced: reads take page 0,
+ * writes are dropped, and bit 4 of the device error word is set
+ * (sg_device_error_check).  No reference counterpart as a C struct (the
+ * reference plans the layout but has no kernel that reads it). */
+typedef struct SgKvPages {
+  const int32_t* table;       /* device int32 page ids                             */
+  int32_t page_size;          /* tokens per page: 16 (the reference's page size)   */
+  int32_t num_pages;          /* pages in the pool                                 */
+  int64_t page_stride;        /* elements between consecutive physical pages       */
+  int64_t table_batch_stride; /* table entries between sequences                   */
+  int64_t table_page_stride;  /* table entries between logical pages               */
+} SgKvPages;
+
 typedef struct SgFlashAttentionParams {
   const void* Q;          /* [B, num_heads,    S_q,  head_dim]                 */
   const void* K;          /* [B, num_kv_heads, S_kv, head_dim]                 */
@@ -121,6 +143,9 @@ typedef struct SgFlashAttentionParams {
    * capacity the launch is sized for.  Lets one captured CUDA graph of a decode
    * step serve every position.  Decode (sg_flash_decode) form only. */
   const int32_t* q_pos_device;
+  /* Optional paged KV cache (NULL: K / V are flat [B, num_kv_heads, S_kv,
+   * head_dim] with the strides above, which are then ignored otherwise). */
+  const SgKvPages* kv_pages;
 } SgFlashAttentionParams;
 
 /* ---------------------------------------------------------------- status */
@@ -302,6 +327,16 @@ SgStatus sg_argmax(const float* logits, int32_t rows, int32_t n, int32_t* out, v
 SgStatus sg_qkv_rope_append(const void* qkv, int32_t tokens, int32_t heads, int32_t kv_heads, int32_t head_dim,
                             const int32_t* positions, int32_t pos0, float base, void* q_out, void* k_cache,
                             void* v_cache, int64_t kv_head_stride, int32_t io_dtype, void* stream);
+
+/* The same with the k / v rows written into a paged KV cache: k_pages / v_pages
+ * are the K and V halves of physical page 0 of the layer's pool and `pages`
+ * says where each position lives (SgKvPages); batch sequences of seq_tokens
+ * tokens each as in sg_qkv_rope_append_batched.  No reference counterpart
+ * (the reference's paged layout has no writer). */
+SgStatus sg_qkv_rope_append_paged(const void* qkv, int32_t batch, int32_t seq_tokens, int32_t heads,
+                                  int32_t kv_heads, int32_t head_dim, const int32_t* positions, int32_t pos0,
+                                  float base, void* q_out, void* k_pages, void* v_pages, const SgKvPages* pages,
+                                  int32_t io_dtype, void* stream);
 
 /* The same for `batch` sequences of seq_tokens tokens each (token t of the
  * input is token t % seq_tokens of sequence t / seq_tokens): q goes to

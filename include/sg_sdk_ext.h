@@ -93,6 +93,26 @@ void sg_session_vocab_range(const ArmSession* sess, uint32_t* lo, uint32_t* hi);
 ArmSession* sg_session_create_ex(ArmGraph* graph, const ArmSessionOptions* opts, uint32_t batch, int32_t rank,
                                  int32_t world, const uint8_t id[128]);
 
+/* ---- paged KV cache ---------------------------------------------------------
+ * Sessions lay out their KV cache as the reference's planner recommends
+ * (compiler/lib/memory/kv_cache_layout.cpp:107-130): flat up to a 4096-token
+ * context, paged above it -- a pool of pages [page][K|V][kv_head][16][dim]
+ * and a page table [logical page][layer][sequence] (:65-102).  Pages are
+ * taken from the pool as the positions advance and returned by
+ * armsess_reset.  SG_KV_LAYOUT=flat or =paged in the environment overrides
+ * the rule.  This call always pages, with a pool of kv_pool_tokens tokens
+ * over all sequences (0: every sequence's full context), so a session
+ * reserves only the KV memory its prompts and generations will use; a
+ * prefill or decode that needs more pages than are left fails with
+ * ARMCC_ERR_OOM before launching anything.  rank / world / id as for
+ * sg_session_create_ex. */
+ArmSession* sg_session_create_paged(ArmGraph* graph, const ArmSessionOptions* opts, uint32_t batch,
+                                    uint64_t kv_pool_tokens, int32_t rank, int32_t world, const uint8_t id[128]);
+
+/* 1 when the session's KV cache is paged (then *pool_pages and
+ * *pages_in_use are set), else 0 (both set to 0). */
+int32_t sg_session_kv_pages(const ArmSession* sess, uint32_t* pool_pages, uint32_t* pages_in_use);
+
 /* Prefills every sequence with n_tokens tokens (tokens[b * n_tokens + i] is
  * token i of sequence b). */
 ArmStatus sg_batch_prefill(ArmSession* sess, const int32_t* tokens, uint32_t n_tokens);

@@ -56,6 +56,18 @@ SG_MM_STATIC_WEIGHTS = 1
 SG_MM_A_SWIGLU = 2
 
 
+class SgKvPages(ctypes.Structure):
+    """Paged KV cache descriptor (include/sg_kernels.h SgKvPages)."""
+    _fields_ = [
+        ("table", ctypes.c_void_p),
+        ("page_size", ctypes.c_int32),
+        ("num_pages", ctypes.c_int32),
+        ("page_stride", ctypes.c_int64),
+        ("table_batch_stride", ctypes.c_int64),
+        ("table_page_stride", ctypes.c_int64),
+    ]
+
+
 class SgFlashAttentionParams(ctypes.Structure):
     """Mirror of armcc::kernels::cpu::FlashAttentionParams (flash_attention.h:25-42) plus extensions."""
     _fields_ = [
@@ -81,6 +93,7 @@ class SgFlashAttentionParams(ctypes.Structure):
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
         ("q_pos_device", ctypes.c_void_p),
+        ("kv_pages", ctypes.POINTER(SgKvPages)),
     ]
 
 
@@ -120,6 +133,14 @@ _SIGS = {
     "sg_embedding": (ctypes.c_int32, [_P, _P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                       ctypes.c_int32, _P]),
     "sg_argmax": (ctypes.c_int32, [_P, ctypes.c_int32, ctypes.c_int32, _P, _P]),
+    "sg_qkv_rope_append_batched": (ctypes.c_int32, [_P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                                    ctypes.c_int32, ctypes.c_int32, _P, ctypes.c_int32,
+                                                    ctypes.c_float, _P, _P, _P, ctypes.c_int64, ctypes.c_int64,
+                                                    ctypes.c_int32, _P]),
+    "sg_qkv_rope_append_paged": (ctypes.c_int32, [_P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                                  ctypes.c_int32, ctypes.c_int32, _P, ctypes.c_int32,
+                                                  ctypes.c_float, _P, _P, _P, ctypes.POINTER(SgKvPages),
+                                                  ctypes.c_int32, _P]),
 }
 
 

@@ -47,7 +47,28 @@ struct AArgs {
   int nsplit, keys_per_split;
   float* part;                  // [B][H][Sq][nsplit][D + 2]  (o..., m, l)
   const int32_t* q_pos_dev;     // device position of query 0 (Skv is then the capacity)
+  // paged KV cache (pt != NULL): key j of sequence b lives in physical page
+  // pt[b * pt_bs + (j / 16) * pt_ps] of the pool, row j % 16
+  const int32_t* pt;
+  int64_t pt_bs, pt_ps, page_stride;
+  int npages;
+  int* err;                     // device error word (a page id outside the pool)
 };
+
+// Element offset of (sequence b, kv head hk, key) in K and in V: the flat
+// [B][Hkv][S][D] layout with the caller's strides, or row key % 16 of the
+// page that holds it, [page][kv_head][16][D] within the pool (the reference's
+// page layout, kv_cache_layout.cpp:65-102).  A page id outside the pool reads
+// page 0 instead and sets bit 4 of the device error word.
+__device__ __forceinline__ int64_t kv_off(const AArgs& a, int b, int hk, int key) {
+  if (!a.pt) return (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs + (int64_t)key * a.D;
+  int page = __ldg(a.pt + (int64_t)b * a.pt_bs + (int64_t)(key >> 4) * a.pt_ps);
+  if ((unsigned)page >= (unsigned)a.npages) {
+    if (a.err) atomicOr(a.err, 4);
+    page = 0;
+  }
+  return (int64_t)page * a.page_stride + ((int64_t)hk * 16 + (key & 15)) * a.D;
+}
 
 __device__ __forceinline__ float ld_io(const void* p, int dt, int64_t i) {
   switch (dt) {
@@ -97,7 +118,6 @@ __global__ void __launch_bounds__(kThreads) attn_cc_kernel(AArgs a) {
   int j0 = split * kps;
   int j1 = min(Skv, j0 + kps);
   if (a.causal) j1 = min(j1, q_pos0 + q0 + nq);  // last visible key + 1
-  const int64_t kvbase = (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs;
 
   float q[kMaxRowsPerWarp][DPL], o[kMaxRowsPerWarp][DPL], m[kMaxRowsPerWarp], l[kMaxRowsPerWarp];
   int pos[kMaxRowsPerWarp];
@@ -130,7 +150,7 @@ __global__ void __launch_bounds__(kThreads) attn_cc_kernel(AArgs a) {
     const int nk = min(kKeyTile, j1 - jt);
     __syncthreads();
     for (int i = threadIdx.x; i < nk * a.D; i += kThreads) {
-      const int64_t off = kvbase + (int64_t)(jt + i / a.D) * a.D + (i % a.D);
+      const int64_t off = kv_off(a, b, hk, jt + i / a.D) + (i % a.D);
       ks[i] = ld_io(a.K, a.io_dt, off);
       vs[i] = ld_io(a.V, a.io_dt, off);
     }
@@ -221,7 +241,6 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(AArgs a) {
   const int j0 = split * kps;
   int j1 = min(Skv, j0 + kps);
   if (a.causal) j1 = min(j1, q_pos0 + nq);
-  const int64_t kvbase = (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs;
   const float qscale = a.scale * 1.4426950408889634f;
   for (int i = tid; i < R * D; i += kThreads) {
     const int r = i / D, d = i % D;
@@ -242,7 +261,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(AArgs a) {
       const int j = i / D, d = i % D;
       float kv = 0.f, vv = 0.f;
       if (j < nk) {
-        const int64_t off = kvbase + (int64_t)(jt + j) * D + d;
+        const int64_t off = kv_off(a, b, hk, jt + j) + d;
         kv = ld_io(a.K, a.io_dt, off);
         vv = ld_io(a.V, a.io_dt, off);
       }
@@ -434,7 +453,6 @@ __global__ void __launch_bounds__(kThreads) attn_dec_cluster_kernel(AArgs a) {
   const int j0 = split * kps;
   int j1 = min(Skv, j0 + kps);
   if (a.causal) j1 = min(j1, q_pos0 + nq);
-  const int64_t kvbase = (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs;
   const float qscale = a.scale * 1.4426950408889634f;
   const int kk = tid >> 1, part = tid & 1;
   float* qpart = qs + part * (R * DH + 4);
@@ -451,10 +469,9 @@ __global__ void __launch_bounds__(kThreads) attn_dec_cluster_kernel(AArgs a) {
   auto load_tile = [&](int jt) {
     const int key = jt + kk;
     const bool live = key < j1;
-    const uint4* kp = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.K) +
-                                                     ((kvbase + (int64_t)key * D + part * DH) * IoVec<IO>::kBytes));
-    const uint4* vp = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.V) +
-                                                     ((kvbase + (int64_t)key * D + part * DH) * IoVec<IO>::kBytes));
+    const int64_t e0 = kv_off(a, b, hk, live ? key : j0) + part * DH;
+    const uint4* kp = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.K) + e0 * IoVec<IO>::kBytes);
+    const uint4* vp = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.V) + e0 * IoVec<IO>::kBytes);
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       kr[i] = live ? __ldg(kp + i) : make_uint4(0u, 0u, 0u, 0u);
@@ -666,7 +683,6 @@ __global__ void __launch_bounds__(kDecMmaThreads) attn_dec_mma_kernel(AArgs a) {
   const int j0 = split * kps;
   int j1 = min(Skv, j0 + kps);
   if (a.causal) j1 = min(j1, q_pos0 + nq);
-  const int64_t kvbase = (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs;
   const int kk = tid >> 2, part = tid & 3;  // loader role: quarter `part` of key kk
 
   const int ntiles = j1 > j0 ? (j1 - j0 + KT - 1) / KT : 0;
@@ -674,7 +690,7 @@ __global__ void __launch_bounds__(kDecMmaThreads) attn_dec_mma_kernel(AArgs a) {
   auto issue_tile = [&](int it) {
     const int key = j0 + it * KT + kk;
     const bool live = key < j1;
-    const int64_t e0 = kvbase + (int64_t)(live ? key : j0) * D + part * (D / 4);
+    const int64_t e0 = kv_off(a, b, hk, live ? key : j0) + part * (D / 4);
     const uint16_t* kp = static_cast<const uint16_t*>(a.K) + e0;
     const uint16_t* vp = static_cast<const uint16_t*>(a.V) + e0;
     __half* kd = kvs + (size_t)(it % kDecMmaStages) * 2 * KT * KP + kk * KP + part * (D / 4);
@@ -900,7 +916,6 @@ __global__ void __launch_bounds__(kDecWarpThreads) attn_dec_warp_kernel(AArgs a)
   const int j0 = split * kps;
   int j1 = min(Skv, j0 + kps);
   if (a.causal) j1 = min(j1, q_pos0 + nq);
-  const int64_t kvbase = (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs;
   const int ngroups = j1 > j0 ? (j1 - j0 + KG - 1) / KG : 0;
   const int nmine = ngroups > warp ? (ngroups - warp + kW - 1) / kW : 0;  // groups warp, warp + kW, ...
 
@@ -915,7 +930,7 @@ __global__ void __launch_bounds__(kDecWarpThreads) attn_dec_warp_kernel(AArgs a)
       const int kl = pc / (D / 8), part = pc % (D / 8);
       const int key = key0 + kl;
       const bool live = key < j1;
-      const int64_t e0 = kvbase + (int64_t)(live ? key : j0) * D + part * 8;
+      const int64_t e0 = kv_off(a, b, hk, live ? key : j0) + part * 8;
       sgd::cp_async_16(kd + kl * KP + part * 8, static_cast<const uint16_t*>(a.K) + e0, live);
       sgd::cp_async_16(vd + kl * KP + part * 8, static_cast<const uint16_t*>(a.V) + e0, live);
     }
@@ -1136,6 +1151,13 @@ SgStatus attn_validate(const SgFlashAttentionParams* p, const char* name) {
                p->io_dtype);
   const int skv = p->S_kv > 0 ? p->S_kv : p->S;
   SG_CHECK_ARG(skv >= 1, "%s: S_kv must be >= 1", name);
+  if (const SgKvPages* pg = p->kv_pages) {
+    SG_CHECK_ARG(pg->table != nullptr && pg->num_pages > 0, "%s: paged KV cache without a table or pages", name);
+    SG_CHECK_ARG(pg->page_size == 16, "%s: page_size %d unsupported (16 tokens per page)", name, pg->page_size);
+    SG_CHECK_ARG(pg->page_stride >= (int64_t)hkv * 16 * p->head_dim,
+                 "%s: page_stride %lld smaller than a page's %d kv heads", name, (long long)pg->page_stride, hkv);
+    SG_CHECK_ARG(pg->table_page_stride != 0 || skv <= 16, "%s: table_page_stride is 0", name);
+  }
   return SG_OK;
 }
 
@@ -1170,6 +1192,17 @@ SgStatus attn_cc_run(const SgFlashAttentionParams* p, void* stream, int want_spl
   a.kv_hs = p->kv_head_stride > 0 ? p->kv_head_stride : (int64_t)a.Skv * a.D;
   a.kv_bs = p->kv_batch_stride > 0 ? p->kv_batch_stride : (int64_t)a.Hkv * a.kv_hs;
   a.io_dt = p->io_dtype == SG_DT_DEFAULT ? SG_DT_F16 : p->io_dtype;
+  if (const SgKvPages* pg = p->kv_pages) {
+    a.pt = pg->table;
+    a.pt_bs = pg->table_batch_stride;
+    a.pt_ps = pg->table_page_stride;
+    a.page_stride = pg->page_stride;
+    a.npages = pg->num_pages;
+    st = device_error_word(&a.err);
+    if (st != SG_OK) return st;
+    a.kv_hs = (int64_t)16 * a.D;  // within a page; for the alignment checks below
+    a.kv_bs = pg->page_stride;
+  }
   // query positions per work item: at most kWarps * kMaxRowsPerWarp rows (G * qb)
   a.qb = std::max(1, (kWarps * kMaxRowsPerWarp) / a.G);
   SG_CHECK_ARG(a.G <= kWarps * kMaxRowsPerWarp, "%s: more than %d query heads per kv head", name,

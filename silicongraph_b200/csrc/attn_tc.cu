@@ -65,7 +65,15 @@ struct TArgs {
   int causal, q_pos0;
   int n_qt;
   int* err;
+  // paged KV cache: the K (and, unless copied flat, V) maps are [page][kv head]
+  // [16 rows][D] and key j of sequence b lives in page pt[b * pt_bs + (j / 16) * pt_ps]
+  const int32_t* pt;
+  int64_t pt_bs, pt_ps;
+  int npages;
+  int paged_k, paged_v;
 };
+constexpr int kPageRows = 16;                // keys per page
+constexpr int kPagesPerTile = kKT / kPageRows;
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -169,30 +177,69 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kWarpK || warp == kWarpV) {
     // ------------------------------------------------------------ loaders
-    if (lane == 0) {
-      const bool is_k = warp == kWarpK;
-      const CUtensorMap* map = is_k ? &tmK : &tmV;
-      uint64_t* fullb = is_k ? k_full : v_full;
-      uint64_t* emptyb = is_k ? k_empty : v_empty;
-      unsigned char* base = smem + (is_k ? C_::kKOff : C_::kVOff);
-      if (is_k) {
-        mbar_arrive_expect_tx(q_full, C_::kTile);
-        for (int bx = 0; bx < C_::kBoxes; ++bx)
-          tma_load_3d(smem + C_::kQOff + bx * C_::kBox, &tmQ, bx * 64, q0, hb, q_full);
-      }
-      uint32_t issued[kStages] = {0, 0};
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j % kStages;
-        const uint32_t use = j / kStages;
-        if (*abort_flag || !mbar_wait(&emptyb[st], (use & 1) ^ 1, a.err)) {
-          *abort_flag = 1;
-          break;
+    // lane 0 issues the copies; with a paged cache lanes 0..7 first look up the
+    // tile's eight page ids, one tile ahead of its copies
+    const bool is_k = warp == kWarpK;
+    const CUtensorMap* map = is_k ? &tmK : &tmV;
+    uint64_t* fullb = is_k ? k_full : v_full;
+    uint64_t* emptyb = is_k ? k_empty : v_empty;
+    unsigned char* base = smem + (is_k ? C_::kKOff : C_::kVOff);
+    const bool paged = is_k ? a.paged_k : a.paged_v;
+    // physical page of logical page kPagesPerTile * j + lane (page 0, whose rows the
+    // mask hides, past the keys; a bad id reads page 0 and is reported)
+    auto page_of = [&](int j) -> int {
+      const int lp = j * kPagesPerTile + lane;
+      int pg = 0;
+      if (lane < kPagesPerTile && j < n_kv && lp * kPageRows < a.Skv) {
+        pg = __ldg(a.pt + (int64_t)b * a.pt_bs + (int64_t)lp * a.pt_ps);
+        if ((unsigned)pg >= (unsigned)a.npages) {
+          atomicOr(a.err, 4);
+          pg = 0;
         }
+      }
+      return pg;
+    };
+    if (is_k && lane == 0) {
+      mbar_arrive_expect_tx(q_full, C_::kTile);
+      for (int bx = 0; bx < C_::kBoxes; ++bx)
+        tma_load_3d(smem + C_::kQOff + bx * C_::kBox, &tmQ, bx * 64, q0, hb, q_full);
+    }
+    uint32_t issued[kStages] = {0, 0};
+    int pg_next = paged ? page_of(0) : 0;
+    for (int j = 0; j < n_kv; ++j) {
+      const int st = j % kStages;
+      const uint32_t use = j / kStages;
+      const int pg_cur = pg_next;
+      if (paged) pg_next = page_of(j + 1);  // in flight while this tile waits for its stage
+      int ok = 1;
+      if (lane == 0) ok = (!*abort_flag && mbar_wait(&emptyb[st], (use & 1) ^ 1, a.err)) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) *abort_flag = 1;
+        break;
+      }
+      if (paged) {
+        int pages[kPagesPerTile];
+#pragma unroll
+        for (int i = 0; i < kPagesPerTile; ++i) pages[i] = __shfl_sync(0xffffffffu, pg_cur, i);
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&fullb[st], C_::kTile);
+          // a 16-row box lands 2 KB into the 128-row block: the 128-byte swizzle
+          // pattern (1 KB period) is that of the whole tile
+#pragma unroll
+          for (int i = 0; i < kPagesPerTile; ++i)
+            for (int bx = 0; bx < C_::kBoxes; ++bx)
+              tma_load_4d(base + st * C_::kTile + bx * C_::kBox + i * kPageRows * 128, map, bx * 64, 0, hkv,
+                          pages[i], &fullb[st]);
+        }
+      } else if (lane == 0) {
         mbar_arrive_expect_tx(&fullb[st], C_::kTile);
         for (int bx = 0; bx < C_::kBoxes; ++bx)
           tma_load_4d(base + st * C_::kTile + bx * C_::kBox, map, bx * 64, j * kKT, hkv, b, &fullb[st]);
-        issued[st] = use + 1;
       }
+      issued[st] = use + 1;
+    }
+    if (lane == 0) {
       for (int st = 0; st < kStages; ++st)
         if (issued[st]) mbar_wait(&fullb[st], (issued[st] - 1) & 1, a.err);
       if (is_k) mbar_wait(q_full, 0, a.err);
@@ -358,8 +405,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // V [B, Hkv, Skv, D] bf16 (strided) -> contiguous fp16, 8 values per thread.
+// bf16 V -> contiguous fp16 [B][Hkv][Skv][D]; from a paged cache when pt != NULL
+// (kv_bs is then the page stride).
 __global__ void v_to_f16_kernel(const __nv_bfloat16* V, int64_t kv_bs, int64_t kv_hs, int Hkv, int Skv, int D,
-                                int64_t total8, __half* out) {
+                                int64_t total8, __half* out, const int32_t* pt, int64_t pt_bs, int64_t pt_ps,
+                                int npages, int* err) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total8; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = i * 8;
     const int d = (int)(e % D);
@@ -367,7 +417,18 @@ __global__ void v_to_f16_kernel(const __nv_bfloat16* V, int64_t kv_bs, int64_t k
     const int s = (int)(row % Skv);
     const int64_t bh = row / Skv;
     const int hk = (int)(bh % Hkv), b = (int)(bh / Hkv);
-    const uint4 v = *reinterpret_cast<const uint4*>(V + b * kv_bs + hk * kv_hs + (int64_t)s * D + d);
+    int64_t src;
+    if (pt) {
+      int pg = __ldg(pt + (int64_t)b * pt_bs + (int64_t)(s / kPageRows) * pt_ps);
+      if ((unsigned)pg >= (unsigned)npages) {
+        atomicOr(err, 4);
+        pg = 0;
+      }
+      src = pg * kv_bs + ((int64_t)hk * kPageRows + s % kPageRows) * D + d;
+    } else {
+      src = b * kv_bs + hk * kv_hs + (int64_t)s * D + d;
+    }
+    const uint4 v = *reinterpret_cast<const uint4*>(V + src);
     const uint32_t* w = reinterpret_cast<const uint32_t*>(&v);
     uint4 o;
     uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
@@ -441,7 +502,11 @@ bool tc_qualifies(const SgFlashAttentionParams* p) {
   const int64_t kv_hs = p->kv_head_stride > 0 ? p->kv_head_stride : (int64_t)Skv * D;
   const int64_t kv_bs = p->kv_batch_stride > 0 ? p->kv_batch_stride : (int64_t)Hkv * kv_hs;
   if (!aligned16(p->Q) || !aligned16(p->K) || !aligned16(p->V) || !aligned16(p->O)) return false;
-  if ((kv_hs * 2) % 16 != 0 || (kv_bs * 2) % 16 != 0) return false;
+  if (p->kv_pages) {
+    if (p->kv_pages->page_size != kPageRows || (p->kv_pages->page_stride * 2) % 16 != 0) return false;
+  } else if ((kv_hs * 2) % 16 != 0 || (kv_bs * 2) % 16 != 0) {
+    return false;
+  }
   const int q_pos0 = p->q_pos0 >= 0 ? p->q_pos0 : Skv - p->S;
   return q_pos0 >= 0;  // queries before the first key: the CUDA-core path reports it
 }
@@ -487,8 +552,11 @@ SgStatus attn_tc_run(const SgFlashAttentionParams* p, cudaStream_t cs, void* ws,
     }
     const int64_t total8 = (int64_t)p->B * Hkv * Skv * D / 8;
     const int blocks = (int)std::min<int64_t>((total8 + 255) / 256, 148 * 16);
-    v_to_f16_kernel<<<blocks, 256, 0, cs>>>(static_cast<const __nv_bfloat16*>(p->V), kv_bs, kv_hs, Hkv, Skv, D,
-                                            total8, static_cast<__half*>(ws));
+    const SgKvPages* pg = p->kv_pages;
+    v_to_f16_kernel<<<blocks, 256, 0, cs>>>(static_cast<const __nv_bfloat16*>(p->V), pg ? pg->page_stride : kv_bs,
+                                            kv_hs, Hkv, Skv, D, total8, static_cast<__half*>(ws),
+                                            pg ? pg->table : nullptr, pg ? pg->table_batch_stride : 0,
+                                            pg ? pg->table_page_stride : 0, pg ? pg->num_pages : 0, err);
     st = check_launch("v_to_f16_kernel");
     if (st != SG_OK) return st;
     vsrc = ws;
@@ -505,12 +573,29 @@ SgStatus attn_tc_run(const SgFlashAttentionParams* p, cudaStream_t cs, void* ws,
     st = make_tensor_map(&tq, dt, 3, const_cast<void*>(p->Q), dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st != SG_OK) return st;
   }
-  {
+  const SgKvPages* pages = p->kv_pages;
+  if (pages) {
+    // the pool as [page][kv head][16 rows][D]; one 16-row box per page
+    const uint64_t pdims[4] = {(uint64_t)D, (uint64_t)kPageRows, (uint64_t)Hkv, (uint64_t)pages->num_pages};
+    const uint64_t pstr[3] = {(uint64_t)D * 2, (uint64_t)kPageRows * D * 2, (uint64_t)pages->page_stride * 2};
+    const uint32_t pbox[4] = {64, (uint32_t)kPageRows, 1, 1};
+    st = make_tensor_map(&tk, dt, 4, const_cast<void*>(p->K), pdims, pstr, pbox, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != SG_OK) return st;
+    if (io != SG_DT_BF16) {
+      st = make_tensor_map(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(p->V), pdims, pstr, pbox,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+      if (st != SG_OK) return st;
+    }
+  } else {
     const uint64_t dims[4] = {(uint64_t)D, (uint64_t)Skv, (uint64_t)Hkv, (uint64_t)p->B};
     const uint64_t str[3] = {(uint64_t)D * 2, (uint64_t)kv_hs * 2, (uint64_t)kv_bs * 2};
     const uint32_t box[4] = {64, (uint32_t)kKT, 1, 1};
     st = make_tensor_map(&tk, dt, 4, const_cast<void*>(p->K), dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st != SG_OK) return st;
+  }
+  if (!pages || io == SG_DT_BF16) {  // V flat: the caller's, or the fp16 copy of a bf16 V
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)Skv, (uint64_t)Hkv, (uint64_t)p->B};
+    const uint32_t box[4] = {64, (uint32_t)kKT, 1, 1};
     const uint64_t vstr[3] = {(uint64_t)D * 2, (uint64_t)v_hs * 2, (uint64_t)v_bs * 2};
     st = make_tensor_map(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(vsrc), dims, vstr, box,
                          CU_TENSOR_MAP_SWIZZLE_128B);
@@ -529,6 +614,14 @@ SgStatus attn_tc_run(const SgFlashAttentionParams* p, cudaStream_t cs, void* ws,
   a.q_pos0 = p->q_pos0 >= 0 ? p->q_pos0 : Skv - p->S;
   a.n_qt = (p->S + kQT - 1) / kQT;
   a.err = err;
+  if (pages) {
+    a.pt = pages->table;
+    a.pt_bs = pages->table_batch_stride;
+    a.pt_ps = pages->table_page_stride;
+    a.npages = pages->num_pages;
+    a.paged_k = 1;
+    a.paged_v = io != SG_DT_BF16;
+  }
   const int grid = a.n_qt * a.H * a.B;
   *handled = true;
   if (D == 64) return io == SG_DT_BF16 ? launch_tc<64, true>(tq, tk, tv, a, grid, cs)

@@ -3,7 +3,9 @@
 //     split, q and k are rotated (rope_apply_neon, matmul_neon.h:262-275),
 //     q is written head-major [H, T, D] for attention and k / v are appended to
 //     the layer's KV cache rows (kv_cache_layout.cpp:16-53 flat layout
-//     [K|V][kv_head][seq][dim]) at each token's position;
+//     [K|V][kv_head][seq][dim], or the paged layout of :65-102, pages
+//     [K|V][kv_head][16][dim] found through a page table) at each token's
+//     position;
 //   head_transpose: attention output [H, T, D] -> [T, H, D] for the output
 //     projection.
 // Positions come from a device array (so one captured decode step serves
@@ -12,11 +14,19 @@
 
 namespace {
 
+// Where a token's k / v rows go in a paged cache (pt == nullptr: flat).
+struct PageView {
+  const int32_t* pt;
+  int64_t pt_bs, pt_ps, page_stride;
+  int npages;
+  int* err;
+};
+
 template <typename T>
 __global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, int T_, int Ts, int H, int Hkv, int D,
                                        const int32_t* __restrict__ pos, int pos0, float base, T* __restrict__ q_out,
                                        T* __restrict__ k_cache, T* __restrict__ v_cache, int64_t kv_head_stride,
-                                       int64_t kv_batch_stride) {
+                                       int64_t kv_batch_stride, PageView pv) {
   sgd::pdl_wait();  // inputs come from the previous kernel on the stream
   sgd::pdl_launch_dependents();
   const int half = D / 2;
@@ -39,9 +49,23 @@ __global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, int T_, int Ts
       x1 = y1;
     }
     T* dst;
-    if (slot < H) dst = q_out + (((int64_t)b * H + slot) * Ts + tl) * D;
-    else if (slot < H + Hkv) dst = k_cache + b * kv_batch_stride + (slot - H) * kv_head_stride + (int64_t)p * D;
-    else dst = v_cache + b * kv_batch_stride + (slot - H - Hkv) * kv_head_stride + (int64_t)p * D;
+    if (slot < H) {
+      dst = q_out + (((int64_t)b * H + slot) * Ts + tl) * D;
+    } else {
+      const bool is_k = slot < H + Hkv;
+      const int hk = is_k ? slot - H : slot - H - Hkv;
+      T* cache = is_k ? k_cache : v_cache;
+      if (pv.pt) {
+        const int pg = __ldg(pv.pt + (int64_t)b * pv.pt_bs + (int64_t)(p >> 4) * pv.pt_ps);
+        if ((unsigned)pg >= (unsigned)pv.npages) {  // no such page: the row is dropped and reported
+          if (i == 0) atomicOr(pv.err, 4);
+          continue;
+        }
+        dst = cache + (int64_t)pg * pv.page_stride + ((int64_t)hk * 16 + (p & 15)) * D;
+      } else {
+        dst = cache + b * kv_batch_stride + hk * kv_head_stride + (int64_t)p * D;
+      }
+    }
     dst[i] = (T)x0;
     dst[i + half] = (T)x1;
   }
@@ -263,10 +287,10 @@ __global__ void tp_argmax_pick_kernel(const float* __restrict__ all, int world, 
 
 extern "C" {
 
-SgStatus sg_qkv_rope_append_batched(const void* qkv, int32_t batch, int32_t seq_tokens, int32_t heads,
-                                    int32_t kv_heads, int32_t head_dim, const int32_t* positions, int32_t pos0,
-                                    float base, void* q_out, void* k_cache, void* v_cache, int64_t kv_head_stride,
-                                    int64_t kv_batch_stride, int32_t io_dtype, void* stream) {
+static SgStatus qkv_rope_append_run(const void* qkv, int32_t batch, int32_t seq_tokens, int32_t heads, int32_t kv_heads,
+                             int32_t head_dim, const int32_t* positions, int32_t pos0, float base, void* q_out,
+                             void* k_cache, void* v_cache, int64_t kv_head_stride, int64_t kv_batch_stride,
+                             const SgKvPages* pages, int32_t io_dtype, void* stream) {
   SG_CHECK_ARG(batch >= 0 && seq_tokens >= 0 && heads > 0 && kv_heads > 0 && head_dim > 0,
                "sg_qkv_rope_append: bad size");
   const int64_t tokens = (int64_t)batch * seq_tokens;
@@ -274,9 +298,24 @@ SgStatus sg_qkv_rope_append_batched(const void* qkv, int32_t batch, int32_t seq_
   SG_CHECK_ARG(tokens <= INT32_MAX, "sg_qkv_rope_append: too many tokens");
   SG_CHECK_ARG(qkv && q_out && k_cache && v_cache, "sg_qkv_rope_append: NULL pointer");
   SG_CHECK_ARG(head_dim % 2 == 0, "sg_qkv_rope_append: head_dim %d is odd", head_dim);
-  SG_CHECK_ARG(kv_head_stride >= head_dim, "sg_qkv_rope_append: kv_head_stride < head_dim");
-  SG_CHECK_ARG(batch == 1 || kv_batch_stride >= kv_heads * kv_head_stride,
-               "sg_qkv_rope_append: kv_batch_stride smaller than one sequence's cache");
+  PageView pv{};
+  if (pages) {
+    SG_CHECK_ARG(pages->table && pages->num_pages > 0 && pages->page_size == 16,
+                 "sg_qkv_rope_append_paged: needs a table, pages and 16 tokens per page");
+    SG_CHECK_ARG(pages->page_stride >= (int64_t)kv_heads * 16 * head_dim,
+                 "sg_qkv_rope_append_paged: page_stride smaller than a page's kv heads");
+    pv.pt = pages->table;
+    pv.pt_bs = pages->table_batch_stride;
+    pv.pt_ps = pages->table_page_stride;
+    pv.page_stride = pages->page_stride;
+    pv.npages = pages->num_pages;
+    SgStatus es = sg::device_error_word(&pv.err);
+    if (es != SG_OK) return es;
+  } else {
+    SG_CHECK_ARG(kv_head_stride >= head_dim, "sg_qkv_rope_append: kv_head_stride < head_dim");
+    SG_CHECK_ARG(batch == 1 || kv_batch_stride >= kv_heads * kv_head_stride,
+                 "sg_qkv_rope_append: kv_batch_stride smaller than one sequence's cache");
+  }
   const int dt = io_dtype == SG_DT_DEFAULT ? SG_DT_F16 : io_dtype;
   SG_CHECK_ARG(dt == SG_DT_F16 || dt == SG_DT_BF16, "sg_qkv_rope_append: io_dtype %d unsupported", io_dtype);
   cudaStream_t cs = static_cast<cudaStream_t>(stream);
@@ -286,14 +325,31 @@ SgStatus sg_qkv_rope_append_batched(const void* qkv, int32_t batch, int32_t seq_
                                 static_cast<const __half*>(qkv), (int)tokens, (int)seq_tokens, (int)heads,
                                 (int)kv_heads, (int)head_dim, positions, (int)pos0, base, static_cast<__half*>(q_out),
                                 static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), kv_head_stride,
-                                kv_batch_stride));
+                                kv_batch_stride, pv));
   else
     SG_CUDA_TRY(sgd::launch_pdl(qkv_rope_append_kernel<__nv_bfloat16>, dim3(grid_of(total)), dim3(256), 0, cs,
                                 static_cast<const __nv_bfloat16*>(qkv), (int)tokens, (int)seq_tokens, (int)heads,
                                 (int)kv_heads, (int)head_dim, positions, (int)pos0, base,
                                 static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_cache),
-                                static_cast<__nv_bfloat16*>(v_cache), kv_head_stride, kv_batch_stride));
+                                static_cast<__nv_bfloat16*>(v_cache), kv_head_stride, kv_batch_stride, pv));
   return SG_OK;
+}
+
+SgStatus sg_qkv_rope_append_batched(const void* qkv, int32_t batch, int32_t seq_tokens, int32_t heads,
+                                    int32_t kv_heads, int32_t head_dim, const int32_t* positions, int32_t pos0,
+                                    float base, void* q_out, void* k_cache, void* v_cache, int64_t kv_head_stride,
+                                    int64_t kv_batch_stride, int32_t io_dtype, void* stream) {
+  return qkv_rope_append_run(qkv, batch, seq_tokens, heads, kv_heads, head_dim, positions, pos0, base, q_out, k_cache,
+                             v_cache, kv_head_stride, kv_batch_stride, nullptr, io_dtype, stream);
+}
+
+SgStatus sg_qkv_rope_append_paged(const void* qkv, int32_t batch, int32_t seq_tokens, int32_t heads,
+                                  int32_t kv_heads, int32_t head_dim, const int32_t* positions, int32_t pos0,
+                                  float base, void* q_out, void* k_pages, void* v_pages, const SgKvPages* pages,
+                                  int32_t io_dtype, void* stream) {
+  SG_CHECK_ARG(pages != nullptr, "sg_qkv_rope_append_paged: pages is NULL");
+  return qkv_rope_append_run(qkv, batch, seq_tokens, heads, kv_heads, head_dim, positions, pos0, base, q_out,
+                             k_pages, v_pages, 0, 0, pages, io_dtype, stream);
 }
 
 SgStatus sg_qkv_rope_append(const void* qkv, int32_t tokens, int32_t heads, int32_t kv_heads, int32_t head_dim,

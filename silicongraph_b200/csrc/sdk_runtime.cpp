@@ -376,6 +376,17 @@ struct ArmSession_ {
   char* kv = nullptr;
   int64_t kv_head_stride = 0;  // elements
   int64_t kv_block = 0;        // elements of one [kv_head][seq][dim] block (K or V of one layer)
+  // Paged KV cache (kv_cache_layout.cpp:65-102): `kv` is then a pool of
+  // pages [page][K|V][kv_head][16][dim] and d_table [logical page][layer]
+  // [sequence] maps every 16 positions of a sequence in a layer to a page.
+  // Pages are taken from the pool as positions advance (all sequences in
+  // lockstep) and returned on reset.
+  bool paged = false;
+  int pool_pages = 0, max_lpages = 0, lpages = 0;
+  int32_t* d_table = nullptr;     // in the slab
+  std::vector<int32_t> h_table;   // host copy
+  std::vector<int32_t> free_pages;
+  std::vector<SgKvPages> kvp;     // per layer
   // activations
   Plan plan;
   char* act = nullptr;
@@ -430,8 +441,11 @@ struct ArmSession_ {
   T* buf(const char* n) { return reinterpret_cast<T*>(act + plan.off(n)); }
   // KV cache [sequence][layer][K|V][kv_head][seq][dim]
   int64_t kv_bstride() const { return (int64_t)c.layers * 2 * kv_block; }  // elements per sequence
-  void* kcache(int l) { return kv + (size_t)(2 * l) * kv_block * 2; }
-  void* vcache(int l) { return kv + (size_t)(2 * l + 1) * kv_block * 2; }
+  // flat: the layer's K / V blocks; paged: the K / V halves of page 0 of the pool
+  void* kcache(int l) { return paged ? kv : kv + (size_t)(2 * l) * kv_block * 2; }
+  void* vcache(int l) {
+    return paged ? kv + (size_t)c.kv_heads * 16 * c.head_dim * 2 : kv + (size_t)(2 * l + 1) * kv_block * 2;
+  }
 };
 
 namespace {
@@ -546,11 +560,18 @@ ArmStatus forward(ArmSession_* S, int Ts, bool from_next, bool dev_pos = false) 
                       st),
            "input rmsnorm");
     if ((r = linear(S, S->qkv[l], S->buf<void>("xnorm"), S->buf<void>("qkv"), T, SG_DT_F16)) != ARMCC_OK) return r;
-    SG_TRY(sg_qkv_rope_append_batched(S->buf<void>("qkv"), B, Ts, c.heads, c.kv_heads, D,
+    if (S->paged) {
+      SG_TRY(sg_qkv_rope_append_paged(S->buf<void>("qkv"), B, Ts, c.heads, c.kv_heads, D,
                                       dev_pos ? S->buf<int32_t>("pos") : nullptr, S->pos, c.rope_theta,
-                                      S->buf<void>("qh"), S->kcache(l), S->vcache(l), S->kv_head_stride,
-                                      S->kv_bstride(), SG_DT_F16, st),
-           "rope / KV append");
+                                      S->buf<void>("qh"), S->kcache(l), S->vcache(l), &S->kvp[l], SG_DT_F16, st),
+             "rope / KV append");
+    } else {
+      SG_TRY(sg_qkv_rope_append_batched(S->buf<void>("qkv"), B, Ts, c.heads, c.kv_heads, D,
+                                        dev_pos ? S->buf<int32_t>("pos") : nullptr, S->pos, c.rope_theta,
+                                        S->buf<void>("qh"), S->kcache(l), S->vcache(l), S->kv_head_stride,
+                                        S->kv_bstride(), SG_DT_F16, st),
+             "rope / KV append");
+    }
     SgFlashAttentionParams a{};
     a.Q = S->buf<void>("qh");
     a.K = S->kcache(l);
@@ -569,6 +590,7 @@ ArmStatus forward(ArmSession_* S, int Ts, bool from_next, bool dev_pos = false) 
     a.q_pos_device = dev_pos ? S->buf<int32_t>("pos") : nullptr;
     a.kv_head_stride = S->kv_head_stride;
     a.kv_batch_stride = S->kv_bstride();
+    a.kv_pages = S->paged ? &S->kvp[l] : nullptr;
     a.workspace = S->attn_ws;
     a.workspace_bytes = S->attn_ws_bytes;
     const void* attn_rows = S->buf<void>("attn");
@@ -690,6 +712,48 @@ ArmStatus decode_step(ArmSession_* S) {
   return r;
 }
 
+// Paged cache: makes sure every sequence has pages for positions < upto in
+// every layer, taking them from the pool; the new table rows go to the
+// device in stream order (one contiguous copy: the table is [logical page]
+// [layer][sequence]).  ARMCC_ERR_OOM when the pool is exhausted.
+ArmStatus ensure_pages(ArmSession_* S, int upto, const char* fn) {
+  if (!S->paged) return ARMCC_OK;
+  const int need = (upto + 15) / 16;
+  if (need <= S->lpages) return ARMCC_OK;
+  const int L = S->c.layers, B = S->batch;
+  if (need > S->max_lpages) {
+    set_err("%s: position %d is past the page table (%d pages of 16 tokens)", fn, upto, S->max_lpages);
+    return ARMCC_ERR_OOM;
+  }
+  const size_t count = (size_t)(need - S->lpages) * L * B;
+  if (S->free_pages.size() < count) {
+    set_err("%s: the KV page pool (%d pages of 16 tokens) cannot hold position %d of %d sequences", fn,
+            S->pool_pages, upto, B);
+    return ARMCC_ERR_OOM;
+  }
+  const size_t first = (size_t)S->lpages * L * B;
+  for (size_t i = first; i < first + count; ++i) {
+    S->h_table[i] = S->free_pages.back();
+    S->free_pages.pop_back();
+  }
+  // from pageable memory: staged before the call returns, so the host copy may change afterwards
+  if (cudaMemcpyAsync(S->d_table + first, S->h_table.data() + first, count * 4, cudaMemcpyHostToDevice, S->st) !=
+      cudaSuccess) {
+    set_err("%s: updating the KV page table failed", fn);
+    return ARMCC_ERR_RUNTIME;
+  }
+  S->lpages = need;
+  return ARMCC_OK;
+}
+
+// Returns every page to the pool (reset): the next positions start from page 0 again.
+void release_pages(ArmSession_* S) {
+  if (!S->paged) return;
+  S->free_pages.clear();
+  for (int pg = S->pool_pages - 1; pg >= 0; --pg) S->free_pages.push_back(pg);
+  S->lpages = 0;
+}
+
 // Reads every sequence's greedy token (and the kernels' error word) back to the host.
 ArmStatus fetch_next(ArmSession_* S) {
   S->next_all.assign(S->batch, -1);
@@ -745,7 +809,8 @@ ArmStatus prefill_tokens(ArmSession_* S, const int32_t* tokens, uint32_t n, cons
       set_err("%s: copying token ids failed", fn);
       return ARMCC_ERR_RUNTIME;
     }
-    const ArmStatus r = forward(S, T, false);
+    ArmStatus r = ensure_pages(S, S->pos + T, fn);
+    if (r == ARMCC_OK) r = forward(S, T, false);
     if (r != ARMCC_OK) return r;
     done += T;
   }
@@ -772,7 +837,8 @@ ArmStatus step_tokens(ArmSession_* S, const char* fn, float* step_ms) {
       set_err("%s: the context of %d tokens is full", fn, S->c.max_context);
       return ARMCC_ERR_OOM;
     }
-    ArmStatus r = decode_step(S);
+    ArmStatus r = ensure_pages(S, S->pos + 1, fn);
+    if (r == ARMCC_OK) r = decode_step(S);
     if (r == ARMCC_OK) r = fetch_next(S);
     if (r != ARMCC_OK) return r;
   }
@@ -939,6 +1005,41 @@ bool setup_peer_allreduce(ArmSession_* S, int max_n) {
 }
 
 // Session of rank `rank` in a group of `world` (world 1: the whole model, no NCCL).
+// KV cache layout of a session: flat [sequence][layer][K|V][kv_head][seq][dim]
+// (kv_cache_layout.cpp:16-53), or paged (:65-102) -- the reference's rule
+// (recommendKVCacheLayout, :107-130) pages contexts above 4096 tokens, in
+// pages of 16 tokens.  kv_mode: 0 that rule, 1 flat, 2 paged; SG_KV_LAYOUT=
+// flat|paged overrides the rule.  pool_tokens: tokens the paged pool holds
+// over all sequences (0 = every sequence's full context).
+struct KvLayout {
+  bool paged = false;
+  int max_lpages = 0, pool_pages = 0;
+  uint64_t pool_bytes = 0, table_bytes = 0;  // paged
+  uint64_t bytes = 0;                          // the KV region of the slab (pool + table, or the flat cache)
+};
+
+KvLayout kv_layout(const ModelCfg& c, int batch, int kv_mode, int64_t pool_tokens) {
+  KvLayout k;
+  k.paged = kv_mode == 2 || (kv_mode == 0 && c.max_context > 4096);
+  if (kv_mode == 0) {
+    if (const char* e = getenv("SG_KV_LAYOUT")) {
+      if (!strcmp(e, "flat")) k.paged = false;
+      else if (!strcmp(e, "paged")) k.paged = true;
+    }
+  }
+  if (!k.paged) {
+    k.bytes = (uint64_t)batch * c.layers * 2 * (uint64_t)c.kv_heads * c.max_context * c.head_dim * 2;
+    return k;
+  }
+  k.max_lpages = (c.max_context + 15) / 16;
+  const int64_t lp_pool = pool_tokens > 0 ? (pool_tokens + 15) / 16 : (int64_t)batch * k.max_lpages;
+  k.pool_pages = (int)std::min<int64_t>(lp_pool * c.layers, INT32_MAX);
+  k.pool_bytes = (uint64_t)k.pool_pages * 2 * c.kv_heads * 16 * c.head_dim * 2;
+  k.table_bytes = align_up((uint64_t)k.max_lpages * c.layers * batch * 4, 256);
+  k.bytes = align_up(k.pool_bytes, 4096) + k.table_bytes;
+  return k;
+}
+
 // Scratch of the linear kernels (largest over the shapes and token counts a
 // session of `batch` sequences uses) and of the attention kernels.
 void session_scratch(const ModelCfg& c, int batch, size_t* lws_out, size_t* aws_out) {
@@ -986,7 +1087,7 @@ void session_scratch(const ModelCfg& c, int batch, size_t* lws_out, size_t* aws_
 }
 
 ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int rank, int world, const uint8_t* id,
-                           int batch) {
+                           int batch, int kv_mode = 0, int64_t pool_tokens = 0) {
   const char* fn = world > 1 ? "sg_session_create_tp" : "armgraph_create_session";
   if (!graph) {
     set_err("%s: graph is NULL", fn);
@@ -1163,7 +1264,8 @@ ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int r
   S->kv_block = (int64_t)c.kv_heads * S->kv_head_stride;
   const uint64_t off_w = 0;
   const uint64_t off_kv = align_up(off_w + w_region, 4096);
-  const uint64_t kv_bytes = (uint64_t)batch * c.layers * 2 * S->kv_block * 2;
+  const KvLayout kl = kv_layout(c, batch, kv_mode, pool_tokens);
+  const uint64_t kv_bytes = kl.bytes;
   const uint64_t off_act = align_up(off_kv + kv_bytes, 4096);
   const uint64_t off_lws = align_up(off_act + S->plan.bytes, 4096);
   S->lin_ws_bytes = align_up(std::max<size_t>(lws, 4096), 256);
@@ -1194,6 +1296,24 @@ ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int r
   graph->peak_bytes = std::max(graph->peak_bytes, S->slab_bytes);
   char* wbase = S->slab + off_w;
   S->kv = S->slab + off_kv;
+  if (kl.paged) {
+    S->paged = true;
+    S->pool_pages = kl.pool_pages;
+    S->max_lpages = kl.max_lpages;
+    S->d_table = reinterpret_cast<int32_t*>(S->kv + align_up(kl.pool_bytes, 4096));
+    S->h_table.assign((size_t)kl.max_lpages * c.layers * batch, 0);
+    S->kvp.resize(c.layers);
+    for (int l = 0; l < c.layers; ++l) {
+      SgKvPages& kp = S->kvp[l];
+      kp.table = S->d_table + (size_t)l * batch;
+      kp.page_size = 16;
+      kp.num_pages = kl.pool_pages;
+      kp.page_stride = (int64_t)2 * c.kv_heads * 16 * c.head_dim;
+      kp.table_batch_stride = 1;
+      kp.table_page_stride = (int64_t)c.layers * batch;
+    }
+    release_pages(S.get());
+  }
   S->act = S->slab + off_act;
   S->lin_ws = S->slab + off_lws;
   S->attn_ws = S->slab + off_aws;
@@ -1362,7 +1482,7 @@ static uint64_t planned_session_bytes(const ArmGraph_* g, int batch) {
   size_t lws = 0, aws = 0;
   session_scratch(c, batch, &lws, &aws);
   const Plan plan = make_plan(c, c.max_chunk * batch, batch, 1);
-  const uint64_t kv_bytes = (uint64_t)batch * c.layers * 2 * (uint64_t)c.kv_heads * c.max_context * c.head_dim * 2;
+  const uint64_t kv_bytes = kv_layout(c, batch, 0, 0).bytes;
   uint64_t off = align_up(w, 4096);
   off = align_up(off + kv_bytes, 4096);
   off = align_up(off + plan.bytes, 4096);
@@ -1483,6 +1603,7 @@ void armsess_destroy(ArmSession* sess) {
 
 void armsess_reset(ArmSession* sess) {
   if (!sess) return;
+  release_pages(sess);
   sess->pos = 0;
   sess->emitted = true;
   sess->next_host = -1;
@@ -1677,6 +1798,31 @@ ArmSession* sg_session_create_ex(ArmGraph* graph, const ArmSessionOptions* opts,
     return nullptr;
   }
   return create_session(graph, opts, rank, world, id, (int)std::min<uint32_t>(batch, 1u << 20));
+}
+
+ArmSession* sg_session_create_paged(ArmGraph* graph, const ArmSessionOptions* opts, uint32_t batch,
+                                    uint64_t kv_pool_tokens, int32_t rank, int32_t world, const uint8_t id[128]) {
+  if (world > 1 && !id) {
+    set_err("sg_session_create_paged: id is NULL");
+    return nullptr;
+  }
+  if (world < 1 || rank < 0 || rank >= world || batch == 0) {
+    set_err("sg_session_create_paged: rank %d outside a group of %d, or batch 0", rank, world);
+    return nullptr;
+  }
+  return create_session(graph, opts, rank, world, id, (int)std::min<uint32_t>(batch, 1u << 20), 2,
+                        (int64_t)std::min<uint64_t>(kv_pool_tokens, (uint64_t)INT64_MAX / 2));
+}
+
+int32_t sg_session_kv_pages(const ArmSession* sess, uint32_t* pool_pages, uint32_t* pages_in_use) {
+  if (!sess || !sess->paged) {
+    if (pool_pages) *pool_pages = 0;
+    if (pages_in_use) *pages_in_use = 0;
+    return 0;
+  }
+  if (pool_pages) *pool_pages = (uint32_t)sess->pool_pages;
+  if (pages_in_use) *pages_in_use = (uint32_t)(sess->pool_pages - (int)sess->free_pages.size());
+  return 1;
 }
 
 ArmStatus sg_batch_prefill(ArmSession* sess, const int32_t* tokens, uint32_t n_tokens) {

@@ -78,6 +78,9 @@ _SIGS = {
     "sg_session_create_tp": (_P, [_P, ctypes.POINTER(ArmSessionOptions), ctypes.c_int32, ctypes.c_int32,
                                   ctypes.POINTER(ctypes.c_uint8)]),
     "sg_session_vocab_range": (None, [_P, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32)]),
+    "sg_session_create_paged": (_P, [_P, ctypes.POINTER(ArmSessionOptions), ctypes.c_uint32, ctypes.c_uint64,
+                                     ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(ctypes.c_uint8)]),
+    "sg_session_kv_pages": (ctypes.c_int32, [_P, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32)]),
     "sg_session_create_ex": (_P, [_P, ctypes.POINTER(ArmSessionOptions), ctypes.c_uint32, ctypes.c_int32,
                                   ctypes.c_int32, ctypes.POINTER(ctypes.c_uint8)]),
     "sg_batch_prefill": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32]),
@@ -206,10 +209,13 @@ class Graph:
         """Device bytes a session of `batch` sequences allocates (one slab)."""
         return lib().sg_graph_session_bytes(self.h, batch)
 
-    def session(self, tp: tuple[int, int, bytes] | None = None, batch: int = 1) -> "Session":
+    def session(self, tp: tuple[int, int, bytes] | None = None, batch: int = 1,
+                kv_pool_tokens: int | None = None) -> "Session":
         """A session; tp = (rank, world, unique id) joins a tensor-parallel group;
-        batch > 1 decodes that many sequences in lockstep."""
-        return Session(self, tp, batch)
+        batch > 1 decodes that many sequences in lockstep; kv_pool_tokens pages
+        the KV cache with a pool of that many tokens over all sequences (0:
+        every sequence's full context)."""
+        return Session(self, tp, batch, kv_pool_tokens)
 
     def run(self, tokens) -> ArmInferenceResult:
         p, n, _keep = _tokens(tokens)
@@ -217,9 +223,14 @@ class Graph:
 
 
 class Session:
-    def __init__(self, graph: Graph, tp: tuple[int, int, bytes] | None = None, batch: int = 1):
+    def __init__(self, graph: Graph, tp: tuple[int, int, bytes] | None = None, batch: int = 1,
+                 kv_pool_tokens: int | None = None):
         self.graph = graph
-        if tp is None and batch == 1:
+        if kv_pool_tokens is not None:
+            rank, world, uid = tp if tp is not None else (0, 1, bytes(128))
+            buf = (ctypes.c_uint8 * 128).from_buffer_copy(uid)
+            self.h = lib().sg_session_create_paged(graph.h, None, batch, kv_pool_tokens, rank, world, buf)
+        elif tp is None and batch == 1:
             self.h = lib().armgraph_create_session(graph.h, None)
         else:
             rank, world, uid = tp if tp is not None else (0, 1, bytes(128))
@@ -301,6 +312,14 @@ class Session:
         if st != ARMCC_OK:
             raise ArmError(st, last_error())
         return out
+
+    @property
+    def kv_pages(self) -> tuple[int, int] | None:
+        """(pages in the pool, pages in use) of a paged KV cache, None when flat."""
+        pool, used = ctypes.c_uint32(), ctypes.c_uint32()
+        if not lib().sg_session_kv_pages(self.h, ctypes.byref(pool), ctypes.byref(used)):
+            return None
+        return pool.value, used.value
 
     @property
     def position(self) -> int:
