@@ -53,6 +53,73 @@ def rank_env():
             int(os.environ.get("WORLD_SIZE", 1)))
 
 
+# ----------------------------------------------------------------------------- process groups
+_PG = {"init": False, "gloo": None}
+
+
+def dist_setup(local_rank):
+    """One NCCL group (device-side barriers and max over ranks) and one gloo
+    group (host-side exchanges) for the whole run; nothing at world 1."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    _, _, world = rank_env()
+    if world == 1 or _PG["init"]:
+        return
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
+                            device_id=torch.device("cuda", local_rank))
+    _PG["gloo"] = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=900))
+    _PG["init"] = True
+
+
+def dist_teardown():
+    if _PG["init"]:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+        _PG["init"] = False
+
+
+def dev_barrier(local_rank):
+    if _PG["init"]:
+        import torch.distributed as dist
+        dist.barrier(device_ids=[local_rank])
+
+
+def dev_max(v, dev):
+    """Max over ranks of a device-timed value (NCCL)."""
+    if not _PG["init"]:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def host_barrier():
+    if _PG["init"]:
+        import torch.distributed as dist
+        dist.barrier(group=_PG["gloo"])
+
+
+def host_max(vals):
+    """Element-wise max over ranks of host values (gloo)."""
+    if not _PG["init"]:
+        return list(vals)
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(list(vals), dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=_PG["gloo"])
+    return [float(x) for x in t]
+
+
+def host_bcast(obj_list, src=0):
+    if _PG["init"]:
+        import torch.distributed as dist
+        dist.broadcast_object_list(obj_list, src=src, group=_PG["gloo"])
+
+
 def read_peak_hbm():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -197,27 +264,39 @@ def cpu_baseline_sample(seconds=12.0):
 
 
 # ----------------------------------------------------------------------------- our arm
+def shard_columns(N, world, rank):
+    """Rank's share of N columns, in whole 128-column strips: (first, count)."""
+    strips = N // 128
+    per, extra = divmod(strips, world)
+    first = (rank * per + min(rank, extra)) * 128
+    count = (per + (1 if rank < extra else 0)) * 128
+    return first, count
+
+
 def run_ours(args):
+    """The INT4 GEMV (K=4096, N=14336, g32, fp32 x and y).  One GPU: the whole
+    GEMV.  N GPUs: its columns split over the ranks (strong scaling, no
+    collective on the data path); value = the algorithmic bytes all ranks
+    streamed / the slowest rank's time."""
     import torch
-    import torch.distributed as dist
 
     from silicongraph_b200 import _lib, kernels
 
     rank, local_rank, world = rank_env()
     torch.cuda.set_device(local_rank)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local_rank))
+    dist_setup(local_rank)
     lib = _lib.load()
     dev = torch.device("cuda", local_rank)
-    K, N, gs = K_DIM, N_DIM, GS
+    K, gs = K_DIM, GS
     G = K // gs
-    nbytes = algorithmic_bytes()
+    n0, N = shard_columns(N_DIM, world, rank)
+    nbytes = algorithmic_bytes(K, N, gs)
+    all_bytes = sum(algorithmic_bytes(K, shard_columns(N_DIM, world, r)[1], gs) for r in range(world))
 
     # inputs generated on the host, copied; weights packed on the device by our packer
-    rng = np.random.default_rng(1234 + rank)
-    W = torch.from_numpy((rng.standard_normal((K, N)) * 0.02).astype(np.float32)).to(dev)
+    # (every rank draws the full matrix from one seed and packs its own columns)
+    rng = np.random.default_rng(1234)
+    W = torch.from_numpy((rng.standard_normal((K, N_DIM)) * 0.02).astype(np.float32)[:, n0:n0 + N].copy()).to(dev)
     x_host = torch.from_numpy(rng.standard_normal((1, K)).astype(np.float32)).pin_memory()
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
     copies = max(2, math.ceil(2.0 * l2 / (nbytes - K * 4 - N * 4)))
@@ -276,20 +355,9 @@ def run_ours(args):
         g_rem.replay()
     stream.synchronize()
 
-    def barrier():
-        if world > 1:
-            dist.barrier(device_ids=[local_rank])
-
-    def max_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     # ---- timed region: exactly K steps
     clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
-    barrier()
+    dev_barrier(local_rank)
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -306,17 +374,17 @@ def run_ours(args):
         e1.record(stream)
     stream.synchronize()
     torch.cuda.synchronize()
-    barrier()
+    dev_barrier(local_rank)
     clk = clocks.stop() if clocks else None
     ms_local = e0.elapsed_time(e1)
-    ms = max_over_ranks(ms_local)
-    value = world * args.steps * nbytes / (ms / 1e3) / 1e9
-    per_gpu = args.steps * nbytes / (ms / 1e3) / 1e9
+    ms = dev_max(ms_local, dev)
+    value = args.steps * all_bytes / (ms / 1e3) / 1e9
+    per_gpu = args.steps * nbytes / (ms_local / 1e3) / 1e9
 
     # ---- end to end: host x -> device, GEMV through the C ABI, y -> host, every step
     e2e_steps = min(args.steps, args.e2e_steps)
     y_host = torch.empty((1, N), dtype=torch.float32).pin_memory()
-    barrier()
+    dev_barrier(local_rank)
     torch.cuda.synchronize()
     with torch.cuda.stream(stream):
         e0.record(stream)
@@ -327,16 +395,17 @@ def run_ours(args):
             stream.synchronize()
         e1.record(stream)
     stream.synchronize()
-    barrier()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-    e2e_value = world * e2e_steps * nbytes / (e2e_ms / 1e3) / 1e9
+    dev_barrier(local_rank)
+    e2e_ms = dev_max(e0.elapsed_time(e1), dev)
+    e2e_value = e2e_steps * all_bytes / (e2e_ms / 1e3) / 1e9
 
     del g, g_rem
     peak, peak_kind = read_peak_hbm()
     # DRAM traffic per launch cannot be read inside a timed run (it needs an ncu
     # capture); the figure is the committed capture of this kernel at this shape
-    # with the default launch heuristics, so it is dropped when tuning knobs are set
-    traffic = None if args.tuning else read_profile_traffic()
+    # with the default launch heuristics, so it is given for the whole GEMV on
+    # one GPU only and dropped when tuning knobs are set
+    traffic = None if (args.tuning or world > 1) else read_profile_traffic()
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -346,14 +415,17 @@ def run_ours(args):
         "warmup": args.warmup,
         "ms_per_step": ms / args.steps,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, host-generated)",
-        "config": {"workload": WORKLOAD, "K": K, "N": N, "group_size": gs,
-                   "bytes_per_step": nbytes, "weight_copies": copies,
-                   "l2": f"{copies} rotating weight copies ({copies * nbytes / 1e6:.0f} MB > L2 {l2 / 1e6:.0f} MB)",
-                   "parallelism": f"replicas x{world} (no data-path collective)",
+        "config": {"workload": WORKLOAD, "K": K, "N": N_DIM, "group_size": gs,
+                   "bytes_per_step": all_bytes, "weight_copies": copies,
+                   "l2": f"{copies} rotating weight copies per GPU ({copies * nbytes / 1e6:.0f} MB > L2 "
+                         f"{l2 / 1e6:.0f} MB)",
+                   "parallelism": ("one GPU: the whole GEMV" if world == 1 else
+                                   f"columns split over {world} GPUs ({N} or fewer of {N_DIM} each, whole "
+                                   "128-column strips; no data-path collective)"),
                    "timing": (f"{n_rep} replay(s) of a CUDA graph of {graph_len} launches"
                               + (f" + one graph of {n_rem}" if n_rem else "")
                               + " (every timed launch inside a graph), CUDA events, max over ranks")},
@@ -363,10 +435,12 @@ def run_ours(args):
                      "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at this "
                                         "shape, default heuristics (profiles/w4_gemv_k4096_n14336_g32.md); not "
                                         "measured in this run") if traffic else None,
-                     "achieved_basis": "algorithmic bytes per launch x launches / "
-                     "event time of back-to-back launches (includes inter-launch gaps)"},
+                     "achieved_basis": ("algorithmic bytes per launch x launches / event time of back-to-back "
+                                        "launches (includes inter-launch gaps)"
+                                        + ("" if world == 1 else "; rank 0's shard and time"))},
         "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "steps": e2e_steps,
-                "h2d_bytes_per_step": int(x_host.numel() * 4), "d2h_bytes_per_step": int(y_host.numel() * 4)},
+                "h2d_bytes_per_step": int(x_host.numel() * 4) * world,
+                "d2h_bytes_per_step": int(N_DIM * 4)},
         "gpu_launches": args.steps,
         "clocks": clk,
     }
@@ -375,10 +449,7 @@ def run_ours(args):
             line["cpu_baseline"] = cpu_baseline_sample(args.cpu_seconds)
         except Exception as e:  # the baseline is reported, never required
             line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+    return line
 
 
 # ----------------------------------------------------------------------------- prefill GEMM workloads
@@ -446,10 +517,7 @@ def run_prefill(args):
 
     rank, local_rank, world = rank_env()
     torch.cuda.set_device(local_rank)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local_rank))
+    dist_setup(local_rank)
     lib = _lib.load()
     dev = torch.device("cuda", local_rank)
     M, K, N, gs = PF_M, PF_K, PF_N, PF_GS
@@ -509,15 +577,10 @@ def run_prefill(args):
     stream.synchronize()
 
     def barrier():
-        if world > 1:
-            dist.barrier(device_ids=[local_rank])
+        dev_barrier(local_rank)
 
     def max_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return dev_max(v, dev)
 
     clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
     barrier()
@@ -572,10 +635,7 @@ def run_prefill(args):
             line["cpu_baseline"] = prefill_cpu_sample(args.workload, args.cpu_seconds)
         except Exception as e:  # the baseline is reported, never required
             line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+    return line
 
 
 # ----------------------------------------------------------------------------- attention workloads
@@ -630,10 +690,7 @@ def run_attention(args):
 
     rank, local_rank, world = rank_env()
     torch.cuda.set_device(local_rank)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local_rank))
+    dist_setup(local_rank)
     lib = _lib.load()
     dev = torch.device("cuda", local_rank)
     B, H, Hkv, S, D, dts, desc = ATTN_WORKLOADS[args.workload]
@@ -669,15 +726,10 @@ def run_attention(args):
     stream.synchronize()
 
     def max_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return dev_max(v, dev)
 
     clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
-    if world > 1:
-        dist.barrier(device_ids=[local_rank])
+    dev_barrier(local_rank)
     torch.cuda.synchronize()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     with torch.cuda.stream(stream):
@@ -733,10 +785,7 @@ def run_attention(args):
             line["cpu_baseline"] = attn_cpu_sample(args.cpu_seconds)
         except Exception as e:  # the baseline is reported, never required
             line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+    return line
 
 
 # ----------------------------------------------------------------------------- end-to-end decode
@@ -791,8 +840,7 @@ def run_decode(args):
     tp = args.workload == "decode_llama1b_tp"
     torch.cuda.set_device(local_rank)
     os.environ["SG_DEVICE"] = str(local_rank)
-    if world > 1:  # host-side group: the NCCL id of a tensor-parallel session, and max-over-ranks timing
-        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    dist_setup(local_rank)  # host-side exchanges (the NCCL id of a tensor-parallel session, max over ranks) on gloo
     c = DECODE_CFG
     cfg = armpack.llama_config(layers=c["layers"], hidden=c["hidden"], heads=c["heads"], kv_heads=c["kv_heads"],
                                head_dim=c["head_dim"], ffn=c["ffn"], vocab=c["vocab"], rope_theta=c["rope_theta"])
@@ -802,8 +850,7 @@ def run_decode(args):
     tp_arg = None
     if tp:
         uid = [sdk.tp_unique_id() if rank == 0 else None]
-        if world > 1:
-            dist.broadcast_object_list(uid, src=0)
+        host_bcast(uid)
         tp_arg = (rank, world, uid[0])
     with tempfile.TemporaryDirectory() as td:
         pkg_path = os.path.join(td, "llama1b_int4")
@@ -825,8 +872,7 @@ def run_decode(args):
                     decode()
                 s.reset()
                 clocks = ClockSampler(torch.cuda.current_device(), interval_ms=5) if rank == 0 else None
-                if world > 1:
-                    dist.barrier()
+                host_barrier()
                 t0 = time.perf_counter()
                 prefill()
                 first = decode()                        # the token predicted by the prompt
@@ -835,12 +881,7 @@ def run_decode(args):
                     decode()
                 t2 = time.perf_counter()
                 clk = clocks.stop() if clocks else None
-    decode_s, ttft_s = t2 - t1, t1 - t0
-    if world > 1:  # the slowest rank
-        tmax = torch.tensor([decode_s, ttft_s], dtype=torch.float64)
-        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
-        decode_s, ttft_s = float(tmax[0]), float(tmax[1])
-        dist.destroy_process_group()
+    decode_s, ttft_s = host_max([t2 - t1, t1 - t0])  # the slowest rank
     tps = steps / decode_s
     seqs = args.batch * (1 if tp else world)  # sequences decoded at once over the whole job
     ctx_mid = prompt_len + steps / 2
@@ -881,8 +922,7 @@ def run_decode(args):
             line["cpu_baseline"] = decode_cpu_sample(cfg, tensors, args.cpu_seconds)
         except Exception as e:  # the baseline is reported, never required
             line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    return line
 
 
 # ----------------------------------------------------------------------------- Qwen-7B shape, tensor-parallel
@@ -908,8 +948,7 @@ def run_qwen(args):
     rank, local_rank, world = rank_env()
     torch.cuda.set_device(local_rank)
     os.environ["SG_DEVICE"] = str(local_rank)
-    if world > 1:
-        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
+    dist_setup(local_rank)
     c = QWEN_CFG
     cfg = armpack.llama_config(layers=c["layers"], hidden=c["hidden"], heads=c["heads"], kv_heads=c["kv_heads"],
                                head_dim=c["head_dim"], ffn=c["ffn"], vocab=c["vocab"], rope_theta=c["rope_theta"])
@@ -923,9 +962,8 @@ def run_qwen(args):
     root = os.environ.get("SG_BENCH_TMP", "/tmp")
     pkg_path = [os.path.join(root, f"sg_qwen7b_{os.getpid()}") if rank == 0 else None]
     uid = [sdk.tp_unique_id() if rank == 0 else None]
-    if world > 1:
-        dist.broadcast_object_list(pkg_path, src=0)
-        dist.broadcast_object_list(uid, src=0)
+    host_bcast(pkg_path)
+    host_bcast(uid)
     pkg_path = pkg_path[0]
     try:
         if rank == 0:
@@ -935,10 +973,9 @@ def run_qwen(args):
             torch.cuda.empty_cache()
         else:
             weight_bytes = 0
-        if world > 1:
-            wb = [weight_bytes]
-            dist.broadcast_object_list(wb, src=0)
-            weight_bytes = wb[0]
+        wb = [weight_bytes]
+        host_bcast(wb)
+        weight_bytes = wb[0]
         prompt = np.random.default_rng(6).integers(0, c["vocab"], (B, QWEN_PROMPT)).astype(np.int32)
         with sdk.Package(pkg_path) as pkg:
             graph = pkg.select(context_length=ctx)
@@ -952,8 +989,7 @@ def run_qwen(args):
                     decode()
                 s.reset()
                 clocks = ClockSampler(torch.cuda.current_device(), interval_ms=5) if rank == 0 else None
-                if world > 1:
-                    dist.barrier()
+                host_barrier()
                 t0 = time.perf_counter()
                 prefill(prompt)
                 first = decode()
@@ -963,16 +999,10 @@ def run_qwen(args):
                 t2 = time.perf_counter()
                 clk = clocks.stop() if clocks else None
     finally:
-        if world > 1:
-            dist.barrier()
+        host_barrier()
         if rank == 0:
             shutil.rmtree(pkg_path, ignore_errors=True)
-    ttft_s, decode_s = t1 - t0, t2 - t1
-    if world > 1:
-        tmax = torch.tensor([ttft_s, decode_s], dtype=torch.float64)
-        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
-        ttft_s, decode_s = float(tmax[0]), float(tmax[1])
-        dist.destroy_process_group()
+    ttft_s, decode_s = host_max([t1 - t0, t2 - t1])
     H, L, F, V, D = c["hidden"], c["layers"], c["ffn"], c["vocab"], c["head_dim"]
     Hq, Hkv = c["heads"], c["kv_heads"]
     lin_params = L * (H * (Hq + 2 * Hkv) * D + Hq * D * H + H * 2 * F + F * H)
@@ -1006,8 +1036,7 @@ def run_qwen(args):
         "clocks": clk,
         "first_token": int(first),
     }
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    return line
 
 
 # ----------------------------------------------------------------------------- reference arm
@@ -1072,7 +1101,7 @@ def run_reference(args):
     line = {
         "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": WORKLOAD, "K": K, "N": N, "group_size": gs},
         "impl": "reference",
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": kind,
@@ -1165,7 +1194,65 @@ def run_int8(args):
         "gpu_launches": args.steps,
         "clocks": clk,
     }
-    print(json.dumps(line), flush=True)
+    return line
+
+
+# Sub-results of the default run, measured in the same process after the
+# headline: (name, workload, batch, steps, warmup).  One GPU: the other
+# kernels of the hot path and the Llama-3.2-1B-shape decode; several GPUs: the
+# same decode tensor-parallel over all of them (NCCL all-reduce after the
+# row-parallel projections).
+SUB_ONE_GPU = [
+    ("gemv_int8", "gemv_int8", 1, 2000, 50),
+    ("prefill_int4", "prefill_int4", 1, 10, 3),
+    ("attn_prefill", "attn_prefill", 1, 10, 3),
+    ("attn_small", "attn_small", 1, 20, 3),
+    ("decode_llama1b_b1", "decode_llama1b", 1, 96, 4),
+    ("decode_llama1b_b16", "decode_llama1b", 16, 96, 4),
+]
+SUB_MULTI_GPU = [
+    ("decode_llama1b_tp_b1", "decode_llama1b_tp", 1, 96, 4),
+    ("decode_llama1b_tp_b16", "decode_llama1b_tp", 16, 96, 4),
+]
+SUB_KEYS = ("metric", "value", "unit", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling", "dtype",
+            "config", "roofline", "e2e", "cpu_baseline", "gpu_launches", "clocks")
+
+
+def run_workload(args):
+    if args.workload == "gemv_int8":
+        return run_int8(args)
+    if args.workload in PF_WORKLOADS:
+        return run_prefill(args)
+    if args.workload in ATTN_WORKLOADS:
+        return run_attention(args)
+    if args.workload in ("decode_llama1b", "decode_llama1b_tp"):
+        return run_decode(args)
+    if args.workload == "qwen7b_tp":
+        return run_qwen(args)
+    return run_ours(args)
+
+
+def run_default(args):
+    """The headline INT4 GEMV line with the sub-results in "sub_results"."""
+    line = run_ours(args)
+    if args.no_sub:
+        return line
+    _, _, world = rank_env()
+    subs = {}
+    for name, workload, batch, steps, warmup in (SUB_ONE_GPU if world == 1 else SUB_MULTI_GPU):
+        ns = argparse.Namespace(**vars(args))
+        ns.workload, ns.batch, ns.steps, ns.warmup = workload, batch, steps, warmup
+        ns.cpu_seconds = min(args.cpu_seconds, 6.0)
+        t0 = time.perf_counter()
+        try:
+            r = run_workload(ns)
+            sub = {k: r[k] for k in SUB_KEYS if k in r}
+        except Exception as e:  # a failing sub-result is reported, the headline stands
+            sub = {"error": f"{type(e).__name__}: {str(e)[:300]}"}
+        sub["wall_s"] = round(time.perf_counter() - t0, 1)
+        subs[name] = sub
+    line["sub_results"] = subs
+    return line
 
 
 def main():
@@ -1179,16 +1266,18 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--ref-budget-s", type=float, default=120.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sub", action="store_true", help="default workload: the headline line only")
     ap.add_argument("--batch", type=int, default=1,
                     help="decode workloads: sequences decoded in lockstep by one session (config: 1 and 16)")
     ap.add_argument("--workload", choices=["gemv_int4", "gemv_int8", *PF_WORKLOADS, *ATTN_WORKLOADS, "decode_llama1b",
                                            "decode_llama1b_tp", "qwen7b_tp"],
                     default="gemv_int4",
-                    help="gemv_int4 (default): the decode GEMV; prefill_int4 / prefill_int8: the prefill GEMM; "
-                         "attn_prefill / attn_small: flash attention; decode_llama1b: Llama-1B-shape decode "
-                         "through the SDK (one session per GPU); decode_llama1b_tp: the same model "
-                         "tensor-parallel over all GPUs; qwen7b_tp: Qwen-7B-shape 8192-token prefill + decode, "
-                         "tensor-parallel over all GPUs")
+                    help="gemv_int4 (default): the decode GEMV (columns split over the GPUs), with the other "
+                         "workloads as sub-results; gemv_int8: the INT8 per-channel GEMV; prefill_int4 / "
+                         "prefill_int8: the prefill GEMM; attn_prefill / attn_small: flash attention; "
+                         "decode_llama1b: Llama-1B-shape decode through the SDK (one session per GPU); "
+                         "decode_llama1b_tp: the same model tensor-parallel over all GPUs; qwen7b_tp: "
+                         "Qwen-7B-shape 8192-token prefill + decode, tensor-parallel over all GPUs")
     ap.add_argument("--tuning", action="append", default=[], metavar="KEY=VALUE",
                     help="kernel tuning knob (sg_set_tuning) applied before the run; repeatable")
     args = ap.parse_args()
@@ -1199,7 +1288,7 @@ def main():
             kernels.set_tuning(key, int(val))
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    _, _, world = rank_env()
+    rank, _, world = rank_env()
     if world != args.gpus and args.impl == "ours":
         if args.gpus > 1 and world == 1:
             ap.error("for --gpus N > 1 launch with torch.distributed.run --nproc-per-node N")
@@ -1207,18 +1296,13 @@ def main():
         if args.workload != "gemv_int4":
             ap.error("--impl reference times the decode GEMV workload")
         run_reference(args)
-    elif args.workload == "gemv_int8":
-        run_int8(args)
-    elif args.workload in PF_WORKLOADS:
-        run_prefill(args)
-    elif args.workload in ATTN_WORKLOADS:
-        run_attention(args)
-    elif args.workload in ("decode_llama1b", "decode_llama1b_tp"):
-        run_decode(args)
-    elif args.workload == "qwen7b_tp":
-        run_qwen(args)
-    else:
-        run_ours(args)
+        return
+    try:
+        line = run_default(args) if args.workload == "gemv_int4" else run_workload(args)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        dist_teardown()
 
 
 if __name__ == "__main__":
