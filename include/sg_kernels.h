@@ -165,6 +165,8 @@ int32_t sg_device_error_check(void* stream);
  *   "w4_gemv_mma.variant"      tensor-core GEMV launch shape (0 default .. 3)
  *   "w4_gemv_mma.sleep"        tensor-core GEMV: sleep between stage polls (0/1)
  *   "w4_gemv_mma.cluster"      tensor-core GEMV: allow the cluster-reduced split (1, default) or not (0)
+ *   "tp_allreduce.wait_ms"     peer all-reduce: how long a rank waits for the others' flags
+ *                              before it gives up and reports (1 .. 2000 ms; <= 0 restores 2000)
  * Returns SG_ERR_NOT_FOUND for an unknown key.  No reference counterpart. */
 int32_t sg_set_tuning(const char* key, int32_t value);
 

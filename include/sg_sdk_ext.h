@@ -93,6 +93,22 @@ void sg_session_vocab_range(const ArmSession* sess, uint32_t* lo, uint32_t* hi);
 ArmSession* sg_session_create_ex(ArmGraph* graph, const ArmSessionOptions* opts, uint32_t batch, int32_t rank,
                                  int32_t world, const uint8_t id[128]);
 
+/* ---- failure handling ------------------------------------------------------
+ * A tensor-parallel session never blocks forever on its group: the host
+ * polls each step, and an asynchronous NCCL error, or a step that has not
+ * completed after SG_TP_TIMEOUT_MS milliseconds (default 60000: a rank that
+ * stopped answering), aborts the group (ncclCommAbort) and the call returns
+ * ARMCC_ERR_RUNTIME with the reason; the peer all-reduce's own waits are
+ * bounded (sg_tp_allreduce_f16).  A caller that learns on the host that a
+ * rank has left (a store, a heartbeat) calls sg_session_abort before the next
+ * step, so nothing is launched towards the departed rank.  An aborted
+ * session refuses every later prefill / decode with ARMCC_ERR_RUNTIME and
+ * the reason, and can still be destroyed.  This mirrors the reference
+ * runtime's refusal with a reason (compiler/lib/runtime/
+ * resource_controller.cpp:195-247); the reference itself has no multi-device
+ * group. */
+ArmStatus sg_session_abort(ArmSession* sess, const char* reason);
+
 /* ---- paged KV cache ---------------------------------------------------------
  * Sessions lay out their KV cache as the reference's planner recommends
  * (compiler/lib/memory/kv_cache_layout.cpp:107-130): flat up to a 4096-token

@@ -42,6 +42,7 @@
 #include <memory>
 #include <string>
 #include <string_view>
+#include <thread>
 #include <vector>
 
 #include "armcc_sdk.h"
@@ -94,6 +95,9 @@ struct NcclApi {
   ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
+  // failure handling (NULL when the loaded NCCL lacks them)
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_get_async_error)(ncclComm_t, ncclResult_t*) = nullptr;
 };
 
 // The NCCL the host process already loaded (e.g. PyTorch's), else SG_NCCL_LIBRARY, else libnccl.so.2.
@@ -116,6 +120,8 @@ const NcclApi& nccl_api() {
     a.all_gather = reinterpret_cast<decltype(a.all_gather)>(dlsym(h, "ncclAllGather"));
     a.comm_destroy = reinterpret_cast<decltype(a.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
     a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
+    a.comm_abort = reinterpret_cast<decltype(a.comm_abort)>(dlsym(h, "ncclCommAbort"));
+    a.comm_get_async_error = reinterpret_cast<decltype(a.comm_get_async_error)>(dlsym(h, "ncclCommGetAsyncError"));
     a.ok = a.get_unique_id && a.comm_init_rank && a.all_reduce && a.all_gather && a.comm_destroy && a.error_string;
     if (!a.ok) a.why = "the loaded NCCL library lacks a required symbol";
     return a;
@@ -422,6 +428,12 @@ struct ArmSession_ {
   void* ar_region = nullptr;
   int ar_max = 0;
   std::vector<void*> ar_regions;  // every rank's region as mapped here (own one at tp_rank)
+  // failure handling: a session whose group failed (or was aborted) refuses
+  // every later call with the reason; tp_timeout_ms bounds a host wait for a
+  // step whose collectives do not complete (SG_TP_TIMEOUT_MS, default 60 s)
+  bool aborted = false;
+  std::string abort_why;
+  int tp_timeout_ms = 60000;
 
   ~ArmSession_() {
     if (st) cudaStreamSynchronize(st);
@@ -754,17 +766,88 @@ void release_pages(ArmSession_* S) {
   S->lpages = 0;
 }
 
+// Ends a tensor-parallel session's group after a failure: the NCCL
+// communicator is aborted (which makes its kernels in flight return), the
+// session's own kernels finish (their waits are bounded), and the peers'
+// mapped regions are closed.  Every later call is refused with `why`; this
+// mirrors the reference runtime's clean refusal with a reason
+// (compiler/lib/runtime/resource_controller.cpp:195-247).
+void abort_session(ArmSession_* S, const std::string& why) {
+  if (S->aborted) return;
+  S->aborted = true;
+  S->abort_why = why;
+  if (S->comm) {
+    if (nccl_api().comm_abort) nccl_api().comm_abort(S->comm);
+    S->comm = nullptr;  // aborted: not destroyed again
+  }
+  cudaStreamSynchronize(S->st);
+  cudaGetLastError();
+  for (size_t q = 0; q < S->ar_regions.size(); ++q)
+    if ((int)q != S->tp_rank && S->ar_regions[q]) cudaIpcCloseMemHandle(S->ar_regions[q]);
+  S->ar_regions.clear();
+}
+
+// Waits for the session's stream.  A tensor-parallel session polls instead of
+// blocking: an asynchronous NCCL error, or no completion within
+// tp_timeout_ms (a peer that stopped answering), aborts the group and returns
+// ARMCC_ERR_RUNTIME instead of hanging the caller.
+ArmStatus wait_stream(ArmSession_* S, const char* fn) {
+  if (S->tp_world == 1 || !S->comm) {
+    if (cudaStreamSynchronize(S->st) != cudaSuccess) {
+      set_err("%s: device error: %s", fn, cudaGetErrorString(cudaGetLastError()));
+      return ARMCC_ERR_RUNTIME;
+    }
+    return ARMCC_OK;
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  for (int spin = 0;; ++spin) {
+    const cudaError_t q = cudaStreamQuery(S->st);
+    if (q == cudaSuccess) return ARMCC_OK;
+    if (q != cudaErrorNotReady) {
+      cudaGetLastError();
+      set_err("%s: device error: %s", fn, cudaGetErrorString(q));
+      return ARMCC_ERR_RUNTIME;
+    }
+    ncclResult_t ae = ncclSuccess;
+    if (nccl_api().comm_get_async_error && nccl_api().comm_get_async_error(S->comm, &ae) == ncclSuccess &&
+        ae != ncclSuccess && ae != ncclInProgress) {
+      const std::string why = std::string("NCCL reported an asynchronous error: ") + nccl_api().error_string(ae);
+      abort_session(S, why);
+      set_err("%s: %s; the tensor-parallel group was aborted", fn, why.c_str());
+      return ARMCC_ERR_RUNTIME;
+    }
+    const auto ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    if (ms > S->tp_timeout_ms) {
+      char buf[160];
+      snprintf(buf, sizeof buf, "a step did not complete within %d ms (a rank stopped answering)",
+               S->tp_timeout_ms);
+      abort_session(S, buf);
+      set_err("%s: %s; the tensor-parallel group was aborted", fn, buf);
+      return ARMCC_ERR_RUNTIME;
+    }
+    if (spin > 64) std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+// Refuses a call on a session whose group failed.
+bool session_usable(ArmSession_* S, const char* fn) {
+  if (!S->aborted) return true;
+  set_err("%s: the session was aborted: %s", fn, S->abort_why.c_str());
+  return false;
+}
+
 // Reads every sequence's greedy token (and the kernels' error word) back to the host.
 ArmStatus fetch_next(ArmSession_* S) {
   S->next_all.assign(S->batch, -1);
   float lp = 0;
   if (cudaMemcpyAsync(S->next_all.data(), S->buf<int32_t>("next"), (size_t)S->batch * 4, cudaMemcpyDeviceToHost,
                       S->st) != cudaSuccess ||
-      cudaMemcpyAsync(&lp, S->buf<float>("logprob"), 4, cudaMemcpyDeviceToHost, S->st) != cudaSuccess ||
-      cudaStreamSynchronize(S->st) != cudaSuccess) {
+      cudaMemcpyAsync(&lp, S->buf<float>("logprob"), 4, cudaMemcpyDeviceToHost, S->st) != cudaSuccess) {
     set_err("device error: %s", cudaGetErrorString(cudaGetLastError()));
     return ARMCC_ERR_RUNTIME;
   }
+  const ArmStatus ws = wait_stream(S, "decode");
+  if (ws != ARMCC_OK) return ws;
   const int32_t derr = sg_device_error_check(S->st);
   if (derr != 0) {
     set_err("a kernel reported device error %d (%s)", derr, sg_last_error());
@@ -779,6 +862,7 @@ ArmStatus fetch_next(ArmSession_* S) {
 // token i at tokens[b * n + i]), in chunks of at most max_chunk per sequence.
 ArmStatus prefill_tokens(ArmSession_* S, const int32_t* tokens, uint32_t n, const char* fn) {
   const ModelCfg& c = S->c;
+  if (!session_usable(S, fn)) return ARMCC_ERR_RUNTIME;
   if ((uint64_t)S->pos + n > (uint64_t)c.max_context) {
     set_err("%s: %u tokens after %d exceed the context of %d", fn, n, S->pos, c.max_context);
     return ARMCC_ERR_OOM;
@@ -825,6 +909,7 @@ ArmStatus prefill_tokens(ArmSession_* S, const int32_t* tokens, uint32_t n, cons
 // Emits the pending greedy tokens, running one decode step first when the
 // previous ones were already emitted.
 ArmStatus step_tokens(ArmSession_* S, const char* fn, float* step_ms) {
+  if (!session_usable(S, fn)) return ARMCC_ERR_RUNTIME;
   if (S->pos == 0) {
     set_err("%s: prefill a prompt first", fn);
     return ARMCC_ERR_RUNTIME;
@@ -1153,6 +1238,7 @@ ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int r
     return nullptr;
   }
   if (const char* gflag = getenv("SG_DECODE_GRAPH")) S->use_graph = atoi(gflag) != 0;
+  if (const char* t = getenv("SG_TP_TIMEOUT_MS")) S->tp_timeout_ms = std::max(1, atoi(t));
   if (world > 1) {
     ncclUniqueId uid;
     memcpy(uid.internal, id, sizeof uid.internal);
@@ -1812,6 +1898,16 @@ ArmSession* sg_session_create_paged(ArmGraph* graph, const ArmSessionOptions* op
   }
   return create_session(graph, opts, rank, world, id, (int)std::min<uint32_t>(batch, 1u << 20), 2,
                         (int64_t)std::min<uint64_t>(kv_pool_tokens, (uint64_t)INT64_MAX / 2));
+}
+
+ArmStatus sg_session_abort(ArmSession* sess, const char* reason) {
+  if (!sess) {
+    set_err("sg_session_abort: session is NULL");
+    return ARMCC_ERR_RUNTIME;
+  }
+  cudaSetDevice(sess->dev);
+  abort_session(sess, reason && *reason ? reason : "aborted by the caller");
+  return ARMCC_OK;
 }
 
 int32_t sg_session_kv_pages(const ArmSession* sess, uint32_t* pool_pages, uint32_t* pages_in_use) {

@@ -15,7 +15,11 @@
 // Rank r can only start call k + 2 after every peer has raised its flags of
 // call k + 1, which they do after finishing call k: two parities suffice.  A
 // wait that runs out records an error in the device error word and leaves the
-// vector unreduced (the host reports it); nothing spins forever.
+// vector unreduced (the host reports it); nothing spins forever.  The limit
+// is 2 s, or what sg_set_tuning("tp_allreduce.wait_ms", ms) sets.
+#include <atomic>
+#include <string_view>
+
 #include "sm100.cuh"
 
 namespace {
@@ -24,6 +28,7 @@ constexpr int kMaxRanks = 8;
 constexpr int kMaxBlocks = 32;
 constexpr int kThreads = 512;
 constexpr int kChunk = 8;  // fp16 per 16-byte vector
+std::atomic<int> g_wait_ms{2000};  // bounded wait for the peers' flags
 
 struct Peers {
   uint8_t* region[kMaxRanks];
@@ -39,7 +44,7 @@ __device__ __forceinline__ uint32_t ld_flag(const uint32_t* p) {
 }
 
 __global__ void __launch_bounds__(kThreads) tp_allreduce_kernel(__half* __restrict__ data, int n, int rank, int world,
-                                                                Peers peers, int max_n, int* err) {
+                                                                Peers peers, int max_n, int* err, uint64_t wait_ns) {
   sgd::pdl_wait();  // the partial comes from the previous kernel
   sgd::pdl_launch_dependents();
   uint8_t* mine = peers.region[rank];
@@ -72,7 +77,7 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_kernel(__half* __restri
       const uint64_t t0 = sgd::global_timer_ns();
       for (;;) {
         if (ld_flag(f) >= epoch) break;
-        if (sgd::global_timer_ns() - t0 > sgd::kWaitLimitNs) {
+        if (sgd::global_timer_ns() - t0 > wait_ns) {
           sgd::record_error(err, sgd::kErrWaitTimeout);
           s_ok = 0;
           break;
@@ -121,6 +126,16 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_kernel(__half* __restri
 
 }  // namespace
 
+namespace sg {
+bool tp_allreduce_tuning(std::string_view key, int value) {
+  if (key == "tp_allreduce.wait_ms") {
+    g_wait_ms.store(value <= 0 ? 2000 : std::min(value, 2000));
+    return true;
+  }
+  return false;
+}
+}  // namespace sg
+
 extern "C" {
 
 size_t sg_tp_allreduce_region_bytes(int32_t world, int32_t max_n) {
@@ -148,7 +163,8 @@ SgStatus sg_tp_allreduce_f16(void* data, int32_t n, int32_t rank, int32_t world,
   const int nvec = n / kChunk;
   const int blocks = std::max(1, std::min(kMaxBlocks, (nvec + 1023) / 1024));
   SG_CUDA_TRY(sgd::launch_pdl(tp_allreduce_kernel, dim3(blocks), dim3(kThreads), 0, static_cast<cudaStream_t>(stream),
-                              static_cast<__half*>(data), (int)n, (int)rank, (int)world, pe, (int)max_n, err));
+                              static_cast<__half*>(data), (int)n, (int)rank, (int)world, pe, (int)max_n, err,
+                              (uint64_t)std::max(1, g_wait_ms.load()) * 1000000ull));
   return SG_OK;
 }
 

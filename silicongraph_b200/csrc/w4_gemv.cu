@@ -394,6 +394,7 @@ bool gemm_tc_tuning(std::string_view key, int value);
 bool attn_tc_tuning(std::string_view key, int value);
 bool attn_tuning(std::string_view key, int value);
 bool sdk_tuning(std::string_view key, int value);
+bool tp_allreduce_tuning(std::string_view key, int value);
 }  // namespace sg
 
 // Core entry.  ws == NULL: library scratch (unless ws_external, then an error
@@ -609,6 +610,7 @@ int32_t sg_set_tuning(const char* key, int32_t value) {
   if (key && sg::attn_tc_tuning(std::string_view(key), value)) return SG_OK;
   if (key && sg::attn_tuning(std::string_view(key), value)) return SG_OK;
   if (key && sg::sdk_tuning(std::string_view(key), value)) return SG_OK;
+  if (key && sg::tp_allreduce_tuning(std::string_view(key), value)) return SG_OK;
   sg::set_error("sg_set_tuning: unknown key");
   return SG_ERR_NOT_FOUND;
 }

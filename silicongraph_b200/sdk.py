@@ -80,6 +80,7 @@ _SIGS = {
     "sg_session_vocab_range": (None, [_P, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32)]),
     "sg_session_create_paged": (_P, [_P, ctypes.POINTER(ArmSessionOptions), ctypes.c_uint32, ctypes.c_uint64,
                                      ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(ctypes.c_uint8)]),
+    "sg_session_abort": (ctypes.c_int, [_P, ctypes.c_char_p]),
     "sg_session_kv_pages": (ctypes.c_int32, [_P, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32)]),
     "sg_session_create_ex": (_P, [_P, ctypes.POINTER(ArmSessionOptions), ctypes.c_uint32, ctypes.c_int32,
                                   ctypes.c_int32, ctypes.POINTER(ctypes.c_uint8)]),
@@ -312,6 +313,12 @@ class Session:
         if st != ARMCC_OK:
             raise ArmError(st, last_error())
         return out
+
+    def abort(self, reason: str = "") -> None:
+        """sg_session_abort: end the session's tensor-parallel group; later calls are refused."""
+        st = lib().sg_session_abort(self.h, reason.encode())
+        if st != ARMCC_OK:
+            raise ArmError(st, last_error())
 
     @property
     def kv_pages(self) -> tuple[int, int] | None:
