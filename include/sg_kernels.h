@@ -62,6 +62,18 @@ typedef enum {
                                    ops_swiglu, fused into the down projection).
                                    INT4 only, on the one-row and 2..16-row
                                    kernels; other shapes return SG_ERR_UNSUPPORTED */
+#define SG_MM_A_RMSNORM 4u      /* A is one row of the decoder's residual stream
+                                   (fp16 or bf16, K values, K % 8 == 0, K <= 8192):
+                                   the GEMV consumes the RMSNorm of it with weight
+                                   norm_weight and eps norm_eps, rounded to A's
+                                   type exactly as sg_rmsnorm writes it (the norm
+                                   fused into the next projection).  INT4, one
+                                   row, groups of 32k; else SG_ERR_UNSUPPORTED */
+#define SG_MM_C_ACCUMULATE 8u   /* C (fp16 or bf16) holds the residual stream:
+                                   C = round(C + round(result)), the residual add
+                                   of sg_rmsnorm with a residual, fused into the
+                                   producing projection.  Same restrictions as
+                                   SG_MM_A_RMSNORM */
 
 /*
  * Mirrors armcc::kernels::cpu::MatMulParams (matmul_neon.h:32-43).
@@ -87,6 +99,8 @@ typedef struct SgMatMulParams {
   void* workspace;        /* optional caller scratch, see *_workspace_size()   */
   size_t workspace_bytes;
   uint32_t flags;         /* SG_MM_* bits; 0 = no assumptions                  */
+  const void* norm_weight;/* SG_MM_A_RMSNORM: [K] weight, A's type             */
+  float norm_eps;         /* SG_MM_A_RMSNORM: eps (rmsnorm_fp16_neon's)        */
 } SgMatMulParams;
 
 /*

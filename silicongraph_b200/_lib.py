@@ -49,11 +49,15 @@ class SgMatMulParams(ctypes.Structure):
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
         ("flags", ctypes.c_uint32),
+        ("norm_weight", ctypes.c_void_p),
+        ("norm_eps", ctypes.c_float),
     ]
 
 
 SG_MM_STATIC_WEIGHTS = 1
 SG_MM_A_SWIGLU = 2
+SG_MM_A_RMSNORM = 4
+SG_MM_C_ACCUMULATE = 8
 
 
 class SgKvPages(ctypes.Structure):

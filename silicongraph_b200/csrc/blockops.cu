@@ -10,6 +10,7 @@
 #include <algorithm>
 #include <cfloat>
 
+#include "rownorm.cuh"
 #include "sm100.cuh"
 
 namespace {
@@ -17,7 +18,7 @@ namespace {
 using sgd::load_as_float;
 using sgd::store_from_float;
 
-constexpr int kRowThreads = 256;
+constexpr int kRowThreads = sgn::kNormThreads;
 
 __device__ __forceinline__ float ld(const void* p, int dt, int64_t i) {
   switch (dt) {
@@ -42,18 +43,7 @@ __device__ __forceinline__ float round_io(float v, int dt) {
   }
 }
 
-__device__ __forceinline__ float block_sum(float v, float* red) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();  // red may still be read by a previous reduction
-  if (lane == 0) red[w] = v;
-  __syncthreads();
-  float t = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.f;
-#pragma unroll
-  for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-  return t;
-}
+using sgn::block_sum;
 
 __device__ __forceinline__ float block_max(float v, float* red) {
 #pragma unroll
@@ -96,22 +86,11 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_kernel(const void* x, voi
 // Same operation for 16-bit rows with n % 8 == 0 and n <= 8 * kRowThreads * kVecPerThread:
 // the row stays in registers between the sum of squares and the scaling,
 // loaded and stored 8 values (16 bytes) at a time.
-constexpr int kVecPerThread = 4;
-
-template <typename T>
-__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
-  const T* h = reinterpret_cast<const T*>(&u);
-#pragma unroll
-  for (int k = 0; k < 8; ++k) f[k] = (float)h[k];
-}
-template <typename T>
-__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
-  uint4 u;
-  T* h = reinterpret_cast<T*>(&u);
-#pragma unroll
-  for (int k = 0; k < 8; ++k) h[k] = (T)f[k];
-  return u;
-}
+// The sum of squares is formed as in sgn::row_rms_inv (rownorm.cuh), which the
+// INT4 GEMV uses when it fuses this norm into its activation staging.
+constexpr int kVecPerThread = sgn::kNormVecPerThread;
+using sgn::pack8;
+using sgn::unpack8;
 
 template <typename T>
 __global__ void __launch_bounds__(kRowThreads) rmsnorm_vec_kernel(const T* __restrict__ x, T* __restrict__ residual,
@@ -136,8 +115,7 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_vec_kernel(const T* __res
         for (int e = 0; e < 8; ++e) h[k][e] = (float)(T)(h[k][e] + r[e]);  // the residual stream keeps T
         reinterpret_cast<uint4*>(residual + base)[v] = pack8<T>(h[k]);
       }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) ss += h[k][e] * h[k][e];
+      ss = sgn::sumsq8(h[k], ss);
     }
   }
   ss = block_sum(ss, red);

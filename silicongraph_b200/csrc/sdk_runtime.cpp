@@ -50,6 +50,11 @@
 #include "sg_sdk_ext.h"
 #include "sg_kernels.h"
 
+namespace sg {  // libsg_b200 internals (w4_gemv_mma.cu, sg_runtime.cu)
+size_t w4_gemv_mma_scratch_bytes(const SgMatMulParams* p, int sms, bool* applicable);
+int sm_count(int dev);
+}  // namespace sg
+
 using sgsdk::Json;
 
 namespace {
@@ -433,6 +438,8 @@ struct ArmSession_ {
   // step whose collectives do not complete (SG_TP_TIMEOUT_MS, default 60 s)
   bool aborted = false;
   std::string abort_why;
+  // every projection's one-row shape runs on the kernel that fuses the norms (SG_MM_A_RMSNORM / C_ACCUMULATE)
+  bool norm_fusable = false;
   int tp_timeout_ms = 60000;
 
   ~ArmSession_() {
@@ -496,8 +503,17 @@ ArmStatus tp_sum(ArmSession_* S, void* buf, size_t count) {
 // separate kernel, 1108 vs 1084 us, so batched steps keep the two kernels.)
 std::atomic<int> g_fuse_swiglu{1};
 
-ArmStatus linear(ArmSession_* S, const Linear& L, const void* A, void* C, int M, int c_dt, uint32_t flags = 0) {
+// Single-row steps on one GPU fuse the decoder's RMSNorms and residual adds
+// into the projections (SG_MM_A_RMSNORM on q|k|v, gate|up and the LM head,
+// SG_MM_C_ACCUMULATE on o and down): the residual stream lives in "resid", the
+// embedding writes it directly, and no separate norm kernel runs.
+std::atomic<int> g_fuse_norm{1};
+
+ArmStatus linear(ArmSession_* S, const Linear& L, const void* A, void* C, int M, int c_dt, uint32_t flags = 0,
+                 const void* norm_w = nullptr) {
   SgMatMulParams p{};
+  p.norm_weight = norm_w;
+  p.norm_eps = S->c.rms_eps;
   p.A = A;
   p.B = L.qw;
   p.C = C;
@@ -519,7 +535,8 @@ ArmStatus linear(ArmSession_* S, const Linear& L, const void* A, void* C, int M,
 
 // down(SwiGLU(gate | up)) over M rows: one fused GEMM where the kernels take
 // it (few rows), else the SwiGLU kernel and the plain GEMM.
-ArmStatus swiglu_down(ArmSession_* S, const Linear& down, void* gu, void* act, void* out, int M, int ffn) {
+ArmStatus swiglu_down(ArmSession_* S, const Linear& down, void* gu, void* act, void* out, int M, int ffn,
+                      uint32_t extra_flags = 0) {
   if (g_fuse_swiglu.load() && M == 1) {
     SgMatMulParams p{};
     p.A = gu;
@@ -537,7 +554,7 @@ ArmStatus swiglu_down(ArmSession_* S, const Linear& down, void* gu, void* act, v
     p.scale_A = 1.0f;
     p.workspace = S->lin_ws;
     p.workspace_bytes = S->lin_ws_bytes;
-    p.flags = SG_MM_STATIC_WEIGHTS | SG_MM_A_SWIGLU;
+    p.flags = SG_MM_STATIC_WEIGHTS | SG_MM_A_SWIGLU | extra_flags;
     const SgStatus st = sg_matmul_int4_grouped(&p, S->st);
     if (st == SG_OK) return ARMCC_OK;
     if (st != SG_ERR_UNSUPPORTED) {
@@ -560,18 +577,31 @@ ArmStatus forward(ArmSession_* S, int Ts, bool from_next, bool dev_pos = false) 
   const int B = S->batch, T = B * Ts;
   const int H = c.hidden, D = c.head_dim;
   const int32_t* ids = from_next ? S->buf<int32_t>("next") : S->buf<int32_t>("ids");
-  SG_TRY(sg_embedding(S->embed, ids, S->buf<void>("x_emb"), T, H, c.vocab_global, SG_DT_F16, st), "embedding");
-  if (cudaMemsetAsync(S->buf<void>("resid"), 0, (size_t)T * H * 2, st) != cudaSuccess) {
-    set_err("cudaMemsetAsync failed");
-    return ARMCC_ERR_RUNTIME;
+  // one row on one GPU: norms and residual adds fused into the projections
+  const bool fuse = T == 1 && S->tp_world == 1 && S->norm_fusable && g_fuse_norm.load() != 0;
+  void* resid = S->buf<void>("resid");
+  if (fuse) {
+    // the residual stream starts as the embedding (round(x + 0) = x)
+    SG_TRY(sg_embedding(S->embed, ids, resid, T, H, c.vocab_global, SG_DT_F16, st), "embedding");
+  } else {
+    SG_TRY(sg_embedding(S->embed, ids, S->buf<void>("x_emb"), T, H, c.vocab_global, SG_DT_F16, st), "embedding");
+    if (cudaMemsetAsync(resid, 0, (size_t)T * H * 2, st) != cudaSuccess) {
+      set_err("cudaMemsetAsync failed");
+      return ARMCC_ERR_RUNTIME;
+    }
   }
   ArmStatus r;
   for (int l = 0; l < c.layers; ++l) {
-    const void* x_in = l == 0 ? S->buf<void>("x_emb") : S->buf<void>("down");
-    SG_TRY(sg_rmsnorm(x_in, S->buf<void>("resid"), S->in_norm[l], S->buf<void>("xnorm"), T, H, c.rms_eps, SG_DT_F16,
-                      st),
-           "input rmsnorm");
-    if ((r = linear(S, S->qkv[l], S->buf<void>("xnorm"), S->buf<void>("qkv"), T, SG_DT_F16)) != ARMCC_OK) return r;
+    if (fuse) {
+      if ((r = linear(S, S->qkv[l], resid, S->buf<void>("qkv"), T, SG_DT_F16, SG_MM_A_RMSNORM, S->in_norm[l])) !=
+          ARMCC_OK)
+        return r;
+    } else {
+      const void* x_in = l == 0 ? S->buf<void>("x_emb") : S->buf<void>("down");
+      SG_TRY(sg_rmsnorm(x_in, resid, S->in_norm[l], S->buf<void>("xnorm"), T, H, c.rms_eps, SG_DT_F16, st),
+             "input rmsnorm");
+      if ((r = linear(S, S->qkv[l], S->buf<void>("xnorm"), S->buf<void>("qkv"), T, SG_DT_F16)) != ARMCC_OK) return r;
+    }
     if (S->paged) {
       SG_TRY(sg_qkv_rope_append_paged(S->buf<void>("qkv"), B, Ts, c.heads, c.kv_heads, D,
                                       dev_pos ? S->buf<int32_t>("pos") : nullptr, S->pos, c.rope_theta,
@@ -617,10 +647,21 @@ ArmStatus forward(ArmSession_* S, int Ts, bool from_next, bool dev_pos = false) 
                "head transpose");
       attn_rows = S->buf<void>("attn_t");
     }
+    if (fuse) {
+      // resid += o; gate|up of the post-attention norm; resid += down(SwiGLU)
+      if ((r = linear(S, S->o[l], attn_rows, resid, T, SG_DT_F16, SG_MM_C_ACCUMULATE)) != ARMCC_OK) return r;
+      if ((r = linear(S, S->gu[l], resid, S->buf<void>("gu"), T, SG_DT_F16, SG_MM_A_RMSNORM, S->post_norm[l])) !=
+          ARMCC_OK)
+        return r;
+      if ((r = swiglu_down(S, S->down[l], S->buf<void>("gu"), S->buf<void>("act"), resid, T, S->down[l].K,
+                           SG_MM_C_ACCUMULATE)) != ARMCC_OK)
+        return r;
+      continue;
+    }
     if ((r = linear(S, S->o[l], attn_rows, S->buf<void>("o"), T, SG_DT_F16)) != ARMCC_OK) return r;
     if ((r = tp_sum(S, S->buf<void>("o"), (size_t)T * H)) != ARMCC_OK) return r;
-    SG_TRY(sg_rmsnorm(S->buf<void>("o"), S->buf<void>("resid"), S->post_norm[l], S->buf<void>("xnorm"), T, H,
-                      c.rms_eps, SG_DT_F16, st),
+    SG_TRY(sg_rmsnorm(S->buf<void>("o"), resid, S->post_norm[l], S->buf<void>("xnorm"), T, H, c.rms_eps, SG_DT_F16,
+                      st),
            "post-attention rmsnorm");
     if ((r = linear(S, S->gu[l], S->buf<void>("xnorm"), S->buf<void>("gu"), T, SG_DT_F16)) != ARMCC_OK) return r;
     if ((r = swiglu_down(S, S->down[l], S->buf<void>("gu"), S->buf<void>("act"), S->buf<void>("down"), T,
@@ -642,10 +683,22 @@ ArmStatus forward(ArmSession_* S, int Ts, bool from_next, bool dev_pos = false) 
     x_last = S->buf<void>("last_x");
     r_last = S->buf<void>("last_r");
   }
-  SG_TRY(sg_rmsnorm(x_last, const_cast<void*>(r_last), S->final_norm, S->buf<void>("last_n"), B, H, c.rms_eps,
-                    SG_DT_F16, st),
-         "final rmsnorm");
-  if (c.lm_int4) {
+  if (fuse && c.lm_int4) {
+    // the residual stream already holds h: the final norm is the LM head's activation staging
+    if ((r = linear(S, S->lm, resid, S->buf<void>("logits"), B, SG_DT_F32, SG_MM_A_RMSNORM, S->final_norm)) !=
+        ARMCC_OK)
+      return r;
+  } else if (fuse) {
+    SG_TRY(sg_rmsnorm(resid, nullptr, S->final_norm, S->buf<void>("last_n"), B, H, c.rms_eps, SG_DT_F16, st),
+           "final rmsnorm");
+  } else {
+    SG_TRY(sg_rmsnorm(x_last, const_cast<void*>(r_last), S->final_norm, S->buf<void>("last_n"), B, H, c.rms_eps,
+                      SG_DT_F16, st),
+           "final rmsnorm");
+  }
+  if (fuse && c.lm_int4) {
+    // done above
+  } else if (c.lm_int4) {
     if ((r = linear(S, S->lm, S->buf<void>("last_n"), S->buf<void>("logits"), B, SG_DT_F32)) != ARMCC_OK) return r;
   } else {
     SgMatMulParams p{};
@@ -1460,6 +1513,32 @@ ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int r
     S->lm_f16 = t("lm_head.weight", (uint64_t)c.vocab * H2);
     if (!S->lm_f16) return cleanup_fail("lm_head.weight missing or of the wrong size");
   }
+  // the norms fuse into the projections when the one-row kernel takes every shape
+  {
+    const int sms = sg::sm_count(S->dev);
+    bool ok = c.hidden % 8 == 0 && c.hidden <= 8192;
+    auto takes = [&](const Linear& L, int cdt) {
+      SgMatMulParams p{};
+      p.A = p.C = S->act;
+      p.B = L.qw;
+      p.scales_B = L.scales;
+      p.zeros_B = L.zeros;
+      p.M = 1;
+      p.K = L.K;
+      p.N = L.N;
+      p.group_size = c.group_size;
+      p.a_dtype = SG_DT_F16;
+      p.c_dtype = cdt;
+      bool applicable = false;
+      sg::w4_gemv_mma_scratch_bytes(&p, sms, &applicable);
+      return applicable;
+    };
+    for (int l = 0; ok && l < c.layers; ++l)
+      ok = takes(S->qkv[l], SG_DT_F16) && takes(S->o[l], SG_DT_F16) && takes(S->gu[l], SG_DT_F16) &&
+           takes(S->down[l], SG_DT_F16);
+    if (ok && c.lm_int4) ok = takes(S->lm, SG_DT_F32);
+    S->norm_fusable = ok;
+  }
   return S.release();
 }
 
@@ -1471,6 +1550,10 @@ namespace sg {
 bool sdk_tuning(std::string_view key, int value) {
   if (key == "sdk.fuse_swiglu") {
     g_fuse_swiglu.store(value);
+    return true;
+  }
+  if (key == "sdk.fuse_norm") {
+    g_fuse_norm.store(value);
     return true;
   }
   return false;

@@ -324,6 +324,15 @@ SgStatus validate(const SgMatMulParams* p) {
   }
   SG_CHECK_ARG(cdt == SG_DT_F32 || cdt == SG_DT_F16 || cdt == SG_DT_BF16,
                "sg_matmul_int4_grouped: bad c_dtype %d", p->c_dtype);
+  if (p->flags & SG_MM_A_RMSNORM) {
+    SG_CHECK_ARG((adt == SG_DT_F16 || adt == SG_DT_BF16) && p->norm_weight && p->K % 8 == 0 && p->K <= 8192 &&
+                     sg::aligned16(p->A) && sg::aligned16(p->norm_weight) && !(p->flags & SG_MM_A_SWIGLU),
+                 "sg_matmul_int4_grouped: SG_MM_A_RMSNORM needs a 16-bit, 16-byte aligned A row of K %% 8 == 0 "
+                 "<= 8192 values, a norm_weight, and no SG_MM_A_SWIGLU");
+  }
+  if (p->flags & SG_MM_C_ACCUMULATE) {
+    SG_CHECK_ARG(cdt == SG_DT_F16 || cdt == SG_DT_BF16, "sg_matmul_int4_grouped: SG_MM_C_ACCUMULATE needs a 16-bit C");
+  }
   return SG_OK;
 }
 
@@ -435,7 +444,8 @@ static SgStatus w4_run(const SgMatMulParams* p, void* stream, void* ws, size_t w
   // weights (the second pass reads them mostly from L2).  Measured on B200 at 24-32 rows
   // (Qwen-7B shapes, g128): q|k|v 30.2 -> 19.7 us, o 30.6 -> 15.4, gate|up 58.3 -> 54.7,
   // LM head 244 -> 203 against the tcgen05 GEMM, whose 128-row tiles are mostly empty there.
-  if (path == 0 && p->M >= 2 && p->M <= std::max(16, g_tune_rows_two_pass.load())) {
+  const bool fused_norm = (p->flags & (SG_MM_A_RMSNORM | SG_MM_C_ACCUMULATE)) != 0;  // one-row kernel only
+  if (path == 0 && !fused_norm && p->M >= 2 && p->M <= std::max(16, g_tune_rows_two_pass.load())) {
     if (err_word == nullptr) {
       st = sg::device_error_word(&err_word);
       if (st != SG_OK) return st;
@@ -466,7 +476,7 @@ static SgStatus w4_run(const SgMatMulParams* p, void* stream, void* ws, size_t w
   const bool swiglu = (p->flags & SG_MM_A_SWIGLU) != 0;
   // Many activation rows: tcgen05 GEMM with the weights dequantized into TMEM (gemm_tc.cu).
   bool tc_ok = false;
-  const size_t tc_ws = path == 0 && !swiglu ? sg::gemm_tc_scratch_bytes(p, false, &tc_ok) : 0;
+  const size_t tc_ws = path == 0 && !swiglu && !fused_norm ? sg::gemm_tc_scratch_bytes(p, false, &tc_ok) : 0;
   if (tc_ok) {
     if (ws == nullptr && tc_ws > 0) {
       if (ws_external) {
@@ -509,6 +519,11 @@ static SgStatus w4_run(const SgMatMulParams* p, void* stream, void* ws, size_t w
   if (swiglu) {
     sg::set_error("sg_matmul_int4_grouped: SG_MM_A_SWIGLU is fused only on the one-row and 2..16-row kernels "
                   "(M=%d K=%d N=%d group %d)", p->M, p->K, p->N, p->group_size);
+    return SG_ERR_UNSUPPORTED;
+  }
+  if (p->flags & (SG_MM_A_RMSNORM | SG_MM_C_ACCUMULATE)) {
+    sg::set_error("sg_matmul_int4_grouped: SG_MM_A_RMSNORM / SG_MM_C_ACCUMULATE are fused only on the one-row "
+                  "tensor-core kernel (M=%d K=%d N=%d group %d)", p->M, p->K, p->N, p->group_size);
     return SG_ERR_UNSUPPORTED;
   }
 

@@ -52,6 +52,7 @@
 #include <mutex>
 #include <string_view>
 
+#include "rownorm.cuh"
 #include "sm100.cuh"
 
 namespace {
@@ -107,6 +108,10 @@ struct MArgs {
   int sleep_wait;      // back off with nanosleep while waiting for a stage
   int static_w;        // weights may be requested before the dependency wait
   int swiglu;          // A is [gate | up]: x = SwiGLU(A[k], A[K + k]) (SG_MM_A_SWIGLU)
+  int norm;            // A is a residual-stream row: x = RMSNorm(A)[k] (SG_MM_A_RMSNORM)
+  const void* norm_w;
+  float norm_eps;
+  int accum;           // C = round(C + round(y)) (SG_MM_C_ACCUMULATE)
   float* slots;        // [nblocks][2][512]: first / last segment partials
   unsigned* tickets;   // [n_tiles]
   int* err;
@@ -128,9 +133,21 @@ __device__ __forceinline__ float load_act(const void* A, int dt, int i) {
   }
 }
 
-// Activation k of the row: A[k], or with SG_MM_A_SWIGLU the SwiGLU of gate
-// A[k] and up A[K + k] rounded to A's type, as sg_swiglu_rows writes it.
-__device__ __forceinline__ float load_x(const MArgs& a, int k) {
+// Activation k of the row: A[k]; with SG_MM_A_SWIGLU the SwiGLU of gate
+// A[k] and up A[K + k] rounded to A's type, as sg_swiglu_rows writes it; with
+// SG_MM_A_RMSNORM h[k] * rms_inv * w[k] rounded to A's type, as sg_rmsnorm
+// writes it (rms_inv of the whole row, formed as sg_rmsnorm forms it).
+__device__ __forceinline__ float load_x(const MArgs& a, int k, float rms_inv) {
+  if (a.norm) {
+    if (a.a_dt == SG_DT_BF16) {
+      const float h = __bfloat162float(static_cast<const __nv_bfloat16*>(a.A)[k]);
+      const float w = __bfloat162float(static_cast<const __nv_bfloat16*>(a.norm_w)[k]);
+      return __bfloat162float(__float2bfloat16_rn(h * rms_inv * w));
+    }
+    const float h = __half2float(static_cast<const __half*>(a.A)[k]);
+    const float w = __half2float(static_cast<const __half*>(a.norm_w)[k]);
+    return __half2float(__float2half_rn(h * rms_inv * w));
+  }
   if (a.swiglu) {
     if (a.a_dt == SG_DT_BF16) {
       const __nv_bfloat16* p = static_cast<const __nv_bfloat16*>(a.A);
@@ -154,6 +171,24 @@ __device__ __forceinline__ float finalize(const MArgs& a, int col, float v) {
   if (a.a_dt == SG_DT_I8) v = v * a.scale_A;
   if (a.bias) v = v + __half2float(a.bias[col]);
   return v;
+}
+
+// The column's final value: finalize, then either stored, or (SG_MM_C_ACCUMULATE)
+// rounded to C's type and added to C with one more rounding -- the residual add
+// of sg_rmsnorm, h = round(x + residual).
+__device__ __forceinline__ void store_final(const MArgs& a, int col, float v) {
+  v = finalize(a, col, v);
+  if (a.accum) {
+    if (a.c_dt == SG_DT_BF16) {
+      __nv_bfloat16* c = static_cast<__nv_bfloat16*>(a.C);
+      c[col] = __float2bfloat16_rn(__bfloat162float(__float2bfloat16_rn(v)) + __bfloat162float(c[col]));
+    } else {
+      __half* c = static_cast<__half*>(a.C);
+      c[col] = __float2half_rn(__half2float(__float2half_rn(v)) + __half2float(c[col]));
+    }
+    return;
+  }
+  store_out(a.C, a.c_dt, col, v);
 }
 
 __device__ __forceinline__ int group_of(const MArgs& a, int k) { return a.gs_shift >= 0 ? (k >> a.gs_shift) : k / a.gs; }
@@ -254,6 +289,14 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS <= 8 ? 2 : 1)
   // promise it is requested first, so that its few bytes are not queued
   // behind this block's weight stream.
   sgd::pdl_wait();
+  // SG_MM_A_RMSNORM: the row's 1 / rms over all K values, as sg_rmsnorm forms it
+  __shared__ float s_red[32];
+  float rms_inv = 0.f;
+  if (a.norm) {
+    rms_inv = a.a_dt == SG_DT_BF16
+                  ? sgn::row_rms_inv(static_cast<const __nv_bfloat16*>(a.A), a.K, a.norm_eps, s_red)
+                  : sgn::row_rms_inv(static_cast<const __half*>(a.A), a.K, a.norm_eps, s_red);
+  }
   auto slot_row = [&](int idx, int& k) {  // staging row idx -> k of its even element
     const int sl = idx / kRows, r = idx - sl * kRows;
     const int crow = a.x_by_row ? sl : (cs + sl) % a.cpt;
@@ -268,8 +311,8 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS <= 8 ? 2 : 1)
     if (idx < nslots * kRows) {
       int k;
       slot_row(idx, k);
-      if (k < a.K) xe_pf[j] = load_x(a, k);
-      if (k + 1 < a.K) xo_pf[j] = load_x(a, k + 1);
+      if (k < a.K) xe_pf[j] = load_x(a, k, rms_inv);
+      if (k + 1 < a.K) xo_pf[j] = load_x(a, k + 1, rms_inv);
     }
   }
   if (!a.static_w && lane == 0) {
@@ -291,8 +334,8 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS <= 8 ? 2 : 1)
       xe = j == 0 ? xe_pf[0] : xe_pf[1];
       xo = j == 0 ? xo_pf[0] : xo_pf[1];
     } else {
-      xe = (k < a.K) ? load_x(a, k) : 0.f;
-      xo = (k + 1 < a.K) ? load_x(a, k + 1) : 0.f;
+      xe = (k < a.K) ? load_x(a, k, rms_inv) : 0.f;
+      xo = (k + 1 < a.K) ? load_x(a, k + 1, rms_inv) : 0.f;
     }
     float m = fmaxf(fabsf(xe), fabsf(xo));
 #pragma unroll
@@ -472,7 +515,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS <= 8 ? 2 : 1)
         float v = 0.f;
         for (int r = 0; r < a.ksplit; ++r) v += csum[r * kTC + cc];
         const int col = tile * kTC + cc;
-        if (col < a.N) store_out(a.C, a.c_dt, col, finalize(a, col, v));
+        if (col < a.N) store_final(a, col, v);
       }
     }
     return;
@@ -490,7 +533,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS <= 8 ? 2 : 1)
       for (int ph = 0; ph < kPhases; ++ph) v += red[(s2 * kPhases + ph) * kTC + cc];
       const int col = tile * kTC + cc;
       if (!shared_tile) {
-        if (col < a.N) store_out(a.C, a.c_dt, col, finalize(a, col, v));
+        if (col < a.N) store_final(a, col, v);
       } else {
         a.slots[((int64_t)b * 2 + slot) * kTC + cc] = v;
       }
@@ -526,7 +569,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS <= 8 ? 2 : 1)
         for (int u = 0; u < 8; ++u)
           if (b0 + u <= b_hi) v += pv[u];
       }
-      if (col < a.N) store_out(a.C, a.c_dt, col, finalize(a, col, v));
+      if (col < a.N) store_final(a, col, v);
     }
     if (threadIdx.x == 0) a.tickets[tile] = 0u;
   }
@@ -738,6 +781,10 @@ SgStatus w4_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, void
   a.sleep_wait = g_sleep.load() ? 1 : 0;
   a.static_w = (p->flags & SG_MM_STATIC_WEIGHTS) ? 1 : 0;
   a.swiglu = (p->flags & SG_MM_A_SWIGLU) ? 1 : 0;
+  a.norm = (p->flags & SG_MM_A_RMSNORM) ? 1 : 0;
+  a.norm_w = p->norm_weight;
+  a.norm_eps = p->norm_eps;
+  a.accum = (p->flags & SG_MM_C_ACCUMULATE) ? 1 : 0;
   a.tickets = static_cast<unsigned*>(ws);
   a.slots = reinterpret_cast<float*>(static_cast<char*>(ws) + pl.tickets_bytes);
   a.err = err_word;

@@ -48,9 +48,12 @@ def _stream(stream) -> int | None:
 
 def matmul_params(A, B, C, *, M: int, K: int, N: int, scales=None, zeros=None, bias=None,
                   group_size: int = 0, scale_A: float = 1.0, lda: int = 0, ldc: int = 0,
-                  workspace: torch.Tensor | None = None, flags: int = 0) -> SgMatMulParams:
+                  workspace: torch.Tensor | None = None, flags: int = 0, norm_weight=None,
+                  norm_eps: float = 1e-5) -> SgMatMulParams:
     p = SgMatMulParams()
     p.flags = flags
+    p.norm_weight = _ptr(norm_weight)
+    p.norm_eps = norm_eps
     p.A = _ptr(A)
     p.B = _ptr(B)
     p.bias = _ptr(bias)

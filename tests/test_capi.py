@@ -87,7 +87,7 @@ def test_flag_values_match_header():
     """The Python binding's SG_MM_* flag values are the header's."""
     from silicongraph_b200 import _lib
     src = open(os.path.join(ROOT, "include", "sg_kernels.h")).read()
-    for name in ("SG_MM_STATIC_WEIGHTS", "SG_MM_A_SWIGLU"):
+    for name in ("SG_MM_STATIC_WEIGHTS", "SG_MM_A_SWIGLU", "SG_MM_A_RMSNORM", "SG_MM_C_ACCUMULATE"):
         m = re.search(rf"#define {name} (\d+)u", src)
         assert m, name
         assert int(m.group(1)) == getattr(_lib, name)
@@ -96,7 +96,7 @@ def test_flag_values_match_header():
 @pytest.mark.parametrize("key,value", [
     ("w4_rows.enable", 1), ("w4_rows.stages", 0), ("w4_rows.producer_sleep", 1), ("w4_rows.max_tiles", 1 << 30),
     ("w4_gemv_mma.strips", 0), ("w4_gemv_mma.variant", 0), ("attn.decode_kernel", 4), ("sdk.fuse_swiglu", 1),
-    ("w4_rows.two_pass_rows", 32),
+    ("w4_rows.two_pass_rows", 32), ("tp_allreduce.wait_ms", 0), ("sdk.fuse_norm", 1),
 ])
 def test_tuning_keys_known(lib, key, value):
     """Every tuning knob the kernels and the SDK read is reachable through
@@ -121,3 +121,25 @@ def test_swiglu_flag_argument_checks(lib):
     p.lda = 64     # < 2K
     assert lib.sg_matmul_int4_grouped(ctypes.byref(p), None) == SG_ERR_INVALID
     assert b"lda" in lib.sg_last_error()
+
+
+def test_fused_norm_flag_argument_checks(lib):
+    """SG_MM_A_RMSNORM needs a 16-bit A, a norm weight and K % 8 == 0 (checked
+    before any device work); SG_MM_C_ACCUMULATE needs a 16-bit C."""
+    from silicongraph_b200._lib import (SG_DT_F32, SG_ERR_INVALID, SG_MM_A_RMSNORM, SG_MM_C_ACCUMULATE,
+                                        SgMatMulParams)
+    buf = (ctypes.c_uint8 * 8192)()
+    base = (ctypes.addressof(buf) + 255) // 256 * 256
+    p = SgMatMulParams()
+    p.A = p.B = p.C = p.scales_B = base
+    p.M, p.K, p.N, p.group_size = 1, 64, 16, 32
+    p.a_dtype, p.c_dtype = 2, 2
+    p.flags = SG_MM_A_RMSNORM
+    assert lib.sg_matmul_int4_grouped(ctypes.byref(p), None) == SG_ERR_INVALID  # no norm weight
+    assert b"SG_MM_A_RMSNORM" in lib.sg_last_error()
+    p.norm_weight = base
+    p.K = 60                                                                   # not a multiple of 8
+    assert lib.sg_matmul_int4_grouped(ctypes.byref(p), None) == SG_ERR_INVALID
+    p.K, p.flags, p.c_dtype = 64, SG_MM_C_ACCUMULATE, SG_DT_F32
+    assert lib.sg_matmul_int4_grouped(ctypes.byref(p), None) == SG_ERR_INVALID
+    assert b"SG_MM_C_ACCUMULATE" in lib.sg_last_error()

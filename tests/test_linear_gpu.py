@@ -507,3 +507,49 @@ def test_int4_two_pass_rows(sg, oracle_mod, M, K, N, gs):
     want = oracle_mod.matmul_int4_grouped(x, B, S, Z, K, N, gs, M=M, c_dt=oracle_mod.DT_F32)
     C = sg.matmul_int4_grouped(t(x), t(B), t(S), t(Z), K, N, gs, out_dtype=torch.float32)
     close(C.cpu().numpy(), want)
+
+
+# ------------------------------------------------------------------ fused norm / residual add
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("K,N,gs", [(2048, 3072, 32), (3584, 4608, 128), (2048, 128256 // 8, 32)])
+def test_fused_rmsnorm_gemv_equals_two_kernels(sg, oracle_mod, dt, K, N, gs):
+    """SG_MM_A_RMSNORM: the GEMV of RMSNorm(h) equals sg_rmsnorm then the GEMV,
+    bit for bit (both form the row's sum of squares the same way)."""
+    from silicongraph_b200._lib import SG_MM_A_RMSNORM
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=K + N)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(K)
+    h = (torch.randn(1, K, generator=g, device="cuda") * 3).to(dt)
+    w = (1 + 0.1 * torch.randn(K, generator=g, device="cuda")).to(dt)
+    xn = sg.rmsnorm(h, w, eps=1e-5)
+    want = sg.matmul_int4_grouped(xn, t(B), t(S), t(Z), K, N, gs, out_dtype=dt)
+    import ctypes
+    from silicongraph_b200 import _lib
+    got = torch.empty_like(want)
+    p = sg.matmul_params(h, t(B), got, M=1, K=K, N=N, scales=t(S), zeros=t(Z), group_size=gs,
+                         flags=SG_MM_A_RMSNORM, norm_weight=w, norm_eps=1e-5)
+    _lib.check(_lib.load().sg_matmul_int4_grouped(ctypes.byref(p), torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_accumulating_gemv_equals_residual_add(sg, oracle_mod, dt):
+    """SG_MM_C_ACCUMULATE: C = round(C + round(y)) equals the GEMV followed by
+    sg_rmsnorm's residual update, bit for bit."""
+    import ctypes
+    from silicongraph_b200 import _lib
+    from silicongraph_b200._lib import SG_MM_C_ACCUMULATE
+    K, N, gs = 8192, 2048, 32
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=3)
+    x = torch.randn(1, K, device="cuda").to(dt)
+    resid0 = (torch.randn(1, N, device="cuda") * 4).to(dt)
+    y = sg.matmul_int4_grouped(x, t(B), t(S), t(Z), K, N, gs, out_dtype=dt)
+    want = resid0.clone()
+    sg.rmsnorm(y, torch.ones(N, dtype=dt, device="cuda"), residual=want)  # want = round(resid0 + y)
+    got = resid0.clone()
+    p = sg.matmul_params(x, t(B), got, M=1, K=K, N=N, scales=t(S), zeros=t(Z), group_size=gs,
+                         flags=SG_MM_C_ACCUMULATE)
+    _lib.check(_lib.load().sg_matmul_int4_grouped(ctypes.byref(p), torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)

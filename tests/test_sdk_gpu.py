@@ -172,3 +172,28 @@ def test_select_graph_refuses_before_allocation(sg, tmp_path):
             pkg.select(64, ram_mb=max(1, budget_mb))
         assert "95%" in str(e.value)
         assert pkg.select(64, ram_mb=budget_mb + 2) is not None
+
+
+def test_fused_norm_decode_equals_unfused(sg, tmp_path):
+    """One-row decode steps with the norms and residual adds fused into the
+    projections give the same tokens and logits, bit for bit, as the steps
+    with separate norm kernels (sdk.fuse_norm 0)."""
+    from silicongraph_b200 import sdk
+    path, _ = _package(tmp_path, 128)
+    prompt = (np.arange(33, dtype=np.int32) * 11) % SMALL["vocab_size"]
+    runs = []
+    try:
+        for fuse in (1, 0):
+            sg.set_tuning("sdk.fuse_norm", fuse)
+            with sdk.Package(path) as pkg:
+                with pkg.select().session() as s:
+                    s.prefill(prompt)
+                    toks, logits = [], []
+                    for _ in range(6):
+                        toks.append(s.decode().next_token_id)
+                        logits.append(s.last_logits(SMALL["vocab_size"]))
+            runs.append((toks, np.stack(logits)))
+    finally:
+        sg.set_tuning("sdk.fuse_norm", 1)
+    assert runs[0][0] == runs[1][0]
+    assert np.array_equal(runs[0][1], runs[1][1])
