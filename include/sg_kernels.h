@@ -354,6 +354,27 @@ SgStatus sg_qkv_rope_append_paged(const void* qkv, int32_t batch, int32_t seq_to
                                   float base, void* q_out, void* k_pages, void* v_pages, const SgKvPages* pages,
                                   int32_t io_dtype, void* stream);
 
+/* The q|k|v projection of one decode row fused with the rotary embedding and
+ * the KV append: C = the INT4 GEMV of p (M = 1, N = (heads + 2 kv_heads) *
+ * head_dim, fp16 or bf16 output; p->C is not written), then exactly what
+ * sg_qkv_rope_append does with that output, done in the GEMV's epilogue.  Any
+ * p->flags apply (e.g. SG_MM_A_RMSNORM).  head_dim 64 or 128; shapes the
+ * one-row tensor-core kernel does not take with a cluster split return
+ * SG_ERR_UNSUPPORTED (use the two calls).  No reference counterpart as one
+ * call (matmul_int4_grouped_neon then rope_apply_neon). */
+typedef struct SgRopeAppend {
+  int32_t heads, kv_heads, head_dim;
+  const int32_t* positions;   /* device position of the row, or NULL for pos0     */
+  int32_t pos0;
+  float base;                 /* RoPE theta base                                  */
+  void* q_out;                /* [heads, head_dim]                                */
+  void* k_cache;              /* flat: [kv_heads] rows at kv_head_stride; paged:   */
+  void* v_cache;              /*   the K / V halves of page 0 (SgKvPages)          */
+  int64_t kv_head_stride;     /* flat: elements between kv heads                   */
+  const SgKvPages* kv_pages;  /* NULL: flat                                        */
+} SgRopeAppend;
+SgStatus sg_qkv_gemv_rope_append(const SgMatMulParams* p, const SgRopeAppend* rope, void* stream);
+
 /* The same for `batch` sequences of seq_tokens tokens each (token t of the
  * input is token t % seq_tokens of sequence t / seq_tokens): q goes to
  * q_out [batch, heads, seq_tokens, head_dim], k / v of sequence b to the

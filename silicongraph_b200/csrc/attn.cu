@@ -60,14 +60,18 @@ struct AArgs {
 // page that holds it, [page][kv_head][16][D] within the pool (the reference's
 // page layout, kv_cache_layout.cpp:65-102).  A page id outside the pool reads
 // page 0 instead and sets bit 4 of the device error word.
-__device__ __forceinline__ int64_t kv_off(const AArgs& a, int b, int hk, int key) {
-  if (!a.pt) return (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs + (int64_t)key * a.D;
+__device__ __forceinline__ int kv_page(const AArgs& a, int b, int key) {
   int page = __ldg(a.pt + (int64_t)b * a.pt_bs + (int64_t)(key >> 4) * a.pt_ps);
   if ((unsigned)page >= (unsigned)a.npages) {
     if (a.err) atomicOr(a.err, 4);
     page = 0;
   }
-  return (int64_t)page * a.page_stride + ((int64_t)hk * 16 + (key & 15)) * a.D;
+  return page;
+}
+
+__device__ __forceinline__ int64_t kv_off(const AArgs& a, int b, int hk, int key) {
+  if (!a.pt) return (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs + (int64_t)key * a.D;
+  return (int64_t)kv_page(a, b, key) * a.page_stride + ((int64_t)hk * 16 + (key & 15)) * a.D;
 }
 
 __device__ __forceinline__ float ld_io(const void* p, int dt, int64_t i) {
@@ -919,18 +923,35 @@ __global__ void __launch_bounds__(kDecWarpThreads) attn_dec_warp_kernel(AArgs a)
   const int ngroups = j1 > j0 ? (j1 - j0 + KG - 1) / KG : 0;
   const int nmine = ngroups > warp ? (ngroups - warp + kW - 1) / kW : 0;  // groups warp, warp + kW, ...
 
+  // Paged cache: a group of KG = 16 keys starts on a page boundary (splits are
+  // whole 64-key tiles), so it is one page; the pages of the warp's first 64
+  // groups are looked up once, lane l holding groups l and l + 32.
+  int pgs[2] = {0, 0};
+  if (a.pt) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int gi = lane + 32 * h;
+      if (gi < nmine) pgs[h] = kv_page(a, b, j0 + (warp + kW * gi) * KG);
+    }
+  }
   // lane's pieces of group i (the warp's i-th) into stage i % ST; zeros past the last key
-  auto issue = [&](int i) {
+  auto issue = [&](int i) {  // called by the whole warp with the same i
     const int key0 = j0 + (warp + kW * i) * KG;
+    int64_t gbase;  // element offset of the group's first key
+    if (a.pt) {
+      const int pg = i < 64 ? __shfl_sync(0xffffffffu, pgs[i >> 5], i & 31) : kv_page(a, b, key0);
+      gbase = (int64_t)pg * a.page_stride + (int64_t)hk * KG * D;
+    } else {
+      gbase = (int64_t)b * a.kv_bs + (int64_t)hk * a.kv_hs + (int64_t)key0 * D;
+    }
     __half* kd = ring + (size_t)(i % ST) * 2 * KG * KP;
     __half* vd = kd + KG * KP;
 #pragma unroll
     for (int u = 0; u < NP; ++u) {
       const int pc = lane + 32 * u;
       const int kl = pc / (D / 8), part = pc % (D / 8);
-      const int key = key0 + kl;
-      const bool live = key < j1;
-      const int64_t e0 = kv_off(a, b, hk, live ? key : j0) + part * 8;
+      const bool live = key0 + kl < j1;
+      const int64_t e0 = gbase + (int64_t)(live ? kl : 0) * D + part * 8;  // a dead key reads nothing
       sgd::cp_async_16(kd + kl * KP + part * 8, static_cast<const uint16_t*>(a.K) + e0, live);
       sgd::cp_async_16(vd + kl * KP + part * 8, static_cast<const uint16_t*>(a.V) + e0, live);
     }

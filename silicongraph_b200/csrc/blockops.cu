@@ -177,12 +177,12 @@ __global__ void rope_kernel(void* x, int tokens, int heads, int D, const int32_t
     const int64_t th = e / half;  // token * heads + head
     const int t = (int)(th / heads);
     const int p = pos ? pos[t] : pos0 + t;
-    const float theta = (float)p / powf(base, 2.0f * i / (float)D);
-    const float c = cosf(theta), s = sinf(theta);
     const int64_t r = th * D;
     const float x0 = ld(x, dt, r + i), x1 = ld(x, dt, r + i + half);
-    st(x, dt, r + i, x0 * c - x1 * s);
-    st(x, dt, r + i + half, x0 * s + x1 * c);
+    float y0, y1;
+    sgd::rope_pair(x0, x1, p, i, D, base, &y0, &y1);
+    st(x, dt, r + i, y0);
+    st(x, dt, r + i + half, y1);
   }
 }
 

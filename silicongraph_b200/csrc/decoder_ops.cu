@@ -42,9 +42,8 @@ __global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, int T_, int Ts
     const T* src = qkv + ((int64_t)t * slots + slot) * D;
     float x0 = (float)src[i], x1 = (float)src[i + half];
     if (slot < H + Hkv) {  // q and k rotate
-      const float theta = (float)p / powf(base, 2.0f * i / (float)D);
-      const float c = cosf(theta), s = sinf(theta);
-      const float y0 = x0 * c - x1 * s, y1 = x0 * s + x1 * c;
+      float y0, y1;
+      sgd::rope_pair(x0, x1, p, i, D, base, &y0, &y1);
       x0 = y0;
       x1 = y1;
     }

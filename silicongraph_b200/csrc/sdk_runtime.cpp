@@ -440,6 +440,7 @@ struct ArmSession_ {
   std::string abort_why;
   // every projection's one-row shape runs on the kernel that fuses the norms (SG_MM_A_RMSNORM / C_ACCUMULATE)
   bool norm_fusable = false;
+  bool rope_fusable = false;  // ... and the q|k|v one is a cluster split with head_dim 64 / 128
   int tp_timeout_ms = 60000;
 
   ~ArmSession_() {
@@ -508,6 +509,9 @@ std::atomic<int> g_fuse_swiglu{1};
 // SG_MM_C_ACCUMULATE on o and down): the residual stream lives in "resid", the
 // embedding writes it directly, and no separate norm kernel runs.
 std::atomic<int> g_fuse_norm{1};
+// ... and the rope + KV append into the q|k|v projection's epilogue
+// (sg_qkv_gemv_rope_append), when its plan is a cluster split.
+std::atomic<int> g_fuse_rope{1};
 
 ArmStatus linear(ArmSession_* S, const Linear& L, const void* A, void* C, int M, int c_dt, uint32_t flags = 0,
                  const void* norm_w = nullptr) {
@@ -592,17 +596,52 @@ ArmStatus forward(ArmSession_* S, int Ts, bool from_next, bool dev_pos = false) 
   }
   ArmStatus r;
   for (int l = 0; l < c.layers; ++l) {
+    bool appended = false;  // the q|k|v GEMV's epilogue did the rope and the KV append
     if (fuse) {
-      if ((r = linear(S, S->qkv[l], resid, S->buf<void>("qkv"), T, SG_DT_F16, SG_MM_A_RMSNORM, S->in_norm[l])) !=
-          ARMCC_OK)
+      if (S->rope_fusable && g_fuse_rope.load()) {
+        SgMatMulParams p{};
+        p.A = resid;
+        p.B = S->qkv[l].qw;
+        p.C = S->buf<void>("qkv");
+        p.M = 1;
+        p.K = S->qkv[l].K;
+        p.N = S->qkv[l].N;
+        p.scales_B = S->qkv[l].scales;
+        p.zeros_B = S->qkv[l].zeros;
+        p.group_size = c.group_size;
+        p.a_dtype = SG_DT_F16;
+        p.c_dtype = SG_DT_F16;
+        p.scale_A = 1.0f;
+        p.flags = SG_MM_STATIC_WEIGHTS | SG_MM_A_RMSNORM;
+        p.norm_weight = S->in_norm[l];
+        p.norm_eps = c.rms_eps;
+        SgRopeAppend ra{};
+        ra.heads = c.heads;
+        ra.kv_heads = c.kv_heads;
+        ra.head_dim = D;
+        ra.positions = dev_pos ? S->buf<int32_t>("pos") : nullptr;
+        ra.pos0 = S->pos;
+        ra.base = c.rope_theta;
+        ra.q_out = S->buf<void>("qh");
+        ra.k_cache = S->kcache(l);
+        ra.v_cache = S->vcache(l);
+        ra.kv_head_stride = S->kv_head_stride;
+        ra.kv_pages = S->paged ? &S->kvp[l] : nullptr;
+        SG_TRY(sg_qkv_gemv_rope_append(&p, &ra, st), "q|k|v projection with rope and KV append");
+        appended = true;
+      } else if ((r = linear(S, S->qkv[l], resid, S->buf<void>("qkv"), T, SG_DT_F16, SG_MM_A_RMSNORM,
+                             S->in_norm[l])) != ARMCC_OK) {
         return r;
+      }
     } else {
       const void* x_in = l == 0 ? S->buf<void>("x_emb") : S->buf<void>("down");
       SG_TRY(sg_rmsnorm(x_in, resid, S->in_norm[l], S->buf<void>("xnorm"), T, H, c.rms_eps, SG_DT_F16, st),
              "input rmsnorm");
       if ((r = linear(S, S->qkv[l], S->buf<void>("xnorm"), S->buf<void>("qkv"), T, SG_DT_F16)) != ARMCC_OK) return r;
     }
-    if (S->paged) {
+    if (appended) {
+      // done in the q|k|v projection
+    } else if (S->paged) {
       SG_TRY(sg_qkv_rope_append_paged(S->buf<void>("qkv"), B, Ts, c.heads, c.kv_heads, D,
                                       dev_pos ? S->buf<int32_t>("pos") : nullptr, S->pos, c.rope_theta,
                                       S->buf<void>("qh"), S->kcache(l), S->vcache(l), &S->kvp[l], SG_DT_F16, st),
@@ -1530,14 +1569,18 @@ ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int r
       p.a_dtype = SG_DT_F16;
       p.c_dtype = cdt;
       bool applicable = false;
-      sg::w4_gemv_mma_scratch_bytes(&p, sms, &applicable);
-      return applicable;
+      const size_t ws = sg::w4_gemv_mma_scratch_bytes(&p, sms, &applicable);
+      return applicable ? (ws == 0 ? 2 : 1) : 0;  // 2: a cluster split (no scratch)
     };
-    for (int l = 0; ok && l < c.layers; ++l)
-      ok = takes(S->qkv[l], SG_DT_F16) && takes(S->o[l], SG_DT_F16) && takes(S->gu[l], SG_DT_F16) &&
-           takes(S->down[l], SG_DT_F16);
-    if (ok && c.lm_int4) ok = takes(S->lm, SG_DT_F32);
+    bool cluster_qkv = c.head_dim == 64 || c.head_dim == 128;
+    for (int l = 0; ok && l < c.layers; ++l) {
+      const int q = takes(S->qkv[l], SG_DT_F16);
+      cluster_qkv = cluster_qkv && q == 2;
+      ok = q && takes(S->o[l], SG_DT_F16) && takes(S->gu[l], SG_DT_F16) && takes(S->down[l], SG_DT_F16);
+    }
+    if (ok && c.lm_int4) ok = takes(S->lm, SG_DT_F32) != 0;
     S->norm_fusable = ok;
+    S->rope_fusable = ok && cluster_qkv;
   }
   return S.release();
 }
@@ -1554,6 +1597,10 @@ bool sdk_tuning(std::string_view key, int value) {
   }
   if (key == "sdk.fuse_norm") {
     g_fuse_norm.store(value);
+    return true;
+  }
+  if (key == "sdk.fuse_rope") {
+    g_fuse_rope.store(value);
     return true;
   }
   return false;

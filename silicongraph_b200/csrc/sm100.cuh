@@ -340,6 +340,18 @@ __device__ __forceinline__ T swiglu_value(float g, float u) {
   return (T)(s * u);
 }
 
+// Rotary embedding of one pair (x0, x1) = (x[i], x[i + D/2]) at position pos
+// (rope_apply_neon, matmul_neon.h:262-275: theta = pos / base^(2i/D)), with
+// every product and sum rounded separately, as the reference's scalar loop
+// does; the rope kernel and the q|k|v GEMV that fuses it share this code.
+__device__ __forceinline__ void rope_pair(float x0, float x1, int pos, int i, int D, float base, float* y0,
+                                          float* y1) {
+  const float theta = (float)pos / powf(base, 2.0f * i / (float)D);
+  const float c = cosf(theta), s = sinf(theta);
+  *y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+  *y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+}
+
 // ---------------------------------------------- cluster shared-memory pushes
 // The shared::cluster address of `p` (this CTA's shared memory) in CTA `rank`.
 __device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {

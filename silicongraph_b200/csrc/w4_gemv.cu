@@ -395,7 +395,7 @@ SgStatus launch_fast(const W4Args& a, const Plan& pl, cudaStream_t st) {
 namespace sg {
 size_t w4_gemv_mma_scratch_bytes(const SgMatMulParams* p, int sms, bool* applicable);
 SgStatus w4_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, void* ws, size_t ws_bytes,
-                         int* err_word, bool* handled);
+                         int* err_word, bool* handled, const SgRopeAppend* rope = nullptr);
 bool w4_gemv_mma_tuning(std::string_view key, int value);
 SgStatus w4_rows_run(const SgMatMulParams* p, cudaStream_t cs, int sms, int* err_word, bool* handled);
 bool w4_rows_tuning(std::string_view key, int value);
@@ -596,6 +596,41 @@ size_t w4_gemv_scratch_bytes(const SgMatMulParams* p) {
 }  // namespace sg
 
 extern "C" {
+
+SgStatus sg_qkv_gemv_rope_append(const SgMatMulParams* p, const SgRopeAppend* r, void* stream) {
+  SgStatus st = validate(p);
+  if (st != SG_OK) return st;
+  SG_CHECK_ARG(r != nullptr, "sg_qkv_gemv_rope_append: rope is NULL");
+  SG_CHECK_ARG(p->M == 1, "sg_qkv_gemv_rope_append: one row only (M=%d)", p->M);
+  SG_CHECK_ARG(r->heads > 0 && r->kv_heads > 0 && (r->head_dim == 64 || r->head_dim == 128) &&
+                   p->N == (r->heads + 2 * r->kv_heads) * r->head_dim,
+               "sg_qkv_gemv_rope_append: N must be (heads + 2 kv_heads) * head_dim with head_dim 64 or 128");
+  const int cdt = p->c_dtype == SG_DT_DEFAULT ? SG_DT_F16 : p->c_dtype;
+  SG_CHECK_ARG(cdt == SG_DT_F16 || cdt == SG_DT_BF16, "sg_qkv_gemv_rope_append: 16-bit output only");
+  SG_CHECK_ARG(r->q_out && r->k_cache && r->v_cache, "sg_qkv_gemv_rope_append: NULL q / k / v");
+  SG_CHECK_ARG(!(p->flags & SG_MM_C_ACCUMULATE), "sg_qkv_gemv_rope_append: SG_MM_C_ACCUMULATE does not apply");
+  if (r->kv_pages) {
+    SG_CHECK_ARG(r->kv_pages->table && r->kv_pages->page_size == 16 && r->kv_pages->num_pages > 0,
+                 "sg_qkv_gemv_rope_append: bad SgKvPages");
+  } else {
+    SG_CHECK_ARG(r->kv_head_stride >= r->head_dim, "sg_qkv_gemv_rope_append: kv_head_stride < head_dim");
+  }
+  int dev = 0;
+  st = sg::current_device(&dev);
+  if (st != SG_OK) return st;
+  int* err = nullptr;
+  st = sg::device_error_word(&err);
+  if (st != SG_OK) return st;
+  bool handled = false;
+  st = sg::w4_gemv_mma_run(p, static_cast<cudaStream_t>(stream), sg::sm_count(dev), nullptr, 0, err, &handled, r);
+  if (st != SG_OK) return st;
+  if (!handled) {
+    sg::set_error("sg_qkv_gemv_rope_append: the one-row kernel does not take K=%d N=%d group %d with a cluster "
+                  "split; use sg_matmul_int4_grouped and sg_qkv_rope_append", p->K, p->N, p->group_size);
+    return SG_ERR_UNSUPPORTED;
+  }
+  return SG_OK;
+}
 
 SgStatus sg_matmul_int4_grouped(const SgMatMulParams* p, void* stream) {
   if (p && p->workspace) return w4_run(p, stream, p->workspace, p->workspace_bytes, true, nullptr);

@@ -112,6 +112,20 @@ struct MArgs {
   const void* norm_w;
   float norm_eps;
   int accum;           // C = round(C + round(y)) (SG_MM_C_ACCUMULATE)
+  // q|k|v epilogue (sg_qkv_gemv_rope_append): rank 0 of each cluster owns its
+  // whole tile, rounds it to C's type, rotates q and k and writes q / k / v
+  int rope;
+  int r_heads, r_kv, r_dim;
+  const int32_t* r_pos;
+  int r_pos0;
+  float r_base;
+  void* r_q;
+  void* r_k;
+  void* r_v;
+  int64_t r_kv_hs;
+  const int32_t* r_pt;
+  int64_t r_pt_bs, r_pt_ps, r_page_stride;
+  int r_npages;
   float* slots;        // [nblocks][2][512]: first / last segment partials
   unsigned* tickets;   // [n_tiles]
   int* err;
@@ -191,6 +205,70 @@ __device__ __forceinline__ void store_final(const MArgs& a, int col, float v) {
   store_out(a.C, a.c_dt, col, v);
 }
 
+// sg_qkv_gemv_rope_append's epilogue on rank 0 of a cluster, which holds every
+// rank's partial of the whole tile in csum[rank][kTC]: each column's sum
+// rounded to C's type (the q|k|v output sg_qkv_rope_append would read), then
+// the rotary pairs (i, i + D/2) of q and k heads and the plain v rows go to
+// q_out and the KV cache, as qkv_rope_append_kernel writes them.  Heads never
+// straddle tiles (D divides 128).
+__device__ __forceinline__ void rope_epilogue(const MArgs& a, float* csum, int tile, int kTC, int nthreads) {
+  const bool bf = a.c_dt == SG_DT_BF16;
+  auto rnd = [&](float v) {
+    return bf ? __bfloat162float(__float2bfloat16_rn(v)) : __half2float(__float2half_rn(v));
+  };
+  for (int cc = threadIdx.x; cc < kTC; cc += nthreads) {
+    float v = 0.f;
+    for (int r = 0; r < a.ksplit; ++r) v += csum[r * kTC + cc];
+    const int col = tile * kTC + cc;
+    csum[cc] = col < a.N ? rnd(finalize(a, col, v)) : 0.f;  // in place: only this thread reads column cc
+  }
+  __syncthreads();
+  const int D = a.r_dim, half = D / 2;
+  const int p = a.r_pos ? *a.r_pos : a.r_pos0;
+  for (int pc = threadIdx.x; pc < kTC / 2; pc += nthreads) {
+    const int cc = (pc / half) * D + pc % half;
+    const int col = tile * kTC + cc;
+    if (col >= a.N) continue;
+    const int slot = col / D, i = col % D;
+    float x0 = csum[cc], x1 = csum[cc + half];
+    if (slot < a.r_heads + a.r_kv) {
+      float y0, y1;
+      sgd::rope_pair(x0, x1, p, i, D, a.r_base, &y0, &y1);
+      x0 = y0;
+      x1 = y1;
+    }
+    int64_t off;
+    void* base;
+    if (slot < a.r_heads) {
+      base = a.r_q;
+      off = (int64_t)slot * D;
+    } else {
+      const bool is_k = slot < a.r_heads + a.r_kv;
+      const int hk = is_k ? slot - a.r_heads : slot - a.r_heads - a.r_kv;
+      base = is_k ? a.r_k : a.r_v;
+      if (a.r_pt) {
+        const int pg = __ldg(a.r_pt + (int64_t)(p >> 4) * a.r_pt_ps);
+        if ((unsigned)pg >= (unsigned)a.r_npages) {  // no such page: dropped and reported
+          if (i == 0) atomicOr(a.err, 4);
+          continue;
+        }
+        off = (int64_t)pg * a.r_page_stride + ((int64_t)hk * 16 + (p & 15)) * D;
+      } else {
+        off = (int64_t)hk * a.r_kv_hs + (int64_t)p * D;
+      }
+    }
+    if (bf) {
+      __nv_bfloat16* d = static_cast<__nv_bfloat16*>(base) + off;
+      d[i] = __float2bfloat16_rn(x0);
+      d[i + half] = __float2bfloat16_rn(x1);
+    } else {
+      __half* d = static_cast<__half*>(base) + off;
+      d[i] = __float2half_rn(x0);
+      d[i + half] = __float2half_rn(x1);
+    }
+  }
+}
+
 __device__ __forceinline__ int group_of(const MArgs& a, int k) { return a.gs_shift >= 0 ? (k >> a.gs_shift) : k / a.gs; }
 
 // CLUSTER: grid (ksplit, n_tiles), clusters of ksplit blocks own one tile and
@@ -236,7 +314,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS <= 8 ? 2 : 1)
   // cluster reduction: rank r owns columns [r * per, r * per + own) of the
   // tile and receives the other ranks' partials of them (plus their abort
   // flags) by st.async on s_rbar
-  const int per = CLUSTER ? ((kTC + a.ksplit - 1) / a.ksplit + 3) & ~3 : 1;
+  const int per = CLUSTER ? (a.rope ? kTC : ((kTC + a.ksplit - 1) / a.ksplit + 3) & ~3) : 1;
   const int own_lo = CLUSTER ? min(kTC, (int)blockIdx.x * per) : 0;
   const int own = CLUSTER ? min(kTC, own_lo + per) - own_lo : 0;
   if (threadIdx.x == 0) {
@@ -509,7 +587,9 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS <= 8 ? 2 : 1)
     int aborted = s_abort || !ok_wait;
     for (int r = 0; r < a.ksplit; ++r)
       if (r != rank) aborted |= s_aborts[r];
-    if (!aborted) {
+    if (!aborted && a.rope) {
+      if (own > 0) rope_epilogue(a, csum, blockIdx.y, kTC, kThreads);  // rank 0: the whole tile
+    } else if (!aborted) {
       const int tile = blockIdx.y;
       for (int cc = own_lo + threadIdx.x; cc < own_lo + own; cc += kThreads) {
         float v = 0.f;
@@ -720,10 +800,11 @@ size_t w4_gemv_mma_scratch_bytes(const SgMatMulParams* p, int sms, bool* applica
 
 // Runs the tensor-core GEMV if it applies; *handled tells the caller.
 SgStatus w4_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, void* ws, size_t ws_bytes,
-                         int* err_word, bool* handled) {
+                         int* err_word, bool* handled, const SgRopeAppend* rope) {
   *handled = false;
   const MPlan pl = make_mplan(p, sms);
   if (!pl.ok) return SG_OK;
+  if (rope && !pl.cluster) return SG_OK;  // the fused epilogue needs the cluster split
   *handled = true;
   SG_CHECK_ARG(pl.ws_bytes == 0 || (ws != nullptr && ws_bytes >= pl.ws_bytes && aligned16(ws)),
                "sg_matmul_int4_grouped: workspace too small (%zu < %zu bytes)", ws_bytes, pl.ws_bytes);
@@ -785,6 +866,25 @@ SgStatus w4_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, void
   a.norm_w = p->norm_weight;
   a.norm_eps = p->norm_eps;
   a.accum = (p->flags & SG_MM_C_ACCUMULATE) ? 1 : 0;
+  if (rope) {
+    a.rope = 1;
+    a.r_heads = rope->heads;
+    a.r_kv = rope->kv_heads;
+    a.r_dim = rope->head_dim;
+    a.r_pos = rope->positions;
+    a.r_pos0 = rope->pos0;
+    a.r_base = rope->base;
+    a.r_q = rope->q_out;
+    a.r_k = rope->k_cache;
+    a.r_v = rope->v_cache;
+    a.r_kv_hs = rope->kv_head_stride;
+    if (const SgKvPages* pg = rope->kv_pages) {
+      a.r_pt = pg->table;
+      a.r_pt_ps = pg->table_page_stride;
+      a.r_page_stride = pg->page_stride;
+      a.r_npages = pg->num_pages;
+    }
+  }
   a.tickets = static_cast<unsigned*>(ws);
   a.slots = reinterpret_cast<float*>(static_cast<char*>(ws) + pl.tickets_bytes);
   a.err = err_word;

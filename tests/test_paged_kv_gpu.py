@@ -241,3 +241,58 @@ def test_long_context_graph_pages_by_default(sg, tmp_path):
     with sdk.Package(_package(tmp_path, 4096)) as pkg:
         with pkg.select().session() as s:
             assert s.kv_pages is None
+
+
+@pytest.mark.parametrize("paged", [False, True], ids=["flat", "paged"])
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("H,Hkv,D,K", [(32, 8, 64, 2048), (28, 4, 128, 3584)])
+def test_qkv_gemv_rope_append_equals_two_calls(sg, oracle_mod, dt, H, Hkv, D, K, paged):
+    """sg_qkv_gemv_rope_append (the q|k|v GEMV with the rope and the KV append
+    in its epilogue) writes the same q and cache rows, bit for bit, as the GEMV
+    followed by sg_qkv_rope_append."""
+    from silicongraph_b200 import _lib
+    from silicongraph_b200._lib import SgKvPages
+    lib = _lib.load()
+    lib.sg_qkv_gemv_rope_append.restype = ctypes.c_int32
+    N, gs, pos = (H + 2 * Hkv) * D, 32, 37
+    rng = np.random.default_rng(H + D)
+    W = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+    B, S, Z = (torch.from_numpy(a).cuda() for a in oracle_mod.quantize_int4_grouped(W, gs))
+    x = torch.randn(1, K, device="cuda").to(dt)
+    st = torch.cuda.current_stream().cuda_stream
+    code = 2 if dt == torch.float16 else 3
+    # two calls: GEMV, then rope + append into a flat cache of 64 positions
+    qkv = sg.matmul_int4_grouped(x, B, S, Z, K, N, gs, out_dtype=dt)
+    q_want = torch.empty(H, D, dtype=dt, device="cuda")
+    Kw = torch.zeros(1, Hkv, 64, D, dtype=dt, device="cuda")
+    Vw = torch.zeros_like(Kw)
+    _lib.check(lib.sg_qkv_rope_append_batched(qkv.data_ptr(), 1, 1, H, Hkv, D, None, pos, 500000.0,
+                                              q_want.data_ptr(), Kw.data_ptr(), Vw.data_ptr(), 64 * D, Hkv * 64 * D,
+                                              code, st))
+
+    class SgRopeAppend(ctypes.Structure):
+        _fields_ = [("heads", ctypes.c_int32), ("kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                    ("positions", ctypes.c_void_p), ("pos0", ctypes.c_int32), ("base", ctypes.c_float),
+                    ("q_out", ctypes.c_void_p), ("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p),
+                    ("kv_head_stride", ctypes.c_int64), ("kv_pages", ctypes.POINTER(SgKvPages))]
+
+    q_got = torch.empty_like(q_want)
+    r = SgRopeAppend(heads=H, kv_heads=Hkv, head_dim=D, positions=None, pos0=pos, base=500000.0,
+                     q_out=q_got.data_ptr())
+    pos_dev = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    r.positions = pos_dev.data_ptr()                      # the position read on the device
+    if paged:
+        pool = Pool(torch.zeros_like(Kw), torch.zeros_like(Vw), seed=3)
+        r.k_cache, r.v_cache = pool.k0.data_ptr(), pool.v0.data_ptr()
+        r.kv_pages = ctypes.pointer(pool.desc)
+    else:
+        Kg, Vg = torch.zeros_like(Kw), torch.zeros_like(Vw)
+        r.k_cache, r.v_cache, r.kv_head_stride = Kg.data_ptr(), Vg.data_ptr(), 64 * D
+    C = torch.empty_like(qkv)
+    p = sg.matmul_params(x, B, C, M=1, K=K, N=N, scales=S, zeros=Z, group_size=gs)
+    _lib.check(lib.sg_qkv_gemv_rope_append(ctypes.byref(p), ctypes.byref(r), st))
+    torch.cuda.synchronize()
+    if paged:
+        Kg, Vg = pool.to_flat(1, 64)
+    assert torch.equal(q_got, q_want)
+    assert torch.equal(Kg[:, :, pos], Kw[:, :, pos]) and torch.equal(Vg[:, :, pos], Vw[:, :, pos])

@@ -176,15 +176,17 @@ def test_select_graph_refuses_before_allocation(sg, tmp_path):
 
 def test_fused_norm_decode_equals_unfused(sg, tmp_path):
     """One-row decode steps with the norms and residual adds fused into the
-    projections give the same tokens and logits, bit for bit, as the steps
-    with separate norm kernels (sdk.fuse_norm 0)."""
+    projections (and the rope + KV append into the q|k|v projection) give the
+    same tokens and logits, bit for bit, as the steps with separate kernels
+    (sdk.fuse_norm / sdk.fuse_rope 0)."""
     from silicongraph_b200 import sdk
     path, _ = _package(tmp_path, 128)
     prompt = (np.arange(33, dtype=np.int32) * 11) % SMALL["vocab_size"]
     runs = []
     try:
-        for fuse in (1, 0):
+        for fuse, rope in ((1, 1), (1, 0), (0, 0)):
             sg.set_tuning("sdk.fuse_norm", fuse)
+            sg.set_tuning("sdk.fuse_rope", rope)
             with sdk.Package(path) as pkg:
                 with pkg.select().session() as s:
                     s.prefill(prompt)
@@ -195,5 +197,7 @@ def test_fused_norm_decode_equals_unfused(sg, tmp_path):
             runs.append((toks, np.stack(logits)))
     finally:
         sg.set_tuning("sdk.fuse_norm", 1)
-    assert runs[0][0] == runs[1][0]
-    assert np.array_equal(runs[0][1], runs[1][1])
+        sg.set_tuning("sdk.fuse_rope", 1)
+    for other in runs[1:]:
+        assert runs[0][0] == other[0]
+        assert np.array_equal(runs[0][1], other[1])
