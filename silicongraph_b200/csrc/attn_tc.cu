@@ -71,6 +71,11 @@ struct TArgs {
   int64_t pt_bs, pt_ps;
   int npages;
   int paged_k, paged_v;
+  // fp32 I/O: Q / K / V were copied to fp16 scaled by powers of two; dscale[0]
+  // undoes the Q and K scales on the scores, dscale[1] the V scale on O, which
+  // is written as fp32
+  int o_f32;
+  const float* dscale;
 };
 constexpr int kPageRows = 16;                // keys per page
 constexpr int kPagesPerTile = kKT / kPageRows;
@@ -296,6 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax + epilogue
+    const float scale_log2 = a.dscale ? a.scale_log2 * a.dscale[0] : a.scale_log2;
     const int r = warp * 32 + lane;  // query row in the tile = TMEM lane
     const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
     const int q = q0 + r;
@@ -328,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float mx = -INFINITY;
 #pragma unroll
       for (int i = 0; i < kKT; i += 2) mx = fmax3(mx, __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
-      mx *= a.scale_log2;
+      mx *= scale_log2;
       float alpha = 1.f;
       const bool rescale = mx > m + kRescaleThreshold;
       if (rescale) {
@@ -341,8 +347,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t pk[kKT / 2];
 #pragma unroll
       for (int i = 0; i < kKT / 2; ++i) {
-        const float p0 = ex2(fmaf(__uint_as_float(sr[2 * i]), a.scale_log2, neg_m));
-        const float p1 = ex2(fmaf(__uint_as_float(sr[2 * i + 1]), a.scale_log2, neg_m));
+        const float p0 = ex2(fmaf(__uint_as_float(sr[2 * i]), scale_log2, neg_m));
+        const float p1 = ex2(fmaf(__uint_as_float(sr[2 * i + 1]), scale_log2, neg_m));
         pk[i] = pack2<false>(p0, p1);
         sum += sum2<false>(pk[i]);  // l sums the rounded weights that PV multiplies
       }
@@ -378,11 +384,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float inv_l = 1.f / l;
       typedef typename std::conditional<BF16, __nv_bfloat16, __half>::type T;
       T* orow = static_cast<T*>(a.O) + ((size_t)hb * a.Sq + q) * D;
+      float* orow32 = static_cast<float*>(a.O) + ((size_t)hb * a.Sq + q) * D;
+      const float omul = a.dscale ? inv_l * a.dscale[1] : inv_l;
 #pragma unroll 1
       for (int dc = 0; dc < D / 32; ++dc) {
         uint32_t o[32];
         tmem_ld_32x32b_x32(tbase + lane_addr + kOCol + dc * 32, o);
         tmem_ld_wait();
+        if (a.o_f32) {  // (l sums the fp16 weights: the normalisation is that of the 16-bit path)
+          if (q < a.Sq) {
+            float4* dst = reinterpret_cast<float4*>(orow32 + dc * 32);
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              dst[v] = make_float4(__uint_as_float(o[4 * v]) * omul, __uint_as_float(o[4 * v + 1]) * omul,
+                                   __uint_as_float(o[4 * v + 2]) * omul, __uint_as_float(o[4 * v + 3]) * omul);
+          }
+          continue;
+        }
         uint32_t pkd[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i)
@@ -442,6 +460,47 @@ __global__ void v_to_f16_kernel(const __nv_bfloat16* V, int64_t kv_bs, int64_t k
   }
 }
 
+// fp32 I/O: the largest |x| of Q, K and V (as float bits, atomicMax on
+// non-negative floats orders like the values), then fp16 copies scaled by
+// 2^(14 - e), e the exponent of that largest value, so every value fits fp16
+// with the largest in [2^14, 2^15); dscale = {2^-(sq + sk), 2^-sv} undoes them.
+__global__ void absmax3_kernel(const float* q, int64_t nq, const float* k, int64_t nk, const float* v, int64_t nv,
+                               unsigned* amax) {
+  unsigned m[3] = {0u, 0u, 0u};
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nq; i += stride)
+    m[0] = max(m[0], __float_as_uint(fabsf(q[i])));
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nk; i += stride)
+    m[1] = max(m[1], __float_as_uint(fabsf(k[i])));
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += stride)
+    m[2] = max(m[2], __float_as_uint(fabsf(v[i])));
+#pragma unroll
+  for (int t = 0; t < 3; ++t) {
+    for (int o = 16; o; o >>= 1) m[t] = max(m[t], __shfl_xor_sync(0xffffffffu, m[t], o));
+    if ((threadIdx.x & 31) == 0) atomicMax(&amax[t], m[t]);
+  }
+}
+
+__device__ __forceinline__ int scale_shift(unsigned amax_bits) {
+  const int e = (int)(amax_bits >> 23) - 127;  // exponent of the largest |x| (denormals and 0: -127)
+  return min(14 - max(e, -100), 120);          // power-of-two multiplier, kept inside fp32's range
+}
+
+__global__ void f32_to_f16_scaled_kernel(const float* q, int64_t nq, const float* k, int64_t nk, const float* v,
+                                         int64_t nv, const unsigned* amax, __half* q16, __half* k16, __half* v16,
+                                         float* dscale) {
+  const int sq = scale_shift(amax[0]), sk = scale_shift(amax[1]), sv = scale_shift(amax[2]);
+  const float fq = ldexpf(1.f, sq), fk = ldexpf(1.f, sk), fv = ldexpf(1.f, sv);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    dscale[0] = ldexpf(1.f, -(sq + sk));
+    dscale[1] = ldexpf(1.f, -sv);
+  }
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nq; i += stride) q16[i] = __float2half_rn(q[i] * fq);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nk; i += stride) k16[i] = __float2half_rn(k[i] * fk);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += stride) v16[i] = __float2half_rn(v[i] * fv);
+}
+
 template <int D, bool BF16>
 SgStatus launch_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const TArgs& a, int grid,
                    cudaStream_t cs) {
@@ -495,7 +554,14 @@ bool tc_qualifies(const SgFlashAttentionParams* p) {
   if (!g_tune_attn_tc.load() || p->q_pos_device) return false;
   const int io = p->io_dtype == SG_DT_DEFAULT ? SG_DT_F16 : p->io_dtype;
   const int D = p->head_dim;
-  if ((io != SG_DT_F16 && io != SG_DT_BF16) || (D != 64 && D != 128)) return false;
+  if ((io != SG_DT_F16 && io != SG_DT_BF16 && io != SG_DT_F32) || (D != 64 && D != 128)) return false;
+  if (io == SG_DT_F32) {  // copied to fp16 first: dense K / V only
+    const int Skv0 = p->S_kv > 0 ? p->S_kv : p->S;
+    const int64_t dense_hs = (int64_t)Skv0 * D, dense_bs = (int64_t)std::max(1, p->num_kv_heads) * dense_hs;
+    if (p->kv_pages || (p->kv_head_stride > 0 && p->kv_head_stride != dense_hs) ||
+        (p->kv_batch_stride > 0 && p->kv_batch_stride != dense_bs))
+      return false;
+  }
   if (p->S < g_tune_attn_min_s.load()) return false;
   const int Hkv = std::max(1, p->num_kv_heads);
   const int Skv = p->S_kv > 0 ? p->S_kv : p->S;
@@ -512,17 +578,88 @@ bool tc_qualifies(const SgFlashAttentionParams* p) {
 }
 }  // namespace
 
-// Scratch of the tensor-core path: the fp16 copy of a bf16 V.
+// fp32 I/O scratch: the three absolute maxima and two scales (256 bytes), then
+// the scaled fp16 copies of Q, K and V.
+size_t f32_scratch_parts(const SgFlashAttentionParams* p, size_t* nq, size_t* nk) {
+  const int Skv = p->S_kv > 0 ? p->S_kv : p->S;
+  *nq = (size_t)p->B * p->num_heads * p->S * p->head_dim;
+  *nk = (size_t)p->B * std::max(1, p->num_kv_heads) * Skv * p->head_dim;
+  return 256 + align_up(*nq * 2, 256) + 2 * align_up(*nk * 2, 256);
+}
+
+// Scratch of the tensor-core path: the fp16 copy of a bf16 V, or the fp16
+// copies of fp32 inputs.
 size_t attn_tc_scratch_bytes(const SgFlashAttentionParams* p) {
   if (!tc_qualifies(p)) return 0;
   const int io = p->io_dtype == SG_DT_DEFAULT ? SG_DT_F16 : p->io_dtype;
+  if (io == SG_DT_F32) {
+    size_t nq, nk;
+    return f32_scratch_parts(p, &nq, &nk);
+  }
   if (io != SG_DT_BF16) return 0;
   const int Skv = p->S_kv > 0 ? p->S_kv : p->S;
   return align_up((size_t)p->B * std::max(1, p->num_kv_heads) * Skv * p->head_dim * 2, 256);
 }
 
+SgStatus attn_tc_run16(const SgFlashAttentionParams* p, cudaStream_t cs, void* ws, size_t ws_bytes, bool ws_external,
+                       bool* handled, const float* dscale, bool o_f32);
+
+// fp32 I/O: Q / K / V copied to fp16 with per-tensor power-of-two scales
+// (exact; every value fits fp16 with 11 significant bits, the precision of the
+// tensor cores' 16-bit operands), the fp16 kernel run on the copies with the
+// scales undone on the scores and on O, and O written as fp32.
 SgStatus attn_tc_run(const SgFlashAttentionParams* p, cudaStream_t cs, void* ws, size_t ws_bytes, bool ws_external,
                      bool* handled) {
+  *handled = false;
+  if (!tc_qualifies(p)) return SG_OK;
+  const int io = p->io_dtype == SG_DT_DEFAULT ? SG_DT_F16 : p->io_dtype;
+  if (io != SG_DT_F32) return attn_tc_run16(p, cs, ws, ws_bytes, ws_external, handled, nullptr, false);
+  size_t nq, nk;
+  const size_t need = f32_scratch_parts(p, &nq, &nk);
+  SgStatus st;
+  if (ws == nullptr) {
+    if (ws_external) {
+      set_error("sg_flash_attention: scratch required (%zu bytes)", need);
+      return SG_ERR_INVALID;
+    }
+    st = library_workspace(cs, need, &ws, kWsAttention);
+    if (st != SG_OK) return st;
+  } else {
+    SG_CHECK_ARG(ws_bytes >= need && aligned16(ws), "sg_flash_attention: workspace too small (%zu < %zu bytes)",
+                 ws_bytes, need);
+  }
+  char* w = static_cast<char*>(ws);
+  unsigned* amax = reinterpret_cast<unsigned*>(w);
+  float* dscale = reinterpret_cast<float*>(w + 16);
+  __half* q16 = reinterpret_cast<__half*>(w + 256);
+  __half* k16 = reinterpret_cast<__half*>(w + 256 + align_up(nq * 2, 256));
+  __half* v16 = reinterpret_cast<__half*>(w + 256 + align_up(nq * 2, 256) + align_up(nk * 2, 256));
+  SG_CUDA_TRY(cudaMemsetAsync(amax, 0, 16, cs));
+  const int blocks = (int)std::min<size_t>((nq + nk * 2 + 255) / 256, 148 * 8);
+  absmax3_kernel<<<blocks, 256, 0, cs>>>(static_cast<const float*>(p->Q), (int64_t)nq,
+                                         static_cast<const float*>(p->K), (int64_t)nk,
+                                         static_cast<const float*>(p->V), (int64_t)nk, amax);
+  st = check_launch("absmax3_kernel");
+  if (st != SG_OK) return st;
+  f32_to_f16_scaled_kernel<<<blocks, 256, 0, cs>>>(static_cast<const float*>(p->Q), (int64_t)nq,
+                                                   static_cast<const float*>(p->K), (int64_t)nk,
+                                                   static_cast<const float*>(p->V), (int64_t)nk, amax, q16, k16, v16,
+                                                   dscale);
+  st = check_launch("f32_to_f16_scaled_kernel");
+  if (st != SG_OK) return st;
+  SgFlashAttentionParams c = *p;
+  c.Q = q16;
+  c.K = k16;
+  c.V = v16;
+  c.io_dtype = SG_DT_F16;
+  const int Skv = p->S_kv > 0 ? p->S_kv : p->S;
+  c.kv_head_stride = (int64_t)Skv * p->head_dim;
+  c.kv_batch_stride = (int64_t)std::max(1, p->num_kv_heads) * c.kv_head_stride;
+  return attn_tc_run16(&c, cs, nullptr, 0, true, handled, dscale, true);
+}
+
+SgStatus attn_tc_run16(const SgFlashAttentionParams* p, cudaStream_t cs, void* ws, size_t ws_bytes, bool ws_external,
+                       bool* handled, const float* dscale, bool o_f32) {
   *handled = false;
   if (!tc_qualifies(p)) return SG_OK;
   const int io = p->io_dtype == SG_DT_DEFAULT ? SG_DT_F16 : p->io_dtype;
@@ -614,6 +751,8 @@ SgStatus attn_tc_run(const SgFlashAttentionParams* p, cudaStream_t cs, void* ws,
   a.q_pos0 = p->q_pos0 >= 0 ? p->q_pos0 : Skv - p->S;
   a.n_qt = (p->S + kQT - 1) / kQT;
   a.err = err;
+  a.o_f32 = o_f32 ? 1 : 0;
+  a.dscale = dscale;
   if (pages) {
     a.pt = pages->table;
     a.pt_bs = pages->table_batch_stride;

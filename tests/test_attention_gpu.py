@@ -197,3 +197,26 @@ def test_decode_warp_split_bf16(sg, oracle_mod, D, H, Hkv):
     finally:
         sg.set_tuning("attn.decode_kernel", 4)
     close(got.float().cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("qs,ks,vs", [(1.0, 1.0, 1.0), (300.0, 1e-3, 1e5), (1e-20, 1e20, 1e-30)],
+                         ids=["unit", "beyond-fp16-range", "extreme-exponents"])
+def test_f32_attention_on_tensor_cores(sg, oracle_mod, qs, ks, vs):
+    """fp32 I/O at the config-1 shape [1, 32, 512, 64] runs on the tcgen05
+    kernel through fp16 copies scaled per tensor by powers of two (exact), so
+    values far outside fp16's range give the same result as the fp32 oracle
+    within the bar; compared with the CUDA-core fp32 path as well."""
+    B, H, S, D = 1, 32, 512, 64
+    rng = np.random.default_rng(int(qs * 7) % 1000 + 3)
+    q = (rng.standard_normal((B, H, S, D)) * qs).astype(np.float32)
+    k = (rng.standard_normal((B, H, S, D)) * ks).astype(np.float32)
+    v = (rng.standard_normal((B, H, S, D)) * vs).astype(np.float32)
+    want = oracle_mod.flash_attention(q, k, v, causal=True)
+    got = sg.flash_attention(dev(q), dev(k), dev(v), causal=True).cpu().numpy()
+    close(got / vs, want / vs)
+    sg.set_tuning("attn_tc.enable", 0)
+    try:
+        cc = sg.flash_attention(dev(q), dev(k), dev(v), causal=True).cpu().numpy()
+    finally:
+        sg.set_tuning("attn_tc.enable", 1)
+    close(got / vs, cc / vs)
