@@ -777,7 +777,8 @@ def run_attention(args):
         "e2e": {"value": round(world * e2e_steps * flops / (e2e_ms / 1e3) / 1e12, 3), "unit": "TFLOP/s",
                 "steps": e2e_steps, "h2d_bytes_per_step": int((hq.numel() + hk.numel() + hv.numel()) * esz),
                 "d2h_bytes_per_step": int(ho.numel() * esz)},
-        "gpu_launches": args.steps * (2 if dts == "bf16" else 1),
+        # bf16: V to fp16 + attention; f32: absolute maxima + scaled fp16 copies + attention
+        "gpu_launches": args.steps * {"bf16": 2, "f32": 3}.get(dts, 1),
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
