@@ -103,7 +103,9 @@ ArmSession* sg_session_create_ex(ArmGraph* graph, const ArmSessionOptions* opts,
  * rank has left (a store, a heartbeat) calls sg_session_abort before the next
  * step, so nothing is launched towards the departed rank.  An aborted
  * session refuses every later prefill / decode with ARMCC_ERR_RUNTIME and
- * the reason, and can still be destroyed.  This mirrors the reference
+ * the reason, and can still be destroyed; after a failure in flight the
+ * destructor waits at most 10 s for the session's stream and otherwise
+ * leaves its device memory allocated (end the process).  This mirrors the reference
  * runtime's refusal with a reason (compiler/lib/runtime/
  * resource_controller.cpp:195-247); the reference itself has no multi-device
  * group. */

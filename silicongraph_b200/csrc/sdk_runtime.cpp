@@ -444,6 +444,17 @@ struct ArmSession_ {
   int tp_timeout_ms = 60000;
 
   ~ArmSession_() {
+    if (aborted && st) {
+      // a group that failed in flight: wait a bounded time for the stream; if
+      // it does not drain, leak the session's device memory rather than block
+      // or free memory a kernel may still use (the process should end)
+      const auto t0 = std::chrono::steady_clock::now();
+      while (cudaStreamQuery(st) == cudaErrorNotReady) {
+        if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(10)) return;
+        std::this_thread::sleep_for(std::chrono::milliseconds(1));
+      }
+      cudaGetLastError();
+    }
     if (st) cudaStreamSynchronize(st);
     if (graph_exec) cudaGraphExecDestroy(graph_exec);
     if (graph) cudaGraphDestroy(graph);
@@ -864,7 +875,10 @@ void release_pages(ArmSession_* S) {
 // mapped regions are closed.  Every later call is refused with `why`; this
 // mirrors the reference runtime's clean refusal with a reason
 // (compiler/lib/runtime/resource_controller.cpp:195-247).
-void abort_session(ArmSession_* S, const std::string& why) {
+// in_flight: a step may still be running on the stream (a collective that did
+// not complete); then nothing here waits for it and the peers' mappings stay
+// open until the stream drains (the destructor's bounded wait).
+void abort_session(ArmSession_* S, const std::string& why, bool in_flight) {
   if (S->aborted) return;
   S->aborted = true;
   S->abort_why = why;
@@ -872,6 +886,7 @@ void abort_session(ArmSession_* S, const std::string& why) {
     if (nccl_api().comm_abort) nccl_api().comm_abort(S->comm);
     S->comm = nullptr;  // aborted: not destroyed again
   }
+  if (in_flight) return;
   cudaStreamSynchronize(S->st);
   cudaGetLastError();
   for (size_t q = 0; q < S->ar_regions.size(); ++q)
@@ -904,7 +919,7 @@ ArmStatus wait_stream(ArmSession_* S, const char* fn) {
     if (nccl_api().comm_get_async_error && nccl_api().comm_get_async_error(S->comm, &ae) == ncclSuccess &&
         ae != ncclSuccess && ae != ncclInProgress) {
       const std::string why = std::string("NCCL reported an asynchronous error: ") + nccl_api().error_string(ae);
-      abort_session(S, why);
+      abort_session(S, why, true);
       set_err("%s: %s; the tensor-parallel group was aborted", fn, why.c_str());
       return ARMCC_ERR_RUNTIME;
     }
@@ -913,7 +928,7 @@ ArmStatus wait_stream(ArmSession_* S, const char* fn) {
       char buf[160];
       snprintf(buf, sizeof buf, "a step did not complete within %d ms (a rank stopped answering)",
                S->tp_timeout_ms);
-      abort_session(S, buf);
+      abort_session(S, buf, true);
       set_err("%s: %s; the tensor-parallel group was aborted", fn, buf);
       return ARMCC_ERR_RUNTIME;
     }
@@ -2036,7 +2051,7 @@ ArmStatus sg_session_abort(ArmSession* sess, const char* reason) {
     return ARMCC_ERR_RUNTIME;
   }
   cudaSetDevice(sess->dev);
-  abort_session(sess, reason && *reason ? reason : "aborted by the caller");
+  abort_session(sess, reason && *reason ? reason : "aborted by the caller", false);
   return ARMCC_OK;
 }
 

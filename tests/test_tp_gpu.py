@@ -96,19 +96,16 @@ def test_tp_session_matches_decoder_oracle(sg, oracle_mod, tmp_path, world, batc
 
 
 # ------------------------------------------------------------------ failure handling on two GPUs
-def _leave_worker(rank, world, uid, path, mode, out_dir):
-    """mode "announce": after two steps rank 1 announces on the host (a marker
-    file) that it leaves; rank 0 learns it before its next launch, aborts its
-    session and gets a clean refusal.  mode "silent" (NCCL only, no peer
-    memory): rank 1 stops calling after two steps but stays alive; rank 0's
-    next step waits on NCCL, its watchdog aborts the group after
-    SG_TP_TIMEOUT_MS and the call returns an error.  Both ranks then leave in
-    order (markers), so no rank frees memory the other still maps."""
+def _leave_worker(rank, world, uid, path, out_dir):
+    """After two steps rank 1 announces on the host (a marker file) that it
+    leaves; rank 0 learns it before its next launch, aborts its session and
+    gets a clean refusal.  Both ranks then leave in order (markers), so no rank
+    frees memory the other still maps, and no collective is in flight when a
+    rank goes."""
     import time
     os.environ["SG_DEVICE"] = str(rank)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
-    os.environ["SG_TP_P2P"] = "0" if mode == "silent" else "1"
-    os.environ["SG_TP_TIMEOUT_MS"] = "3000"
+    os.environ["SG_TP_P2P"] = "1"
     torch.cuda.set_device(rank)
     from silicongraph_b200 import sdk
     marker = lambda name: os.path.join(out_dir, name)  # noqa: E731
@@ -132,9 +129,8 @@ def _leave_worker(rank, world, uid, path, mode, out_dir):
                 s.abort("leaving")
             else:
                 t0 = time.time()
-                if mode == "announce":
-                    wait_for("leaving")           # learned on the host, before the next launch
-                    s.abort("rank 1 left")
+                wait_for("leaving")               # learned on the host, before the next launch
+                s.abort("rank 1 left")
                 try:
                     s.decode()
                     result["status"] = 0
@@ -148,18 +144,14 @@ def _leave_worker(rank, world, uid, path, mode, out_dir):
     np.save(os.path.join(out_dir, f"leave{rank}.npy"), np.array([result], dtype=object), allow_pickle=True)
 
 
-@pytest.mark.parametrize("mode", ["announce", "silent"])
-def test_tp_rank_leaving_between_steps(sg, tmp_path, mode):
+def test_tp_rank_leaving_between_steps(sg, tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     from silicongraph_b200 import sdk
     t = armpack.cuda_tensors(SMALL, armpack.random_llama_weights(SMALL, seed=4), group_size=32)
     path = armpack.write_package(str(tmp_path / "tp.armpack"), SMALL, t, max_context=256, max_prefill_chunk=64)
-    mp.start_processes(_leave_worker, args=(2, sdk.tp_unique_id(), path, mode, str(tmp_path)), nprocs=2,
+    mp.start_processes(_leave_worker, args=(2, sdk.tp_unique_id(), path, str(tmp_path)), nprocs=2,
                        join=True, start_method="spawn")
     r0 = np.load(tmp_path / "leave0.npy", allow_pickle=True)[0]
     assert r0["status"] == -5, r0
-    if mode == "announce":
-        assert "rank 1 left" in r0["msg"] and r0["seconds"] < 10
-    else:
-        assert "did not complete within 3000 ms" in r0["msg"] and r0["seconds"] < 30
+    assert "rank 1 left" in r0["msg"] and r0["seconds"] < 10
