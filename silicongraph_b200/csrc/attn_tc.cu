@@ -464,20 +464,34 @@ __global__ void v_to_f16_kernel(const __nv_bfloat16* V, int64_t kv_bs, int64_t k
 // non-negative floats orders like the values), then fp16 copies scaled by
 // 2^(14 - e), e the exponent of that largest value, so every value fits fp16
 // with the largest in [2^14, 2^15); dscale = {2^-(sq + sk), 2^-sv} undoes them.
-__global__ void absmax3_kernel(const float* q, int64_t nq, const float* k, int64_t nk, const float* v, int64_t nv,
-                               unsigned* amax) {
+__global__ void __launch_bounds__(256) absmax3_kernel(const float* q, int64_t nq, const float* k, int64_t nk,
+                                                       const float* v, int64_t nv, unsigned* amax) {
+  // 16-byte loads (the tensors are 16-byte aligned; n % 4 tails scalar), a
+  // block reduction in shared memory, then one atomic per block and tensor
+  __shared__ unsigned red[3][8];
   unsigned m[3] = {0u, 0u, 0u};
+  const float* src[3] = {q, k, v};
+  const int64_t n[3] = {nq, nk, nv};
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nq; i += stride)
-    m[0] = max(m[0], __float_as_uint(fabsf(q[i])));
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nk; i += stride)
-    m[1] = max(m[1], __float_as_uint(fabsf(k[i])));
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += stride)
-    m[2] = max(m[2], __float_as_uint(fabsf(v[i])));
 #pragma unroll
   for (int t = 0; t < 3; ++t) {
+    const float4* s4 = reinterpret_cast<const float4*>(src[t]);
+    const int64_t n4 = n[t] / 4;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+      const float4 x = __ldg(s4 + i);
+      m[t] = max(m[t], max(max(__float_as_uint(fabsf(x.x)), __float_as_uint(fabsf(x.y))),
+                           max(__float_as_uint(fabsf(x.z)), __float_as_uint(fabsf(x.w)))));
+    }
+    for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n[t]; i += stride)
+      m[t] = max(m[t], __float_as_uint(fabsf(src[t][i])));
     for (int o = 16; o; o >>= 1) m[t] = max(m[t], __shfl_xor_sync(0xffffffffu, m[t], o));
-    if ((threadIdx.x & 31) == 0) atomicMax(&amax[t], m[t]);
+    if ((threadIdx.x & 31) == 0) red[t][threadIdx.x >> 5] = m[t];
+  }
+  __syncthreads();
+  if (threadIdx.x < 3) {
+    unsigned b = 0u;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) b = max(b, red[threadIdx.x][w]);
+    atomicMax(&amax[threadIdx.x], b);
   }
 }
 
@@ -486,19 +500,33 @@ __device__ __forceinline__ int scale_shift(unsigned amax_bits) {
   return min(14 - max(e, -100), 120);          // power-of-two multiplier, kept inside fp32's range
 }
 
-__global__ void f32_to_f16_scaled_kernel(const float* q, int64_t nq, const float* k, int64_t nk, const float* v,
-                                         int64_t nv, const unsigned* amax, __half* q16, __half* k16, __half* v16,
-                                         float* dscale) {
+__global__ void __launch_bounds__(256) f32_to_f16_scaled_kernel(const float* q, int64_t nq, const float* k,
+                                                                 int64_t nk, const float* v, int64_t nv,
+                                                                 const unsigned* amax, __half* q16, __half* k16,
+                                                                 __half* v16, float* dscale) {
   const int sq = scale_shift(amax[0]), sk = scale_shift(amax[1]), sv = scale_shift(amax[2]);
-  const float fq = ldexpf(1.f, sq), fk = ldexpf(1.f, sk), fv = ldexpf(1.f, sv);
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     dscale[0] = ldexpf(1.f, -(sq + sk));
     dscale[1] = ldexpf(1.f, -sv);
   }
+  const float* src[3] = {q, k, v};
+  __half* dst[3] = {q16, k16, v16};
+  const int64_t n[3] = {nq, nk, nv};
+  const float f[3] = {ldexpf(1.f, sq), ldexpf(1.f, sk), ldexpf(1.f, sv)};
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nq; i += stride) q16[i] = __float2half_rn(q[i] * fq);
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nk; i += stride) k16[i] = __float2half_rn(k[i] * fk);
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += stride) v16[i] = __float2half_rn(v[i] * fv);
+#pragma unroll
+  for (int t = 0; t < 3; ++t) {
+    const float4* s4 = reinterpret_cast<const float4*>(src[t]);
+    uint2* d4 = reinterpret_cast<uint2*>(dst[t]);  // 4 halves
+    const int64_t n4 = n[t] / 4;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+      const float4 x = __ldg(s4 + i);
+      __half2 lo = __floats2half2_rn(x.x * f[t], x.y * f[t]), hi = __floats2half2_rn(x.z * f[t], x.w * f[t]);
+      d4[i] = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+    }
+    for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n[t]; i += stride)
+      dst[t][i] = __float2half_rn(src[t][i] * f[t]);
+  }
 }
 
 template <int D, bool BF16>
@@ -635,7 +663,7 @@ SgStatus attn_tc_run(const SgFlashAttentionParams* p, cudaStream_t cs, void* ws,
   __half* k16 = reinterpret_cast<__half*>(w + 256 + align_up(nq * 2, 256));
   __half* v16 = reinterpret_cast<__half*>(w + 256 + align_up(nq * 2, 256) + align_up(nk * 2, 256));
   SG_CUDA_TRY(cudaMemsetAsync(amax, 0, 16, cs));
-  const int blocks = (int)std::min<size_t>((nq + nk * 2 + 255) / 256, 148 * 8);
+  const int blocks = (int)std::max<size_t>(1, std::min<size_t>((nq + nk * 2) / 1024, 148 * 4));
   absmax3_kernel<<<blocks, 256, 0, cs>>>(static_cast<const float*>(p->Q), (int64_t)nq,
                                          static_cast<const float*>(p->K), (int64_t)nk,
                                          static_cast<const float*>(p->V), (int64_t)nk, amax);
