@@ -416,6 +416,12 @@ SgStatus sg_tp_argmax_pick(const float* all3, int32_t world, int32_t rows, int32
 size_t sg_tp_allreduce_region_bytes(int32_t world, int32_t max_n);
 SgStatus sg_tp_allreduce_f16(void* data, int32_t n, int32_t rank, int32_t world, void* const* regions, int32_t max_n,
                              void* stream);
+/* The same sum, not written back to data: residual (fp16 [n]) becomes
+ * round(residual + round(sum)) -- the decoder's residual add after a
+ * row-parallel projection, fused (what sg_rmsnorm with a residual does to its
+ * residual).  No reference counterpart. */
+SgStatus sg_tp_allreduce_f16_residual(void* data, int32_t n, int32_t rank, int32_t world, void* const* regions,
+                                      int32_t max_n, void* residual, void* stream);
 
 /* in [heads, tokens, head_dim] -> out [tokens, heads, head_dim]. */
 SgStatus sg_head_transpose(const void* in, void* out, int32_t heads, int32_t tokens, int32_t head_dim,

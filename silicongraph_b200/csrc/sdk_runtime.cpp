@@ -593,7 +593,9 @@ ArmStatus forward(ArmSession_* S, int Ts, bool from_next, bool dev_pos = false) 
   const int H = c.hidden, D = c.head_dim;
   const int32_t* ids = from_next ? S->buf<int32_t>("next") : S->buf<int32_t>("ids");
   // one row on one GPU: norms and residual adds fused into the projections
-  const bool fuse = T == 1 && S->tp_world == 1 && S->norm_fusable && g_fuse_norm.load() != 0;
+  // (tensor-parallel: the peer all-reduce adds the row-parallel sums into the residual stream)
+  const bool tp_peer = S->tp_world > 1 && S->ar_region && H % 8 == 0 && H <= S->ar_max;
+  const bool fuse = T == 1 && (S->tp_world == 1 || tp_peer) && S->norm_fusable && g_fuse_norm.load() != 0;
   void* resid = S->buf<void>("resid");
   if (fuse) {
     // the residual stream starts as the embedding (round(x + 0) = x)
@@ -698,14 +700,31 @@ ArmStatus forward(ArmSession_* S, int Ts, bool from_next, bool dev_pos = false) 
       attn_rows = S->buf<void>("attn_t");
     }
     if (fuse) {
-      // resid += o; gate|up of the post-attention norm; resid += down(SwiGLU)
-      if ((r = linear(S, S->o[l], attn_rows, resid, T, SG_DT_F16, SG_MM_C_ACCUMULATE)) != ARMCC_OK) return r;
+      // resid += o; gate|up of the post-attention norm; resid += down(SwiGLU).  Tensor-parallel:
+      // the partial sums go through the peer all-reduce, which adds them into resid.
+      if (S->tp_world == 1) {
+        if ((r = linear(S, S->o[l], attn_rows, resid, T, SG_DT_F16, SG_MM_C_ACCUMULATE)) != ARMCC_OK) return r;
+      } else {
+        if ((r = linear(S, S->o[l], attn_rows, S->buf<void>("o"), T, SG_DT_F16)) != ARMCC_OK) return r;
+        SG_TRY(sg_tp_allreduce_f16_residual(S->buf<void>("o"), H, S->tp_rank, S->tp_world, S->ar_regions.data(),
+                                            S->ar_max, resid, st),
+               "peer all-reduce into the residual");
+      }
       if ((r = linear(S, S->gu[l], resid, S->buf<void>("gu"), T, SG_DT_F16, SG_MM_A_RMSNORM, S->post_norm[l])) !=
           ARMCC_OK)
         return r;
-      if ((r = swiglu_down(S, S->down[l], S->buf<void>("gu"), S->buf<void>("act"), resid, T, S->down[l].K,
-                           SG_MM_C_ACCUMULATE)) != ARMCC_OK)
-        return r;
+      if (S->tp_world == 1) {
+        if ((r = swiglu_down(S, S->down[l], S->buf<void>("gu"), S->buf<void>("act"), resid, T, S->down[l].K,
+                             SG_MM_C_ACCUMULATE)) != ARMCC_OK)
+          return r;
+      } else {
+        if ((r = swiglu_down(S, S->down[l], S->buf<void>("gu"), S->buf<void>("act"), S->buf<void>("down"), T,
+                             S->down[l].K)) != ARMCC_OK)
+          return r;
+        SG_TRY(sg_tp_allreduce_f16_residual(S->buf<void>("down"), H, S->tp_rank, S->tp_world, S->ar_regions.data(),
+                                            S->ar_max, resid, st),
+               "peer all-reduce into the residual");
+      }
       continue;
     }
     if ((r = linear(S, S->o[l], attn_rows, S->buf<void>("o"), T, SG_DT_F16)) != ARMCC_OK) return r;
@@ -1278,6 +1297,42 @@ void session_scratch(const ModelCfg& c, int batch, size_t* lws_out, size_t* aws_
   *aws_out = aws;
 }
 
+// The norms (and the rope + KV append) fuse into the projections when the
+// one-row kernel takes every shape of this session (its shards when
+// tensor-parallel).
+void decide_fusion(ArmSession_* S) {
+  const ModelCfg& c = S->c;
+  {
+    const int sms = sg::sm_count(S->dev);
+    bool ok = c.hidden % 8 == 0 && c.hidden <= 8192;
+    auto takes = [&](const Linear& L, int cdt) {
+      SgMatMulParams p{};
+      p.A = p.C = S->act;
+      p.B = L.qw;
+      p.scales_B = L.scales;
+      p.zeros_B = L.zeros;
+      p.M = 1;
+      p.K = L.K;
+      p.N = L.N;
+      p.group_size = c.group_size;
+      p.a_dtype = SG_DT_F16;
+      p.c_dtype = cdt;
+      bool applicable = false;
+      const size_t ws = sg::w4_gemv_mma_scratch_bytes(&p, sms, &applicable);
+      return applicable ? (ws == 0 ? 2 : 1) : 0;  // 2: a cluster split (no scratch)
+    };
+    bool cluster_qkv = c.head_dim == 64 || c.head_dim == 128;
+    for (int l = 0; ok && l < c.layers; ++l) {
+      const int q = takes(S->qkv[l], SG_DT_F16);
+      cluster_qkv = cluster_qkv && q == 2;
+      ok = q && takes(S->o[l], SG_DT_F16) && takes(S->gu[l], SG_DT_F16) && takes(S->down[l], SG_DT_F16);
+    }
+    if (ok && c.lm_int4) ok = takes(S->lm, SG_DT_F32) != 0;
+    S->norm_fusable = ok;
+    S->rope_fusable = ok && cluster_qkv;
+  }
+}
+
 ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int rank, int world, const uint8_t* id,
                            int batch, int kv_mode = 0, int64_t pool_tokens = 0) {
   const char* fn = world > 1 ? "sg_session_create_tp" : "armgraph_create_session";
@@ -1531,6 +1586,7 @@ ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int r
     if (cudaStreamSynchronize(S->st) != cudaSuccess) return cleanup_fail("cutting the weight shards failed");
     cudaFree(full);
     full = nullptr;
+    decide_fusion(S.get());
     return S.release();
   }
   if (cudaStreamSynchronize(S->st) != cudaSuccess) {
@@ -1567,36 +1623,7 @@ ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int r
     S->lm_f16 = t("lm_head.weight", (uint64_t)c.vocab * H2);
     if (!S->lm_f16) return cleanup_fail("lm_head.weight missing or of the wrong size");
   }
-  // the norms fuse into the projections when the one-row kernel takes every shape
-  {
-    const int sms = sg::sm_count(S->dev);
-    bool ok = c.hidden % 8 == 0 && c.hidden <= 8192;
-    auto takes = [&](const Linear& L, int cdt) {
-      SgMatMulParams p{};
-      p.A = p.C = S->act;
-      p.B = L.qw;
-      p.scales_B = L.scales;
-      p.zeros_B = L.zeros;
-      p.M = 1;
-      p.K = L.K;
-      p.N = L.N;
-      p.group_size = c.group_size;
-      p.a_dtype = SG_DT_F16;
-      p.c_dtype = cdt;
-      bool applicable = false;
-      const size_t ws = sg::w4_gemv_mma_scratch_bytes(&p, sms, &applicable);
-      return applicable ? (ws == 0 ? 2 : 1) : 0;  // 2: a cluster split (no scratch)
-    };
-    bool cluster_qkv = c.head_dim == 64 || c.head_dim == 128;
-    for (int l = 0; ok && l < c.layers; ++l) {
-      const int q = takes(S->qkv[l], SG_DT_F16);
-      cluster_qkv = cluster_qkv && q == 2;
-      ok = q && takes(S->o[l], SG_DT_F16) && takes(S->gu[l], SG_DT_F16) && takes(S->down[l], SG_DT_F16);
-    }
-    if (ok && c.lm_int4) ok = takes(S->lm, SG_DT_F32) != 0;
-    S->norm_fusable = ok;
-    S->rope_fusable = ok && cluster_qkv;
-  }
+  decide_fusion(S.get());
   return S.release();
 }
 

@@ -43,8 +43,12 @@ __device__ __forceinline__ uint32_t ld_flag(const uint32_t* p) {
   return v;
 }
 
+// residual != NULL: the sum is not written back to data; instead
+// residual = round(residual + round(sum)) (the decoder's residual add, as
+// sg_rmsnorm with a residual does it).
 __global__ void __launch_bounds__(kThreads) tp_allreduce_kernel(__half* __restrict__ data, int n, int rank, int world,
-                                                                Peers peers, int max_n, int* err, uint64_t wait_ns) {
+                                                                Peers peers, int max_n, int* err, uint64_t wait_ns,
+                                                                __half* __restrict__ residual) {
   sgd::pdl_wait();  // the partial comes from the previous kernel
   sgd::pdl_launch_dependents();
   uint8_t* mine = peers.region[rank];
@@ -105,7 +109,18 @@ __global__ void __launch_bounds__(kThreads) tp_allreduce_kernel(__half* __restri
       __half2* oh = reinterpret_cast<__half2*>(&o);
 #pragma unroll
       for (int i = 0; i < 4; ++i) oh[i] = __floats2half2_rn(acc[2 * i], acc[2 * i + 1]);
-      reinterpret_cast<uint4*>(data)[v] = o;
+      if (residual) {
+        uint4 r = reinterpret_cast<const uint4*>(residual)[v];
+        __half2* rh = reinterpret_cast<__half2*>(&r);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 a = __half22float2(oh[i]), b = __half22float2(rh[i]);
+          rh[i] = __floats2half2_rn(a.x + b.x, a.y + b.y);
+        }
+        reinterpret_cast<uint4*>(residual)[v] = r;
+      } else {
+        reinterpret_cast<uint4*>(data)[v] = o;
+      }
     }
   }
   // the epoch advances once every block has taken it (all blocks read it before any flag of this call)
@@ -144,8 +159,8 @@ size_t sg_tp_allreduce_region_bytes(int32_t world, int32_t max_n) {
   return sg::align_up((size_t)2 * world * n * sizeof(__half) + (size_t)world * kMaxBlocks * 4 + 8, 256);
 }
 
-SgStatus sg_tp_allreduce_f16(void* data, int32_t n, int32_t rank, int32_t world, void* const* regions, int32_t max_n,
-                             void* stream) {
+static SgStatus allreduce_run(void* data, int32_t n, int32_t rank, int32_t world, void* const* regions,
+                              int32_t max_n, void* residual, void* stream) {
   SG_CHECK_ARG(world >= 1 && world <= kMaxRanks, "sg_tp_allreduce_f16: world %d outside [1, %d]", world, kMaxRanks);
   SG_CHECK_ARG(rank >= 0 && rank < world, "sg_tp_allreduce_f16: rank %d outside the group", rank);
   SG_CHECK_ARG(n >= 0 && n <= max_n && max_n % kChunk == 0 && n % kChunk == 0,
@@ -164,8 +179,19 @@ SgStatus sg_tp_allreduce_f16(void* data, int32_t n, int32_t rank, int32_t world,
   const int blocks = std::max(1, std::min(kMaxBlocks, (nvec + 1023) / 1024));
   SG_CUDA_TRY(sgd::launch_pdl(tp_allreduce_kernel, dim3(blocks), dim3(kThreads), 0, static_cast<cudaStream_t>(stream),
                               static_cast<__half*>(data), (int)n, (int)rank, (int)world, pe, (int)max_n, err,
-                              (uint64_t)std::max(1, g_wait_ms.load()) * 1000000ull));
+                              (uint64_t)std::max(1, g_wait_ms.load()) * 1000000ull, static_cast<__half*>(residual)));
   return SG_OK;
+}
+
+SgStatus sg_tp_allreduce_f16(void* data, int32_t n, int32_t rank, int32_t world, void* const* regions, int32_t max_n,
+                             void* stream) {
+  return allreduce_run(data, n, rank, world, regions, max_n, nullptr, stream);
+}
+
+SgStatus sg_tp_allreduce_f16_residual(void* data, int32_t n, int32_t rank, int32_t world, void* const* regions,
+                                      int32_t max_n, void* residual, void* stream) {
+  SG_CHECK_ARG(residual && sg::aligned16(residual), "sg_tp_allreduce_f16_residual: residual NULL or unaligned");
+  return allreduce_run(data, n, rank, world, regions, max_n, residual, stream);
 }
 
 }  // extern "C"

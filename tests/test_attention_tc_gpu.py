@@ -102,3 +102,21 @@ def test_tc_attention_long_sequence(sg, oracle_mod, dtype):
     for row in (0, 1, 127, 128, 2047, 4095):
         want = _oracle(oracle_mod, np.ascontiguousarray(qo[:, :, row:row + 1]), ko, vo, io, True, row)
         close(got[:, :, row:row + 1], want)
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_tc_attention_config5_layer(sg, oracle_mod, dtype):
+    """The Qwen2.5-7B prefill layer of the configuration itself: 28 query / 4
+    KV heads (GQA 7), S = 8192, head_dim 128, causal.  Every head's rows at
+    sampled positions across all 64 query tiles (tile starts and ends, and
+    the last row) against the oracle, and every output finite."""
+    rng = np.random.default_rng(5)
+    B, H, Hkv, S, D = 1, 28, 4, 8192, 128
+    q, k, v = _qkv(rng, B, H, Hkv, S, S, D, dtype)
+    (qo, qt, io), (ko, kt, _), (vo, vt, _) = (_to(a, dtype, oracle_mod) for a in (q, k, v))
+    got = sg.flash_attention(qt, kt, vt, causal=True).float().cpu().numpy()
+    assert np.isfinite(got).all()
+    for row in (0, 127, 128, 1000, 4095, 4096, 6143, 8064, 8191):
+        want = _oracle(oracle_mod, np.ascontiguousarray(qo[:, :, row:row + 1]), ko[:, :, :row + 1],
+                       vo[:, :, :row + 1], io, True, row)
+        close(got[:, :, row:row + 1], want)
