@@ -463,6 +463,8 @@ size_t rows_smem(int mt, int x_slots, int stages) {
 }
 
 // Blocks of this kernel (at the given shared memory, no cluster) resident per SM.
+// This cache and the next are process-wide, not per device: they assume every
+// GPU of the process is the same model (true of one B200 node).
 int rows_blocks_per_sm(size_t smem) {
   static std::mutex mu;
   static int cache[8] = {};  // [smem bucket of 32 KB]

@@ -665,7 +665,8 @@ struct MPlan {
 };
 
 // Clusters of k blocks that can be resident at once: one 16-warp block per
-// SM, or (pair) two 8-warp blocks per SM.
+// SM, or (pair) two 8-warp blocks per SM.  The cache is process-wide: it
+// assumes every GPU of the process is the same model (true of one B200 node).
 int max_active_clusters(int k, int pair) {
   static std::mutex mu;
   static int cache[2][17] = {};
