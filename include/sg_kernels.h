@@ -181,6 +181,11 @@ int32_t sg_device_error_check(void* stream);
  *   "w4_gemv_mma.cluster"      tensor-core GEMV: allow the cluster-reduced split (1, default) or not (0)
  *   "tp_allreduce.wait_ms"     peer all-reduce: how long a rank waits for the others' flags
  *                              before it gives up and reports (1 .. 2000 ms; <= 0 restores 2000)
+ *   "sdk.fuse_norm", "sdk.fuse_rope", "sdk.fuse_swiglu"
+ *                              SDK one-row steps: fuse the norms / rope + KV append / SwiGLU
+ *                              into the projections (1, default) or run separate kernels (0)
+ *   "sdk.decode_step_kernel"   SDK one-sequence decode steps as one persistent kernel (1, when
+ *                              the model qualifies) or one kernel per op (0, default)
  * Returns SG_ERR_NOT_FOUND for an unknown key.  No reference counterpart. */
 int32_t sg_set_tuning(const char* key, int32_t value);
 

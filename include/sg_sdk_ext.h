@@ -131,6 +131,19 @@ ArmSession* sg_session_create_paged(ArmGraph* graph, const ArmSessionOptions* op
  * *pages_in_use are set), else 0 (both set to 0). */
 int32_t sg_session_kv_pages(const ArmSession* sess, uint32_t* pool_pages, uint32_t* pages_in_use);
 
+/* 1 when the session's one-token decode steps run as the persistent
+ * decode-step kernel (one sequence on one GPU, built on the first decode
+ * step while tuning key "sdk.decode_step_kernel" is 1), else 0 with the
+ * reason in *why (static or session-owned text; may be NULL). */
+int32_t sg_session_step_kernel(const ArmSession* sess, const char** why);
+
+/* Diagnostics of the decode-step kernel: on != 0 makes the following steps
+ * record a timeline (on == 0 stops and frees it); host (may be NULL) receives
+ * up to cap global-timer stamps in ns, [cta][512]: the step's start, then per
+ * grid barrier its arrival and its release, then the end of the LM head.
+ * Returns the stamps copied (and the CTA count in *ctas), or -1. */
+int32_t sg_session_step_trace(ArmSession* sess, int32_t on, uint64_t* host, uint32_t cap, int32_t* ctas);
+
 /* Prefills every sequence with n_tokens tokens (tokens[b * n_tokens + i] is
  * token i of sequence b). */
 ArmStatus sg_batch_prefill(ArmSession* sess, const int32_t* tokens, uint32_t n_tokens);

@@ -460,14 +460,43 @@ __global__ void v_to_f16_kernel(const __nv_bfloat16* V, int64_t kv_bs, int64_t k
   }
 }
 
+// A paged K / V read as the flat [B][Hkv][Skv][D] tensor: element e of it
+// lives on the page the table gives for its (sequence, key) (a page id outside
+// the pool reads page 0 and sets bit 4 of the device error word, as the
+// kernels' own lookups do).  table == nullptr: the tensor is flat already.
+struct KvGather {
+  const int32_t* table = nullptr;
+  int npages = 0, Hkv = 1, Skv = 0, D = 0;
+  int64_t page_stride = 0, tbs = 0, tps = 0;
+  int* err = nullptr;
+};
+
+__device__ __forceinline__ int64_t gather_index(const KvGather& g, int64_t e) {
+  if (!g.table) return e;
+  const int d = (int)(e % g.D);
+  const int64_t row = e / g.D;
+  const int key = (int)(row % g.Skv);
+  const int64_t bh = row / g.Skv;
+  const int hk = (int)(bh % g.Hkv), b = (int)(bh / g.Hkv);
+  int page = __ldg(g.table + (int64_t)b * g.tbs + (int64_t)(key >> 4) * g.tps);
+  if ((unsigned)page >= (unsigned)g.npages) {
+    if (g.err) atomicOr(g.err, 4);
+    page = 0;
+  }
+  return (int64_t)page * g.page_stride + ((int64_t)hk * 16 + (key & 15)) * g.D + d;
+}
+
 // fp32 I/O: the largest |x| of Q, K and V (as float bits, atomicMax on
 // non-negative floats orders like the values), then fp16 copies scaled by
 // 2^(14 - e), e the exponent of that largest value, so every value fits fp16
 // with the largest in [2^14, 2^15); dscale = {2^-(sq + sk), 2^-sv} undoes them.
+// A paged K / V is read through its table (only the live rows count) and
+// copied flat.
 __global__ void __launch_bounds__(256) absmax3_kernel(const float* q, int64_t nq, const float* k, int64_t nk,
-                                                       const float* v, int64_t nv, unsigned* amax) {
-  // 16-byte loads (the tensors are 16-byte aligned; n % 4 tails scalar), a
-  // block reduction in shared memory, then one atomic per block and tensor
+                                                       const float* v, int64_t nv, unsigned* amax, KvGather g) {
+  // 16-byte loads (the tensors are 16-byte aligned and D % 4 == 0, so the 4
+  // values share a row; n % 4 tails scalar), a block reduction in shared
+  // memory, then one atomic per block and tensor
   __shared__ unsigned red[3][8];
   unsigned m[3] = {0u, 0u, 0u};
   const float* src[3] = {q, k, v};
@@ -475,15 +504,15 @@ __global__ void __launch_bounds__(256) absmax3_kernel(const float* q, int64_t nq
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
 #pragma unroll
   for (int t = 0; t < 3; ++t) {
-    const float4* s4 = reinterpret_cast<const float4*>(src[t]);
     const int64_t n4 = n[t] / 4;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
-      const float4 x = __ldg(s4 + i);
+      const int64_t e = t ? gather_index(g, 4 * i) : 4 * i;
+      const float4 x = __ldg(reinterpret_cast<const float4*>(src[t] + e));
       m[t] = max(m[t], max(max(__float_as_uint(fabsf(x.x)), __float_as_uint(fabsf(x.y))),
                            max(__float_as_uint(fabsf(x.z)), __float_as_uint(fabsf(x.w)))));
     }
     for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n[t]; i += stride)
-      m[t] = max(m[t], __float_as_uint(fabsf(src[t][i])));
+      m[t] = max(m[t], __float_as_uint(fabsf(src[t][t ? gather_index(g, i) : i])));
     for (int o = 16; o; o >>= 1) m[t] = max(m[t], __shfl_xor_sync(0xffffffffu, m[t], o));
     if ((threadIdx.x & 31) == 0) red[t][threadIdx.x >> 5] = m[t];
   }
@@ -503,7 +532,7 @@ __device__ __forceinline__ int scale_shift(unsigned amax_bits) {
 __global__ void __launch_bounds__(256) f32_to_f16_scaled_kernel(const float* q, int64_t nq, const float* k,
                                                                  int64_t nk, const float* v, int64_t nv,
                                                                  const unsigned* amax, __half* q16, __half* k16,
-                                                                 __half* v16, float* dscale) {
+                                                                 __half* v16, float* dscale, KvGather g) {
   const int sq = scale_shift(amax[0]), sk = scale_shift(amax[1]), sv = scale_shift(amax[2]);
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     dscale[0] = ldexpf(1.f, -(sq + sk));
@@ -516,16 +545,16 @@ __global__ void __launch_bounds__(256) f32_to_f16_scaled_kernel(const float* q, 
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
 #pragma unroll
   for (int t = 0; t < 3; ++t) {
-    const float4* s4 = reinterpret_cast<const float4*>(src[t]);
     uint2* d4 = reinterpret_cast<uint2*>(dst[t]);  // 4 halves
     const int64_t n4 = n[t] / 4;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
-      const float4 x = __ldg(s4 + i);
+      const int64_t e = t ? gather_index(g, 4 * i) : 4 * i;
+      const float4 x = __ldg(reinterpret_cast<const float4*>(src[t] + e));
       __half2 lo = __floats2half2_rn(x.x * f[t], x.y * f[t]), hi = __floats2half2_rn(x.z * f[t], x.w * f[t]);
       d4[i] = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
     }
     for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n[t]; i += stride)
-      dst[t][i] = __float2half_rn(src[t][i] * f[t]);
+      dst[t][i] = __float2half_rn(src[t][t ? gather_index(g, i) : i] * f[t]);
   }
 }
 
@@ -583,12 +612,17 @@ bool tc_qualifies(const SgFlashAttentionParams* p) {
   const int io = p->io_dtype == SG_DT_DEFAULT ? SG_DT_F16 : p->io_dtype;
   const int D = p->head_dim;
   if ((io != SG_DT_F16 && io != SG_DT_BF16 && io != SG_DT_F32) || (D != 64 && D != 128)) return false;
-  if (io == SG_DT_F32) {  // copied to fp16 first: dense K / V only
+  if (io == SG_DT_F32) {  // copied to flat fp16 first: dense K / V, or pages gathered through the table
     const int Skv0 = p->S_kv > 0 ? p->S_kv : p->S;
     const int64_t dense_hs = (int64_t)Skv0 * D, dense_bs = (int64_t)std::max(1, p->num_kv_heads) * dense_hs;
-    if (p->kv_pages || (p->kv_head_stride > 0 && p->kv_head_stride != dense_hs) ||
-        (p->kv_batch_stride > 0 && p->kv_batch_stride != dense_bs))
+    if (p->kv_pages) {
+      if (p->kv_pages->page_size != kPageRows || !aligned16(p->K) || !aligned16(p->V) ||
+          (p->kv_pages->page_stride * 4) % 16 != 0)
+        return false;
+    } else if ((p->kv_head_stride > 0 && p->kv_head_stride != dense_hs) ||
+               (p->kv_batch_stride > 0 && p->kv_batch_stride != dense_bs)) {
       return false;
+    }
   }
   if (p->S < g_tune_attn_min_s.load()) return false;
   const int Hkv = std::max(1, p->num_kv_heads);
@@ -596,9 +630,9 @@ bool tc_qualifies(const SgFlashAttentionParams* p) {
   const int64_t kv_hs = p->kv_head_stride > 0 ? p->kv_head_stride : (int64_t)Skv * D;
   const int64_t kv_bs = p->kv_batch_stride > 0 ? p->kv_batch_stride : (int64_t)Hkv * kv_hs;
   if (!aligned16(p->Q) || !aligned16(p->K) || !aligned16(p->V) || !aligned16(p->O)) return false;
-  if (p->kv_pages) {
+  if (p->kv_pages && io != SG_DT_F32) {
     if (p->kv_pages->page_size != kPageRows || (p->kv_pages->page_stride * 2) % 16 != 0) return false;
-  } else if ((kv_hs * 2) % 16 != 0 || (kv_bs * 2) % 16 != 0) {
+  } else if (!p->kv_pages && ((kv_hs * 2) % 16 != 0 || (kv_bs * 2) % 16 != 0)) {
     return false;
   }
   const int q_pos0 = p->q_pos0 >= 0 ? p->q_pos0 : Skv - p->S;
@@ -663,16 +697,30 @@ SgStatus attn_tc_run(const SgFlashAttentionParams* p, cudaStream_t cs, void* ws,
   __half* k16 = reinterpret_cast<__half*>(w + 256 + align_up(nq * 2, 256));
   __half* v16 = reinterpret_cast<__half*>(w + 256 + align_up(nq * 2, 256) + align_up(nk * 2, 256));
   SG_CUDA_TRY(cudaMemsetAsync(amax, 0, 16, cs));
+  KvGather g;
+  if (p->kv_pages) {
+    const SgKvPages* pg = p->kv_pages;
+    g.table = pg->table;
+    g.npages = pg->num_pages;
+    g.Hkv = std::max(1, p->num_kv_heads);
+    g.Skv = p->S_kv > 0 ? p->S_kv : p->S;
+    g.D = p->head_dim;
+    g.page_stride = pg->page_stride;
+    g.tbs = pg->table_batch_stride;
+    g.tps = pg->table_page_stride;
+    st = device_error_word(&g.err);
+    if (st != SG_OK) return st;
+  }
   const int blocks = (int)std::max<size_t>(1, std::min<size_t>((nq + nk * 2) / 1024, 148 * 4));
   absmax3_kernel<<<blocks, 256, 0, cs>>>(static_cast<const float*>(p->Q), (int64_t)nq,
                                          static_cast<const float*>(p->K), (int64_t)nk,
-                                         static_cast<const float*>(p->V), (int64_t)nk, amax);
+                                         static_cast<const float*>(p->V), (int64_t)nk, amax, g);
   st = check_launch("absmax3_kernel");
   if (st != SG_OK) return st;
   f32_to_f16_scaled_kernel<<<blocks, 256, 0, cs>>>(static_cast<const float*>(p->Q), (int64_t)nq,
                                                    static_cast<const float*>(p->K), (int64_t)nk,
                                                    static_cast<const float*>(p->V), (int64_t)nk, amax, q16, k16, v16,
-                                                   dscale);
+                                                   dscale, g);
   st = check_launch("f32_to_f16_scaled_kernel");
   if (st != SG_OK) return st;
   SgFlashAttentionParams c = *p;
@@ -680,6 +728,7 @@ SgStatus attn_tc_run(const SgFlashAttentionParams* p, cudaStream_t cs, void* ws,
   c.K = k16;
   c.V = v16;
   c.io_dtype = SG_DT_F16;
+  c.kv_pages = nullptr;  // the copies are flat
   const int Skv = p->S_kv > 0 ? p->S_kv : p->S;
   c.kv_head_stride = (int64_t)Skv * p->head_dim;
   c.kv_batch_stride = (int64_t)std::max(1, p->num_kv_heads) * c.kv_head_stride;

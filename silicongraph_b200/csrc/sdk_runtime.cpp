@@ -49,10 +49,12 @@
 #include "sdk_io.h"
 #include "sg_sdk_ext.h"
 #include "sg_kernels.h"
+#include "decode_step.h"
 
 namespace sg {  // libsg_b200 internals (w4_gemv_mma.cu, sg_runtime.cu)
 size_t w4_gemv_mma_scratch_bytes(const SgMatMulParams* p, int sms, bool* applicable);
 int sm_count(int dev);
+int* existing_device_error_word(int dev);
 }  // namespace sg
 
 using sgsdk::Json;
@@ -421,6 +423,10 @@ struct ArmSession_ {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t graph_exec = nullptr;
   int32_t* h_pos = nullptr;  // pinned
+  // pinned landing block of a step's results: [batch] greedy tokens, the
+  // log-probability, the library's device error word
+  int32_t* h_res = nullptr;
+  int* graph_err_word = nullptr;  // the device error word the decode graph copies (null: none existed)
   // sequences decoded together (sg_session_create_ex), in lockstep at one position
   int batch = 1;
   std::vector<int32_t> next_all;  // host copy of every sequence's greedy token
@@ -441,6 +447,11 @@ struct ArmSession_ {
   // every projection's one-row shape runs on the kernel that fuses the norms (SG_MM_A_RMSNORM / C_ACCUMULATE)
   bool norm_fusable = false;
   bool rope_fusable = false;  // ... and the q|k|v one is a cluster split with head_dim 64 / 128
+  // one-sequence decode steps as one persistent kernel (decode_step.cu), built
+  // on the first such step; ds_why says why not when it could not be
+  sg::DecodeStep* ds = nullptr;
+  bool ds_tried = false;
+  std::string ds_why;
   int tp_timeout_ms = 60000;
 
   ~ArmSession_() {
@@ -457,6 +468,7 @@ struct ArmSession_ {
     }
     if (st) cudaStreamSynchronize(st);
     if (graph_exec) cudaGraphExecDestroy(graph_exec);
+    sg::decode_step_destroy(ds);
     if (graph) cudaGraphDestroy(graph);
     for (size_t q = 0; q < ar_regions.size(); ++q)
       if ((int)q != tp_rank && ar_regions[q]) cudaIpcCloseMemHandle(ar_regions[q]);
@@ -465,6 +477,7 @@ struct ArmSession_ {
     if (tp_flag) cudaFree(tp_flag);
     if (slab) cudaFree(slab);
     if (h_pos) cudaFreeHost(h_pos);
+    if (h_res) cudaFreeHost(h_res);
     if (st) cudaStreamDestroy(st);
   }
 
@@ -523,6 +536,9 @@ std::atomic<int> g_fuse_norm{1};
 // ... and the rope + KV append into the q|k|v projection's epilogue
 // (sg_qkv_gemv_rope_append), when its plan is a cluster split.
 std::atomic<int> g_fuse_rope{1};
+// ... and, for one sequence, the whole step runs as one persistent kernel
+// (decode_step.cu) when the model qualifies and the switch is on.
+std::atomic<int> g_step_kernel{0};
 
 ArmStatus linear(ArmSession_* S, const Linear& L, const void* A, void* C, int M, int c_dt, uint32_t flags = 0,
                  const void* norm_w = nullptr) {
@@ -803,14 +819,78 @@ ArmStatus forward(ArmSession_* S, int Ts, bool from_next, bool dev_pos = false) 
   return ARMCC_OK;
 }
 
+ArmStatus enqueue_results(ArmSession_* S);
+
+// Whether this session's one-token steps run as the persistent decode-step
+// kernel: one sequence on one GPU with the norms fused, and a model the kernel
+// takes (built here on the first such step, outside any capture).
+bool use_step_kernel(ArmSession_* S) {
+  if (S->batch != 1 || S->tp_world != 1 || !S->norm_fusable || g_fuse_norm.load() == 0 ||
+      g_step_kernel.load() == 0 || !S->c.lm_int4)
+    return false;
+  if (S->ds || S->ds_tried) return S->ds != nullptr;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(S->st, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return false;  // built on an eager step only (it allocates)
+  }
+  S->ds_tried = true;
+  const ModelCfg& c = S->c;
+  sg::DsModel m;
+  m.layers = c.layers;
+  m.hidden = c.hidden;
+  m.heads = c.heads;
+  m.kv_heads = c.kv_heads;
+  m.head_dim = c.head_dim;
+  m.ffn = c.ffn;
+  m.vocab = c.vocab;
+  m.group_size = c.group_size;
+  m.rope_theta = c.rope_theta;
+  m.rms_eps = c.rms_eps;
+  m.embed = S->embed;
+  m.vocab_rows = c.vocab_global;
+  m.final_norm = S->final_norm;
+  m.in_norm = S->in_norm;
+  m.post_norm = S->post_norm;
+  auto lin = [](const Linear& L) {
+    sg::DsLinear d;
+    d.qw = L.qw;
+    d.scales = L.scales;
+    d.zeros = L.zeros;
+    d.K = L.K;
+    d.N = L.N;
+    return d;
+  };
+  for (int l = 0; l < c.layers; ++l) {
+    m.qkv.push_back(lin(S->qkv[l]));
+    m.o.push_back(lin(S->o[l]));
+    m.gu.push_back(lin(S->gu[l]));
+    m.down.push_back(lin(S->down[l]));
+    m.k_cache.push_back(S->kcache(l));
+    m.v_cache.push_back(S->vcache(l));
+    if (S->paged) m.pages.push_back(S->kvp[l]);
+  }
+  m.lm = lin(S->lm);
+  m.kv_head_stride = S->kv_head_stride;
+  m.max_context = c.max_context;
+  if (const char* why = sg::decode_step_unsupported(m, S->dev)) {
+    S->ds_why = why;
+    return false;
+  }
+  if (sg::decode_step_create(m, S->dev, &S->ds) != SG_OK) {
+    S->ds_why = sg_last_error();
+    S->ds = nullptr;
+    return false;
+  }
+  return true;
+}
+
 // One decode token through the captured graph (captured on the second step,
 // after an eager step has done every first-use allocation and attribute call).
+// The graph holds the whole step: the position from the pinned host word, the
+// forward pass and the copies of the results into the pinned result block.
 ArmStatus decode_step(ArmSession_* S) {
   *S->h_pos = S->pos;
-  if (cudaMemcpyAsync(S->buf<int32_t>("pos"), S->h_pos, 4, cudaMemcpyHostToDevice, S->st) != cudaSuccess) {
-    set_err("copying the position failed");
-    return ARMCC_ERR_RUNTIME;
-  }
   if (S->use_graph && S->graph_exec) {
     if (cudaGraphLaunch(S->graph_exec, S->st) != cudaSuccess) {
       set_err("cudaGraphLaunch failed: %s", cudaGetErrorString(cudaGetLastError()));
@@ -819,16 +899,32 @@ ArmStatus decode_step(ArmSession_* S) {
     S->pos += 1;
     return ARMCC_OK;
   }
+  auto whole_step = [&]() -> ArmStatus {
+    if (cudaMemcpyAsync(S->buf<int32_t>("pos"), S->h_pos, 4, cudaMemcpyHostToDevice, S->st) != cudaSuccess) {
+      set_err("copying the position failed");
+      return ARMCC_ERR_RUNTIME;
+    }
+    if (use_step_kernel(S)) {
+      SG_TRY(sg::decode_step_run(S->ds, S->buf<int32_t>("pos"), S->buf<int32_t>("next"), S->buf<float>("logprob"),
+                                 S->buf<float>("logits"), S->st),
+             "decode step kernel");
+      S->pos += 1;
+      return enqueue_results(S);
+    }
+    const ArmStatus r = forward(S, 1, true, true);
+    return r == ARMCC_OK ? enqueue_results(S) : r;
+  };
   if (S->use_graph && !S->graph_failed && S->eager_steps > 0) {
     const int pos_before = S->pos;
     if (cudaStreamBeginCapture(S->st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
-      const ArmStatus r = forward(S, 1, true, true);
+      const ArmStatus r = whole_step();
       cudaGraph_t g = nullptr;
       const cudaError_t e = cudaStreamEndCapture(S->st, &g);
       cudaGraphExec_t x = nullptr;
       if (r == ARMCC_OK && e == cudaSuccess && g && cudaGraphInstantiate(&x, g, 0) == cudaSuccess) {
         S->graph = g;
         S->graph_exec = x;
+        S->graph_err_word = sg::existing_device_error_word(S->dev);
         if (cudaGraphLaunch(x, S->st) != cudaSuccess) {
           set_err("cudaGraphLaunch failed: %s", cudaGetErrorString(cudaGetLastError()));
           return ARMCC_ERR_RUNTIME;
@@ -841,7 +937,7 @@ ArmStatus decode_step(ArmSession_* S) {
     S->graph_failed = true;  // run eagerly from now on
     S->pos = pos_before;
   }
-  const ArmStatus r = forward(S, 1, true, true);
+  const ArmStatus r = whole_step();
   if (r == ARMCC_OK) S->eager_steps += 1;
   return r;
 }
@@ -962,23 +1058,48 @@ bool session_usable(ArmSession_* S, const char* fn) {
   return false;
 }
 
-// Reads every sequence's greedy token (and the kernels' error word) back to the host.
-ArmStatus fetch_next(ArmSession_* S) {
-  S->next_all.assign(S->batch, -1);
-  float lp = 0;
-  if (cudaMemcpyAsync(S->next_all.data(), S->buf<int32_t>("next"), (size_t)S->batch * 4, cudaMemcpyDeviceToHost,
-                      S->st) != cudaSuccess ||
-      cudaMemcpyAsync(&lp, S->buf<float>("logprob"), 4, cudaMemcpyDeviceToHost, S->st) != cudaSuccess) {
+// Queues the copies of every sequence's greedy token, the log-probability and
+// the library's device error word into the pinned result block (inside the
+// decode graph for a captured step, so a step costs one launch and one wait).
+ArmStatus enqueue_results(ArmSession_* S) {
+  const int B = S->batch;
+  int* derr = sg::existing_device_error_word(S->dev);
+  if (cudaMemcpyAsync(S->h_res, S->buf<int32_t>("next"), (size_t)B * 4, cudaMemcpyDeviceToHost, S->st) !=
+          cudaSuccess ||
+      cudaMemcpyAsync(S->h_res + B, S->buf<float>("logprob"), 4, cudaMemcpyDeviceToHost, S->st) != cudaSuccess ||
+      (derr && cudaMemcpyAsync(S->h_res + B + 1, derr, 4, cudaMemcpyDeviceToHost, S->st) != cudaSuccess)) {
     set_err("device error: %s", cudaGetErrorString(cudaGetLastError()));
     return ARMCC_ERR_RUNTIME;
   }
+  if (!derr) S->h_res[B + 1] = 0;
+  return ARMCC_OK;
+}
+
+// Waits for the step and takes every sequence's greedy token from the pinned
+// result block; enqueued: the step already queued the copies (enqueue_results).
+// A nonzero device error word is read and cleared through sg_device_error_check.
+ArmStatus fetch_next(ArmSession_* S, bool enqueued = false) {
+  const int B = S->batch;
+  if (!enqueued) {
+    const ArmStatus e = enqueue_results(S);
+    if (e != ARMCC_OK) return e;
+  }
   const ArmStatus ws = wait_stream(S, "decode");
   if (ws != ARMCC_OK) return ws;
-  const int32_t derr = sg_device_error_check(S->st);
-  if (derr != 0) {
-    set_err("a kernel reported device error %d (%s)", derr, sg_last_error());
+  // a graph captured before the error word existed does not copy it: read it directly
+  const bool direct = S->graph_exec && !S->graph_err_word && sg::existing_device_error_word(S->dev);
+  if (direct && sg_device_error_check(S->st) != 0) {
+    set_err("a kernel reported a device error (%s)", sg_last_error());
     return ARMCC_ERR_RUNTIME;
   }
+  if (S->h_res[B + 1] != 0) {
+    const int32_t derr = sg_device_error_check(S->st);
+    set_err("a kernel reported device error %d (%s)", S->h_res[B + 1], derr != 0 ? sg_last_error() : "");
+    return ARMCC_ERR_RUNTIME;
+  }
+  S->next_all.assign(S->h_res, S->h_res + B);
+  float lp = 0;
+  memcpy(&lp, S->h_res + B, 4);
   S->next_host = S->next_all[0];
   S->logprob_host = lp;
   return ARMCC_OK;
@@ -1050,7 +1171,7 @@ ArmStatus step_tokens(ArmSession_* S, const char* fn, float* step_ms) {
     }
     ArmStatus r = ensure_pages(S, S->pos + 1, fn);
     if (r == ARMCC_OK) r = decode_step(S);
-    if (r == ARMCC_OK) r = fetch_next(S);
+    if (r == ARMCC_OK) r = fetch_next(S, true);
     if (r != ARMCC_OK) return r;
   }
   const auto t1 = std::chrono::steady_clock::now();
@@ -1394,7 +1515,8 @@ ArmSession* create_session(ArmGraph* graph, const ArmSessionOptions* opts, int r
     return nullptr;
   }
   if (cudaStreamCreateWithFlags(&S->st, cudaStreamNonBlocking) != cudaSuccess ||
-      cudaMallocHost(&S->h_pos, sizeof(int32_t)) != cudaSuccess) {
+      cudaMallocHost(&S->h_pos, sizeof(int32_t)) != cudaSuccess ||
+      cudaMallocHost(&S->h_res, sizeof(int32_t) * ((size_t)S->batch + 2)) != cudaSuccess) {
     cudaGetLastError();
     set_err("%s: cannot create the session's stream", fn);
     return nullptr;
@@ -1643,6 +1765,10 @@ bool sdk_tuning(std::string_view key, int value) {
   }
   if (key == "sdk.fuse_rope") {
     g_fuse_rope.store(value);
+    return true;
+  }
+  if (key == "sdk.decode_step_kernel") {
+    g_step_kernel.store(value);
     return true;
   }
   return false;
@@ -2091,6 +2217,36 @@ int32_t sg_session_kv_pages(const ArmSession* sess, uint32_t* pool_pages, uint32
   if (pool_pages) *pool_pages = (uint32_t)sess->pool_pages;
   if (pages_in_use) *pages_in_use = (uint32_t)(sess->pool_pages - (int)sess->free_pages.size());
   return 1;
+}
+
+int32_t sg_session_step_trace(ArmSession* sess, int32_t on, uint64_t* host, uint32_t cap, int32_t* ctas) {
+  if (!sess || !sess->ds) {
+    set_err("sg_session_step_trace: the session has no decode-step kernel");
+    return -1;
+  }
+  cudaSetDevice(sess->dev);
+  cudaStreamSynchronize(sess->st);
+  size_t n = 0;
+  int nct = 0;
+  if (sg::decode_step_trace(sess->ds, on != 0, host, cap, &n, &nct) != SG_OK) {
+    set_err("sg_session_step_trace: %s", sg_last_error());
+    return -1;
+  }
+  if (ctas) *ctas = nct;
+  return (int32_t)n;
+}
+
+int32_t sg_session_step_kernel(const ArmSession* sess, const char** why) {
+  const char* w = nullptr;
+  if (!sess) w = "no session";
+  else if (sess->ds) w = nullptr;
+  else if (!sess->ds_why.empty()) w = sess->ds_why.c_str();
+  else if (sess->batch != 1) w = "more than one sequence";
+  else if (sess->tp_world != 1) w = "tensor-parallel";
+  else if (!sess->ds_tried) w = "not built yet (the first decode step builds it)";
+  else w = "not eligible (norm fusion off, an fp16 LM head, or the switch is off)";
+  if (why) *why = w;
+  return sess && sess->ds ? 1 : 0;
 }
 
 ArmStatus sg_batch_prefill(ArmSession* sess, const int32_t* tokens, uint32_t n_tokens) {

@@ -82,6 +82,9 @@ _SIGS = {
                                      ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(ctypes.c_uint8)]),
     "sg_session_abort": (ctypes.c_int, [_P, ctypes.c_char_p]),
     "sg_session_kv_pages": (ctypes.c_int32, [_P, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32)]),
+    "sg_session_step_kernel": (ctypes.c_int32, [_P, ctypes.POINTER(ctypes.c_char_p)]),
+    "sg_session_step_trace": (ctypes.c_int32, [_P, ctypes.c_int32, _P, ctypes.c_uint32,
+                                               ctypes.POINTER(ctypes.c_int32)]),
     "sg_session_create_ex": (_P, [_P, ctypes.POINTER(ArmSessionOptions), ctypes.c_uint32, ctypes.c_int32,
                                   ctypes.c_int32, ctypes.POINTER(ctypes.c_uint8)]),
     "sg_batch_prefill": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32]),
@@ -327,6 +330,31 @@ class Session:
         if not lib().sg_session_kv_pages(self.h, ctypes.byref(pool), ctypes.byref(used)):
             return None
         return pool.value, used.value
+
+    @property
+    def step_kernel(self) -> tuple[bool, str | None]:
+        """(whether one-token steps run as the persistent decode-step kernel, why not)."""
+        why = ctypes.c_char_p()
+        on = bool(lib().sg_session_step_kernel(self.h, ctypes.byref(why)))
+        return on, (why.value.decode() if why.value else None)
+
+    def step_trace(self, on: bool = True):
+        """Decode-step kernel timeline: step_trace(True) records the following
+        steps; step_trace(False) returns the last step's stamps as an int64
+        array [cta][512] (ns) and stops."""
+        import numpy as np
+        n_ct = ctypes.c_int32()
+        if on:
+            if lib().sg_session_step_trace(self.h, 1, None, 0, ctypes.byref(n_ct)) < 0:
+                raise ArmError(-5, last_error())
+            return None
+        lib().sg_session_step_trace(self.h, 1, None, 0, ctypes.byref(n_ct))
+        out = np.zeros(n_ct.value * 512, np.uint64)
+        n = lib().sg_session_step_trace(self.h, 1, out.ctypes.data, out.size, ctypes.byref(n_ct))
+        lib().sg_session_step_trace(self.h, 0, None, 0, ctypes.byref(n_ct))
+        if n < 0:
+            raise ArmError(-5, last_error())
+        return out.reshape(n_ct.value, 512).astype(np.int64)
 
     @property
     def position(self) -> int:

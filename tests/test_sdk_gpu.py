@@ -178,11 +178,13 @@ def test_fused_norm_decode_equals_unfused(sg, tmp_path):
     """One-row decode steps with the norms and residual adds fused into the
     projections (and the rope + KV append into the q|k|v projection) give the
     same tokens and logits, bit for bit, as the steps with separate kernels
-    (sdk.fuse_norm / sdk.fuse_rope 0)."""
+    (sdk.fuse_norm / sdk.fuse_rope 0); the per-op step (sdk.decode_step_kernel
+    0), which these switches select between."""
     from silicongraph_b200 import sdk
     path, _ = _package(tmp_path, 128)
     prompt = (np.arange(33, dtype=np.int32) * 11) % SMALL["vocab_size"]
     runs = []
+    sg.set_tuning("sdk.decode_step_kernel", 0)
     try:
         for fuse, rope in ((1, 1), (1, 0), (0, 0)):
             sg.set_tuning("sdk.fuse_norm", fuse)

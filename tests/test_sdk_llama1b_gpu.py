@@ -5,7 +5,7 @@ against the decoder composition oracle (oracle/decoder.py: the reference's
 kernel semantics, matmul_neon.h:113-147 / flash_attention.h:95-144 /
 matmul_neon.h:154-275, fp16 values at op boundaries).  Batch 1, and two
 sequences of a batch-16 session; the logits after the prompt and after each of
-four greedy steps.
+four greedy steps (batch 1: the persistent decode-step kernel, decode_step.cu).
 
 The yardstick is the reference's own rounding noise.  With fp16 values between
 ops, the reference's logits at this width and depth sit about 3e-3 (relative
@@ -69,7 +69,7 @@ def llama1b(sg, tmp_path_factory):
     return path, t
 
 
-def test_llama1b_batch1_matches_decoder_oracle(llama1b, oracle_mod):
+def test_llama1b_batch1_matches_decoder_oracle(sg, llama1b, oracle_mod):
     from oracle.decoder import DecoderOracle
     from silicongraph_b200 import sdk
     path, t = llama1b
@@ -77,6 +77,7 @@ def test_llama1b_batch1_matches_decoder_oracle(llama1b, oracle_mod):
     prompt = np.random.default_rng(24).integers(0, V, 24).astype(np.int32)
     r16 = DecoderOracle(LLAMA_1B, t, group_size=32)
     r32 = DecoderOracle(LLAMA_1B, t, group_size=32, precision="f32")
+    sg.set_tuning("sdk.decode_step_kernel", 1)
     with sdk.Package(path) as pkg:
         with pkg.select(context_length=64).session() as s:
             s.prefill(prompt)
@@ -91,6 +92,9 @@ def test_llama1b_batch1_matches_decoder_oracle(llama1b, oracle_mod):
                 slack = check(s.last_logits(V), want, r32.forward([tok]), f"step {step}")
                 check_token(r.next_token_id, want, slack)
                 tok = r.next_token_id
+            on, why = s.step_kernel
+    sg.set_tuning("sdk.decode_step_kernel", 0)
+    assert on, why  # the steps ran as the persistent decode-step kernel
 
 
 def test_llama1b_batch16_matches_decoder_oracle(llama1b, oracle_mod):
