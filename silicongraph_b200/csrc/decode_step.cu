@@ -97,8 +97,11 @@ struct DArgs {
   float* argp;       // [nct][3]
   unsigned* sync;    // [0] barrier arrivals, [1] pick ticket, [2] abort
   int* err;
-  // optional timeline (null: off): per CTA [kTraceEvents] global-timer stamps --
-  // the start, then per grid barrier its arrival and its release, then the end
+  // optional timeline (null: off), per CTA [kTraceEvents] (ns): [0] start;
+  // [1 + 2 k] / [2 + 2 k] arrival at / release from grid barrier k, then the
+  // end; [200 + p] activation staged in phase p; [300 + p] warp 0's wait for
+  // weight chunks in phase p; [400] the producer's wait for free slots, [401]
+  // its last issue; [420 + 4 l + kind] the producer's first issue of a projection
   uint64_t* trace;
   int ns, x_slots;
   // shared-memory layout (bytes from the 1024-aligned base)
@@ -138,8 +141,11 @@ __device__ void producer(const DArgs& a, uint8_t* smem, uint64_t* full, uint64_t
   const uint32_t tx = kWBytes + kSBytes + (a.has_z ? kZBytes : 0);
   uint32_t ci = 0;
   bool ok = true;
+  uint64_t* tr = a.trace ? a.trace + (size_t)b * kTraceEvents : nullptr;
+  uint64_t waited_ns = 0;
   for (int l = 0; l <= a.layers && ok; ++l) {
     for (int kind = 0; kind < (l < a.layers ? kKinds : 1) && ok; ++kind) {
+      if (tr && 420 + l * kKinds + kind < kTraceEvents) tr[420 + l * kKinds + kind] = sgd::global_timer_ns();
       const Gemv& g = a.g[l < a.layers ? kind : 4];
       const CUtensorMap* m = maps_of(a, l, kind);
       // the next projection's descriptors, ahead of their first use
@@ -153,11 +159,13 @@ __device__ void producer(const DArgs& a, uint8_t* smem, uint64_t* full, uint64_t
         unit_chunks(g, u, strip, piece, c0, c1);
         for (int c = c0; c < c1; ++c) {
           const uint32_t slot = ci % ns;
+          const uint64_t tw = tr ? sgd::global_timer_ns() : 0;
           if (ci >= ns && !sgd::mbar_wait(&empty[slot], ((ci / ns) - 1) & 1, a.err)) {
             atomicExch(a.sync + 2, 1u);
             ok = false;
             break;
           }
+          if (tr) waited_ns += sgd::global_timer_ns() - tw;
           const int x0 = strip * 128, row0 = c * kRows;
           const int gA = group_of(a, 2 * row0);
           uint8_t* wdst = smem + (size_t)slot * kWBytes;
@@ -170,6 +178,10 @@ __device__ void producer(const DArgs& a, uint8_t* smem, uint64_t* full, uint64_t
         }
       }
     }
+  }
+  if (tr) {
+    tr[400] = waited_ns;
+    tr[401] = sgd::global_timer_ns();
   }
   // copies still in flight land before the CTA may exit
   for (uint32_t j = ci > ns ? ci - ns : 0; j < ci; ++j) sgd::mbar_wait(&full[j % ns], (j / ns) & 1, a.err);
@@ -216,61 +228,98 @@ __device__ bool grid_barrier(const DArgs& a, unsigned& nb, int* s_abort) {
   return false;
 }
 
-// 1 / sqrt(mean(h^2) + eps) of a 16-bit row in shared memory, summed in the
-// order of sgn::row_rms_inv (threads 0..255 take 16-byte vectors tid, tid +
-// 256, ...; then a butterfly per warp and over the warps' sums), so the value
-// equals the norm kernel's bit for bit.  Called by all consumer threads.
-__device__ float cons_rms_inv(const __half* row, int n, float eps, float* red32) {
+// Sum of P k-split partials in p order, the loads batched 8 at a time so that
+// they are in flight together (a loop with a runtime trip count would wait for
+// each in turn).
+__device__ __forceinline__ float sum_parts(const float* p0, size_t stride, int P) {
+  float s = 0.f;
+  for (int p = 0; p < P; p += 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = p + j < P ? __ldcg(p0 + (size_t)(p + j) * stride) : 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (p + j < P) s += v[j];
+  }
+  return s;
+}
+
+// The residual row h and its RMSNorm, for a norm phase:
+//   h[k] = round(base[k] + round(sum_p part[p][k]))   (or base itself: the embedding)
+//   xn[k] = round(h[k] * rms_inv * w[k])              (shared memory, fp16)
+// with rms_inv summed in the order of sgn::row_rms_inv (threads 0..255 take the
+// 16-byte vectors tid, tid + 256, ... and add their squares in element order,
+// then a butterfly per warp and over the warps' sums), so it equals the norm
+// kernel's bit for bit.  CTA 0 stores h to dst.  Vector loads of the partials,
+// the residual and the norm weight are issued together.
+__device__ void norm_row(const DArgs& a, __half* xn, const __half* base, const float* part, int P, __half* dst,
+                         const __half* w, float* red32) {
+  const int nv = a.H / 8;
   float ss = 0.f;
   if (threadIdx.x < sgn::kNormThreads) {
-    const int nv = n / 8;
+#pragma unroll 1
+    for (int j = 0; j < sgn::kNormVecPerThread; ++j) {
+      const int v = threadIdx.x + j * sgn::kNormThreads;
+      if (v >= nv) break;
+      float b8[8];
+      sgn::unpack8<__half>(__ldcg(reinterpret_cast<const uint4*>(base) + v), b8);
+      if (part) {
+        float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int p = 0; p < P; p += 4) {
+          float4 q[4][2];
 #pragma unroll
-    for (int k = 0; k < sgn::kNormVecPerThread; ++k) {
-      const int v = threadIdx.x + k * sgn::kNormThreads;
-      if (v < nv) {
-        float h[8];
-        sgn::unpack8<__half>(reinterpret_cast<const uint4*>(row)[v], h);
-        ss = sgn::sumsq8(h, ss);
+          for (int t = 0; t < 4; ++t) {
+            const float4* src = reinterpret_cast<const float4*>(part + (size_t)(p + t) * a.H) + 2 * v;
+            q[t][0] = p + t < P ? __ldcg(src) : make_float4(0.f, 0.f, 0.f, 0.f);
+            q[t][1] = p + t < P ? __ldcg(src + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            if (p + t >= P) continue;
+            s8[0] += q[t][0].x;
+            s8[1] += q[t][0].y;
+            s8[2] += q[t][0].z;
+            s8[3] += q[t][0].w;
+            s8[4] += q[t][1].x;
+            s8[5] += q[t][1].y;
+            s8[6] += q[t][1].z;
+            s8[7] += q[t][1].w;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) b8[e] = __half2float(__float2half_rn(__half2float(__float2half_rn(s8[e])) + b8[e]));
       }
+      ss = sgn::sumsq8(b8, ss);
+      const uint4 hv = sgn::pack8<__half>(b8);
+      reinterpret_cast<uint4*>(xn)[v] = hv;
+      if (dst && blockIdx.x == 0) reinterpret_cast<uint4*>(dst)[v] = hv;
     }
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   cbar();  // red32 may still be read by a previous reduction
-  if (lane == 0) red32[w] = ss;
+  if (lane == 0) red32[wp] = ss;
   cbar();
   float t = lane < kCW ? red32[lane] : 0.f;
 #pragma unroll
   for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-  return 1.0f / sqrtf(t / (float)n + eps);
-}
-
-// xf[k] = round(base[k] + round(sum_p part[p][k])) for k < H (partials added in
-// p order), or the embedding row when part is null; CTA 0 also stores it to dst.
-__device__ void build_row(const DArgs& a, __half* xf, const __half* base, const float* part, int P, __half* dst) {
-  for (int k4 = threadIdx.x; k4 < a.H / 4; k4 += kCT) {
-    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-    uint2 hv = __ldcg(reinterpret_cast<const uint2*>(base) + k4);
-    if (part) {
-      for (int p = 0; p < P; ++p) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(part + (size_t)p * a.H) + k4);
-        s.x += v.x;
-        s.y += v.y;
-        s.z += v.z;
-        s.w += v.w;
-      }
-      const __half* h = reinterpret_cast<const __half*>(&hv);
-      __half o[4];
-      const float sv[4] = {s.x, s.y, s.z, s.w};
+  const float rms = 1.0f / sqrtf(t / (float)a.H + a.eps);
+  // the same thread rewrites the vectors it wrote: no barrier needed in between
+  if (threadIdx.x < sgn::kNormThreads) {
+#pragma unroll 1
+    for (int j = 0; j < sgn::kNormVecPerThread; ++j) {
+      const int v = threadIdx.x + j * sgn::kNormThreads;
+      if (v >= nv) break;
+      float h8[8], w8[8], y[8];
+      sgn::unpack8<__half>(reinterpret_cast<const uint4*>(xn)[v], h8);
+      sgn::unpack8<__half>(__ldg(reinterpret_cast<const uint4*>(w) + v), w8);
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        o[j] = __float2half_rn(__half2float(__float2half_rn(sv[j])) + __half2float(h[j]));
-      hv = *reinterpret_cast<const uint2*>(o);
+      for (int e = 0; e < 8; ++e) y[e] = __half2float(__float2half_rn(h8[e] * rms * w8[e]));
+      reinterpret_cast<uint4*>(xn)[v] = sgn::pack8<__half>(y);
     }
-    reinterpret_cast<uint2*>(xf)[k4] = hv;
-    if (dst && blockIdx.x == 0) reinterpret_cast<uint2*>(dst)[k4] = hv;
   }
+  cbar();
 }
 
 // Stages x over k-pair rows [lo * 32, hi * 32) as 24-bit fixed point with one
@@ -368,7 +417,7 @@ __device__ __forceinline__ void chunk_mma(const DArgs& a, const uint8_t* wst, co
 // in warp order, out(piece, col, value, unit index) for every column < N.
 template <bool HAS_Z, class X, class OUT>
 __device__ bool gemv_phase(const DArgs& a, const Gemv& g, uint8_t* smem, uint64_t* full, uint64_t* empty,
-                           uint32_t& ci, int* s_abort, X xfn, OUT out) {
+                           uint32_t& ci, int* s_abort, unsigned ph, X xfn, OUT out) {
   const int b = blockIdx.x;
   if (b >= g.units) return true;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -385,6 +434,9 @@ __device__ bool gemv_phase(const DArgs& a, const Gemv& g, uint8_t* smem, uint64_
   stage_rows(xst, xgrp, lo, hi, xfn);
   cbar();
   const uint32_t ns = (uint32_t)a.ns;
+  uint64_t wait0 = 0;  // warp 0's time waiting for weight chunks (timeline only)
+  if (a.trace && threadIdx.x == 0 && 200 + ph < (unsigned)kTraceEvents)
+    a.trace[(size_t)b * kTraceEvents + 200 + ph] = sgd::global_timer_ns();  // staging done
   int j = 0;
   for (int u = b; u < g.units; u += a.nct, ++j) {
     int strip, piece, c0, c1;
@@ -393,7 +445,9 @@ __device__ bool gemv_phase(const DArgs& a, const Gemv& g, uint8_t* smem, uint64_
     for (int c = c0; c < c1; ++c, ++ci) {
       if ((int)(ci % kCW) != warp) continue;
       const uint32_t slot = ci % ns;
+      const uint64_t tw = (a.trace && warp == 0) ? sgd::global_timer_ns() : 0;
       const bool waited = sgd::mbar_wait(&full[slot], (ci / ns) & 1, a.err);
+      if (a.trace && warp == 0) wait0 += sgd::global_timer_ns() - tw;
       if (!__all_sync(0xffffffffu, waited)) {
         if (lane == 0) {
           *s_abort = 1;
@@ -420,6 +474,8 @@ __device__ bool gemv_phase(const DArgs& a, const Gemv& g, uint8_t* smem, uint64_
     cbar();
     if (*s_abort) return false;
   }
+  if (a.trace && threadIdx.x == 0 && 300 + ph < (unsigned)kTraceEvents)
+    a.trace[(size_t)b * kTraceEvents + 300 + ph] = wait0;
   return true;
 }
 
@@ -511,9 +567,7 @@ __device__ bool attn_do_unit(const DArgs& a, int l, const AttnUnit<D>& u, int po
     if (i < grp * D) col = (u.hk * grp) * D + i;
     else if (i < (grp + 1) * D) col = (a.heads + u.hk) * D + (i - grp * D);
     else col = (a.heads + a.kvh + u.hk) * D + (i - (grp + 1) * D);
-    float s = 0.f;
-    for (int p = 0; p < P; ++p) s += __ldcg(a.part_qkv + (size_t)p * nq + col);
-    qs[i] = __half2float(__float2half_rn(s));
+    qs[i] = __half2float(__float2half_rn(sum_parts(a.part_qkv + col, nq, P)));
   }
   cbar();
   // ---- rotary pairs (i, i + D/2) of q and k
@@ -723,18 +777,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DArgs a) {
   for (int l = 0; l < a.layers; ++l) {
     // ---- q|k|v of RMSNorm(h): h is the embedding row or h1 + down partials
     if (l > 0 && !grid_barrier(a, nb, &s_abort)) return;
-    if (l == 0) build_row(a, xf, emb, nullptr, 0, a.r0);
-    else build_row(a, xf, a.r1, a.part_down, a.g[3].P, a.r0);
-    cbar();
+    if (l == 0) norm_row(a, xf, emb, nullptr, 0, a.r0, a.in_norm[l], s_red);
+    else norm_row(a, xf, a.r1, a.part_down, a.g[3].P, a.r0, a.in_norm[l], s_red);
     {
-      const __half* w = a.in_norm[l];
-      const float rms = cons_rms_inv(xf, H, a.eps, s_red);
-      auto xfn = [&](int k) -> float {
-        return k < H ? __half2float(__float2half_rn(__half2float(xf[k]) * rms * __half2float(w[k]))) : 0.f;
-      };
+      auto xfn = [&](int k) -> float { return k < H ? __half2float(xf[k]) : 0.f; };
       const int nq = a.g[0].N;
       auto out = [&](int piece, int col, float v, int) { a.part_qkv[(size_t)piece * nq + col] = v; };
-      if (!gemv_phase<HAS_Z>(a, a.g[0], smem, full, empty, ci, &s_abort, xfn, out)) return;
+      if (!gemv_phase<HAS_Z>(a, a.g[0], smem, full, empty, ci, &s_abort, nb, xfn, out)) return;
     }
     // ---- attention: key groups that do not depend on this step first
     const int nunits = a.kvh * a.nspl;
@@ -761,27 +810,38 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DArgs a) {
         const int k_lo = c0 * 64, k_hi = min(H, c1 * 64);
         const int h0 = k_lo / D, h1 = (k_hi + D - 1) / D;
         const int nsp = a.nspl;
-        // per head: the splits' weights exp2(m_sp - M) and 1 / sum
-        for (int hh = warp; hh < h1 - h0; hh += kCW) {
+        // per head: the splits' (max, sum) into shared memory, their weights
+        // exp2(m_sp - M) and the sum L = sum_sp l_sp w_sp in split order
+        const int nh = h1 - h0;
+        const size_t sstride = (size_t)a.grp * (D + 2);
+        float* wts = misc;                        // [nh][nsp + 1]: weights, then L
+        float* mls = misc + nh * (nsp + 1);       // [nh][nsp][2]: max, sum
+        for (int i = threadIdx.x; i < nh * nsp; i += kCT) {
+          const int hh = i / nsp, sp = i - hh * nsp;
           const int h = h0 + hh, hk = h / a.grp, r = h - hk * a.grp;
-          const float* pr = a.part_attn + ((size_t)hk * nsp * a.grp + r) * (D + 2);
-          const size_t sstride = (size_t)a.grp * (D + 2);
+          const float* pr = a.part_attn + ((size_t)hk * nsp * a.grp + r) * (D + 2) + sp * sstride;
+          mls[2 * i] = __ldcg(pr + D);
+          mls[2 * i + 1] = __ldcg(pr + D + 1);
+        }
+        cbar();
+        for (int hh = warp; hh < nh; hh += kCW) {
+          const int lane = threadIdx.x & 31;
           float M = -INFINITY;
-          for (int sp = threadIdx.x & 31; sp < nsp; sp += 32) M = fmaxf(M, __ldcg(pr + sp * sstride + D));
+          for (int sp = lane; sp < nsp; sp += 32) M = fmaxf(M, mls[2 * (hh * nsp + sp)]);
 #pragma unroll
           for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-          for (int sp = threadIdx.x & 31; sp < nsp; sp += 32) {
-            const float m = __ldcg(pr + sp * sstride + D);
-            misc[hh * (nsp + 1) + sp] = m == -INFINITY ? 0.f : exp2f(m - M);
+          for (int sp = lane; sp < nsp; sp += 32) {
+            const float m = mls[2 * (hh * nsp + sp)];
+            wts[hh * (nsp + 1) + sp] = m == -INFINITY ? 0.f : exp2f(m - M);
           }
           __syncwarp();
-          if ((threadIdx.x & 31) == 0) {  // in split order; empty splits (weight 0) add nothing
+          if (lane == 0) {  // in split order; empty splits (weight 0) add nothing
             float L = 0.f;
             for (int sp = 0; sp < nsp; ++sp) {
-              const float wt = misc[hh * (nsp + 1) + sp];
-              if (wt != 0.f) L = fmaf(__ldcg(pr + sp * sstride + D + 1), wt, L);
+              const float wt = wts[hh * (nsp + 1) + sp];
+              if (wt != 0.f) L = fmaf(mls[2 * (hh * nsp + sp) + 1], wt, L);
             }
-            misc[hh * (nsp + 1) + nsp] = L;
+            wts[hh * (nsp + 1) + nsp] = L;
           }
         }
         cbar();
@@ -789,61 +849,70 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(DArgs a) {
           const int h = k / D, d = k - h * D, hh = h - h0;
           const int hk = h / a.grp, r = h - hk * a.grp;
           const float* pr = a.part_attn + ((size_t)hk * nsp * a.grp + r) * (D + 2) + d;
-          const size_t sstride = (size_t)a.grp * (D + 2);
+          const float* wt = wts + hh * (nsp + 1);
           float acc = 0.f;
-          for (int sp = 0; sp < nsp; ++sp) {
-            const float wt = misc[hh * (nsp + 1) + sp];
-            if (wt != 0.f) acc = fmaf(__ldcg(pr + sp * sstride), wt, acc);
+          for (int sp = 0; sp < nsp; sp += 8) {  // loads batched; an empty split holds O = 0 and weight 0
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = sp + j < nsp ? __ldcg(pr + (sp + j) * sstride) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              if (sp + j < nsp && wt[sp + j] != 0.f) acc = fmaf(v[j], wt[sp + j], acc);
           }
-          const float L = misc[hh * (nsp + 1) + nsp];
+          const float L = wt[nsp];
           xa[k - k_lo] = __half2float(__float2half_rn(L > 0.f ? acc / L : 0.f));
         }
         cbar();
         auto xfn = [&](int k) -> float { return k < k_hi ? xa[k - k_lo] : 0.f; };
         auto out = [&](int piece2, int col, float v, int) { a.part_o[(size_t)piece2 * H + col] = v; };
-        if (!gemv_phase<HAS_Z>(a, g, smem, full, empty, ci, &s_abort, xfn, out)) return;
+        if (!gemv_phase<HAS_Z>(a, g, smem, full, empty, ci, &s_abort, nb, xfn, out)) return;
       }
     }
     // ---- gate|up of RMSNorm(h1), h1 = h + o
     if (!grid_barrier(a, nb, &s_abort)) return;
-    build_row(a, xf, a.r0, a.part_o, a.g[1].P, a.r1);
-    cbar();
+    norm_row(a, xf, a.r0, a.part_o, a.g[1].P, a.r1, a.post_norm[l], s_red);
     {
-      const __half* w = a.post_norm[l];
-      const float rms = cons_rms_inv(xf, H, a.eps, s_red);
-      auto xfn = [&](int k) -> float {
-        return k < H ? __half2float(__float2half_rn(__half2float(xf[k]) * rms * __half2float(w[k]))) : 0.f;
-      };
+      auto xfn = [&](int k) -> float { return k < H ? __half2float(xf[k]) : 0.f; };
       auto out = [&](int, int col, float v, int) { a.gu[col] = __float2half_rn(v); };
-      if (!gemv_phase<HAS_Z>(a, a.g[2], smem, full, empty, ci, &s_abort, xfn, out)) return;
+      if (!gemv_phase<HAS_Z>(a, a.g[2], smem, full, empty, ci, &s_abort, nb, xfn, out)) return;
     }
     // ---- down of SwiGLU(gate, up)
     if (!grid_barrier(a, nb, &s_abort)) return;
     {
       const int F = a.F;
-      auto xfn = [&](int k) -> float {
-        if (k >= F) return 0.f;
-        return __half2float(sgd::swiglu_value<__half>(__half2float(__ldcg(a.gu + k)), __half2float(__ldcg(a.gu + F + k))));
-      };
+      const Gemv& g = a.g[3];
+      int k_lo = 0, k_hi = 0;
+      if (b < g.units) {  // one unit per CTA
+        int strip, piece, c0, c1;
+        unit_chunks(g, b, strip, piece, c0, c1);
+        k_lo = c0 * 64;
+        k_hi = min(F, c1 * 64);
+        for (int v = threadIdx.x; v < (k_hi - k_lo) / 8; v += kCT) {  // k_lo, k_hi: multiples of 8
+          float g8[8], u8[8];
+          sgn::unpack8<__half>(__ldcg(reinterpret_cast<const uint4*>(a.gu + k_lo) + v), g8);
+          sgn::unpack8<__half>(__ldcg(reinterpret_cast<const uint4*>(a.gu + F + k_lo) + v), u8);
+          __half y[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) y[e] = sgd::swiglu_value<__half>(g8[e], u8[e]);
+          reinterpret_cast<uint4*>(xf)[v] = *reinterpret_cast<const uint4*>(y);
+        }
+        cbar();
+      }
+      auto xfn = [&](int k) -> float { return k < k_hi ? __half2float(xf[k - k_lo]) : 0.f; };
       auto out = [&](int piece, int col, float v, int) { a.part_down[(size_t)piece * H + col] = v; };
-      if (!gemv_phase<HAS_Z>(a, a.g[3], smem, full, empty, ci, &s_abort, xfn, out)) return;
+      if (!gemv_phase<HAS_Z>(a, a.g[3], smem, full, empty, ci, &s_abort, nb, xfn, out)) return;
     }
   }
   // ---- final norm, LM head, greedy pick
   if (!grid_barrier(a, nb, &s_abort)) return;
-  build_row(a, xf, a.r1, a.part_down, a.g[3].P, nullptr);
-  cbar();
+  norm_row(a, xf, a.r1, a.part_down, a.g[3].P, nullptr, a.final_norm, s_red);
   {
-    const float rms = cons_rms_inv(xf, H, a.eps, s_red);
-    const __half* w = a.final_norm;
-    auto xfn = [&](int k) -> float {
-      return k < H ? __half2float(__float2half_rn(__half2float(xf[k]) * rms * __half2float(w[k]))) : 0.f;
-    };
+    auto xfn = [&](int k) -> float { return k < H ? __half2float(xf[k]) : 0.f; };
     auto out = [&](int, int col, float v, int j) {
       a.logits[col] = v;
       lmv[j * 128 + (col & 127)] = v;
     };
-    if (!gemv_phase<HAS_Z>(a, a.g[4], smem, full, empty, ci, &s_abort, xfn, out)) return;
+    if (!gemv_phase<HAS_Z>(a, a.g[4], smem, full, empty, ci, &s_abort, nb, xfn, out)) return;
   }
   // this CTA's (max, first index of the max, sum of exp(x - max)) over its columns
   const Gemv& gl = a.g[4];
@@ -984,6 +1053,7 @@ const char* decode_step_unsupported(const DsModel& m, int dev) {
   if (m.head_dim != 64 && m.head_dim != 128) return "head_dim other than 64 or 128";
   if (m.heads % m.kv_heads != 0 || m.heads / m.kv_heads > 16) return "query heads per kv head";
   if (m.hidden % 8 != 0 || m.hidden > sgn::kNormMaxN) return "hidden size";
+  if (m.ffn % 8 != 0) return "SwiGLU width";
   if (m.group_size <= 0 || m.group_size % 32 != 0) return "group size";
   if (!m.lm.qw) return "an fp16 LM head";
   const DsLinear* all[4] = {nullptr, nullptr, nullptr, nullptr};
@@ -1093,11 +1163,16 @@ SgStatus decode_step_create(const DsModel& m, int dev, DecodeStep** out) {
   const size_t q_bytes = align_up((size_t)(a.grp + 2) * D * 4, 128);
   const size_t lm_bytes = align_up((size_t)lm_units * 128 * 4, 128);
   const size_t x_bytes = align_up((size_t)x_slots * kXSlotBytes, 128);
+  // xf: the normed row (H fp16), the o phase's merged attention (its k range, fp32)
+  // or the down phase's SwiGLU values (its k range, fp16)
   const int o_range = (a.g[1].cpt + a.g[1].P - 1) / a.g[1].P + 1;
-  const size_t xf_bytes = align_up(std::max((size_t)H * 2, (size_t)o_range * 64 * 4), 128);
+  const int d_range = (a.g[3].cpt + a.g[3].P - 1) / a.g[3].P + 1;
+  const size_t xf_bytes =
+      align_up(std::max({(size_t)H * 2, (size_t)o_range * 64 * 4, (size_t)d_range * 64 * 2}), 128);
+  // misc: the o phase's per-head split weights and (max, sum) pairs, or the greedy pick's scratch
   const int o_heads = o_range * 64 / D + 2;
   const size_t misc_bytes =
-      align_up(std::max({(size_t)o_heads * (a.nspl + 1) * 4, (size_t)(64 + 3 * sms) * 4, (size_t)64 * 4}), 128);
+      align_up(std::max({(size_t)o_heads * (3 * a.nspl + 1) * 4, (size_t)(64 + 3 * sms) * 4, (size_t)64 * 4}), 128);
   const size_t fixed = a_bytes + q_bytes + lm_bytes + x_bytes + xf_bytes + misc_bytes;
   int max_optin = 0;
   SG_CUDA_TRY(cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
