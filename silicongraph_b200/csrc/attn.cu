@@ -909,8 +909,6 @@ __global__ void __launch_bounds__(kDecWarpThreads) attn_dec_warp_kernel(AArgs a)
   float* wm = reinterpret_cast<float*>(smb);                  // after the loop: [warp][16][D + 2]
   float* comb = reinterpret_cast<float*>(smb + main_bytes);  // rank 0: [rank][R][D + 2]
   asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-  sgd::pdl_wait();  // the newest key and the queries come from the previous kernel
-  sgd::pdl_launch_dependents();
 
   const int b = blockIdx.z, hk = blockIdx.y, split = blockIdx.x;
   const int nq = a.Sq, R = a.G * nq;  // row r: head hk*G + r / nq, query r % nq
@@ -956,10 +954,18 @@ __global__ void __launch_bounds__(kDecWarpThreads) attn_dec_warp_kernel(AArgs a)
       sgd::cp_async_16(vd + kl * KP + part * 8, static_cast<const uint16_t*>(a.V) + e0, live);
     }
   };
-  for (int i = 0; i < ST - 1; ++i) {
-    if (i < nmine) issue(i);
-    sgd::cp_async_commit();
-  }
+  // Keys before q_pos0 were written by earlier steps (or chunks), and the
+  // position, the page table and the ranges above come from the host: the
+  // warp's first group streams before the dependency wait unless it holds one
+  // of the newest keys, which the previous kernel on the stream writes.
+  static_assert(ST == 2, "one group in flight ahead of the loop");
+  const bool pre = nmine > 0 && j0 + (warp + 1) * KG <= q_pos0;
+  if (pre) issue(0);
+  sgd::cp_async_commit();
+  sgd::pdl_wait();  // the newest keys and the queries come from the previous kernel
+  sgd::pdl_launch_dependents();
+  if (nmine > 0 && !pre) issue(0);
+  sgd::cp_async_commit();
 
   // Q fragments (A of S = Q K^T), prescaled by scale * log2(e); rows >= R are zero.
   const float qscale = a.scale * 1.4426950408889634f;
