@@ -856,12 +856,12 @@ def run_decode(args):
     with tempfile.TemporaryDirectory() as td:
         pkg_path = os.path.join(td, "llama1b_int4")
         weight_bytes, tensors = build_decode_package(pkg_path, cfg, seed=11 + seed_rank,
-                                                     max_context=prompt_len + steps + args.warmup + 8)
+                                                     max_context=prompt_len + steps + args.warmup + 32)
         rng = np.random.default_rng(5 + seed_rank)
         B = args.batch
         prompt = rng.integers(0, c["vocab"], (B, prompt_len)).astype(np.int32)
         with sdk.Package(pkg_path) as pkg:
-            graph = pkg.select(context_length=prompt_len + steps + args.warmup)
+            graph = pkg.select(context_length=prompt_len + steps + args.warmup + 24)
             with graph.session(tp=tp_arg, batch=B) as s:
                 if B == 1:
                     prefill, decode = (lambda: s.prefill(prompt[0])), (lambda: s.decode().next_token_id)
@@ -882,6 +882,11 @@ def run_decode(args):
                     decode()
                 t2 = time.perf_counter()
                 clk = clocks.stop() if clocks else None
+                # the device time of a step (CUDA events around it), after the timed region
+                s.step_gpu_ms(True)
+                for _ in range(16):
+                    decode()
+                gpu_ms = s.step_gpu_ms(False)
     decode_s, ttft_s = host_max([t2 - t1, t1 - t0])  # the slowest rank
     tps = steps / decode_s
     seqs = args.batch * (1 if tp else world)  # sequences decoded at once over the whole job
@@ -899,6 +904,7 @@ def run_decode(args):
         "config": {"workload": DECODE_WORKLOAD, "batch": args.batch, "prompt": prompt_len, "decode_steps": steps,
                    "ttft_ms": round(1e3 * ttft_s, 3), "prefill_tokens_per_s": round(prompt_len / ttft_s, 1),
                    "bytes_per_token": int(bytes_per_token),
+                   "gpu_ms_per_step": round(gpu_ms, 4),
                    "parallelism": (f"tensor-parallel x{world} (one session over {world} GPUs, NCCL all-reduce "
                                    "after the o and down projections)") if tp else
                                   f"replicas x{world} (one session per GPU)",
@@ -955,7 +961,7 @@ def run_qwen(args):
                                head_dim=c["head_dim"], ffn=c["ffn"], vocab=c["vocab"], rope_theta=c["rope_theta"])
     steps = args.steps
     B = args.batch
-    ctx = QWEN_PROMPT + steps + args.warmup + 8
+    ctx = QWEN_PROMPT + steps + args.warmup + 24  # + 16 steps timed on the device after the timed region
     # prompt chunk per forward pass: the whole prompt for one sequence; about 32 K tokens per
     # pass when batched (the activation buffers scale with sequences x chunk)
     chunk = QWEN_PROMPT if B == 1 else max(256, (32768 // B) // 256 * 256)
@@ -999,6 +1005,11 @@ def run_qwen(args):
                     decode()
                 t2 = time.perf_counter()
                 clk = clocks.stop() if clocks else None
+                # the device time of a step (CUDA events around it), after the timed region
+                s.step_gpu_ms(True)
+                for _ in range(16):
+                    decode()
+                gpu_ms = s.step_gpu_ms(False)
     finally:
         host_barrier()
         if rank == 0:
@@ -1025,6 +1036,7 @@ def run_qwen(args):
                    "ttft_ms": round(1e3 * ttft_s, 2),
                    "decode_steps": steps, "decode_tokens_per_s": round(dec_tps, 2),
                    "decode_ms_per_token": round(1e3 * decode_s / steps, 3),
+                   "decode_gpu_ms_per_step": round(gpu_ms, 4),
                    "weight_bytes": int(weight_bytes), "flops_prefill": flops,
                    "parallelism": f"tensor-parallel x{world} (NCCL all-reduce after o and down)",
                    "timing": "host clock around armsess_prefill / armsess_decode, max over ranks"},

@@ -144,6 +144,13 @@ int32_t sg_session_step_kernel(const ArmSession* sess, const char** why);
  * Returns the stamps copied (and the CTA count in *ctas), or -1. */
 int32_t sg_session_step_trace(ArmSession* sess, int32_t on, uint64_t* host, uint32_t cap, int32_t* ctas);
 
+/* Device time of decode steps: on != 0 starts timing the following steps
+ * (CUDA events on the session's stream around each step) and returns 0;
+ * on == 0 stops and returns the mean device milliseconds per timed step (0
+ * when none ran).  -1 on error.  The host-side time per step is
+ * ArmInferenceResult.tpot_ms. */
+double sg_session_step_gpu_ms(ArmSession* sess, int32_t on);
+
 /* Prefills every sequence with n_tokens tokens (tokens[b * n_tokens + i] is
  * token i of sequence b). */
 ArmStatus sg_batch_prefill(ArmSession* sess, const int32_t* tokens, uint32_t n_tokens);

@@ -452,6 +452,12 @@ struct ArmSession_ {
   sg::DecodeStep* ds = nullptr;
   bool ds_tried = false;
   std::string ds_why;
+  // optional device time of the decode steps (sg_session_step_gpu_ms): events
+  // recorded on the stream around each step
+  cudaEvent_t ev_step[2] = {nullptr, nullptr};
+  bool ev_pending = false;
+  double step_gpu_ms = 0;
+  uint64_t step_gpu_n = 0;
   int tp_timeout_ms = 60000;
 
   ~ArmSession_() {
@@ -469,6 +475,8 @@ struct ArmSession_ {
     if (st) cudaStreamSynchronize(st);
     if (graph_exec) cudaGraphExecDestroy(graph_exec);
     sg::decode_step_destroy(ds);
+    for (cudaEvent_t e : ev_step)
+      if (e) cudaEventDestroy(e);
     if (graph) cudaGraphDestroy(graph);
     for (size_t q = 0; q < ar_regions.size(); ++q)
       if ((int)q != tp_rank && ar_regions[q]) cudaIpcCloseMemHandle(ar_regions[q]);
@@ -889,7 +897,21 @@ bool use_step_kernel(ArmSession_* S) {
 // after an eager step has done every first-use allocation and attribute call).
 // The graph holds the whole step: the position from the pinned host word, the
 // forward pass and the copies of the results into the pinned result block.
+ArmStatus decode_step_inner(ArmSession_* S);
+
+// A decode step, bracketed by the timing events when they are on.
 ArmStatus decode_step(ArmSession_* S) {
+  const bool timed = S->ev_step[0] != nullptr;
+  if (timed) cudaEventRecord(S->ev_step[0], S->st);
+  const ArmStatus r = decode_step_inner(S);
+  if (timed && r == ARMCC_OK) {
+    cudaEventRecord(S->ev_step[1], S->st);
+    S->ev_pending = true;
+  }
+  return r;
+}
+
+ArmStatus decode_step_inner(ArmSession_* S) {
   *S->h_pos = S->pos;
   if (S->use_graph && S->graph_exec) {
     if (cudaGraphLaunch(S->graph_exec, S->st) != cudaSuccess) {
@@ -1096,6 +1118,15 @@ ArmStatus fetch_next(ArmSession_* S, bool enqueued = false) {
     const int32_t derr = sg_device_error_check(S->st);
     set_err("a kernel reported device error %d (%s)", S->h_res[B + 1], derr != 0 ? sg_last_error() : "");
     return ARMCC_ERR_RUNTIME;
+  }
+  if (S->ev_pending) {
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, S->ev_step[0], S->ev_step[1]) == cudaSuccess) {
+      S->step_gpu_ms += ms;
+      S->step_gpu_n += 1;
+    }
+    cudaGetLastError();
+    S->ev_pending = false;
   }
   S->next_all.assign(S->h_res, S->h_res + B);
   float lp = 0;
@@ -2234,6 +2265,31 @@ int32_t sg_session_step_trace(ArmSession* sess, int32_t on, uint64_t* host, uint
   }
   if (ctas) *ctas = nct;
   return (int32_t)n;
+}
+
+double sg_session_step_gpu_ms(ArmSession* sess, int32_t on) {
+  if (!sess) return -1.0;
+  cudaSetDevice(sess->dev);
+  if (on && !sess->ev_step[0]) {
+    if (cudaEventCreate(&sess->ev_step[0]) != cudaSuccess || cudaEventCreate(&sess->ev_step[1]) != cudaSuccess) {
+      cudaGetLastError();
+      return -1.0;
+    }
+    sess->step_gpu_ms = 0;
+    sess->step_gpu_n = 0;
+    return 0.0;
+  }
+  const double avg = sess->step_gpu_n ? sess->step_gpu_ms / (double)sess->step_gpu_n : 0.0;
+  if (!on) {
+    cudaStreamSynchronize(sess->st);
+    for (cudaEvent_t& e : sess->ev_step)
+      if (e) {
+        cudaEventDestroy(e);
+        e = nullptr;
+      }
+    sess->ev_pending = false;
+  }
+  return avg;
 }
 
 int32_t sg_session_step_kernel(const ArmSession* sess, const char** why) {

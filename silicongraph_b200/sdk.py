@@ -85,6 +85,7 @@ _SIGS = {
     "sg_session_step_kernel": (ctypes.c_int32, [_P, ctypes.POINTER(ctypes.c_char_p)]),
     "sg_session_step_trace": (ctypes.c_int32, [_P, ctypes.c_int32, _P, ctypes.c_uint32,
                                                ctypes.POINTER(ctypes.c_int32)]),
+    "sg_session_step_gpu_ms": (ctypes.c_double, [_P, ctypes.c_int32]),
     "sg_session_create_ex": (_P, [_P, ctypes.POINTER(ArmSessionOptions), ctypes.c_uint32, ctypes.c_int32,
                                   ctypes.c_int32, ctypes.POINTER(ctypes.c_uint8)]),
     "sg_batch_prefill": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32]),
@@ -337,6 +338,14 @@ class Session:
         why = ctypes.c_char_p()
         on = bool(lib().sg_session_step_kernel(self.h, ctypes.byref(why)))
         return on, (why.value.decode() if why.value else None)
+
+    def step_gpu_ms(self, on: bool) -> float:
+        """Device time of decode steps: step_gpu_ms(True) starts timing;
+        step_gpu_ms(False) stops and returns the mean ms per step."""
+        v = lib().sg_session_step_gpu_ms(self.h, 1 if on else 0)
+        if v < 0:
+            raise ArmError(-5, last_error())
+        return v
 
     def step_trace(self, on: bool = True):
         """Decode-step kernel timeline: step_trace(True) records the following
