@@ -887,6 +887,7 @@ def run_decode(args):
                 for _ in range(16):
                     decode()
                 gpu_ms = s.step_gpu_ms(False)
+                graph_kernels = s.graph_kernels
     decode_s, ttft_s = host_max([t2 - t1, t1 - t0])  # the slowest rank
     tps = steps / decode_s
     seqs = args.batch * (1 if tp else world)  # sequences decoded at once over the whole job
@@ -917,10 +918,8 @@ def run_decode(args):
                      "achieved_basis": "(weights + KV cache of every sequence) bytes per step x steps/s, per GPU"},
         "e2e": {"value": round(seqs * tps, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 8},
-        # per layer: 2 rmsnorm, q|k|v, rope + KV append, attention, o, gate|up, down,
-        # SwiGLU unless fused into down (one sequence), 2 all-reduces (tensor-parallel);
-        # per step: embedding, final rmsnorm, LM head, greedy pick (2 kernels)
-        "gpu_launches": steps * (c["layers"] * (8 + (0 if args.batch == 1 else 1) + (2 if tp else 0)) + 5),
+        # this library's kernel nodes in the captured decode step (counted in the graph; NCCL's excluded)
+        "gpu_launches": steps * graph_kernels if graph_kernels > 0 else None,
         "clocks": clk,
         "first_token": int(first),
     }

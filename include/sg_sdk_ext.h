@@ -151,6 +151,11 @@ int32_t sg_session_step_trace(ArmSession* sess, int32_t on, uint64_t* host, uint
  * ArmInferenceResult.tpot_ms. */
 double sg_session_step_gpu_ms(ArmSession* sess, int32_t on);
 
+/* Kernel launches in one captured decode step (the kernel nodes of the
+ * session's decode graph whose kernels are this library's: NCCL's excluded), or -1 before the
+ * graph exists (the second decode step captures it) or when steps run eagerly. */
+int32_t sg_session_graph_kernels(const ArmSession* sess);
+
 /* Prefills every sequence with n_tokens tokens (tokens[b * n_tokens + i] is
  * token i of sequence b). */
 ArmStatus sg_batch_prefill(ArmSession* sess, const int32_t* tokens, uint32_t n_tokens);

@@ -2267,6 +2267,36 @@ int32_t sg_session_step_trace(ArmSession* sess, int32_t on, uint64_t* host, uint
   return (int32_t)n;
 }
 
+int32_t sg_session_graph_kernels(const ArmSession* sess) {
+  if (!sess || !sess->graph) return -1;
+  size_t n = 0;
+  if (cudaGraphGetNodes(sess->graph, nullptr, &n) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  std::vector<cudaGraphNode_t> nodes(n);
+  if (n && cudaGraphGetNodes(sess->graph, nodes.data(), &n) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  // only this library's kernels: a kernel node's function lies in this shared object
+  Dl_info self{};
+  const bool know_self = dladdr(reinterpret_cast<void*>(&sg_session_graph_kernels), &self) != 0 && self.dli_fname;
+  int k = 0;
+  for (size_t i = 0; i < n; ++i) {
+    cudaGraphNodeType t;
+    if (cudaGraphNodeGetType(nodes[i], &t) != cudaSuccess || t != cudaGraphNodeTypeKernel) continue;
+    cudaKernelNodeParams kp{};
+    Dl_info where{};
+    if (know_self && cudaGraphKernelNodeGetParams(nodes[i], &kp) == cudaSuccess && kp.func &&
+        dladdr(kp.func, &where) != 0 && where.dli_fname && strcmp(where.dli_fname, self.dli_fname) != 0)
+      continue;  // another library's kernel (NCCL's collectives)
+    ++k;
+  }
+  cudaGetLastError();
+  return k;
+}
+
 double sg_session_step_gpu_ms(ArmSession* sess, int32_t on) {
   if (!sess) return -1.0;
   cudaSetDevice(sess->dev);

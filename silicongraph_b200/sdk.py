@@ -86,6 +86,7 @@ _SIGS = {
     "sg_session_step_trace": (ctypes.c_int32, [_P, ctypes.c_int32, _P, ctypes.c_uint32,
                                                ctypes.POINTER(ctypes.c_int32)]),
     "sg_session_step_gpu_ms": (ctypes.c_double, [_P, ctypes.c_int32]),
+    "sg_session_graph_kernels": (ctypes.c_int32, [_P]),
     "sg_session_create_ex": (_P, [_P, ctypes.POINTER(ArmSessionOptions), ctypes.c_uint32, ctypes.c_int32,
                                   ctypes.c_int32, ctypes.POINTER(ctypes.c_uint8)]),
     "sg_batch_prefill": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32]),
@@ -338,6 +339,11 @@ class Session:
         why = ctypes.c_char_p()
         on = bool(lib().sg_session_step_kernel(self.h, ctypes.byref(why)))
         return on, (why.value.decode() if why.value else None)
+
+    @property
+    def graph_kernels(self) -> int:
+        """Kernel launches in one captured decode step (-1 before capture or when eager)."""
+        return lib().sg_session_graph_kernels(self.h)
 
     def step_gpu_ms(self, on: bool) -> float:
         """Device time of decode steps: step_gpu_ms(True) starts timing;
