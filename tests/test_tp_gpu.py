@@ -18,6 +18,9 @@ pytestmark = pytest.mark.gpu
 
 SMALL = armpack.llama_config(layers=2, hidden=256, heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=1008,
                              rope_theta=500000.0, max_pos=4096)
+# eight ranks need a query head each
+SMALL8 = armpack.llama_config(layers=2, hidden=512, heads=8, kv_heads=2, head_dim=64, ffn=1024, vocab=1008,
+                              rope_theta=500000.0, max_pos=4096)
 RTOL, ATOL = 1e-2, 2e-3
 STEPS = 4
 
@@ -51,23 +54,26 @@ def _worker(rank, world, uid, path, prompt, batch, p2p, out_dir):
              toks=np.array(toks), lo=lo, hi=hi)
 
 
-@pytest.mark.parametrize("world,batch,p2p", [(2, 1, True), (2, 2, True), (2, 2, False)],
-                         ids=["peer-allreduce", "batch2-peer-allreduce", "batch2-nccl"])
+@pytest.mark.parametrize("world,batch,p2p", [(2, 1, True), (2, 2, True), (2, 2, False), (4, 1, True), (4, 2, False),
+                                             (8, 1, True)],
+                         ids=["peer-allreduce", "batch2-peer-allreduce", "batch2-nccl", "world4-peer-allreduce",
+                              "world4-batch2-nccl", "world8-peer-allreduce"])
 def test_tp_session_matches_decoder_oracle(sg, oracle_mod, tmp_path, world, batch, p2p):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     from oracle.decoder import DecoderOracle
     from silicongraph_b200 import sdk
-    w = armpack.random_llama_weights(SMALL, seed=4)
-    t = armpack.cuda_tensors(SMALL, w, group_size=32)
-    path = armpack.write_package(str(tmp_path / "tp.armpack"), SMALL, t, max_context=256, max_prefill_chunk=64)
-    prompt = np.random.default_rng(9).integers(0, SMALL["vocab_size"], (batch, 90)).astype(np.int32)  # 2 chunks
+    cfg = SMALL8 if world > 4 else SMALL
+    w = armpack.random_llama_weights(cfg, seed=4)
+    t = armpack.cuda_tensors(cfg, w, group_size=32)
+    path = armpack.write_package(str(tmp_path / "tp.armpack"), cfg, t, max_context=256, max_prefill_chunk=64)
+    prompt = np.random.default_rng(9).integers(0, cfg["vocab_size"], (batch, 90)).astype(np.int32)  # 2 chunks
     uid = sdk.tp_unique_id()
     mp.start_processes(_worker, args=(world, uid, path, prompt, batch, p2p, str(tmp_path)), nprocs=world,
                        join=True, start_method="spawn")
     ranks = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
     assert [int(r["lo"]) for r in ranks] == sorted(int(r["lo"]) for r in ranks)
-    assert int(ranks[-1]["hi"]) == SMALL["vocab_size"]
+    assert int(ranks[-1]["hi"]) == cfg["vocab_size"]
     for r in ranks[1:]:
         assert np.array_equal(r["toks"], ranks[0]["toks"])  # every rank emits the same tokens
     logits = np.concatenate([r["logits"] for r in ranks], axis=2)  # [steps + 1, batch, vocab]
@@ -84,7 +90,7 @@ def test_tp_session_matches_decoder_oracle(sg, oracle_mod, tmp_path, world, batc
             assert tok == int(np.argmax(want))
 
     for b in range(batch):
-        ref = DecoderOracle(SMALL, t, group_size=32)
+        ref = DecoderOracle(cfg, t, group_size=32)
         want = ref.forward(prompt[b])
         close(logits[0, b], want)
         check_token(int(toks[0][b]), want)
