@@ -481,6 +481,15 @@ SgStatus dense_run(const char* name, const SgMatMulParams* p, void* stream, bool
       if (handled || st != SG_OK) return st;
     }
   }
+  // One float activation row: the int8 tensor-core GEMV when a cluster split fills the GPU.
+  if (kind == W_INT8_FA && p->M == 1 && p->bias == nullptr) {
+    int* err = nullptr;
+    st = sg::device_error_word(&err);
+    if (st != SG_OK) return st;
+    bool handled = false;
+    st = sg::w8_gemv_mma_run(p, cs, sg::sm_count(dev), err, &handled);
+    if (handled || st != SG_OK) return st;
+  }
   const Plan pl = make_plan(kind, p, sg::sm_count(dev));
   if (!pl.fast) {
     dim3 grid((p->N + 127) / 128, p->M);

@@ -397,6 +397,7 @@ size_t w4_gemv_mma_scratch_bytes(const SgMatMulParams* p, int sms, bool* applica
 SgStatus w4_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, void* ws, size_t ws_bytes,
                          int* err_word, bool* handled, const SgRopeAppend* rope = nullptr);
 bool w4_gemv_mma_tuning(std::string_view key, int value);
+bool w8_gemv_mma_tuning(std::string_view key, int value);
 SgStatus w4_rows_run(const SgMatMulParams* p, cudaStream_t cs, int sms, int* err_word, bool* handled);
 bool w4_rows_tuning(std::string_view key, int value);
 bool gemm_tc_tuning(std::string_view key, int value);
@@ -655,6 +656,7 @@ int32_t sg_set_tuning(const char* key, int32_t value) {
     return SG_OK;
   }
   if (key && sg::w4_gemv_mma_tuning(std::string_view(key), value)) return SG_OK;
+  if (key && sg::w8_gemv_mma_tuning(std::string_view(key), value)) return SG_OK;
   if (key && sg::w4_rows_tuning(std::string_view(key), value)) return SG_OK;
   if (key && sg::gemm_tc_tuning(std::string_view(key), value)) return SG_OK;
   if (key && sg::attn_tc_tuning(std::string_view(key), value)) return SG_OK;
