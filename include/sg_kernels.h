@@ -179,6 +179,8 @@ int32_t sg_device_error_check(void* stream);
  *   "w4_gemv_mma.variant"      tensor-core GEMV launch shape (0 default .. 3)
  *   "w4_gemv_mma.sleep"        tensor-core GEMV: sleep between stage polls (0/1)
  *   "w4_gemv_mma.cluster"      tensor-core GEMV: allow the cluster-reduced split (1, default) or not (0)
+ *   "attn_tc.pair"             tensor-core flash attention: two 128-query tiles per CTA (1, default)
+ *                              or one (0); the same bits either way
  *   "w8_gemv_mma.enable"       INT8 per-channel GEMV, one float activation row: the int8 tensor-core
  *                              kernel (1, default) or the dp4a kernel (0)
  *   "tp_allreduce.wait_ms"     peer all-reduce: how long a rank waits for the others' flags

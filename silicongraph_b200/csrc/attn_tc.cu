@@ -422,6 +422,375 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Two query tiles per CTA (attn_tc2_kernel): tiles A (queries q0 ..) and B
+// (q0 + 128 ..) of one head share the K and V tiles; 8 softmax warps (4 per
+// tile, two per scheduler) and one MMA issuer that interleaves the tiles,
+//   QK_A(0) QK_B(0) | PV_A(j) QK_A(j+1) | PV_B(j) QK_B(j+1) | ...
+// so that while one tile's softmax runs, the tensor pipe works on the other
+// tile's products.  Each tile has one S/P buffer in TMEM (QK_t(j+1) is issued
+// after PV_t(j), and the tensor pipe runs them in order) and its own O:
+// tile t at TMEM columns 256 t (S/P) and 256 t + 128 (O).  The arithmetic per
+// row is the single-tile kernel's (same softmax, masks, rescaling rule and
+// rounding), so both kernels give the same bits.
+constexpr int kWarpK2 = 8, kWarpV2 = 9, kWarpMma2 = 10;
+constexpr int kThreads2 = 11 * 32;
+
+template <int D>
+struct ACfg2 {
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kBox = 128 * 128;
+  static constexpr int kTile = kBoxes * kBox;
+  static constexpr int kQOff = 0;  // Q tiles A and B
+  static constexpr int kKOff = 2 * kTile;
+  static constexpr int kVOff = kKOff + kStages * kTile;
+  static constexpr int kBarOff = kVOff + kStages * kTile;
+  static constexpr int kBars = 1 + 4 * kStages + 2 + 2 + 2 + 1;
+  static constexpr int kSmem0 = kBarOff + kBars * 8 + 16 + 1024;
+  static constexpr int kSmem = kSmem0 < 120 * 1024 ? 120 * 1024 : kSmem0;
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreads2, 1)
+    attn_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, TArgs a) {
+  using C_ = ACfg2<D>;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = sgd::align_smem_1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C_::kBarOff);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + kStages;
+  uint64_t* v_full = k_empty + kStages;
+  uint64_t* v_empty = v_full + kStages;
+  uint64_t* s_full = v_empty + kStages;  // [tile]
+  uint64_t* p_full = s_full + 2;         // [tile]
+  uint64_t* o_ready = p_full + 2;        // [tile]
+  uint64_t* done = o_ready + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Work item: the heaviest pairs of query tiles (most keys under a causal mask) first.
+  const int hb_count = a.H * a.B;
+  const int n_pairs = (a.n_qt + 1) / 2;
+  const int pr = n_pairs - 1 - (int)(blockIdx.x / hb_count);
+  const int hb = (int)(blockIdx.x % hb_count);
+  const int h = hb % a.H, b = hb / a.H;
+  const int hkv = h / a.G;
+  const int q0 = pr * 2 * kQT;
+  const int kv_tiles_all = (a.Skv + kKT - 1) / kKT;
+  int n_t[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int qa = q0 + t * kQT;
+    const int q_last = min(qa + kQT, a.Sq) - 1;
+    n_t[t] = qa >= a.Sq ? 0 : (a.causal ? min(kv_tiles_all, (a.q_pos0 + q_last) / kKT + 1) : kv_tiles_all);
+  }
+  const int n_kv = max(n_t[0], n_t[1]);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&o_ready[t], 1);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kWarpMma2) {
+    tmem_alloc(tslot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == kWarpK2 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+  }
+  if (warp == kWarpV2 && lane == 0) tma_prefetch_desc(&tmV);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  pdl_wait();
+
+  if (warp == kWarpK2 || warp == kWarpV2) {
+    // ------------------------------------------------------------ loaders (as in attn_tc_kernel)
+    const bool is_k = warp == kWarpK2;
+    const CUtensorMap* map = is_k ? &tmK : &tmV;
+    uint64_t* fullb = is_k ? k_full : v_full;
+    uint64_t* emptyb = is_k ? k_empty : v_empty;
+    unsigned char* base = smem + (is_k ? C_::kKOff : C_::kVOff);
+    const bool paged = is_k ? a.paged_k : a.paged_v;
+    auto page_of = [&](int j) -> int {
+      const int lp = j * kPagesPerTile + lane;
+      int pg = 0;
+      if (lane < kPagesPerTile && j < n_kv && lp * kPageRows < a.Skv) {
+        pg = __ldg(a.pt + (int64_t)b * a.pt_bs + (int64_t)lp * a.pt_ps);
+        if ((unsigned)pg >= (unsigned)a.npages) {
+          atomicOr(a.err, 4);
+          pg = 0;
+        }
+      }
+      return pg;
+    };
+    if (is_k && lane == 0) {
+      const int nq = n_t[1] > 0 ? 2 : 1;
+      mbar_arrive_expect_tx(q_full, nq * C_::kTile);
+      for (int t = 0; t < nq; ++t)
+        for (int bx = 0; bx < C_::kBoxes; ++bx)
+          tma_load_3d(smem + C_::kQOff + t * C_::kTile + bx * C_::kBox, &tmQ, bx * 64, q0 + t * kQT, hb, q_full);
+    }
+    uint32_t issued[kStages] = {0, 0};
+    int pg_next = paged ? page_of(0) : 0;
+    for (int j = 0; j < n_kv; ++j) {
+      const int st = j % kStages;
+      const uint32_t use = j / kStages;
+      const int pg_cur = pg_next;
+      if (paged) pg_next = page_of(j + 1);
+      int ok = 1;
+      if (lane == 0) ok = (!*abort_flag && mbar_wait(&emptyb[st], (use & 1) ^ 1, a.err)) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) *abort_flag = 1;
+        break;
+      }
+      if (paged) {
+        int pages[kPagesPerTile];
+#pragma unroll
+        for (int i = 0; i < kPagesPerTile; ++i) pages[i] = __shfl_sync(0xffffffffu, pg_cur, i);
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&fullb[st], C_::kTile);
+#pragma unroll
+          for (int i = 0; i < kPagesPerTile; ++i)
+            for (int bx = 0; bx < C_::kBoxes; ++bx)
+              tma_load_4d(base + st * C_::kTile + bx * C_::kBox + i * kPageRows * 128, map, bx * 64, 0, hkv,
+                          pages[i], &fullb[st]);
+        }
+      } else if (lane == 0) {
+        mbar_arrive_expect_tx(&fullb[st], C_::kTile);
+        for (int bx = 0; bx < C_::kBoxes; ++bx)
+          tma_load_4d(base + st * C_::kTile + bx * C_::kBox, map, bx * 64, j * kKT, hkv, b, &fullb[st]);
+      }
+      issued[st] = use + 1;
+    }
+    if (lane == 0) {
+      for (int st = 0; st < kStages; ++st)
+        if (issued[st]) mbar_wait(&fullb[st], (issued[st] - 1) & 1, a.err);
+      if (is_k) mbar_wait(q_full, 0, a.err);
+    }
+  } else if (warp == kWarpMma2) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_qk = umma_idesc_f16(kQT, kKT, BF16 ? 1 : 0, 0, 0);
+      const uint32_t idesc_pv = umma_idesc_f16(kQT, D, 0, 0, 1);
+      bool ok = mbar_wait(q_full, 0, a.err);
+      auto wait_k = [&](int j) -> bool {
+        if (*abort_flag || !mbar_wait(&k_full[j % kStages], (j / kStages) & 1, a.err)) return false;
+        tc_fence_after();
+        return true;
+      };
+      auto qk = [&](int t, int j) {  // S_t = Q_t K_j^T
+        const int st = j % kStages;
+        const uint32_t d = tbase + 256 * t;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int bx = kk / 4, off = (kk % 4) * 32;
+          const uint64_t ad = umma_smem_desc(smem_u32(smem + C_::kQOff + t * C_::kTile + bx * C_::kBox + off), 16,
+                                             1024, kSwizzle128B);
+          const uint64_t bd =
+              umma_smem_desc(smem_u32(smem + C_::kKOff + st * C_::kTile + bx * C_::kBox + off), 16, 1024, kSwizzle128B);
+          umma_f16_ss(d, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[t]);
+      };
+      auto pv = [&](int t, int j) {  // O_t += P_t V_j
+        const int st = j % kStages;
+        const uint32_t ap = tbase + 256 * t;
+#pragma unroll
+        for (int kk = 0; kk < kKT / 16; ++kk) {
+          const uint64_t bd = umma_smem_desc(smem_u32(smem + C_::kVOff + st * C_::kTile + kk * 2048), C_::kBox, 1024,
+                                             kSwizzle128B);
+          umma_f16_ts(tbase + 256 * t + 128, ap + kk * 8, bd, idesc_pv, (j | kk) != 0 ? 1u : 0u);
+        }
+        umma_commit(&o_ready[t]);
+      };
+      if (ok && n_kv > 0) {
+        ok = wait_k(0);
+        if (ok) {
+          if (n_t[0] > 0) qk(0, 0);
+          if (n_t[1] > 0) qk(1, 0);
+          umma_commit(&k_empty[0]);
+        }
+      }
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = j % kStages;
+        bool v_waited = false, k_next = false;
+        if (j < n_t[0]) {
+          if (*abort_flag || !mbar_wait(&p_full[0], j & 1, a.err) ||
+              !mbar_wait(&v_full[st], (j / kStages) & 1, a.err)) {
+            ok = false;
+            break;
+          }
+          v_waited = true;
+          tc_fence_after();
+          pv(0, j);
+          if (j + 1 < n_t[0]) {
+            if (!(ok = wait_k(j + 1))) break;
+            k_next = true;
+            qk(0, j + 1);
+          }
+        }
+        if (j < n_t[1]) {
+          if (*abort_flag || !mbar_wait(&p_full[1], j & 1, a.err) ||
+              (!v_waited && !mbar_wait(&v_full[st], (j / kStages) & 1, a.err))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          pv(1, j);
+        }
+        umma_commit(&v_empty[st]);  // V_j: both products issued
+        if (j + 1 < n_t[1]) {
+          if (!k_next && !(ok = wait_k(j + 1))) break;
+          k_next = true;
+          qk(1, j + 1);
+        }
+        if (k_next) umma_commit(&k_empty[(j + 1) % kStages]);  // K_{j+1}: every product issued
+      }
+      if (!ok) *abort_flag = 1;
+      umma_commit(done);
+      mbar_wait(done, 0, a.err);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue, tile warp / 4
+    const int t = warp >> 2, quarter = warp & 3;
+    const int nt = n_t[t];
+    const float scale_log2 = a.dscale ? a.scale_log2 * a.dscale[0] : a.scale_log2;
+    const int r = quarter * 32 + lane;  // query row in the tile = TMEM lane
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    const int q = q0 + t * kQT + r;
+    const int q_pos = a.q_pos0 + q;
+    const uint32_t scol = tbase + lane_addr + 256 * t;
+    const uint32_t ocol = scol + 128;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      __syncwarp();
+      if (*abort_flag) {
+        ok = false;
+        break;
+      }
+      warp_wait_all(&s_full[t], j & 1, a.err, abort_flag);
+      tc_fence_after();
+      uint32_t sr[kKT];
+#pragma unroll
+      for (int c = 0; c < kKT / 32; ++c)
+        tmem_ld_32x32b_x32(scol + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+      tmem_ld_wait();
+      const int key0 = j * kKT;
+      const int lim = min(a.causal ? q_pos : 0x7fffffff, a.Skv - 1) - key0;
+      if (__any_sync(0xffffffffu, lim < kKT - 1)) {
+#pragma unroll
+        for (int i = 0; i < kKT; ++i)
+          if (i > lim) sr[i] = __float_as_uint(-INFINITY);
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < kKT; i += 2) mx = fmax3(mx, __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
+      mx *= scale_log2;
+      float alpha = 1.f;
+      const bool rescale = mx > m + kRescaleThreshold;
+      if (rescale) {
+        alpha = ex2(m - mx);
+        m = mx;
+        l *= alpha;
+      }
+      const float neg_m = -m;
+      float sum = 0.f;
+      uint32_t pk[kKT / 2];
+#pragma unroll
+      for (int i = 0; i < kKT / 2; ++i) {
+        const float p0 = ex2(fmaf(__uint_as_float(sr[2 * i]), scale_log2, neg_m));
+        const float p1 = ex2(fmaf(__uint_as_float(sr[2 * i + 1]), scale_log2, neg_m));
+        pk[i] = pack2<false>(p0, p1);
+        sum += sum2<false>(pk[i]);
+      }
+      l += sum;
+      tmem_st_32x32b_x16(scol, *reinterpret_cast<uint32_t(*)[16]>(&pk[0]));
+      tmem_st_32x32b_x16(scol + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[16]));
+      tmem_st_32x32b_x16(scol + 32, *reinterpret_cast<uint32_t(*)[16]>(&pk[32]));
+      tmem_st_32x32b_x16(scol + 48, *reinterpret_cast<uint32_t(*)[16]>(&pk[48]));
+      if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+        warp_wait_all(&o_ready[t], (j - 1) & 1, a.err, abort_flag);
+        tc_fence_after();
+#pragma unroll 1
+        for (int dc = 0; dc < D / 32; ++dc) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(ocol + dc * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st_32x32b_x16(ocol + dc * 32, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
+          tmem_st_32x32b_x16(ocol + dc * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+    }
+    if (ok && nt > 0) {
+      warp_wait_all(&o_ready[t], (nt - 1) & 1, a.err, abort_flag);
+      tc_fence_after();
+      const float inv_l = 1.f / l;
+      typedef typename std::conditional<BF16, __nv_bfloat16, __half>::type T;
+      T* orow = static_cast<T*>(a.O) + ((size_t)hb * a.Sq + q) * D;
+      float* orow32 = static_cast<float*>(a.O) + ((size_t)hb * a.Sq + q) * D;
+      const float omul = a.dscale ? inv_l * a.dscale[1] : inv_l;
+#pragma unroll 1
+      for (int dc = 0; dc < D / 32; ++dc) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(ocol + dc * 32, o);
+        tmem_ld_wait();
+        if (a.o_f32) {
+          if (q < a.Sq) {
+            float4* dst = reinterpret_cast<float4*>(orow32 + dc * 32);
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              dst[v] = make_float4(__uint_as_float(o[4 * v]) * omul, __uint_as_float(o[4 * v + 1]) * omul,
+                                   __uint_as_float(o[4 * v + 2]) * omul, __uint_as_float(o[4 * v + 3]) * omul);
+          }
+          continue;
+        }
+        uint32_t pkd[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          pkd[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
+        if (q < a.Sq) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + dc * 32);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pkd[4 * v], pkd[4 * v + 1], pkd[4 * v + 2], pkd[4 * v + 3]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma2) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
 // V [B, Hkv, Skv, D] bf16 (strided) -> contiguous fp16, 8 values per thread.
 // bf16 V -> contiguous fp16 [B][Hkv][Skv][D]; from a paged cache when pt != NULL
 // (kv_bs is then the page stride).
@@ -558,29 +927,29 @@ __global__ void __launch_bounds__(256) f32_to_f16_scaled_kernel(const float* q, 
   }
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool PAIR>
 SgStatus launch_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const TArgs& a, int grid,
                    cudaStream_t cs) {
-  using C_ = ACfg<D>;
-  auto kfn = attn_tc_kernel<D, BF16>;
+  const int smem = PAIR ? ACfg2<D>::kSmem : ACfg<D>::kSmem;
+  auto kfn = PAIR ? attn_tc2_kernel<D, BF16> : attn_tc_kernel<D, BF16>;
   static std::atomic<uint64_t> attr_set{0};
   int dev = 0;
   SgStatus st = sg::current_device(&dev);
   if (st != SG_OK) return st;
   const uint64_t bit = dev < 64 ? (uint64_t)1 << dev : 0;
   if (!(attr_set.load() & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::kSmem);
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) {
       cudaGetLastError();
-      sg::set_error("attn_tc_kernel: cannot reserve %d bytes of shared memory: %s", C_::kSmem, cudaGetErrorString(e));
+      sg::set_error("attn_tc_kernel: cannot reserve %d bytes of shared memory: %s", smem, cudaGetErrorString(e));
       return SG_ERR_RUNTIME;
     }
     attr_set.fetch_or(bit);
   }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = C_::kSmem;
+  cfg.blockDim = dim3(PAIR ? kThreads2 : kThreads);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = cs;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -597,6 +966,7 @@ SgStatus launch_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorM
 }
 
 std::atomic<int> g_tune_attn_tc{1};    // 0: tensor-core attention off
+std::atomic<int> g_tune_attn_pair{1};  // 1: two query tiles per CTA (attn_tc2_kernel)
 std::atomic<int> g_tune_attn_min_s{256};  // shortest query length sent to it
 
 }  // namespace
@@ -838,15 +1208,26 @@ SgStatus attn_tc_run16(const SgFlashAttentionParams* p, cudaStream_t cs, void* w
     a.paged_k = 1;
     a.paged_v = io != SG_DT_BF16;
   }
-  const int grid = a.n_qt * a.H * a.B;
   *handled = true;
-  if (D == 64) return io == SG_DT_BF16 ? launch_tc<64, true>(tq, tk, tv, a, grid, cs)
-                                       : launch_tc<64, false>(tq, tk, tv, a, grid, cs);
-  return io == SG_DT_BF16 ? launch_tc<128, true>(tq, tk, tv, a, grid, cs)
-                          : launch_tc<128, false>(tq, tk, tv, a, grid, cs);
+  if (g_tune_attn_pair.load()) {
+    const int grid = ((a.n_qt + 1) / 2) * a.H * a.B;
+    if (D == 64) return io == SG_DT_BF16 ? launch_tc<64, true, true>(tq, tk, tv, a, grid, cs)
+                                         : launch_tc<64, false, true>(tq, tk, tv, a, grid, cs);
+    return io == SG_DT_BF16 ? launch_tc<128, true, true>(tq, tk, tv, a, grid, cs)
+                            : launch_tc<128, false, true>(tq, tk, tv, a, grid, cs);
+  }
+  const int grid = a.n_qt * a.H * a.B;
+  if (D == 64) return io == SG_DT_BF16 ? launch_tc<64, true, false>(tq, tk, tv, a, grid, cs)
+                                       : launch_tc<64, false, false>(tq, tk, tv, a, grid, cs);
+  return io == SG_DT_BF16 ? launch_tc<128, true, false>(tq, tk, tv, a, grid, cs)
+                          : launch_tc<128, false, false>(tq, tk, tv, a, grid, cs);
 }
 
 bool attn_tc_tuning(std::string_view key, int value) {
+  if (key == "attn_tc.pair") {
+    g_tune_attn_pair.store(value);
+    return true;
+  }
   if (key == "attn_tc.enable") {
     g_tune_attn_tc.store(value);
     return true;
