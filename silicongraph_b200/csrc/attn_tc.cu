@@ -15,8 +15,8 @@
 // The running max moves (and O is rescaled) only when a row's max grows by
 // more than 2^8 in exp2 units; otherwise P is taken against the old max, at
 // most 2^8, which the 16-bit P and fp32 sums hold exactly enough.  The final
-// O / l is invariant to the reference point of the max, and l sums the same
-// rounded 16-bit weights that PV multiplies, so O stays a weighted average.
+// O / l is invariant to the reference point of the max; l sums the fp32
+// weights whose 16-bit roundings PV multiplies (within 2^-12 of each other).
 //
 // Warps: 0..3 softmax + epilogue (TMEM lane quarter = warp), 4: K loader,
 // 5: V loader, 6: MMA issuer.  K and V tiles have separate two-stage rings:
@@ -90,14 +90,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
-}
-
-// The two 16-bit values of a packed pair, back in fp32.
-template <bool BF16>
-__device__ __forceinline__ float sum2(uint32_t u) {
-  if (BF16) return __uint_as_float(u << 16) + __uint_as_float(u & 0xffff0000u);
-  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u));
-  return f.x + f.y;
 }
 
 template <bool BF16>
@@ -342,17 +334,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         m = mx;
         l *= alpha;
       }
-      const float neg_m = -m;
-      float sum = 0.f;
+      // packed fp32x2 arithmetic for the scale-and-shift and the sum (the softmax is
+      // issue-bound); l sums the fp32 weights as two interleaved partial sums (their
+      // fp16 roundings, which PV multiplies, differ from them by 2^-12 at most)
+      const float2 sl2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(-m, -m), one2 = make_float2(1.f, 1.f);
+      float2 sum2v = make_float2(0.f, 0.f);
       uint32_t pk[kKT / 2];
 #pragma unroll
       for (int i = 0; i < kKT / 2; ++i) {
-        const float p0 = ex2(fmaf(__uint_as_float(sr[2 * i]), scale_log2, neg_m));
-        const float p1 = ex2(fmaf(__uint_as_float(sr[2 * i + 1]), scale_log2, neg_m));
-        pk[i] = pack2<false>(p0, p1);
-        sum += sum2<false>(pk[i]);  // l sums the rounded weights that PV multiplies
+        const float2 x = ffma2(make_float2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), sl2, nm2);
+        const float2 p = make_float2(ex2(x.x), ex2(x.y));
+        pk[i] = pack2<false>(p.x, p.y);
+        sum2v = ffma2(p, one2, sum2v);
       }
-      l += sum;
+      l += sum2v.x + sum2v.y;
       tmem_st_32x32b_x16(scol, *reinterpret_cast<uint32_t(*)[16]>(&pk[0]));
       tmem_st_32x32b_x16(scol + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[16]));
       tmem_st_32x32b_x16(scol + 32, *reinterpret_cast<uint32_t(*)[16]>(&pk[32]));
@@ -713,17 +708,18 @@ __global__ void __launch_bounds__(kThreads2, 1)
         m = mx;
         l *= alpha;
       }
-      const float neg_m = -m;
-      float sum = 0.f;
+      // as in attn_tc_kernel: packed fp32x2 scale-and-shift and sum of the fp32 weights
+      const float2 sl2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(-m, -m), one2 = make_float2(1.f, 1.f);
+      float2 sum2v = make_float2(0.f, 0.f);
       uint32_t pk[kKT / 2];
 #pragma unroll
       for (int i = 0; i < kKT / 2; ++i) {
-        const float p0 = ex2(fmaf(__uint_as_float(sr[2 * i]), scale_log2, neg_m));
-        const float p1 = ex2(fmaf(__uint_as_float(sr[2 * i + 1]), scale_log2, neg_m));
-        pk[i] = pack2<false>(p0, p1);
-        sum += sum2<false>(pk[i]);
+        const float2 x = ffma2(make_float2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), sl2, nm2);
+        const float2 p = make_float2(ex2(x.x), ex2(x.y));
+        pk[i] = pack2<false>(p.x, p.y);
+        sum2v = ffma2(p, one2, sum2v);
       }
-      l += sum;
+      l += sum2v.x + sum2v.y;
       tmem_st_32x32b_x16(scol, *reinterpret_cast<uint32_t(*)[16]>(&pk[0]));
       tmem_st_32x32b_x16(scol + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[16]));
       tmem_st_32x32b_x16(scol + 32, *reinterpret_cast<uint32_t(*)[16]>(&pk[32]));
