@@ -1205,7 +1205,12 @@ SgStatus attn_tc_run16(const SgFlashAttentionParams* p, cudaStream_t cs, void* w
     a.paged_v = io != SG_DT_BF16;
   }
   *handled = true;
-  if (g_tune_attn_pair.load()) {
+  // two query tiles per CTA when the pairs still fill the GPU (small problems keep
+  // the wider grid of one tile per CTA)
+  int dev = 0;
+  st = sg::current_device(&dev);
+  if (st != SG_OK) return st;
+  if (g_tune_attn_pair.load() && (int64_t)((a.n_qt + 1) / 2) * a.H * a.B >= sg::sm_count(dev)) {
     const int grid = ((a.n_qt + 1) / 2) * a.H * a.B;
     if (D == 64) return io == SG_DT_BF16 ? launch_tc<64, true, true>(tq, tk, tv, a, grid, cs)
                                          : launch_tc<64, false, true>(tq, tk, tv, a, grid, cs);
