@@ -183,6 +183,17 @@ int32_t sg_device_error_check(void* stream);
  *                              or one (0); the same bits either way
  *   "w8_gemv_mma.enable"       INT8 per-channel GEMV, one float activation row: the int8 tensor-core
  *                              kernel (1, default) or the dp4a kernel (0)
+ *   "gemm_tc.bt"               prefill GEMM token tile: 128, 192 or 256 (0 = heuristic)
+ *   "gemm_tc.par"              prefill GEMM dequant warp groups on alternate k steps (1 or 2, default)
+ *   "gemm_tc.split"            prefill GEMM: a last round of tiles that fills at most half the SMs runs
+ *                              as two k halves per tile on two SMs (1, default; needs the scratch
+ *                              the workspace query reports) or whole (0)
+ *   "gemm_tc.pair"             prefill GEMM on clusters of two CTAs sharing each MMA (tcgen05
+ *                              cta_group::2, 256-column tiles): 0 never (default), 1 when the tiles
+ *                              fill the pairs, 2 whenever the token tile is 256
+ *   "gemm_tc.tma_store"        prefill GEMM 16-bit C through TMA stores (1, default) or direct stores (0)
+ *   "gemm_tc.min_rows"         fewest activation rows sent to the prefill GEMM (default 5)
+ *   "gemm_tc.spin"             prefill GEMM single-thread waits spin on test_wait (0 default)
  *   "tp_allreduce.wait_ms"     peer all-reduce: how long a rank waits for the others' flags
  *                              before it gives up and reports (1 .. 2000 ms; <= 0 restores 2000)
  *   "sdk.fuse_norm", "sdk.fuse_rope", "sdk.fuse_swiglu"

@@ -66,9 +66,13 @@ constexpr int kTmemCols = 512;
 
 enum WKind : int { kW4Grouped = 0, kW8Channel = 1 };
 
-template <int BT, int WK>
+// PAIR: two CTAs of a cluster share one MMA (tcgen05 cta_group::2) over 256
+// weight columns x BT tokens; each holds its 128 columns in TMEM and half of
+// the tokens' activations in shared memory.
+template <int BT, int WK, bool PAIR = false>
 struct Cfg {
-  static constexpr int kActBytes = BT * 128;                             // BT rows x 64 x 16-bit
+  static constexpr int kActRows = PAIR ? BT / 2 : BT;                     // token rows of this CTA
+  static constexpr int kActBytes = kActRows * 128;                       // rows x 64 x 16-bit
   static constexpr int kWBytes = (WK == kW4Grouped ? kKStep / 2 : kKStep) * kWCols;  // packed rows x 128
   static constexpr int kSBytes = (WK == kW4Grouped) ? 4 * kWCols * 2 : 0;          // <= 4 scale rows
   static constexpr int kZBytes = (WK == kW4Grouped) ? 4 * kWCols : 0;              // <= 4 zero rows
@@ -81,12 +85,15 @@ struct Cfg {
   static constexpr int kSlots = kSlots0 > 8 ? 8 : kSlots0;
   static constexpr int kStages0 = (227 * 1024 - 2048 - kOutBufs * kOutBuf) / kStride;
   static constexpr int kStages = kStages0 > 12 ? 12 : kStages0;
-  static constexpr int kBarBytes = (2 * kStages + 2 * kSlots + 2 * 2 + 1) * 8 + 16;
+  static constexpr int kBarBytes = (2 * kStages + 2 * kSlots + 2 * 2 + 2) * 8 + 16;
   static constexpr int kOutOff = kStages * kStride;  // epilogue staging ring
   static constexpr int kBarOff = kOutOff + kOutBufs * kOutBuf;
   static constexpr int kSmem = kBarOff + kBarBytes + 1024;  // + alignment slack
   static_assert(kStages >= 2 && kSlots >= 2, "pipeline needs two stages");
+  static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
   static_assert(BT % 32 == 0 && BT >= 32 && BT <= 256, "token tile");
+  // the other half's fp32 sums of a split tile land in the (then idle) stage ring
+  static_assert(BT * kWCols * 4 <= kStages * kStride, "split-tile partial fits the stage ring");
 };
 
 struct GArgs {
@@ -104,7 +111,117 @@ struct GArgs {
   int spin;       // 1: single-thread waits spin on test_wait
   int tma_store;  // 1: 16-bit C written by TMA stores from shared memory
   int* err;
+  // Work units: tiles 0 .. whole-1 whole, then each remaining tile as two k
+  // halves (units whole .. units-1), which two CTAs of the last round compute.
+  int whole, units;
+  unsigned* tickets;  // [tiles - whole], zero between calls
+  float* partials;    // [tiles - whole][2][BT tokens][128 columns] fp32
 };
+
+// Unit u of the launch: a whole tile, or one k half of a tile of the last
+// round.  Both halves write their fp32 sums to the scratch; the one that
+// finishes second adds the other's and writes C.  The two-term sum does not
+// depend on which half finished first, so results are the same on every run.
+struct Unit {
+  int tile, k0, k1;
+  int slot;  // split tile index (-1: whole tile)
+  int half;
+};
+__device__ __forceinline__ Unit unit_of(const GArgs& a, int u) {
+  Unit r;
+  if (u < a.whole) {
+    r.tile = u;
+    r.k0 = 0;
+    r.k1 = a.ksteps;
+    r.slot = -1;
+    r.half = 0;
+  } else {
+    const int v = u - a.whole, kh = a.ksteps >> 1;
+    r.slot = v >> 1;
+    r.half = v & 1;
+    r.tile = a.whole + r.slot;
+    r.k0 = r.half ? kh : 0;
+    r.k1 = r.half ? a.ksteps : kh;
+  }
+  return r;
+}
+
+// ---------------------------------------------------------------- CTA pairs
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of both CTAs; orders shared-memory writes (barrier inits) before what follows.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive on an mbarrier of CTA 0 of the pair (address from cluster_addr).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait (as mbar_wait) on a barrier that CTAs of the pair arrive on.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (;;) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      record_error(err, kErrWaitTimeout);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_slot)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D (+)= A * B over the pair: M = 256 (A: 128 rows in each CTA's TMEM), B's N
+// columns split between the two CTAs' shared memory at the same address.
+__device__ __forceinline__ void umma_f16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on the barrier at this offset in both CTAs of the pair when the MMAs issued so far complete.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+
+// Bulk copy global -> this CTA's shared memory, completing on an mbarrier.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
 
 __device__ __forceinline__ uint32_t lop3_and_or_u(uint32_t a, uint32_t b, uint32_t c) {
   uint32_t d;
@@ -182,13 +299,15 @@ __device__ __forceinline__ uint16_t to_out16(float v, int dt) {
   return __half_as_ushort(__float2half_rn(v));
 }
 
-// BT tokens per tile; WK weight kind; BF16_OP: operand type (INT8 with bf16 activations); HAS_Z: INT4 zeros.
-template <int BT, int WK, bool BF16_OP, bool HAS_Z, int PAR>
+// BT tokens per tile; WK weight kind; BF16_OP: operand type (INT8 with bf16 activations); HAS_Z: INT4 zeros;
+// PAIR: clusters of two CTAs share each MMA (tiles of 256 weight columns; a.n_tiles counts those).
+template <int BT, int WK, bool BF16_OP, bool HAS_Z, int PAR, bool PAIR>
 __global__ void __launch_bounds__(threads_of(PAR), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmAct, const __grid_constant__ CUtensorMap tmW,
                    const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmZ,
                    const __grid_constant__ CUtensorMap tmC, GArgs a) {
-  using C_ = Cfg<BT, WK>;
+  using C_ = Cfg<BT, WK, PAIR>;
+  constexpr int kTileCols = PAIR ? 2 * kWCols : kWCols;  // weight columns per tile
   constexpr int S = C_::kStages, J = C_::kSlots, kAcc = C_::kAcc;
   constexpr int kWarpAct = warp_tma_act(PAR), kWarpW = warp_tma_w(PAR), kWarpMma = warp_mma(PAR);
   extern __shared__ unsigned char smem_raw[];
@@ -200,30 +319,43 @@ __global__ void __launch_bounds__(threads_of(PAR), 1)
   uint64_t* accfull = aempty + J;
   uint64_t* accempty = accfull + 2;
   uint64_t* done = accempty + 2;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* pfull = done + 1;  // the other half's partial of a split tile has arrived
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(pfull + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+  volatile int* last_half = abort_flag + 1;  // epilogue: this CTA finishes its split tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // In a pair, CTA 0 issues the MMAs: the dequant and epilogue warps of both CTAs
+  // arrive on its afull / accempty, and its commits reach the barriers of both.
+  const uint32_t rank = PAIR ? cluster_rank() : 0;
+  const int cta0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;   // this CTA's (pair's) index
+  const int nctas = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 2);  // one expect_tx arrival per producer
       mbar_init(&empty[s], 1);
     }
     for (int j = 0; j < J; ++j) {
-      mbar_init(&afull[j], kStepWarps);
+      mbar_init(&afull[j], kStepWarps * (PAIR ? 2 : 1));
       mbar_init(&aempty[j], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accfull[i], 1);
-      mbar_init(&accempty[i], kEpiWarps);
+      mbar_init(&accempty[i], kEpiWarps * (PAIR ? 2 : 1));
     }
     mbar_init(done, 1);
+    mbar_init(pfull, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == kWarpMma) {
-    tmem_alloc(tslot, kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tslot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tslot, kTmemCols);
+      tmem_relinquish();
+    }
   }
   if (warp == kWarpAct && lane == 0) tma_prefetch_desc(&tmAct);
   if (warp == kWarpW && lane == 0) {
@@ -234,13 +366,11 @@ __global__ void __launch_bounds__(threads_of(PAR), 1)
   if (warp == 0 && lane == 0 && a.tma_store) tma_prefetch_desc(&tmC);
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();  // both CTAs' barriers exist before either arrives on the other's
   tc_fence_after();
   const uint32_t tbase = *tslot;
   // Inputs written by the preceding kernel on the stream are visible after this.
   pdl_wait();
-
-  const int tiles = a.n_tiles * a.m_tiles;
-  const int ksteps = a.ksteps;
 
   if (warp == kWarpAct || warp == kWarpW) {
     // ------------------------------------------------------------ TMA producers
@@ -256,9 +386,11 @@ __global__ void __launch_bounds__(threads_of(PAR), 1)
       }
       uint32_t g = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-        const int n0 = (tile % a.n_tiles) * kWCols, m0 = (tile / a.n_tiles) * BT;
-        for (int ks = 0; ks < ksteps; ++ks, ++g) {
+      for (int u = cta0; u < a.units && ok; u += nctas) {
+        const Unit un = unit_of(a, u);
+        const int n0 = (un.tile % a.n_tiles) * kTileCols + (int)rank * kWCols;
+        const int m0 = (un.tile / a.n_tiles) * BT + (int)rank * C_::kActRows;
+        for (int ks = un.k0; ks < un.k1; ++ks, ++g) {
           const int s = g % S;
           const uint32_t use = g / S;
           if (*abort_flag || !(a.spin ? mbar_wait_spin(&empty[s], (use & 1) ^ 1, a.err)
@@ -288,27 +420,30 @@ __global__ void __launch_bounds__(threads_of(PAR), 1)
     }
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = umma_idesc_f16(kWCols, BT, BF16_OP ? 1 : 0, 0, 0);
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = umma_idesc_f16(PAIR ? 2 * kWCols : kWCols, BT, BF16_OP ? 1 : 0, 0, 0);
       uint32_t g = 0;
       int lt = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++lt) {
+      for (int u = cta0; u < a.units && ok; u += nctas, ++lt) {
+        const Unit un = unit_of(a, u);
         const int acc = lt % kAcc;
         const uint32_t ause = lt / kAcc;
-        if (*abort_flag || !mbar_wait(&accempty[acc], (ause & 1) ^ 1, a.err)) {
+        if (*abort_flag || !(PAIR ? mbar_wait_cluster(&accempty[acc], (ause & 1) ^ 1, a.err)
+                                  : mbar_wait(&accempty[acc], (ause & 1) ^ 1, a.err))) {
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
         const uint32_t dt = tbase + acc * BT;
-        for (int ks = 0; ks < ksteps; ++ks, ++g) {
+        for (int ks = un.k0; ks < un.k1; ++ks, ++g) {
           const int s = g % S, j = g % J;
           const uint32_t juse = g / J;
-          // The dequant warps arrive on afull[j] only after they observed full[s], which
-          // also covers the activation tile of this stage.
-          if (*abort_flag || !(a.spin ? mbar_wait_spin(&afull[j], juse & 1, a.err)
-                                      : mbar_wait(&afull[j], juse & 1, a.err))) {
+          // The dequant warps (in a pair: of both CTAs) arrive on afull[j] only after they
+          // observed full[s], which also covers the activation tile of this stage.
+          if (*abort_flag || !(PAIR     ? mbar_wait_cluster(&afull[j], juse & 1, a.err)
+                               : a.spin ? mbar_wait_spin(&afull[j], juse & 1, a.err)
+                                        : mbar_wait(&afull[j], juse & 1, a.err))) {
             *abort_flag = 1;
             ok = false;
             break;
@@ -316,17 +451,35 @@ __global__ void __launch_bounds__(threads_of(PAR), 1)
           tc_fence_after();
           const uint64_t bdesc = umma_smem_desc(smem_u32(smem + s * C_::kStride), 16, 1024, kSwizzle128B);
           const uint32_t at = tbase + kAcc * BT + j * 32;
+          if constexpr (PAIR) {
 #pragma unroll
-          for (int kk = 0; kk < kKStep / 16; ++kk)
-            umma_f16_ts(dt, at + kk * 8, bdesc + (uint64_t)(kk * 2), idesc, (ks | kk) != 0 ? 1u : 0u);
-          umma_commit(&empty[s]);
-          umma_commit(&aempty[j]);
+            for (int kk = 0; kk < kKStep / 16; ++kk)
+              umma_f16_ts_pair(dt, at + kk * 8, bdesc + (uint64_t)(kk * 2), idesc,
+                               (ks != un.k0 || kk != 0) ? 1u : 0u);
+            umma_commit_pair(&empty[s]);
+            umma_commit_pair(&aempty[j]);
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < kKStep / 16; ++kk)
+              umma_f16_ts(dt, at + kk * 8, bdesc + (uint64_t)(kk * 2), idesc, (ks != un.k0 || kk != 0) ? 1u : 0u);
+            umma_commit(&empty[s]);
+            umma_commit(&aempty[j]);
+          }
         }
-        if (ok) umma_commit(&accfull[acc]);
+        if (ok) {
+          if constexpr (PAIR)
+            umma_commit_pair(&accfull[acc]);
+          else
+            umma_commit(&accfull[acc]);
+        }
       }
-      umma_commit(done);
-      mbar_wait(done, 0, a.err);
+      if constexpr (PAIR)
+        umma_commit_pair(done);
+      else
+        umma_commit(done);
     }
+    // Every MMA (which in a pair also writes the other CTA's TMEM) is complete before TMEM is freed.
+    if (lane == 0) mbar_wait(done, 0, a.err);
   } else if (warp >= kEpiWarps) {
     // ------------------------------------------------------------ dequant warps
     const int pw = warp - kEpiWarps;
@@ -335,8 +488,9 @@ __global__ void __launch_bounds__(threads_of(PAR), 1)
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     uint32_t g = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-      for (int ks = 0; ks < ksteps; ++ks, ++g) {
+    for (int u = cta0; u < a.units && ok; u += nctas) {
+      const Unit un = unit_of(a, u);
+      for (int ks = un.k0; ks < un.k1; ++ks, ++g) {
         if (PAR > 1 && (int)(g % PAR) != par) continue;
         __syncwarp();
         if (*abort_flag) {  // one shared load of a converged warp: the same value in every lane
@@ -401,7 +555,12 @@ __global__ void __launch_bounds__(threads_of(PAR), 1)
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&afull[j]);
+        if (lane == 0) {
+          if (PAIR && rank != 0)
+            mbar_arrive_remote(cluster_addr(&afull[j], 0));
+          else
+            mbar_arrive(&afull[j]);
+        }
       }
     }
   } else {
@@ -412,7 +571,8 @@ __global__ void __launch_bounds__(threads_of(PAR), 1)
     unsigned char* out_ring = smem + C_::kOutOff;
     uint32_t chunk = 0;  // chunks stored so far: staging buffer = chunk % kOutBufs
     int lt = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++lt) {
+    for (int u = cta0; u < a.units; u += nctas, ++lt) {
+      const Unit un = unit_of(a, u);
       const int acc = lt % kAcc;
       const uint32_t ause = lt / kAcc;
       const bool ok = *abort_flag == 0 && mbar_wait_sleep(&accfull[acc], ause & 1, a.err);
@@ -422,9 +582,55 @@ __global__ void __launch_bounds__(threads_of(PAR), 1)
         break;
       }
       tc_fence_after();
-      const int n0 = (tile % a.n_tiles) * kWCols;
+      const float* other = nullptr;  // split tile, second half to finish: the first half's sums (shared memory)
+      if (un.slot >= 0) {
+        // Both halves store their raw fp32 sums, token-major ([token][128 columns], coalesced), then
+        // take a ticket; the second to arrive adds the other's sums below.  A split tile is the
+        // last unit of its CTA, so its accumulator is not reused and the stage ring is idle.
+        float* mine = a.partials + (size_t)(un.slot * 2 + un.half) * BT * kWCols;
+#pragma unroll 1
+        for (int c = 0; c < BT / kOutChunk; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + lane_addr + acc * BT + c * kOutChunk, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) mine[(size_t)(c * kOutChunk + j) * kWCols + col] = __uint_as_float(r[j]);
+        }
+        __threadfence();
+        epi_bar_sync();
+        if (threadIdx.x == 0) {
+          const unsigned prev = atomicAdd(&a.tickets[un.slot], 1u);
+          *last_half = prev == 1u;
+          if (prev == 1u) a.tickets[un.slot] = 0;  // zero again for the next call
+        }
+        epi_bar_sync();
+        if (!*last_half) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&accempty[acc]);
+          continue;
+        }
+        const float* theirs = a.partials + (size_t)(un.slot * 2 + (un.half ^ 1)) * BT * kWCols;
+        float* ring = reinterpret_cast<float*>(smem);
+        if (threadIdx.x == 0) {
+          __threadfence();
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          fence_proxy_async_smem();
+          mbar_arrive_expect_tx(pfull, (uint32_t)(BT * kWCols * 4));
+          for (int c = 0; c < BT / kOutChunk; ++c)
+            bulk_load(ring + c * kOutChunk * kWCols, theirs + (size_t)c * kOutChunk * kWCols,
+                      (uint32_t)(kOutChunk * kWCols * 4), pfull);
+        }
+        const bool got = mbar_wait_sleep(pfull, 0, a.err);
+        if (epi_bar_or(!got)) {
+          *abort_flag = 1;
+          break;
+        }
+        other = ring;
+      }
+      const int n0 = (un.tile % a.n_tiles) * kTileCols + (int)rank * kWCols;
       const int n = n0 + col;
-      const int m0 = (tile / a.n_tiles) * BT;
+      const int m0 = (un.tile / a.n_tiles) * BT;
       const bool nvalid = n < a.N;
       float mul = 1.f, add = 0.f;
       if (nvalid) {
@@ -440,9 +646,19 @@ __global__ void __launch_bounds__(threads_of(PAR), 1)
         if (c == BT / kOutChunk - 1) {  // accumulator read out: the MMA may reuse it
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&accempty[acc]);
+          if (lane == 0) {
+            if (PAIR && rank != 0)
+              mbar_arrive_remote(cluster_addr(&accempty[acc], 0));
+            else
+              mbar_arrive(&accempty[acc]);
+          }
         }
         if (c * kOutChunk >= mrows) continue;  // uniform over the epilogue warps
+        if (other != nullptr) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), other[(c * kOutChunk + j) * kWCols + col]));
+        }
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           float v = __uint_as_float(r[j]);
@@ -486,9 +702,14 @@ __global__ void __launch_bounds__(threads_of(PAR), 1)
 
   tc_fence_before();
   __syncthreads();
+  // A pair leaves together: no CTA exits while the other may still arrive on its barriers.
+  if constexpr (PAIR) cluster_sync_all();
   if (warp == kWarpMma) {
     tc_fence_after();
-    tmem_dealloc(tbase, kTmemCols);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tbase, kTmemCols);
+    else
+      tmem_dealloc(tbase, kTmemCols);
   }
 }
 
@@ -539,6 +760,8 @@ std::atomic<int> g_tune_min_rows{5};  // smallest M sent to the tensor-core GEMM
 std::atomic<int> g_tune_par{2};        // dequant warp groups working on alternate k steps
 std::atomic<int> g_tune_spin{0};       // single-thread waits spin on test_wait
 std::atomic<int> g_tune_tma_store{1};  // 16-bit outputs through TMA stores
+std::atomic<int> g_tune_split{1};      // split the tiles of a partial last round into k halves
+std::atomic<int> g_tune_pair{0};       // 256-token tiles on CTA pairs (tcgen05 cta_group::2)
 
 struct GPlan {
   bool ok = false;
@@ -560,6 +783,42 @@ int pick_bt(int M, int N, int sms) {
   if (M > 192 && rounds(256) <= rounds(192)) return 256;
   if (M > 128 && rounds(192) <= rounds(128)) return 192;
   return M > 128 ? 256 : 128;
+}
+
+// Split of the last round: when the tiles leave a last round that fills at
+// most half of the SMs, each of its tiles becomes two k halves on two SMs
+// (fp32 partial sums in the scratch, after a ticket prefix), which halves the
+// round's length for a few hundred KB of L2 traffic per tile.  Short k
+// ranges gain too little to pay for that.
+struct SplitPlan {
+  int whole = 0, rem = 0;   // whole tiles, split tiles
+  size_t part_off = 0;      // partial sums' offset in the scratch
+  size_t bytes = 0;         // scratch the split needs (conversion included)
+};
+SplitPlan split_plan(const GPlan& pl, int M, int N, int K, int bt, int sms) {
+  SplitPlan sp;
+  const int tiles = ((N + kWCols - 1) / kWCols) * ((M + bt - 1) / bt);
+  const int ksteps = (K + kKStep - 1) / kKStep;
+  sp.whole = tiles;
+  sp.bytes = pl.conv_bytes;
+  if (!g_tune_split.load() || ksteps < 16 || sms <= 0) return sp;
+  const int r = tiles % sms;
+  if (r == 0 || 2 * r > sms || r > 1024) return sp;
+  sp.whole = tiles - r;
+  sp.rem = r;
+  sp.part_off = pl.convert ? pl.conv_bytes : kConvOffset;
+  sp.bytes = sp.part_off + (size_t)r * 2 * bt * kWCols * 4;
+  return sp;
+}
+
+// CTA pairs: each MMA covers 256 weight columns, so every CTA stages half as
+// many activation bytes per FLOP and holds more pipeline stages; used when the
+// 256 x 256 tiles give every pair of SMs at least one.
+bool use_pair(int M, int N, int bt, int sms) {
+  const int mode = g_tune_pair.load();  // 0 never, 1 when the tiles fill the pairs, 2 whenever bt is 256
+  if (mode == 0 || bt != 256) return false;
+  const int tiles = ((N + 2 * kWCols - 1) / (2 * kWCols)) * ((M + bt - 1) / bt);
+  return mode == 2 || tiles >= sms / 2;
 }
 
 GPlan make_plan(const SgMatMulParams* p, int wkind) {
@@ -586,12 +845,15 @@ GPlan make_plan(const SgMatMulParams* p, int wkind) {
   return pl;
 }
 
-template <int BT, int WK, bool BF16_OP, bool HAS_Z, int PAR>
+// grid: CTAs for a.units work units on `sms` SMs; a pair kernel launches
+// clusters of two, as many as can be resident at once.
+template <int BT, int WK, bool BF16_OP, bool HAS_Z, int PAR, bool PAIR>
 SgStatus launch(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tz,
-                const CUtensorMap& tc, const GArgs& a, int grid, cudaStream_t cs) {
-  using C_ = Cfg<BT, WK>;
-  auto kfn = gemm_tc_kernel<BT, WK, BF16_OP, HAS_Z, PAR>;
+                const CUtensorMap& tc, const GArgs& a, int sms, cudaStream_t cs) {
+  using C_ = Cfg<BT, WK, PAIR>;
+  auto kfn = gemm_tc_kernel<BT, WK, BF16_OP, HAS_Z, PAR, PAIR>;
   static std::atomic<uint64_t> attr_set{0};  // bit per device ordinal
+  static std::atomic<int> max_pairs[64];      // resident clusters of two, per device (0 = not known yet)
   int dev = 0;
   SgStatus dst = sg::current_device(&dev);
   if (dst != SG_OK) return dst;
@@ -607,15 +869,36 @@ SgStatus launch(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap&
     attr_set.fetch_or(bit);
   }
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(threads_of(PAR));
   cfg.dynamicSmemBytes = C_::kSmem;
   cfg.stream = cs;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  int grid = std::min(a.units, sms);
+  if (PAIR) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+    const int slot = dev < 64 ? dev : 63;
+    int pairs = max_pairs[slot].load();
+    if (pairs <= 0) {
+      cfg.gridDim = dim3(2 * std::max(1, sms / 2));
+      cudaError_t e = cudaOccupancyMaxActiveClusters(&pairs, kfn, &cfg);
+      if (e != cudaSuccess || pairs <= 0) {
+        cudaGetLastError();
+        sg::set_error("gemm_tc_kernel: no resident CTA pair (%s)", cudaGetErrorString(e));
+        return SG_ERR_RUNTIME;
+      }
+      max_pairs[slot].store(pairs);
+    }
+    grid = 2 * std::min(a.units, pairs);
+  }
+  cfg.gridDim = dim3(grid);
   cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, ta, tw, ts, tz, tc, a);
   if (e != cudaSuccess) {
     cudaGetLastError();
@@ -627,19 +910,21 @@ SgStatus launch(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap&
 
 template <int WK, bool BF16_OP, bool HAS_Z, int PAR>
 SgStatus launch_bt(int bt, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& ts,
-                   const CUtensorMap& tz, const CUtensorMap& tc, const GArgs& a, int grid, cudaStream_t cs) {
+                   const CUtensorMap& tz, const CUtensorMap& tc, const GArgs& a, int sms, cudaStream_t cs) {
   switch (bt) {
-    case 256: return launch<256, WK, BF16_OP, HAS_Z, PAR>(ta, tw, ts, tz, tc, a, grid, cs);
-    case 192: return launch<192, WK, BF16_OP, HAS_Z, PAR>(ta, tw, ts, tz, tc, a, grid, cs);
-    default: return launch<128, WK, BF16_OP, HAS_Z, PAR>(ta, tw, ts, tz, tc, a, grid, cs);
+    case 256: return launch<256, WK, BF16_OP, HAS_Z, PAR, false>(ta, tw, ts, tz, tc, a, sms, cs);
+    case 192: return launch<192, WK, BF16_OP, HAS_Z, PAR, false>(ta, tw, ts, tz, tc, a, sms, cs);
+    default: return launch<128, WK, BF16_OP, HAS_Z, PAR, false>(ta, tw, ts, tz, tc, a, sms, cs);
   }
 }
 
+// pair: 256-token tiles shared by two CTAs (always two dequant groups).
 template <int WK, bool BF16_OP, bool HAS_Z>
-SgStatus launch_par(int par, int bt, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& ts,
-                    const CUtensorMap& tz, const CUtensorMap& tc, const GArgs& a, int grid, cudaStream_t cs) {
-  if (par == 1) return launch_bt<WK, BF16_OP, HAS_Z, 1>(bt, ta, tw, ts, tz, tc, a, grid, cs);
-  return launch_bt<WK, BF16_OP, HAS_Z, 2>(bt, ta, tw, ts, tz, tc, a, grid, cs);
+SgStatus launch_par(bool pair, int par, int bt, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& ts,
+                    const CUtensorMap& tz, const CUtensorMap& tc, const GArgs& a, int sms, cudaStream_t cs) {
+  if (pair) return launch<256, WK, BF16_OP, HAS_Z, 2, true>(ta, tw, ts, tz, tc, a, sms, cs);
+  if (par == 1) return launch_bt<WK, BF16_OP, HAS_Z, 1>(bt, ta, tw, ts, tz, tc, a, sms, cs);
+  return launch_bt<WK, BF16_OP, HAS_Z, 2>(bt, ta, tw, ts, tz, tc, a, sms, cs);
 }
 
 }  // namespace
@@ -648,10 +933,20 @@ namespace sg {
 
 // Scratch bytes the tensor-core GEMM needs for this problem (0 when it takes
 // the activations as they are); *ok = false when the problem goes elsewhere.
-size_t gemm_tc_scratch_bytes(const SgMatMulParams* p, bool int8_weights, bool* ok) {
+size_t gemm_tc_scratch_bytes(const SgMatMulParams* p, bool int8_weights, bool* ok, bool minimal) {
   const GPlan pl = make_plan(p, int8_weights ? kW8Channel : kW4Grouped);
   *ok = pl.ok;
-  return pl.ok ? pl.conv_bytes : 0;
+  if (!pl.ok) return 0;
+  if (minimal) return pl.conv_bytes;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return pl.conv_bytes;
+  }
+  const int sms = sm_count(dev);
+  const int bt = pick_bt(p->M, p->N, sms);
+  if (use_pair(p->M, p->N, bt, sms)) return pl.conv_bytes;
+  return split_plan(pl, p->M, p->N, p->K, bt, sms).bytes;
 }
 
 // Runs the tensor-core GEMM when the problem qualifies (*handled = true).
@@ -668,6 +963,7 @@ SgStatus gemm_tc_run(const SgMatMulParams* p, bool int8_weights, cudaStream_t cs
   const int a_dt = p->a_dtype == SG_DT_DEFAULT ? (wk == kW4Grouped ? SG_DT_I8 : SG_DT_F16) : p->a_dtype;
   const int lda = p->lda > 0 ? p->lda : p->K;
   const void* act = p->A;
+  void* const ws_base = ws;
   if (pl.convert) {
     ws = static_cast<unsigned char*>(ws) + kConvOffset;
     const int chunks = pl.ld_act / 8;
@@ -681,6 +977,7 @@ SgStatus gemm_tc_run(const SgMatMulParams* p, bool int8_weights, cudaStream_t cs
     act = ws;
   }
   const int bt = pick_bt(p->M, p->N, sms);
+  const bool pair = use_pair(p->M, p->N, bt, sms);
   const int gs = p->group_size > 0 ? p->group_size : 128;
   const int G = (p->K + gs - 1) / gs;
 
@@ -689,7 +986,7 @@ SgStatus gemm_tc_run(const SgMatMulParams* p, bool int8_weights, cudaStream_t cs
   {
     const uint64_t dims[2] = {(uint64_t)p->K, (uint64_t)p->M};
     const uint64_t str[1] = {(uint64_t)pl.ld_act * 2};
-    const uint32_t box[2] = {(uint32_t)kKStep, (uint32_t)bt};
+    const uint32_t box[2] = {(uint32_t)kKStep, (uint32_t)(pair ? bt / 2 : bt)};
     st = make_tensor_map(&ta, pl.bf16_op ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                          const_cast<void*>(act), dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st != SG_OK) return st;
@@ -740,7 +1037,7 @@ SgStatus gemm_tc_run(const SgMatMulParams* p, bool int8_weights, cudaStream_t cs
   a.K = p->K;
   a.gs = gs;
   a.ksteps = (p->K + kKStep - 1) / kKStep;
-  a.n_tiles = (p->N + kWCols - 1) / kWCols;
+  a.n_tiles = pair ? (p->N + 2 * kWCols - 1) / (2 * kWCols) : (p->N + kWCols - 1) / kWCols;
   a.m_tiles = (p->M + bt - 1) / bt;
   a.err = err_word;
   a.spin = g_tune_spin.load() ? 1 : 0;
@@ -758,15 +1055,25 @@ SgStatus gemm_tc_run(const SgMatMulParams* p, bool int8_weights, cudaStream_t cs
     a.tma_store = 1;
   }
   const int tiles = a.n_tiles * a.m_tiles;
-  const int grid = std::min(tiles, sms);
+  // Split of the last round, when the scratch has room for it.  Every CTA then
+  // gets at most one split unit, as its last one (the kernel relies on that).
+  const SplitPlan sp = pair ? SplitPlan{} : split_plan(pl, p->M, p->N, p->K, bt, sms);
+  a.whole = tiles;
+  a.units = tiles;
+  if (sp.rem > 0 && ws_base != nullptr && ws_bytes >= sp.bytes && aligned16(ws_base)) {
+    a.whole = sp.whole;
+    a.units = sp.whole + 2 * sp.rem;
+    a.tickets = static_cast<unsigned*>(ws_base);
+    a.partials = reinterpret_cast<float*>(static_cast<unsigned char*>(ws_base) + sp.part_off);
+  }
   *handled = true;
   const int par = g_tune_par.load() == 1 ? 1 : 2;
   if (wk == kW4Grouped) {
-    if (p->zeros_B) return launch_par<kW4Grouped, false, true>(par, bt, ta, tw, ts, tz, tc, a, grid, cs);
-    return launch_par<kW4Grouped, false, false>(par, bt, ta, tw, ts, tz, tc, a, grid, cs);
+    if (p->zeros_B) return launch_par<kW4Grouped, false, true>(pair, par, bt, ta, tw, ts, tz, tc, a, sms, cs);
+    return launch_par<kW4Grouped, false, false>(pair, par, bt, ta, tw, ts, tz, tc, a, sms, cs);
   }
-  if (pl.bf16_op) return launch_par<kW8Channel, true, false>(par, bt, ta, tw, ts, tz, tc, a, grid, cs);
-  return launch_par<kW8Channel, false, false>(par, bt, ta, tw, ts, tz, tc, a, grid, cs);
+  if (pl.bf16_op) return launch_par<kW8Channel, true, false>(pair, par, bt, ta, tw, ts, tz, tc, a, sms, cs);
+  return launch_par<kW8Channel, false, false>(pair, par, bt, ta, tw, ts, tz, tc, a, sms, cs);
 }
 
 bool gemm_tc_tuning(std::string_view key, int value) {
@@ -784,6 +1091,14 @@ bool gemm_tc_tuning(std::string_view key, int value) {
   }
   if (key == "gemm_tc.par") {
     g_tune_par.store(value);
+    return true;
+  }
+  if (key == "gemm_tc.pair") {
+    g_tune_pair.store(value);
+    return true;
+  }
+  if (key == "gemm_tc.split") {
+    g_tune_split.store(value);
     return true;
   }
   if (key == "gemm_tc.min_rows") {

@@ -64,7 +64,8 @@ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 // Tensor-core prefill GEMM (gemm_tc.cu) for INT4-grouped or INT8-per-channel
 // weights.  gemm_tc_scratch_bytes: *ok tells whether the problem qualifies;
 // the result is the scratch it needs (0 when activations are used in place).
-size_t gemm_tc_scratch_bytes(const SgMatMulParams* p, bool int8_weights, bool* ok);
+// minimal: the least scratch it runs with (no split of the last round of tiles).
+size_t gemm_tc_scratch_bytes(const SgMatMulParams* p, bool int8_weights, bool* ok, bool minimal = false);
 // Tensor-core INT8 GEMV for one float activation row (w8_gemv_mma.cu); *handled says whether it ran.
 SgStatus w8_gemv_mma_run(const SgMatMulParams* p, cudaStream_t cs, int sms, int* err_word, bool* handled);
 SgStatus gemm_tc_run(const SgMatMulParams* p, bool int8_weights, cudaStream_t cs, int sms, void* ws,

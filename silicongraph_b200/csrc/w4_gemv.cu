@@ -576,7 +576,7 @@ SgStatus w4_gemv_run(const SgMatMulParams* p, void* stream, void* ws, size_t ws_
                      int* err_word) {
   return w4_run(p, stream, ws, ws_bytes, ws_external, err_word);
 }
-size_t w4_gemv_scratch_bytes(const SgMatMulParams* p) {
+size_t w4_gemv_scratch_bytes(const SgMatMulParams* p, bool minimal) {
   if (validate(p) != SG_OK || p->M == 0 || p->N == 0) return 0;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {
@@ -586,7 +586,7 @@ size_t w4_gemv_scratch_bytes(const SgMatMulParams* p) {
   const int sms = sm_count(dev);
   const int path = g_tune_path.load();
   bool tc_ok = false;
-  const size_t tws = gemm_tc_scratch_bytes(p, false, &tc_ok);
+  const size_t tws = gemm_tc_scratch_bytes(p, false, &tc_ok, minimal);
   if (tc_ok && path == 0) return tws;
   bool mma_ok = false;
   const size_t mws = w4_gemv_mma_scratch_bytes(p, sms, &mma_ok);
@@ -639,7 +639,7 @@ SgStatus sg_matmul_int4_grouped(const SgMatMulParams* p, void* stream) {
 }
 
 size_t sg_matmul_int4_grouped_workspace_size(const SgMatMulParams* p) {
-  return sg::w4_gemv_scratch_bytes(p);
+  return sg::w4_gemv_scratch_bytes(p, false);
 }
 
 int32_t sg_set_tuning(const char* key, int32_t value) {

@@ -92,7 +92,7 @@ int* noalloc_error_word(int dev) {
 
 SgStatus w4_gemv_run(const SgMatMulParams* p, void* stream, void* ws, size_t ws_bytes, bool ws_external,
                      int* err_word);
-size_t w4_gemv_scratch_bytes(const SgMatMulParams* p);
+size_t w4_gemv_scratch_bytes(const SgMatMulParams* p, bool minimal);
 }  // namespace sg
 
 extern "C" SgStatus sg_matmul_int4_grouped_noalloc(const SgMatMulParams* p, void* stream) {
@@ -107,7 +107,9 @@ extern "C" SgStatus sg_matmul_int4_grouped_noalloc(const SgMatMulParams* p, void
   SgMatMulParams q = *p;
   q.workspace = nullptr;
   q.workspace_bytes = 0;
-  const size_t need = sg::w4_gemv_scratch_bytes(&q);
+  // the least scratch the call runs with: the prefill GEMM splits its last
+  // round of tiles only when the fixed array has room for the partial sums
+  const size_t need = sg::w4_gemv_scratch_bytes(&q, true);
   if (need > kNoAllocScratchBytes) {
     sg::set_error(
         "sg_matmul_int4_grouped_noalloc: this problem (M=%d K=%d N=%d) needs %zu bytes of scratch; the fixed "

@@ -98,6 +98,7 @@ def test_flag_values_match_header():
     ("w4_gemv_mma.strips", 0), ("w4_gemv_mma.variant", 0), ("attn.decode_kernel", 4), ("sdk.fuse_swiglu", 1),
     ("w4_rows.two_pass_rows", 32), ("tp_allreduce.wait_ms", 0), ("sdk.fuse_norm", 1), ("sdk.fuse_rope", 1),
     ("sdk.decode_step_kernel", 0), ("w8_gemv_mma.enable", 1), ("attn_tc.pair", 1),
+    ("gemm_tc.split", 1), ("gemm_tc.pair", 0), ("gemm_tc.bt", 0), ("gemm_tc.par", 2),
 ])
 def test_tuning_keys_known(lib, key, value):
     """Every tuning knob the kernels and the SDK read is reachable through

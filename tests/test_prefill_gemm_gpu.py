@@ -178,3 +178,94 @@ def test_prefill_store_paths_identical(sg, oracle_mod, cdt):
     want = oracle_mod.matmul_int4_grouped(oracle_mod.f32_to_bf16_bits(x.float().cpu().numpy()), B, S, Z, K, N, gs,
                                           M=M, c_dt=oracle_mod.DT_F32, a_bf16=True)
     close(outs[0][:, :N].float().cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("M,K,N,gs,zeros,cdt", [
+    (256, 2048, 2048, 32, True, torch.float32),      # one round of 16 tiles: every tile split in two k halves
+    (200, 1024, 1000, 64, False, torch.bfloat16),    # ragged rows and columns in the split tiles
+    (1300, 1024, 4096, 128, True, torch.float16),    # 6 x 32 = 192 tiles: 44 of them split after one whole round
+])
+def test_prefill_split_last_round(sg, oracle_mod, M, K, N, gs, zeros, cdt):
+    """The last, partial round of tiles split into two k halves on two SMs
+    (fp32 partial sums in the scratch, the second half to finish adds them):
+    within tolerance of the oracle on every row and of the unsplit GEMM, and
+    the same bits on every run."""
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=M + N, sym=not zeros)
+    x32 = np.random.default_rng(M).standard_normal((M, K)).astype(np.float32)
+    args = (t(x32), t(B), t(S), None if Z is None else t(Z), K, N, gs)
+    split = sg.matmul_int4_grouped(*args, out_dtype=cdt)
+    assert torch.equal(split, sg.matmul_int4_grouped(*args, out_dtype=cdt))
+    sg.set_tuning("gemm_tc.split", 0)
+    try:
+        whole = sg.matmul_int4_grouped(*args, out_dtype=cdt)
+    finally:
+        sg.set_tuning("gemm_tc.split", 1)
+    want = oracle_mod.matmul_int4_grouped(x32, B, S, Z, K, N, gs, M=M, c_dt=oracle_mod.DT_F32)
+    close(split.float().cpu().numpy(), want)
+    close(whole.float().cpu().numpy(), want)
+    close(split.float().cpu().numpy(), whole.float().cpu().numpy())
+
+
+@pytest.fixture
+def cta_pairs(sg):
+    """Tiles of 256 weight columns x 256 tokens on clusters of two CTAs
+    (tcgen05 cta_group::2), forced for every shape."""
+    sg.set_tuning("gemm_tc.bt", 256)
+    sg.set_tuning("gemm_tc.pair", 2)
+    yield
+    sg.set_tuning("gemm_tc.pair", 0)
+    sg.set_tuning("gemm_tc.bt", 0)
+
+
+@pytest.mark.parametrize("M,K,N,gs,zeros,adt,cdt", [
+    (300, 512, 1000, 32, True, "f32", torch.float32),     # ragged rows and a ragged last column pair
+    (256, 2048, 384, 64, False, "bf16", torch.bfloat16),  # the second CTA of the last pair: 128 columns
+    (520, 1024, 2048, 16, False, "f16", torch.float16),   # groups of 16; last token tile 8 rows
+    (96, 1000, 640, 128, True, "i8", torch.float16),      # int8 activations, partial last group
+])
+def test_int4_prefill_cta_pairs_vs_oracle(sg, oracle_mod, cta_pairs, M, K, N, gs, zeros, adt, cdt):
+    B, S, Z = w4_problem(oracle_mod, K, N, gs, seed=M + 3 * N, sym=not zeros)
+    rng = np.random.default_rng(K + N)
+    xo, xt, kw = _acts(oracle_mod, rng, M, K, adt)
+    bias = (0.1 * rng.standard_normal(N)).astype(np.float16)
+    scale_A = 0.05 if adt == "i8" else 1.0
+    want = oracle_mod.matmul_int4_grouped(xo, B, S, Z, K, N, gs, M=M, bias=bias, c_dt=oracle_mod.DT_F32,
+                                          scale_A=scale_A, **kw)
+    args = (xt, t(B), t(S), None if Z is None else t(Z), K, N, gs)
+    C = sg.matmul_int4_grouped(*args, out_dtype=cdt, bias=t(bias), scale_A=scale_A)
+    close(C.float().cpu().numpy(), want)
+    assert torch.equal(C, sg.matmul_int4_grouped(*args, out_dtype=cdt, bias=t(bias), scale_A=scale_A))
+
+
+@pytest.mark.parametrize("M,K,N,adt", [(300, 1000, 1040, "f32"), (512, 512, 512, "bf16")])
+def test_int8_prefill_cta_pairs_vs_oracle(sg, oracle_mod, cta_pairs, M, K, N, adt):
+    rng = np.random.default_rng(M + 1)
+    xo, xt, kw = _acts(oracle_mod, rng, M, K, adt)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    s = (rng.random(N) * 1e-3).astype(np.float32)
+    want = oracle_mod.gemm_w8_channel(xo, B, s, M, K, N, **kw)
+    C = torch.zeros((M, N), dtype=torch.float32, device=DEV)
+    _mm(sg, "sg_matmul_int8_channel", xt, t(B), C, M, K, N, scales=t(s))
+    close(C.cpu().numpy(), want)
+
+
+def test_prefill_benchmark_shape_cta_pairs(sg, oracle_mod):
+    """[2048, 2048] bf16 x INT4 symmetric g64 [2048, 8192] on CTA pairs: within
+    tolerance of the oracle on sampled rows and of the one-CTA kernel on all."""
+    M, K, N, gs = 2048, 2048, 8192, 64
+    B, S, _ = w4_problem(oracle_mod, K, N, gs, seed=31, sym=True)
+    x32 = np.random.default_rng(32).standard_normal((M, K)).astype(np.float32)
+    args = (bf16_tensor(x32), t(B), t(S), None, K, N, gs)
+    sg.set_tuning("gemm_tc.pair", 1)
+    try:
+        C = sg.matmul_int4_grouped(*args, out_dtype=torch.bfloat16)
+    finally:
+        sg.set_tuning("gemm_tc.pair", 0)
+    one = sg.matmul_int4_grouped(*args, out_dtype=torch.bfloat16)
+    rows = _row_subset(M, 34)
+    xo = oracle_mod.f32_to_bf16_bits(x32[rows])
+    want = oracle_mod.matmul_int4_grouped(xo, B, S, None, K, N, gs, M=len(rows), c_dt=oracle_mod.DT_F32,
+                                          a_bf16=True)
+    got = C.float().cpu().numpy()
+    close(got[rows], want)
+    close(got, one.float().cpu().numpy())
