@@ -47,16 +47,20 @@ constexpr int kWCols = 128;   // weight columns per tile = TMEM lanes = UMMA M
 // Warp roles.  Warps 0..3: epilogue, TMEM lane quarter = warp.  Then 8 * PAR
 // dequant warps: lane quarter = warp % 4, k half of the step = bit 2 of the
 // dequant index, and with PAR = 2 the step parity = bit 3 (two steps are
-// dequantized concurrently).  Then two TMA producer warps (activations;
-// weights, scales and zeros) and the MMA warp.  One thread cannot issue
-// tcgen05.mma faster than about one per 105 cycles, and each TMA issue costs
-// on the order of 100 cycles, so every single-thread role gets its own warp.
+// dequantized concurrently).  Then three TMA producer warps (activation
+// tiles; packed weights; scale and zero rows) and the MMA warp.  One thread
+// cannot issue tcgen05.mma faster than about one per 120 cycles, and under the
+// kernel's load one thread issues a TMA copy only every ~450 cycles (per-role
+// clock64 timeline: with weights and scales on one thread, that thread set the
+// pace of the whole pipeline at ~920 cycles per 64-k step), so every
+// single-thread role gets its own warp and each producer issues one copy per step.
 constexpr int kEpiWarps = 4;
 constexpr int kStepWarps = 8;  // dequant warps that complete one step (4 quarters x 2 k halves)
 __host__ __device__ constexpr int prep_warps(int par) { return kStepWarps * par; }
 __host__ __device__ constexpr int warp_tma_act(int par) { return kEpiWarps + prep_warps(par); }
 __host__ __device__ constexpr int warp_tma_w(int par) { return warp_tma_act(par) + 1; }
-__host__ __device__ constexpr int warp_mma(int par) { return warp_tma_w(par) + 1; }
+__host__ __device__ constexpr int warp_tma_s(int par) { return warp_tma_w(par) + 1; }
+__host__ __device__ constexpr int warp_mma(int par) { return warp_tma_s(par) + 1; }
 __host__ __device__ constexpr int threads_of(int par) { return (warp_mma(par) + 1) * 32; }
 constexpr int kOutChunk = 32;                         // tokens per epilogue TMA store
 constexpr int kOutBuf = kOutChunk * 128 * 2;          // one 16-bit [32 x 128] staging tile
@@ -309,7 +313,9 @@ __global__ void __launch_bounds__(threads_of(PAR), 1)
   using C_ = Cfg<BT, WK, PAIR>;
   constexpr int kTileCols = PAIR ? 2 * kWCols : kWCols;  // weight columns per tile
   constexpr int S = C_::kStages, J = C_::kSlots, kAcc = C_::kAcc;
-  constexpr int kWarpAct = warp_tma_act(PAR), kWarpW = warp_tma_w(PAR), kWarpMma = warp_mma(PAR);
+  constexpr int kWarpAct = warp_tma_act(PAR), kWarpW = warp_tma_w(PAR), kWarpS = warp_tma_s(PAR);
+  constexpr int kWarpMma = warp_mma(PAR);
+  constexpr int kProducers = WK == kW4Grouped ? 3 : 2;  // INT8 weights have no scale rows to stage
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = sgd::align_smem_1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C_::kBarOff);
@@ -332,7 +338,7 @@ __global__ void __launch_bounds__(threads_of(PAR), 1)
   const int nctas = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 2);  // one expect_tx arrival per producer
+      mbar_init(&full[s], kProducers);  // one expect_tx arrival per producer
       mbar_init(&empty[s], 1);
     }
     for (int j = 0; j < J; ++j) {
@@ -358,9 +364,9 @@ __global__ void __launch_bounds__(threads_of(PAR), 1)
     }
   }
   if (warp == kWarpAct && lane == 0) tma_prefetch_desc(&tmAct);
-  if (warp == kWarpW && lane == 0) {
-    tma_prefetch_desc(&tmW);
-    if (WK == kW4Grouped) tma_prefetch_desc(&tmS);
+  if (warp == kWarpW && lane == 0) tma_prefetch_desc(&tmW);
+  if (warp == kWarpS && lane == 0 && WK == kW4Grouped) {
+    tma_prefetch_desc(&tmS);
     if (HAS_Z) tma_prefetch_desc(&tmZ);
   }
   if (warp == 0 && lane == 0 && a.tma_store) tma_prefetch_desc(&tmC);
@@ -372,18 +378,17 @@ __global__ void __launch_bounds__(threads_of(PAR), 1)
   // Inputs written by the preceding kernel on the stream are visible after this.
   pdl_wait();
 
-  if (warp == kWarpAct || warp == kWarpW) {
+  if (warp == kWarpAct || warp == kWarpW || warp == kWarpS) {
     // ------------------------------------------------------------ TMA producers
-    if (lane == 0) {
-      const bool is_act = warp == kWarpAct;
+    if (lane == 0 && (warp != kWarpS || WK == kW4Grouped)) {
+      const bool is_act = warp == kWarpAct, is_w = warp == kWarpW;
       uint32_t issued[S];
       for (int s = 0; s < S; ++s) issued[s] = 0;
       const int gs = a.gs;
-      uint32_t bytes = is_act ? C_::kActBytes : C_::kWBytes;
-      if (!is_act && WK == kW4Grouped) {
-        const int srows = gs >= kKStep ? 1 : kKStep / gs;
-        bytes += srows * kWCols * 2 + (HAS_Z ? srows * kWCols : 0);
-      }
+      const int srows = gs >= kKStep ? 1 : kKStep / gs;
+      const uint32_t bytes = is_act ? (uint32_t)C_::kActBytes
+                             : is_w ? (uint32_t)C_::kWBytes
+                                    : (uint32_t)(srows * kWCols * 2 + (HAS_Z ? srows * kWCols : 0));
       uint32_t g = 0;
       bool ok = true;
       for (int u = cta0; u < a.units && ok; u += nctas) {
@@ -403,13 +408,12 @@ __global__ void __launch_bounds__(threads_of(PAR), 1)
           mbar_arrive_expect_tx(&full[s], bytes);
           if (is_act) {
             tma_load_2d(st, &tmAct, ks * kKStep, m0, &full[s]);
-          } else if (WK == kW4Grouped) {
-            tma_load_2d(st + C_::kActBytes, &tmW, n0, ks * (kKStep / 2), &full[s]);
+          } else if (is_w) {
+            tma_load_2d(st + C_::kActBytes, &tmW, n0, WK == kW4Grouped ? ks * (kKStep / 2) : ks * kKStep, &full[s]);
+          } else {
             const int grow = (ks * kKStep) / gs;
             tma_load_2d(st + C_::kActBytes + C_::kWBytes, &tmS, n0, grow, &full[s]);
             if (HAS_Z) tma_load_2d(st + C_::kActBytes + C_::kWBytes + C_::kSBytes, &tmZ, n0, grow, &full[s]);
-          } else {
-            tma_load_2d(st + C_::kActBytes, &tmW, n0, ks * kKStep, &full[s]);
           }
           issued[s] = use + 1;
         }
