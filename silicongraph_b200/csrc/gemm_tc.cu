@@ -6,7 +6,8 @@
 // (dense GEMV FA form: C = scales[n] * sum_k A*float(B), opencl_kernels.h:36-52
 // restated for float A).
 //
-// Design (one persistent CTA per SM, 448 threads, warp-specialised):
+// Design (one persistent CTA per SM, 768 threads with two dequant groups,
+// warp-specialised; roles listed below the constants):
 //   * The weights are the MMA's A operand and live in TMEM: dequant warps read
 //     the packed bytes that TMA staged in shared memory, expand them in
 //     registers (fp16(scale * (q - 8 - zero)) for INT4, exact integers for
@@ -19,8 +20,13 @@
 //     K = 16) into a TMEM accumulator of 128 lanes x BT columns.
 //   * Four epilogue warps (one per TMEM lane quarter) read the accumulator
 //     with tcgen05.ld, apply scale_A / per-channel scales / bias and store C.
-//     With two accumulators the epilogue of one tile overlaps the main loop
-//     of the next.
+//     With two accumulators (token tiles up to 192) the epilogue of one tile
+//     overlaps the main loop of the next; the 256-token tile has room for one,
+//     and the MMA waits for its epilogue at each tile boundary.
+//   * A last round of tiles that fills at most half of the SMs runs as two k
+//     halves per tile (fp32 partials in the scratch, added by the second half
+//     to finish); optionally, clusters of two CTAs share each MMA
+//     (tcgen05 cta_group::2, 256 weight columns per tile).
 //   * Every wait is bounded (2 s); a timed-out wait records an error code in
 //     the device error word, the CTA drains its copies in flight, frees TMEM
 //     and exits.
