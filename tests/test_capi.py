@@ -107,6 +107,23 @@ def test_tuning_keys_known(lib, key, value):
     assert lib.sg_set_tuning(key.encode(), value) == SG_OK
 
 
+def test_documented_tuning_keys_accepted():
+    """Every key that include/sg_kernels.h documents for sg_set_tuning is one
+    the library accepts.  Set in a child process, so the values do not leak
+    into the other tests of this session."""
+    import subprocess
+    import sys
+    src = open(os.path.join(ROOT, "include", "sg_kernels.h")).read()
+    block = src[src.index("Override a launch heuristic"):src.index("int32_t sg_set_tuning")]
+    keys = sorted(set(re.findall(r'^ \*\s+"([a-z0-9_.]+)"', block, re.M) + re.findall(r', "([a-z0-9_.]+)"', block)))
+    assert len(keys) >= 15, keys
+    code = ("import sys; from silicongraph_b200 import _lib; lib = _lib.load(); "
+            "bad = [k for k in sys.argv[1:] if lib.sg_set_tuning(k.encode(), 0) != 0]; "
+            "print(bad); sys.exit(1 if bad else 0)")
+    r = subprocess.run([sys.executable, "-c", code, *keys], cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+
+
 def test_swiglu_flag_argument_checks(lib):
     """SG_MM_A_SWIGLU is refused for int8 / fp32 activations and for an lda
     shorter than the gate | up row, before any device work."""
